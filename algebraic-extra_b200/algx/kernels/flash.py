@@ -1,0 +1,192 @@
+"""Causal flash attention, softmax and asinh-power kinds (drop-in for kernels/flash.py).
+
+Same call signature, variant resolution and ValueError conditions as the
+reference's ``flash_attention`` (kernels/flash.py:732-857). The schedule
+knobs of the TPU kernels (``block*``, ``resident_bwd``, ``diagonal_*``,
+``head_resident``, ``compact_stat``) are validated exactly as the reference
+validates them and otherwise ignored: the sm_100a kernels choose their own
+tiles, and none of those knobs changes the function computed.
+
+The range guard (``range_guard=True``) is evaluated on the device:
+``algx_attn_prepare`` folds the score scale into q and writes the guard
+maxima, and the forward/backward kernels pick the unshifted (low) or the
+shifted (high) branch from them, so no host synchronisation happens.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from .. import _lib as L
+
+
+def _root(value: float, n: int) -> float:
+    """value^(1/n) for n a power of two by repeated sqrt (kernels/flash.py:117-123)."""
+    out = float(value)
+    while n > 1:
+        out = math.sqrt(out)
+        n //= 2
+    return out
+
+
+class Variant(dict):
+    """Resolved asinh/softmax variant (mirrors kernels/flash.py:59-73)."""
+
+
+def make_variant(kind: str, n: int = 16, c: float = 16.0, seq_len: int = 2048,
+                 shift: Optional[bool] = None, fast_rho: Optional[bool] = None,
+                 inv_stat: Optional[bool] = None, compact_stat: bool = True,
+                 poly_rho: bool = False) -> Variant:
+    """Variant resolution of kernels/flash.py:732-760."""
+    if kind == "softmax":
+        return Variant(kind="softmax", n=16, shift=True, fast_rho=False, clamp=0.0, inv_stat=False,
+                       compact_stat=bool(compact_stat), poly_rho=False)
+    if kind != "asinh":
+        raise ValueError(f"unknown attention kernel: {kind}")
+    if n < 2 or n & (n - 1):
+        raise ValueError("asinh kernel needs n to be a power of two")
+    if not math.isfinite(c) or c <= 0:
+        raise ValueError("asinh scale c must be positive and finite")
+    t = _root(1e37 / (seq_len + 1), n)
+    clamp = 0.5 * (t - 1.0 / t)
+    if shift is None:
+        shift = clamp < 20.0
+    if fast_rho is None:
+        fast_rho = True
+    if inv_stat is None:
+        inv_stat = not shift
+    if inv_stat and shift:
+        raise ValueError("inverse-denominator statistic requires shift=False")
+    if poly_rho and (shift or n != 16):
+        raise ValueError("bounded radical approximation requires shift=False and n=16")
+    return Variant(kind="asinh", n=int(n), shift=bool(shift), fast_rho=bool(fast_rho), clamp=float(clamp),
+                   inv_stat=bool(inv_stat), compact_stat=bool(compact_stat), poly_rho=bool(poly_rho))
+
+
+class _Flash(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, sink, cfg: L.AttnConfig):
+        B, H, T, D = q.shape
+        dt = L.dtype_code(q.dtype)
+        st = L.stream_of(q)
+        q_s = torch.empty_like(q)
+        guard = torch.empty(4, dtype=torch.float32, device=q.device)
+        sp = sink.data_ptr() if sink is not None else None
+        L.check(L.lib().algx_attn_prepare(cfg, q.data_ptr(), k.data_ptr(), v.data_ptr(), sp, q_s.data_ptr(),
+                                          guard.data_ptr(), B, H, T, D, dt, st), "algx_attn_prepare")
+        o = torch.empty_like(q)
+        stat = torch.empty((B, H, T), dtype=torch.float32, device=q.device)
+        o_prec = None
+        if cfg.kind == L.ALGX_ATTN_ASINH and cfg.mode == L.ALGX_MODE_GUARDED:
+            o_prec = torch.empty((B, H, T, D), dtype=torch.float32, device=q.device)
+        L.check(L.lib().algx_attn_fwd(cfg, q_s.data_ptr(), k.data_ptr(), v.data_ptr(), sp, guard.data_ptr(),
+                                      o.data_ptr(), L.ptr(o_prec), stat.data_ptr(), B, H, T, D, dt, st),
+                "algx_attn_fwd")
+        ctx.cfg = cfg
+        ctx.has_sink = sink is not None
+        ctx.save_for_backward(q_s, k, v, sink, o, o_prec, stat, guard)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q_s, k, v, sink, o, o_prec, stat, guard = ctx.saved_tensors
+        cfg = ctx.cfg
+        B, H, T, D = q_s.shape
+        do = do.to(q_s.dtype).contiguous()
+        dq = torch.empty_like(q_s)
+        dk = torch.empty_like(k)
+        dv = torch.empty_like(v)
+        dsink = torch.empty(H, dtype=torch.float32, device=q_s.device) if ctx.has_sink else None
+        nbytes = L.lib().algx_attn_bwd_workspace_size(B, H, T, D)
+        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q_s.device)
+        L.check(L.lib().algx_attn_bwd(cfg, q_s.data_ptr(), k.data_ptr(), v.data_ptr(), L.ptr(sink),
+                                      guard.data_ptr(), o.data_ptr(), L.ptr(o_prec), stat.data_ptr(),
+                                      do.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), L.ptr(dsink),
+                                      B, H, T, D, L.dtype_code(q_s.dtype), ws.data_ptr(), nbytes,
+                                      L.stream_of(q_s)), "algx_attn_bwd")
+        return dq, dk, dv, dsink, None
+
+
+def build_config(kind, var: Variant, T: int, D: int, c: float, has_sink: bool,
+                 range_guard: bool) -> L.AttnConfig:
+    """Pack the resolved variant and the wrapper constants (kernels/flash.py:823-856)."""
+    cfg = L.AttnConfig()
+    unit = 1.0 if kind == "softmax" else float(c)
+    cfg.kind = L.ALGX_ATTN_SOFTMAX if kind == "softmax" else L.ALGX_ATTN_ASINH
+    cfg.n = int(var["n"])
+    cfg.fast_rho = int(var["fast_rho"])
+    cfg.inv_stat = int(var["inv_stat"])
+    cfg.has_sink = int(has_sink)
+    cfg.clamp = float(var["clamp"])
+    cfg.scale = 1.0 / (math.sqrt(D) * unit)
+    cfg.guard_qk = cfg.guard_sink = cfg.guard_v = 0.0
+    if kind == "asinh" and range_guard and var["n"] <= 32:
+        bound = min(16.0, var["clamp"] / 2)
+        cfg.mode = L.ALGX_MODE_GUARDED
+        cfg.guard_qk = (bound / 1.01) ** 2
+        cfg.guard_sink = bound / 1.01
+        cfg.guard_v = min(1e8, 1e37 / ((T + int(has_sink)) * (2 * bound + 1) ** var["n"]))
+    elif kind == "asinh":
+        cfg.mode = L.ALGX_MODE_SHIFTED if var["shift"] else L.ALGX_MODE_CLIPPED
+    else:
+        cfg.mode = L.ALGX_MODE_SHIFTED
+    return cfg
+
+
+def flash_attention(q, k, v, sink_logit=None, *, kind: str = "softmax",
+                    n: int = 16, c: float = 16.0, block: int = 512,
+                    block_q: Optional[int] = None, block_k: Optional[int] = None,
+                    shift: Optional[bool] = None, fast_rho: Optional[bool] = None,
+                    inv_stat: Optional[bool] = None, compact_stat: bool = True,
+                    poly_rho: bool = False, range_guard: bool = False,
+                    resident_bwd: Optional[bool] = None,
+                    diagonal_bwd: Optional[bool] = None,
+                    diagonal_fwd: Optional[bool] = None,
+                    head_resident: Optional[bool] = None):
+    """Causal attention on (B, H, T, D); ``sink_logit`` broadcastable to (H,).
+
+    Same semantics as the reference (kernels/flash.py:763-857). ``poly_rho``
+    selects a TPU-only polynomial radical there; here it is validated the
+    same way and the exact radical is evaluated (the same function, within
+    the reference's own polynomial-mode tolerance). D must be 64.
+    """
+    B, H, T, D = q.shape
+    bq = min(block_q or block, T)
+    bk = min(block_k or block, T)
+    if T % bq or T % bk:
+        raise ValueError(f"sequence length {T} must be divisible by blocks ({bq}, {bk})")
+    var = make_variant(kind, n, c, T, shift, fast_rho, inv_stat, compact_stat, poly_rho)
+    resident_supported = (T in (512, 1024, 2048) and D == 64 and
+                          q.dtype == k.dtype == v.dtype == torch.bfloat16 and not poly_rho and
+                          (kind == "softmax" or n == 16))
+    if resident_bwd is True and not resident_supported:
+        raise ValueError("resident backward needs bfloat16, T=512/1024/2048, D=64, "
+                         "and softmax or exact asinh n=16")
+    use_resident = (resident_supported and T == 2048 and bq == bk == 512 and compact_stat
+                    if resident_bwd is None else bool(resident_bwd))
+    if diagonal_bwd is True and not use_resident:
+        raise ValueError("diagonal backward requires the resident backward backend")
+    head_supported = (use_resident and T == 2048 and bq == bk == 512 and compact_stat)
+    if head_resident is True and not head_supported:
+        raise ValueError("whole-head residency needs resident bfloat16 T=2048,D=64, "
+                         "512-square public tiles, and compact statistics")
+    if range_guard and kind == "asinh" and n <= 32 and poly_rho:
+        raise ValueError("range_guard is for exact radical evaluation")
+    if D != 64:
+        raise ValueError(f"algx attention supports head_dim 64, got {D}")
+    if not (q.dtype == k.dtype == v.dtype) or q.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("q, k, v must share one dtype, bfloat16 or float32")
+    if k.shape != q.shape or v.shape != q.shape:
+        raise ValueError("q, k, v must have the same (B, H, T, D) shape")
+    L.require_cuda(q, k, v)
+    unit = 1.0 if kind == "softmax" else float(c)
+    has_sink = sink_logit is not None
+    sink = None
+    if has_sink:
+        s_in = torch.as_tensor(sink_logit, dtype=torch.float32, device=q.device)
+        sink = (torch.broadcast_to(torch.reshape(s_in, (-1,)), (H,)) / unit).contiguous()
+    cfg = build_config(kind, var, T, D, c, has_sink, range_guard)
+    return _Flash.apply(q.contiguous(), k.contiguous(), v.contiguous(), sink, cfg)

@@ -1,0 +1,606 @@
+// Attention: scale fold + range guard (prepare), the generic CUDA-core
+// forward/backward for every variant and I/O dtype, the di / sink-gradient
+// reductions, and the C-ABI entry points that dispatch between these and the
+// tcgen05 fast path (attn_tc.cu).
+//
+// The generic kernels restate kernels/flash.py:189-284 (forward) and
+// :333-361 (_tile_grads) one query row (or key row) per thread, with the
+// reference's rounding points: p is rounded to the value dtype before P.V
+// and dV, ds to the query dtype before dK/dQ, o to the query dtype. They
+// serve fp32 I/O, the shifted/softmax branches and shapes the fast path
+// does not take.
+#include <algorithm>
+
+#include "attn_common.cuh"
+#include "attn_tc.h"
+#include "tmap.h"
+#include "vec_io.cuh"
+
+namespace algx {
+namespace {
+
+constexpr int kD = 64;
+constexpr int kRows = 128;  // query (or key) rows per CTA, one per thread
+constexpr int kKT = 32;     // keys (or queries) per shared-memory tile
+constexpr int kPrepThreads = 256;
+
+// ------------------------------------------------------------------ prepare
+template <typename T>
+__global__ void __launch_bounds__(kPrepThreads) attn_prepare_kernel(const T* __restrict__ q,
+                                                                    const T* __restrict__ k,
+                                                                    const T* __restrict__ v,
+                                                                    const float* __restrict__ sink, int H,
+                                                                    T* __restrict__ qs, float* guard,
+                                                                    int64_t rows, float scale) {
+  using V = Vec<T>;
+  const int which = blockIdx.y;  // 0: q (scaled, written), 1: k, 2: v
+  const T* src = which == 0 ? q : (which == 1 ? k : v);
+  const int lane = threadIdx.x & 31;
+  const int sub = lane % V::TPR;
+  const int rl = lane / V::TPR;
+  const int64_t warps = (int64_t)gridDim.x * (kPrepThreads / 32);
+  const int64_t w = (int64_t)blockIdx.x * (kPrepThreads / 32) + (threadIdx.x >> 5);
+  float local = 0.f;
+  for (int64_t r0 = w * V::RPW; r0 < rows; r0 += warps * V::RPW) {
+    const int64_t row = r0 + rl;
+    const bool ok = row < rows;
+    float x[V::N];
+    uint4 raw = ok ? ld_stream(src + row * kD + sub * V::N) : make_uint4(0, 0, 0, 0);
+    unpack<T>(raw, x);
+    if (which == 2) {
+#pragma unroll
+      for (int i = 0; i < V::N; ++i) local = nan_max(local, fabsf(x[i]));
+    } else {
+      if (which == 0) {
+#pragma unroll
+        for (int i = 0; i < V::N; ++i) x[i] = round_io<T>(x[i] * scale);
+        if (ok) *reinterpret_cast<uint4*>(qs + row * kD + sub * V::N) = pack<T>(x);
+      }
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < V::N; ++i) ss = fmaf(x[i], x[i], ss);
+      ss = row_sum<V::TPR>(ss);
+      local = nan_max(local, ss);
+    }
+  }
+  __shared__ float red[kPrepThreads / 32];
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) local = nan_max(local, __shfl_xor_sync(0xffffffffu, local, off));
+  if (lane == 0) red[threadIdx.x >> 5] = local;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float m = 0.f;
+    for (int i = 0; i < kPrepThreads / 32; ++i) m = nan_max(m, red[i]);
+    atomic_max_nonneg(&guard[which], __int_as_float(__float_as_int(m) & 0x7fffffff));
+  }
+  if (which == 0 && blockIdx.x == 0 && sink != nullptr) {
+    for (int t = threadIdx.x; t < H; t += kPrepThreads) {
+      const float a = fabsf(sink[t]);
+      atomic_max_nonneg(&guard[3], __int_as_float(__float_as_int(a) & 0x7fffffff));
+    }
+  }
+}
+
+// ------------------------------------------------------------------ forward
+template <typename T>
+__global__ void __launch_bounds__(kRows) attn_fwd_generic(algx_attn_config cfg, const T* __restrict__ q,
+                                                          const T* __restrict__ k, const T* __restrict__ v,
+                                                          const float* __restrict__ sink,
+                                                          const float* __restrict__ guard, T* __restrict__ o,
+                                                          float* __restrict__ o_prec, float* __restrict__ stat,
+                                                          int H, int T_, int branch_mask) {
+  const Eff e = resolve_variant(cfg, guard);
+  if (!((branch_mask >> e.branch) & 1)) return;
+  __shared__ float ks[kKT][kD];
+  __shared__ float vs[kKT][kD];
+  const int bh = blockIdx.y;
+  const int h = bh % H;
+  const int row0 = blockIdx.x * kRows;
+  const int row = row0 + threadIdx.x;
+  const bool active = row < T_;
+  const size_t base = (size_t)bh * T_ * kD;
+  const int n = cfg.n;
+  float qr[kD], acc[kD];
+#pragma unroll
+  for (int d = 0; d < kD; ++d) {
+    qr[d] = active ? to_f32(q[base + (size_t)row * kD + d]) : 0.f;
+    acc[d] = 0.f;
+  }
+  const bool hs = cfg.has_sink != 0;
+  const float b = hs ? sink[h] : 0.f;
+  float m = 0.f, l = 0.f, r;
+  if (e.branch == BR_UNSHIFTED) {
+    if (hs) l = ipow(rho_sel(e.clip ? fminf(b, cfg.clamp) : b, e.fast, r), n);
+  } else if (hs) {
+    m = b;
+    l = 1.f;
+  } else {
+    m = -1e4f;
+  }
+  bool first = true;
+  const int last = min(T_, row0 + kRows) - 1;
+  const int ntiles = last / kKT + 1;
+  for (int t = 0; t < ntiles; ++t) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < kKT * kD; i += kRows) {
+      const int j = i / kD, d = i % kD, key = t * kKT + j;
+      ks[j][d] = key < T_ ? to_f32(k[base + (size_t)key * kD + d]) : 0.f;
+      vs[j][d] = key < T_ ? to_f32(v[base + (size_t)key * kD + d]) : 0.f;
+    }
+    __syncthreads();
+    if (!active || t * kKT > row) continue;
+    const int nvalid = min(kKT, row - t * kKT + 1);
+    float s[kKT];
+#pragma unroll
+    for (int j = 0; j < kKT; ++j) {
+      float a = 0.f;
+#pragma unroll
+      for (int d = 0; d < kD; ++d) a = fmaf(qr[d], ks[j][d], a);
+      s[j] = a;
+    }
+    if (e.branch == BR_UNSHIFTED) {
+#pragma unroll
+      for (int j = 0; j < kKT; ++j) {
+        if (j < nvalid) {
+          const float x = e.clip ? fminf(s[j], cfg.clamp) : s[j];
+          const float p = ipow(rho_sel(x, e.fast, r), n);
+          l += p;
+          const float pb = round_io<T>(p);
+#pragma unroll
+          for (int d = 0; d < kD; ++d) acc[d] = fmaf(pb, vs[j][d], acc[d]);
+        }
+      }
+    } else {
+      float tmax = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < kKT; ++j)
+        if (j < nvalid) tmax = fmaxf(tmax, s[j]);
+      float m_new = fmaxf(m, tmax), m_prev = m;
+      if (!hs && first) {
+        m_new = tmax;
+        m_prev = m_new;
+      }
+      float alpha, shift = 1.f;
+      if (e.branch == BR_SOFTMAX) {
+        alpha = expf(m_prev - m_new);
+      } else {
+        shift = rho_exact(-m_new, r);
+        alpha = ipow(rho_exact(m_prev, r) * shift, n);
+      }
+      l *= alpha;
+#pragma unroll
+      for (int d = 0; d < kD; ++d) acc[d] *= alpha;
+#pragma unroll
+      for (int j = 0; j < kKT; ++j) {
+        if (j < nvalid) {
+          const float p = e.branch == BR_SOFTMAX ? expf(s[j] - m_new)
+                                                 : ipow(rho_sel(s[j], e.fast, r) * shift, n);
+          l += p;
+          const float pb = round_io<T>(p);
+#pragma unroll
+          for (int d = 0; d < kD; ++d) acc[d] = fmaf(pb, vs[j][d], acc[d]);
+        }
+      }
+      m = m_new;
+      first = false;
+    }
+  }
+  if (!active) return;
+  const float inv = 1.f / l;
+  const size_t ob = base + (size_t)row * kD;
+#pragma unroll
+  for (int d = 0; d < kD; ++d) {
+    const float ov = acc[d] * inv;
+    o[ob + d] = from_f32<T>(ov);
+    if (e.precise && o_prec) o_prec[ob + d] = ov;
+  }
+  float st;
+  if (e.branch == BR_UNSHIFTED)
+    st = e.inv_stat ? inv : inv_root(l, n);
+  else if (e.branch == BR_SHIFTED)
+    st = rho_exact(-m, r) * inv_root(l, n);
+  else
+    st = m + logf(l);
+  stat[(size_t)bh * T_ + row] = st;
+}
+
+// ------------------------------------------------------------------ backward
+// di = sum_d dO*O (flash.py:633) per row, plus per-block partial sums of
+// mass*di for the sink gradient (flash.py:694-705, 721-723).
+template <typename T>
+__global__ void __launch_bounds__(256) attn_di_kernel(algx_attn_config cfg, const float* __restrict__ guard,
+                                                      const T* __restrict__ o, const float* __restrict__ o_prec,
+                                                      const T* __restrict__ dout, const float* __restrict__ stat,
+                                                      const float* __restrict__ sink, float* __restrict__ di,
+                                                      float* __restrict__ sink_part, int H, int T_) {
+  const Eff e = resolve_variant(cfg, guard);
+  const int bh = blockIdx.y, h = bh % H;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = blockIdx.x * kRows;
+  const bool hs = cfg.has_sink != 0;
+  float rb = 1.f, r;
+  const float b = hs ? sink[h] : 0.f;
+  if (hs && e.branch != BR_SOFTMAX) rb = rho_exact(e.clip ? fminf(b, cfg.clamp) : b, r);
+  float part = 0.f;
+  for (int i = warp; i < kRows; i += 8) {
+    const int row = row0 + i;
+    if (row >= T_) break;
+    const size_t off = ((size_t)bh * T_ + row) * kD + 2 * lane;
+    float o0, o1;
+    if (e.precise && o_prec) {
+      o0 = o_prec[off];
+      o1 = o_prec[off + 1];
+    } else {
+      o0 = to_f32(o[off]);
+      o1 = to_f32(o[off + 1]);
+    }
+    float s = to_f32(dout[off]) * o0 + to_f32(dout[off + 1]) * o1;
+#pragma unroll
+    for (int x = 16; x > 0; x >>= 1) s += __shfl_xor_sync(0xffffffffu, s, x);
+    if (lane == 0) {
+      di[(size_t)bh * T_ + row] = s;
+      if (hs) {
+        const float st = stat[(size_t)bh * T_ + row];
+        float mass;
+        if (e.branch == BR_SOFTMAX)
+          mass = expf(b - st);
+        else if (e.branch == BR_UNSHIFTED && e.inv_stat)
+          mass = ipow(rb, cfg.n) * st;
+        else
+          mass = ipow(rb * st, cfg.n);
+        part += mass * s;
+      }
+    }
+  }
+  if (!hs) return;
+  __shared__ float red[8];
+  if (lane == 0) red[warp] = part;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int i = 0; i < 8; ++i) t += red[i];
+    sink_part[(size_t)bh * gridDim.x + blockIdx.x] = t;
+  }
+}
+
+// dsink[h] = -slope(h) * sum_{b, blocks} partial  (fixed summation order).
+__global__ void attn_dsink_kernel(algx_attn_config cfg, const float* __restrict__ guard,
+                                  const float* __restrict__ sink, const float* __restrict__ sink_part, int B,
+                                  int H, int nblk, float* __restrict__ dsink) {
+  const int h = threadIdx.x;
+  if (h >= H) return;
+  const Eff e = resolve_variant(cfg, guard);
+  float s = 0.f;
+  for (int b = 0; b < B; ++b)
+    for (int i = 0; i < nblk; ++i) s += sink_part[((size_t)b * H + h) * nblk + i];
+  float slope = 1.f, r;
+  if (e.branch != BR_SOFTMAX) {
+    const float bb = e.clip ? fminf(sink[h], cfg.clamp) : sink[h];
+    rho_exact(bb, r);
+    slope = (float)cfg.n * r;
+    if (e.clip && !(sink[h] < cfg.clamp)) slope = 0.f;
+  }
+  dsink[h] = -s * slope;
+}
+
+// p and ds of one score (flash.py:333-361), ds without the slope n.
+struct PDs {
+  float p, ds;
+};
+__device__ __forceinline__ PDs tile_grad(const Eff& e, const algx_attn_config& cfg, float s, float dp, float st,
+                                         float dii) {
+  float p, r = 1.f;
+  if (e.branch == BR_SOFTMAX) {
+    p = expf(s - st);
+  } else {
+    const float x = e.clip ? fminf(s, cfg.clamp) : s;
+    const float rho = rho_sel(x, e.fast, r);
+    p = (e.branch == BR_UNSHIFTED && e.inv_stat) ? ipow(rho, cfg.n) * st : ipow(rho * st, cfg.n);
+  }
+  float ds = p * (dp - dii);
+  if (e.branch != BR_SOFTMAX) {
+    ds *= r;
+    if (e.clip && !(s < cfg.clamp)) ds = 0.f;
+  }
+  return {p, ds};
+}
+
+// dK, dV: one key row per thread; query tiles streamed through shared memory.
+template <typename T>
+__global__ void __launch_bounds__(kRows) attn_dkdv_generic(algx_attn_config cfg, const T* __restrict__ q,
+                                                           const T* __restrict__ k, const T* __restrict__ v,
+                                                           const T* __restrict__ dout,
+                                                           const float* __restrict__ stat,
+                                                           const float* __restrict__ di,
+                                                           const float* __restrict__ guard, T* __restrict__ dk,
+                                                           T* __restrict__ dv, int T_, int branch_mask) {
+  const Eff e = resolve_variant(cfg, guard);
+  if (!((branch_mask >> e.branch) & 1)) return;
+  extern __shared__ float smem[];
+  float(*kown)[kD + 1] = reinterpret_cast<float(*)[kD + 1]>(smem);
+  float(*vown)[kD + 1] = reinterpret_cast<float(*)[kD + 1]>(smem + kRows * (kD + 1));
+  float(*qt)[kD] = reinterpret_cast<float(*)[kD]>(smem + 2 * kRows * (kD + 1));
+  float(*dot)[kD] = reinterpret_cast<float(*)[kD]>(smem + 2 * kRows * (kD + 1) + kKT * kD);
+  float* st = smem + 2 * kRows * (kD + 1) + 2 * kKT * kD;
+  float* dit = st + kKT;
+  const int bh = blockIdx.y;
+  const int key0 = blockIdx.x * kRows;
+  const int key = key0 + threadIdx.x;
+  const bool active = key < T_;
+  const size_t base = (size_t)bh * T_ * kD;
+  for (int i = threadIdx.x; i < kRows * kD; i += kRows) {
+    const int j = i / kD, d = i % kD, kk = key0 + j;
+    kown[j][d] = kk < T_ ? to_f32(k[base + (size_t)kk * kD + d]) : 0.f;
+    vown[j][d] = kk < T_ ? to_f32(v[base + (size_t)kk * kD + d]) : 0.f;
+  }
+  float dka[kD], dva[kD];
+#pragma unroll
+  for (int d = 0; d < kD; ++d) dka[d] = dva[d] = 0.f;
+  const int t0 = key0 / kKT;
+  const int ntiles = (T_ + kKT - 1) / kKT;
+  for (int t = t0; t < ntiles; ++t) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < kKT * kD; i += kRows) {
+      const int j = i / kD, d = i % kD, qi = t * kKT + j;
+      qt[j][d] = qi < T_ ? to_f32(q[base + (size_t)qi * kD + d]) : 0.f;
+      dot[j][d] = qi < T_ ? to_f32(dout[base + (size_t)qi * kD + d]) : 0.f;
+    }
+    if (threadIdx.x < kKT) {
+      const int qi = t * kKT + threadIdx.x;
+      st[threadIdx.x] = qi < T_ ? stat[(size_t)bh * T_ + qi] : 0.f;
+      dit[threadIdx.x] = qi < T_ ? di[(size_t)bh * T_ + qi] : 0.f;
+    }
+    __syncthreads();
+    if (!active) continue;
+    for (int j = 0; j < kKT; ++j) {
+      const int qi = t * kKT + j;
+      if (qi < key || qi >= T_) continue;
+      float s = 0.f, dp = 0.f;
+#pragma unroll
+      for (int d = 0; d < kD; ++d) {
+        s = fmaf(qt[j][d], kown[threadIdx.x][d], s);
+        dp = fmaf(dot[j][d], vown[threadIdx.x][d], dp);
+      }
+      const PDs g = tile_grad(e, cfg, s, dp, st[j], dit[j]);
+      const float pb = round_io<T>(g.p), dsb = round_io<T>(g.ds);
+#pragma unroll
+      for (int d = 0; d < kD; ++d) {
+        dva[d] = fmaf(pb, dot[j][d], dva[d]);
+        dka[d] = fmaf(dsb, qt[j][d], dka[d]);
+      }
+    }
+  }
+  if (!active) return;
+  const float slope = e.branch == BR_SOFTMAX ? 1.f : (float)cfg.n;
+  const size_t ob = base + (size_t)key * kD;
+#pragma unroll
+  for (int d = 0; d < kD; ++d) {
+    dk[ob + d] = from_f32<T>(dka[d] * slope);
+    dv[ob + d] = from_f32<T>(dva[d]);
+  }
+}
+
+// dQ: one query row per thread; key tiles streamed through shared memory.
+template <typename T>
+__global__ void __launch_bounds__(kRows) attn_dq_generic(algx_attn_config cfg, const T* __restrict__ q,
+                                                         const T* __restrict__ k, const T* __restrict__ v,
+                                                         const T* __restrict__ dout, const float* __restrict__ stat,
+                                                         const float* __restrict__ di,
+                                                         const float* __restrict__ guard, T* __restrict__ dq,
+                                                         int T_, int branch_mask) {
+  const Eff e = resolve_variant(cfg, guard);
+  if (!((branch_mask >> e.branch) & 1)) return;
+  extern __shared__ float smem[];
+  float(*qown)[kD + 1] = reinterpret_cast<float(*)[kD + 1]>(smem);
+  float(*down)[kD + 1] = reinterpret_cast<float(*)[kD + 1]>(smem + kRows * (kD + 1));
+  float(*kt)[kD] = reinterpret_cast<float(*)[kD]>(smem + 2 * kRows * (kD + 1));
+  float(*vt)[kD] = reinterpret_cast<float(*)[kD]>(smem + 2 * kRows * (kD + 1) + kKT * kD);
+  const int bh = blockIdx.y;
+  const int row0 = blockIdx.x * kRows;
+  const int row = row0 + threadIdx.x;
+  const bool active = row < T_;
+  const size_t base = (size_t)bh * T_ * kD;
+  for (int i = threadIdx.x; i < kRows * kD; i += kRows) {
+    const int j = i / kD, d = i % kD, qi = row0 + j;
+    qown[j][d] = qi < T_ ? to_f32(q[base + (size_t)qi * kD + d]) : 0.f;
+    down[j][d] = qi < T_ ? to_f32(dout[base + (size_t)qi * kD + d]) : 0.f;
+  }
+  const float myst = active ? stat[(size_t)bh * T_ + row] : 0.f;
+  const float mydi = active ? di[(size_t)bh * T_ + row] : 0.f;
+  float dqa[kD];
+#pragma unroll
+  for (int d = 0; d < kD; ++d) dqa[d] = 0.f;
+  const int last = min(T_, row0 + kRows) - 1;
+  const int ntiles = last / kKT + 1;
+  for (int t = 0; t < ntiles; ++t) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < kKT * kD; i += kRows) {
+      const int j = i / kD, d = i % kD, kk = t * kKT + j;
+      kt[j][d] = kk < T_ ? to_f32(k[base + (size_t)kk * kD + d]) : 0.f;
+      vt[j][d] = kk < T_ ? to_f32(v[base + (size_t)kk * kD + d]) : 0.f;
+    }
+    __syncthreads();
+    if (!active) continue;
+    for (int j = 0; j < kKT; ++j) {
+      const int kk = t * kKT + j;
+      if (kk > row) break;
+      float s = 0.f, dp = 0.f;
+#pragma unroll
+      for (int d = 0; d < kD; ++d) {
+        s = fmaf(qown[threadIdx.x][d], kt[j][d], s);
+        dp = fmaf(down[threadIdx.x][d], vt[j][d], dp);
+      }
+      const PDs g = tile_grad(e, cfg, s, dp, myst, mydi);
+      const float dsb = round_io<T>(g.ds);
+#pragma unroll
+      for (int d = 0; d < kD; ++d) dqa[d] = fmaf(dsb, kt[j][d], dqa[d]);
+    }
+  }
+  if (!active) return;
+  const float f = (e.branch == BR_SOFTMAX ? 1.f : (float)cfg.n) * cfg.scale;
+  const size_t ob = base + (size_t)row * kD;
+#pragma unroll
+  for (int d = 0; d < kD; ++d) dq[ob + d] = from_f32<T>(dqa[d] * f);
+}
+
+constexpr size_t kGenericBwdSmem = (2 * kRows * (kD + 1) + 2 * kKT * kD + 2 * kKT) * sizeof(float);
+
+int check_attn(const algx_attn_config* cfg, int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype) {
+  ALGX_REQUIRE(cfg, "attention: NULL config");
+  ALGX_REQUIRE(D == kD, "attention: head dim must be 64");
+  ALGX_REQUIRE(B >= 1 && H >= 1 && T >= 1, "attention: empty shape");
+  ALGX_REQUIRE(T <= (1 << 24) && B * H <= 65535, "attention: shape too large");
+  ALGX_REQUIRE(H <= 1024, "attention: at most 1024 heads");
+  ALGX_REQUIRE(dtype == ALGX_F32 || dtype == ALGX_BF16, "attention: dtype must be float32 or bfloat16");
+  ALGX_REQUIRE(cfg->kind == ALGX_ATTN_ASINH || cfg->kind == ALGX_ATTN_SOFTMAX, "attention: unknown kind");
+  if (cfg->kind == ALGX_ATTN_ASINH) {
+    ALGX_REQUIRE(cfg->n >= 2 && (cfg->n & (cfg->n - 1)) == 0, "asinh kernel needs n to be a power of two");
+    ALGX_REQUIRE(cfg->mode >= ALGX_MODE_CLIPPED && cfg->mode <= ALGX_MODE_GUARDED, "attention: unknown mode");
+  }
+  return ALGX_OK;
+}
+
+size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+}  // namespace
+
+// Backward workspace layout: [di (B*H*T fp32) | sink partials | fast-path area].
+size_t ws_off_sink(int64_t B, int64_t H, int64_t T) { return align256((size_t)B * H * T * sizeof(float)); }
+size_t ws_off_tc(int64_t B, int64_t H, int64_t T) {
+  const int64_t nblk = (T + kRows - 1) / kRows;
+  return ws_off_sink(B, H, T) + align256((size_t)B * H * nblk * sizeof(float));
+}
+
+}  // namespace algx
+
+using namespace algx;
+
+extern "C" {
+
+int algx_attn_prepare(const algx_attn_config* cfg, const void* q, const void* k, const void* v, const float* sink,
+                      void* q_scaled, float* guard, int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype,
+                      void* stream) {
+  if (int s = check_attn(cfg, B, H, T, D, dtype)) return s;
+  ALGX_REQUIRE(q && k && v && q_scaled && guard, "attn_prepare: NULL pointer");
+  ALGX_REQUIRE(!cfg->has_sink || sink, "attn_prepare: has_sink without a sink pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  ALGX_CUDA(cudaMemsetAsync(guard, 0, 4 * sizeof(float), st));
+  const int64_t rows = B * H * T;
+  const int64_t rows_per_block = (kPrepThreads / 32) * (dtype == ALGX_BF16 ? 4 : 2);
+  const int gx = (int)std::min<int64_t>((rows + rows_per_block - 1) / rows_per_block, 148 * 8);
+  dim3 grid(gx, 3);
+  const float* sk = cfg->has_sink ? sink : nullptr;
+  if (dtype == ALGX_BF16)
+    attn_prepare_kernel<__nv_bfloat16><<<grid, kPrepThreads, 0, st>>>(
+        (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, sk, (int)H,
+        (__nv_bfloat16*)q_scaled, guard, rows, cfg->scale);
+  else
+    attn_prepare_kernel<float><<<grid, kPrepThreads, 0, st>>>((const float*)q, (const float*)k, (const float*)v,
+                                                              sk, (int)H, (float*)q_scaled, guard, rows,
+                                                              cfg->scale);
+  ALGX_LAUNCHED("attn_prepare launch");
+  return ALGX_OK;
+}
+
+int algx_attn_fwd(const algx_attn_config* cfg, const void* q_scaled, const void* k, const void* v, const float* sink,
+                  const float* guard, void* o, float* o_precise, float* stat, int64_t B, int64_t H, int64_t T,
+                  int64_t D, int32_t dtype, void* stream) {
+  if (int s = check_attn(cfg, B, H, T, D, dtype)) return s;
+  ALGX_REQUIRE(q_scaled && k && v && guard && o && stat, "attn_fwd: NULL pointer");
+  ALGX_REQUIRE(!cfg->has_sink || sink, "attn_fwd: has_sink without a sink pointer");
+  ALGX_REQUIRE(cfg->kind != ALGX_ATTN_ASINH || cfg->mode != ALGX_MODE_GUARDED || o_precise,
+               "attn_fwd: guarded mode needs o_precise");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int mask = 7;
+  bool fast = false;
+  if (int s = tc_attn_fwd(*cfg, q_scaled, k, v, sink, guard, o, stat, B, H, T, dtype, st, &fast)) return s;
+  if (fast) mask = 1 << BR_SHIFTED | 1 << BR_SOFTMAX;  // the fast kernel covers the unshifted branch
+  dim3 grid((unsigned)((T + kRows - 1) / kRows), (unsigned)(B * H));
+  if (dtype == ALGX_BF16)
+    attn_fwd_generic<__nv_bfloat16><<<grid, kRows, 0, st>>>(*cfg, (const __nv_bfloat16*)q_scaled,
+                                                             (const __nv_bfloat16*)k, (const __nv_bfloat16*)v,
+                                                             sink, guard, (__nv_bfloat16*)o, o_precise, stat,
+                                                             (int)H, (int)T, mask);
+  else
+    attn_fwd_generic<float><<<grid, kRows, 0, st>>>(*cfg, (const float*)q_scaled, (const float*)k, (const float*)v,
+                                                    sink, guard, (float*)o, o_precise, stat, (int)H, (int)T, mask);
+  ALGX_LAUNCHED("attn_fwd_generic launch");
+  return ALGX_OK;
+}
+
+size_t algx_attn_bwd_workspace_size(int64_t B, int64_t H, int64_t T, int64_t D) {
+  return ws_off_tc(B, H, T) + tc_attn_bwd_workspace(B, H, T, D);
+}
+
+int algx_attn_bwd(const algx_attn_config* cfg, const void* q_scaled, const void* k, const void* v, const float* sink,
+                  const float* guard, const void* o, const float* o_precise, const float* stat, const void* dout,
+                  void* dq, void* dk, void* dv, float* dsink, int64_t B, int64_t H, int64_t T, int64_t D,
+                  int32_t dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int s = check_attn(cfg, B, H, T, D, dtype)) return s;
+  ALGX_REQUIRE(q_scaled && k && v && guard && o && stat && dout && dq && dk && dv, "attn_bwd: NULL pointer");
+  ALGX_REQUIRE(!cfg->has_sink || (sink && dsink), "attn_bwd: has_sink needs sink and dsink");
+  ALGX_REQUIRE(workspace && workspace_bytes >= algx_attn_bwd_workspace_size(B, H, T, D),
+               "attn_bwd: workspace too small (see algx_attn_bwd_workspace_size)");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  float* di = reinterpret_cast<float*>(ws);
+  float* sink_part = reinterpret_cast<float*>(ws + ws_off_sink(B, H, T));
+  void* tc_ws = ws + ws_off_tc(B, H, T);
+  const int nblk = (int)((T + kRows - 1) / kRows);
+  dim3 grid((unsigned)nblk, (unsigned)(B * H));
+  if (dtype == ALGX_BF16)
+    attn_di_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(*cfg, guard, (const __nv_bfloat16*)o, o_precise,
+                                                        (const __nv_bfloat16*)dout, stat, sink, di, sink_part,
+                                                        (int)H, (int)T);
+  else
+    attn_di_kernel<float><<<grid, 256, 0, st>>>(*cfg, guard, (const float*)o, o_precise, (const float*)dout, stat,
+                                                sink, di, sink_part, (int)H, (int)T);
+  ALGX_LAUNCHED("attn_di launch");
+  if (cfg->has_sink) {
+    attn_dsink_kernel<<<1, (unsigned)((H + 31) / 32 * 32), 0, st>>>(*cfg, guard, sink, sink_part, (int)B, (int)H,
+                                                                    nblk, dsink);
+    ALGX_LAUNCHED("attn_dsink launch");
+  }
+  int mask = 7;
+  bool fast = false;
+  if (int s = tc_attn_bwd(*cfg, q_scaled, k, v, dout, stat, di, guard, dq, dk, dv, tc_ws, B, H, T, dtype, st,
+                          &fast))
+    return s;
+  if (fast) mask = 1 << BR_SHIFTED | 1 << BR_SOFTMAX;
+  int dev = 0;
+  ALGX_CUDA(cudaGetDevice(&dev));
+  static bool attr_set[64][2] = {};
+  if (dev >= 0 && dev < 64 && !attr_set[dev][dtype]) {
+    if (dtype == ALGX_BF16) {
+      ALGX_CUDA(cudaFuncSetAttribute(attn_dkdv_generic<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kGenericBwdSmem));
+      ALGX_CUDA(cudaFuncSetAttribute(attn_dq_generic<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kGenericBwdSmem));
+    } else {
+      ALGX_CUDA(cudaFuncSetAttribute(attn_dkdv_generic<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kGenericBwdSmem));
+      ALGX_CUDA(cudaFuncSetAttribute(attn_dq_generic<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)kGenericBwdSmem));
+    }
+    attr_set[dev][dtype] = true;
+  }
+  if (dtype == ALGX_BF16) {
+    attn_dkdv_generic<__nv_bfloat16><<<grid, kRows, kGenericBwdSmem, st>>>(
+        *cfg, (const __nv_bfloat16*)q_scaled, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v,
+        (const __nv_bfloat16*)dout, stat, di, guard, (__nv_bfloat16*)dk, (__nv_bfloat16*)dv, (int)T, mask);
+    attn_dq_generic<__nv_bfloat16><<<grid, kRows, kGenericBwdSmem, st>>>(
+        *cfg, (const __nv_bfloat16*)q_scaled, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v,
+        (const __nv_bfloat16*)dout, stat, di, guard, (__nv_bfloat16*)dq, (int)T, mask);
+  } else {
+    attn_dkdv_generic<float><<<grid, kRows, kGenericBwdSmem, st>>>(*cfg, (const float*)q_scaled, (const float*)k,
+                                                                   (const float*)v, (const float*)dout, stat, di,
+                                                                   guard, (float*)dk, (float*)dv, (int)T, mask);
+    attn_dq_generic<float><<<grid, kRows, kGenericBwdSmem, st>>>(*cfg, (const float*)q_scaled, (const float*)k,
+                                                                 (const float*)v, (const float*)dout, stat, di,
+                                                                 guard, (float*)dq, (int)T, mask);
+  }
+  ALGX_LAUNCHED("attn_bwd_generic launch");
+  return ALGX_OK;
+}
+
+}  // extern "C"

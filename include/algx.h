@@ -1,0 +1,128 @@
+/*
+ * libalgx: C ABI of the B200 (sm_100a) kernels for the Algebraic Transformer
+ * hot path (asinh-power flash attention, fused LM head, QK RMS norm).
+ *
+ * Conventions for every entry point:
+ *   - pointers are device pointers unless stated; tensors are contiguous,
+ *     row-major; attention tensors are (B, H, T, D), D = 64;
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream);
+ *   - the library never allocates device memory on a call path: the caller
+ *     passes outputs and any workspace (sized by the *_workspace_size query);
+ *   - calls are stream-ordered and never synchronize the host;
+ *   - the return value is an algx status; on failure algx_last_error()
+ *     returns a message for the calling thread.
+ *
+ * Each declaration names the reference function it replaces
+ * (paths relative to the reference project, tasmaikeni13/algebraic-extra).
+ */
+#ifndef ALGX_H_
+#define ALGX_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ALGX_API __attribute__((visibility("default")))
+#else
+#define ALGX_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum { ALGX_OK = 0, ALGX_ERR_INVALID = 1, ALGX_ERR_UNSUPPORTED = 2, ALGX_ERR_CUDA = 3 };
+enum { ALGX_F32 = 0, ALGX_BF16 = 1 };
+enum { ALGX_ATTN_ASINH = 0, ALGX_ATTN_SOFTMAX = 1 };
+/* asinh accumulation strategy (kernels/flash.py:9-22):
+ *   CLIPPED  unshifted, scores clamped above at `clamp` (explicit shift=False);
+ *   SHIFTED  running maximum with rho(-m) shifts (explicit shift=True);
+ *   GUARDED  range_guard=True: the device picks unshifted-unclamped when the
+ *            Cauchy-Schwarz guard passes, else shifted with exact rho. */
+enum { ALGX_MODE_CLIPPED = 0, ALGX_MODE_SHIFTED = 1, ALGX_MODE_GUARDED = 2 };
+enum { ALGX_HEAD_CE = 0, ALGX_HEAD_ALG_CE = 1 };
+
+/* Message of the last failed call on this thread. */
+ALGX_API const char* algx_last_error(void);
+/* Library version (major*10000 + minor*100 + patch). */
+ALGX_API int algx_version(void);
+/* Reads and clears the device error word of the current device (bounded
+ * waits that gave up set it). Synchronizes the device. */
+ALGX_API int algx_device_error(int32_t* code);
+
+/* ------------------------------------------------------------------ QK norm */
+
+/* y = rms_norm(x) * gain over rows of `dim` (= 64) elements.
+ * Replaces kernels/qk_norm.py:62-76 `qk_rms_norm` forward (algebraic.py:76-83). */
+ALGX_API int algx_qknorm_fwd(const void* x, const float* gain, void* y, int64_t rows, int64_t dim,
+                    int32_t dtype, float eps, void* stream);
+
+/* Bytes of workspace algx_qknorm_bwd needs. */
+ALGX_API size_t algx_qknorm_bwd_workspace_size(int64_t rows, int64_t dim);
+
+/* dx and dgain of the QK norm. Replaces kernels/qk_norm.py:39-55 `_norm_bwd`
+ * (dx by the AD formula of rms_norm, dgain = sum_rows dy * x * tau). */
+ALGX_API int algx_qknorm_bwd(const void* x, const float* gain, const void* dy, void* dx, float* dgain,
+                    int64_t rows, int64_t dim, int32_t dtype, float eps, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------- attention */
+
+/* Resolved variant of kernels/flash.py:732-760 plus the wrapper's constants. */
+typedef struct algx_attn_config {
+  int32_t kind;     /* ALGX_ATTN_ASINH or ALGX_ATTN_SOFTMAX */
+  int32_t mode;     /* ALGX_MODE_* (asinh only) */
+  int32_t n;        /* weight power, a power of two >= 2 */
+  int32_t fast_rho; /* 1: rho(x) = x + rad*rsqrt(rad) (flash.py:83-88) */
+  int32_t inv_stat; /* unshifted row statistic: 1 -> 1/Z, 0 -> Z^(-1/n) */
+  int32_t has_sink; /* sink logit present (kernel units, shape (H,)) */
+  float clamp;      /* make_variant clamp, kernel units (flash.py:747-748) */
+  float scale;      /* 1/(sqrt(D)*unit), folded into q (flash.py:823-833) */
+  float guard_qk;   /* (bound/1.01)^2 (flash.py:840-843) */
+  float guard_sink; /* bound/1.01 (flash.py:844-845) */
+  float guard_v;    /* vmax (flash.py:848-849) */
+} algx_attn_config;
+
+/* q_scaled = (q*scale) rounded to the I/O dtype, and the range-guard maxima
+ * guard[0] = max ||q_scaled||^2, guard[1] = max ||k||^2, guard[2] = max |v|,
+ * guard[3] = max |sink| (guard: 4 device floats, overwritten).
+ * Replaces the XLA glue of kernels/flash.py:823-849. */
+ALGX_API int algx_attn_prepare(const algx_attn_config* cfg, const void* q, const void* k, const void* v,
+                      const float* sink, void* q_scaled, float* guard, int64_t B, int64_t H,
+                      int64_t T, int64_t D, int32_t dtype, void* stream);
+
+/* Causal forward: o (I/O dtype), stat (B,H,T) fp32, and on the shifted
+ * guard fallback the unrounded output o_precise (B,H,T,D) fp32 (nullable when
+ * cfg->mode != GUARDED). Replaces kernels/flash.py:189-326 `_forward` and
+ * kernels/head_resident.py:24-155 `forward`. */
+ALGX_API int algx_attn_fwd(const algx_attn_config* cfg, const void* q_scaled, const void* k, const void* v,
+                  const float* sink, const float* guard, void* o, float* o_precise, float* stat,
+                  int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype, void* stream);
+
+/* Bytes of workspace algx_attn_bwd needs. */
+ALGX_API size_t algx_attn_bwd_workspace_size(int64_t B, int64_t H, int64_t T, int64_t D);
+
+/* Causal backward: dq (with the scale fold applied, i.e. d/dq of the
+ * unscaled q), dk, dv and, when cfg->has_sink, dsink (H,) fp32 in kernel
+ * units. Replaces kernels/flash.py:630-642 `_backward` (+ :435-627,
+ * head_resident.py:95-176) and the sink VJP of flash.py:694-726. */
+ALGX_API int algx_attn_bwd(const algx_attn_config* cfg, const void* q_scaled, const void* k, const void* v,
+                  const float* sink, const float* guard, const void* o, const float* o_precise,
+                  const float* stat, const void* dout, void* dq, void* dk, void* dv, float* dsink,
+                  int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
+/* --------------------------------------------------------------- diagnostics */
+
+/* One-CTA tcgen05/TMA self-test: D = A*B for the operand layouts the
+ * attention kernels use (mode 0: SS K-major x K-major, N=128; 1: B MN-major;
+ * 2: A from TMEM; 3: A MN-major; 4: N=256). Inputs are bf16 device buffers:
+ * a (128 x ka, row-major; for mode 3 the transpose 128 x 128), b (nb x kb).
+ * out: fp32 128 x nout. No counterpart in the reference (hardware check). */
+ALGX_API int algx_selftest_tcgen05(int32_t mode, const void* a, const void* b, float* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ALGX_H_ */

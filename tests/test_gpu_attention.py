@@ -1,0 +1,210 @@
+"""Attention kernels vs the float64 oracle.
+
+Cases and tolerances port tests/test_flash_kernel_tpu.py of the reference
+(file:line cited per test), plus the golden fixtures made from the
+reference's own dense code and the BASELINE fp32 bar (1e-3 relative).
+"""
+
+import math
+import os
+from functools import partial
+
+import numpy as np
+import pytest
+import torch
+
+from algx.kernels.flash import flash_attention
+from oracle import reference_math as R
+from tests.golden import cases
+from tests.gpu_util import algx_attention, dump, oracle_attention, rel_l2
+
+pytestmark = pytest.mark.gpu
+
+GOLD = np.load(os.path.join(os.path.dirname(__file__), "golden", "reference_dense.npz"))
+
+CASES = [("asinh", 16, 16.0, True, True, False), ("asinh", 16, 16.0, True, True, True),
+         ("asinh", 16, 16.0, True, False, True), ("asinh", 16, 16.0, False, False, True),
+         ("asinh", 8, 1.0, True, True, False), ("asinh", 32, 8.0, False, True, True)]
+
+
+def _randn(seed, shape, dtype=torch.float32, scale=1.0):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(shape, generator=g) * scale).to(dtype)
+
+
+@pytest.mark.parametrize("kind,n,c,with_sink,shift,fast", CASES)
+@pytest.mark.parametrize("block", [128, 256])
+def test_flash_matches_dense(kind, n, c, with_sink, shift, fast, block):
+    """test_flash_kernel_tpu.py:38-66 (fp32, atol/rtol 2e-3, grads 3e-3 max-normalised)."""
+    B, H, T, D = 2, 3, 512, 64
+    q = _randn(1, (B, H, T, D), scale=1.5)
+    k = _randn(2, (B, H, T, D), scale=1.5)
+    v = _randn(3, (B, H, T, D))
+    g = _randn(4, (B, H, T, D))
+    sink = (_randn(5, (H,)) * 0.5).reshape(1, H, 1, 1) if with_sink else None
+    fn = partial(flash_attention, kind=kind, n=n, c=c, block=block, shift=shift, fast_rho=fast)
+    got = algx_attention(fn, *(t.cuda() for t in (q, k, v, g)), None if sink is None else sink.cuda())
+    want = R.attention_grads(lambda a, b, c_, s: R.asinh_attention(a, b, c_, n=n, c=c, sink_logit=s),
+                             q.double(), k.double(), v.double(), g.double(),
+                             None if sink is None else sink.double())
+    np.testing.assert_allclose(got[0].cpu().double(), want[0], atol=2e-3, rtol=2e-3)
+    for a, b in zip(got[1:], want[1:]):
+        if b is None:
+            continue
+        scale = float(b.abs().max()) + 1e-6
+        np.testing.assert_allclose(a.cpu().double() / scale, b / scale, atol=3e-3)
+
+
+@pytest.mark.parametrize("mode", ["root", "inverse", "compact", "guarded", "polynomial"])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_model_attention_statistics(mode, dtype):
+    """test_flash_kernel_tpu.py:69-97 (n=16, c=8, learned sink; bf16 rel-L2 .02, fp32 .005)."""
+    shape = (1, 2, 512, 64)
+    q, k, v, g = (_randn(13 + i, shape, dtype) for i in range(4))
+    sink = _randn(17, (1, 2, 1, 1))
+    fn = partial(flash_attention, kind="asinh", n=16, c=8., shift=False, fast_rho=True,
+                 inv_stat=mode != "root", compact_stat=mode in ("compact", "guarded"),
+                 range_guard=mode == "guarded", poly_rho=mode == "polynomial")
+    got = algx_attention(fn, *(t.cuda() for t in (q, k, v, g)), sink.cuda())
+    io = None if dtype == torch.float32 else torch.bfloat16
+    want = oracle_attention(q, k, v, g, sink, io_dtype=io, kind="asinh", n=16, c=8.,
+                            range_guard=mode == "guarded", shift=False)
+    np.testing.assert_allclose(got[0].float().cpu(), want[0].float(), atol=.012, rtol=.012)
+    lim = .02 if dtype == torch.bfloat16 else .005
+    for name, a, b in zip(("dq", "dk", "dv", "dsink"), got[1:], want[1:]):
+        assert rel_l2(a, b) < lim, name
+
+
+@pytest.mark.parametrize("score_sign", [-1., 1.])
+@pytest.mark.parametrize("with_sink", [False, True])
+@pytest.mark.parametrize("magnitude", [1000., 1e7])
+def test_guarded_attention_tail(score_sign, with_sink, magnitude):
+    """test_flash_kernel_tpu.py:100-119: the guard falls back to the shifted branch."""
+    shape = (1, 1, 256, 64)
+    q = torch.full(shape, math.sqrt(magnitude))
+    k = q * score_sign
+    v = _randn(29, shape)
+    g = torch.ones(shape)
+    sink = torch.zeros((1,)) if with_sink else None
+    fn = partial(flash_attention, kind="asinh", n=16, c=8., block=128, compact_stat=True, range_guard=True)
+    got = algx_attention(fn, q.cuda(), k.cuda(), v.cuda(), g.cuda(), None if sink is None else sink.cuda())
+    assert torch.isfinite(got[0]).all()
+    want = R.asinh_attention(q.double(), k.double(), v.double(), n=16, c=8.,
+                             sink_logit=None if sink is None else sink.double())
+    np.testing.assert_allclose(got[0].cpu().double(), want, atol=2e-3, rtol=2e-3)
+    for t in got[1:4]:
+        assert torch.isfinite(t).all()
+
+
+def test_explicit_clipping_vjp_is_zero_above_cap():
+    """test_flash_kernel_tpu.py:122-138: the clipped primal is flat above the clamp."""
+    shape = (1, 1, 256, 64)
+    q = torch.full(shape, math.sqrt(1000)).cuda()
+    v = _randn(39, shape).cuda()
+    g = _randn(40, shape).cuda()
+    sink = torch.full((1,), 1000.).cuda()
+    fn = partial(flash_attention, kind="asinh", n=16, c=8., block=128, shift=False, range_guard=False)
+    _, dq, dk, _, ds = algx_attention(fn, q, q.clone(), v, g, sink)
+    for t in (dq, dk, ds):
+        assert torch.count_nonzero(t) == 0
+
+
+@pytest.mark.parametrize("mode", ["sink", "no_sink", "negative", "gain_two", "positive_tail", "negative_tail"])
+def test_whole_head_model_shape(mode):
+    """test_flash_kernel_tpu.py:253-328: T=2048 bf16 model shape, guarded (rel-L2 .025)."""
+    shape = (1, 2, 2048, 64)
+    q, k, v, g = (_randn(563 + i, shape, torch.bfloat16) for i in range(4))
+    sink = torch.tensor([-.35, .125]).reshape(1, 2, 1, 1)
+    if mode in ("no_sink", "negative"):
+        sink = None
+    if mode == "negative":
+        q = (1 + .05 * q.float()).to(torch.bfloat16)
+        k = (-1 + .05 * k.float()).to(torch.bfloat16)
+    if mode == "gain_two":
+        q = (2 * R.rms_norm(q.double(), None, 1e-5, io_dtype=torch.bfloat16)).to(torch.bfloat16)
+        k = (2 * R.rms_norm(k.double(), None, 1e-5, io_dtype=torch.bfloat16)).to(torch.bfloat16)
+    if mode.endswith("tail"):
+        q = torch.full(shape, math.sqrt(1000)).to(torch.bfloat16)
+        k = q if mode == "positive_tail" else -q
+    fn = partial(flash_attention, kind="asinh", n=16, c=8., range_guard=True)
+    got = algx_attention(fn, *(t.cuda() for t in (q, k, v, g)), None if sink is None else sink.cuda())
+    io = None if mode.endswith("tail") else torch.bfloat16
+    want = oracle_attention(q, k, v, g, sink, io_dtype=io, kind="asinh", n=16, c=8., range_guard=True)
+    np.testing.assert_allclose(got[0].float().cpu(), want[0].float(), atol=.015, rtol=.015)
+    err2 = norm2 = 0.0
+    for idx, (a, b) in enumerate(zip(got[1:], want[1:])):
+        if b is None:
+            continue
+        assert torch.isfinite(a).all()
+        a64, b64 = a.double().cpu(), b.double()
+        err2 += float(torch.sum((a64 - b64) ** 2))
+        norm2 += float(torch.sum(b64 ** 2))
+        if mode == "positive_tail" and idx == 0:
+            # Equal keys: dQ vanishes up to the rounding of the centred score
+            # VJP; bound it by u*sum|ds| as test_flash_kernel_tpu.py:295-314 does.
+            va, ga = v.double().numpy(), g.double().numpy()
+            count = np.arange(1, shape[-2] + 1, dtype=np.float64)
+            ideal = np.cumsum(va, axis=-2) / count[None, None, :, None]
+            centered = np.sum(ga * ideal, axis=-1)
+            dp = ga @ np.swapaxes(va, -1, -2)
+            visible = np.tril(np.ones((shape[-2], shape[-2]), bool))
+            mean_abs = np.sum(np.where(visible, np.abs(dp - centered[..., None]), 0.), axis=-1) / count
+            kval = float(k[0, 0, 0, 0])
+            x = shape[-1] * kval * kval / (8 * math.sqrt(shape[-1]))
+            factor = (16 / (8 * math.sqrt(shape[-1]))) * abs(kval) / math.sqrt(1 + x * x)
+            roundoff = (2 ** -8 + shape[-2] * 2 ** -24) * (1 + 2 ** -8)
+            bound = factor * roundoff * mean_abs + 2e-6
+            assert np.all(np.abs(a64.numpy() - b64.numpy()) <= bound[..., None])
+        elif mode != "negative":
+            assert rel_l2(a64, b64) < .025, idx
+    assert math.sqrt(err2 / max(norm2, 1e-12)) < .025
+
+
+@pytest.mark.parametrize("case", cases.ATTN_CASES, ids=[c[0] for c in cases.ATTN_CASES])
+@pytest.mark.parametrize("prec", ["f64", "bf16"])
+def test_against_reference_goldens(case, prec):
+    """Kernel vs outputs of the reference's own dense code (tests/golden)."""
+    name, n, c, with_sink, scale = case
+    idx = cases.ATTN_CASES.index(case)
+    q, k, v, g, sink = cases.attn_inputs(100 + 10 * idx, scale=scale, with_sink=with_sink)
+    dt = torch.float32 if prec == "f64" else torch.bfloat16
+    t = [torch.from_numpy(a).to(dt).cuda() for a in (q, k, v)]
+    gg = torch.from_numpy(g).cuda()
+    s = None if sink is None else torch.from_numpy(sink).cuda()
+    fn = partial(flash_attention, kind="asinh", n=n, c=c, range_guard=True)
+    got = algx_attention(fn, *t, gg, s)
+    key = f"attn_{name}_{prec}"
+    tol = 1e-3 if prec == "f64" else 2e-2
+    names = ["o", "dq", "dk", "dv"] + (["dsink"] if with_sink else [])
+    for nm, a in zip(names, got):
+        err = rel_l2(a, torch.from_numpy(GOLD[f"{key}_{nm}"]))
+        if err >= tol:
+            dump(f"golden_{key}_{nm}", got=a, want=GOLD[f"{key}_{nm}"])
+        assert err < tol, (nm, err)
+
+
+def test_baseline_config1_qknorm_then_attention():
+    """B2 H4 S512 D64 fp32, QK-norm (gain 1) then guarded asinh n16 c8.
+
+    The fp32 bar of the north star: outputs and grads within 1e-3 relative.
+    """
+    from algx.kernels.qk_norm import qk_rms_norm
+    shape = (2, 4, 512, 64)
+    q, k, v = (_randn(i, shape) for i in (0, 10, 20))
+    do = _randn(1, shape)
+    gain = torch.ones(64)
+    leaves = [t.cuda().requires_grad_(True) for t in (q, k, v)]
+    gq = gain.cuda().requires_grad_(True)
+    gk = gain.cuda().requires_grad_(True)
+    o = flash_attention(qk_rms_norm(leaves[0], gq), qk_rms_norm(leaves[1], gk), leaves[2],
+                        kind="asinh", n=16, c=8., range_guard=True)
+    torch.sum(o * do.cuda()).backward()
+    ref_leaves = [t.double().requires_grad_(True) for t in (q, k, v)]
+    rq = gain.double().requires_grad_(True)
+    rk = gain.double().requires_grad_(True)
+    ro = R.flash_attention(R.rms_norm(ref_leaves[0], rq), R.rms_norm(ref_leaves[1], rk), ref_leaves[2],
+                           kind="asinh", n=16, c=8., range_guard=True)
+    torch.sum(ro * do.double()).backward()
+    assert rel_l2(o.detach(), ro.detach()) < 1e-3
+    for a, b in zip([*leaves, gq, gk], [*ref_leaves, rq, rk]):
+        assert rel_l2(a.grad, b.grad) < 1e-3
