@@ -208,3 +208,23 @@ def test_baseline_config1_qknorm_then_attention():
     assert rel_l2(o.detach(), ro.detach()) < 1e-3
     for a, b in zip([*leaves, gq, gk], [*ref_leaves, rq, rk]):
         assert rel_l2(a.grad, b.grad) < 1e-3
+
+
+@pytest.mark.parametrize("T", [128, 256, 1024])
+@pytest.mark.parametrize("n,c", [(16, 8.0), (8, 2.0), (32, 8.0)])
+def test_fast_path_shapes(T, n, c):
+    """tcgen05 path (bf16, T % 128 == 0) at single-tile, two-tile and longer rows."""
+    from algx import _lib as L
+    shape = (2, 3, T, 64)
+    q, k, v, g = (_randn(700 + i + T, shape, torch.bfloat16) for i in range(4))
+    sink = _randn(7, (3,)) * 0.3
+    fn = partial(flash_attention, kind="asinh", n=n, c=c, range_guard=True)
+    got = algx_attention(fn, *(t.cuda() for t in (q, k, v, g)), sink.cuda())
+    assert L.device_error() == 0
+    want = oracle_attention(q, k, v, g, sink, io_dtype=torch.bfloat16, kind="asinh", n=n, c=c, range_guard=True)
+    np.testing.assert_allclose(got[0].float().cpu(), want[0].float(), atol=.015, rtol=.015)
+    for name, a, b in zip(("dq", "dk", "dv", "dsink"), got[1:], want[1:]):
+        err = rel_l2(a, b)
+        if err >= .025:
+            dump(f"fast_T{T}_n{n}_{name}", got=a, want=b)
+        assert err < .025, (name, err)
