@@ -51,6 +51,7 @@ _SZ = ctypes.c_size_t
 SIGNATURES = {
     "algx_last_error": ([], ctypes.c_char_p),
     "algx_version": ([], ctypes.c_int),
+    "algx_launch_count": ([], ctypes.c_uint64),
     "algx_device_error": ([ctypes.POINTER(_I32)], ctypes.c_int),
     "algx_qknorm_fwd": ([_P, _P, _P, _I64, _I64, _I32, _F, _P], ctypes.c_int),
     "algx_qknorm_bwd_workspace_size": ([_I64, _I64], _SZ),

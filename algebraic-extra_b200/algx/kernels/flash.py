@@ -66,47 +66,58 @@ def make_variant(kind: str, n: int = 16, c: float = 16.0, seq_len: int = 2048,
                    inv_stat=bool(inv_stat), compact_stat=bool(compact_stat), poly_rho=bool(poly_rho))
 
 
+def attn_forward(q, k, v, sink, cfg: L.AttnConfig):
+    """Forward launch group (prepare + forward); returns (o, saved residuals)."""
+    B, H, T, D = q.shape
+    dt = L.dtype_code(q.dtype)
+    st = L.stream_of(q)
+    q_s = torch.empty_like(q)
+    guard = torch.empty(4, dtype=torch.float32, device=q.device)
+    sp = sink.data_ptr() if sink is not None else None
+    L.check(L.lib().algx_attn_prepare(cfg, q.data_ptr(), k.data_ptr(), v.data_ptr(), sp, q_s.data_ptr(),
+                                      guard.data_ptr(), B, H, T, D, dt, st), "algx_attn_prepare")
+    o = torch.empty_like(q)
+    stat = torch.empty((B, H, T), dtype=torch.float32, device=q.device)
+    o_prec = None
+    if cfg.kind == L.ALGX_ATTN_ASINH and cfg.mode == L.ALGX_MODE_GUARDED:
+        o_prec = torch.empty((B, H, T, D), dtype=torch.float32, device=q.device)
+    L.check(L.lib().algx_attn_fwd(cfg, q_s.data_ptr(), k.data_ptr(), v.data_ptr(), sp, guard.data_ptr(),
+                                  o.data_ptr(), L.ptr(o_prec), stat.data_ptr(), B, H, T, D, dt, st),
+            "algx_attn_fwd")
+    return o, (q_s, k, v, sink, o, o_prec, stat, guard)
+
+
+def attn_backward(saved, cfg: L.AttnConfig, do, workspace=None):
+    """Backward launch group; returns (dq, dk, dv, dsink)."""
+    q_s, k, v, sink, o, o_prec, stat, guard = saved
+    B, H, T, D = q_s.shape
+    do = do.to(q_s.dtype).contiguous()
+    dq = torch.empty_like(q_s)
+    dk = torch.empty_like(k)
+    dv = torch.empty_like(v)
+    dsink = torch.empty(H, dtype=torch.float32, device=q_s.device) if sink is not None else None
+    nbytes = L.lib().algx_attn_bwd_workspace_size(B, H, T, D)
+    if workspace is None or workspace.numel() < nbytes:
+        workspace = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q_s.device)
+    L.check(L.lib().algx_attn_bwd(cfg, q_s.data_ptr(), k.data_ptr(), v.data_ptr(), L.ptr(sink),
+                                  guard.data_ptr(), o.data_ptr(), L.ptr(o_prec), stat.data_ptr(),
+                                  do.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), L.ptr(dsink),
+                                  B, H, T, D, L.dtype_code(q_s.dtype), workspace.data_ptr(), nbytes,
+                                  L.stream_of(q_s)), "algx_attn_bwd")
+    return dq, dk, dv, dsink
+
+
 class _Flash(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, sink, cfg: L.AttnConfig):
-        B, H, T, D = q.shape
-        dt = L.dtype_code(q.dtype)
-        st = L.stream_of(q)
-        q_s = torch.empty_like(q)
-        guard = torch.empty(4, dtype=torch.float32, device=q.device)
-        sp = sink.data_ptr() if sink is not None else None
-        L.check(L.lib().algx_attn_prepare(cfg, q.data_ptr(), k.data_ptr(), v.data_ptr(), sp, q_s.data_ptr(),
-                                          guard.data_ptr(), B, H, T, D, dt, st), "algx_attn_prepare")
-        o = torch.empty_like(q)
-        stat = torch.empty((B, H, T), dtype=torch.float32, device=q.device)
-        o_prec = None
-        if cfg.kind == L.ALGX_ATTN_ASINH and cfg.mode == L.ALGX_MODE_GUARDED:
-            o_prec = torch.empty((B, H, T, D), dtype=torch.float32, device=q.device)
-        L.check(L.lib().algx_attn_fwd(cfg, q_s.data_ptr(), k.data_ptr(), v.data_ptr(), sp, guard.data_ptr(),
-                                      o.data_ptr(), L.ptr(o_prec), stat.data_ptr(), B, H, T, D, dt, st),
-                "algx_attn_fwd")
+        o, saved = attn_forward(q, k, v, sink, cfg)
         ctx.cfg = cfg
-        ctx.has_sink = sink is not None
-        ctx.save_for_backward(q_s, k, v, sink, o, o_prec, stat, guard)
+        ctx.save_for_backward(*saved)
         return o
 
     @staticmethod
     def backward(ctx, do):
-        q_s, k, v, sink, o, o_prec, stat, guard = ctx.saved_tensors
-        cfg = ctx.cfg
-        B, H, T, D = q_s.shape
-        do = do.to(q_s.dtype).contiguous()
-        dq = torch.empty_like(q_s)
-        dk = torch.empty_like(k)
-        dv = torch.empty_like(v)
-        dsink = torch.empty(H, dtype=torch.float32, device=q_s.device) if ctx.has_sink else None
-        nbytes = L.lib().algx_attn_bwd_workspace_size(B, H, T, D)
-        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q_s.device)
-        L.check(L.lib().algx_attn_bwd(cfg, q_s.data_ptr(), k.data_ptr(), v.data_ptr(), L.ptr(sink),
-                                      guard.data_ptr(), o.data_ptr(), L.ptr(o_prec), stat.data_ptr(),
-                                      do.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), L.ptr(dsink),
-                                      B, H, T, D, L.dtype_code(q_s.dtype), ws.data_ptr(), nbytes,
-                                      L.stream_of(q_s)), "algx_attn_bwd")
+        dq, dk, dv, dsink = attn_backward(ctx.saved_tensors, ctx.cfg, do)
         return dq, dk, dv, dsink, None
 
 

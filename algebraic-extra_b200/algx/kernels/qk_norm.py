@@ -9,15 +9,34 @@ import torch
 from .. import _lib as L
 
 
+def qknorm_forward(x, gain, eps):
+    """y = rms_norm(x) * gain (one launch)."""
+    y = torch.empty_like(x)
+    L.check(L.lib().algx_qknorm_fwd(x.data_ptr(), gain.data_ptr(), y.data_ptr(), x.numel() // 64, 64,
+                                    L.dtype_code(x.dtype), float(eps), L.stream_of(x)), "algx_qknorm_fwd")
+    return y
+
+
+def qknorm_backward(x, gain, dy, eps, workspace=None):
+    """(dx, dgain) of the QK norm (two launches: rows, then the fixed-order dgain sum)."""
+    dy = dy.to(x.dtype).contiguous()
+    rows = x.numel() // 64
+    dx = torch.empty_like(x)
+    dgain = torch.empty(64, dtype=torch.float32, device=x.device)
+    nbytes = L.lib().algx_qknorm_bwd_workspace_size(rows, 64)
+    if workspace is None or workspace.numel() < nbytes:
+        workspace = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=x.device)
+    L.check(L.lib().algx_qknorm_bwd(x.data_ptr(), gain.data_ptr(), dy.data_ptr(), dx.data_ptr(),
+                                    dgain.data_ptr(), rows, 64, L.dtype_code(x.dtype), float(eps),
+                                    workspace.data_ptr(), nbytes, L.stream_of(x)), "algx_qknorm_bwd")
+    return dx, dgain
+
+
 class _QKNorm(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, gain, eps):
         xc = x.contiguous()
-        y = torch.empty_like(xc)
-        rows = xc.numel() // 64
-        L.check(L.lib().algx_qknorm_fwd(xc.data_ptr(), gain.data_ptr(), y.data_ptr(), rows, 64,
-                                        L.dtype_code(xc.dtype), float(eps), L.stream_of(xc)),
-                "algx_qknorm_fwd")
+        y = qknorm_forward(xc, gain, eps)
         ctx.save_for_backward(xc, gain)
         ctx.eps = float(eps)
         return y
@@ -25,16 +44,7 @@ class _QKNorm(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy):
         x, gain = ctx.saved_tensors
-        dy = dy.to(x.dtype).contiguous()
-        rows = x.numel() // 64
-        dx = torch.empty_like(x)
-        dgain = torch.empty(64, dtype=torch.float32, device=x.device)
-        nbytes = L.lib().algx_qknorm_bwd_workspace_size(rows, 64)
-        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=x.device)
-        L.check(L.lib().algx_qknorm_bwd(x.data_ptr(), gain.data_ptr(), dy.data_ptr(), dx.data_ptr(),
-                                        dgain.data_ptr(), rows, 64, L.dtype_code(x.dtype), ctx.eps,
-                                        ws.data_ptr(), nbytes, L.stream_of(x)),
-                "algx_qknorm_bwd")
+        dx, dgain = qknorm_backward(x, gain, dy, ctx.eps)
         return dx, dgain.to(gain.dtype), None
 
 

@@ -3,6 +3,7 @@
 // so the library does not link libcuda directly).
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -12,6 +13,9 @@
 namespace algx {
 
 static thread_local std::string g_last_error;
+static std::atomic<uint64_t> g_launches{0};
+
+void count_launches(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
 
 void set_error(const std::string& msg) { g_last_error = msg; }
 
@@ -79,6 +83,8 @@ extern "C" {
 const char* algx_last_error(void) { return algx::g_last_error.c_str(); }
 
 int algx_version(void) { return 100; }
+
+uint64_t algx_launch_count(void) { return algx::g_launches.load(std::memory_order_relaxed); }
 
 int algx_device_error(int32_t* code) {
   if (!code) return algx::fail(ALGX_ERR_INVALID, "code is NULL");

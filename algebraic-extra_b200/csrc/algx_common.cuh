@@ -15,13 +15,14 @@ namespace algx {
 void set_error(const std::string& msg);
 int fail(int status, const std::string& msg);
 int check_cuda(cudaError_t err, const char* what);
+void count_launches(int n);
 
 #define ALGX_REQUIRE(cond, msg) \
   do { if (!(cond)) return ::algx::fail(ALGX_ERR_INVALID, (msg)); } while (0)
 #define ALGX_CUDA(call) \
   do { int _s = ::algx::check_cuda((call), #call); if (_s) return _s; } while (0)
 #define ALGX_LAUNCHED(what) \
-  do { int _s = ::algx::check_cuda(cudaGetLastError(), what); if (_s) return _s; } while (0)
+  do { ::algx::count_launches(1); int _s = ::algx::check_cuda(cudaGetLastError(), what); if (_s) return _s; } while (0)
 
 // Device-side error word. A bounded wait that gives up ORs a code in here
 // instead of spinning forever; algx_device_error() reads and clears it.

@@ -599,6 +599,7 @@ int algx_attn_bwd(const algx_attn_config* cfg, const void* q_scaled, const void*
                                                                  (const float*)v, (const float*)dout, stat, di,
                                                                  guard, (float*)dq, (int)T, mask);
   }
+  count_launches(1);  // two kernels above, one counted by the macro
   ALGX_LAUNCHED("attn_bwd_generic launch");
   return ALGX_OK;
 }

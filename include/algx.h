@@ -46,6 +46,8 @@ enum { ALGX_HEAD_CE = 0, ALGX_HEAD_ALG_CE = 1 };
 ALGX_API const char* algx_last_error(void);
 /* Library version (major*10000 + minor*100 + patch). */
 ALGX_API int algx_version(void);
+/* Number of kernels this process launched through libalgx so far. */
+ALGX_API uint64_t algx_launch_count(void);
 /* Reads and clears the device error word of the current device (bounded
  * waits that gave up set it). Synchronizes the device. */
 ALGX_API int algx_device_error(int32_t* code);
