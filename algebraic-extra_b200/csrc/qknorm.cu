@@ -3,6 +3,8 @@
 // (8 for bf16, 16 for fp32), row reductions by warp shuffles, a fixed grid
 // of a few CTAs per SM looping over rows. dgain is reduced deterministically:
 // per-CTA column partials in a workspace, then one fixed-order sum.
+#include <mutex>
+
 #include "algx_common.cuh"
 #include "vec_io.cuh"
 
@@ -131,6 +133,31 @@ int grid_for(int64_t rows) {
   return (int)(g < 1 ? 1 : g);
 }
 
+// Scratch of algx_qknorm_bwd_noalloc: one row of kDim fp32 dgain partials per
+// CTA, for at most kNoAllocBlocks CTAs (64 KiB per device, held by every GPU
+// that loads the library until the process exits). Host code must not pass
+// the symbol itself to a kernel: its device address comes from
+// cudaGetSymbolAddress, taken once per device in noalloc_scratch().
+constexpr int kNoAllocBlocks = 256;
+constexpr int64_t kNoAllocMaxRows = 2147483647;  // rows beyond int32 range are rejected
+static __device__ __align__(256) float g_noalloc_partials[kNoAllocBlocks * kDim];
+
+int noalloc_scratch(float** out) {
+  static std::mutex mu;
+  static float* addr[64] = {nullptr};
+  int dev = 0;
+  ALGX_CUDA(cudaGetDevice(&dev));
+  ALGX_REQUIRE(dev >= 0 && dev < 64, "qknorm_bwd_noalloc: device ordinal out of range");
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    ALGX_CUDA(cudaGetSymbolAddress(&p, g_noalloc_partials));
+    addr[dev] = static_cast<float*>(p);
+  }
+  *out = addr[dev];
+  return ALGX_OK;
+}
+
 int check_args(const void* x, const float* gain, const void* y, int64_t rows, int64_t dim, int32_t dtype,
                float eps) {
   ALGX_REQUIRE(x && gain && y, "qknorm: NULL pointer");
@@ -198,6 +225,42 @@ int algx_qknorm_bwd(const void* x, const float* gain, const void* dy, void* dx, 
                                                         partial, rows, eps);
   }
   ALGX_LAUNCHED("qknorm_bwd launch");
+  qknorm_dgain_reduce<<<1, kDim, 0, st>>>(partial, grid, dgain);
+  ALGX_LAUNCHED("qknorm_dgain_reduce launch");
+  return ALGX_OK;
+}
+
+// The same backward as algx_qknorm_bwd, for callers that cannot allocate
+// device memory: its dgain partials live in g_noalloc_partials instead of a
+// caller workspace. See include/algx.h for the contract.
+int algx_qknorm_bwd_noalloc(const void* x, const float* gain, const void* dy, void* dx, float* dgain, int64_t rows,
+                            int64_t dim, int32_t dtype, float eps, void* stream) {
+  if (int s = check_args(x, gain, dx, rows, dim, dtype, eps)) return s;
+  ALGX_REQUIRE(dy && dgain, "qknorm_bwd_noalloc: NULL pointer");
+  ALGX_REQUIRE((reinterpret_cast<uintptr_t>(dy) & 15) == 0, "qknorm: tensors must be 16-byte aligned");
+  ALGX_REQUIRE(rows <= kNoAllocMaxRows,
+               "qknorm_bwd_noalloc: at most 2147483647 rows (use algx_qknorm_bwd with a workspace)");
+  float* partial = nullptr;
+  if (int s = noalloc_scratch(&partial)) return s;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (rows == 0) {
+    ALGX_CUDA(cudaMemsetAsync(dgain, 0, kDim * sizeof(float), st));
+    return ALGX_OK;
+  }
+  // Every CTA of the grid writes its whole partial row, so nothing in the
+  // scratch needs clearing; the reduction reads exactly those rows.
+  int grid = dtype == ALGX_BF16 ? grid_for<__nv_bfloat16>(rows) : grid_for<float>(rows);
+  if (grid > kNoAllocBlocks) grid = kNoAllocBlocks;
+  if (dtype == ALGX_BF16) {
+    qknorm_bwd_kernel<__nv_bfloat16><<<grid, kThreads, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(x), gain, static_cast<const __nv_bfloat16*>(dy),
+        static_cast<__nv_bfloat16*>(dx), partial, rows, eps);
+  } else {
+    qknorm_bwd_kernel<float><<<grid, kThreads, 0, st>>>(static_cast<const float*>(x), gain,
+                                                        static_cast<const float*>(dy), static_cast<float*>(dx),
+                                                        partial, rows, eps);
+  }
+  ALGX_LAUNCHED("qknorm_bwd_noalloc launch");
   qknorm_dgain_reduce<<<1, kDim, 0, st>>>(partial, grid, dgain);
   ALGX_LAUNCHED("qknorm_dgain_reduce launch");
   return ALGX_OK;

@@ -68,6 +68,21 @@ ALGX_API int algx_qknorm_bwd(const void* x, const float* gain, const void* dy, v
                     int64_t rows, int64_t dim, int32_t dtype, float eps, void* workspace,
                     size_t workspace_bytes, void* stream);
 
+/* QK-norm backward that allocates nothing, for callers that cannot call
+ * cudaMalloc (a host framework that owns all device memory, code running
+ * while a pool allocator is locked, or a foreign-function layer with no
+ * workspace channel). No counterpart in the reference.
+ * Same arguments and results as algx_qknorm_bwd minus the workspace: the
+ * per-CTA dgain partials live in a library-owned static device array of
+ * 256 x 64 fp32 (64 KiB per device, kept until the process exits).
+ * Limits: rows <= 2147483647 (larger counts return ALGX_ERR_INVALID).
+ * The first call on each device looks up the array's device address; make
+ * that first call before any stream capture. Every call shares the array, so
+ * calls that overlap on the GPU (other streams, other threads) race; serialise
+ * them on one stream. */
+ALGX_API int algx_qknorm_bwd_noalloc(const void* x, const float* gain, const void* dy, void* dx, float* dgain,
+                                     int64_t rows, int64_t dim, int32_t dtype, float eps, void* stream);
+
 /* ---------------------------------------------------------------- attention */
 
 /* Resolved variant of kernels/flash.py:732-760 plus the wrapper's constants. */
