@@ -42,6 +42,17 @@ class AttnConfig(ctypes.Structure):
     ]
 
 
+class HeadConfig(ctypes.Structure):
+    _fields_ = [
+        ("kind", ctypes.c_int32),
+        ("n", ctypes.c_int32),
+        ("inv_c", ctypes.c_float),
+        ("clamp", ctypes.c_float),
+        ("has_ignore", ctypes.c_int32),
+        ("ignore_index", ctypes.c_int32),
+    ]
+
+
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
 _I32 = ctypes.c_int32
@@ -64,6 +75,14 @@ SIGNATURES = {
     "algx_attn_bwd_workspace_size": ([_I64, _I64, _I64, _I64], _SZ),
     "algx_attn_bwd": ([ctypes.POINTER(AttnConfig), _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                        _I64, _I64, _I64, _I64, _I32, _P, _SZ, _P], ctypes.c_int),
+    "algx_head_fwd_splits": ([_I64, _I64], ctypes.c_int),
+    "algx_head_fwd": ([ctypes.POINTER(HeadConfig), _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _I32, _P],
+                      ctypes.c_int),
+    "algx_head_reduce": ([ctypes.POINTER(HeadConfig), _P, _P, _P, _I32, _I64, _P, _P, _P, _P], ctypes.c_int),
+    "algx_head_finalize": ([ctypes.POINTER(HeadConfig), _P, _P, _P, _P, _I64, _I64, _P, _P, _P, _P, _P],
+                           ctypes.c_int),
+    "algx_head_bwd": ([ctypes.POINTER(HeadConfig), _P, _P, _P, _P, _P, _P, _I32, _P, _I64, _I64, _I64, _I64, _I32,
+                       _P], ctypes.c_int),
     "algx_selftest_tcgen05": ([_I32, _P, _P, _P, _P], ctypes.c_int),
 }
 

@@ -1,0 +1,86 @@
+"""Multi-GPU pieces of the hot path (one process per GPU, torch.distributed).
+
+* Attention and QK-norm shard by (batch x heads) with no exchange: each rank
+  calls the single-GPU API on its own heads.
+* The fused head is vocabulary-parallel: rank r holds a
+  contiguous slice of the embedding rows. The forward computes per-token
+  (max, sum, target logit) over the local slice, then all-reduces them
+  (MAX then SUM for "ce"; SUM only for the additive "alg_ce"); the backward
+  computes the local dE slice with no communication and all-reduces the
+  partial dh. Collectives go through NCCL on GPU (gloo in the CPU tests).
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from . import _lib as L
+from .kernels import fused_head as FH
+
+
+def shard_rows(total: int, world: int, rank: int):
+    """Contiguous split of ``total`` rows over ``world`` ranks: (offset, count)."""
+    base, extra = divmod(total, world)
+    count = base + (1 if rank < extra else 0)
+    offset = rank * base + min(rank, extra)
+    return offset, count
+
+
+def combine_vocab_stats(mlz: torch.Tensor, kind: str, group=None) -> torch.Tensor:
+    """Turn per-shard (m, l, zt) rows of ``mlz`` (3, N) into global ones, in place.
+
+    "ce": m_g = max_r m_r, l = sum_r l_r exp(m_r - m_g); "alg_ce": l = sum_r l_r.
+    zt is a sum (only the rank owning the target column contributes).
+    """
+    m, l = mlz[0], mlz[1]
+    if kind == "ce":
+        mg = m.clone()
+        dist.all_reduce(mg, op=dist.ReduceOp.MAX, group=group)
+        l.mul_(torch.exp(m - mg))
+        m.copy_(mg)
+    dist.all_reduce(mlz[1:], op=dist.ReduceOp.SUM, group=group)
+    return mlz
+
+
+class _VocabParallelHead(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, h, embed_shard, targets, cfg, slope, kind, vocab_offset, vocab_total, group):
+        h16 = h.to(torch.bfloat16).contiguous()
+        e16 = embed_shard.to(torch.bfloat16).contiguous()
+        t32 = targets.to(torch.int32).contiguous()
+        mlz = FH.head_forward_partials(h16, e16, t32, cfg, vocab_offset)
+        combine_vocab_stats(mlz, kind, group)
+        stat, tel, obj, count = FH.head_finalize(cfg, t32, mlz, vocab_total)
+        ctx.save_for_backward(h16, e16, t32, stat, count)
+        ctx.cfg, ctx.slope, ctx.voff, ctx.group = cfg, slope, vocab_offset, group
+        ctx.h_dtype, ctx.e_dtype = h.dtype, embed_shard.dtype
+        ctx.mark_non_differentiable(tel)
+        return obj.reshape(()), tel
+
+    @staticmethod
+    def backward(ctx, g_obj, g_tel):
+        h16, e16, t32, stat, count = ctx.saved_tensors
+        scale = (g_obj.reshape(1).float() * ctx.slope / count).contiguous()
+        dh, de = FH.head_backward(h16, e16, t32, stat, scale, ctx.cfg, ctx.voff, dh_dtype=torch.float32)
+        dist.all_reduce(dh, op=dist.ReduceOp.SUM, group=ctx.group)
+        return dh.to(ctx.h_dtype), de.to(ctx.e_dtype), None, None, None, None, None, None, None
+
+
+def vocab_parallel_fused_head(h, embed_shard, targets, *, vocab_offset: int, vocab_total: int, kind="ce", n=16,
+                              c=16.0, ignore_index=None, group=None):
+    """``fused_head`` with the embedding rows split over the ranks of ``group``.
+
+    Every rank passes the same ``h`` and ``targets`` and its own slice
+    ``embed_shard`` = embed[vocab_offset : vocab_offset + V_local]. Returns the
+    same (objective, telemetry) on every rank; gradients: dh (all-reduced) and
+    the local slice of dE.
+    """
+    if kind not in ("ce", "alg_ce"):
+        raise ValueError(kind)
+    L.require_cuda(h, embed_shard, targets)
+    cfg = FH.head_config(kind, n, c, vocab_total, ignore_index)
+    slope = 1.0 if kind == "ce" else n / c
+    obj, tel = _VocabParallelHead.apply(h, embed_shard, targets, cfg, slope, kind, vocab_offset, vocab_total,
+                                        group)
+    return obj, tel.detach()

@@ -170,7 +170,7 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
     if (cfg.has_sink) l = weight<N, CLIP>(sink[bh % H], cfg.clamp, rr);
     bool ok = true;
     for (int j = 0; j < nk; ++j) {
-      if (!mbar_wait(&bar_s_full, j & 1, abort_v, dev_err)) {
+      if (!mbar_wait_warp(&bar_s_full, j & 1, abort_v, dev_err)) {
         ok = false;
         break;
       }
@@ -193,7 +193,7 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
           l += p0 + p1;
           pk[i] = pack_bf16x2(p0, p1);
         }
-        if (c == 0 && j > 0 && !mbar_wait(&bar_p_free, (j - 1) & 1, abort_v, dev_err)) {
+        if (c == 0 && j > 0 && !mbar_wait_warp(&bar_p_free, (j - 1) & 1, abort_v, dev_err)) {
           ok = false;
           break;
         }
@@ -204,7 +204,7 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar_p_full);
     }
-    if (ok && mbar_wait(&bar_o_full, 0, abort_v, dev_err)) {
+    if (ok && mbar_wait_warp(&bar_o_full, 0, abort_v, dev_err)) {
       tc_fence_after();
       const float inv = 1.f / l;
       const size_t row = (size_t)row_base + (size_t)qt * kTile + r;
@@ -395,7 +395,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     bool ok = true;
     for (int ii = 0; ii < ni; ++ii) {
       const int s = ii & 1;
-      if (!mbar_wait(&bar_st_full, ii & 1, abort_v, dev_err)) {
+      if (!mbar_wait_warp(&bar_st_full, ii & 1, abort_v, dev_err)) {
         ok = false;
         break;
       }
@@ -434,7 +434,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           pk[i] = pack_bf16x2(pp[0], pp[1]);
           dk2[i] = pack_bf16x2(dd2[0], dd2[1]);
         }
-        if (c == 0 && ii > 0 && !mbar_wait(&bar_ps_free, (ii - 1) & 1, abort_v, dev_err)) {
+        if (c == 0 && ii > 0 && !mbar_wait_warp(&bar_ps_free, (ii - 1) & 1, abort_v, dev_err)) {
           ok = false;
           break;
         }
@@ -452,7 +452,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar_ps_ready);
     }
-    if (ok && mbar_wait(&bar_fin, 0, abort_v, dev_err)) {
+    if (ok && mbar_wait_warp(&bar_fin, 0, abort_v, dev_err)) {
       tc_fence_after();
       const size_t row = (size_t)row_base + (size_t)kt * kTile + r;
       const float slope = (float)N;
@@ -483,7 +483,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     const int r = threadIdx.x - 128;
     const uint32_t lane_off = (uint32_t)((warp - 4) * 32) << 16;
     for (int ii = 0; ii < ni; ++ii) {
-      if (!mbar_wait(&bar_dq_full, ii & 1, abort_v, dev_err)) break;
+      if (!mbar_wait_warp(&bar_dq_full, ii & 1, abort_v, dev_err)) break;
       tc_fence_after();
       uint32_t a[32], b[32];
       tmem_ld32(tdQ + lane_off, a);

@@ -68,6 +68,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Warp-uniform bounded wait for consumer warps: every lane waits and the
+// result is the AND over the warp, so the .sync.aligned tcgen05 loads and
+// stores that follow are executed by all 32 lanes or by none.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
+                                               int* dev_err) {
+  const bool ok = mbar_wait(bar, parity, abort_flag, dev_err);
+  return __all_sync(0xffffffffu, ok);
+}
+
 // ------------------------------------------------------------------ TMA
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0,
                                             int c1) {

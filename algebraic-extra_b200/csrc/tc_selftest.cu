@@ -80,7 +80,7 @@ __global__ void __launch_bounds__(128) tc_selftest_kernel(const __grid_constant_
     __syncthreads();
     tc_fence_after();
   }
-  bool ok = mbar_wait(&bar_load, 0, &abort_flag, dev_err);
+  bool ok = mbar_wait_warp(&bar_load, 0, &abort_flag, dev_err);
   if (threadIdx.x == 0 && ok) {
     tc_fence_after();
     const uint32_t a0 = smem_u32(sa), b0 = smem_u32(sb);
@@ -104,7 +104,7 @@ __global__ void __launch_bounds__(128) tc_selftest_kernel(const __grid_constant_
     mma_commit(&bar_mma);
   }
   __syncthreads();
-  ok = ok && mbar_wait(&bar_mma, 0, &abort_flag, dev_err);
+  ok = mbar_wait_warp(&bar_mma, 0, &abort_flag, dev_err) && ok;
   tc_fence_after();
   if (ok) {
     const int row = threadIdx.x;

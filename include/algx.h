@@ -129,6 +129,56 @@ ALGX_API int algx_attn_bwd(const algx_attn_config* cfg, const void* q_scaled, co
                   int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype, void* workspace,
                   size_t workspace_bytes, void* stream);
 
+/* --------------------------------------------------------------- fused head */
+
+/* kernels/fused_head.py:260-275 (+ the ignore_index extension). */
+typedef struct algx_head_config {
+  int32_t kind;         /* ALGX_HEAD_CE or ALGX_HEAD_ALG_CE */
+  int32_t n;            /* alg_ce power (2..32, power of two) */
+  float inv_c;          /* 1/c */
+  float clamp;          /* alg_ce kernel-argument clamp X = 0.25*(1e38/V)^(1/n) (fused_head.py:273) */
+  int32_t has_ignore;   /* 1: rows with target == ignore_index leave loss, gradients and mean */
+  int32_t ignore_index;
+} algx_head_config;
+
+/* Vocabulary splits algx_head_fwd uses for N tokens over V local rows. */
+ALGX_API int algx_head_fwd_splits(int64_t N, int64_t V);
+
+/* Forward partial statistics per (split, token): running max m, sum l and
+ * target logit zt over this rank's V vocabulary rows (global row index =
+ * local + vocab_offset). h (N, d) and embed (V, d) are bf16, d % 64 == 0.
+ * part_* are (splits, N) fp32. Replaces kernels/fused_head.py:72-117
+ * `_fwd_kernel` / `_forward` without materialising the logits. */
+ALGX_API int algx_head_fwd(const algx_head_config* cfg, const void* h, const void* embed,
+                           const int32_t* targets, float* part_m, float* part_l, float* part_zt,
+                           int64_t N, int64_t d, int64_t V, int64_t vocab_offset, int32_t splits,
+                           int32_t dtype, void* stream);
+
+/* Combine split partials into one (m, l, zt) per token (max and rescaled
+ * sum for ce; plain sums for alg_ce). Part of fused_head.py:174-191. */
+ALGX_API int algx_head_reduce(const algx_head_config* cfg, const float* part_m, const float* part_l,
+                              const float* part_zt, int32_t splits, int64_t N, float* m, float* l,
+                              float* zt, void* stream);
+
+/* stat (lse or l^(-1/n)), telemetry (nll or target probability), objective
+ * (device scalar) and the loss row count (device scalar). Replaces
+ * kernels/fused_head.py:219-229 `_telemetry`. Labels outside [0, V_total)
+ * other than ignore_index raise the device error word when has_ignore. */
+ALGX_API int algx_head_finalize(const algx_head_config* cfg, const int32_t* targets, const float* m,
+                                const float* l, const float* zt, int64_t N, int64_t V_total,
+                                float* stat, float* telemetry, float* objective, float* count,
+                                void* stream);
+
+/* dh (N, d) in dh_dtype (partial over this rank's vocabulary rows) and
+ * dembed (V, d) fp32, with scale = g * slope / count read from device
+ * memory. Recomputes logit tiles; dz never reaches HBM. Replaces
+ * kernels/fused_head.py:120-156, 194-216 (`_bwd_kernel`, `_backward`,
+ * including the XLA dE = dz^T h product). */
+ALGX_API int algx_head_bwd(const algx_head_config* cfg, const void* h, const void* embed,
+                           const int32_t* targets, const float* stat, const float* scale, void* dh,
+                           int32_t dh_dtype, float* dembed, int64_t N, int64_t d, int64_t V,
+                           int64_t vocab_offset, int32_t dtype, void* stream);
+
 /* --------------------------------------------------------------- diagnostics */
 
 /* One-CTA tcgen05/TMA self-test: D = A*B for the operand layouts the
