@@ -63,6 +63,14 @@ template <int N> __device__ __forceinline__ float ipow_t(float x) {
   else return x * ipow_t<N - 1>(x);
 }
 
+// 1/sqrt(x) on the MUFU pipe, flushing denormals (the arguments here are
+// 1 + x^2 >= 1 or positive row sums, never denormal).
+__device__ __forceinline__ float rsqrt_fast(float x) {
+  float y;
+  asm("rsqrt.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // rho(x) = x + sqrt(1+x^2): fast form (kernels/flash.py:83-88) and stable
 // form with the reciprocal for x < 0 (kernels/flash.py:76-80). Both return
 // r = 1/sqrt(1+x^2) through the out-parameter.
@@ -85,6 +93,46 @@ __device__ __forceinline__ float inv_root(float l, int n) {
   float y = rsqrtf(l);
   for (int k = n / 2; k > 1; k /= 2) y = y * rsqrtf(y);
   return y;
+}
+
+// Packed FP32 pairs (sm_100 f32x2 arithmetic): two lanes of work per
+// instruction on the FMA pipe.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  float2 d;
+  asm("{.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+  return d;
+}
+__device__ __forceinline__ float2 mul2(float2 a, float2 b) {
+  float2 d;
+  asm("{.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  float2 d;
+  asm("{.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+  float2 d;
+  asm("{.reg .b64 ra, rb, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+      "sub.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;}"
+      : "=f"(d.x), "=f"(d.y)
+      : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+  return d;
+}
+template <int N> __device__ __forceinline__ float2 ipow2_t(float2 x) {
+  if constexpr (N == 1) return x;
+  else if constexpr ((N & 1) == 0) { float2 h = ipow2_t<N / 2>(x); return mul2(h, h); }
+  else return mul2(x, ipow2_t<N - 1>(x));
 }
 
 // Reinterpretation helpers for order-preserving float max via integer atomics

@@ -222,36 +222,51 @@ __global__ void __launch_bounds__(256) attn_di_kernel(algx_attn_config cfg, cons
   const float b = hs ? sink[h] : 0.f;
   if (hs && e.branch != BR_SOFTMAX) rb = rho_exact(e.clip ? fminf(b, cfg.clamp) : b, r);
   float part = 0.f;
-  for (int i = warp; i < kRows; i += 8) {
-    const int row = row0 + i;
-    if (row >= T_) break;
-    const size_t off = ((size_t)bh * T_ + row) * kD + 2 * lane;
-    float o0, o1;
-    if (e.precise && o_prec) {
-      o0 = o_prec[off];
-      o1 = o_prec[off + 1];
-    } else {
-      o0 = to_f32(o[off]);
-      o1 = to_f32(o[off + 1]);
+  auto accumulate = [&](int row, float s) {
+    di[(size_t)bh * T_ + row] = s;
+    if (hs) {
+      const float st = stat[(size_t)bh * T_ + row];
+      float mass;
+      if (e.branch == BR_SOFTMAX)
+        mass = expf(b - st);
+      else if (e.branch == BR_UNSHIFTED && e.inv_stat)
+        mass = ipow(rb, cfg.n) * st;
+      else
+        mass = ipow(rb * st, cfg.n);
+      part += mass * s;
     }
-    float s = to_f32(dout[off]) * o0 + to_f32(dout[off + 1]) * o1;
+  };
+  if (e.precise && o_prec) {
+    // shifted guard fallback: the unrounded fp32 output, one warp per row
+    for (int i = warp; i < kRows; i += 8) {
+      const int row = row0 + i;
+      if (row >= T_) break;
+      const size_t off = ((size_t)bh * T_ + row) * kD + 2 * lane;
+      float s = to_f32(dout[off]) * o_prec[off] + to_f32(dout[off + 1]) * o_prec[off + 1];
 #pragma unroll
-    for (int x = 16; x > 0; x >>= 1) s += __shfl_xor_sync(0xffffffffu, s, x);
-    if (lane == 0) {
-      di[(size_t)bh * T_ + row] = s;
-      if (hs) {
-        const float st = stat[(size_t)bh * T_ + row];
-        float mass;
-        if (e.branch == BR_SOFTMAX)
-          mass = expf(b - st);
-        else if (e.branch == BR_UNSHIFTED && e.inv_stat)
-          mass = ipow(rb, cfg.n) * st;
-        else
-          mass = ipow(rb * st, cfg.n);
-        part += mass * s;
-      }
+      for (int x = 16; x > 0; x >>= 1) s += __shfl_xor_sync(0xffffffffu, s, x);
+      if (lane == 0) accumulate(row, s);
+    }
+  } else {
+    // 128-bit row loads: Vec<T>::TPR threads per row
+    using V = Vec<T>;
+    const int sub = lane % V::TPR, rl = lane / V::TPR;
+    for (int i0 = warp * V::RPW; i0 < kRows; i0 += 8 * V::RPW) {
+      const int row = row0 + i0 + rl;
+      const bool ok = row < T_;
+      const size_t off = ((size_t)bh * T_ + row) * kD + sub * V::N;
+      float ov[V::N], dv[V::N];
+      unpack<T>(ok ? ld_stream(o + off) : make_uint4(0, 0, 0, 0), ov);
+      unpack<T>(ok ? ld_stream(dout + off) : make_uint4(0, 0, 0, 0), dv);
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < V::N; ++i) s = fmaf(dv[i], ov[i], s);
+      s = row_sum<V::TPR>(s);
+      if (ok && sub == 0) accumulate(row, s);
     }
   }
+#pragma unroll
+  for (int x = 16; x > 0; x >>= 1) part += __shfl_xor_sync(0xffffffffu, part, x);
   if (!hs) return;
   __shared__ float red[8];
   if (lane == 0) red[warp] = part;
@@ -449,7 +464,7 @@ int check_attn(const algx_attn_config* cfg, int64_t B, int64_t H, int64_t T, int
   ALGX_REQUIRE(cfg, "attention: NULL config");
   ALGX_REQUIRE(D == kD, "attention: head dim must be 64");
   ALGX_REQUIRE(B >= 1 && H >= 1 && T >= 1, "attention: empty shape");
-  ALGX_REQUIRE(T <= (1 << 24) && B * H <= 65535, "attention: shape too large");
+  ALGX_REQUIRE(T <= (1 << 23) && B * H <= 65535, "attention: shape too large");
   ALGX_REQUIRE(H <= 1024, "attention: at most 1024 heads");
   ALGX_REQUIRE(dtype == ALGX_F32 || dtype == ALGX_BF16, "attention: dtype must be float32 or bfloat16");
   ALGX_REQUIRE(cfg->kind == ALGX_ATTN_ASINH || cfg->kind == ALGX_ATTN_SOFTMAX, "attention: unknown kind");

@@ -37,7 +37,7 @@ constexpr int kTileBytes = kTile * 64 * 2;  // 128 rows x 64 bf16
 constexpr int kFwdStages = 2;
 constexpr int kFwdThreads = 192;
 constexpr int kFwdSmem = kTileBytes * (1 + 2 * kFwdStages) + 1024;
-constexpr int kBwdThreads = 320;
+constexpr int kBwdThreads = 448;
 constexpr int kBwdSmem = kTileBytes * 10 + 4 * kTile * 4 + 1024;
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
@@ -53,7 +53,84 @@ __device__ __forceinline__ float weight(float x, float clamp, float& r) {
   return ipow_t<N>(fmaf(rad, r, x));
 }
 
+// Weights of 32 scores of one row (one TMEM chunk): p = rho(x)^N with the
+// fast radical, packed to bf16 pairs for the P.V MMA; returns the fp32 sum.
+// DIAG masks keys after the query (col > r) on the diagonal tile only.
+template <int N, bool CLIP, bool DIAG>
+__device__ __forceinline__ float weights_chunk(const uint32_t (&sv)[32], uint32_t (&pk)[16], float clamp, int col0,
+                                               int r) {
+  const float2 one = make_float2(1.f, 1.f);
+  float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    float2 x = make_float2(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1]));
+    if constexpr (CLIP) {
+      x.x = fminf(x.x, clamp);
+      x.y = fminf(x.y, clamp);
+    }
+    const float2 rad = fma2(x, x, one);
+    const float2 rr = make_float2(rsqrt_fast(rad.x), rsqrt_fast(rad.y));
+    float2 p = ipow2_t<N>(fma2(rad, rr, x));
+    if constexpr (DIAG) {
+      if (col0 + 2 * i > r) p.x = 0.f;
+      if (col0 + 2 * i + 1 > r) p.y = 0.f;
+    }
+    acc = add2(acc, p);
+    pk[i] = pack_bf16x2(p.x, p.y);
+  }
+  return acc.x + acc.y;
+}
+
+// p and ds (without the slope n) of 32 scores of one key row against 32
+// query columns (kernels/flash.py:333-361), packed to bf16 pairs.
+template <int N, bool CLIP, bool INV, bool DIAG>
+__device__ __forceinline__ void grads_chunk(const uint32_t (&sv)[32], const uint32_t (&pv)[32],
+                                            const float* __restrict__ st, const float* __restrict__ dd,
+                                            uint32_t (&pk)[16], uint32_t (&dk)[16], float clamp, int col0, int r) {
+  const float2 one = make_float2(1.f, 1.f);
+#pragma unroll
+  for (int i4 = 0; i4 < 8; ++i4) {
+    const float4 s4 = *reinterpret_cast<const float4*>(st + 4 * i4);
+    const float4 d4 = *reinterpret_cast<const float4*>(dd + 4 * i4);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int i = 2 * i4 + h;
+      const float2 sc = make_float2(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1]));
+      float2 x = sc;
+      if constexpr (CLIP) {
+        x.x = fminf(x.x, clamp);
+        x.y = fminf(x.y, clamp);
+      }
+      const float2 rad = fma2(x, x, one);
+      const float2 rr = make_float2(rsqrt_fast(rad.x), rsqrt_fast(rad.y));
+      const float2 rho = fma2(rad, rr, x);
+      const float2 stc = h ? make_float2(s4.z, s4.w) : make_float2(s4.x, s4.y);
+      const float2 dic = h ? make_float2(d4.z, d4.w) : make_float2(d4.x, d4.y);
+      float2 p = INV ? mul2(ipow2_t<N>(rho), stc) : ipow2_t<N>(mul2(rho, stc));
+      const float2 dpv = make_float2(__uint_as_float(pv[2 * i]), __uint_as_float(pv[2 * i + 1]));
+      float2 ds = mul2(mul2(p, sub2(dpv, dic)), rr);
+      if constexpr (CLIP) {
+        if (!(sc.x < clamp)) ds.x = 0.f;
+        if (!(sc.y < clamp)) ds.y = 0.f;
+      }
+      if constexpr (DIAG) {
+        if (col0 + 2 * i < r) p.x = ds.x = 0.f;
+        if (col0 + 2 * i + 1 < r) p.y = ds.y = 0.f;
+      }
+      pk[i] = pack_bf16x2(p.x, p.y);
+      dk[i] = pack_bf16x2(ds.x, ds.y);
+    }
+  }
+}
+
 // ---------------------------------------------------------------- forward
+// The key loop runs over 64-key sub-tiles u = 2j + h of the 128-key TMA
+// tiles j. TMEM (256 columns): three score buffers B[u % 3] = base + 64(u % 3)
+// (fp32, 128 x 64) and O = base + 192 (fp32, 128 x 64). The weight warps read
+// S_u into registers and write the bf16 P_u into the first 32 columns of the
+// same buffer; O += P_u V reads it there. An MMA takes ~1000 cycles from
+// issue to a visible completion, so the MMA thread keeps S two sub-tiles
+// ahead: S_{u+3} is issued into buffer u % 3 as soon as P_u.V has completed.
 template <int N, bool CLIP>
 __global__ void __launch_bounds__(kFwdThreads, 2)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -67,7 +144,7 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
   uint8_t* sQ = smem;
   uint8_t* sK = smem + kTileBytes;
   uint8_t* sV = sK + kFwdStages * kTileBytes;
-  __shared__ uint64_t bar_q, bar_s_full, bar_p_full, bar_p_free, bar_o_full;
+  __shared__ uint64_t bar_q, bar_o_full, bar_s_full[3], bar_p_full[3], bar_p_free[3];
   __shared__ uint64_t bar_kv_full[kFwdStages], bar_kv_empty[kFwdStages];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
@@ -75,17 +152,22 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nq = T / kTile;
-  const int qt = nq - 1 - (int)blockIdx.x;  // longest rows first
-  const int bh = blockIdx.y;
-  const int nk = qt + 1;
+  // The scheduler dispatches blockIdx.x fastest: heads along x and the query
+  // tile along y (reversed) start every head's longest rows first.
+  const int qt = nq - 1 - (int)blockIdx.y;
+  const int bh = blockIdx.x;
+  const int nk = qt + 1;   // 128-key tiles
+  const int nu = 2 * nk;   // 64-key sub-tiles
   const int row_base = bh * T;
 
   if (threadIdx.x == 0) {
     mbar_init(&bar_q, 1);
-    mbar_init(&bar_s_full, 1);
-    mbar_init(&bar_p_full, 4);
-    mbar_init(&bar_p_free, 1);
     mbar_init(&bar_o_full, 1);
+    for (int b = 0; b < 3; ++b) {
+      mbar_init(&bar_s_full[b], 1);
+      mbar_init(&bar_p_full[b], 4);
+      mbar_init(&bar_p_free[b], 1);
+    }
     for (int s = 0; s < kFwdStages; ++s) {
       mbar_init(&bar_kv_full[s], 1);
       mbar_init(&bar_kv_empty[s], 1);
@@ -100,7 +182,7 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tS = tmem_base, tO = tmem_base + 128, tP = tmem_base + 192;
+  const uint32_t tS = tmem_base, tO = tmem_base + 192;
 
   if (warp == 4) {
     if (lane == 0) {
@@ -128,38 +210,41 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
     }
   } else if (warp == 5) {
     if (lane == 0) {
-      const uint32_t idS = idesc_bf16_f32(128, 128, 0, 0);
+      const uint32_t idS = idesc_bf16_f32(128, 64, 0, 0);
       const uint32_t idO = idesc_bf16_f32(128, 64, 0, 1);
       const uint32_t q0 = smem_u32(sQ), k0 = smem_u32(sK), v0 = smem_u32(sV);
-      bool ok = mbar_wait(&bar_q, 0, abort_v, dev_err);
-      for (int j = 0; ok && j < nk; ++j) {
-        const int s = j % kFwdStages;
-        if (!mbar_wait(&bar_kv_full[s], (j / kFwdStages) & 1, abort_v, dev_err)) break;
-        if (j > 0 && !mbar_wait(&bar_p_full, (j - 1) & 1, abort_v, dev_err)) break;
+      // S_w = Q K_w^T into buffer w % 3 (K rows of half w & 1 of tile w >> 1)
+      auto issue_s = [&](int w) -> bool {
+        const int b = w % 3, j = w >> 1, s = j % kFwdStages;
+        if ((w & 1) == 0 && !mbar_wait(&bar_kv_full[s], (j / kFwdStages) & 1, abort_v, dev_err)) return false;
+        if (w >= 3 && !mbar_wait(&bar_p_free[b], (w / 3 - 1) & 1, abort_v, dev_err)) return false;
         tc_fence_after();
-        const uint32_t kb = k0 + s * kTileBytes;
+        const uint32_t kb = k0 + s * kTileBytes + (w & 1) * (kTileBytes / 2);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          mma_ss(tS, desc_sw128(q0 + k * 32, 16, 1024), desc_sw128(kb + k * 32, 16, 1024), idS, k > 0);
-        mma_commit(&bar_s_full);
-        if (j > 0) {
-          const int sp = (j - 1) % kFwdStages;
-          const uint32_t vb = v0 + sp * kTileBytes;
-#pragma unroll
-          for (int k = 0; k < 8; ++k)
-            mma_ts(tO, tP + k * 8, desc_sw128(vb + k * 2048, 8192, 1024), idO, (j - 1 > 0 || k > 0));
-          mma_commit(&bar_p_free);
-          mma_commit(&bar_kv_empty[sp]);
-        }
-      }
-      if (!*abort_v && mbar_wait(&bar_p_full, (nk - 1) & 1, abort_v, dev_err)) {
+          mma_ss(tS + 64 * b, desc_sw128(q0 + k * 32, 16, 1024), desc_sw128(kb + k * 32, 16, 1024), idS, k > 0);
+        mma_commit(&bar_s_full[b]);
+        return true;
+      };
+      // O += P_w V_w, P_w in the first 32 columns of buffer w % 3
+      auto pv = [&](int w) -> bool {
+        const int b = w % 3, j = w >> 1, s = j % kFwdStages;
+        if (!mbar_wait(&bar_p_full[b], (w / 3) & 1, abort_v, dev_err)) return false;
         tc_fence_after();
-        const int sp = (nk - 1) % kFwdStages;
-        const uint32_t vb = v0 + sp * kTileBytes;
+        const uint32_t vb = v0 + s * kTileBytes + (w & 1) * (kTileBytes / 2);
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          mma_ts(tO, tP + k * 8, desc_sw128(vb + k * 2048, 8192, 1024), idO, (nk - 1 > 0 || k > 0));
-        mma_commit(&bar_o_full);
+        for (int k = 0; k < 4; ++k)
+          mma_ts(tO, tS + 64 * b + k * 8, desc_sw128(vb + k * 2048, 8192, 1024), idO, (w > 0 || k > 0));
+        mma_commit(&bar_p_free[b]);
+        if (w & 1) mma_commit(&bar_kv_empty[s]);
+        return true;
+      };
+      bool ok = mbar_wait(&bar_q, 0, abort_v, dev_err);
+      for (int w = 0; ok && w < 2 && w < nu; ++w) ok = issue_s(w);
+      for (int u = 0; ok && u < nu; ++u) {
+        if (!pv(u)) break;
+        if (u + 2 < nu && !issue_s(u + 2)) break;
+        if (u == nu - 1) mma_commit(&bar_o_full);
       }
     }
   } else {
@@ -169,58 +254,48 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
     float l = 0.f, rr;
     if (cfg.has_sink) l = weight<N, CLIP>(sink[bh % H], cfg.clamp, rr);
     bool ok = true;
-    for (int j = 0; j < nk; ++j) {
-      if (!mbar_wait_warp(&bar_s_full, j & 1, abort_v, dev_err)) {
+    for (int u = 0; u < nu; ++u) {
+      const int b = u % 3;
+      if (!mbar_wait_warp(&bar_s_full[b], (u / 3) & 1, abort_v, dev_err)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const bool diag = j == qt;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sv[32];
-        tmem_ld32(tS + lane_off + c * 32, sv);
-        uint32_t pk[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float p0 = weight<N, CLIP>(__uint_as_float(sv[2 * i]), cfg.clamp, rr);
-          float p1 = weight<N, CLIP>(__uint_as_float(sv[2 * i + 1]), cfg.clamp, rr);
-          if (diag) {
-            const int col = c * 32 + 2 * i;
-            if (col > r) p0 = 0.f;
-            if (col + 1 > r) p1 = 0.f;
-          }
-          l += p0 + p1;
-          pk[i] = pack_bf16x2(p0, p1);
-        }
-        if (c == 0 && j > 0 && !mbar_wait_warp(&bar_p_free, (j - 1) & 1, abort_v, dev_err)) {
-          ok = false;
-          break;
-        }
-        tmem_st16(tP + lane_off + c * 16, pk);
+      uint32_t sa[32], sb[32];
+      tmem_ld32x2(tS + 64 * b + lane_off, sa, tS + 64 * b + 32 + lane_off, sb);
+      const int col0 = 64 * (u & 1);  // key offset within the 128-key tile
+      uint32_t pa[16], pb[16];
+      if ((u >> 1) == qt) {
+        l += weights_chunk<N, CLIP, true>(sa, pa, cfg.clamp, col0, r);
+        l += weights_chunk<N, CLIP, true>(sb, pb, cfg.clamp, col0 + 32, r);
+      } else {
+        l += weights_chunk<N, CLIP, false>(sa, pa, cfg.clamp, col0, r);
+        l += weights_chunk<N, CLIP, false>(sb, pb, cfg.clamp, col0 + 32, r);
       }
-      if (!ok) break;
+      tmem_st16(tS + 64 * b + lane_off, pa);
+      tmem_st16(tS + 64 * b + 16 + lane_off, pb);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar_p_full);
+      if (lane == 0) mbar_arrive(&bar_p_full[b]);
     }
     if (ok && mbar_wait_warp(&bar_o_full, 0, abort_v, dev_err)) {
       tc_fence_after();
       const float inv = 1.f / l;
       const size_t row = (size_t)row_base + (size_t)qt * kTile + r;
       uint4* dst = reinterpret_cast<uint4*>(o + row * 64);
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        uint32_t ov[32];
-        tmem_ld32(tO + lane_off + c * 32, ov);
+      uint32_t oa[32], ob[32];
+      tmem_ld32x2(tO + lane_off, oa, tO + lane_off + 32, ob);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+      for (int c = 0; c < 2; ++c) {
+        const uint32_t* ov = c == 0 ? oa : ob;
+#pragma unroll
+        for (int un = 0; un < 4; ++un) {
           uint4 w;
-          w.x = pack_bf16x2(__uint_as_float(ov[8 * u + 0]) * inv, __uint_as_float(ov[8 * u + 1]) * inv);
-          w.y = pack_bf16x2(__uint_as_float(ov[8 * u + 2]) * inv, __uint_as_float(ov[8 * u + 3]) * inv);
-          w.z = pack_bf16x2(__uint_as_float(ov[8 * u + 4]) * inv, __uint_as_float(ov[8 * u + 5]) * inv);
-          w.w = pack_bf16x2(__uint_as_float(ov[8 * u + 6]) * inv, __uint_as_float(ov[8 * u + 7]) * inv);
-          dst[c * 4 + u] = w;
+          w.x = pack_bf16x2(__uint_as_float(ov[8 * un + 0]) * inv, __uint_as_float(ov[8 * un + 1]) * inv);
+          w.y = pack_bf16x2(__uint_as_float(ov[8 * un + 2]) * inv, __uint_as_float(ov[8 * un + 3]) * inv);
+          w.z = pack_bf16x2(__uint_as_float(ov[8 * un + 4]) * inv, __uint_as_float(ov[8 * un + 5]) * inv);
+          w.w = pack_bf16x2(__uint_as_float(ov[8 * un + 6]) * inv, __uint_as_float(ov[8 * un + 7]) * inv);
+          dst[c * 4 + un] = w;
         }
       }
       stat[row] = e.inv_stat ? inv : inv_root(l, N);
@@ -252,6 +327,13 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int col16) {
   return half * kTileBytes + row * 128 + ((u ^ (row & 7)) << 4);
 }
 
+// Backward loop over 64-query sub-tiles u = 2*ii + h of the 128-query tiles
+// ii (h = u & 1 is also the buffer index b). TMEM (512 columns):
+//   S^T[b] = base + 64b, dP^T[b] = base + 128 + 64b (fp32, 128 keys x 64
+//   queries), dV = base + 256, dK = base + 320, dQ_tile = base + 384.
+// Shared memory keeps P^T and dS^T of the two halves of a query tile side by
+// side (two 128B-swizzled 64-column halves), which is exactly the MN-major
+// A operand of dQ_tile = dS K once both halves are written.
 template <int N, bool CLIP, bool INV_STAT>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -271,35 +353,41 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint8_t* sdST = smem + 8 * kTileBytes;  // idem
   float* sStat = reinterpret_cast<float*>(smem + 10 * kTileBytes);  // [2][128]
   float* sDi = sStat + 2 * kTile;                                    // [2][128]
-  __shared__ uint64_t bar_kv, bar_st_full, bar_ps_ready, bar_ps_free, bar_dq_full, bar_dq_free, bar_fin;
+  __shared__ uint64_t bar_kv, bar_dq_full, bar_dq_free, bar_fin;
+  __shared__ uint64_t bar_st_full[2], bar_st_free[2], bar_ps_ready[2], bar_ps_free[2];
   __shared__ uint64_t bar_qd_full[2], bar_qd_empty[2];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
   volatile int* abort_v = &abort_flag;
 
+  // warps 0-7: score gradients (warp w: TMEM lanes 32*(w%4).., 32 query columns 32*(w/4).. of a sub-tile)
+  // warps 8-11: dQ drain; warp 12: TMA producer (+ TMEM owner); warp 13: MMA issuer
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nq = T / kTile;
-  const int kt = (int)blockIdx.x;  // key tile; kt = 0 has the most query tiles
-  const int bh = blockIdx.y;
+  // heads along x, key tiles along y: key tile 0 (the most query tiles) first
+  const int kt = (int)blockIdx.y;
+  const int bh = blockIdx.x;
   const int row_base = bh * T;
   const int ni = nq - kt;  // query tiles kt .. nq-1
+  const int nu = 2 * ni;   // 64-query sub-tiles
 
   if (threadIdx.x == 0) {
     mbar_init(&bar_kv, 1);
-    mbar_init(&bar_st_full, 1);
-    mbar_init(&bar_ps_ready, 4);
-    mbar_init(&bar_ps_free, 1);
     mbar_init(&bar_dq_full, 1);
     mbar_init(&bar_dq_free, 4);
     mbar_init(&bar_fin, 1);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(&bar_qd_full[s], 1);
-      mbar_init(&bar_qd_empty[s], 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bar_st_full[b], 1);
+      mbar_init(&bar_st_free[b], 8);
+      mbar_init(&bar_ps_ready[b], 8);
+      mbar_init(&bar_ps_free[b], 1);
+      mbar_init(&bar_qd_full[b], 1);
+      mbar_init(&bar_qd_empty[b], 1);
     }
     fence_mbar_init();
     abort_flag = 0;
   }
-  if (warp == 8) {
+  if (warp == 12) {
     tmem_alloc(&tmem_base, 512);
     tmem_relinquish();
   }
@@ -309,7 +397,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const uint32_t tS = tmem_base, tdP = tmem_base + 128, tdV = tmem_base + 256, tdK = tmem_base + 320,
                  tdQ = tmem_base + 384;
 
-  if (warp == 8) {
+  if (warp == 12) {
     // ----- producer
     if (lane == 0) {
       prefetch_tmap(&tq);
@@ -338,27 +426,31 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           }
       }
     }
-  } else if (warp == 9) {
+  } else if (warp == 13) {
     // ----- MMA issuer
     if (lane == 0) {
-      const uint32_t idS = idesc_bf16_f32(128, 128, 0, 0);
+      const uint32_t idS = idesc_bf16_f32(128, 64, 0, 0);
       const uint32_t idKM = idesc_bf16_f32(128, 64, 0, 1);  // A K-major smem, B MN-major
       const uint32_t idMM = idesc_bf16_f32(128, 64, 1, 1);  // A MN-major smem, B MN-major
       const uint32_t k0 = smem_u32(sK), v0 = smem_u32(sV), q0 = smem_u32(sQ), do0 = smem_u32(sdO);
       const uint32_t pt0 = smem_u32(sPT), ds0 = smem_u32(sdST);
       bool ok = mbar_wait(&bar_kv, 0, abort_v, dev_err);
-      auto consume = [&](int ii) -> bool {  // dV, dK, dQ of query tile ii
-        const int s = ii & 1;
-        const uint32_t qb = q0 + s * kTileBytes, db = do0 + s * kTileBytes;
+      // dV, dK of sub-tile w; after the second half, dQ of its query tile.
+      auto consume = [&](int w) -> bool {
+        const int b = w & 1, ii = w >> 1, s = ii & 1;
+        if (!mbar_wait(&bar_ps_ready[b], (w >> 1) & 1, abort_v, dev_err)) return false;
         tc_fence_after();
+        const uint32_t qb = q0 + s * kTileBytes + b * (kTileBytes / 2);
+        const uint32_t db = do0 + s * kTileBytes + b * (kTileBytes / 2);
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          mma_ss(tdV, desc_sw128(pt0 + (k >> 2) * kTileBytes + (k & 3) * 32, 16, 1024),
-                 desc_sw128(db + k * 2048, 8192, 1024), idKM, (ii > 0 || k > 0));
+        for (int k = 0; k < 4; ++k)
+          mma_ss(tdV, desc_sw128(pt0 + b * kTileBytes + k * 32, 16, 1024), desc_sw128(db + k * 2048, 8192, 1024),
+                 idKM, (w > 0 || k > 0));
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          mma_ss(tdK, desc_sw128(ds0 + (k >> 2) * kTileBytes + (k & 3) * 32, 16, 1024),
-                 desc_sw128(qb + k * 2048, 8192, 1024), idKM, (ii > 0 || k > 0));
+        for (int k = 0; k < 4; ++k)
+          mma_ss(tdK, desc_sw128(ds0 + b * kTileBytes + k * 32, 16, 1024), desc_sw128(qb + k * 2048, 8192, 1024),
+                 idKM, (w > 0 || k > 0));
+        if (b == 0) return true;
         mma_commit(&bar_qd_empty[s]);
         if (ii > 0 && !mbar_wait(&bar_dq_free, (ii - 1) & 1, abort_v, dev_err)) return false;
         tc_fence_after();
@@ -367,144 +459,121 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           mma_ss(tdQ, desc_sw128(ds0 + k * 2048, kTileBytes, 1024), desc_sw128(k0 + k * 2048, 8192, 1024), idMM,
                  k > 0);
         mma_commit(&bar_dq_full);
-        mma_commit(&bar_ps_free);
+        mma_commit(&bar_ps_free[0]);
+        mma_commit(&bar_ps_free[1]);
         return true;
       };
-      for (int ii = 0; ok && ii < ni; ++ii) {
-        const int s = ii & 1;
-        if (!mbar_wait(&bar_qd_full[s], (ii >> 1) & 1, abort_v, dev_err)) break;
-        if (ii > 0 && !mbar_wait(&bar_ps_ready, (ii - 1) & 1, abort_v, dev_err)) break;
+      for (int u = 0; ok && u < nu; ++u) {
+        const int b = u & 1, ii = u >> 1, s = ii & 1;
+        if (b == 0 && !mbar_wait(&bar_qd_full[s], (ii >> 1) & 1, abort_v, dev_err)) break;
+        if (u >= 2 && !mbar_wait(&bar_st_free[b], ((u >> 1) - 1) & 1, abort_v, dev_err)) break;
         tc_fence_after();
-        const uint32_t qb = q0 + s * kTileBytes, db = do0 + s * kTileBytes;
+        const uint32_t qb = q0 + s * kTileBytes + b * (kTileBytes / 2);
+        const uint32_t db = do0 + s * kTileBytes + b * (kTileBytes / 2);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          mma_ss(tS, desc_sw128(k0 + k * 32, 16, 1024), desc_sw128(qb + k * 32, 16, 1024), idS, k > 0);
+          mma_ss(tS + 64 * b, desc_sw128(k0 + k * 32, 16, 1024), desc_sw128(qb + k * 32, 16, 1024), idS, k > 0);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          mma_ss(tdP, desc_sw128(v0 + k * 32, 16, 1024), desc_sw128(db + k * 32, 16, 1024), idS, k > 0);
-        mma_commit(&bar_st_full);
-        if (ii > 0 && !consume(ii - 1)) break;
+          mma_ss(tdP + 64 * b, desc_sw128(v0 + k * 32, 16, 1024), desc_sw128(db + k * 32, 16, 1024), idS, k > 0);
+        mma_commit(&bar_st_full[b]);
+        if (u >= 1 && !consume(u - 1)) {
+          ok = false;
+          break;
+        }
       }
-      if (!*abort_v && mbar_wait(&bar_ps_ready, (ni - 1) & 1, abort_v, dev_err) && consume(ni - 1))
-        mma_commit(&bar_fin);
+      if (ok && !*abort_v && consume(nu - 1)) mma_commit(&bar_fin);
     }
-  } else if (warp < 4) {
-    // ----- score-gradient warps: thread r owns key row kt*128 + r (TMEM lane r)
-    const int r = threadIdx.x;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+  } else if (warp < 8) {
+    // ----- score-gradient warps
+    const int q4 = warp & 3, hc = warp >> 2;
+    const int r = q4 * 32 + lane;  // key row within the tile (TMEM lane)
+    const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     bool ok = true;
-    for (int ii = 0; ii < ni; ++ii) {
-      const int s = ii & 1;
-      if (!mbar_wait_warp(&bar_st_full, ii & 1, abort_v, dev_err)) {
+    for (int u = 0; u < nu; ++u) {
+      const int b = u & 1, ii = u >> 1, s = ii & 1;
+      if (!mbar_wait_warp(&bar_st_full[b], (u >> 1) & 1, abort_v, dev_err)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const bool diag = ii == 0;  // query tile == key tile
-      const float* st = sStat + s * kTile;
-      const float* dd = sDi + s * kTile;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t sv[32], pv[32];
-        tmem_ld32(tS + lane_off + c * 32, sv);
-        tmem_ld32(tdP + lane_off + c * 32, pv);
-        uint32_t pk[16], dk2[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float pp[2], dd2[2];
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int col = c * 32 + 2 * i + h;
-            const float sc = __uint_as_float(sv[2 * i + h]);
-            const float x = CLIP ? fminf(sc, cfg.clamp) : sc;
-            const float rad = fmaf(x, x, 1.f);
-            const float rr = rsqrtf(rad);
-            const float rho = fmaf(rad, rr, x);
-            const float stc = st[col];
-            float p = INV_STAT ? ipow_t<N>(rho) * stc : ipow_t<N>(rho * stc);
-            float ds = p * (__uint_as_float(pv[2 * i + h]) - dd[col]) * rr;
-            if constexpr (CLIP) ds = sc < cfg.clamp ? ds : 0.f;
-            if (diag && col < r) {
-              p = 0.f;
-              ds = 0.f;
-            }
-            pp[h] = p;
-            dd2[h] = ds;
-          }
-          pk[i] = pack_bf16x2(pp[0], pp[1]);
-          dk2[i] = pack_bf16x2(dd2[0], dd2[1]);
-        }
-        if (c == 0 && ii > 0 && !mbar_wait_warp(&bar_ps_free, (ii - 1) & 1, abort_v, dev_err)) {
-          ok = false;
-          break;
-        }
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const uint32_t off = sw128_off(r, c * 4 + u);
-          *reinterpret_cast<uint4*>(sPT + off) = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
-          *reinterpret_cast<uint4*>(sdST + off) =
-              make_uint4(dk2[4 * u], dk2[4 * u + 1], dk2[4 * u + 2], dk2[4 * u + 3]);
-        }
-      }
-      if (!ok) break;
-      fence_proxy_async_smem();
+      uint32_t sv[32], pv[32];
+      tmem_ld32x2(tS + 64 * b + 32 * hc + lane_off, sv, tdP + 64 * b + 32 * hc + lane_off, pv);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar_ps_ready);
+      if (lane == 0) mbar_arrive(&bar_st_free[b]);
+      const int col0 = 64 * b + 32 * hc;  // query column within the 128-query tile
+      const float* st = sStat + s * kTile + col0;
+      const float* dd = sDi + s * kTile + col0;
+      uint32_t pk[16], dk2[16];
+      if (ii == 0)
+        grads_chunk<N, CLIP, INV_STAT, true>(sv, pv, st, dd, pk, dk2, cfg.clamp, col0, r);
+      else
+        grads_chunk<N, CLIP, INV_STAT, false>(sv, pv, st, dd, pk, dk2, cfg.clamp, col0, r);
+      if (ii > 0 && !mbar_wait_warp(&bar_ps_free[b], (ii - 1) & 1, abort_v, dev_err)) {
+        ok = false;
+        break;
+      }
+#pragma unroll
+      for (int un = 0; un < 4; ++un) {
+        const uint32_t off = sw128_off(r, col0 / 8 + un);
+        *reinterpret_cast<uint4*>(sPT + off) = make_uint4(pk[4 * un], pk[4 * un + 1], pk[4 * un + 2], pk[4 * un + 3]);
+        *reinterpret_cast<uint4*>(sdST + off) =
+            make_uint4(dk2[4 * un], dk2[4 * un + 1], dk2[4 * un + 2], dk2[4 * un + 3]);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar_ps_ready[b]);
     }
     if (ok && mbar_wait_warp(&bar_fin, 0, abort_v, dev_err)) {
       tc_fence_after();
       const size_t row = (size_t)row_base + (size_t)kt * kTile + r;
       const float slope = (float)N;
-#pragma unroll 1
+      uint32_t vk[32], vv[32];
+      tmem_ld32x2(tdK + lane_off + hc * 32, vk, tdV + lane_off + hc * 32, vv);
+#pragma unroll
       for (int which = 0; which < 2; ++which) {
         __nv_bfloat16* dst = which == 0 ? dk : dv;
-        const uint32_t tsrc = which == 0 ? tdK : tdV;
+        const uint32_t* v = which == 0 ? vk : vv;
         const float f = which == 0 ? slope : 1.f;
-        uint4* d4 = reinterpret_cast<uint4*>(dst + row * 64);
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          uint32_t v[32];
-          tmem_ld32(tsrc + lane_off + c * 32, v);
+        uint4* d4 = reinterpret_cast<uint4*>(dst + row * 64 + hc * 32);
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            uint4 w;
-            w.x = pack_bf16x2(__uint_as_float(v[8 * u + 0]) * f, __uint_as_float(v[8 * u + 1]) * f);
-            w.y = pack_bf16x2(__uint_as_float(v[8 * u + 2]) * f, __uint_as_float(v[8 * u + 3]) * f);
-            w.z = pack_bf16x2(__uint_as_float(v[8 * u + 4]) * f, __uint_as_float(v[8 * u + 5]) * f);
-            w.w = pack_bf16x2(__uint_as_float(v[8 * u + 6]) * f, __uint_as_float(v[8 * u + 7]) * f);
-            d4[c * 4 + u] = w;
-          }
+        for (int un = 0; un < 4; ++un) {
+          uint4 w;
+          w.x = pack_bf16x2(__uint_as_float(v[8 * un + 0]) * f, __uint_as_float(v[8 * un + 1]) * f);
+          w.y = pack_bf16x2(__uint_as_float(v[8 * un + 2]) * f, __uint_as_float(v[8 * un + 3]) * f);
+          w.z = pack_bf16x2(__uint_as_float(v[8 * un + 4]) * f, __uint_as_float(v[8 * un + 5]) * f);
+          w.w = pack_bf16x2(__uint_as_float(v[8 * un + 6]) * f, __uint_as_float(v[8 * un + 7]) * f);
+          d4[un] = w;
         }
       }
     }
   } else {
-    // ----- dQ drain warps 4-7: thread owns query row qi*128 + (threadIdx.x - 128) (TMEM lane)
-    const int r = threadIdx.x - 128;
-    const uint32_t lane_off = (uint32_t)((warp - 4) * 32) << 16;
+    // ----- dQ drain warps 8-11: thread owns query row qi*128 + r (TMEM lane r)
+    const int r = (warp - 8) * 32 + lane;
+    const uint32_t lane_off = (uint32_t)((warp - 8) * 32) << 16;
     for (int ii = 0; ii < ni; ++ii) {
       if (!mbar_wait_warp(&bar_dq_full, ii & 1, abort_v, dev_err)) break;
       tc_fence_after();
       uint32_t a[32], b[32];
-      tmem_ld32(tdQ + lane_off, a);
-      tmem_ld32(tdQ + lane_off + 32, b);
+      tmem_ld32x2(tdQ + lane_off, a, tdQ + lane_off + 32, b);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar_dq_free);
       float* dst = dq_acc + ((size_t)row_base + (size_t)(kt + ii) * kTile + r) * 64;
 #pragma unroll
-      for (int u = 0; u < 8; ++u)
-        red_add_v4(dst + 4 * u, __uint_as_float(a[4 * u]), __uint_as_float(a[4 * u + 1]),
-                   __uint_as_float(a[4 * u + 2]), __uint_as_float(a[4 * u + 3]));
+      for (int un = 0; un < 8; ++un)
+        red_add_v4(dst + 4 * un, __uint_as_float(a[4 * un]), __uint_as_float(a[4 * un + 1]),
+                   __uint_as_float(a[4 * un + 2]), __uint_as_float(a[4 * un + 3]));
 #pragma unroll
-      for (int u = 0; u < 8; ++u)
-        red_add_v4(dst + 32 + 4 * u, __uint_as_float(b[4 * u]), __uint_as_float(b[4 * u + 1]),
-                   __uint_as_float(b[4 * u + 2]), __uint_as_float(b[4 * u + 3]));
+      for (int un = 0; un < 8; ++un)
+        red_add_v4(dst + 32 + 4 * un, __uint_as_float(b[4 * un]), __uint_as_float(b[4 * un + 1]),
+                   __uint_as_float(b[4 * un + 2]), __uint_as_float(b[4 * un + 3]));
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 8) tmem_dealloc(tmem_base, 512);
+  if (warp == 12) tmem_dealloc(tmem_base, 512);
 }
 
 // dq = bf16(acc * n * scale), only when the fast path ran (unshifted branch).
@@ -537,7 +606,7 @@ int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& 
                cudaStream_t st) {
   auto kern = attn_fwd_tc_kernel<N, CLIP>;
   ALGX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem));
-  dim3 grid((unsigned)(T / kTile), (unsigned)(B * H));
+  dim3 grid((unsigned)(B * H), (unsigned)(T / kTile));
   kern<<<grid, kFwdThreads, kFwdSmem, st>>>(tq, tk, tv, cfg, sink, guard, static_cast<__nv_bfloat16*>(o), stat,
                                             (int)H, (int)T, device_error_word());
   ALGX_LAUNCHED("attn_fwd_tc launch");
@@ -550,7 +619,7 @@ int launch_bwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& 
                void* dk, void* dv, int64_t B, int64_t H, int64_t T, cudaStream_t st) {
   auto kern = attn_bwd_tc_kernel<N, CLIP, INV>;
   ALGX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem));
-  dim3 grid((unsigned)(T / kTile), (unsigned)(B * H));
+  dim3 grid((unsigned)(B * H), (unsigned)(T / kTile));
   kern<<<grid, kBwdThreads, kBwdSmem, st>>>(tq, tk, tv, tdo, cfg, stat, di, guard, dq_acc,
                                             static_cast<__nv_bfloat16*>(dk), static_cast<__nv_bfloat16*>(dv),
                                             (int)T, device_error_word());

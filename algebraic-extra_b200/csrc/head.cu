@@ -188,7 +188,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
             if (i < nvalid) {
               const float x = fminf(__uint_as_float(zr[i]) * a.cfg.inv_c, a.cfg.clamp);
               const float rad = fmaf(x, x, 1.f);
-              s += ipow_t<NPOW>(fmaf(rad, rsqrtf(rad), x));
+              s += ipow_t<NPOW>(fmaf(rad, rsqrt_fast(rad), x));
             }
           }
           l += s;
@@ -387,7 +387,7 @@ __global__ void __launch_bounds__(kGradThreads, 1)
             } else {
               const float x = fminf(z * c.inv_c, c.clamp);
               const float rad = fmaf(x, x, 1.f);
-              const float rr = rsqrtf(rad);
+              const float rr = rsqrt_fast(rad);
               g = (ipow_t<NPOW>(fmaf(rad, rr, x) * st) - y) * rr;
             }
             dzv[h] = valid ? g * scale : 0.f;

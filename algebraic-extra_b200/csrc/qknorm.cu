@@ -117,12 +117,22 @@ __global__ void __launch_bounds__(kThreads) qknorm_bwd_kernel(const T* __restric
   }
 }
 
-__global__ void qknorm_dgain_reduce(const float* __restrict__ partial, int nblocks, float* __restrict__ dgain) {
-  const int c = threadIdx.x;
-  if (c >= kDim) return;
+// dgain[c] = sum_b partial[b][c]: 16 strided partial sums per column, then a
+// fixed-order sum of the 16 (deterministic for a given grid size).
+constexpr int kReduceThreads = 1024;
+__global__ void __launch_bounds__(kReduceThreads) qknorm_dgain_reduce(const float* __restrict__ partial, int nblocks,
+                                                                      float* __restrict__ dgain) {
+  __shared__ float red[kReduceThreads / kDim][kDim];
+  const int c = threadIdx.x % kDim, p = threadIdx.x / kDim;
   float s = 0.f;
-  for (int b = 0; b < nblocks; ++b) s += partial[(int64_t)b * kDim + c];
-  dgain[c] = s;
+  for (int b = p; b < nblocks; b += kReduceThreads / kDim) s += partial[(int64_t)b * kDim + c];
+  red[p][c] = s;
+  __syncthreads();
+  if (threadIdx.x < kDim) {
+    float t = 0.f;
+    for (int i = 0; i < kReduceThreads / kDim; ++i) t += red[i][threadIdx.x];
+    dgain[threadIdx.x] = t;
+  }
 }
 
 template <typename T>
@@ -225,7 +235,7 @@ int algx_qknorm_bwd(const void* x, const float* gain, const void* dy, void* dx, 
                                                         partial, rows, eps);
   }
   ALGX_LAUNCHED("qknorm_bwd launch");
-  qknorm_dgain_reduce<<<1, kDim, 0, st>>>(partial, grid, dgain);
+  qknorm_dgain_reduce<<<1, kReduceThreads, 0, st>>>(partial, grid, dgain);
   ALGX_LAUNCHED("qknorm_dgain_reduce launch");
   return ALGX_OK;
 }
@@ -261,7 +271,7 @@ int algx_qknorm_bwd_noalloc(const void* x, const float* gain, const void* dy, vo
                                                         partial, rows, eps);
   }
   ALGX_LAUNCHED("qknorm_bwd_noalloc launch");
-  qknorm_dgain_reduce<<<1, kDim, 0, st>>>(partial, grid, dgain);
+  qknorm_dgain_reduce<<<1, kReduceThreads, 0, st>>>(partial, grid, dgain);
   ALGX_LAUNCHED("qknorm_dgain_reduce launch");
   return ALGX_OK;
 }
