@@ -17,9 +17,12 @@
 // key row) recompute p = rho^n * stat, ds = p (dp - di) r, write bf16 P^T and
 // dS^T to shared memory (128-byte swizzled K-major); then dV += P^T dO,
 // dK += dS^T Q, and dQ_tile = dS K (the same dS^T buffer read MN-major).
-// Warps 4-7 drain dQ_tile from TMEM into an fp32 accumulator with vector
-// reductions; a final pass scales and rounds it. Every mbarrier wait is
-// bounded (sm100.cuh).
+// dQ_tile alternates between two TMEM buffers; warps 8-11 drain it into a
+// 128-byte-swizzled fp32 staging tile in shared memory, from which one thread
+// adds it to the fp32 accumulator in global memory with two TMA reduce-adds
+// (the reduction runs in L2, off the SM's load/store path). A final pass
+// scales and rounds the accumulator. Every mbarrier wait is bounded
+// (sm100.cuh).
 #include <algorithm>
 
 #include "attn_common.cuh"
@@ -38,7 +41,7 @@ constexpr int kFwdStages = 2;
 constexpr int kFwdThreads = 192;
 constexpr int kFwdSmem = kTileBytes * (1 + 2 * kFwdStages) + 1024;
 constexpr int kBwdThreads = 448;
-constexpr int kBwdSmem = kTileBytes * 10 + 4 * kTile * 4 + 1024;
+constexpr int kBwdSmem = kTileBytes * 13 + 4 * kTile * 4 + 1024;
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
@@ -314,11 +317,6 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
                : "memory");
 }
 
-__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
-               : "memory");
-}
-
 // Byte offset of bf16 element (row, col) in a [128 rows][128 cols] tile kept
 // as two 128-byte-swizzled K-major halves of 64 columns.
 __device__ __forceinline__ uint32_t sw128_off(int row, int col16) {
@@ -330,15 +328,18 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int col16) {
 // Backward loop over 64-query sub-tiles u = 2*ii + h of the 128-query tiles
 // ii (h = u & 1 is also the buffer index b). TMEM (512 columns):
 //   S^T[b] = base + 64b, dP^T[b] = base + 128 + 64b (fp32, 128 keys x 64
-//   queries), dV = base + 256, dK = base + 320, dQ_tile = base + 384.
-// Shared memory keeps P^T and dS^T of the two halves of a query tile side by
-// side (two 128B-swizzled 64-column halves), which is exactly the MN-major
-// A operand of dQ_tile = dS K once both halves are written.
+//   queries), dV = base + 256, dK = base + 320, dQ_tile[ii & 1] = base + 384
+//   + 64 (ii & 1).
+// Shared memory keeps P^T of the two sub-tiles b, freed as soon as dV of the
+// sub-tile has completed, and dS^T of two query tiles, each as two
+// 128B-swizzled 64-column halves side by side: exactly the MN-major A operand
+// of dQ_tile = dS K once both halves are written. With dS^T double-buffered,
+// the next tile's score gradients never wait for this tile's dQ product.
 template <int N, bool CLIP, bool INV_STAT>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                        const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
-                       algx_attn_config cfg, const float* __restrict__ stat, const float* __restrict__ di,
+                       const __grid_constant__ CUtensorMap tdq, algx_attn_config cfg, const float* __restrict__ stat, const float* __restrict__ di,
                        const float* __restrict__ guard, float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dk,
                        __nv_bfloat16* __restrict__ dv, int T, int* dev_err) {
   const Eff e = resolve_variant(cfg, guard);
@@ -349,12 +350,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint8_t* sV = smem + kTileBytes;
   uint8_t* sQ = smem + 2 * kTileBytes;    // 2 stages
   uint8_t* sdO = smem + 4 * kTileBytes;   // 2 stages
-  uint8_t* sPT = smem + 6 * kTileBytes;   // 128 keys x 128 queries bf16 (2 halves)
-  uint8_t* sdST = smem + 8 * kTileBytes;  // idem
-  float* sStat = reinterpret_cast<float*>(smem + 10 * kTileBytes);  // [2][128]
+  uint8_t* sPT = smem + 6 * kTileBytes;   // 128 keys x 64 queries bf16, [2 sub-tiles]
+  uint8_t* sdST = smem + 8 * kTileBytes;  // 128 keys x 128 queries bf16, [2 query tiles][2 halves]
+  uint8_t* sDQ = smem + 12 * kTileBytes;  // fp32 dQ staging: one 128-row x 32-column swizzled box
+  float* sStat = reinterpret_cast<float*>(smem + 13 * kTileBytes);  // [2][128]
   float* sDi = sStat + 2 * kTile;                                    // [2][128]
-  __shared__ uint64_t bar_kv, bar_dq_full, bar_dq_free, bar_fin;
-  __shared__ uint64_t bar_st_full[2], bar_st_free[2], bar_ps_ready[2], bar_ps_free[2];
+  __shared__ uint64_t bar_kv, bar_fin, bar_dq_full[2], bar_dq_free[2], bar_stage_full, bar_stage_free;
+  __shared__ uint64_t bar_st_full[2], bar_st_free[2], bar_ps_ready[2], bar_p_free[2], bar_ds_free[2];
   __shared__ uint64_t bar_qd_full[2], bar_qd_empty[2];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
@@ -373,14 +375,17 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(&bar_kv, 1);
-    mbar_init(&bar_dq_full, 1);
-    mbar_init(&bar_dq_free, 4);
     mbar_init(&bar_fin, 1);
+    mbar_init(&bar_stage_full, 4);
+    mbar_init(&bar_stage_free, 1);
     for (int b = 0; b < 2; ++b) {
+      mbar_init(&bar_dq_full[b], 1);
+      mbar_init(&bar_dq_free[b], 4);
       mbar_init(&bar_st_full[b], 1);
       mbar_init(&bar_st_free[b], 8);
       mbar_init(&bar_ps_ready[b], 8);
-      mbar_init(&bar_ps_free[b], 1);
+      mbar_init(&bar_p_free[b], 1);
+      mbar_init(&bar_ds_free[b], 1);
       mbar_init(&bar_qd_full[b], 1);
       mbar_init(&bar_qd_empty[b], 1);
     }
@@ -395,7 +400,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tS = tmem_base, tdP = tmem_base + 128, tdV = tmem_base + 256, tdK = tmem_base + 320,
-                 tdQ = tmem_base + 384;
+                 tdQ = tmem_base + 384;  // two 64-column buffers
 
   if (warp == 12) {
     // ----- producer
@@ -404,6 +409,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       prefetch_tmap(&tk);
       prefetch_tmap(&tv);
       prefetch_tmap(&tdo);
+      prefetch_tmap(&tdq);
       mbar_expect_tx(&bar_kv, 2 * kTileBytes);
       tma_load_2d(sK, &tk, &bar_kv, 0, row_base + kt * kTile);
       tma_load_2d(sV, &tv, &bar_kv, 0, row_base + kt * kTile);
@@ -433,7 +439,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const uint32_t idKM = idesc_bf16_f32(128, 64, 0, 1);  // A K-major smem, B MN-major
       const uint32_t idMM = idesc_bf16_f32(128, 64, 1, 1);  // A MN-major smem, B MN-major
       const uint32_t k0 = smem_u32(sK), v0 = smem_u32(sV), q0 = smem_u32(sQ), do0 = smem_u32(sdO);
-      const uint32_t pt0 = smem_u32(sPT), ds0 = smem_u32(sdST);
+      const uint32_t pt0 = smem_u32(sPT), dsb = smem_u32(sdST);
       bool ok = mbar_wait(&bar_kv, 0, abort_v, dev_err);
       // dV, dK of sub-tile w; after the second half, dQ of its query tile.
       auto consume = [&](int w) -> bool {
@@ -442,25 +448,27 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         tc_fence_after();
         const uint32_t qb = q0 + s * kTileBytes + b * (kTileBytes / 2);
         const uint32_t db = do0 + s * kTileBytes + b * (kTileBytes / 2);
+        const uint32_t ds0 = dsb + s * 2 * kTileBytes;  // dS^T buffer of query tile ii
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_ss(tdV, desc_sw128(pt0 + b * kTileBytes + k * 32, 16, 1024), desc_sw128(db + k * 2048, 8192, 1024),
                  idKM, (w > 0 || k > 0));
+        mma_commit(&bar_p_free[b]);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_ss(tdK, desc_sw128(ds0 + b * kTileBytes + k * 32, 16, 1024), desc_sw128(qb + k * 2048, 8192, 1024),
                  idKM, (w > 0 || k > 0));
         if (b == 0) return true;
         mma_commit(&bar_qd_empty[s]);
-        if (ii > 0 && !mbar_wait(&bar_dq_free, (ii - 1) & 1, abort_v, dev_err)) return false;
+        const int qb2 = ii & 1;
+        if (ii >= 2 && !mbar_wait(&bar_dq_free[qb2], ((ii >> 1) - 1) & 1, abort_v, dev_err)) return false;
         tc_fence_after();
 #pragma unroll
         for (int k = 0; k < 8; ++k)
-          mma_ss(tdQ, desc_sw128(ds0 + k * 2048, kTileBytes, 1024), desc_sw128(k0 + k * 2048, 8192, 1024), idMM,
-                 k > 0);
-        mma_commit(&bar_dq_full);
-        mma_commit(&bar_ps_free[0]);
-        mma_commit(&bar_ps_free[1]);
+          mma_ss(tdQ + 64 * qb2, desc_sw128(ds0 + k * 2048, kTileBytes, 1024), desc_sw128(k0 + k * 2048, 8192, 1024),
+                 idMM, k > 0);
+        mma_commit(&bar_dq_full[qb2]);
+        mma_commit(&bar_ds_free[s]);
         return true;
       };
       for (int u = 0; ok && u < nu; ++u) {
@@ -510,7 +518,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         grads_chunk<N, CLIP, INV_STAT, true>(sv, pv, st, dd, pk, dk2, cfg.clamp, col0, r);
       else
         grads_chunk<N, CLIP, INV_STAT, false>(sv, pv, st, dd, pk, dk2, cfg.clamp, col0, r);
-      if (ii > 0 && !mbar_wait_warp(&bar_ps_free[b], (ii - 1) & 1, abort_v, dev_err)) {
+      // P^T of sub-tile u - 2 must have been consumed by its dV product,
+      // dS^T of query tile ii - 2 by its dQ product.
+      if (u >= 2 && !mbar_wait_warp(&bar_p_free[b], ((u >> 1) - 1) & 1, abort_v, dev_err)) {
         ok = false;
         break;
       }
@@ -518,7 +528,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       for (int un = 0; un < 4; ++un) {
         const uint32_t off = sw128_off(r, col0 / 8 + un);
         *reinterpret_cast<uint4*>(sPT + off) = make_uint4(pk[4 * un], pk[4 * un + 1], pk[4 * un + 2], pk[4 * un + 3]);
-        *reinterpret_cast<uint4*>(sdST + off) =
+      }
+      if (ii >= 2 && !mbar_wait_warp(&bar_ds_free[s], ((ii >> 1) - 1) & 1, abort_v, dev_err)) {
+        ok = false;
+        break;
+      }
+      uint8_t* ds_tile = sdST + s * 2 * kTileBytes;
+#pragma unroll
+      for (int un = 0; un < 4; ++un) {
+        const uint32_t off = sw128_off(r, col0 / 8 + un);
+        *reinterpret_cast<uint4*>(ds_tile + off) =
             make_uint4(dk2[4 * un], dk2[4 * un + 1], dk2[4 * un + 2], dk2[4 * un + 3]);
       }
       fence_proxy_async_smem();
@@ -552,24 +571,54 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // ----- dQ drain warps 8-11: thread owns query row qi*128 + r (TMEM lane r)
     const int r = (warp - 8) * 32 + lane;
     const uint32_t lane_off = (uint32_t)((warp - 8) * 32) << 16;
+    const bool issuer = warp == 8 && lane == 0;
+    bool ok = true;
     for (int ii = 0; ii < ni; ++ii) {
-      if (!mbar_wait_warp(&bar_dq_full, ii & 1, abort_v, dev_err)) break;
+      const int qb2 = ii & 1;
+      if (!mbar_wait_warp(&bar_dq_full[qb2], (ii >> 1) & 1, abort_v, dev_err)) break;
       tc_fence_after();
       uint32_t a[32], b[32];
-      tmem_ld32x2(tdQ + lane_off, a, tdQ + lane_off + 32, b);
+      tmem_ld32x2(tdQ + 64 * qb2 + lane_off, a, tdQ + 64 * qb2 + lane_off + 32, b);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar_dq_free);
-      float* dst = dq_acc + ((size_t)row_base + (size_t)(kt + ii) * kTile + r) * 64;
+      if (lane == 0) mbar_arrive(&bar_dq_free[qb2]);
+      // Two rounds (columns 0-31, then 32-63) through one 16 KB staging box;
+      // row r, 16-byte chunk c of a 128-byte box row sits at chunk c ^ (r & 7).
+      const int y = row_base + (kt + ii) * kTile;
 #pragma unroll
-      for (int un = 0; un < 8; ++un)
-        red_add_v4(dst + 4 * un, __uint_as_float(a[4 * un]), __uint_as_float(a[4 * un + 1]),
-                   __uint_as_float(a[4 * un + 2]), __uint_as_float(a[4 * un + 3]));
+      for (int h = 0; h < 2; ++h) {
+        const int round = 2 * ii + h;
+        if (round > 0 && !mbar_wait_warp(&bar_stage_free, (round - 1) & 1, abort_v, dev_err)) {
+          ok = false;
+          break;
+        }
+        const uint32_t* v = h == 0 ? a : b;
 #pragma unroll
-      for (int un = 0; un < 8; ++un)
-        red_add_v4(dst + 32 + 4 * un, __uint_as_float(b[4 * un]), __uint_as_float(b[4 * un + 1]),
-                   __uint_as_float(b[4 * un + 2]), __uint_as_float(b[4 * un + 3]));
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<uint4*>(sDQ + r * 128 + ((c ^ (r & 7)) << 4)) =
+              make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar_stage_full);
+        if (issuer) {
+          if (mbar_wait(&bar_stage_full, round & 1, abort_v, dev_err)) {
+            tma_reduce_add_2d(&tdq, sDQ, 32 * h, y);
+            bulk_commit_group();
+            bulk_wait_group_read0();
+            mbar_arrive(&bar_stage_free);
+          } else {
+            ok = false;
+          }
+        }
+        __syncwarp();
+        if (!__all_sync(0xffffffffu, ok)) {
+          ok = false;
+          break;
+        }
+      }
+      if (!ok) break;
     }
+    if (issuer) bulk_wait_group0();
   }
   tc_fence_before();
   __syncthreads();
@@ -615,12 +664,12 @@ int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& 
 
 template <int N, bool CLIP, bool INV>
 int launch_bwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tdo,
-               const algx_attn_config& cfg, const float* stat, const float* di, const float* guard, float* dq_acc,
+               const CUtensorMap& tdq, const algx_attn_config& cfg, const float* stat, const float* di, const float* guard, float* dq_acc,
                void* dk, void* dv, int64_t B, int64_t H, int64_t T, cudaStream_t st) {
   auto kern = attn_bwd_tc_kernel<N, CLIP, INV>;
   ALGX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem));
   dim3 grid((unsigned)(B * H), (unsigned)(T / kTile));
-  kern<<<grid, kBwdThreads, kBwdSmem, st>>>(tq, tk, tv, tdo, cfg, stat, di, guard, dq_acc,
+  kern<<<grid, kBwdThreads, kBwdSmem, st>>>(tq, tk, tv, tdo, tdq, cfg, stat, di, guard, dq_acc,
                                             static_cast<__nv_bfloat16*>(dk), static_cast<__nv_bfloat16*>(dv),
                                             (int)T, device_error_word());
   ALGX_LAUNCHED("attn_bwd_tc launch");
@@ -673,13 +722,15 @@ int tc_attn_bwd(const algx_attn_config& cfg, const void* q_scaled, const void* k
   if (int s = make_maps(ptrs, 4, maps, B * H * T)) return s;
   float* acc = static_cast<float*>(workspace);
   const size_t nacc = (size_t)B * H * T * 64;
+  CUtensorMap tdq;  // fp32 accumulator, reduce-added in 128-row x 32-column boxes
+  if (int s = make_tmap_2d(&tdq, acc, ALGX_F32, 64, (uint64_t)(B * H * T), 256, 32, kTile, true)) return s;
   ALGX_CUDA(cudaMemsetAsync(acc, 0, nacc * sizeof(float), st));
   const bool clip = cfg.mode == ALGX_MODE_CLIPPED;
   // The guarded low branch uses the 1/Z statistic; the clipped link follows cfg.inv_stat.
   const bool inv = clip ? cfg.inv_stat != 0 : true;
   int s;
 #define ALGX_BWD(NN, CC, II) \
-  launch_bwd<NN, CC, II>(maps[0], maps[1], maps[2], maps[3], cfg, stat, di, guard, acc, dk, dv, B, H, T, st)
+  launch_bwd<NN, CC, II>(maps[0], maps[1], maps[2], maps[3], tdq, cfg, stat, di, guard, acc, dk, dv, B, H, T, st)
   if (cfg.n == 16)
     s = clip ? (inv ? ALGX_BWD(16, true, true) : ALGX_BWD(16, true, false)) : ALGX_BWD(16, false, true);
   else if (cfg.n == 8)
