@@ -13,10 +13,15 @@
 //
 // Backward (kernels/flash.py:333-361, 435-627): one CTA per (128-key tile,
 // head). K, V stay resident; query tiles stream through a 2-stage TMA ring.
-// Per query tile: S^T = K Q^T and dP^T = V dO^T in TMEM; warps 0-3 (thread =
-// key row) recompute p = rho^n * stat, ds = p (dp - di) r, write bf16 P^T and
-// dS^T to shared memory (128-byte swizzled K-major); then dV += P^T dO,
-// dK += dS^T Q, and dQ_tile = dS K (the same dS^T buffer read MN-major).
+// Per query tile: S^T = K Q^T and dP^T = V dO^T in TMEM; the score-gradient
+// warps (thread = key row) recompute p = rho^n * stat, ds = p (dp - di) r,
+// write bf16 P^T and dS^T to shared memory (128-byte swizzled K-major); then
+// dV += P^T dO, dK += dS^T Q, and dQ_tile = dS K (the same dS^T buffer read
+// MN-major). The score gradients are computed by two groups of eight warps
+// that take alternate 64-query sub-tiles, so one sub-tile's stores and
+// barrier round trips overlap the next one's arithmetic. A thread waits ~100
+// cycles per tcgen05.mma it issues, so the three groups of products are
+// issued by three threads that keep the tensor pipe fed in parallel.
 // dQ_tile alternates between two TMEM buffers; warps 8-11 drain it into a
 // 128-byte-swizzled fp32 staging tile in shared memory, from which one thread
 // adds it to the fp32 accumulator in global memory with two TMA reduce-adds
@@ -40,7 +45,8 @@ constexpr int kTileBytes = kTile * 64 * 2;  // 128 rows x 64 bf16
 constexpr int kFwdStages = 2;
 constexpr int kFwdThreads = 192;
 constexpr int kFwdSmem = kTileBytes * (1 + 2 * kFwdStages) + 1024;
-constexpr int kBwdThreads = 448;
+constexpr int kBwdThreads = 768;
+constexpr int kBwdGradWarps = 16, kBwdDrain = 16, kBwdProducer = 20;
 constexpr int kBwdSmem = kTileBytes * 13 + 4 * kTile * 4 + 1024;
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
@@ -84,15 +90,16 @@ __device__ __forceinline__ float weights_chunk(const uint32_t (&sv)[32], uint32_
   return acc.x + acc.y;
 }
 
-// p and ds (without the slope n) of 32 scores of one key row against 32
-// query columns (kernels/flash.py:333-361), packed to bf16 pairs.
-template <int N, bool CLIP, bool INV, bool DIAG>
-__device__ __forceinline__ void grads_chunk(const uint32_t (&sv)[32], const uint32_t (&pv)[32],
+// p and ds (without the slope n) of C scores of one key row against C query
+// columns (kernels/flash.py:333-361), packed to bf16 pairs.
+template <int N, bool CLIP, bool INV, bool DIAG, int C>
+__device__ __forceinline__ void grads_chunk(const uint32_t (&sv)[C], const uint32_t (&pv)[C],
                                             const float* __restrict__ st, const float* __restrict__ dd,
-                                            uint32_t (&pk)[16], uint32_t (&dk)[16], float clamp, int col0, int r) {
+                                            uint32_t (&pk)[C / 2], uint32_t (&dk)[C / 2], float clamp, int col0,
+                                            int r) {
   const float2 one = make_float2(1.f, 1.f);
 #pragma unroll
-  for (int i4 = 0; i4 < 8; ++i4) {
+  for (int i4 = 0; i4 < C / 4; ++i4) {
     const float4 s4 = *reinterpret_cast<const float4*>(st + 4 * i4);
     const float4 d4 = *reinterpret_cast<const float4*>(dd + 4 * i4);
 #pragma unroll
@@ -356,14 +363,23 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   float* sStat = reinterpret_cast<float*>(smem + 13 * kTileBytes);  // [2][128]
   float* sDi = sStat + 2 * kTile;                                    // [2][128]
   __shared__ uint64_t bar_kv, bar_fin, bar_dq_full[2], bar_dq_free[2], bar_stage_full, bar_stage_free;
-  __shared__ uint64_t bar_st_full[2], bar_st_free[2], bar_ps_ready[2], bar_p_free[2], bar_ds_free[2];
-  __shared__ uint64_t bar_qd_full[2], bar_qd_empty[2];
+  __shared__ uint64_t bar_st_full[2], bar_st_free[2], bar_ps_ready[2], bar_p_free[2], bar_ds_free[2], bar_ds_ready[2];
+  __shared__ uint64_t bar_qd_full[2], bar_qd_empty[2], bar_issued[3];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
   volatile int* abort_v = &abort_flag;
+  // Before the CTA frees TMEM, each issuer waits (bounded) until its own
+  // products have completed, on the normal and on the abort path alike.
+  auto settle_issuer = [&](int i) {
+    mma_commit(&bar_issued[i]);
+    volatile int quiet = 0;
+    mbar_wait(&bar_issued[i], 0, &quiet, dev_err);
+  };
 
-  // warps 0-7: score gradients (warp w: TMEM lanes 32*(w%4).., 32 query columns 32*(w/4).. of a sub-tile)
-  // warps 8-11: dQ drain; warp 12: TMA producer (+ TMEM owner); warp 13: MMA issuer
+  // warps 0-15: score gradients; warp w takes the sub-tiles u with u % 2 == w / 8 (TMEM buffer w / 8),
+  //   TMEM lanes 32 (w % 4).. and query columns 32 ((w / 4) % 2).. of each
+  // warps 16-19: dQ drain; warp 20: TMA producer (+ TMEM owner); warps 21-23: MMA issuers
+  // (21: S^T and dP^T, 22: dV and dK, 23: dQ)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nq = T / kTile;
   // heads along x, key tiles along y: key tile 0 (the most query tiles) first
@@ -378,6 +394,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(&bar_fin, 1);
     mbar_init(&bar_stage_full, 4);
     mbar_init(&bar_stage_free, 1);
+    for (int i = 0; i < 3; ++i) mbar_init(&bar_issued[i], 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bar_dq_full[b], 1);
       mbar_init(&bar_dq_free[b], 4);
@@ -386,13 +403,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(&bar_ps_ready[b], 8);
       mbar_init(&bar_p_free[b], 1);
       mbar_init(&bar_ds_free[b], 1);
+      mbar_init(&bar_ds_ready[b], 16);  // 8 gradient warps x 2 sub-tiles of a query tile
       mbar_init(&bar_qd_full[b], 1);
       mbar_init(&bar_qd_empty[b], 1);
     }
     fence_mbar_init();
     abort_flag = 0;
   }
-  if (warp == 12) {
+  if (warp == kBwdProducer) {
     tmem_alloc(&tmem_base, 512);
     tmem_relinquish();
   }
@@ -402,7 +420,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   const uint32_t tS = tmem_base, tdP = tmem_base + 128, tdV = tmem_base + 256, tdK = tmem_base + 320,
                  tdQ = tmem_base + 384;  // two 64-column buffers
 
-  if (warp == 12) {
+  if (warp == kBwdProducer) {
     // ----- producer
     if (lane == 0) {
       prefetch_tmap(&tq);
@@ -432,45 +450,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           }
       }
     }
-  } else if (warp == 13) {
-    // ----- MMA issuer
+  } else if (warp == kBwdProducer + 1) {
+    // ----- S^T = K Q^T and dP^T = V dO^T of sub-tile u into buffer u & 1
     if (lane == 0) {
       const uint32_t idS = idesc_bf16_f32(128, 64, 0, 0);
-      const uint32_t idKM = idesc_bf16_f32(128, 64, 0, 1);  // A K-major smem, B MN-major
-      const uint32_t idMM = idesc_bf16_f32(128, 64, 1, 1);  // A MN-major smem, B MN-major
       const uint32_t k0 = smem_u32(sK), v0 = smem_u32(sV), q0 = smem_u32(sQ), do0 = smem_u32(sdO);
-      const uint32_t pt0 = smem_u32(sPT), dsb = smem_u32(sdST);
       bool ok = mbar_wait(&bar_kv, 0, abort_v, dev_err);
-      // dV, dK of sub-tile w; after the second half, dQ of its query tile.
-      auto consume = [&](int w) -> bool {
-        const int b = w & 1, ii = w >> 1, s = ii & 1;
-        if (!mbar_wait(&bar_ps_ready[b], (w >> 1) & 1, abort_v, dev_err)) return false;
-        tc_fence_after();
-        const uint32_t qb = q0 + s * kTileBytes + b * (kTileBytes / 2);
-        const uint32_t db = do0 + s * kTileBytes + b * (kTileBytes / 2);
-        const uint32_t ds0 = dsb + s * 2 * kTileBytes;  // dS^T buffer of query tile ii
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          mma_ss(tdV, desc_sw128(pt0 + b * kTileBytes + k * 32, 16, 1024), desc_sw128(db + k * 2048, 8192, 1024),
-                 idKM, (w > 0 || k > 0));
-        mma_commit(&bar_p_free[b]);
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          mma_ss(tdK, desc_sw128(ds0 + b * kTileBytes + k * 32, 16, 1024), desc_sw128(qb + k * 2048, 8192, 1024),
-                 idKM, (w > 0 || k > 0));
-        if (b == 0) return true;
-        mma_commit(&bar_qd_empty[s]);
-        const int qb2 = ii & 1;
-        if (ii >= 2 && !mbar_wait(&bar_dq_free[qb2], ((ii >> 1) - 1) & 1, abort_v, dev_err)) return false;
-        tc_fence_after();
-#pragma unroll
-        for (int k = 0; k < 8; ++k)
-          mma_ss(tdQ + 64 * qb2, desc_sw128(ds0 + k * 2048, kTileBytes, 1024), desc_sw128(k0 + k * 2048, 8192, 1024),
-                 idMM, k > 0);
-        mma_commit(&bar_dq_full[qb2]);
-        mma_commit(&bar_ds_free[s]);
-        return true;
-      };
       for (int u = 0; ok && u < nu; ++u) {
         const int b = u & 1, ii = u >> 1, s = ii & 1;
         if (b == 0 && !mbar_wait(&bar_qd_full[s], (ii >> 1) & 1, abort_v, dev_err)) break;
@@ -485,49 +470,107 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         for (int k = 0; k < 4; ++k)
           mma_ss(tdP + 64 * b, desc_sw128(v0 + k * 32, 16, 1024), desc_sw128(db + k * 32, 16, 1024), idS, k > 0);
         mma_commit(&bar_st_full[b]);
-        if (u >= 1 && !consume(u - 1)) {
+      }
+      settle_issuer(0);
+    }
+  } else if (warp == kBwdProducer + 2) {
+    // ----- dV += P^T dO and dK += dS^T Q of sub-tile w. Every MMA reading
+    // Q/dO stage s (S^T, dP^T of this tile) completed before the score
+    // gradients of its second sub-tile were ready, so the commit after dK
+    // of that sub-tile releases the stage.
+    if (lane == 0) {
+      const uint32_t idKM = idesc_bf16_f32(128, 64, 0, 1);  // A K-major smem, B MN-major
+      const uint32_t q0 = smem_u32(sQ), do0 = smem_u32(sdO), pt0 = smem_u32(sPT), dsb = smem_u32(sdST);
+      bool ok = true;
+      for (int w = 0; w < nu; ++w) {
+        const int b = w & 1, ii = w >> 1, s = ii & 1;
+        if (!mbar_wait(&bar_ps_ready[b], (w >> 1) & 1, abort_v, dev_err)) {
           ok = false;
           break;
         }
+        tc_fence_after();
+        const uint32_t qb = q0 + s * kTileBytes + b * (kTileBytes / 2);
+        const uint32_t db = do0 + s * kTileBytes + b * (kTileBytes / 2);
+        const uint32_t ds0 = dsb + s * 2 * kTileBytes;
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          mma_ss(tdV, desc_sw128(pt0 + b * kTileBytes + k * 32, 16, 1024), desc_sw128(db + k * 2048, 8192, 1024),
+                 idKM, (w > 0 || k > 0));
+        mma_commit(&bar_p_free[b]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          mma_ss(tdK, desc_sw128(ds0 + b * kTileBytes + k * 32, 16, 1024), desc_sw128(qb + k * 2048, 8192, 1024),
+                 idKM, (w > 0 || k > 0));
+        if (b == 1) mma_commit(&bar_qd_empty[s]);
       }
-      if (ok && !*abort_v && consume(nu - 1)) mma_commit(&bar_fin);
+      if (ok && !*abort_v) mma_commit(&bar_fin);
+      settle_issuer(1);
     }
-  } else if (warp < 8) {
-    // ----- score-gradient warps
-    const int q4 = warp & 3, hc = warp >> 2;
+  } else if (warp == kBwdProducer + 3) {
+    // ----- dQ_tile = dS K of query tile ii into TMEM buffer ii & 1
+    if (lane == 0) {
+      const uint32_t idMM = idesc_bf16_f32(128, 64, 1, 1);  // A MN-major smem, B MN-major
+      const uint32_t k0 = smem_u32(sK), dsb = smem_u32(sdST);
+      bool ok = mbar_wait(&bar_kv, 0, abort_v, dev_err);
+      for (int ii = 0; ok && ii < ni; ++ii) {
+        const int s = ii & 1, qb2 = ii & 1;
+        if (!mbar_wait(&bar_ds_ready[s], (ii >> 1) & 1, abort_v, dev_err)) break;
+        if (ii >= 2 && !mbar_wait(&bar_dq_free[qb2], ((ii >> 1) - 1) & 1, abort_v, dev_err)) break;
+        tc_fence_after();
+        const uint32_t ds0 = dsb + s * 2 * kTileBytes;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          mma_ss(tdQ + 64 * qb2, desc_sw128(ds0 + k * 2048, kTileBytes, 1024), desc_sw128(k0 + k * 2048, 8192, 1024),
+                 idMM, k > 0);
+        mma_commit(&bar_dq_full[qb2]);
+        mma_commit(&bar_ds_free[s]);
+      }
+      settle_issuer(2);
+    }
+  } else if (warp < kBwdGradWarps) {
+    // ----- score-gradient warps: group g = warp / 8 takes sub-tiles g, g + 2, ...
+    const int g = warp >> 3, q4 = warp & 3, hc = (warp >> 2) & 1;
     const int r = q4 * 32 + lane;  // key row within the tile (TMEM lane)
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
+    const int b = g;  // TMEM S^T / dP^T buffer and P^T half of this group
     bool ok = true;
-    for (int u = 0; u < nu; ++u) {
-      const int b = u & 1, ii = u >> 1, s = ii & 1;
+    for (int u = g; u < nu; u += 2) {
+      const int ii = u >> 1, s = ii & 1;
       if (!mbar_wait_warp(&bar_st_full[b], (u >> 1) & 1, abort_v, dev_err)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      uint32_t sv[32], pv[32];
-      tmem_ld32x2(tS + 64 * b + 32 * hc + lane_off, sv, tdP + 64 * b + 32 * hc + lane_off, pv);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar_st_free[b]);
-      const int col0 = 64 * b + 32 * hc;  // query column within the 128-query tile
-      const float* st = sStat + s * kTile + col0;
-      const float* dd = sDi + s * kTile + col0;
-      uint32_t pk[16], dk2[16];
-      if (ii == 0)
-        grads_chunk<N, CLIP, INV_STAT, true>(sv, pv, st, dd, pk, dk2, cfg.clamp, col0, r);
-      else
-        grads_chunk<N, CLIP, INV_STAT, false>(sv, pv, st, dd, pk, dk2, cfg.clamp, col0, r);
+      uint32_t pk[2][8], dk2[2][8];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        uint32_t sv[16], pv[16];
+        const uint32_t col = 64 * b + 32 * hc + 16 * j;  // TMEM column of the chunk within S^T / dP^T
+        tmem_ld16x2(tS + col + lane_off, sv, tdP + col + lane_off, pv);
+        if (j == 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bar_st_free[b]);
+        }
+        const int col0 = 64 * b + 32 * hc + 16 * j;  // query column within the 128-query tile
+        const float* st = sStat + s * kTile + col0;
+        const float* dd = sDi + s * kTile + col0;
+        if (ii == 0)
+          grads_chunk<N, CLIP, INV_STAT, true, 16>(sv, pv, st, dd, pk[j], dk2[j], cfg.clamp, col0, r);
+        else
+          grads_chunk<N, CLIP, INV_STAT, false, 16>(sv, pv, st, dd, pk[j], dk2[j], cfg.clamp, col0, r);
+      }
       // P^T of sub-tile u - 2 must have been consumed by its dV product,
       // dS^T of query tile ii - 2 by its dQ product.
       if (u >= 2 && !mbar_wait_warp(&bar_p_free[b], ((u >> 1) - 1) & 1, abort_v, dev_err)) {
         ok = false;
         break;
       }
+      const int c16 = 8 * b + 4 * hc;  // first 16-byte unit of this warp's 32 columns
 #pragma unroll
       for (int un = 0; un < 4; ++un) {
-        const uint32_t off = sw128_off(r, col0 / 8 + un);
-        *reinterpret_cast<uint4*>(sPT + off) = make_uint4(pk[4 * un], pk[4 * un + 1], pk[4 * un + 2], pk[4 * un + 3]);
+        const uint32_t* v = pk[un >> 1] + 4 * (un & 1);
+        *reinterpret_cast<uint4*>(sPT + sw128_off(r, c16 + un)) = make_uint4(v[0], v[1], v[2], v[3]);
       }
       if (ii >= 2 && !mbar_wait_warp(&bar_ds_free[s], ((ii >> 1) - 1) & 1, abort_v, dev_err)) {
         ok = false;
@@ -536,63 +579,62 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       uint8_t* ds_tile = sdST + s * 2 * kTileBytes;
 #pragma unroll
       for (int un = 0; un < 4; ++un) {
-        const uint32_t off = sw128_off(r, col0 / 8 + un);
-        *reinterpret_cast<uint4*>(ds_tile + off) =
-            make_uint4(dk2[4 * un], dk2[4 * un + 1], dk2[4 * un + 2], dk2[4 * un + 3]);
+        const uint32_t* v = dk2[un >> 1] + 4 * (un & 1);
+        *reinterpret_cast<uint4*>(ds_tile + sw128_off(r, c16 + un)) = make_uint4(v[0], v[1], v[2], v[3]);
       }
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar_ps_ready[b]);
+      if (lane == 0) {
+        mbar_arrive(&bar_ps_ready[b]);
+        mbar_arrive(&bar_ds_ready[s]);
+      }
     }
+    // dK (group 0) and dV (group 1): 32 columns per thread
     if (ok && mbar_wait_warp(&bar_fin, 0, abort_v, dev_err)) {
       tc_fence_after();
       const size_t row = (size_t)row_base + (size_t)kt * kTile + r;
-      const float slope = (float)N;
-      uint32_t vk[32], vv[32];
-      tmem_ld32x2(tdK + lane_off + hc * 32, vk, tdV + lane_off + hc * 32, vv);
+      uint32_t v[32];
+      tmem_ld32((g == 0 ? tdK : tdV) + lane_off + hc * 32, v);
+      __nv_bfloat16* dst = g == 0 ? dk : dv;
+      const float f = g == 0 ? (float)N : 1.f;
+      uint4* d4 = reinterpret_cast<uint4*>(dst + row * 64 + hc * 32);
 #pragma unroll
-      for (int which = 0; which < 2; ++which) {
-        __nv_bfloat16* dst = which == 0 ? dk : dv;
-        const uint32_t* v = which == 0 ? vk : vv;
-        const float f = which == 0 ? slope : 1.f;
-        uint4* d4 = reinterpret_cast<uint4*>(dst + row * 64 + hc * 32);
-#pragma unroll
-        for (int un = 0; un < 4; ++un) {
-          uint4 w;
-          w.x = pack_bf16x2(__uint_as_float(v[8 * un + 0]) * f, __uint_as_float(v[8 * un + 1]) * f);
-          w.y = pack_bf16x2(__uint_as_float(v[8 * un + 2]) * f, __uint_as_float(v[8 * un + 3]) * f);
-          w.z = pack_bf16x2(__uint_as_float(v[8 * un + 4]) * f, __uint_as_float(v[8 * un + 5]) * f);
-          w.w = pack_bf16x2(__uint_as_float(v[8 * un + 6]) * f, __uint_as_float(v[8 * un + 7]) * f);
-          d4[un] = w;
-        }
+      for (int un = 0; un < 4; ++un) {
+        uint4 w;
+        w.x = pack_bf16x2(__uint_as_float(v[8 * un + 0]) * f, __uint_as_float(v[8 * un + 1]) * f);
+        w.y = pack_bf16x2(__uint_as_float(v[8 * un + 2]) * f, __uint_as_float(v[8 * un + 3]) * f);
+        w.z = pack_bf16x2(__uint_as_float(v[8 * un + 4]) * f, __uint_as_float(v[8 * un + 5]) * f);
+        w.w = pack_bf16x2(__uint_as_float(v[8 * un + 6]) * f, __uint_as_float(v[8 * un + 7]) * f);
+        d4[un] = w;
       }
     }
-  } else {
-    // ----- dQ drain warps 8-11: thread owns query row qi*128 + r (TMEM lane r)
-    const int r = (warp - 8) * 32 + lane;
-    const uint32_t lane_off = (uint32_t)((warp - 8) * 32) << 16;
-    const bool issuer = warp == 8 && lane == 0;
+  } else if (warp < kBwdDrain + 4) {
+    // ----- dQ drain warps: thread owns query row qi*128 + r (TMEM lane r).
+    // Two rounds (columns 0-31, then 32-63) through one 16 KB staging box;
+    // row r, 16-byte chunk c of a 128-byte box row sits at chunk c ^ (r & 7).
+    const int r = (warp - kBwdDrain) * 32 + lane;
+    const uint32_t lane_off = (uint32_t)((warp - kBwdDrain) * 32) << 16;
+    const bool issuer = warp == kBwdDrain && lane == 0;
     bool ok = true;
-    for (int ii = 0; ii < ni; ++ii) {
+    for (int ii = 0; ok && ii < ni; ++ii) {
       const int qb2 = ii & 1;
       if (!mbar_wait_warp(&bar_dq_full[qb2], (ii >> 1) & 1, abort_v, dev_err)) break;
-      tc_fence_after();
-      uint32_t a[32], b[32];
-      tmem_ld32x2(tdQ + 64 * qb2 + lane_off, a, tdQ + 64 * qb2 + lane_off + 32, b);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar_dq_free[qb2]);
-      // Two rounds (columns 0-31, then 32-63) through one 16 KB staging box;
-      // row r, 16-byte chunk c of a 128-byte box row sits at chunk c ^ (r & 7).
       const int y = row_base + (kt + ii) * kTile;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int round = 2 * ii + h;
+        tc_fence_after();
+        uint32_t v[32];
+        tmem_ld32(tdQ + 64 * qb2 + 32 * h + lane_off, v);
+        if (h == 1) {  // both halves are in registers: the TMEM buffer is free
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bar_dq_free[qb2]);
+        }
         if (round > 0 && !mbar_wait_warp(&bar_stage_free, (round - 1) & 1, abort_v, dev_err)) {
           ok = false;
           break;
         }
-        const uint32_t* v = h == 0 ? a : b;
 #pragma unroll
         for (int c = 0; c < 8; ++c)
           *reinterpret_cast<uint4*>(sDQ + r * 128 + ((c ^ (r & 7)) << 4)) =
@@ -616,13 +658,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           break;
         }
       }
-      if (!ok) break;
     }
     if (issuer) bulk_wait_group0();
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 12) tmem_dealloc(tmem_base, 512);
+  if (warp == kBwdProducer) tmem_dealloc(tmem_base, 512);
 }
 
 // dq = bf16(acc * n * scale), only when the fast path ran (unshifted branch).
