@@ -83,19 +83,17 @@ __global__ void __launch_bounds__(kPrepThreads) attn_prepare_kernel(const T* __r
 
 // ------------------------------------------------------------------ forward
 template <typename T>
-__global__ void __launch_bounds__(kRows) attn_fwd_generic(algx_attn_config cfg, const T* __restrict__ q,
+__device__ __forceinline__ void attn_fwd_generic_tile(algx_attn_config cfg, const T* __restrict__ q,
                                                           const T* __restrict__ k, const T* __restrict__ v,
                                                           const float* __restrict__ sink,
                                                           const float* __restrict__ guard, T* __restrict__ o,
                                                           float* __restrict__ o_prec, float* __restrict__ stat,
-                                                          int H, int T_, int branch_mask) {
-  const Eff e = resolve_variant(cfg, guard);
-  if (!((branch_mask >> e.branch) & 1)) return;
+                                                          int H, int T_, int blk_tile, int bh_tile, const Eff e) {
   __shared__ float ks[kKT][kD];
   __shared__ float vs[kKT][kD];
-  const int bh = blockIdx.y;
+  const int bh = bh_tile;
   const int h = bh % H;
-  const int row0 = blockIdx.x * kRows;
+  const int row0 = blk_tile * kRows;
   const int row = row0 + threadIdx.x;
   const bool active = row < T_;
   const size_t base = (size_t)bh * T_ * kD;
@@ -202,6 +200,24 @@ __global__ void __launch_bounds__(kRows) attn_fwd_generic(algx_attn_config cfg, 
   else
     st = m + logf(l);
   stat[(size_t)bh * T_ + row] = st;
+}
+
+// Grid-stride over (row block, head) tiles; returns at once unless the
+// resolved branch is one of branch_mask (the launch is then nearly free).
+template <typename T>
+__global__ void __launch_bounds__(kRows) attn_fwd_generic(algx_attn_config cfg, const T* __restrict__ q,
+                                                          const T* __restrict__ k, const T* __restrict__ v,
+                                                          const float* __restrict__ sink,
+                                                          const float* __restrict__ guard, T* __restrict__ o,
+                                                          float* __restrict__ o_prec, float* __restrict__ stat,
+                                                          int H, int T_, int branch_mask, int BH) {
+  const Eff e = resolve_variant(cfg, guard);
+  if (!((branch_mask >> e.branch) & 1)) return;
+  const int nblk = (T_ + kRows - 1) / kRows;
+  for (int w = blockIdx.x; w < nblk * BH; w += gridDim.x) {
+    attn_fwd_generic_tile<T>(cfg, q, k, v, sink, guard, o, o_prec, stat, H, T_, w % nblk, w / nblk, e);
+    __syncthreads();
+  }
 }
 
 // ------------------------------------------------------------------ backward
@@ -322,15 +338,13 @@ __device__ __forceinline__ PDs tile_grad(const Eff& e, const algx_attn_config& c
 
 // dK, dV: one key row per thread; query tiles streamed through shared memory.
 template <typename T>
-__global__ void __launch_bounds__(kRows) attn_dkdv_generic(algx_attn_config cfg, const T* __restrict__ q,
+__device__ __forceinline__ void attn_dkdv_generic_tile(algx_attn_config cfg, const T* __restrict__ q,
                                                            const T* __restrict__ k, const T* __restrict__ v,
                                                            const T* __restrict__ dout,
                                                            const float* __restrict__ stat,
                                                            const float* __restrict__ di,
                                                            const float* __restrict__ guard, T* __restrict__ dk,
-                                                           T* __restrict__ dv, int T_, int branch_mask) {
-  const Eff e = resolve_variant(cfg, guard);
-  if (!((branch_mask >> e.branch) & 1)) return;
+                                                           T* __restrict__ dv, int T_, int blk_tile, int bh_tile, const Eff e) {
   extern __shared__ float smem[];
   float(*kown)[kD + 1] = reinterpret_cast<float(*)[kD + 1]>(smem);
   float(*vown)[kD + 1] = reinterpret_cast<float(*)[kD + 1]>(smem + kRows * (kD + 1));
@@ -338,8 +352,8 @@ __global__ void __launch_bounds__(kRows) attn_dkdv_generic(algx_attn_config cfg,
   float(*dot)[kD] = reinterpret_cast<float(*)[kD]>(smem + 2 * kRows * (kD + 1) + kKT * kD);
   float* st = smem + 2 * kRows * (kD + 1) + 2 * kKT * kD;
   float* dit = st + kKT;
-  const int bh = blockIdx.y;
-  const int key0 = blockIdx.x * kRows;
+  const int bh = bh_tile;
+  const int key0 = blk_tile * kRows;
   const int key = key0 + threadIdx.x;
   const bool active = key < T_;
   const size_t base = (size_t)bh * T_ * kD;
@@ -395,23 +409,40 @@ __global__ void __launch_bounds__(kRows) attn_dkdv_generic(algx_attn_config cfg,
   }
 }
 
+// Grid-stride over (row block, head) tiles; returns at once unless the
+// resolved branch is one of branch_mask (the launch is then nearly free).
+template <typename T>
+__global__ void __launch_bounds__(kRows) attn_dkdv_generic(algx_attn_config cfg, const T* __restrict__ q,
+                                                           const T* __restrict__ k, const T* __restrict__ v,
+                                                           const T* __restrict__ dout,
+                                                           const float* __restrict__ stat,
+                                                           const float* __restrict__ di,
+                                                           const float* __restrict__ guard, T* __restrict__ dk,
+                                                           T* __restrict__ dv, int T_, int branch_mask, int BH) {
+  const Eff e = resolve_variant(cfg, guard);
+  if (!((branch_mask >> e.branch) & 1)) return;
+  const int nblk = (T_ + kRows - 1) / kRows;
+  for (int w = blockIdx.x; w < nblk * BH; w += gridDim.x) {
+    attn_dkdv_generic_tile<T>(cfg, q, k, v, dout, stat, di, guard, dk, dv, T_, w % nblk, w / nblk, e);
+    __syncthreads();
+  }
+}
+
 // dQ: one query row per thread; key tiles streamed through shared memory.
 template <typename T>
-__global__ void __launch_bounds__(kRows) attn_dq_generic(algx_attn_config cfg, const T* __restrict__ q,
+__device__ __forceinline__ void attn_dq_generic_tile(algx_attn_config cfg, const T* __restrict__ q,
                                                          const T* __restrict__ k, const T* __restrict__ v,
                                                          const T* __restrict__ dout, const float* __restrict__ stat,
                                                          const float* __restrict__ di,
                                                          const float* __restrict__ guard, T* __restrict__ dq,
-                                                         int T_, int branch_mask) {
-  const Eff e = resolve_variant(cfg, guard);
-  if (!((branch_mask >> e.branch) & 1)) return;
+                                                         int T_, int blk_tile, int bh_tile, const Eff e) {
   extern __shared__ float smem[];
   float(*qown)[kD + 1] = reinterpret_cast<float(*)[kD + 1]>(smem);
   float(*down)[kD + 1] = reinterpret_cast<float(*)[kD + 1]>(smem + kRows * (kD + 1));
   float(*kt)[kD] = reinterpret_cast<float(*)[kD]>(smem + 2 * kRows * (kD + 1));
   float(*vt)[kD] = reinterpret_cast<float(*)[kD]>(smem + 2 * kRows * (kD + 1) + kKT * kD);
-  const int bh = blockIdx.y;
-  const int row0 = blockIdx.x * kRows;
+  const int bh = bh_tile;
+  const int row0 = blk_tile * kRows;
   const int row = row0 + threadIdx.x;
   const bool active = row < T_;
   const size_t base = (size_t)bh * T_ * kD;
@@ -458,6 +489,24 @@ __global__ void __launch_bounds__(kRows) attn_dq_generic(algx_attn_config cfg, c
   for (int d = 0; d < kD; ++d) dq[ob + d] = from_f32<T>(dqa[d] * f);
 }
 
+// Grid-stride over (row block, head) tiles; returns at once unless the
+// resolved branch is one of branch_mask (the launch is then nearly free).
+template <typename T>
+__global__ void __launch_bounds__(kRows) attn_dq_generic(algx_attn_config cfg, const T* __restrict__ q,
+                                                         const T* __restrict__ k, const T* __restrict__ v,
+                                                         const T* __restrict__ dout, const float* __restrict__ stat,
+                                                         const float* __restrict__ di,
+                                                         const float* __restrict__ guard, T* __restrict__ dq,
+                                                         int T_, int branch_mask, int BH) {
+  const Eff e = resolve_variant(cfg, guard);
+  if (!((branch_mask >> e.branch) & 1)) return;
+  const int nblk = (T_ + kRows - 1) / kRows;
+  for (int w = blockIdx.x; w < nblk * BH; w += gridDim.x) {
+    attn_dq_generic_tile<T>(cfg, q, k, v, dout, stat, di, guard, dq, T_, w % nblk, w / nblk, e);
+    __syncthreads();
+  }
+}
+
 constexpr size_t kGenericBwdSmem = (2 * kRows * (kD + 1) + 2 * kKT * kD + 2 * kKT) * sizeof(float);
 
 int check_attn(const algx_attn_config* cfg, int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype) {
@@ -476,6 +525,14 @@ int check_attn(const algx_attn_config* cfg, int64_t B, int64_t H, int64_t T, int
 }
 
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// Grid of the generic kernels: every (row block, head) tile when they do the
+// work; when the fast kernels ran they only stand by for the shifted
+// fallback, and a grid of four CTAs per SM returns almost at once.
+unsigned generic_grid(int64_t BH, int64_t T, bool fast) {
+  const int64_t tiles = BH * ((T + kRows - 1) / kRows);
+  return (unsigned)(fast ? std::min<int64_t>(tiles, 148 * 4) : tiles);
+}
 
 }  // namespace
 
@@ -529,16 +586,22 @@ int algx_attn_fwd(const algx_attn_config* cfg, const void* q_scaled, const void*
   int mask = 7;
   bool fast = false;
   if (int s = tc_attn_fwd(*cfg, q_scaled, k, v, sink, guard, o, stat, B, H, T, dtype, st, &fast)) return s;
-  if (fast) mask = 1 << BR_SHIFTED | 1 << BR_SOFTMAX;  // the fast kernel covers the unshifted branch
-  dim3 grid((unsigned)((T + kRows - 1) / kRows), (unsigned)(B * H));
+  if (fast) {
+    // The fast kernel covers the unshifted branch, which the clipped link
+    // always takes; only a guarded call may still need the shifted fallback.
+    if (cfg->mode == ALGX_MODE_CLIPPED) return ALGX_OK;
+    mask = 1 << BR_SHIFTED | 1 << BR_SOFTMAX;
+  }
+  const unsigned grid = generic_grid(B * H, T, fast);
   if (dtype == ALGX_BF16)
     attn_fwd_generic<__nv_bfloat16><<<grid, kRows, 0, st>>>(*cfg, (const __nv_bfloat16*)q_scaled,
                                                              (const __nv_bfloat16*)k, (const __nv_bfloat16*)v,
                                                              sink, guard, (__nv_bfloat16*)o, o_precise, stat,
-                                                             (int)H, (int)T, mask);
+                                                             (int)H, (int)T, mask, (int)(B * H));
   else
     attn_fwd_generic<float><<<grid, kRows, 0, st>>>(*cfg, (const float*)q_scaled, (const float*)k, (const float*)v,
-                                                    sink, guard, (float*)o, o_precise, stat, (int)H, (int)T, mask);
+                                                    sink, guard, (float*)o, o_precise, stat, (int)H, (int)T, mask,
+                                                    (int)(B * H));
   ALGX_LAUNCHED("attn_fwd_generic launch");
   return ALGX_OK;
 }
@@ -581,7 +644,11 @@ int algx_attn_bwd(const algx_attn_config* cfg, const void* q_scaled, const void*
   if (int s = tc_attn_bwd(*cfg, q_scaled, k, v, dout, stat, di, guard, dq, dk, dv, tc_ws, B, H, T, dtype, st,
                           &fast))
     return s;
-  if (fast) mask = 1 << BR_SHIFTED | 1 << BR_SOFTMAX;
+  if (fast) {
+    if (cfg->mode == ALGX_MODE_CLIPPED) return ALGX_OK;  // see algx_attn_fwd
+    mask = 1 << BR_SHIFTED | 1 << BR_SOFTMAX;
+  }
+  const unsigned ggrid = generic_grid(B * H, T, fast);
   int dev = 0;
   ALGX_CUDA(cudaGetDevice(&dev));
   static bool attr_set[64][2] = {};
@@ -599,20 +666,21 @@ int algx_attn_bwd(const algx_attn_config* cfg, const void* q_scaled, const void*
     }
     attr_set[dev][dtype] = true;
   }
+  const int bh = (int)(B * H);
   if (dtype == ALGX_BF16) {
-    attn_dkdv_generic<__nv_bfloat16><<<grid, kRows, kGenericBwdSmem, st>>>(
+    attn_dkdv_generic<__nv_bfloat16><<<ggrid, kRows, kGenericBwdSmem, st>>>(
         *cfg, (const __nv_bfloat16*)q_scaled, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v,
-        (const __nv_bfloat16*)dout, stat, di, guard, (__nv_bfloat16*)dk, (__nv_bfloat16*)dv, (int)T, mask);
-    attn_dq_generic<__nv_bfloat16><<<grid, kRows, kGenericBwdSmem, st>>>(
+        (const __nv_bfloat16*)dout, stat, di, guard, (__nv_bfloat16*)dk, (__nv_bfloat16*)dv, (int)T, mask, bh);
+    attn_dq_generic<__nv_bfloat16><<<ggrid, kRows, kGenericBwdSmem, st>>>(
         *cfg, (const __nv_bfloat16*)q_scaled, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v,
-        (const __nv_bfloat16*)dout, stat, di, guard, (__nv_bfloat16*)dq, (int)T, mask);
+        (const __nv_bfloat16*)dout, stat, di, guard, (__nv_bfloat16*)dq, (int)T, mask, bh);
   } else {
-    attn_dkdv_generic<float><<<grid, kRows, kGenericBwdSmem, st>>>(*cfg, (const float*)q_scaled, (const float*)k,
-                                                                   (const float*)v, (const float*)dout, stat, di,
-                                                                   guard, (float*)dk, (float*)dv, (int)T, mask);
-    attn_dq_generic<float><<<grid, kRows, kGenericBwdSmem, st>>>(*cfg, (const float*)q_scaled, (const float*)k,
-                                                                 (const float*)v, (const float*)dout, stat, di,
-                                                                 guard, (float*)dq, (int)T, mask);
+    attn_dkdv_generic<float><<<ggrid, kRows, kGenericBwdSmem, st>>>(*cfg, (const float*)q_scaled, (const float*)k,
+                                                                    (const float*)v, (const float*)dout, stat, di,
+                                                                    guard, (float*)dk, (float*)dv, (int)T, mask, bh);
+    attn_dq_generic<float><<<ggrid, kRows, kGenericBwdSmem, st>>>(*cfg, (const float*)q_scaled, (const float*)k,
+                                                                  (const float*)v, (const float*)dout, stat, di,
+                                                                  guard, (float*)dq, (int)T, mask, bh);
   }
   count_launches(1);  // two kernels above, one counted by the macro
   ALGX_LAUNCHED("attn_bwd_generic launch");

@@ -12,7 +12,9 @@
 // rescaling; O = acc / l and stat = 1/l (or l^(-1/n)) at the end.
 //
 // Backward (kernels/flash.py:333-361, 435-627): one CTA per (128-key tile,
-// head). K, V stay resident; query tiles stream through a 2-stage TMA ring.
+// head). K, V stay resident; Q, dO, stat and di stream through a 4-stage TMA
+// ring of 64-query halves, each released as soon as its sub-tile's products
+// have read it.
 // Per query tile: S^T = K Q^T and dP^T = V dO^T in TMEM; the score-gradient
 // warps (thread = key row) recompute p = rho^n * stat, ds = p (dp - di) r,
 // write bf16 P^T and dS^T to shared memory (128-byte swizzled K-major); then
@@ -46,6 +48,8 @@ constexpr int kFwdStages = 2;
 constexpr int kFwdThreads = 192;
 constexpr int kFwdSmem = kTileBytes * (1 + 2 * kFwdStages) + 1024;
 constexpr int kBwdThreads = 768;
+constexpr int kHalfBytes = kTileBytes / 2;  // 64 rows x 64 bf16
+constexpr int kBwdStages = 4;               // Q / dO ring of 64-query halves
 constexpr int kBwdGradWarps = 16, kBwdDrain = 16, kBwdProducer = 20;
 constexpr int kBwdSmem = kTileBytes * 13 + 4 * kTile * 4 + 1024;
 
@@ -355,16 +359,16 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sK = smem;
   uint8_t* sV = smem + kTileBytes;
-  uint8_t* sQ = smem + 2 * kTileBytes;    // 2 stages
-  uint8_t* sdO = smem + 4 * kTileBytes;   // 2 stages
+  uint8_t* sQ = smem + 2 * kTileBytes;    // kBwdStages x 64 queries
+  uint8_t* sdO = smem + 4 * kTileBytes;   // kBwdStages x 64 queries
   uint8_t* sPT = smem + 6 * kTileBytes;   // 128 keys x 64 queries bf16, [2 sub-tiles]
   uint8_t* sdST = smem + 8 * kTileBytes;  // 128 keys x 128 queries bf16, [2 query tiles][2 halves]
   uint8_t* sDQ = smem + 12 * kTileBytes;  // fp32 dQ staging: one 128-row x 32-column swizzled box
-  float* sStat = reinterpret_cast<float*>(smem + 13 * kTileBytes);  // [2][128]
-  float* sDi = sStat + 2 * kTile;                                    // [2][128]
+  float* sStat = reinterpret_cast<float*>(smem + 13 * kTileBytes);  // [kBwdStages][64]
+  float* sDi = sStat + kBwdStages * 64;                              // [kBwdStages][64]
   __shared__ uint64_t bar_kv, bar_fin, bar_dq_full[2], bar_dq_free[2], bar_stage_full, bar_stage_free;
   __shared__ uint64_t bar_st_full[2], bar_st_free[2], bar_ps_ready[2], bar_p_free[2], bar_ds_free[2], bar_ds_ready[2];
-  __shared__ uint64_t bar_qd_full[2], bar_qd_empty[2], bar_issued[3];
+  __shared__ uint64_t bar_qd_full[kBwdStages], bar_qd_empty[kBwdStages], bar_issued[3];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
   volatile int* abort_v = &abort_flag;
@@ -406,6 +410,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(&bar_ds_ready[b], 16);  // 8 gradient warps x 2 sub-tiles of a query tile
       mbar_init(&bar_qd_full[b], 1);
       mbar_init(&bar_qd_empty[b], 1);
+      mbar_init(&bar_qd_full[b + 2], 1);
+      mbar_init(&bar_qd_empty[b + 2], 1);
     }
     fence_mbar_init();
     abort_flag = 0;
@@ -431,22 +437,23 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_expect_tx(&bar_kv, 2 * kTileBytes);
       tma_load_2d(sK, &tk, &bar_kv, 0, row_base + kt * kTile);
       tma_load_2d(sV, &tv, &bar_kv, 0, row_base + kt * kTile);
-      int issued[2] = {-1, -1};
-      for (int ii = 0; ii < ni; ++ii) {
-        const int s = ii & 1, qi = kt + ii;
-        if (ii >= 2 && !mbar_wait(&bar_qd_empty[s], ((ii >> 1) - 1) & 1, abort_v, dev_err)) break;
-        mbar_expect_tx(&bar_qd_full[s], 2 * kTileBytes + 2 * kTile * 4);
-        tma_load_2d(sQ + s * kTileBytes, &tq, &bar_qd_full[s], 0, row_base + qi * kTile);
-        tma_load_2d(sdO + s * kTileBytes, &tdo, &bar_qd_full[s], 0, row_base + qi * kTile);
-        bulk_load(sStat + s * kTile, stat + row_base + qi * kTile, kTile * 4, &bar_qd_full[s]);
-        bulk_load(sDi + s * kTile, di + row_base + qi * kTile, kTile * 4, &bar_qd_full[s]);
-        issued[s] = ii;
+      int issued[kBwdStages] = {-1, -1, -1, -1};
+      for (int u = 0; u < nu; ++u) {
+        const int hs = u & (kBwdStages - 1);
+        const int q_row = row_base + (kt + (u >> 1)) * kTile + 64 * (u & 1);
+        if (u >= kBwdStages && !mbar_wait(&bar_qd_empty[hs], ((u / kBwdStages) - 1) & 1, abort_v, dev_err)) break;
+        mbar_expect_tx(&bar_qd_full[hs], 2 * kHalfBytes + 2 * 64 * 4);
+        tma_load_2d(sQ + hs * kHalfBytes, &tq, &bar_qd_full[hs], 0, q_row);
+        tma_load_2d(sdO + hs * kHalfBytes, &tdo, &bar_qd_full[hs], 0, q_row);
+        bulk_load(sStat + hs * 64, stat + q_row, 64 * 4, &bar_qd_full[hs]);
+        bulk_load(sDi + hs * 64, di + q_row, 64 * 4, &bar_qd_full[hs]);
+        issued[hs] = u;
       }
       if (*abort_v) {
-        for (int s = 0; s < 2; ++s)
-          if (issued[s] >= 0) {
+        for (int i = 0; i < kBwdStages; ++i)
+          if (issued[i] >= 0) {
             volatile int quiet = 0;
-            mbar_wait(&bar_qd_full[s], (issued[s] >> 1) & 1, &quiet, nullptr);
+            mbar_wait(&bar_qd_full[i], (issued[i] / kBwdStages) & 1, &quiet, nullptr);
           }
       }
     }
@@ -457,12 +464,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const uint32_t k0 = smem_u32(sK), v0 = smem_u32(sV), q0 = smem_u32(sQ), do0 = smem_u32(sdO);
       bool ok = mbar_wait(&bar_kv, 0, abort_v, dev_err);
       for (int u = 0; ok && u < nu; ++u) {
-        const int b = u & 1, ii = u >> 1, s = ii & 1;
-        if (b == 0 && !mbar_wait(&bar_qd_full[s], (ii >> 1) & 1, abort_v, dev_err)) break;
+        const int b = u & 1, hs = u & (kBwdStages - 1);
+        if (!mbar_wait(&bar_qd_full[hs], (u / kBwdStages) & 1, abort_v, dev_err)) break;
         if (u >= 2 && !mbar_wait(&bar_st_free[b], ((u >> 1) - 1) & 1, abort_v, dev_err)) break;
         tc_fence_after();
-        const uint32_t qb = q0 + s * kTileBytes + b * (kTileBytes / 2);
-        const uint32_t db = do0 + s * kTileBytes + b * (kTileBytes / 2);
+        const uint32_t qb = q0 + hs * kHalfBytes;
+        const uint32_t db = do0 + hs * kHalfBytes;
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_ss(tS + 64 * b, desc_sw128(k0 + k * 32, 16, 1024), desc_sw128(qb + k * 32, 16, 1024), idS, k > 0);
@@ -474,23 +481,22 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       settle_issuer(0);
     }
   } else if (warp == kBwdProducer + 2) {
-    // ----- dV += P^T dO and dK += dS^T Q of sub-tile w. Every MMA reading
-    // Q/dO stage s (S^T, dP^T of this tile) completed before the score
-    // gradients of its second sub-tile were ready, so the commit after dK
-    // of that sub-tile releases the stage.
+    // ----- dV += P^T dO and dK += dS^T Q of sub-tile w. S^T and dP^T of the
+    // sub-tile, the other readers of its Q/dO half-stage, completed before its
+    // score gradients were ready, so the commit after dK releases the stage.
     if (lane == 0) {
       const uint32_t idKM = idesc_bf16_f32(128, 64, 0, 1);  // A K-major smem, B MN-major
       const uint32_t q0 = smem_u32(sQ), do0 = smem_u32(sdO), pt0 = smem_u32(sPT), dsb = smem_u32(sdST);
       bool ok = true;
       for (int w = 0; w < nu; ++w) {
-        const int b = w & 1, ii = w >> 1, s = ii & 1;
+        const int b = w & 1, ii = w >> 1, s = ii & 1, hs = w & (kBwdStages - 1);
         if (!mbar_wait(&bar_ps_ready[b], (w >> 1) & 1, abort_v, dev_err)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t qb = q0 + s * kTileBytes + b * (kTileBytes / 2);
-        const uint32_t db = do0 + s * kTileBytes + b * (kTileBytes / 2);
+        const uint32_t qb = q0 + hs * kHalfBytes;
+        const uint32_t db = do0 + hs * kHalfBytes;
         const uint32_t ds0 = dsb + s * 2 * kTileBytes;
 #pragma unroll
         for (int k = 0; k < 4; ++k)
@@ -501,7 +507,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         for (int k = 0; k < 4; ++k)
           mma_ss(tdK, desc_sw128(ds0 + b * kTileBytes + k * 32, 16, 1024), desc_sw128(qb + k * 2048, 8192, 1024),
                  idKM, (w > 0 || k > 0));
-        if (b == 1) mma_commit(&bar_qd_empty[s]);
+        mma_commit(&bar_qd_empty[hs]);
       }
       if (ok && !*abort_v) mma_commit(&bar_fin);
       settle_issuer(1);
@@ -553,8 +559,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           if (lane == 0) mbar_arrive(&bar_st_free[b]);
         }
         const int col0 = 64 * b + 32 * hc + 16 * j;  // query column within the 128-query tile
-        const float* st = sStat + s * kTile + col0;
-        const float* dd = sDi + s * kTile + col0;
+        const int hs = u & (kBwdStages - 1);
+        const float* st = sStat + hs * 64 + 32 * hc + 16 * j;
+        const float* dd = sDi + hs * 64 + 32 * hc + 16 * j;
         if (ii == 0)
           grads_chunk<N, CLIP, INV_STAT, true, 16>(sv, pv, st, dd, pk[j], dk2[j], cfg.clamp, col0, r);
         else
@@ -761,6 +768,9 @@ int tc_attn_bwd(const algx_attn_config& cfg, const void* q_scaled, const void* k
   CUtensorMap maps[4];
   const void* ptrs[4] = {q_scaled, k, v, dout};
   if (int s = make_maps(ptrs, 4, maps, B * H * T)) return s;
+  // Q and dO stream in 64-query halves
+  for (int i : {0, 3})
+    if (int s = make_tmap_2d(&maps[i], ptrs[i], ALGX_BF16, 64, (uint64_t)(B * H * T), 128, 64, 64, true)) return s;
   float* acc = static_cast<float*>(workspace);
   const size_t nacc = (size_t)B * H * T * 64;
   CUtensorMap tdq;  // fp32 accumulator, reduce-added in 128-row x 32-column boxes
