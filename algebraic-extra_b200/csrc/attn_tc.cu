@@ -50,8 +50,11 @@ constexpr int kFwdSmem = kTileBytes * (1 + 2 * kFwdStages) + 1024;
 constexpr int kBwdThreads = 768;
 constexpr int kHalfBytes = kTileBytes / 2;  // 64 rows x 64 bf16
 constexpr int kBwdStages = 4;               // Q / dO ring of 64-query halves
+// K x2, V, the Q / dO ring, dS^T x2 tiles, the dQ box, stat / di, alignment slack
+constexpr int kBwdSmem = 3 * kTileBytes + 2 * kBwdStages * kHalfBytes + 4 * kTileBytes + kTileBytes +
+                         2 * kBwdStages * 64 * 4 + 1024;
 constexpr int kBwdGradWarps = 16, kBwdDrain = 16, kBwdProducer = 20;
-constexpr int kBwdSmem = kTileBytes * 13 + 4 * kTile * 4 + 1024;
+
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
@@ -336,42 +339,63 @@ __device__ __forceinline__ uint32_t sw128_off(int row, int col16) {
   return half * kTileBytes + row * 128 + ((u ^ (row & 7)) << 4);
 }
 
-// Backward loop over 64-query sub-tiles u = 2*ii + h of the 128-query tiles
-// ii (h = u & 1 is also the buffer index b). TMEM (512 columns):
-//   S^T[b] = base + 64b, dP^T[b] = base + 128 + 64b (fp32, 128 keys x 64
-//   queries), dV = base + 256, dK = base + 320, dQ_tile[ii & 1] = base + 384
-//   + 64 (ii & 1).
-// Shared memory keeps P^T of the two sub-tiles b, freed as soon as dV of the
-// sub-tile has completed, and dS^T of two query tiles, each as two
-// 128B-swizzled 64-column halves side by side: exactly the MN-major A operand
-// of dQ_tile = dS K once both halves are written. With dS^T double-buffered,
-// the next tile's score gradients never wait for this tile's dQ product.
+// One work item of the persistent backward: key tile kt of head bh. Items
+// are handed out heaviest first (kt ascending: key tile kt meets nq - kt
+// query tiles) through a global counter, so SMs that finish early take the
+// next largest remaining item.
+struct BwdItem {
+  int kt, bh, ni;  // ni query tiles, 2 * ni sub-tiles
+};
+__device__ __forceinline__ BwdItem bwd_item(int it, int BH, int nq) {
+  BwdItem r;
+  r.kt = it / BH;
+  r.bh = it - r.kt * BH;
+  r.ni = nq - r.kt;
+  return r;
+}
+
+// Persistent backward: one CTA per SM walks work items. Per item, the
+// 64-query sub-tiles u = 2*ii + h of its query tiles ii (h = u & 1 is also
+// the TMEM buffer) run through the pipeline below; every ring and barrier
+// is indexed by counters that continue across items, so the next item's
+// loads and products overlap the end of the current one.
+// TMEM (512 columns): S^T[b] = base + 64b, dP^T[b] = base + 128 + 64b (fp32,
+// 128 keys x 64 queries), dV = base + 256, dK = base + 320, dQ_tile = base +
+// 384, P^T[b] = base + 448 + 32b (bf16 pairs: the A operand of dV += P^T dO).
+// Shared memory: K double-buffered (S^T and the dQ products of an item read
+// it), V, a 4-stage ring of 64-query Q / dO / stat / di halves, dS^T of two
+// query tiles (each two 128B-swizzled 64-column halves side by side: exactly
+// the MN-major A operand of dQ_tile = dS K), and a 16 KB fp32 staging box
+// for the dQ reduce-adds.
 template <int N, bool CLIP, bool INV_STAT>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                        const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
-                       const __grid_constant__ CUtensorMap tdq, algx_attn_config cfg, const float* __restrict__ stat, const float* __restrict__ di,
-                       const float* __restrict__ guard, float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dk,
-                       __nv_bfloat16* __restrict__ dv, int T, int* dev_err) {
+                       const __grid_constant__ CUtensorMap tdq, algx_attn_config cfg, const float* __restrict__ stat,
+                       const float* __restrict__ di, const float* __restrict__ guard, __nv_bfloat16* __restrict__ dk,
+                       __nv_bfloat16* __restrict__ dv, int* __restrict__ item_counter, int BH, int T, int* dev_err) {
   const Eff e = resolve_variant(cfg, guard);
   if (e.branch != BR_UNSHIFTED) return;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
-  uint8_t* sK = smem;
-  uint8_t* sV = smem + kTileBytes;
-  uint8_t* sQ = smem + 2 * kTileBytes;    // kBwdStages x 64 queries
-  uint8_t* sdO = smem + 4 * kTileBytes;   // kBwdStages x 64 queries
-  uint8_t* sPT = smem + 6 * kTileBytes;   // 128 keys x 64 queries bf16, [2 sub-tiles]
-  uint8_t* sdST = smem + 8 * kTileBytes;  // 128 keys x 128 queries bf16, [2 query tiles][2 halves]
-  uint8_t* sDQ = smem + 12 * kTileBytes;  // fp32 dQ staging: one 128-row x 32-column swizzled box
-  float* sStat = reinterpret_cast<float*>(smem + 13 * kTileBytes);  // [kBwdStages][64]
+  uint8_t* sK = smem;                     // 2 buffers
+  uint8_t* sV = smem + 2 * kTileBytes;
+  uint8_t* sQ = smem + 3 * kTileBytes;    // kBwdStages x 64 queries
+  uint8_t* sdO = sQ + kBwdStages * kHalfBytes;
+  uint8_t* sdST = sdO + kBwdStages * kHalfBytes;  // 128 keys x 128 queries bf16, [2 query tiles][2 halves]
+  uint8_t* sDQ = sdST + 4 * kTileBytes;           // fp32 dQ staging: one 128-row x 32-column swizzled box
+  float* sStat = reinterpret_cast<float*>(sDQ + kTileBytes);  // [kBwdStages][64]
   float* sDi = sStat + kBwdStages * 64;                              // [kBwdStages][64]
-  __shared__ uint64_t bar_kv, bar_fin, bar_dq_full[2], bar_dq_free[2], bar_stage_full, bar_stage_free;
+  __shared__ uint64_t bar_k_full[2], bar_k_free[2], bar_v_full, bar_v_free, bar_fin, bar_acc_free;
+  __shared__ uint64_t bar_dq_full, bar_dq_free, bar_stage_full, bar_stage_free;
   __shared__ uint64_t bar_st_full[2], bar_st_free[2], bar_ps_ready[2], bar_p_free[2], bar_ds_free[2], bar_ds_ready[2];
   __shared__ uint64_t bar_qd_full[kBwdStages], bar_qd_empty[kBwdStages], bar_issued[3];
+  __shared__ uint64_t bar_item_full[4], bar_item_empty[4];
+  __shared__ int item_q[4];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
   volatile int* abort_v = &abort_flag;
+  volatile int* item_v = item_q;
   // Before the CTA frees TMEM, each issuer waits (bounded) until its own
   // products have completed, on the normal and on the abort path alike.
   auto settle_issuer = [&](int i) {
@@ -379,40 +403,55 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     volatile int quiet = 0;
     mbar_wait(&bar_issued[i], 0, &quiet, dev_err);
   };
+  // Consumers of the item queue: one arrival per consumer warp on
+  // bar_item_empty (16 gradient + 4 drain warps + 3 issuers).
+  constexpr int kItemConsumers = kBwdGradWarps + 4 + 3;
+  auto next_item = [&](int j, bool whole_warp) -> int {
+    const int slot = j & 3;
+    bool ok = whole_warp ? mbar_wait_warp(&bar_item_full[slot], (j >> 2) & 1, abort_v, dev_err)
+                         : mbar_wait(&bar_item_full[slot], (j >> 2) & 1, abort_v, dev_err);
+    const int it = ok ? item_v[slot] : -1;
+    if (whole_warp) __syncwarp();
+    if (!whole_warp || (threadIdx.x & 31) == 0) mbar_arrive(&bar_item_empty[slot]);
+    return it;
+  };
 
   // warps 0-15: score gradients; warp w takes the sub-tiles u with u % 2 == w / 8 (TMEM buffer w / 8),
   //   TMEM lanes 32 (w % 4).. and query columns 32 ((w / 4) % 2).. of each
-  // warps 16-19: dQ drain; warp 20: TMA producer (+ TMEM owner); warps 21-23: MMA issuers
-  // (21: S^T and dP^T, 22: dV and dK, 23: dQ)
+  // warps 16-19: dQ drain and the dK / dV write-out; warp 20: item queue + TMA producer (+ TMEM owner);
+  // warps 21-23: MMA issuers (21: S^T and dP^T, 22: dV and dK, 23: dQ)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nq = T / kTile;
-  // heads along x, key tiles along y: key tile 0 (the most query tiles) first
-  const int kt = (int)blockIdx.y;
-  const int bh = blockIdx.x;
-  const int row_base = bh * T;
-  const int ni = nq - kt;  // query tiles kt .. nq-1
-  const int nu = 2 * ni;   // 64-query sub-tiles
+  const int total_items = BH * nq;
 
   if (threadIdx.x == 0) {
-    mbar_init(&bar_kv, 1);
-    mbar_init(&bar_fin, 1);
-    mbar_init(&bar_stage_full, 4);
-    mbar_init(&bar_stage_free, 1);
-    for (int i = 0; i < 3; ++i) mbar_init(&bar_issued[i], 1);
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&bar_dq_full[b], 1);
-      mbar_init(&bar_dq_free[b], 4);
+      mbar_init(&bar_k_full[b], 1);
+      mbar_init(&bar_k_free[b], 1);
       mbar_init(&bar_st_full[b], 1);
       mbar_init(&bar_st_free[b], 8);
       mbar_init(&bar_ps_ready[b], 8);
       mbar_init(&bar_p_free[b], 1);
       mbar_init(&bar_ds_free[b], 1);
       mbar_init(&bar_ds_ready[b], 16);  // 8 gradient warps x 2 sub-tiles of a query tile
-      mbar_init(&bar_qd_full[b], 1);
-      mbar_init(&bar_qd_empty[b], 1);
-      mbar_init(&bar_qd_full[b + 2], 1);
-      mbar_init(&bar_qd_empty[b + 2], 1);
     }
+    for (int i = 0; i < kBwdStages; ++i) {
+      mbar_init(&bar_qd_full[i], 1);
+      mbar_init(&bar_qd_empty[i], 1);
+    }
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&bar_item_full[i], 1);
+      mbar_init(&bar_item_empty[i], kItemConsumers);
+    }
+    for (int i = 0; i < 3; ++i) mbar_init(&bar_issued[i], 1);
+    mbar_init(&bar_v_full, 1);
+    mbar_init(&bar_v_free, 1);
+    mbar_init(&bar_fin, 1);
+    mbar_init(&bar_acc_free, 4);
+    mbar_init(&bar_dq_full, 1);
+    mbar_init(&bar_dq_free, 4);
+    mbar_init(&bar_stage_full, 4);
+    mbar_init(&bar_stage_free, 1);
     fence_mbar_init();
     abort_flag = 0;
   }
@@ -424,37 +463,61 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tS = tmem_base, tdP = tmem_base + 128, tdV = tmem_base + 256, tdK = tmem_base + 320,
-                 tdQ = tmem_base + 384;  // two 64-column buffers
+                 tdQ = tmem_base + 384, tPT = tmem_base + 448;
 
   if (warp == kBwdProducer) {
-    // ----- producer
+    // ----- item queue and TMA producer
     if (lane == 0) {
       prefetch_tmap(&tq);
       prefetch_tmap(&tk);
       prefetch_tmap(&tv);
       prefetch_tmap(&tdo);
       prefetch_tmap(&tdq);
-      mbar_expect_tx(&bar_kv, 2 * kTileBytes);
-      tma_load_2d(sK, &tk, &bar_kv, 0, row_base + kt * kTile);
-      tma_load_2d(sV, &tv, &bar_kv, 0, row_base + kt * kTile);
-      int issued[kBwdStages] = {-1, -1, -1, -1};
-      for (int u = 0; u < nu; ++u) {
-        const int hs = u & (kBwdStages - 1);
-        const int q_row = row_base + (kt + (u >> 1)) * kTile + 64 * (u & 1);
-        if (u >= kBwdStages && !mbar_wait(&bar_qd_empty[hs], ((u / kBwdStages) - 1) & 1, abort_v, dev_err)) break;
-        mbar_expect_tx(&bar_qd_full[hs], 2 * kHalfBytes + 2 * 64 * 4);
-        tma_load_2d(sQ + hs * kHalfBytes, &tq, &bar_qd_full[hs], 0, q_row);
-        tma_load_2d(sdO + hs * kHalfBytes, &tdo, &bar_qd_full[hs], 0, q_row);
-        bulk_load(sStat + hs * 64, stat + q_row, 64 * 4, &bar_qd_full[hs]);
-        bulk_load(sDi + hs * 64, di + q_row, 64 * 4, &bar_qd_full[hs]);
-        issued[hs] = u;
-      }
-      if (*abort_v) {
-        for (int i = 0; i < kBwdStages; ++i)
-          if (issued[i] >= 0) {
-            volatile int quiet = 0;
-            mbar_wait(&bar_qd_full[i], (issued[i] / kBwdStages) & 1, &quiet, nullptr);
+      int pending_k[2] = {-1, -1}, pending_v = -1, pending_qd[kBwdStages] = {-1, -1, -1, -1};
+      int U = 0;  // global sub-tile counter
+      for (int j = 0;; ++j) {
+        const int slot = j & 3;
+        if (j >= 4 && !mbar_wait(&bar_item_empty[slot], ((j >> 2) - 1) & 1, abort_v, dev_err)) break;
+        int it = atomicAdd(item_counter, 1);
+        if (it >= total_items) it = -1;
+        item_v[slot] = it;
+        mbar_arrive(&bar_item_full[slot]);  // release: the item index is visible to the waiters
+        if (it < 0) break;
+        const BwdItem w = bwd_item(it, BH, nq);
+        const int row_base = w.bh * T;
+        const int kb = j & 1;
+        if (j >= 2 && !mbar_wait(&bar_k_free[kb], ((j >> 1) - 1) & 1, abort_v, dev_err)) break;
+        mbar_expect_tx(&bar_k_full[kb], kTileBytes);
+        tma_load_2d(sK + kb * kTileBytes, &tk, &bar_k_full[kb], 0, row_base + w.kt * kTile);
+        pending_k[kb] = j;
+        if (j >= 1 && !mbar_wait(&bar_v_free, (j - 1) & 1, abort_v, dev_err)) break;
+        mbar_expect_tx(&bar_v_full, kTileBytes);
+        tma_load_2d(sV, &tv, &bar_v_full, 0, row_base + w.kt * kTile);
+        pending_v = j;
+        bool ok = true;
+        for (int u = 0; u < 2 * w.ni; ++u, ++U) {
+          const int hs = U % kBwdStages;
+          const int q_row = row_base + (w.kt + (u >> 1)) * kTile + 64 * (u & 1);
+          if (U >= kBwdStages && !mbar_wait(&bar_qd_empty[hs], ((U / kBwdStages) - 1) & 1, abort_v, dev_err)) {
+            ok = false;
+            break;
           }
+          mbar_expect_tx(&bar_qd_full[hs], 2 * kHalfBytes + 2 * 64 * 4);
+          tma_load_2d(sQ + hs * kHalfBytes, &tq, &bar_qd_full[hs], 0, q_row);
+          tma_load_2d(sdO + hs * kHalfBytes, &tdo, &bar_qd_full[hs], 0, q_row);
+          bulk_load(sStat + hs * 64, stat + q_row, 64 * 4, &bar_qd_full[hs]);
+          bulk_load(sDi + hs * 64, di + q_row, 64 * 4, &bar_qd_full[hs]);
+          pending_qd[hs] = U;
+        }
+        if (!ok) break;
+      }
+      if (*abort_v) {  // let copies in flight land before the CTA exits
+        volatile int quiet = 0;
+        for (int b = 0; b < 2; ++b)
+          if (pending_k[b] >= 0) mbar_wait(&bar_k_full[b], (pending_k[b] >> 1) & 1, &quiet, nullptr);
+        if (pending_v >= 0) mbar_wait(&bar_v_full, pending_v & 1, &quiet, nullptr);
+        for (int i = 0; i < kBwdStages; ++i)
+          if (pending_qd[i] >= 0) mbar_wait(&bar_qd_full[i], (pending_qd[i] / kBwdStages) & 1, &quiet, nullptr);
       }
     }
   } else if (warp == kBwdProducer + 1) {
@@ -462,21 +525,34 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     if (lane == 0) {
       const uint32_t idS = idesc_bf16_f32(128, 64, 0, 0);
       const uint32_t k0 = smem_u32(sK), v0 = smem_u32(sV), q0 = smem_u32(sQ), do0 = smem_u32(sdO);
-      bool ok = mbar_wait(&bar_kv, 0, abort_v, dev_err);
-      for (int u = 0; ok && u < nu; ++u) {
-        const int b = u & 1, hs = u & (kBwdStages - 1);
-        if (!mbar_wait(&bar_qd_full[hs], (u / kBwdStages) & 1, abort_v, dev_err)) break;
-        if (u >= 2 && !mbar_wait(&bar_st_free[b], ((u >> 1) - 1) & 1, abort_v, dev_err)) break;
-        tc_fence_after();
-        const uint32_t qb = q0 + hs * kHalfBytes;
-        const uint32_t db = do0 + hs * kHalfBytes;
+      int U = 0;
+      bool ok = true;
+      for (int j = 0; ok; ++j) {
+        const int it = next_item(j, false);
+        if (it < 0) break;
+        const BwdItem w = bwd_item(it, BH, nq);
+        const int kb = j & 1;
+        ok = mbar_wait(&bar_k_full[kb], (j >> 1) & 1, abort_v, dev_err) &&
+             mbar_wait(&bar_v_full, j & 1, abort_v, dev_err);
+        const uint32_t kbase = k0 + kb * kTileBytes;
+        for (int u = 0; ok && u < 2 * w.ni; ++u, ++U) {
+          const int b = U & 1, hs = U % kBwdStages;
+          if (!mbar_wait(&bar_qd_full[hs], (U / kBwdStages) & 1, abort_v, dev_err)) ok = false;
+          if (ok && U >= 2 && !mbar_wait(&bar_st_free[b], ((U >> 1) - 1) & 1, abort_v, dev_err)) ok = false;
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t qb = q0 + hs * kHalfBytes;
+          const uint32_t db = do0 + hs * kHalfBytes;
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          mma_ss(tS + 64 * b, desc_sw128(k0 + k * 32, 16, 1024), desc_sw128(qb + k * 32, 16, 1024), idS, k > 0);
+          for (int k = 0; k < 4; ++k)
+            mma_ss(tS + 64 * b, desc_sw128(kbase + k * 32, 16, 1024), desc_sw128(qb + k * 32, 16, 1024), idS,
+                   k > 0);
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          mma_ss(tdP + 64 * b, desc_sw128(v0 + k * 32, 16, 1024), desc_sw128(db + k * 32, 16, 1024), idS, k > 0);
-        mma_commit(&bar_st_full[b]);
+          for (int k = 0; k < 4; ++k)
+            mma_ss(tdP + 64 * b, desc_sw128(v0 + k * 32, 16, 1024), desc_sw128(db + k * 32, 16, 1024), idS, k > 0);
+          mma_commit(&bar_st_full[b]);
+        }
+        if (ok) mma_commit(&bar_v_free);  // every dP^T of the item has read V
       }
       settle_issuer(0);
     }
@@ -485,163 +561,176 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     // sub-tile, the other readers of its Q/dO half-stage, completed before its
     // score gradients were ready, so the commit after dK releases the stage.
     if (lane == 0) {
-      const uint32_t idKM = idesc_bf16_f32(128, 64, 0, 1);  // A K-major smem, B MN-major
-      const uint32_t q0 = smem_u32(sQ), do0 = smem_u32(sdO), pt0 = smem_u32(sPT), dsb = smem_u32(sdST);
+      const uint32_t idKM = idesc_bf16_f32(128, 64, 0, 1);  // A K-major (smem or TMEM), B MN-major
+      const uint32_t q0 = smem_u32(sQ), do0 = smem_u32(sdO), dsb = smem_u32(sdST);
+      int U = 0, I = 0;
       bool ok = true;
-      for (int w = 0; w < nu; ++w) {
-        const int b = w & 1, ii = w >> 1, s = ii & 1, hs = w & (kBwdStages - 1);
-        if (!mbar_wait(&bar_ps_ready[b], (w >> 1) & 1, abort_v, dev_err)) {
-          ok = false;
-          break;
+      for (int j = 0; ok; ++j) {
+        const int it = next_item(j, false);
+        if (it < 0) break;
+        const BwdItem w = bwd_item(it, BH, nq);
+        // the write-out of the previous item has read dK and dV out of TMEM
+        if (j >= 1 && !mbar_wait(&bar_acc_free, (j - 1) & 1, abort_v, dev_err)) break;
+        for (int u = 0; u < 2 * w.ni; ++u, ++U) {
+          const int b = U & 1, hs = U % kBwdStages, s = (I + (u >> 1)) & 1;
+          if (!mbar_wait(&bar_ps_ready[b], (U >> 1) & 1, abort_v, dev_err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t qb = q0 + hs * kHalfBytes;
+          const uint32_t db = do0 + hs * kHalfBytes;
+          const uint32_t ds0 = dsb + s * 2 * kTileBytes;
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            mma_ts(tdV, tPT + 32 * b + 8 * k, desc_sw128(db + k * 2048, 8192, 1024), idKM, (u > 0 || k > 0));
+          mma_commit(&bar_p_free[b]);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            mma_ss(tdK, desc_sw128(ds0 + b * kTileBytes + k * 32, 16, 1024), desc_sw128(qb + k * 2048, 8192, 1024),
+                   idKM, (u > 0 || k > 0));
+          mma_commit(&bar_qd_empty[hs]);
         }
-        tc_fence_after();
-        const uint32_t qb = q0 + hs * kHalfBytes;
-        const uint32_t db = do0 + hs * kHalfBytes;
-        const uint32_t ds0 = dsb + s * 2 * kTileBytes;
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          mma_ss(tdV, desc_sw128(pt0 + b * kTileBytes + k * 32, 16, 1024), desc_sw128(db + k * 2048, 8192, 1024),
-                 idKM, (w > 0 || k > 0));
-        mma_commit(&bar_p_free[b]);
-#pragma unroll
-        for (int k = 0; k < 4; ++k)
-          mma_ss(tdK, desc_sw128(ds0 + b * kTileBytes + k * 32, 16, 1024), desc_sw128(qb + k * 2048, 8192, 1024),
-                 idKM, (w > 0 || k > 0));
-        mma_commit(&bar_qd_empty[hs]);
+        I += w.ni;
+        if (ok) mma_commit(&bar_fin);  // dK and dV of the item are complete
       }
-      if (ok && !*abort_v) mma_commit(&bar_fin);
       settle_issuer(1);
     }
   } else if (warp == kBwdProducer + 3) {
-    // ----- dQ_tile = dS K of query tile ii into TMEM buffer ii & 1
+    // ----- dQ_tile = dS K of query tile i
     if (lane == 0) {
       const uint32_t idMM = idesc_bf16_f32(128, 64, 1, 1);  // A MN-major smem, B MN-major
       const uint32_t k0 = smem_u32(sK), dsb = smem_u32(sdST);
-      bool ok = mbar_wait(&bar_kv, 0, abort_v, dev_err);
-      for (int ii = 0; ok && ii < ni; ++ii) {
-        const int s = ii & 1, qb2 = ii & 1;
-        if (!mbar_wait(&bar_ds_ready[s], (ii >> 1) & 1, abort_v, dev_err)) break;
-        if (ii >= 2 && !mbar_wait(&bar_dq_free[qb2], ((ii >> 1) - 1) & 1, abort_v, dev_err)) break;
-        tc_fence_after();
-        const uint32_t ds0 = dsb + s * 2 * kTileBytes;
+      int I = 0;
+      bool ok = true;
+      for (int j = 0; ok; ++j) {
+        const int it = next_item(j, false);
+        if (it < 0) break;
+        const BwdItem w = bwd_item(it, BH, nq);
+        const int kb = j & 1;
+        if (!mbar_wait(&bar_k_full[kb], (j >> 1) & 1, abort_v, dev_err)) break;
+        const uint32_t kbase = k0 + kb * kTileBytes;
+        for (int ii = 0; ii < w.ni; ++ii, ++I) {
+          const int s = I & 1;
+          if (!mbar_wait(&bar_ds_ready[s], (I >> 1) & 1, abort_v, dev_err) ||
+              (I >= 1 && !mbar_wait(&bar_dq_free, (I - 1) & 1, abort_v, dev_err))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t ds0 = dsb + s * 2 * kTileBytes;
 #pragma unroll
-        for (int k = 0; k < 8; ++k)
-          mma_ss(tdQ + 64 * qb2, desc_sw128(ds0 + k * 2048, kTileBytes, 1024), desc_sw128(k0 + k * 2048, 8192, 1024),
-                 idMM, k > 0);
-        mma_commit(&bar_dq_full[qb2]);
-        mma_commit(&bar_ds_free[s]);
+          for (int k = 0; k < 8; ++k)
+            mma_ss(tdQ, desc_sw128(ds0 + k * 2048, kTileBytes, 1024), desc_sw128(kbase + k * 2048, 8192, 1024),
+                   idMM, k > 0);
+          mma_commit(&bar_dq_full);
+          mma_commit(&bar_ds_free[s]);
+        }
+        if (ok) mma_commit(&bar_k_free[kb]);  // the item's last product that reads K
       }
       settle_issuer(2);
     }
   } else if (warp < kBwdGradWarps) {
-    // ----- score-gradient warps: group g = warp / 8 takes sub-tiles g, g + 2, ...
+    // ----- score-gradient warps: group g = warp / 8 takes global sub-tiles U with U % 2 == g
     const int g = warp >> 3, q4 = warp & 3, hc = (warp >> 2) & 1;
     const int r = q4 * 32 + lane;  // key row within the tile (TMEM lane)
     const uint32_t lane_off = (uint32_t)(q4 * 32) << 16;
     const int b = g;  // TMEM S^T / dP^T buffer and P^T half of this group
+    int U = 0, I = 0;
     bool ok = true;
-    for (int u = g; u < nu; u += 2) {
-      const int ii = u >> 1, s = ii & 1;
-      if (!mbar_wait_warp(&bar_st_full[b], (u >> 1) & 1, abort_v, dev_err)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      uint32_t pk[2][8], dk2[2][8];
-#pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        uint32_t sv[16], pv[16];
-        const uint32_t col = 64 * b + 32 * hc + 16 * j;  // TMEM column of the chunk within S^T / dP^T
-        tmem_ld16x2(tS + col + lane_off, sv, tdP + col + lane_off, pv);
-        if (j == 1) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&bar_st_free[b]);
-        }
-        const int col0 = 64 * b + 32 * hc + 16 * j;  // query column within the 128-query tile
-        const int hs = u & (kBwdStages - 1);
-        const float* st = sStat + hs * 64 + 32 * hc + 16 * j;
-        const float* dd = sDi + hs * 64 + 32 * hc + 16 * j;
-        if (ii == 0)
-          grads_chunk<N, CLIP, INV_STAT, true, 16>(sv, pv, st, dd, pk[j], dk2[j], cfg.clamp, col0, r);
-        else
-          grads_chunk<N, CLIP, INV_STAT, false, 16>(sv, pv, st, dd, pk[j], dk2[j], cfg.clamp, col0, r);
-      }
-      // P^T of sub-tile u - 2 must have been consumed by its dV product,
-      // dS^T of query tile ii - 2 by its dQ product.
-      if (u >= 2 && !mbar_wait_warp(&bar_p_free[b], ((u >> 1) - 1) & 1, abort_v, dev_err)) {
-        ok = false;
-        break;
-      }
-      const int c16 = 8 * b + 4 * hc;  // first 16-byte unit of this warp's 32 columns
-#pragma unroll
-      for (int un = 0; un < 4; ++un) {
-        const uint32_t* v = pk[un >> 1] + 4 * (un & 1);
-        *reinterpret_cast<uint4*>(sPT + sw128_off(r, c16 + un)) = make_uint4(v[0], v[1], v[2], v[3]);
-      }
-      if (ii >= 2 && !mbar_wait_warp(&bar_ds_free[s], ((ii >> 1) - 1) & 1, abort_v, dev_err)) {
-        ok = false;
-        break;
-      }
-      uint8_t* ds_tile = sdST + s * 2 * kTileBytes;
-#pragma unroll
-      for (int un = 0; un < 4; ++un) {
-        const uint32_t* v = dk2[un >> 1] + 4 * (un & 1);
-        *reinterpret_cast<uint4*>(ds_tile + sw128_off(r, c16 + un)) = make_uint4(v[0], v[1], v[2], v[3]);
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&bar_ps_ready[b]);
-        mbar_arrive(&bar_ds_ready[s]);
-      }
-    }
-    // dK (group 0) and dV (group 1): 32 columns per thread
-    if (ok && mbar_wait_warp(&bar_fin, 0, abort_v, dev_err)) {
-      tc_fence_after();
-      const size_t row = (size_t)row_base + (size_t)kt * kTile + r;
-      uint32_t v[32];
-      tmem_ld32((g == 0 ? tdK : tdV) + lane_off + hc * 32, v);
-      __nv_bfloat16* dst = g == 0 ? dk : dv;
-      const float f = g == 0 ? (float)N : 1.f;
-      uint4* d4 = reinterpret_cast<uint4*>(dst + row * 64 + hc * 32);
-#pragma unroll
-      for (int un = 0; un < 4; ++un) {
-        uint4 w;
-        w.x = pack_bf16x2(__uint_as_float(v[8 * un + 0]) * f, __uint_as_float(v[8 * un + 1]) * f);
-        w.y = pack_bf16x2(__uint_as_float(v[8 * un + 2]) * f, __uint_as_float(v[8 * un + 3]) * f);
-        w.z = pack_bf16x2(__uint_as_float(v[8 * un + 4]) * f, __uint_as_float(v[8 * un + 5]) * f);
-        w.w = pack_bf16x2(__uint_as_float(v[8 * un + 6]) * f, __uint_as_float(v[8 * un + 7]) * f);
-        d4[un] = w;
-      }
-    }
-  } else if (warp < kBwdDrain + 4) {
-    // ----- dQ drain warps: thread owns query row qi*128 + r (TMEM lane r).
-    // Two rounds (columns 0-31, then 32-63) through one 16 KB staging box;
-    // row r, 16-byte chunk c of a 128-byte box row sits at chunk c ^ (r & 7).
-    const int r = (warp - kBwdDrain) * 32 + lane;
-    const uint32_t lane_off = (uint32_t)((warp - kBwdDrain) * 32) << 16;
-    const bool issuer = warp == kBwdDrain && lane == 0;
-    bool ok = true;
-    for (int ii = 0; ok && ii < ni; ++ii) {
-      const int qb2 = ii & 1;
-      if (!mbar_wait_warp(&bar_dq_full[qb2], (ii >> 1) & 1, abort_v, dev_err)) break;
-      const int y = row_base + (kt + ii) * kTile;
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int round = 2 * ii + h;
-        tc_fence_after();
-        uint32_t v[32];
-        tmem_ld32(tdQ + 64 * qb2 + 32 * h + lane_off, v);
-        if (h == 1) {  // both halves are in registers: the TMEM buffer is free
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&bar_dq_free[qb2]);
-        }
-        if (round > 0 && !mbar_wait_warp(&bar_stage_free, (round - 1) & 1, abort_v, dev_err)) {
+    for (int j = 0; ok; ++j) {
+      const int it = next_item(j, true);
+      if (it < 0) break;
+      const BwdItem w = bwd_item(it, BH, nq);
+      const int nu = 2 * w.ni;
+      for (int u = g; u < nu; u += 2) {
+        const int Ug = U + u, ii = u >> 1, Ig = I + ii, s = Ig & 1;
+        if (!mbar_wait_warp(&bar_st_full[b], (Ug >> 1) & 1, abort_v, dev_err)) {
           ok = false;
           break;
         }
+        tc_fence_after();
+        const int hs = Ug % kBwdStages;
+        uint32_t pk[2][8], dk2[2][8];
+#pragma unroll
+        for (int jj = 0; jj < 2; ++jj) {
+          uint32_t sv[16], pv[16];
+          const uint32_t col = 64 * b + 32 * hc + 16 * jj;  // TMEM column of the chunk within S^T / dP^T
+          tmem_ld16x2(tS + col + lane_off, sv, tdP + col + lane_off, pv);
+          if (jj == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar_st_free[b]);
+          }
+          const int col0 = 64 * b + 32 * hc + 16 * jj;  // query column within the 128-query tile
+          const float* st = sStat + hs * 64 + 32 * hc + 16 * jj;
+          const float* dd = sDi + hs * 64 + 32 * hc + 16 * jj;
+          if (ii == 0)
+            grads_chunk<N, CLIP, INV_STAT, true, 16>(sv, pv, st, dd, pk[jj], dk2[jj], cfg.clamp, col0, r);
+          else
+            grads_chunk<N, CLIP, INV_STAT, false, 16>(sv, pv, st, dd, pk[jj], dk2[jj], cfg.clamp, col0, r);
+        }
+        // P^T of sub-tile Ug - 2 must have been consumed by its dV product,
+        // dS^T of query tile Ig - 2 by its dQ product.
+        if (Ug >= 2 && !mbar_wait_warp(&bar_p_free[b], ((Ug >> 1) - 1) & 1, abort_v, dev_err)) {
+          ok = false;
+          break;
+        }
+        {  // bf16 P^T pairs of this warp's 32 query columns -> 16 TMEM columns of P^T[b]
+          uint32_t pv16[16];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            pv16[i] = pk[0][i];
+            pv16[8 + i] = pk[1][i];
+          }
+          tmem_st16(tPT + 32 * b + 16 * hc + lane_off, pv16);
+        }
+        const int c16 = 8 * b + 4 * hc;  // first 16-byte unit of this warp's 32 columns
+        if (Ig >= 2 && !mbar_wait_warp(&bar_ds_free[s], ((Ig >> 1) - 1) & 1, abort_v, dev_err)) {
+          ok = false;
+          break;
+        }
+        uint8_t* ds_tile = sdST + s * 2 * kTileBytes;
+#pragma unroll
+        for (int un = 0; un < 4; ++un) {
+          const uint32_t* v = dk2[un >> 1] + 4 * (un & 1);
+          *reinterpret_cast<uint4*>(ds_tile + sw128_off(r, c16 + un)) = make_uint4(v[0], v[1], v[2], v[3]);
+        }
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&bar_ps_ready[b]);
+          mbar_arrive(&bar_ds_ready[s]);
+        }
+      }
+      U += nu;
+      I += w.ni;
+    }
+  } else if (warp < kBwdDrain + 4) {
+    // ----- dQ drain and the items' dK / dV write-out: thread owns TMEM lane r.
+    // dQ goes through one 16 KB staging box in two rounds per tile (columns
+    // 0-31, then 32-63); row r, 16-byte chunk c of a 128-byte box row sits at
+    // chunk c ^ (r & 7). The write-out of an item comes before the drain of
+    // its last dQ tile: the next item's first dV / dK products wait for it.
+    const int dw = warp - kBwdDrain, r = dw * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(dw * 32) << 16;
+    const bool issuer = dw == 0 && lane == 0;
+    int I = 0, rounds = 0;
+    bool ok = true;
+    // drain dQ tile I (query rows y..y+127) through the box
+    auto drain_tile = [&](int y) -> bool {
+      if (!mbar_wait_warp(&bar_dq_full, I & 1, abort_v, dev_err)) return false;
+      for (int h = 0; h < 2; ++h, ++rounds) {
+        tc_fence_after();
+        uint32_t v[32];
+        tmem_ld32(tdQ + 32 * h + lane_off, v);
+        if (h == 1) {  // both halves read: the next tile's product may overwrite TMEM
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bar_dq_free);
+        }
+        if (rounds > 0 && !mbar_wait_warp(&bar_stage_free, (rounds - 1) & 1, abort_v, dev_err)) return false;
 #pragma unroll
         for (int c = 0; c < 8; ++c)
           *reinterpret_cast<uint4*>(sDQ + r * 128 + ((c ^ (r & 7)) << 4)) =
@@ -649,22 +738,60 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bar_stage_full);
+        bool good = true;
         if (issuer) {
-          if (mbar_wait(&bar_stage_full, round & 1, abort_v, dev_err)) {
+          if (mbar_wait(&bar_stage_full, rounds & 1, abort_v, dev_err)) {
             tma_reduce_add_2d(&tdq, sDQ, 32 * h, y);
             bulk_commit_group();
             bulk_wait_group_read0();
             mbar_arrive(&bar_stage_free);
           } else {
-            ok = false;
+            good = false;
           }
         }
         __syncwarp();
-        if (!__all_sync(0xffffffffu, ok)) {
-          ok = false;
-          break;
+        if (!__all_sync(0xffffffffu, good)) return false;
+      }
+      ++I;
+      return true;
+    };
+    for (int j = 0; ok; ++j) {
+      const int it = next_item(j, true);
+      if (it < 0) break;
+      const BwdItem w = bwd_item(it, BH, nq);
+      const int row_base = w.bh * T;
+      for (int ii = 0; ok && ii + 1 < w.ni; ++ii) ok = drain_tile(row_base + (w.kt + ii) * kTile);
+      // dK = n * acc, dV = acc, rounded to bf16; then TMEM is free for the next item
+      if (!ok || !mbar_wait_warp(&bar_fin, j & 1, abort_v, dev_err)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const size_t row = (size_t)row_base + (size_t)w.kt * kTile + r;
+#pragma unroll 1
+      for (int part = 0; part < 4; ++part) {
+        const bool is_k = part < 2;
+        const int c0 = 32 * (part & 1);
+        uint32_t v[32];
+        tmem_ld32((is_k ? tdK : tdV) + lane_off + c0, v);
+        if (part == 3) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&bar_acc_free);
+        }
+        const float f = is_k ? (float)N : 1.f;
+        uint4* d4 = reinterpret_cast<uint4*>((is_k ? dk : dv) + row * 64 + c0);
+#pragma unroll
+        for (int un = 0; un < 4; ++un) {
+          uint4 q;
+          q.x = pack_bf16x2(__uint_as_float(v[8 * un + 0]) * f, __uint_as_float(v[8 * un + 1]) * f);
+          q.y = pack_bf16x2(__uint_as_float(v[8 * un + 2]) * f, __uint_as_float(v[8 * un + 3]) * f);
+          q.z = pack_bf16x2(__uint_as_float(v[8 * un + 4]) * f, __uint_as_float(v[8 * un + 5]) * f);
+          q.w = pack_bf16x2(__uint_as_float(v[8 * un + 6]) * f, __uint_as_float(v[8 * un + 7]) * f);
+          d4[un] = q;
         }
       }
+      ok = drain_tile(row_base + (w.kt + w.ni - 1) * kTile);
     }
     if (issuer) bulk_wait_group0();
   }
@@ -712,14 +839,19 @@ int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& 
 
 template <int N, bool CLIP, bool INV>
 int launch_bwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tdo,
-               const CUtensorMap& tdq, const algx_attn_config& cfg, const float* stat, const float* di, const float* guard, float* dq_acc,
-               void* dk, void* dv, int64_t B, int64_t H, int64_t T, cudaStream_t st) {
+               const CUtensorMap& tdq, const algx_attn_config& cfg, const float* stat, const float* di,
+               const float* guard, int* item_counter, void* dk, void* dv, int64_t B, int64_t H, int64_t T,
+               cudaStream_t st) {
   auto kern = attn_bwd_tc_kernel<N, CLIP, INV>;
   ALGX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem));
-  dim3 grid((unsigned)(B * H), (unsigned)(T / kTile));
-  kern<<<grid, kBwdThreads, kBwdSmem, st>>>(tq, tk, tv, tdo, tdq, cfg, stat, di, guard, dq_acc,
+  int dev = 0, sms = 0;
+  ALGX_CUDA(cudaGetDevice(&dev));
+  ALGX_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int64_t items = B * H * (T / kTile);
+  const unsigned grid = (unsigned)std::min<int64_t>(items, sms);  // persistent: one CTA per SM
+  kern<<<grid, kBwdThreads, kBwdSmem, st>>>(tq, tk, tv, tdo, tdq, cfg, stat, di, guard,
                                             static_cast<__nv_bfloat16*>(dk), static_cast<__nv_bfloat16*>(dv),
-                                            (int)T, device_error_word());
+                                            item_counter, (int)(B * H), (int)T, device_error_word());
   ALGX_LAUNCHED("attn_bwd_tc launch");
   return ALGX_OK;
 }
@@ -756,8 +888,10 @@ int tc_attn_fwd(const algx_attn_config& cfg, const void* q_scaled, const void* k
   return ALGX_OK;
 }
 
+// fp32 dQ accumulator, then the persistent kernel's work-item counter (both
+// zeroed by one memset per call).
 size_t tc_attn_bwd_workspace(int64_t B, int64_t H, int64_t T, int64_t D) {
-  return (size_t)B * H * T * D * sizeof(float);
+  return (size_t)B * H * T * D * sizeof(float) + 256;
 }
 
 int tc_attn_bwd(const algx_attn_config& cfg, const void* q_scaled, const void* k, const void* v, const void* dout,
@@ -775,13 +909,15 @@ int tc_attn_bwd(const algx_attn_config& cfg, const void* q_scaled, const void* k
   const size_t nacc = (size_t)B * H * T * 64;
   CUtensorMap tdq;  // fp32 accumulator, reduce-added in 128-row x 32-column boxes
   if (int s = make_tmap_2d(&tdq, acc, ALGX_F32, 64, (uint64_t)(B * H * T), 256, 32, kTile, true)) return s;
-  ALGX_CUDA(cudaMemsetAsync(acc, 0, nacc * sizeof(float), st));
+  int* item_counter = reinterpret_cast<int*>(acc + nacc);
+  ALGX_CUDA(cudaMemsetAsync(acc, 0, nacc * sizeof(float) + 256, st));
   const bool clip = cfg.mode == ALGX_MODE_CLIPPED;
   // The guarded low branch uses the 1/Z statistic; the clipped link follows cfg.inv_stat.
   const bool inv = clip ? cfg.inv_stat != 0 : true;
   int s;
 #define ALGX_BWD(NN, CC, II) \
-  launch_bwd<NN, CC, II>(maps[0], maps[1], maps[2], maps[3], tdq, cfg, stat, di, guard, acc, dk, dv, B, H, T, st)
+  launch_bwd<NN, CC, II>(maps[0], maps[1], maps[2], maps[3], tdq, cfg, stat, di, guard, item_counter, dk, dv, B, H, \
+                         T, st)
   if (cfg.n == 16)
     s = clip ? (inv ? ALGX_BWD(16, true, true) : ALGX_BWD(16, true, false)) : ALGX_BWD(16, false, true);
   else if (cfg.n == 8)
