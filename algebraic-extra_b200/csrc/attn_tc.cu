@@ -50,8 +50,8 @@ constexpr int kFwdSmem = kTileBytes * (1 + 2 * kFwdStages) + 1024;
 constexpr int kBwdThreads = 768;
 constexpr int kHalfBytes = kTileBytes / 2;  // 64 rows x 64 bf16
 constexpr int kBwdStages = 4;               // Q / dO ring of 64-query halves
-// K x2, V, the Q / dO ring, dS^T x2 tiles, the dQ box, stat / di, alignment slack
-constexpr int kBwdSmem = 3 * kTileBytes + 2 * kBwdStages * kHalfBytes + 4 * kTileBytes + kTileBytes +
+// K x2, V, the Q / dO ring, dS^T x2 tiles, dQ boxes x2, stat / di, alignment slack
+constexpr int kBwdSmem = 3 * kTileBytes + 2 * kBwdStages * kHalfBytes + 4 * kTileBytes + 2 * kTileBytes +
                          2 * kBwdStages * 64 * 4 + 1024;
 constexpr int kBwdGradWarps = 16, kBwdDrain = 16, kBwdProducer = 20;
 
@@ -365,8 +365,8 @@ __device__ __forceinline__ BwdItem bwd_item(int it, int BH, int nq) {
 // Shared memory: K double-buffered (S^T and the dQ products of an item read
 // it), V, a 4-stage ring of 64-query Q / dO / stat / di halves, dS^T of two
 // query tiles (each two 128B-swizzled 64-column halves side by side: exactly
-// the MN-major A operand of dQ_tile = dS K), and a 16 KB fp32 staging box
-// for the dQ reduce-adds.
+// the MN-major A operand of dQ_tile = dS K), and two 16 KB fp32 staging
+// boxes for the dQ reduce-adds.
 template <int N, bool CLIP, bool INV_STAT>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -383,11 +383,11 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   uint8_t* sQ = smem + 3 * kTileBytes;    // kBwdStages x 64 queries
   uint8_t* sdO = sQ + kBwdStages * kHalfBytes;
   uint8_t* sdST = sdO + kBwdStages * kHalfBytes;  // 128 keys x 128 queries bf16, [2 query tiles][2 halves]
-  uint8_t* sDQ = sdST + 4 * kTileBytes;           // fp32 dQ staging: one 128-row x 32-column swizzled box
-  float* sStat = reinterpret_cast<float*>(sDQ + kTileBytes);  // [kBwdStages][64]
+  uint8_t* sDQ = sdST + 4 * kTileBytes;           // fp32 dQ staging: two 128-row x 32-column swizzled boxes
+  float* sStat = reinterpret_cast<float*>(sDQ + 2 * kTileBytes);  // [kBwdStages][64]
   float* sDi = sStat + kBwdStages * 64;                              // [kBwdStages][64]
   __shared__ uint64_t bar_k_full[2], bar_k_free[2], bar_v_full, bar_v_free, bar_fin, bar_acc_free;
-  __shared__ uint64_t bar_dq_full, bar_dq_free, bar_stage_full, bar_stage_free;
+  __shared__ uint64_t bar_dq_full, bar_dq_free, bar_stage_full[2], bar_stage_free[2];
   __shared__ uint64_t bar_st_full[2], bar_st_free[2], bar_ps_ready[2], bar_p_free[2], bar_ds_free[2], bar_ds_ready[2];
   __shared__ uint64_t bar_qd_full[kBwdStages], bar_qd_empty[kBwdStages], bar_issued[3];
   __shared__ uint64_t bar_item_full[4], bar_item_empty[4];
@@ -450,8 +450,10 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_init(&bar_acc_free, 4);
     mbar_init(&bar_dq_full, 1);
     mbar_init(&bar_dq_free, 4);
-    mbar_init(&bar_stage_full, 4);
-    mbar_init(&bar_stage_free, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&bar_stage_full[b], 4);
+      mbar_init(&bar_stage_free[b], 1);
+    }
     fence_mbar_init();
     abort_flag = 0;
   }
@@ -709,10 +711,12 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     }
   } else if (warp < kBwdDrain + 4) {
     // ----- dQ drain and the items' dK / dV write-out: thread owns TMEM lane r.
-    // dQ goes through one 16 KB staging box in two rounds per tile (columns
-    // 0-31, then 32-63); row r, 16-byte chunk c of a 128-byte box row sits at
-    // chunk c ^ (r & 7). The write-out of an item comes before the drain of
-    // its last dQ tile: the next item's first dV / dK products wait for it.
+    // dQ goes out in two rounds per tile (columns 0-31, then 32-63) through
+    // two alternating 16 KB staging boxes, so the stores of one round overlap
+    // the reduce-add of the previous; row r, 16-byte chunk c of a 128-byte box
+    // row sits at chunk c ^ (r & 7). The write-out of an item comes before the
+    // drain of its last dQ tile: the next item's first dV / dK products wait
+    // for it.
     const int dw = warp - kBwdDrain, r = dw * 32 + lane;
     const uint32_t lane_off = (uint32_t)(dw * 32) << 16;
     const bool issuer = dw == 0 && lane == 0;
@@ -730,21 +734,26 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&bar_dq_free);
         }
-        if (rounds > 0 && !mbar_wait_warp(&bar_stage_free, (rounds - 1) & 1, abort_v, dev_err)) return false;
+        const int sb = rounds & 1;
+        uint8_t* box = sDQ + sb * kTileBytes;
+        if (rounds >= 2 && !mbar_wait_warp(&bar_stage_free[sb], ((rounds >> 1) - 1) & 1, abort_v, dev_err))
+          return false;
 #pragma unroll
         for (int c = 0; c < 8; ++c)
-          *reinterpret_cast<uint4*>(sDQ + r * 128 + ((c ^ (r & 7)) << 4)) =
+          *reinterpret_cast<uint4*>(box + r * 128 + ((c ^ (r & 7)) << 4)) =
               make_uint4(v[4 * c], v[4 * c + 1], v[4 * c + 2], v[4 * c + 3]);
         fence_proxy_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&bar_stage_full);
+        if (lane == 0) mbar_arrive(&bar_stage_full[sb]);
         bool good = true;
         if (issuer) {
-          if (mbar_wait(&bar_stage_full, rounds & 1, abort_v, dev_err)) {
-            tma_reduce_add_2d(&tdq, sDQ, 32 * h, y);
+          if (mbar_wait(&bar_stage_full[sb], (rounds >> 1) & 1, abort_v, dev_err)) {
+            tma_reduce_add_2d(&tdq, box, 32 * h, y);
             bulk_commit_group();
-            bulk_wait_group_read0();
-            mbar_arrive(&bar_stage_free);
+            if (rounds >= 1) {  // the previous round's box has been read: release it
+              bulk_wait_group_read1();
+              mbar_arrive(&bar_stage_free[sb ^ 1]);
+            }
           } else {
             good = false;
           }
