@@ -371,9 +371,10 @@ template <int N, bool CLIP, bool INV_STAT>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                        const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
-                       const __grid_constant__ CUtensorMap tdq, algx_attn_config cfg, const float* __restrict__ stat,
-                       const float* __restrict__ di, const float* __restrict__ guard, __nv_bfloat16* __restrict__ dk,
-                       __nv_bfloat16* __restrict__ dv, int* __restrict__ item_counter, int BH, int T, int* dev_err) {
+                       const __grid_constant__ CUtensorMap tdq, const __grid_constant__ CUtensorMap tdk,
+                       const __grid_constant__ CUtensorMap tdv, algx_attn_config cfg, const float* __restrict__ stat,
+                       const float* __restrict__ di, const float* __restrict__ guard, int* __restrict__ item_counter,
+                       int BH, int T, int* dev_err) {
   const Eff e = resolve_variant(cfg, guard);
   if (e.branch != BR_UNSHIFTED) return;
   extern __shared__ uint8_t smem_raw[];
@@ -475,6 +476,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       prefetch_tmap(&tv);
       prefetch_tmap(&tdo);
       prefetch_tmap(&tdq);
+      prefetch_tmap(&tdk);
+      prefetch_tmap(&tdv);
       int pending_k[2] = {-1, -1}, pending_v = -1, pending_qd[kBwdStages] = {-1, -1, -1, -1};
       int U = 0;  // global sub-tile counter
       for (int j = 0;; ++j) {
@@ -770,36 +773,63 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       const BwdItem w = bwd_item(it, BH, nq);
       const int row_base = w.bh * T;
       for (int ii = 0; ok && ii + 1 < w.ni; ++ii) ok = drain_tile(row_base + (w.kt + ii) * kTile);
-      // dK = n * acc, dV = acc, rounded to bf16; then TMEM is free for the next item
+      // dK = n * acc and dV = acc, rounded to bf16, leave through the staging
+      // boxes as two swizzled 128 x 64 tiles with TMA stores; TMEM is free for
+      // the next item as soon as both accumulators are in registers.
       if (!ok || !mbar_wait_warp(&bar_fin, j & 1, abort_v, dev_err)) {
         ok = false;
         break;
       }
-      tc_fence_after();
-      const size_t row = (size_t)row_base + (size_t)w.kt * kTile + r;
+      const int key_row = row_base + w.kt * kTile;
+      for (int which = 0; ok && which < 2; ++which, ++rounds) {
+        const int sb = rounds & 1;
+        uint8_t* box = sDQ + sb * kTileBytes;
+        if (rounds >= 2 && !mbar_wait_warp(&bar_stage_free[sb], ((rounds >> 1) - 1) & 1, abort_v, dev_err)) {
+          ok = false;
+          break;
+        }
+        const float f = which == 0 ? (float)N : 1.f;
 #pragma unroll 1
-      for (int part = 0; part < 4; ++part) {
-        const bool is_k = part < 2;
-        const int c0 = 32 * (part & 1);
-        uint32_t v[32];
-        tmem_ld32((is_k ? tdK : tdV) + lane_off + c0, v);
-        if (part == 3) {
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&bar_acc_free);
-        }
-        const float f = is_k ? (float)N : 1.f;
-        uint4* d4 = reinterpret_cast<uint4*>((is_k ? dk : dv) + row * 64 + c0);
+        for (int part = 0; part < 2; ++part) {
+          tc_fence_after();
+          uint32_t v[32];
+          tmem_ld32((which == 0 ? tdK : tdV) + lane_off + 32 * part, v);
+          if (which == 1 && part == 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bar_acc_free);
+          }
 #pragma unroll
-        for (int un = 0; un < 4; ++un) {
-          uint4 q;
-          q.x = pack_bf16x2(__uint_as_float(v[8 * un + 0]) * f, __uint_as_float(v[8 * un + 1]) * f);
-          q.y = pack_bf16x2(__uint_as_float(v[8 * un + 2]) * f, __uint_as_float(v[8 * un + 3]) * f);
-          q.z = pack_bf16x2(__uint_as_float(v[8 * un + 4]) * f, __uint_as_float(v[8 * un + 5]) * f);
-          q.w = pack_bf16x2(__uint_as_float(v[8 * un + 6]) * f, __uint_as_float(v[8 * un + 7]) * f);
-          d4[un] = q;
+          for (int un = 0; un < 4; ++un) {
+            uint4 q;
+            q.x = pack_bf16x2(__uint_as_float(v[8 * un + 0]) * f, __uint_as_float(v[8 * un + 1]) * f);
+            q.y = pack_bf16x2(__uint_as_float(v[8 * un + 2]) * f, __uint_as_float(v[8 * un + 3]) * f);
+            q.z = pack_bf16x2(__uint_as_float(v[8 * un + 4]) * f, __uint_as_float(v[8 * un + 5]) * f);
+            q.w = pack_bf16x2(__uint_as_float(v[8 * un + 6]) * f, __uint_as_float(v[8 * un + 7]) * f);
+            const int c = 4 * part + un;  // 16-byte unit (8 columns) of the 128-byte row
+            *reinterpret_cast<uint4*>(box + r * 128 + ((c ^ (r & 7)) << 4)) = q;
+          }
         }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar_stage_full[sb]);
+        bool good = true;
+        if (issuer) {
+          if (mbar_wait(&bar_stage_full[sb], (rounds >> 1) & 1, abort_v, dev_err)) {
+            tma_store_2d(which == 0 ? &tdk : &tdv, box, 0, key_row);
+            bulk_commit_group();
+            if (rounds >= 1) {
+              bulk_wait_group_read1();
+              mbar_arrive(&bar_stage_free[sb ^ 1]);
+            }
+          } else {
+            good = false;
+          }
+        }
+        __syncwarp();
+        if (!__all_sync(0xffffffffu, good)) ok = false;
       }
+      if (!ok) break;
       ok = drain_tile(row_base + (w.kt + w.ni - 1) * kTile);
     }
     if (issuer) bulk_wait_group0();
@@ -848,9 +878,9 @@ int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& 
 
 template <int N, bool CLIP, bool INV>
 int launch_bwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tdo,
-               const CUtensorMap& tdq, const algx_attn_config& cfg, const float* stat, const float* di,
-               const float* guard, int* item_counter, void* dk, void* dv, int64_t B, int64_t H, int64_t T,
-               cudaStream_t st) {
+               const CUtensorMap& tdq, const CUtensorMap& tdk, const CUtensorMap& tdv, const algx_attn_config& cfg,
+               const float* stat, const float* di, const float* guard, int* item_counter, int64_t B, int64_t H,
+               int64_t T, cudaStream_t st) {
   auto kern = attn_bwd_tc_kernel<N, CLIP, INV>;
   ALGX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem));
   int dev = 0, sms = 0;
@@ -858,9 +888,8 @@ int launch_bwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& 
   ALGX_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int64_t items = B * H * (T / kTile);
   const unsigned grid = (unsigned)std::min<int64_t>(items, sms);  // persistent: one CTA per SM
-  kern<<<grid, kBwdThreads, kBwdSmem, st>>>(tq, tk, tv, tdo, tdq, cfg, stat, di, guard,
-                                            static_cast<__nv_bfloat16*>(dk), static_cast<__nv_bfloat16*>(dv),
-                                            item_counter, (int)(B * H), (int)T, device_error_word());
+  kern<<<grid, kBwdThreads, kBwdSmem, st>>>(tq, tk, tv, tdo, tdq, tdk, tdv, cfg, stat, di, guard, item_counter,
+                                            (int)(B * H), (int)T, device_error_word());
   ALGX_LAUNCHED("attn_bwd_tc launch");
   return ALGX_OK;
 }
@@ -908,9 +937,9 @@ int tc_attn_bwd(const algx_attn_config& cfg, const void* q_scaled, const void* k
                 int64_t B, int64_t H, int64_t T, int32_t dtype, cudaStream_t st, bool* launched) {
   *launched = false;
   if (!fast_eligible(cfg, T, dtype)) return ALGX_OK;
-  CUtensorMap maps[4];
-  const void* ptrs[4] = {q_scaled, k, v, dout};
-  if (int s = make_maps(ptrs, 4, maps, B * H * T)) return s;
+  CUtensorMap maps[6];  // q, k, v, dO (loads), dK, dV (stores)
+  const void* ptrs[6] = {q_scaled, k, v, dout, dk, dv};
+  if (int s = make_maps(ptrs, 6, maps, B * H * T)) return s;
   // Q and dO stream in 64-query halves
   for (int i : {0, 3})
     if (int s = make_tmap_2d(&maps[i], ptrs[i], ALGX_BF16, 64, (uint64_t)(B * H * T), 128, 64, 64, true)) return s;
@@ -925,8 +954,8 @@ int tc_attn_bwd(const algx_attn_config& cfg, const void* q_scaled, const void* k
   const bool inv = clip ? cfg.inv_stat != 0 : true;
   int s;
 #define ALGX_BWD(NN, CC, II) \
-  launch_bwd<NN, CC, II>(maps[0], maps[1], maps[2], maps[3], tdq, cfg, stat, di, guard, item_counter, dk, dv, B, H, \
-                         T, st)
+  launch_bwd<NN, CC, II>(maps[0], maps[1], maps[2], maps[3], tdq, maps[4], maps[5], cfg, stat, di, guard, item_counter, \
+                         B, H, T, st)
   if (cfg.n == 16)
     s = clip ? (inv ? ALGX_BWD(16, true, true) : ALGX_BWD(16, true, false)) : ALGX_BWD(16, false, true);
   else if (cfg.n == 8)
