@@ -3,9 +3,9 @@
 // fast rho, n in {8, 16, 32}.
 //
 // Forward (kernels/flash.py:189-284, head_resident.py:24-93): one CTA per
-// (128-query tile, head), two CTAs per SM. Warp roles: warps 0-3 compute the
-// weights (thread = query row = TMEM lane), warp 4 issues TMA loads, warp 5
-// issues tcgen05 MMAs. S = Q K^T lands in TMEM (fp32), the weight warps turn
+// (128-query tile, head), two CTAs per SM. Warp roles: warps 0-7 compute the
+// weights in two groups (thread = query row = TMEM lane), warp 8 issues TMA
+// loads, warps 9 and 10 issue the tcgen05 MMAs (O += P V and S = Q K^T). S = Q K^T lands in TMEM (fp32), the weight warps turn
 // each row into p = rho(x)^n, accumulate the fp32 row sum, and write bf16 P
 // back into TMEM; O += P V reads P from TMEM (A operand) and V from shared
 // memory (MN-major). No running maximum exists on this branch, so O needs no
@@ -45,7 +45,8 @@ using namespace sm100;
 constexpr int kTile = 128;
 constexpr int kTileBytes = kTile * 64 * 2;  // 128 rows x 64 bf16
 constexpr int kFwdStages = 2;
-constexpr int kFwdThreads = 192;
+constexpr int kFwdThreads = 352;  // 8 weight warps, producer, P.V issuer, S issuer
+constexpr int kFwdProducer = 8;
 constexpr int kFwdSmem = kTileBytes * (1 + 2 * kFwdStages) + 1024;
 constexpr int kBwdThreads = 768;
 constexpr int kHalfBytes = kTileBytes / 2;  // 64 rows x 64 bf16
@@ -145,9 +146,13 @@ __device__ __forceinline__ void grads_chunk(const uint32_t (&sv)[C], const uint3
 // tiles j. TMEM (256 columns): three score buffers B[u % 3] = base + 64(u % 3)
 // (fp32, 128 x 64) and O = base + 192 (fp32, 128 x 64). The weight warps read
 // S_u into registers and write the bf16 P_u into the first 32 columns of the
-// same buffer; O += P_u V reads it there. An MMA takes ~1000 cycles from
-// issue to a visible completion, so the MMA thread keeps S two sub-tiles
-// ahead: S_{u+3} is issued into buffer u % 3 as soon as P_u.V has completed.
+// same buffer; O += P_u V reads it there. S and P.V are issued by two
+// threads (a thread waits ~100 cycles per tcgen05.mma it issues); the S
+// thread runs up to three sub-tiles ahead: S_{u+3} goes into buffer u % 3 as
+// soon as P_u.V has completed. Two groups of four weight warps take alternate sub-tiles (each
+// warp: its 32 query rows, the sub-tile's 64 keys in two 32-column chunks),
+// so one group's TMEM round trips and barrier waits overlap the other's
+// arithmetic; their partial row sums meet in shared memory at the end.
 template <int N, bool CLIP>
 __global__ void __launch_bounds__(kFwdThreads, 2)
     attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
@@ -161,12 +166,15 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
   uint8_t* sQ = smem;
   uint8_t* sK = smem + kTileBytes;
   uint8_t* sV = sK + kFwdStages * kTileBytes;
-  __shared__ uint64_t bar_q, bar_o_full, bar_s_full[3], bar_p_full[3], bar_p_free[3];
+  __shared__ uint64_t bar_q, bar_o_full, bar_l_ready, bar_s_full[3], bar_p_full[3], bar_p_free[3], bar_issued[2];
   __shared__ uint64_t bar_kv_full[kFwdStages], bar_kv_empty[kFwdStages];
+  __shared__ float l_part[kTile];  // row sums of weight group 1
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
   volatile int* abort_v = &abort_flag;
 
+  // warps 0-7: weights (group g = warp / 4 takes sub-tiles u % 2 == g; rows 32 (warp % 4)..)
+  // warp 8: TMA producer (+ TMEM owner); warp 9: O += P V issuer; warp 10: S = Q K^T issuer
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nq = T / kTile;
   // The scheduler dispatches blockIdx.x fastest: heads along x and the query
@@ -180,9 +188,12 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
   if (threadIdx.x == 0) {
     mbar_init(&bar_q, 1);
     mbar_init(&bar_o_full, 1);
+    mbar_init(&bar_l_ready, 4);
+    mbar_init(&bar_issued[0], 1);
+    mbar_init(&bar_issued[1], 1);
     for (int b = 0; b < 3; ++b) {
       mbar_init(&bar_s_full[b], 1);
-      mbar_init(&bar_p_full[b], 4);
+      mbar_init(&bar_p_full[b], 4);  // the four warps of the group that owns the sub-tile
       mbar_init(&bar_p_free[b], 1);
     }
     for (int s = 0; s < kFwdStages; ++s) {
@@ -192,7 +203,7 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
     fence_mbar_init();
     abort_flag = 0;
   }
-  if (warp == 4) {
+  if (warp == kFwdProducer) {
     tmem_alloc(&tmem_base, 256);
     tmem_relinquish();
   }
@@ -200,8 +211,15 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tS = tmem_base, tO = tmem_base + 192;
+  // Before the CTA frees TMEM, each issuer waits (bounded) until its own
+  // products have completed, on the normal and on the abort path alike.
+  auto settle_issuer = [&](int i) {
+    mma_commit(&bar_issued[i]);
+    volatile int quiet = 0;
+    mbar_wait(&bar_issued[i], 0, &quiet, dev_err);
+  };
 
-  if (warp == 4) {
+  if (warp == kFwdProducer) {
     if (lane == 0) {
       prefetch_tmap(&tq);
       prefetch_tmap(&tk);
@@ -225,86 +243,94 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
           }
       }
     }
-  } else if (warp == 5) {
+  } else if (warp == kFwdProducer + 2) {
+    // ----- S_w = Q K_w^T into buffer w % 3 (K rows of half w & 1 of tile w >> 1),
+    // up to three sub-tiles ahead of the P.V products
     if (lane == 0) {
       const uint32_t idS = idesc_bf16_f32(128, 64, 0, 0);
-      const uint32_t idO = idesc_bf16_f32(128, 64, 0, 1);
-      const uint32_t q0 = smem_u32(sQ), k0 = smem_u32(sK), v0 = smem_u32(sV);
-      // S_w = Q K_w^T into buffer w % 3 (K rows of half w & 1 of tile w >> 1)
-      auto issue_s = [&](int w) -> bool {
+      const uint32_t q0 = smem_u32(sQ), k0 = smem_u32(sK);
+      bool ok = mbar_wait(&bar_q, 0, abort_v, dev_err);
+      for (int w = 0; ok && w < nu; ++w) {
         const int b = w % 3, j = w >> 1, s = j % kFwdStages;
-        if ((w & 1) == 0 && !mbar_wait(&bar_kv_full[s], (j / kFwdStages) & 1, abort_v, dev_err)) return false;
-        if (w >= 3 && !mbar_wait(&bar_p_free[b], (w / 3 - 1) & 1, abort_v, dev_err)) return false;
+        if ((w & 1) == 0 && !mbar_wait(&bar_kv_full[s], (j / kFwdStages) & 1, abort_v, dev_err)) break;
+        if (w >= 3 && !mbar_wait(&bar_p_free[b], (w / 3 - 1) & 1, abort_v, dev_err)) break;
         tc_fence_after();
         const uint32_t kb = k0 + s * kTileBytes + (w & 1) * (kTileBytes / 2);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_ss(tS + 64 * b, desc_sw128(q0 + k * 32, 16, 1024), desc_sw128(kb + k * 32, 16, 1024), idS, k > 0);
         mma_commit(&bar_s_full[b]);
-        return true;
-      };
-      // O += P_w V_w, P_w in the first 32 columns of buffer w % 3
-      auto pv = [&](int w) -> bool {
-        const int b = w % 3, j = w >> 1, s = j % kFwdStages;
-        if (!mbar_wait(&bar_p_full[b], (w / 3) & 1, abort_v, dev_err)) return false;
+      }
+      settle_issuer(0);
+    }
+  } else if (warp == kFwdProducer + 1) {
+    // ----- O += P_u V_u, P_u in the first 32 columns of buffer u % 3. The
+    // S issuer's K reads of tile j completed before its weights were ready,
+    // so the commit after P.V of the tile's second half releases the K/V stage.
+    if (lane == 0) {
+      const uint32_t idO = idesc_bf16_f32(128, 64, 0, 1);
+      const uint32_t v0 = smem_u32(sV);
+      for (int u = 0; u < nu; ++u) {
+        const int b = u % 3, j = u >> 1, s = j % kFwdStages;
+        if (!mbar_wait(&bar_p_full[b], (u / 3) & 1, abort_v, dev_err)) break;
         tc_fence_after();
-        const uint32_t vb = v0 + s * kTileBytes + (w & 1) * (kTileBytes / 2);
+        const uint32_t vb = v0 + s * kTileBytes + (u & 1) * (kTileBytes / 2);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          mma_ts(tO, tS + 64 * b + k * 8, desc_sw128(vb + k * 2048, 8192, 1024), idO, (w > 0 || k > 0));
+          mma_ts(tO, tS + 64 * b + k * 8, desc_sw128(vb + k * 2048, 8192, 1024), idO, (u > 0 || k > 0));
         mma_commit(&bar_p_free[b]);
-        if (w & 1) mma_commit(&bar_kv_empty[s]);
-        return true;
-      };
-      bool ok = mbar_wait(&bar_q, 0, abort_v, dev_err);
-      for (int w = 0; ok && w < 2 && w < nu; ++w) ok = issue_s(w);
-      for (int u = 0; ok && u < nu; ++u) {
-        if (!pv(u)) break;
-        if (u + 2 < nu && !issue_s(u + 2)) break;
+        if (u & 1) mma_commit(&bar_kv_empty[s]);
         if (u == nu - 1) mma_commit(&bar_o_full);
       }
+      settle_issuer(1);
     }
   } else {
     // ----- weight warps: thread r owns query row qt*128 + r (TMEM lane r)
-    const int r = threadIdx.x;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const int g = warp >> 2;
+    const int r = (warp & 3) * 32 + lane;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     float l = 0.f, rr;
-    if (cfg.has_sink) l = weight<N, CLIP>(sink[bh % H], cfg.clamp, rr);
+    if (g == 0 && cfg.has_sink) l = weight<N, CLIP>(sink[bh % H], cfg.clamp, rr);
     bool ok = true;
-    for (int u = 0; u < nu; ++u) {
+    for (int u = g; u < nu; u += 2) {
       const int b = u % 3;
       if (!mbar_wait_warp(&bar_s_full[b], (u / 3) & 1, abort_v, dev_err)) {
         ok = false;
         break;
       }
-      tc_fence_after();
-      uint32_t sa[32], sb[32];
-      tmem_ld32x2(tS + 64 * b + lane_off, sa, tS + 64 * b + 32 + lane_off, sb);
+      const bool diag = (u >> 1) == qt;
       const int col0 = 64 * (u & 1);  // key offset within the 128-key tile
-      uint32_t pa[16], pb[16];
-      if ((u >> 1) == qt) {
-        l += weights_chunk<N, CLIP, true>(sa, pa, cfg.clamp, col0, r);
-        l += weights_chunk<N, CLIP, true>(sb, pb, cfg.clamp, col0 + 32, r);
-      } else {
-        l += weights_chunk<N, CLIP, false>(sa, pa, cfg.clamp, col0, r);
-        l += weights_chunk<N, CLIP, false>(sb, pb, cfg.clamp, col0 + 32, r);
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        tc_fence_after();
+        uint32_t sv[32], pk[16];
+        tmem_ld32(tS + 64 * b + 32 * c + lane_off, sv);
+        if (diag)
+          l += weights_chunk<N, CLIP, true>(sv, pk, cfg.clamp, col0 + 32 * c, r);
+        else
+          l += weights_chunk<N, CLIP, false>(sv, pk, cfg.clamp, col0 + 32 * c, r);
+        // P (bf16 pairs) over S columns 16c..16c+15, already consumed by this thread
+        tmem_st16(tS + 64 * b + 16 * c + lane_off, pk);
       }
-      tmem_st16(tS + 64 * b + lane_off, pa);
-      tmem_st16(tS + 64 * b + 16 + lane_off, pb);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar_p_full[b]);
     }
-    if (ok && mbar_wait_warp(&bar_o_full, 0, abort_v, dev_err)) {
+    if (g == 1) {
+      l_part[r] = l;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar_l_ready);  // release: l_part is visible to group 0
+    } else if (ok && mbar_wait_warp(&bar_l_ready, 0, abort_v, dev_err) &&
+               mbar_wait_warp(&bar_o_full, 0, abort_v, dev_err)) {
       tc_fence_after();
+      l += l_part[r];
       const float inv = 1.f / l;
       const size_t row = (size_t)row_base + (size_t)qt * kTile + r;
       uint4* dst = reinterpret_cast<uint4*>(o + row * 64);
-      uint32_t oa[32], ob[32];
-      tmem_ld32x2(tO + lane_off, oa, tO + lane_off + 32, ob);
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        const uint32_t* ov = c == 0 ? oa : ob;
+        uint32_t ov[32];
+        tmem_ld32(tO + lane_off + 32 * c, ov);
 #pragma unroll
         for (int un = 0; un < 4; ++un) {
           uint4 w;
@@ -320,7 +346,7 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) tmem_dealloc(tmem_base, 256);
+  if (warp == kFwdProducer) tmem_dealloc(tmem_base, 256);
 }
 
 // ---------------------------------------------------------------- backward
