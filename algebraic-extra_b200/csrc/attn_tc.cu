@@ -44,10 +44,11 @@ using namespace sm100;
 
 constexpr int kTile = 128;
 constexpr int kTileBytes = kTile * 64 * 2;  // 128 rows x 64 bf16
-constexpr int kFwdStages = 2;
+constexpr int kFwdKStages = 3;  // S = Q K^T runs up to three sub-tiles ahead of P.V ...
+constexpr int kFwdVStages = 2;  // ... so K tiles are needed earlier than V tiles
 constexpr int kFwdThreads = 352;  // 8 weight warps, producer, P.V issuer, S issuer
 constexpr int kFwdProducer = 8;
-constexpr int kFwdSmem = kTileBytes * (1 + 2 * kFwdStages) + 1024;
+constexpr int kFwdSmem = kTileBytes * (1 + kFwdKStages + kFwdVStages) + 1024;
 constexpr int kBwdThreads = 768;
 constexpr int kHalfBytes = kTileBytes / 2;  // 64 rows x 64 bf16
 constexpr int kBwdStages = 4;               // Q / dO ring of 64-query halves
@@ -165,9 +166,10 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sQ = smem;
   uint8_t* sK = smem + kTileBytes;
-  uint8_t* sV = sK + kFwdStages * kTileBytes;
+  uint8_t* sV = sK + kFwdKStages * kTileBytes;
   __shared__ uint64_t bar_q, bar_o_full, bar_l_ready, bar_s_full[3], bar_p_full[3], bar_p_free[3], bar_issued[2];
-  __shared__ uint64_t bar_kv_full[kFwdStages], bar_kv_empty[kFwdStages];
+  __shared__ uint64_t bar_k_full[kFwdKStages], bar_k_empty[kFwdKStages], bar_v_full[kFwdVStages],
+      bar_v_empty[kFwdVStages];
   __shared__ float l_part[kTile];  // row sums of weight group 1
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
@@ -196,9 +198,13 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
       mbar_init(&bar_p_full[b], 4);  // the four warps of the group that owns the sub-tile
       mbar_init(&bar_p_free[b], 1);
     }
-    for (int s = 0; s < kFwdStages; ++s) {
-      mbar_init(&bar_kv_full[s], 1);
-      mbar_init(&bar_kv_empty[s], 1);
+    for (int s = 0; s < kFwdKStages; ++s) {
+      mbar_init(&bar_k_full[s], 1);
+      mbar_init(&bar_k_empty[s], 1);
+    }
+    for (int s = 0; s < kFwdVStages; ++s) {
+      mbar_init(&bar_v_full[s], 1);
+      mbar_init(&bar_v_empty[s], 1);
     }
     fence_mbar_init();
     abort_flag = 0;
@@ -226,21 +232,26 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
       prefetch_tmap(&tv);
       mbar_expect_tx(&bar_q, kTileBytes);
       tma_load_2d(sQ, &tq, &bar_q, 0, row_base + qt * kTile);
-      int issued[kFwdStages] = {-1, -1};
+      // K tile j, then V tile j: K waits for the S products of tile j - 3,
+      // V for the P.V products of tile j - 2.
+      int issued_k[kFwdKStages] = {-1, -1, -1}, issued_v[kFwdVStages] = {-1, -1};
       for (int j = 0; j < nk; ++j) {
-        const int s = j % kFwdStages;
-        if (j >= kFwdStages && !mbar_wait(&bar_kv_empty[s], ((j / kFwdStages) - 1) & 1, abort_v, dev_err)) break;
-        mbar_expect_tx(&bar_kv_full[s], 2 * kTileBytes);
-        tma_load_2d(sK + s * kTileBytes, &tk, &bar_kv_full[s], 0, row_base + j * kTile);
-        tma_load_2d(sV + s * kTileBytes, &tv, &bar_kv_full[s], 0, row_base + j * kTile);
-        issued[s] = j;
+        const int sk = j % kFwdKStages, sv = j % kFwdVStages;
+        if (j >= kFwdKStages && !mbar_wait(&bar_k_empty[sk], ((j / kFwdKStages) - 1) & 1, abort_v, dev_err)) break;
+        mbar_expect_tx(&bar_k_full[sk], kTileBytes);
+        tma_load_2d(sK + sk * kTileBytes, &tk, &bar_k_full[sk], 0, row_base + j * kTile);
+        issued_k[sk] = j;
+        if (j >= kFwdVStages && !mbar_wait(&bar_v_empty[sv], ((j / kFwdVStages) - 1) & 1, abort_v, dev_err)) break;
+        mbar_expect_tx(&bar_v_full[sv], kTileBytes);
+        tma_load_2d(sV + sv * kTileBytes, &tv, &bar_v_full[sv], 0, row_base + j * kTile);
+        issued_v[sv] = j;
       }
       if (*abort_v) {  // let copies in flight land before the CTA exits
-        for (int s = 0; s < kFwdStages; ++s)
-          if (issued[s] >= 0) {
-            volatile int quiet = 0;
-            mbar_wait(&bar_kv_full[s], (issued[s] / kFwdStages) & 1, &quiet, nullptr);
-          }
+        volatile int quiet = 0;
+        for (int s = 0; s < kFwdKStages; ++s)
+          if (issued_k[s] >= 0) mbar_wait(&bar_k_full[s], (issued_k[s] / kFwdKStages) & 1, &quiet, nullptr);
+        for (int s = 0; s < kFwdVStages; ++s)
+          if (issued_v[s] >= 0) mbar_wait(&bar_v_full[s], (issued_v[s] / kFwdVStages) & 1, &quiet, nullptr);
       }
     }
   } else if (warp == kFwdProducer + 2) {
@@ -251,8 +262,8 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
       const uint32_t q0 = smem_u32(sQ), k0 = smem_u32(sK);
       bool ok = mbar_wait(&bar_q, 0, abort_v, dev_err);
       for (int w = 0; ok && w < nu; ++w) {
-        const int b = w % 3, j = w >> 1, s = j % kFwdStages;
-        if ((w & 1) == 0 && !mbar_wait(&bar_kv_full[s], (j / kFwdStages) & 1, abort_v, dev_err)) break;
+        const int b = w % 3, j = w >> 1, s = j % kFwdKStages;
+        if ((w & 1) == 0 && !mbar_wait(&bar_k_full[s], (j / kFwdKStages) & 1, abort_v, dev_err)) break;
         if (w >= 3 && !mbar_wait(&bar_p_free[b], (w / 3 - 1) & 1, abort_v, dev_err)) break;
         tc_fence_after();
         const uint32_t kb = k0 + s * kTileBytes + (w & 1) * (kTileBytes / 2);
@@ -260,26 +271,27 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
         for (int k = 0; k < 4; ++k)
           mma_ss(tS + 64 * b, desc_sw128(q0 + k * 32, 16, 1024), desc_sw128(kb + k * 32, 16, 1024), idS, k > 0);
         mma_commit(&bar_s_full[b]);
+        if (w & 1) mma_commit(&bar_k_empty[s]);  // both halves of K tile j have been read
       }
       settle_issuer(0);
     }
   } else if (warp == kFwdProducer + 1) {
-    // ----- O += P_u V_u, P_u in the first 32 columns of buffer u % 3. The
-    // S issuer's K reads of tile j completed before its weights were ready,
-    // so the commit after P.V of the tile's second half releases the K/V stage.
+    // ----- O += P_u V_u, P_u in the first 32 columns of buffer u % 3; the
+    // commit after P.V of a tile's second half releases its V stage.
     if (lane == 0) {
       const uint32_t idO = idesc_bf16_f32(128, 64, 0, 1);
       const uint32_t v0 = smem_u32(sV);
       for (int u = 0; u < nu; ++u) {
-        const int b = u % 3, j = u >> 1, s = j % kFwdStages;
+        const int b = u % 3, j = u >> 1, s = j % kFwdVStages;
         if (!mbar_wait(&bar_p_full[b], (u / 3) & 1, abort_v, dev_err)) break;
+        if ((u & 1) == 0 && !mbar_wait(&bar_v_full[s], (j / kFwdVStages) & 1, abort_v, dev_err)) break;
         tc_fence_after();
         const uint32_t vb = v0 + s * kTileBytes + (u & 1) * (kTileBytes / 2);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
           mma_ts(tO, tS + 64 * b + k * 8, desc_sw128(vb + k * 2048, 8192, 1024), idO, (u > 0 || k > 0));
         mma_commit(&bar_p_free[b]);
-        if (u & 1) mma_commit(&bar_kv_empty[s]);
+        if (u & 1) mma_commit(&bar_v_empty[s]);
         if (u == nu - 1) mma_commit(&bar_o_full);
       }
       settle_issuer(1);
