@@ -81,8 +81,9 @@ SIGNATURES = {
     "algx_head_reduce": ([ctypes.POINTER(HeadConfig), _P, _P, _P, _I32, _I64, _P, _P, _P, _P], ctypes.c_int),
     "algx_head_finalize": ([ctypes.POINTER(HeadConfig), _P, _P, _P, _P, _I64, _I64, _P, _P, _P, _P, _P],
                            ctypes.c_int),
+    "algx_head_bwd_workspace_size": ([_I64, _I64, _I64, _I32], ctypes.c_size_t),
     "algx_head_bwd": ([ctypes.POINTER(HeadConfig), _P, _P, _P, _P, _P, _P, _I32, _P, _I64, _I64, _I64, _I64, _I32,
-                       _P], ctypes.c_int),
+                       _P, ctypes.c_size_t, _P], ctypes.c_int),
     "algx_selftest_tcgen05": ([_I32, _P, _P, _P, _P], ctypes.c_int),
 }
 

@@ -75,15 +75,25 @@ def head_finalize(cfg, t32, mlz, vocab_total):
     return out[0], out[1], sc[0:1], sc[1:2]
 
 
-def head_backward(h16, e16, t32, stat, scale, cfg, vocab_offset=0, dh_dtype=torch.bfloat16):
-    """(dh, dembed fp32) for this shard; ``scale`` is a 1-element device tensor."""
+def head_backward(h16, e16, t32, stat, scale, cfg, vocab_offset=0, dh_dtype=torch.bfloat16, workspace=None):
+    """(dh, dembed fp32) for this shard; ``scale`` is a 1-element device tensor.
+
+    ``workspace`` (uint8, at least ``algx_head_bwd_workspace_size`` bytes)
+    holds one bf16 logit-gradient slab; it is allocated here when not given.
+    """
     N, d = h16.shape
     V = e16.shape[0]
+    lib = L.lib()
+    code = L.dtype_code(dh_dtype)
+    need = lib.algx_head_bwd_workspace_size(N, d, V, code)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(need, dtype=torch.uint8, device=h16.device)
     dh = torch.empty((N, d), dtype=dh_dtype, device=h16.device)
     de = torch.empty((V, d), dtype=torch.float32, device=h16.device)
-    L.check(L.lib().algx_head_bwd(cfg, h16.data_ptr(), e16.data_ptr(), t32.data_ptr(), stat.data_ptr(),
-                                  scale.data_ptr(), dh.data_ptr(), L.dtype_code(dh_dtype), de.data_ptr(), N, d, V,
-                                  vocab_offset, L.ALGX_BF16, L.stream_of(h16)), "algx_head_bwd")
+    L.check(lib.algx_head_bwd(cfg, h16.data_ptr(), e16.data_ptr(), t32.data_ptr(), stat.data_ptr(),
+                              scale.data_ptr(), dh.data_ptr(), code, de.data_ptr(), N, d, V, vocab_offset,
+                              L.ALGX_BF16, workspace.data_ptr(), workspace.numel(), L.stream_of(h16)),
+            "algx_head_bwd")
     return dh, de
 
 

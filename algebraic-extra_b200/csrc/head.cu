@@ -10,14 +10,19 @@
 // by column compare. Per-split partials are combined by algx_head_reduce and
 // finished by algx_head_finalize (stat, telemetry, objective).
 //
-// Backward (fused_head.py:120-156, 194-216): two launches of one kernel.
-// Mode 0 (dh): rows = tokens, columns = vocabulary; mode 1 (dE): rows =
-// vocabulary, columns = tokens. A CTA owns 128 rows and one d-chunk (<= 256
-// columns) of the output. Per 128-column tile it recomputes the logit tile
-// (K loop over d), turns it into dz (softmax - y, or (p - y) r) scaled and
-// rounded to bf16, stores dz into TMEM, and accumulates out += dz . Y[:, chunk]
-// with dz as the TMEM A operand. dz is never written to HBM.
+// Backward (fused_head.py:120-156, 194-216), one vocabulary slab of
+// kSlabCols columns at a time, so the logits are never materialised in full:
+// head_dz_tc_kernel recomputes the slab's logits with the forward's pipeline
+// and its epilogue writes dz = (softmax - y) or (p - y) r, scaled and rounded
+// to bf16 (the reference's dzb), into a slab-sized workspace; two plain GEMMs
+// then consume the slab: dh += dz . E_slab (fp32 accumulation across slabs)
+// and dE_slab = dz^T . h. At config 3 a slab is 16384 x 4096 bf16 (134 MB,
+// about the size of L2), so both GEMMs read it mostly from L2.
+#include <cublas_v2.h>
+
 #include <algorithm>
+#include <mutex>
+#include <string>
 
 #include "algx_common.cuh"
 #include "sm100.cuh"
@@ -211,50 +216,48 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
 }
 
 // ------------------------------------------------------------------ backward
-constexpr int kGradStages = 3;
-constexpr int kGradStageBytes = 2 * kChunkBytes;  // X chunk + Y chunk (128 rows each)
-constexpr int kGradThreads = 192;
+constexpr int kSlabCols = 4096;  // vocabulary columns per backward slab (16 forward tiles)
 
-struct GradArgs {
+struct DzArgs {
   algx_head_config cfg;
   const int32_t* targets;
-  const float* stat;    // per token
-  const float* scale;   // device scalar: g * slope / count
+  const float* stat;   // per token
+  const float* scale;  // device scalar: g * slope / count
   int N, d, V, voff;
-  int rows, cols;       // rows / columns of this launch (tokens or vocabulary)
-  int dc;               // output d-chunk width (64..256, divides d)
-  int out_bf16;         // output dtype
+  int tile0;           // first (local) vocabulary tile of the slab
+  int ntiles;          // tiles in the slab
+  int splits;          // CTAs per 128-token block
+  int ldz;             // row stride of the dz slab (elements)
 };
 
-template <int MODE, int KIND, int NPOW>
-__global__ void __launch_bounds__(kGradThreads, 1)
-    head_grad_tc_kernel(const __grid_constant__ CUtensorMap tx, const __grid_constant__ CUtensorMap ty, GradArgs a,
-                        void* __restrict__ out, int* dev_err) {
+// Logits of one slab with the forward's load / MMA pipeline; the epilogue
+// (thread = token) turns each fp32 logit into bf16 dz and stores its row
+// segment of the slab. Columns past the vocabulary and ignored rows give 0.
+template <int KIND, int NPOW>
+__global__ void __launch_bounds__(kHeadThreads, 1)
+    head_dz_tc_kernel(const __grid_constant__ CUtensorMap th, const __grid_constant__ CUtensorMap te, DzArgs a,
+                      __nv_bfloat16* __restrict__ dz, int* dev_err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1k(smem_raw);
-  uint8_t* yout = smem + kGradStages * kGradStageBytes;         // [dc/64 boxes][128 rows][64]
-  __shared__ uint64_t full[kGradStages], empty[kGradStages];
-  __shared__ uint64_t z_full, dz_full, dz_free, yo_full, yo_empty, acc_done;
+  __shared__ uint64_t full[kFwdStages], empty[kFwdStages], acc_full[2], acc_empty[2];
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
   volatile int* abort_v = &abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rb = blockIdx.x, chunk = blockIdx.y;
+  const int tb = blockIdx.x, split = blockIdx.y;
+  const int per = (a.ntiles + a.splits - 1) / a.splits;
+  const int t0 = a.tile0 + split * per, t1 = a.tile0 + min(a.ntiles, (split + 1) * per);
   const int nk = a.d / 64;
-  const int nct = (a.cols + 127) / 128;
-  const int nbox = a.dc / 64;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kGradStages; ++s) {
+    for (int s = 0; s < kFwdStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(&z_full, 1);
-    mbar_init(&dz_full, 4);
-    mbar_init(&dz_free, 1);
-    mbar_init(&yo_full, 1);
-    mbar_init(&yo_empty, 1);
-    mbar_init(&acc_done, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
     fence_mbar_init();
     abort_flag = 0;
   }
@@ -265,177 +268,124 @@ __global__ void __launch_bounds__(kGradThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  const uint32_t tZ = tmem_base, tDZ = tmem_base + 128, tACC = tmem_base + 256;
 
   if (warp == 4) {
-    if (lane == 0) {
-      prefetch_tmap(&tx);
-      prefetch_tmap(&ty);
+    if (lane == 0 && t0 < t1) {
+      prefetch_tmap(&th);
+      prefetch_tmap(&te);
       int it = 0;
-      bool ok = true;
-      for (int ct = 0; ok && ct < nct; ++ct) {
+      int last_stage_it[kFwdStages] = {-1, -1, -1, -1};
+      for (int t = t0; t < t1 && !*abort_v; ++t)
         for (int kc = 0; kc < nk; ++kc, ++it) {
-          const int s = it % kGradStages;
-          if (it >= kGradStages && !mbar_wait(&empty[s], ((it / kGradStages) - 1) & 1, abort_v, dev_err)) {
-            ok = false;
-            break;
-          }
-          uint8_t* st = smem + s * kGradStageBytes;
-          mbar_expect_tx(&full[s], kGradStageBytes);
-          tma_load_2d(st, &tx, &full[s], kc * 64, rb * kRowsT);
-          tma_load_2d(st + kChunkBytes, &ty, &full[s], kc * 64, ct * 128);
+          const int s = it % kFwdStages;
+          if (it >= kFwdStages && !mbar_wait(&empty[s], ((it / kFwdStages) - 1) & 1, abort_v, dev_err)) break;
+          uint8_t* st = smem + s * kFwdStageBytes;
+          mbar_expect_tx(&full[s], kFwdStageBytes);
+          tma_load_2d(st, &th, &full[s], kc * 64, tb * kRowsT);
+          tma_load_2d(st + kChunkBytes, &te, &full[s], kc * 64, t * kFwdNT);
+          last_stage_it[s] = it;
         }
-        if (!ok) break;
-        if (ct > 0 && !mbar_wait(&yo_empty, (ct - 1) & 1, abort_v, dev_err)) break;
-        mbar_expect_tx(&yo_full, nbox * kChunkBytes);
-        for (int bx = 0; bx < nbox; ++bx)
-          tma_load_2d(yout + bx * kChunkBytes, &ty, &yo_full, chunk * a.dc + bx * 64, ct * 128);
-      }
+      if (*abort_v)
+        for (int s = 0; s < kFwdStages; ++s)
+          if (last_stage_it[s] >= 0) {
+            volatile int quiet = 0;
+            mbar_wait(&full[s], (last_stage_it[s] / kFwdStages) & 1, &quiet, nullptr);
+          }
     }
   } else if (warp == 5) {
-    if (lane == 0) {
-      const uint32_t idz = idesc_bf16_f32(128, 128, 0, 0);
-      const uint32_t ido = idesc_bf16_f32(128, a.dc, 0, 1);
-      const uint32_t s0 = smem_u32(smem), y0 = smem_u32(yout);
+    if (lane == 0 && t0 < t1) {
+      const uint32_t id = idesc_bf16_f32(128, kFwdNT, 0, 0);
+      const uint32_t s0 = smem_u32(smem);
       int it = 0;
       bool ok = true;
-      auto out_mma = [&](int ct) -> bool {
-        if (!mbar_wait(&dz_full, ct & 1, abort_v, dev_err)) return false;
-        if (!mbar_wait(&yo_full, ct & 1, abort_v, dev_err)) return false;
+      for (int t = t0; ok && t < t1; ++t) {
+        const int buf = (t - t0) & 1, use = (t - t0) >> 1;
+        if (use > 0 && !mbar_wait(&acc_empty[buf], (use - 1) & 1, abort_v, dev_err)) break;
         tc_fence_after();
-#pragma unroll
-        for (int k = 0; k < 8; ++k)
-          mma_ts(tACC, tDZ + k * 8, desc_sw128(y0 + k * 2048, kChunkBytes, 1024), ido, (ct > 0 || k > 0));
-        mma_commit(&dz_free);
-        mma_commit(&yo_empty);
-        return true;
-      };
-      for (int ct = 0; ok && ct < nct; ++ct) {
-        // the z buffer is free once the epilogue has turned z_{ct-1} into dz
-        if (ct > 0 && !out_mma(ct - 1)) break;
+        const uint32_t acc = tmem_base + buf * kFwdNT;
         for (int kc = 0; kc < nk; ++kc, ++it) {
-          const int s = it % kGradStages;
-          if (!mbar_wait(&full[s], (it / kGradStages) & 1, abort_v, dev_err)) {
+          const int s = it % kFwdStages;
+          if (!mbar_wait(&full[s], (it / kFwdStages) & 1, abort_v, dev_err)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t xb = s0 + s * kGradStageBytes, yb = xb + kChunkBytes;
+          const uint32_t hb = s0 + s * kFwdStageBytes, eb = hb + kChunkBytes;
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            mma_ss(tZ, desc_sw128(xb + k * 32, 16, 1024), desc_sw128(yb + k * 32, 16, 1024), idz, (kc > 0 || k > 0));
+            mma_ss(acc, desc_sw128(hb + k * 32, 16, 1024), desc_sw128(eb + k * 32, 16, 1024), id, (kc > 0 || k > 0));
           mma_commit(&empty[s]);
         }
-        if (ok) mma_commit(&z_full);
+        if (ok) mma_commit(&acc_full[buf]);
       }
-      if (ok && !*abort_v && out_mma(nct - 1)) mma_commit(&acc_done);
     }
   } else {
+    // epilogue: thread r owns token tb*128 + r
     const int r = threadIdx.x;
-    const int row = rb * kRowsT + r;  // token (mode 0) or local vocabulary row (mode 1)
+    const int tok = tb * kRowsT + r;
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
     const algx_head_config& c = a.cfg;
+    const int tgt = tok < a.N ? a.targets[tok] : -2147483647 - 1;
+    const bool row_ok = tok < a.N && !(c.has_ignore && tgt == c.ignore_index);
+    const int tloc = tgt - a.voff;  // local column of the target, may be out of range
+    const float st = tok < a.N ? a.stat[tok] : 0.f;
     const float scale = *a.scale;
-    // mode 0: per-row token statistics
-    float rstat = 0.f;
-    int rtgt = 0;
-    bool rvalid = row < a.rows;
-    if (MODE == 0 && rvalid) {
-      rstat = a.stat[row];
-      rtgt = a.targets[row];
-      if (c.has_ignore && rtgt == c.ignore_index) rvalid = false;
-    }
-    const int vrow = row + a.voff;  // mode 1: global vocabulary index of this row
-    bool ok = true;
-    for (int ct = 0; ct < nct; ++ct) {
-      if (!mbar_wait_warp(&z_full, ct & 1, abort_v, dev_err)) {
-        ok = false;
-        break;
-      }
+    const float log2e = 1.4426950408889634f;
+    const float stl = st * log2e;
+    __nv_bfloat16* drow = dz + (size_t)tok * a.ldz - (size_t)a.tile0 * kFwdNT;
+    for (int t = t0; t < t1; ++t) {
+      const int buf = (t - t0) & 1, use = (t - t0) >> 1;
+      if (!mbar_wait_warp(&acc_full[buf], use & 1, abort_v, dev_err)) break;
       tc_fence_after();
+      const uint32_t acc = tmem_base + buf * kFwdNT + lane_off;
 #pragma unroll 1
-      for (int cc = 0; cc < 4; ++cc) {
+      for (int cc = 0; cc < kFwdNT / 32; ++cc) {
         uint32_t zr[32];
-        tmem_ld32(tZ + lane_off + cc * 32, zr);
+        tmem_ld32(acc + cc * 32, zr);
+        const int col0 = t * kFwdNT + cc * 32;
         uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          float dzv[2];
+          float g2[2];
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const int jj = cc * 32 + 2 * i + h;      // column within the tile
-            const int col = ct * 128 + jj;          // token (mode 1) or local vocab (mode 0)
+            const int col = col0 + 2 * i + h;
             const float z = __uint_as_float(zr[2 * i + h]);
-            float st, y;
-            bool valid;
-            if (MODE == 0) {
-              valid = rvalid && col < a.cols;
-              st = rstat;
-              y = (col + a.voff == rtgt) ? 1.f : 0.f;
-            } else {
-              // token statistics of column col (the same address in every
-              // lane: one broadcast load)
-              const bool in = col < a.N;
-              const int tg = in ? __ldg(a.targets + col) : 0;
-              valid = row < a.rows && in && !(c.has_ignore && tg == c.ignore_index);
-              st = in ? __ldg(a.stat + col) : 0.f;
-              y = (vrow == tg) ? 1.f : 0.f;
-            }
+            const float y = col == tloc ? 1.f : 0.f;
             float g;
             if constexpr (KIND == ALGX_HEAD_CE) {
-              g = __expf(z - st) - y;
+              g = exp2f(fmaf(z, log2e, -stl)) - y;
             } else {
               const float x = fminf(z * c.inv_c, c.clamp);
               const float rad = fmaf(x, x, 1.f);
               const float rr = rsqrt_fast(rad);
               g = (ipow_t<NPOW>(fmaf(rad, rr, x) * st) - y) * rr;
             }
-            dzv[h] = valid ? g * scale : 0.f;
+            g2[h] = (row_ok && col < a.V) ? g * scale : 0.f;
           }
-          pk[i] = pack_bf16x2(dzv[0], dzv[1]);
+          pk[i] = pack_bf16x2(g2[0], g2[1]);
         }
-        if (cc == 0 && ct > 0 && !mbar_wait_warp(&dz_free, (ct - 1) & 1, abort_v, dev_err)) {
-          ok = false;
-          break;
+        if (tok < a.N) {
+          uint4* d4 = reinterpret_cast<uint4*>(drow + col0);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) d4[u] = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
         }
-        tmem_st16(tDZ + lane_off + cc * 16, pk);
       }
-      if (!ok) break;
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&dz_full);
-    }
-    // The TMEM loads are warp-collective: every lane reads, only rows in
-    // range store.
-    if (ok && mbar_wait_warp(&acc_done, 0, abort_v, dev_err)) {
-      tc_fence_after();
-      const bool store = row < a.rows;
-      for (int c0 = 0; c0 < a.dc; c0 += 32) {
-        uint32_t v[32];
-        tmem_ld32(tACC + lane_off + c0, v);
-        if (!store) continue;
-        const size_t o = (size_t)row * a.d + (size_t)chunk * a.dc + c0;
-        if (a.out_bf16) {
-          uint4* d4 = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(out) + o);
-#pragma unroll
-          for (int u = 0; u < 4; ++u)
-            d4[u] = make_uint4(pack_bf16x2(__uint_as_float(v[8 * u]), __uint_as_float(v[8 * u + 1])),
-                               pack_bf16x2(__uint_as_float(v[8 * u + 2]), __uint_as_float(v[8 * u + 3])),
-                               pack_bf16x2(__uint_as_float(v[8 * u + 4]), __uint_as_float(v[8 * u + 5])),
-                               pack_bf16x2(__uint_as_float(v[8 * u + 6]), __uint_as_float(v[8 * u + 7])));
-        } else {
-          float4* d4 = reinterpret_cast<float4*>(static_cast<float*>(out) + o);
-#pragma unroll
-          for (int u = 0; u < 8; ++u)
-            d4[u] = make_float4(__uint_as_float(v[4 * u]), __uint_as_float(v[4 * u + 1]),
-                                __uint_as_float(v[4 * u + 2]), __uint_as_float(v[4 * u + 3]));
-        }
-      }
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 4) tmem_dealloc(tmem_base, 512);
+}
+
+__global__ void f32_to_bf16_kernel(const float4* __restrict__ in, uint2* __restrict__ out, int64_t n4) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 v = in[i];
+    out[i] = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+  }
 }
 
 // ------------------------------------------------------------------ statistics
@@ -544,31 +494,54 @@ int launch_fwd_k(const CUtensorMap& th, const CUtensorMap& te, const HeadArgs& a
   }
 }
 
-template <int MODE, int KIND>
-int launch_grad_k(const CUtensorMap& tx, const CUtensorMap& ty, const GradArgs& a, void* out, cudaStream_t st) {
-  const int smem = kGradStages * kGradStageBytes + 4 * kChunkBytes + 1024;
-  const dim3 grid((unsigned)((a.rows + 127) / 128), (unsigned)(a.d / a.dc));
+template <int KIND>
+int launch_dz_k(const CUtensorMap& th, const CUtensorMap& te, const DzArgs& a, __nv_bfloat16* dz, cudaStream_t st) {
+  const int tb = (a.N + 127) / 128;
   auto run = [&](auto kern) -> int {
-    ALGX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    kern<<<grid, kGradThreads, smem, st>>>(tx, ty, a, out, device_error_word());
-    ALGX_LAUNCHED("head_grad_tc launch");
+    ALGX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem));
+    kern<<<dim3(tb, a.splits), kHeadThreads, kFwdSmem, st>>>(th, te, a, dz, device_error_word());
+    ALGX_LAUNCHED("head_dz_tc launch");
     return ALGX_OK;
   };
-  if (KIND == ALGX_HEAD_CE) return run(head_grad_tc_kernel<MODE, ALGX_HEAD_CE, 1>);
+  if (KIND == ALGX_HEAD_CE) return run(head_dz_tc_kernel<ALGX_HEAD_CE, 1>);
   switch (a.cfg.n) {
-    case 2: return run(head_grad_tc_kernel<MODE, ALGX_HEAD_ALG_CE, 2>);
-    case 4: return run(head_grad_tc_kernel<MODE, ALGX_HEAD_ALG_CE, 4>);
-    case 8: return run(head_grad_tc_kernel<MODE, ALGX_HEAD_ALG_CE, 8>);
-    case 16: return run(head_grad_tc_kernel<MODE, ALGX_HEAD_ALG_CE, 16>);
-    default: return run(head_grad_tc_kernel<MODE, ALGX_HEAD_ALG_CE, 32>);
+    case 2: return run(head_dz_tc_kernel<ALGX_HEAD_ALG_CE, 2>);
+    case 4: return run(head_dz_tc_kernel<ALGX_HEAD_ALG_CE, 4>);
+    case 8: return run(head_dz_tc_kernel<ALGX_HEAD_ALG_CE, 8>);
+    case 16: return run(head_dz_tc_kernel<ALGX_HEAD_ALG_CE, 16>);
+    default: return run(head_dz_tc_kernel<ALGX_HEAD_ALG_CE, 32>);
   }
 }
 
-int pick_chunk(int64_t d) {
-  for (int c : {256, 192, 128, 64})
-    if (d % c == 0) return c;
-  return 64;
+int64_t slab_cols(int64_t V) {
+  const int64_t vt = (V + kFwdNT - 1) / kFwdNT * kFwdNT;
+  return std::min<int64_t>(kSlabCols, vt);
 }
+
+// One cuBLAS handle per device, created on first use (the only allocation
+// the library makes for the head backward besides the caller's workspace).
+std::mutex g_blas_mu;
+cublasHandle_t g_blas[64] = {};
+int blas_handle(cublasHandle_t* out) {
+  int dev = 0;
+  ALGX_CUDA(cudaGetDevice(&dev));
+  ALGX_REQUIRE(dev >= 0 && dev < 64, "head_bwd: device index out of range");
+  std::lock_guard<std::mutex> lock(g_blas_mu);
+  if (!g_blas[dev]) {
+    cublasHandle_t hnd = nullptr;
+    if (cublasCreate(&hnd) != CUBLAS_STATUS_SUCCESS) return fail(ALGX_ERR_CUDA, "cublasCreate failed");
+    g_blas[dev] = hnd;
+  }
+  *out = g_blas[dev];
+  return ALGX_OK;
+}
+
+#define ALGX_BLAS(call)                                                                        \
+  do {                                                                                        \
+    cublasStatus_t _st = (call);                                                              \
+    if (_st != CUBLAS_STATUS_SUCCESS)                                                         \
+      return fail(ALGX_ERR_CUDA, std::string(#call) + " failed (" + std::to_string((int)_st) + ")"); \
+  } while (0)
 
 }  // namespace
 }  // namespace algx
@@ -625,33 +598,65 @@ int algx_head_finalize(const algx_head_config* cfg, const int32_t* targets, cons
   return ALGX_OK;
 }
 
+size_t algx_head_bwd_workspace_size(int64_t N, int64_t d, int64_t V, int32_t dh_dtype) {
+  if (N < 1 || d < 1 || V < 1) return 0;
+  size_t bytes = (size_t)N * (size_t)slab_cols(V) * 2;               // dz slab, bf16
+  if (dh_dtype == ALGX_BF16) bytes += (size_t)N * (size_t)d * 4;     // fp32 dh accumulator
+  return bytes;
+}
+
 int algx_head_bwd(const algx_head_config* cfg, const void* h, const void* embed, const int32_t* targets,
                   const float* stat, const float* scale, void* dh, int32_t dh_dtype, float* dembed, int64_t N,
-                  int64_t d, int64_t V, int64_t vocab_offset, int32_t dtype, void* stream) {
+                  int64_t d, int64_t V, int64_t vocab_offset, int32_t dtype, void* workspace, size_t workspace_bytes,
+                  void* stream) {
   if (int s = check_head(cfg, N, d, V, dtype)) return s;
   ALGX_REQUIRE(h && embed && targets && stat && scale && dh && dembed, "head_bwd: NULL pointer");
   ALGX_REQUIRE(dh_dtype == ALGX_F32 || dh_dtype == ALGX_BF16, "head_bwd: dh dtype must be float32 or bfloat16");
+  ALGX_REQUIRE(workspace && workspace_bytes >= algx_head_bwd_workspace_size(N, d, V, dh_dtype),
+               "head_bwd: workspace too small (see algx_head_bwd_workspace_size)");
+  const int64_t vs = slab_cols(V);
   CUtensorMap th, te;
   if (int s = make_tmap_2d(&th, h, ALGX_BF16, (uint64_t)d, (uint64_t)N, (uint64_t)d * 2, 64, 128, true)) return s;
-  if (int s = make_tmap_2d(&te, embed, ALGX_BF16, (uint64_t)d, (uint64_t)V, (uint64_t)d * 2, 64, 128, true))
+  if (int s = make_tmap_2d(&te, embed, ALGX_BF16, (uint64_t)d, (uint64_t)V, (uint64_t)d * 2, 64, kFwdNT, true))
     return s;
-  GradArgs a{*cfg, targets, stat, scale, (int)N, (int)d, (int)V, (int)vocab_offset, 0, 0, pick_chunk(d), 0};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // dh: rows = tokens, columns = vocabulary
-  GradArgs ah = a;
-  ah.rows = (int)N;
-  ah.cols = (int)V;
-  ah.out_bf16 = dh_dtype == ALGX_BF16;
-  int s = cfg->kind == ALGX_HEAD_CE ? launch_grad_k<0, ALGX_HEAD_CE>(th, te, ah, dh, st)
-                                    : launch_grad_k<0, ALGX_HEAD_ALG_CE>(th, te, ah, dh, st);
-  if (s) return s;
-  // dE: rows = vocabulary, columns = tokens
-  GradArgs ae = a;
-  ae.rows = (int)V;
-  ae.cols = (int)N;
-  ae.out_bf16 = 0;
-  return cfg->kind == ALGX_HEAD_CE ? launch_grad_k<1, ALGX_HEAD_CE>(te, th, ae, dembed, st)
-                                   : launch_grad_k<1, ALGX_HEAD_ALG_CE>(te, th, ae, dembed, st);
+  cublasHandle_t blas;
+  if (int s = blas_handle(&blas)) return s;
+  ALGX_BLAS(cublasSetStream(blas, st));
+  __nv_bfloat16* dz = static_cast<__nv_bfloat16*>(workspace);
+  float* dh_acc = dh_dtype == ALGX_F32 ? static_cast<float*>(dh)
+                                       : reinterpret_cast<float*>(static_cast<char*>(workspace) + (size_t)N * vs * 2);
+  const int tb = (int)((N + 127) / 128);
+  const int ntiles_total = (int)((V + kFwdNT - 1) / kFwdNT);
+  const float one = 1.f, zero = 0.f;
+  for (int64_t c0 = 0; c0 < V; c0 += vs) {
+    const int64_t vc = std::min<int64_t>(vs, V - c0);  // valid columns of this slab
+    DzArgs a{*cfg, targets, stat, scale, (int)N, (int)d, (int)V, (int)vocab_offset, (int)(c0 / kFwdNT), 0, 1, (int)vs};
+    a.ntiles = std::min<int>((int)(vs / kFwdNT), ntiles_total - a.tile0);
+    // enough CTAs for a few waves: 128-token blocks x tile groups
+    a.splits = std::max(1, std::min(a.ntiles, (4 * 148 + tb - 1) / tb));
+    int s = cfg->kind == ALGX_HEAD_CE ? launch_dz_k<ALGX_HEAD_CE>(th, te, a, dz, st)
+                                      : launch_dz_k<ALGX_HEAD_ALG_CE>(th, te, a, dz, st);
+    if (s) return s;
+    // dh (row-major N x d) += dz (N x vc) . E[c0 : c0 + vc] (vc x d); column-major view:
+    // dh^T (d x N) = E_slab^T (d x vc) . dz^T (vc x N)
+    const __nv_bfloat16* eslab = static_cast<const __nv_bfloat16*>(embed) + (size_t)c0 * d;
+    ALGX_BLAS(cublasGemmEx(blas, CUBLAS_OP_N, CUBLAS_OP_N, (int)d, (int)N, (int)vc, &one, eslab, CUDA_R_16BF, (int)d,
+                           dz, CUDA_R_16BF, (int)vs, c0 == 0 ? &zero : &one, dh_acc, CUDA_R_32F, (int)d,
+                           CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT));
+    // dE[c0 : c0 + vc] (row-major vc x d) = dz^T . h; column-major view:
+    // dE_slab^T (d x vc) = h^T (d x N) . dz (N x vc)
+    ALGX_BLAS(cublasGemmEx(blas, CUBLAS_OP_N, CUBLAS_OP_T, (int)d, (int)vc, (int)N, &one, h, CUDA_R_16BF, (int)d, dz,
+                           CUDA_R_16BF, (int)vs, &zero, dembed + (size_t)c0 * d, CUDA_R_32F, (int)d,
+                           CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT));
+  }
+  if (dh_dtype == ALGX_BF16) {
+    const int64_t n4 = N * d / 4;
+    f32_to_bf16_kernel<<<(unsigned)std::min<int64_t>((n4 + 255) / 256, 148 * 8), 256, 0, st>>>(
+        reinterpret_cast<const float4*>(dh_acc), static_cast<uint2*>(dh), n4);
+    ALGX_LAUNCHED("head dh rounding launch");
+  }
+  return ALGX_OK;
 }
 
 }  // extern "C"

@@ -169,15 +169,23 @@ ALGX_API int algx_head_finalize(const algx_head_config* cfg, const int32_t* targ
                                 float* stat, float* telemetry, float* objective, float* count,
                                 void* stream);
 
+/* Workspace bytes of algx_head_bwd: one bf16 dz slab of N x min(4096, V
+ * rounded up to 256) plus, when dh is bf16, an fp32 dh accumulator. */
+ALGX_API size_t algx_head_bwd_workspace_size(int64_t N, int64_t d, int64_t V, int32_t dh_dtype);
+
 /* dh (N, d) in dh_dtype (partial over this rank's vocabulary rows) and
  * dembed (V, d) fp32, with scale = g * slope / count read from device
- * memory. Recomputes logit tiles; dz never reaches HBM. Replaces
- * kernels/fused_head.py:120-156, 194-216 (`_bwd_kernel`, `_backward`,
- * including the XLA dE = dz^T h product). */
+ * memory. The logits are recomputed one vocabulary slab of at most 4096
+ * columns at a time (never in full): a tcgen05 kernel writes the slab's
+ * bf16 dz = scale * (softmax - y) or scale * (p - y) r into the workspace,
+ * then cuBLAS computes dh += dz . E_slab and dE_slab = dz^T . h (fp32
+ * accumulation). Replaces kernels/fused_head.py:120-156, 194-216
+ * (`_bwd_kernel`, `_backward`, including the XLA dE = dz^T h product). */
 ALGX_API int algx_head_bwd(const algx_head_config* cfg, const void* h, const void* embed,
                            const int32_t* targets, const float* stat, const float* scale, void* dh,
                            int32_t dh_dtype, float* dembed, int64_t N, int64_t d, int64_t V,
-                           int64_t vocab_offset, int32_t dtype, void* stream);
+                           int64_t vocab_offset, int32_t dtype, void* workspace, size_t workspace_bytes,
+                           void* stream);
 
 /* --------------------------------------------------------------- diagnostics */
 
