@@ -41,7 +41,8 @@ constexpr int kFwdNT = 256;     // vocabulary columns per tile
 constexpr int kFwdStages = 4;
 constexpr int kFwdStageBytes = kChunkBytes + kFwdNT * 64 * 2;  // h chunk + E chunk
 constexpr int kFwdSmem = kFwdStages * kFwdStageBytes + 1024;
-constexpr int kHeadThreads = 192;
+constexpr int kHeadThreads = 320;  // 2 x 4 epilogue warps, TMA warp, MMA warp
+constexpr int kHeadTma = 8;
 
 __device__ __forceinline__ uint8_t* align1k(uint8_t* p) {
   return reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p) + 1023) & ~uintptr_t(1023));
@@ -64,7 +65,8 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
                        int* dev_err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1k(smem_raw);
-  __shared__ uint64_t full[kFwdStages], empty[kFwdStages], acc_full[2], acc_empty[2];
+  __shared__ uint64_t full[kFwdStages], empty[kFwdStages], acc_full[2], acc_empty[2], x_ready;
+  __shared__ float xm[kRowsT], xl[kRowsT], xz[kRowsT];  // statistics of epilogue group 1
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
   volatile int* abort_v = &abort_flag;
@@ -84,10 +86,11 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], 4);
     }
+    mbar_init(&x_ready, 4);
     fence_mbar_init();
     abort_flag = 0;
   }
-  if (warp == 4) {
+  if (warp == kHeadTma) {
     tmem_alloc(&tmem_base, 512);
     tmem_relinquish();
   }
@@ -95,7 +98,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
   __syncthreads();
   tc_fence_after();
 
-  if (warp == 4) {
+  if (warp == kHeadTma) {
     if (lane == 0 && t0 < t1) {
       prefetch_tmap(&th);
       prefetch_tmap(&te);
@@ -118,7 +121,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
             mbar_wait(&full[s], (last_stage_it[s] / kFwdStages) & 1, &quiet, nullptr);
           }
     }
-  } else if (warp == 5) {
+  } else if (warp == kHeadTma + 1) {
     if (lane == 0 && t0 < t1) {
       const uint32_t id = idesc_bf16_f32(128, kFwdNT, 0, 0);
       const uint32_t s0 = smem_u32(smem);
@@ -146,16 +149,18 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
       }
     }
   } else {
-    // epilogue: thread r owns token tb*128 + r
-    const int r = threadIdx.x;
+    // epilogue: two groups of four warps take alternate tiles (group g owns
+    // accumulator buffer g); thread r of a group owns token tb*128 + r
+    const int g = warp >> 2;
+    const int r = (warp & 3) * 32 + lane;
     const int tok = tb * kRowsT + r;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const int tgt = tok < a.N ? a.targets[tok] : -2147483647 - 1;
     const int tloc = tgt - a.voff;  // local column of the target, may be out of range
     float m = -1e30f, l = 0.f, zt = 0.f;
     const float log2e = 1.4426950408889634f;
-    for (int t = t0; t < t1; ++t) {
-      const int buf = (t - t0) & 1, use = (t - t0) >> 1;
+    for (int t = t0 + g; t < t1; t += 2) {
+      const int buf = g, use = (t - t0) >> 1;
       if (!mbar_wait_warp(&acc_full[buf], use & 1, abort_v, dev_err)) break;
       tc_fence_after();
       const uint32_t acc = tmem_base + buf * kFwdNT + lane_off;
@@ -203,7 +208,23 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
-    if (tok < a.N) {
+    // group 1 hands its statistics to group 0, which merges and writes them
+    if (g == 1) {
+      xm[r] = m;
+      xl[r] = l;
+      xz[r] = zt;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&x_ready);  // release: the row statistics are visible to group 0
+    } else if (mbar_wait_warp(&x_ready, 0, abort_v, dev_err) && tok < a.N) {
+      const float m1 = xm[r], l1 = xl[r];
+      if constexpr (KIND == ALGX_HEAD_CE) {
+        const float mm = fmaxf(m, m1);
+        l = l * exp2f((m - mm) * log2e) + l1 * exp2f((m1 - mm) * log2e);
+        m = mm;
+      } else {
+        l += l1;
+      }
+      zt += xz[r];
       const size_t o = (size_t)split * a.N + tok;
       part_m[o] = m;
       part_l[o] = l;
@@ -212,7 +233,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) tmem_dealloc(tmem_base, 512);
+  if (warp == kHeadTma) tmem_dealloc(tmem_base, 512);
 }
 
 // ------------------------------------------------------------------ backward
@@ -261,7 +282,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
     fence_mbar_init();
     abort_flag = 0;
   }
-  if (warp == 4) {
+  if (warp == kHeadTma) {
     tmem_alloc(&tmem_base, 512);
     tmem_relinquish();
   }
@@ -269,7 +290,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
   __syncthreads();
   tc_fence_after();
 
-  if (warp == 4) {
+  if (warp == kHeadTma) {
     if (lane == 0 && t0 < t1) {
       prefetch_tmap(&th);
       prefetch_tmap(&te);
@@ -292,7 +313,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
             mbar_wait(&full[s], (last_stage_it[s] / kFwdStages) & 1, &quiet, nullptr);
           }
     }
-  } else if (warp == 5) {
+  } else if (warp == kHeadTma + 1) {
     if (lane == 0 && t0 < t1) {
       const uint32_t id = idesc_bf16_f32(128, kFwdNT, 0, 0);
       const uint32_t s0 = smem_u32(smem);
@@ -320,10 +341,12 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
       }
     }
   } else {
-    // epilogue: thread r owns token tb*128 + r
-    const int r = threadIdx.x;
+    // epilogue: two groups of four warps take alternate tiles (group g owns
+    // accumulator buffer g); thread r of a group owns token tb*128 + r
+    const int g = warp >> 2;
+    const int r = (warp & 3) * 32 + lane;
     const int tok = tb * kRowsT + r;
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const algx_head_config& c = a.cfg;
     const int tgt = tok < a.N ? a.targets[tok] : -2147483647 - 1;
     const bool row_ok = tok < a.N && !(c.has_ignore && tgt == c.ignore_index);
@@ -333,8 +356,8 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
     const float log2e = 1.4426950408889634f;
     const float stl = st * log2e;
     __nv_bfloat16* drow = dz + (size_t)tok * a.ldz - (size_t)a.tile0 * kFwdNT;
-    for (int t = t0; t < t1; ++t) {
-      const int buf = (t - t0) & 1, use = (t - t0) >> 1;
+    for (int t = t0 + g; t < t1; t += 2) {
+      const int buf = g, use = (t - t0) >> 1;
       if (!mbar_wait_warp(&acc_full[buf], use & 1, abort_v, dev_err)) break;
       tc_fence_after();
       const uint32_t acc = tmem_base + buf * kFwdNT + lane_off;
@@ -378,7 +401,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) tmem_dealloc(tmem_base, 512);
+  if (warp == kHeadTma) tmem_dealloc(tmem_base, 512);
 }
 
 __global__ void f32_to_bf16_kernel(const float4* __restrict__ in, uint2* __restrict__ out, int64_t n4) {
