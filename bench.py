@@ -38,6 +38,8 @@ STEP_FLOP = 3.5 * FWD_FLOP                    # forward + backward
 BWD_FLOP = 2.5 * FWD_FLOP                     # the backward launch group alone
 WORKLOAD = ("BASELINE config 2: QK-norm(q,k) -> causal asinh-power flash attention (n=16, c=8, "
             "range guard) fwd+bwd, B=8 H=12 S=2048 D=64 bf16, fp32 accumulation")
+# BASELINE config 3 (and the 350M shapes of config 4): fused LM head + likelihood
+HEAD_N, HEAD_V = 16384, 50304
 
 
 def _peaks():
@@ -190,6 +192,84 @@ def run_reference(args, rank):
     print(json.dumps(line), flush=True)
 
 
+def time_cuda(fn, steps, warmup, stream, sync_all, max_over_ranks):
+    """ms per call of ``fn`` over ``steps`` calls after ``warmup`` calls (CUDA events, max over ranks)."""
+    for _ in range(warmup):
+        fn()
+    sync_all()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(steps):
+        fn()
+    b.record(stream)
+    sync_all()
+    return max_over_ranks(a.elapsed_time(b)) / steps
+
+
+def secondary(dev, rank, world, stream, sync_all, max_over_ranks, steps=5, warmup=3):
+    """The other BASELINE lines: fused head tok/s (config 3, ce and alg_ce n=8 c=2;
+    vocabulary-parallel over the ranks when N > 1) and the 350M shapes (config 4)."""
+    from algx.kernels.flash import build_config, flash_attention, make_variant
+    from algx.kernels.fused_head import fused_head
+    from algx.kernels.qk_norm import qk_rms_norm
+    from algx.parallel import shard_rows, vocab_parallel_fused_head
+
+    out = {}
+    gen = torch.Generator(device=dev).manual_seed(4321 + rank)
+
+    def head_line(d, kind, n, c):
+        h = torch.randn((HEAD_N, d), device=dev, generator=gen).to(torch.bfloat16)
+        torch.distributed.broadcast(h, 0) if world > 1 else None
+        lo, hi = shard_rows(HEAD_V, world, rank)
+        e = (0.02 * torch.randn((hi - lo, d), device=dev, generator=gen)).to(torch.bfloat16)
+        t = torch.randint(0, HEAD_V, (HEAD_N,), device=dev, generator=torch.Generator(device=dev).manual_seed(99))
+        t[torch.rand(HEAD_N, device=dev, generator=torch.Generator(device=dev).manual_seed(98)) < 0.05] = -100
+        hh = h.requires_grad_(True)
+        ee = e.requires_grad_(True)
+
+        def step():
+            if world > 1:
+                obj, _ = vocab_parallel_fused_head(hh, ee, t, vocab_offset=lo, vocab_total=HEAD_V, kind=kind, n=n,
+                                                   c=c, ignore_index=-100)
+            else:
+                obj, _ = fused_head(hh, ee, t, kind=kind, n=n, c=c, ignore_index=-100)
+            obj.backward()
+            hh.grad = None
+            ee.grad = None
+
+        ms = time_cuda(step, steps, warmup, stream, sync_all, max_over_ranks)
+        flop = 3 * 2 * HEAD_N * d * HEAD_V  # bench_head.py:36 convention (recompute excluded)
+        return {"metric": "fused CE head tok/s", "value": HEAD_N / (ms / 1e3), "unit": "tok/s",
+                "ms_per_step": ms, "tflops_3gemm": flop / (ms / 1e3) / 1e12, "kind": kind, "n": n, "c": c,
+                "config": f"N={HEAD_N} d={d} V={HEAD_V} bf16, 5% labels = ignore_index -100, fwd+bwd",
+                "scaling": "strong (vocabulary rows split over the ranks)" if world > 1 else "single GPU"}
+
+    out["head_cfg3_ce"] = head_line(768, "ce", 16, 16.0)
+    out["head_cfg3_alg_ce"] = head_line(768, "alg_ce", 8, 2.0)
+    out["head_cfg4_ce"] = head_line(1024, "ce", 16, 16.0)
+    # config 4 attention: B=8, H=16 per GPU (weak scaling like config 2)
+    B4, H4 = 8, 16
+    q, k, v, do = (torch.randn((B4, H4, T, D), device=dev, generator=gen).to(torch.bfloat16) for _ in range(4))
+    gq = 1 + 0.02 * torch.randn(D, device=dev, generator=gen)
+    gk = 1 + 0.02 * torch.randn(D, device=dev, generator=gen)
+    leaves = [x.requires_grad_(True) for x in (q, k, v, gq, gk)]
+
+    def attn_step():
+        o = flash_attention(qk_rms_norm(leaves[0], leaves[3], EPS), qk_rms_norm(leaves[1], leaves[4], EPS),
+                            leaves[2], kind="asinh", n=N_POW, c=C_SCALE, range_guard=True)
+        o.backward(do)
+        for x in leaves:
+            x.grad = None
+
+    ms = time_cuda(attn_step, steps, warmup, stream, sync_all, max_over_ranks)
+    flop = 3.5 * 4 * B4 * H4 * T * T * D / 2
+    out["attn_cfg4"] = {"metric": "asinh-attn fwd+bwd TFLOP/s", "value": world * flop / (ms / 1e3) / 1e12,
+                        "unit": "TFLOP/s", "ms_per_step": ms,
+                        "config": f"B={B4} H={H4} S={T} D={D} bf16 per GPU, QK-norm + guarded asinh n=16 c=8, "
+                                  "public API (autograd)", "scaling": "weak"}
+    return out
+
+
 def run_algx(args, rank, world, local_rank):
     import torch.distributed as dist
 
@@ -325,6 +405,7 @@ def run_algx(args, rank, world, local_rank):
     if clocks:
         clocks.mark(w2, w3)
     e2e_ms = max_over_ranks(ev2.elapsed_time(ev3))
+    extra = secondary(dev, rank, world, stream, sync_all, max_over_ranks) if not args.no_secondary else None
     dev_err = L.device_error()
     clk = clocks.stop() if clocks else None
 
@@ -354,6 +435,7 @@ def run_algx(args, rank, world, local_rank):
                      "algorithmic": "2.5 x 4*B*H*T^2*D/2 FLOP per launch", "ms_per_launch": bwd_ms,
                      "peak_source": f"{peak_src} bf16 dense (burst)"},
         "gpu_launches": int(launches),
+        "secondary": extra,
         "device_error": dev_err,
         "clocks": clk,
     }
@@ -369,6 +451,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["algx", "reference"], default="algx")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true", help="skip the head and config 4 lines")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
