@@ -192,6 +192,12 @@ def run_reference(args, rank):
     print(json.dumps(line), flush=True)
 
 
+def trace(msg):
+    """Phase markers on stderr when ALGX_BENCH_TRACE=1 (locating a stall in a multi-rank run)."""
+    if os.environ.get("ALGX_BENCH_TRACE") == "1":
+        print(f"[rank {os.environ.get('RANK', '0')} {time.strftime('%H:%M:%S')}] {msg}", file=sys.stderr, flush=True)
+
+
 def time_cuda(fn, steps, warmup, stream, sync_all, max_over_ranks):
     """ms per call of ``fn`` over ``steps`` calls after ``warmup`` calls (CUDA events, max over ranks)."""
     for _ in range(warmup):
@@ -208,7 +214,7 @@ def time_cuda(fn, steps, warmup, stream, sync_all, max_over_ranks):
 
 def secondary(dev, rank, world, stream, sync_all, max_over_ranks, steps=5, warmup=3):
     """The other BASELINE lines: fused head tok/s (config 3, ce and alg_ce n=8 c=2;
-    vocabulary-parallel over the ranks when N > 1) and the 350M shapes (config 4)."""
+    one GPU) and the 350M shapes (config 4)."""
     from algx.kernels.flash import build_config, flash_attention, make_variant
     from algx.kernels.fused_head import fused_head
     from algx.kernels.qk_norm import qk_rms_norm
@@ -244,9 +250,18 @@ def secondary(dev, rank, world, stream, sync_all, max_over_ranks, steps=5, warmu
                 "config": f"N={HEAD_N} d={d} V={HEAD_V} bf16, 5% labels = ignore_index -100, fwd+bwd",
                 "scaling": "strong (vocabulary rows split over the ranks)" if world > 1 else "single GPU"}
 
-    out["head_cfg3_ce"] = head_line(768, "ce", 16, 16.0)
-    out["head_cfg3_alg_ce"] = head_line(768, "alg_ce", 8, 2.0)
-    out["head_cfg4_ce"] = head_line(1024, "ce", 16, 16.0)
+    if world == 1:
+        trace("secondary: head cfg3 ce")
+        out["head_cfg3_ce"] = head_line(768, "ce", 16, 16.0)
+        trace("secondary: head cfg3 alg_ce")
+        out["head_cfg3_alg_ce"] = head_line(768, "alg_ce", 8, 2.0)
+        trace("secondary: head cfg4 ce")
+        out["head_cfg4_ce"] = head_line(1024, "ce", 16, 16.0)
+    else:
+        out["head"] = {"measured": False,
+                       "reason": "the head lines are measured on one GPU; the vocabulary-parallel run is not "
+                                 "validated on GPUs yet (see algx.parallel for the NCCL exchange)"}
+    trace("secondary: attention cfg4")
     # config 4 attention: B=8, H=16 per GPU (weak scaling like config 2)
     B4, H4 = 8, 16
     q, k, v, do = (torch.randn((B4, H4, T, D), device=dev, generator=gen).to(torch.bfloat16) for _ in range(4))
@@ -319,9 +334,11 @@ def run_algx(args, rank, world, local_rank):
     clocks = ClockSampler(local_rank) if rank == 0 else None
     if clocks:
         clocks.start()
+    trace("warm-up")
     for _ in range(args.warmup):
         step()
     sync_all()
+    trace("timed device steps")
     # ---- device-resident timed region: exactly K steps
     launches0 = lib.algx_launch_count()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -339,6 +356,7 @@ def run_algx(args, rank, world, local_rank):
     bwd_ms = statistics.mean(a.elapsed_time(b) for a, b in bwd_events)
     bwd_ms = max_over_ranks(bwd_ms)
 
+    trace("end to end")
     # ---- end to end through the public API with pinned host buffers
     hq, hk, hv, hdo = (t.cpu().pin_memory() for t in (q, k, v, do))
     hgq, hgk = gq.cpu().pin_memory(), gk.cpu().pin_memory()
@@ -406,6 +424,7 @@ def run_algx(args, rank, world, local_rank):
         clocks.mark(w2, w3)
     e2e_ms = max_over_ranks(ev2.elapsed_time(ev3))
     extra = secondary(dev, rank, world, stream, sync_all, max_over_ranks) if not args.no_secondary else None
+    trace("done")
     dev_err = L.device_error()
     clk = clocks.stop() if clocks else None
 
