@@ -70,6 +70,8 @@ SIGNATURES = {
     "algx_qknorm_bwd_noalloc": ([_P, _P, _P, _P, _P, _I64, _I64, _I32, _F, _P], ctypes.c_int),
     "algx_attn_prepare": ([ctypes.POINTER(AttnConfig), _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _P],
                           ctypes.c_int),
+    "algx_qknorm_attn_prepare": ([ctypes.POINTER(AttnConfig), _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64,
+                                  _I64, _I32, _F, _P], ctypes.c_int),
     "algx_attn_fwd": ([ctypes.POINTER(AttnConfig), _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _P],
                       ctypes.c_int),
     "algx_attn_bwd_workspace_size": ([_I64, _I64, _I64, _I64], _SZ),

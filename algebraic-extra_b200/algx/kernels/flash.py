@@ -21,6 +21,7 @@ from typing import Optional
 import torch
 
 from .. import _lib as L
+from .qk_norm import qknorm_backward
 
 
 def _root(value: float, n: int) -> float:
@@ -69,13 +70,37 @@ def make_variant(kind: str, n: int = 16, c: float = 16.0, seq_len: int = 2048,
 def attn_forward(q, k, v, sink, cfg: L.AttnConfig):
     """Forward launch group (prepare + forward); returns (o, saved residuals)."""
     B, H, T, D = q.shape
-    dt = L.dtype_code(q.dtype)
-    st = L.stream_of(q)
     q_s = torch.empty_like(q)
     guard = torch.empty(4, dtype=torch.float32, device=q.device)
     sp = sink.data_ptr() if sink is not None else None
     L.check(L.lib().algx_attn_prepare(cfg, q.data_ptr(), k.data_ptr(), v.data_ptr(), sp, q_s.data_ptr(),
-                                      guard.data_ptr(), B, H, T, D, dt, st), "algx_attn_prepare")
+                                      guard.data_ptr(), B, H, T, D, L.dtype_code(q.dtype), L.stream_of(q)),
+            "algx_attn_prepare")
+    return _attn_forward_prepared(q_s, k, v, sink, guard, cfg)
+
+
+def attn_forward_qknorm(q, k, v, gain_q, gain_k, sink, cfg: L.AttnConfig, eps: float):
+    """Forward launch group with the fused QK-norm prologue: attention of
+    (rms_norm(q) * gain_q, rms_norm(k) * gain_k, v) with the QK norm, the
+    scale fold and the guard maxima in one launch; returns (o, saved)."""
+    B, H, T, D = q.shape
+    q_s = torch.empty_like(q)
+    k_n = torch.empty_like(k)
+    guard = torch.empty(4, dtype=torch.float32, device=q.device)
+    sp = sink.data_ptr() if sink is not None else None
+    L.check(L.lib().algx_qknorm_attn_prepare(cfg, q.data_ptr(), k.data_ptr(), v.data_ptr(), gain_q.data_ptr(),
+                                             gain_k.data_ptr(), sp, q_s.data_ptr(), k_n.data_ptr(),
+                                             guard.data_ptr(), B, H, T, D, L.dtype_code(q.dtype), float(eps),
+                                             L.stream_of(q)), "algx_qknorm_attn_prepare")
+    return _attn_forward_prepared(q_s, k_n, v, sink, guard, cfg)
+
+
+def _attn_forward_prepared(q_s, k, v, sink, guard, cfg: L.AttnConfig):
+    B, H, T, D = q_s.shape
+    q = q_s
+    dt = L.dtype_code(q.dtype)
+    st = L.stream_of(q)
+    sp = sink.data_ptr() if sink is not None else None
     o = torch.empty_like(q)
     stat = torch.empty((B, H, T), dtype=torch.float32, device=q.device)
     o_prec = None
@@ -186,6 +211,13 @@ def flash_attention(q, k, v, sink_logit=None, *, kind: str = "softmax",
                          "512-square public tiles, and compact statistics")
     if range_guard and kind == "asinh" and n <= 32 and poly_rho:
         raise ValueError("range_guard is for exact radical evaluation")
+    cfg, sink = _checked_call(q, k, v, sink_logit, kind, var, c, range_guard)
+    return _Flash.apply(q.contiguous(), k.contiguous(), v.contiguous(), sink, cfg)
+
+
+def _checked_call(q, k, v, sink_logit, kind, var, c, range_guard):
+    """Shape / dtype / device checks shared by the public entry points; (cfg, sink)."""
+    B, H, T, D = q.shape
     if D != 64:
         raise ValueError(f"algx attention supports head_dim 64, got {D}")
     if not (q.dtype == k.dtype == v.dtype) or q.dtype not in (torch.bfloat16, torch.float32):
@@ -199,5 +231,46 @@ def flash_attention(q, k, v, sink_logit=None, *, kind: str = "softmax",
     if has_sink:
         s_in = torch.as_tensor(sink_logit, dtype=torch.float32, device=q.device)
         sink = (torch.broadcast_to(torch.reshape(s_in, (-1,)), (H,)) / unit).contiguous()
-    cfg = build_config(kind, var, T, D, c, has_sink, range_guard)
-    return _Flash.apply(q.contiguous(), k.contiguous(), v.contiguous(), sink, cfg)
+    return build_config(kind, var, T, D, c, has_sink, range_guard), sink
+
+
+class _QKNormFlash(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, gain_q, gain_k, sink, cfg: L.AttnConfig, eps: float):
+        o, saved = attn_forward_qknorm(q, k, v, gain_q, gain_k, sink, cfg, eps)
+        ctx.cfg, ctx.eps = cfg, eps
+        ctx.save_for_backward(q, k, gain_q, gain_k, *saved)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, gain_q, gain_k, *saved = ctx.saved_tensors
+        dq, dk, dv, dsink = attn_backward(saved, ctx.cfg, do)
+        dxq, dgq = qknorm_backward(q, gain_q, dq, ctx.eps)
+        dxk, dgk = qknorm_backward(k, gain_k, dk, ctx.eps)
+        return dxq, dxk, dv, dgq, dgk, dsink, None, None
+
+
+def qknorm_flash_attention(q, k, v, gain_q, gain_k, sink_logit=None, *, eps: float = 1e-5,
+                           kind: str = "asinh", n: int = 16, c: float = 16.0, block: int = 512,
+                           range_guard: bool = False, shift: Optional[bool] = None,
+                           fast_rho: Optional[bool] = None, inv_stat: Optional[bool] = None):
+    """``flash_attention(qk_rms_norm(q, gain_q, eps), qk_rms_norm(k, gain_k, eps), v, sink_logit, ...)``
+    with the QK norm, the scale fold and the range-guard maxima fused into one
+    prologue launch (model.py:170-174; no rotary in between). Same values and
+    gradients (q, k, v, both gains and the sink) as the two calls composed;
+    the reference has no fused entry of this kind.
+    """
+    B, H, T, D = q.shape
+    bq = min(block, T)
+    if T % bq:
+        raise ValueError(f"sequence length {T} must be divisible by blocks ({bq}, {bq})")
+    if eps <= 0:
+        raise ValueError("eps must be positive")
+    var = make_variant(kind, n, c, T, shift, fast_rho, inv_stat, True, False)
+    cfg, sink = _checked_call(q, k, v, sink_logit, kind, var, c, range_guard)
+    gq = gain_q.to(device=q.device, dtype=torch.float32).contiguous()
+    gk = gain_k.to(device=q.device, dtype=torch.float32).contiguous()
+    if gq.shape != (64,) or gk.shape != (64,):
+        raise ValueError("gains must have shape (64,)")
+    return _QKNormFlash.apply(q.contiguous(), k.contiguous(), v.contiguous(), gq, gk, sink, cfg, float(eps))

@@ -81,6 +81,87 @@ __global__ void __launch_bounds__(kPrepThreads) attn_prepare_kernel(const T* __r
   }
 }
 
+// Fused attention prologue (model.py:170-174 then flash.py:823-849): the QK
+// RMS norm of q and k (qk_norm.py:29-43, algebraic.py:76-83) and the prepare
+// step above in one pass over q, k and v. Each value goes through the same
+// rounding points as the separate launches: y = bf16((x * tau) * gain), then
+// q_scaled = bf16(y * scale); the guard maxima are taken over the rounded
+// q_scaled and normalised k rows, and over v and the sink as in prepare.
+template <typename T>
+__global__ void __launch_bounds__(kPrepThreads) qknorm_attn_prepare_kernel(
+    const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v, const float* __restrict__ gain_q,
+    const float* __restrict__ gain_k, const float* __restrict__ sink, int H, T* __restrict__ qs,
+    T* __restrict__ kn, float* guard, int64_t rows, float scale, float eps) {
+  using V = Vec<T>;
+  constexpr int kUnroll = 4;
+  const int which = blockIdx.y;  // 0: q (normalised, scaled, written), 1: k (normalised, written), 2: v
+  const T* src = which == 0 ? q : (which == 1 ? k : v);
+  T* dst = which == 0 ? qs : kn;
+  const float* gain = which == 0 ? gain_q : gain_k;
+  const int lane = threadIdx.x & 31;
+  const int sub = lane % V::TPR;
+  const int rl = lane / V::TPR;
+  float g[V::N];
+#pragma unroll
+  for (int i = 0; i < V::N; ++i) g[i] = which == 2 ? 0.f : gain[sub * V::N + i];
+  const int64_t warps = (int64_t)gridDim.x * (kPrepThreads / 32);
+  const int64_t w = (int64_t)blockIdx.x * (kPrepThreads / 32) + (threadIdx.x >> 5);
+  float local = 0.f;
+  for (int64_t r0 = w * V::RPW * kUnroll; r0 < rows; r0 += warps * V::RPW * kUnroll) {
+    uint4 raw[kUnroll];
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t row = r0 + u * V::RPW + rl;
+      raw[u] = row < rows ? ld_stream(src + row * kD + sub * V::N) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < kUnroll; ++u) {
+      const int64_t row = r0 + u * V::RPW + rl;
+      const bool ok = row < rows;
+      float x[V::N];
+      unpack<T>(raw[u], x);
+      if (which == 2) {
+#pragma unroll
+        for (int i = 0; i < V::N; ++i) local = nan_max(local, fabsf(x[i]));
+        continue;
+      }
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < V::N; ++i) ss = fmaf(x[i], x[i], ss);
+      ss = row_sum<V::TPR>(ss);
+      const float tau = rsqrtf(ss * (1.0f / kD) + eps);
+#pragma unroll
+      for (int i = 0; i < V::N; ++i) x[i] = round_io<T>((x[i] * tau) * g[i]);
+      if (which == 0) {
+#pragma unroll
+        for (int i = 0; i < V::N; ++i) x[i] = round_io<T>(x[i] * scale);
+      }
+      if (ok) *reinterpret_cast<uint4*>(dst + row * kD + sub * V::N) = pack<T>(x);
+      float s2 = 0.f;
+#pragma unroll
+      for (int i = 0; i < V::N; ++i) s2 = fmaf(x[i], x[i], s2);
+      s2 = row_sum<V::TPR>(s2);
+      local = nan_max(local, s2);
+    }
+  }
+  __shared__ float red[kPrepThreads / 32];
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) local = nan_max(local, __shfl_xor_sync(0xffffffffu, local, off));
+  if (lane == 0) red[threadIdx.x >> 5] = local;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float m = 0.f;
+    for (int i = 0; i < kPrepThreads / 32; ++i) m = nan_max(m, red[i]);
+    atomic_max_nonneg(&guard[which], __int_as_float(__float_as_int(m) & 0x7fffffff));
+  }
+  if (which == 0 && blockIdx.x == 0 && sink != nullptr) {
+    for (int t = threadIdx.x; t < H; t += kPrepThreads) {
+      const float a = fabsf(sink[t]);
+      atomic_max_nonneg(&guard[3], __int_as_float(__float_as_int(a) & 0x7fffffff));
+    }
+  }
+}
+
 // ------------------------------------------------------------------ forward
 template <typename T>
 __device__ __forceinline__ void attn_fwd_generic_tile(algx_attn_config cfg, const T* __restrict__ q,
@@ -571,6 +652,33 @@ int algx_attn_prepare(const algx_attn_config* cfg, const void* q, const void* k,
                                                               sk, (int)H, (float*)q_scaled, guard, rows,
                                                               cfg->scale);
   ALGX_LAUNCHED("attn_prepare launch");
+  return ALGX_OK;
+}
+
+int algx_qknorm_attn_prepare(const algx_attn_config* cfg, const void* q, const void* k, const void* v,
+                             const float* gain_q, const float* gain_k, const float* sink, void* q_scaled,
+                             void* k_norm, float* guard, int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype,
+                             float eps, void* stream) {
+  if (int s = check_attn(cfg, B, H, T, D, dtype)) return s;
+  ALGX_REQUIRE(q && k && v && gain_q && gain_k && q_scaled && k_norm && guard, "qknorm_attn_prepare: NULL pointer");
+  ALGX_REQUIRE(!cfg->has_sink || sink, "qknorm_attn_prepare: has_sink without a sink pointer");
+  ALGX_REQUIRE(eps > 0.f, "qknorm_attn_prepare: eps must be positive");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  ALGX_CUDA(cudaMemsetAsync(guard, 0, 4 * sizeof(float), st));
+  const int64_t rows = B * H * T;
+  const int64_t rows_per_block = (kPrepThreads / 32) * (dtype == ALGX_BF16 ? 4 : 2) * 4;
+  const int gx = (int)std::min<int64_t>((rows + rows_per_block - 1) / rows_per_block, 148 * 8);
+  dim3 grid(gx, 3);
+  const float* sk = cfg->has_sink ? sink : nullptr;
+  if (dtype == ALGX_BF16)
+    qknorm_attn_prepare_kernel<__nv_bfloat16><<<grid, kPrepThreads, 0, st>>>(
+        (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, gain_q, gain_k, sk, (int)H,
+        (__nv_bfloat16*)q_scaled, (__nv_bfloat16*)k_norm, guard, rows, cfg->scale, eps);
+  else
+    qknorm_attn_prepare_kernel<float><<<grid, kPrepThreads, 0, st>>>(
+        (const float*)q, (const float*)k, (const float*)v, gain_q, gain_k, sk, (int)H, (float*)q_scaled,
+        (float*)k_norm, guard, rows, cfg->scale, eps);
+  ALGX_LAUNCHED("qknorm_attn_prepare launch");
   return ALGX_OK;
 }
 

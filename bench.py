@@ -1,8 +1,9 @@
 #!/usr/bin/env python3
 """Hot-path benchmark: BASELINE config 2 (asinh-power attention + QK-norm, fwd+bwd).
 
-One step = QK-norm forward of q and k, guarded asinh-power causal flash
-attention forward (n=16, c=8), its backward, and the QK-norm backward, on
+One step = QK-norm forward of q and k fused into the attention prologue,
+guarded asinh-power causal flash attention forward (n=16, c=8), its
+backward, and the QK-norm backward, on
 B=8, H=12, S=2048, D=64 bf16 per GPU (weak scaling: every rank runs its own
 batch; no collective sits on the data path). FLOPs per step follow the
 reference's convention (scripts/bench_attention.py:50,65): 3.5 x 4*B*H*T^2*D/2.
@@ -215,9 +216,8 @@ def time_cuda(fn, steps, warmup, stream, sync_all, max_over_ranks):
 def secondary(dev, rank, world, stream, sync_all, max_over_ranks, steps=5, warmup=3):
     """The other BASELINE lines: fused head tok/s (config 3, ce and alg_ce n=8 c=2;
     one GPU) and the 350M shapes (config 4)."""
-    from algx.kernels.flash import build_config, flash_attention, make_variant
+    from algx.kernels.flash import qknorm_flash_attention
     from algx.kernels.fused_head import fused_head
-    from algx.kernels.qk_norm import qk_rms_norm
     from algx.parallel import shard_rows, vocab_parallel_fused_head
 
     out = {}
@@ -270,8 +270,8 @@ def secondary(dev, rank, world, stream, sync_all, max_over_ranks, steps=5, warmu
     leaves = [x.requires_grad_(True) for x in (q, k, v, gq, gk)]
 
     def attn_step():
-        o = flash_attention(qk_rms_norm(leaves[0], leaves[3], EPS), qk_rms_norm(leaves[1], leaves[4], EPS),
-                            leaves[2], kind="asinh", n=N_POW, c=C_SCALE, range_guard=True)
+        o = qknorm_flash_attention(leaves[0], leaves[1], leaves[2], leaves[3], leaves[4], eps=EPS, kind="asinh",
+                                   n=N_POW, c=C_SCALE, range_guard=True)
         o.backward(do)
         for x in leaves:
             x.grad = None
@@ -289,8 +289,9 @@ def run_algx(args, rank, world, local_rank):
     import torch.distributed as dist
 
     from algx import _lib as L
-    from algx.kernels.flash import attn_backward, attn_forward, build_config, flash_attention, make_variant
-    from algx.kernels.qk_norm import qk_rms_norm, qknorm_backward, qknorm_forward
+    from algx.kernels.flash import attn_backward, attn_forward_qknorm, build_config, make_variant, \
+        qknorm_flash_attention
+    from algx.kernels.qk_norm import qknorm_backward
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
@@ -306,9 +307,7 @@ def run_algx(args, rank, world, local_rank):
     bwd_events = []
 
     def step(record=False):
-        qn = qknorm_forward(q, gq, EPS)
-        kn = qknorm_forward(k, gk, EPS)
-        o, saved = attn_forward(qn, kn, v, None, cfg)
+        o, saved = attn_forward_qknorm(q, k, v, gq, gk, None, cfg, EPS)
         if record:
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
@@ -394,8 +393,8 @@ def run_algx(args, rank, world, local_rank):
                 upload(i + 1)
             qq, kk, vv, dd, g1, g2 = (t.detach().requires_grad_(t.is_floating_point()) if j != 3 else t
                                       for j, t in enumerate(slots[slot]))
-            o = flash_attention(qk_rms_norm(qq, g1, EPS), qk_rms_norm(kk, g2, EPS), vv, kind="asinh", n=N_POW,
-                                c=C_SCALE, range_guard=True)
+            o = qknorm_flash_attention(qq, kk, vv, g1, g2, eps=EPS, kind="asinh", n=N_POW, c=C_SCALE,
+                                       range_guard=True)
             o.backward(dd)
             in_free[slot].record(stream)
             results = (o.detach(), qq.grad, kk.grad, vv.grad, g1.grad, g2.grad)
@@ -446,8 +445,9 @@ def run_algx(args, rank, world, local_rank):
                          "exceeds the 126 MB L2"},
         "e2e": {"value": total_flop / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / args.steps,
-                "path": "qk_rms_norm -> flash_attention -> backward, pinned host buffers; uploads of step i+1 "
-                        "and downloads of step i overlap step i on two copy streams"},
+                "path": "qknorm_flash_attention (QK norm fused into the attention prologue) -> backward, pinned "
+                        "host buffers; uploads of step i+1 and downloads of step i overlap step i on two copy "
+                        "streams"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                      "frac": achieved / peak_tf, "traffic": _traffic(),
                      "kernel": "attention backward launch group (di, tcgen05 bwd, dq finish)",

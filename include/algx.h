@@ -108,6 +108,19 @@ ALGX_API int algx_attn_prepare(const algx_attn_config* cfg, const void* q, const
                       const float* sink, void* q_scaled, float* guard, int64_t B, int64_t H,
                       int64_t T, int64_t D, int32_t dtype, void* stream);
 
+/* Fused attention prologue: the QK RMS norm of q and k followed by
+ * algx_attn_prepare, in one pass. k_norm = round(rmsnorm(k) * gain_k) and
+ * q_scaled = round(round(rmsnorm(q) * gain_q) * scale) are bit-identical to
+ * algx_qknorm_fwd on q and k followed by algx_attn_prepare; guard as there.
+ * Replaces the model's qk-norm -> flash_attention prologue (model.py:170-174,
+ * qk_norm.py:29-43, flash.py:823-849); no rotary is applied (the attention
+ * block of BASELINE config 2 has none). */
+ALGX_API int algx_qknorm_attn_prepare(const algx_attn_config* cfg, const void* q, const void* k,
+                                      const void* v, const float* gain_q, const float* gain_k,
+                                      const float* sink, void* q_scaled, void* k_norm, float* guard,
+                                      int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype, float eps,
+                                      void* stream);
+
 /* Causal forward: o (I/O dtype), stat (B,H,T) fp32, and on the shifted
  * guard fallback the unrounded output o_precise (B,H,T,D) fp32 (nullable when
  * cfg->mode != GUARDED). Replaces kernels/flash.py:189-326 `_forward` and

@@ -228,3 +228,39 @@ def test_fast_path_shapes(T, n, c):
         if err >= .025:
             dump(f"fast_T{T}_n{n}_{name}", got=a, want=b)
         assert err < .025, (name, err)
+
+
+@pytest.mark.parametrize("dtype,with_sink", [(torch.bfloat16, False), (torch.bfloat16, True), (torch.float32, False)])
+def test_fused_qknorm_prologue_matches_composed(dtype, with_sink):
+    """qknorm_flash_attention == flash_attention(qk_rms_norm(q), qk_rms_norm(k), v) (model.py:170-174).
+
+    The fused prologue goes through the same rounding points, so the output is
+    bit-identical; gradients agree up to the order of the dQ reduce-adds.
+    """
+    from algx.kernels.flash import qknorm_flash_attention
+    from algx.kernels.qk_norm import qk_rms_norm
+    shape = (2, 3, 512, 64)
+    q, k, v, do = (_randn(40 + i, shape, dtype) for i in range(4))
+    gq0, gk0 = 1 + 0.02 * _randn(50, (64,)), 1 + 0.02 * _randn(51, (64,))
+    sink0 = _randn(52, (3,)) if with_sink else None
+
+    def run(fused):
+        leaves = [t.cuda().requires_grad_(True) for t in (q, k, v)]
+        gains = [g.cuda().requires_grad_(True) for g in (gq0, gk0)]
+        sink = sink0.cuda().requires_grad_(True) if with_sink else None
+        opts = dict(kind="asinh", n=16, c=8., range_guard=True)
+        if fused:
+            o = qknorm_flash_attention(*leaves, *gains, sink, eps=1e-5, **opts)
+        else:
+            o = flash_attention(qk_rms_norm(leaves[0], gains[0]), qk_rms_norm(leaves[1], gains[1]), leaves[2],
+                                sink, **opts)
+        torch.sum(o.float() * do.cuda().float()).backward()
+        grads = [t.grad for t in leaves + gains] + ([sink.grad] if with_sink else [])
+        return o.detach(), grads
+
+    o_f, g_f = run(True)
+    o_c, g_c = run(False)
+    assert torch.equal(o_f, o_c)
+    lim = 1e-2 if dtype == torch.bfloat16 else 1e-5
+    for a, b in zip(g_f, g_c):
+        assert rel_l2(a, b) < lim
