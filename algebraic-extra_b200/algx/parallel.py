@@ -78,6 +78,8 @@ def vocab_parallel_fused_head(h, embed_shard, targets, *, vocab_offset: int, voc
     """
     if kind not in ("ce", "alg_ce"):
         raise ValueError(kind)
+    if embed_shard.shape[0] < 1:
+        raise ValueError("every rank needs at least one vocabulary row (embed_shard is empty)")
     L.require_cuda(h, embed_shard, targets)
     cfg = FH.head_config(kind, n, c, vocab_total, ignore_index)
     slope = 1.0 if kind == "ce" else n / c

@@ -215,7 +215,7 @@ def time_cuda(fn, steps, warmup, stream, sync_all, max_over_ranks):
 
 def secondary(dev, rank, world, stream, sync_all, max_over_ranks, steps=5, warmup=3):
     """The other BASELINE lines: fused head tok/s (config 3, ce and alg_ce n=8 c=2;
-    one GPU) and the 350M shapes (config 4)."""
+    vocabulary-parallel over the ranks when N > 1) and the 350M shapes (config 4)."""
     from algx.kernels.flash import qknorm_flash_attention
     from algx.kernels.fused_head import fused_head
     from algx.parallel import shard_rows, vocab_parallel_fused_head
@@ -226,8 +226,8 @@ def secondary(dev, rank, world, stream, sync_all, max_over_ranks, steps=5, warmu
     def head_line(d, kind, n, c):
         h = torch.randn((HEAD_N, d), device=dev, generator=gen).to(torch.bfloat16)
         torch.distributed.broadcast(h, 0) if world > 1 else None
-        lo, hi = shard_rows(HEAD_V, world, rank)
-        e = (0.02 * torch.randn((hi - lo, d), device=dev, generator=gen)).to(torch.bfloat16)
+        lo, rows = shard_rows(HEAD_V, world, rank)  # (offset, count) of this rank's vocabulary rows
+        e = (0.02 * torch.randn((rows, d), device=dev, generator=gen)).to(torch.bfloat16)
         t = torch.randint(0, HEAD_V, (HEAD_N,), device=dev, generator=torch.Generator(device=dev).manual_seed(99))
         t[torch.rand(HEAD_N, device=dev, generator=torch.Generator(device=dev).manual_seed(98)) < 0.05] = -100
         hh = h.requires_grad_(True)
@@ -250,17 +250,12 @@ def secondary(dev, rank, world, stream, sync_all, max_over_ranks, steps=5, warmu
                 "config": f"N={HEAD_N} d={d} V={HEAD_V} bf16, 5% labels = ignore_index -100, fwd+bwd",
                 "scaling": "strong (vocabulary rows split over the ranks)" if world > 1 else "single GPU"}
 
-    if world == 1:
-        trace("secondary: head cfg3 ce")
-        out["head_cfg3_ce"] = head_line(768, "ce", 16, 16.0)
-        trace("secondary: head cfg3 alg_ce")
-        out["head_cfg3_alg_ce"] = head_line(768, "alg_ce", 8, 2.0)
-        trace("secondary: head cfg4 ce")
-        out["head_cfg4_ce"] = head_line(1024, "ce", 16, 16.0)
-    else:
-        out["head"] = {"measured": False,
-                       "reason": "the head lines are measured on one GPU; the vocabulary-parallel run is not "
-                                 "validated on GPUs yet (see algx.parallel for the NCCL exchange)"}
+    trace("secondary: head cfg3 ce")
+    out["head_cfg3_ce"] = head_line(768, "ce", 16, 16.0)
+    trace("secondary: head cfg3 alg_ce")
+    out["head_cfg3_alg_ce"] = head_line(768, "alg_ce", 8, 2.0)
+    trace("secondary: head cfg4 ce")
+    out["head_cfg4_ce"] = head_line(1024, "ce", 16, 16.0)
     trace("secondary: attention cfg4")
     # config 4 attention: B=8, H=16 per GPU (weak scaling like config 2)
     B4, H4 = 8, 16
@@ -464,6 +459,13 @@ def run_algx(args, rank, world, local_rank):
 
 
 def main():
+    # stdout carries the one JSON line and nothing else: native libraries that
+    # write to file descriptor 1 (NCCL prints its version banner there at
+    # communicator set-up) are sent to stderr, and Python's stdout keeps the
+    # original descriptor.
+    json_fd = os.dup(1)
+    os.dup2(2, 1)
+    sys.stdout = os.fdopen(json_fd, "w", buffering=1)
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
