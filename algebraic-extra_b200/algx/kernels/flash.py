@@ -146,30 +146,40 @@ class _Flash(torch.autograd.Function):
         return dq, dk, dv, dsink, None
 
 
+def config_lists(kind, var: Variant, T: int, D: int, c: float, has_sink: bool, range_guard: bool):
+    """The resolved variant and the wrapper constants (kernels/flash.py:823-856)
+    as plain scalars: ints ``[kind, mode, n, fast_rho, inv_stat, has_sink]`` and
+    floats ``[clamp, scale, guard_qk, guard_sink, guard_v]``."""
+    unit = 1.0 if kind == "softmax" else float(c)
+    guard_qk = guard_sink = guard_v = 0.0
+    if kind == "asinh" and range_guard and var["n"] <= 32:
+        bound = min(16.0, var["clamp"] / 2)
+        mode = L.ALGX_MODE_GUARDED
+        guard_qk = (bound / 1.01) ** 2
+        guard_sink = bound / 1.01
+        guard_v = min(1e8, 1e37 / ((T + int(has_sink)) * (2 * bound + 1) ** var["n"]))
+    elif kind == "asinh":
+        mode = L.ALGX_MODE_SHIFTED if var["shift"] else L.ALGX_MODE_CLIPPED
+    else:
+        mode = L.ALGX_MODE_SHIFTED
+    ints = [L.ALGX_ATTN_SOFTMAX if kind == "softmax" else L.ALGX_ATTN_ASINH, mode, int(var["n"]),
+            int(var["fast_rho"]), int(var["inv_stat"]), int(has_sink)]
+    floats = [float(var["clamp"]), 1.0 / (math.sqrt(D) * unit), guard_qk, guard_sink, guard_v]
+    return ints, floats
+
+
+def config_from_lists(ints, floats) -> L.AttnConfig:
+    """Pack :func:`config_lists` into the C ABI's ``AlgxAttnConfig``."""
+    cfg = L.AttnConfig()
+    cfg.kind, cfg.mode, cfg.n, cfg.fast_rho, cfg.inv_stat, cfg.has_sink = (int(i) for i in ints)
+    cfg.clamp, cfg.scale, cfg.guard_qk, cfg.guard_sink, cfg.guard_v = (float(f) for f in floats)
+    return cfg
+
+
 def build_config(kind, var: Variant, T: int, D: int, c: float, has_sink: bool,
                  range_guard: bool) -> L.AttnConfig:
     """Pack the resolved variant and the wrapper constants (kernels/flash.py:823-856)."""
-    cfg = L.AttnConfig()
-    unit = 1.0 if kind == "softmax" else float(c)
-    cfg.kind = L.ALGX_ATTN_SOFTMAX if kind == "softmax" else L.ALGX_ATTN_ASINH
-    cfg.n = int(var["n"])
-    cfg.fast_rho = int(var["fast_rho"])
-    cfg.inv_stat = int(var["inv_stat"])
-    cfg.has_sink = int(has_sink)
-    cfg.clamp = float(var["clamp"])
-    cfg.scale = 1.0 / (math.sqrt(D) * unit)
-    cfg.guard_qk = cfg.guard_sink = cfg.guard_v = 0.0
-    if kind == "asinh" and range_guard and var["n"] <= 32:
-        bound = min(16.0, var["clamp"] / 2)
-        cfg.mode = L.ALGX_MODE_GUARDED
-        cfg.guard_qk = (bound / 1.01) ** 2
-        cfg.guard_sink = bound / 1.01
-        cfg.guard_v = min(1e8, 1e37 / ((T + int(has_sink)) * (2 * bound + 1) ** var["n"]))
-    elif kind == "asinh":
-        cfg.mode = L.ALGX_MODE_SHIFTED if var["shift"] else L.ALGX_MODE_CLIPPED
-    else:
-        cfg.mode = L.ALGX_MODE_SHIFTED
-    return cfg
+    return config_from_lists(*config_lists(kind, var, T, D, c, has_sink, range_guard))
 
 
 def flash_attention(q, k, v, sink_logit=None, *, kind: str = "softmax",
@@ -215,8 +225,9 @@ def flash_attention(q, k, v, sink_logit=None, *, kind: str = "softmax",
     return _Flash.apply(q.contiguous(), k.contiguous(), v.contiguous(), sink, cfg)
 
 
-def _checked_call(q, k, v, sink_logit, kind, var, c, range_guard):
-    """Shape / dtype / device checks shared by the public entry points; (cfg, sink)."""
+def check_inputs(q, k, v, sink_logit, kind, c):
+    """Shape / dtype / device checks shared by the public entry points; returns
+    the sink logits divided by the score unit, broadcast to (H,), or None."""
     B, H, T, D = q.shape
     if D != 64:
         raise ValueError(f"algx attention supports head_dim 64, got {D}")
@@ -225,13 +236,18 @@ def _checked_call(q, k, v, sink_logit, kind, var, c, range_guard):
     if k.shape != q.shape or v.shape != q.shape:
         raise ValueError("q, k, v must have the same (B, H, T, D) shape")
     L.require_cuda(q, k, v)
+    if sink_logit is None:
+        return None
     unit = 1.0 if kind == "softmax" else float(c)
-    has_sink = sink_logit is not None
-    sink = None
-    if has_sink:
-        s_in = torch.as_tensor(sink_logit, dtype=torch.float32, device=q.device)
-        sink = (torch.broadcast_to(torch.reshape(s_in, (-1,)), (H,)) / unit).contiguous()
-    return build_config(kind, var, T, D, c, has_sink, range_guard), sink
+    s_in = torch.as_tensor(sink_logit, dtype=torch.float32, device=q.device)
+    return (torch.broadcast_to(torch.reshape(s_in, (-1,)), (H,)) / unit).contiguous()
+
+
+def _checked_call(q, k, v, sink_logit, kind, var, c, range_guard):
+    """:func:`check_inputs` plus the packed configuration; (cfg, sink)."""
+    sink = check_inputs(q, k, v, sink_logit, kind, c)
+    B, H, T, D = q.shape
+    return build_config(kind, var, T, D, c, sink is not None, range_guard), sink
 
 
 class _QKNormFlash(torch.autograd.Function):

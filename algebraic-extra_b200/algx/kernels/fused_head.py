@@ -35,15 +35,26 @@ def _root(value: float, n: int) -> float:
     return out
 
 
-def head_config(kind: str, n: int, c: float, vocab: int, ignore_index=None) -> L.HeadConfig:
+def head_config_lists(kind: str, n: int, c: float, vocab: int, ignore_index=None):
+    """The objective's constants as plain scalars: ints ``[kind, n, has_ignore,
+    ignore_index]`` and floats ``[inv_c, clamp]``."""
+    ints = [L.ALGX_HEAD_CE if kind == "ce" else L.ALGX_HEAD_ALG_CE, int(n), int(ignore_index is not None),
+            int(ignore_index) if ignore_index is not None else 0]
+    floats = [1.0 / float(c) if kind == "alg_ce" else 1.0,
+              0.25 * _root(1e38 / vocab, n) if kind == "alg_ce" else 0.0]
+    return ints, floats
+
+
+def head_config_from_lists(ints, floats) -> L.HeadConfig:
+    """Pack :func:`head_config_lists` into the C ABI's ``AlgxHeadConfig``."""
     cfg = L.HeadConfig()
-    cfg.kind = L.ALGX_HEAD_CE if kind == "ce" else L.ALGX_HEAD_ALG_CE
-    cfg.n = int(n)
-    cfg.inv_c = 1.0 / float(c) if kind == "alg_ce" else 1.0
-    cfg.clamp = 0.25 * _root(1e38 / vocab, n) if kind == "alg_ce" else 0.0
-    cfg.has_ignore = int(ignore_index is not None)
-    cfg.ignore_index = int(ignore_index) if ignore_index is not None else 0
+    cfg.kind, cfg.n, cfg.has_ignore, cfg.ignore_index = (int(i) for i in ints)
+    cfg.inv_c, cfg.clamp = (float(f) for f in floats[:2])
     return cfg
+
+
+def head_config(kind: str, n: int, c: float, vocab: int, ignore_index=None) -> L.HeadConfig:
+    return head_config_from_lists(*head_config_lists(kind, n, c, vocab, ignore_index))
 
 
 def head_forward_partials(h16, e16, t32, cfg, vocab_offset=0):
@@ -66,13 +77,15 @@ def head_forward_partials(h16, e16, t32, cfg, vocab_offset=0):
 def head_finalize(cfg, t32, mlz, vocab_total):
     """(stat, telemetry, objective[1], count[1]) from combined statistics."""
     N = t32.shape[0]
-    out = torch.empty((2, N), dtype=torch.float32, device=t32.device)
-    sc = torch.empty(2, dtype=torch.float32, device=t32.device)
+    # Four separate tensors (no views of one buffer), so the custom operator
+    # front-end can return them without aliasing.
+    stat, tel = (torch.empty(N, dtype=torch.float32, device=t32.device) for _ in range(2))
+    obj, count = (torch.empty(1, dtype=torch.float32, device=t32.device) for _ in range(2))
     L.check(L.lib().algx_head_finalize(cfg, t32.data_ptr(), mlz[0].data_ptr(), mlz[1].data_ptr(),
-                                       mlz[2].data_ptr(), N, vocab_total, out[0].data_ptr(), out[1].data_ptr(),
-                                       sc[0:1].data_ptr(), sc[1:2].data_ptr(), L.stream_of(t32)),
+                                       mlz[2].data_ptr(), N, vocab_total, stat.data_ptr(), tel.data_ptr(),
+                                       obj.data_ptr(), count.data_ptr(), L.stream_of(t32)),
             "algx_head_finalize")
-    return out[0], out[1], sc[0:1], sc[1:2]
+    return stat, tel, obj, count
 
 
 def head_backward(h16, e16, t32, stat, scale, cfg, vocab_offset=0, dh_dtype=torch.bfloat16, workspace=None):

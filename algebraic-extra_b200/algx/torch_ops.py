@@ -84,16 +84,17 @@ def qk_rms_norm(x, gain, eps=1e-5, *, block=1024):
 # The resolved variant travels as plain scalars (a custom operator's schema
 # has no place for the ctypes struct): kind, mode, n, fast_rho, inv_stat,
 # has_sink as ints; clamp, scale and the three guard bounds as floats.
-def _cfg(ints: List[int], floats: List[float]) -> L.AttnConfig:
-    cfg = L.AttnConfig()
-    cfg.kind, cfg.mode, cfg.n, cfg.fast_rho, cfg.inv_stat, cfg.has_sink = (int(i) for i in ints)
-    cfg.clamp, cfg.scale, cfg.guard_qk, cfg.guard_sink, cfg.guard_v = (float(f) for f in floats)
-    return cfg
+# The ctypes struct is built only inside the operators, so a tracer sees no
+# ctypes object; the lists come from the same resolution as the eager path.
+_cfg = F.config_from_lists
 
 
-def _cfg_lists(cfg: L.AttnConfig):
-    return ([cfg.kind, cfg.mode, cfg.n, cfg.fast_rho, cfg.inv_stat, cfg.has_sink],
-            [cfg.clamp, cfg.scale, cfg.guard_qk, cfg.guard_sink, cfg.guard_v])
+@torch.compiler.assume_constant_result
+def _attn_lists(kind, n, c, T, D, shift, fast_rho, inv_stat, compact_stat, poly_rho, range_guard, has_sink):
+    var = F.make_variant(kind, n, c, T, shift, fast_rho, inv_stat, compact_stat, poly_rho)
+    if range_guard and kind == "asinh" and n <= 32 and poly_rho:
+        raise ValueError("range_guard is for exact radical evaluation")
+    return F.config_lists(kind, var, T, D, c, has_sink, range_guard)
 
 
 def _guarded(ints: List[int]) -> bool:
@@ -168,21 +169,23 @@ def flash_attention(q, k, v, sink_logit=None, *, kind: str = "softmax", n: int =
     bk = min(block_k or block, T)
     if T % bq or T % bk:
         raise ValueError(f"sequence length {T} must be divisible by blocks ({bq}, {bk})")
-    var = F.make_variant(kind, n, c, T, shift, fast_rho, inv_stat, compact_stat, poly_rho)
-    if range_guard and kind == "asinh" and n <= 32 and poly_rho:
-        raise ValueError("range_guard is for exact radical evaluation")
-    cfg, sink = F._checked_call(q, k, v, sink_logit, kind, var, c, range_guard)
-    ints, floats = _cfg_lists(cfg)
+    sink = F.check_inputs(q, k, v, sink_logit, kind, c)
+    ints, floats = _attn_lists(kind, n, c, T, D, shift, fast_rho, inv_stat, compact_stat, poly_rho, range_guard,
+                               sink is not None)
     o, *_ = _attn_fwd_op(q.contiguous(), k.contiguous(), v.contiguous(), sink, ints, floats)
     return o
 
 
 # ------------------------------------------------------------------ fused head
-def _head_cfg(ints: List[int], floats: List[float]) -> L.HeadConfig:
-    cfg = L.HeadConfig()
-    cfg.kind, cfg.n, cfg.has_ignore, cfg.ignore_index = (int(i) for i in ints)
-    cfg.inv_c, cfg.clamp = (float(f) for f in floats)
-    return cfg
+# ints [kind, n, has_ignore, ignore_index]; floats [inv_c, clamp, slope], slope
+# being d(objective)/d(mean per-token term): 1 for ce, n / c for alg_ce.
+_head_cfg = FH.head_config_from_lists
+
+
+@torch.compiler.assume_constant_result
+def _head_lists(kind, n, c, vocab, ignore_index):
+    ints, floats = FH.head_config_lists(kind, n, c, vocab, ignore_index)
+    return ints, floats + [1.0 if kind == "ce" else n / c]
 
 
 # h and embed enter in their own dtypes and are rounded to bfloat16 inside the
@@ -233,9 +236,7 @@ def _head_setup(ctx, inputs, output):
 
 def _head_backward(ctx, g_obj, _g_tel, _g_stat, _g_count):
     h, embed, targets, stat, count = ctx.saved_tensors
-    kind, n = ctx.ints[0], ctx.ints[1]
-    slope = 1.0 if kind == L.ALGX_HEAD_CE else n * ctx.floats[0]  # n / c, with floats[0] = 1 / c
-    scale = (g_obj.reshape(1).float() * slope / count).contiguous()
+    scale = (g_obj.reshape(1).float() * ctx.floats[2] / count).contiguous()
     dh, de = _head_bwd_op(h, embed, targets, stat, scale, ctx.ints, ctx.floats)
     return dh, de, None, None, None
 
@@ -260,8 +261,6 @@ def fused_head(h, embed, targets, *, kind="ce", n=16, c=16.0, block_n=128, block
     if embed.shape[1] != d or targets.shape != (N,):
         raise ValueError("h (N, d), embed (V, d) and targets (N,) shapes disagree")
     L.require_cuda(h, embed, targets)
-    cfg = FH.head_config(kind, n, c, embed.shape[0], ignore_index)
-    ints = [cfg.kind, cfg.n, cfg.has_ignore, cfg.ignore_index]
-    floats = [cfg.inv_c, cfg.clamp]
+    ints, floats = _head_lists(kind, n, c, embed.shape[0], ignore_index)
     obj, tel, _, _ = _head_fwd_op(h, embed, targets, ints, floats)
     return obj, tel.detach()

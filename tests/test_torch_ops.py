@@ -45,11 +45,35 @@ def test_fake_shapes_attention_and_norm():
 def test_fake_shapes_head():
     mode, (h, e, t) = _fake(((512, 128), torch.bfloat16), ((1000, 128), torch.float32), ((512,), torch.int32))
     with mode:
-        obj, tel, stat, count = torch.ops.algx.fused_head_fwd(h, e, t, [L.ALGX_HEAD_CE, 16, 0, 0], [1.0, 0.0])
+        obj, tel, stat, count = torch.ops.algx.fused_head_fwd(h, e, t, [L.ALGX_HEAD_CE, 16, 0, 0], [1.0, 0.0, 1.0])
         assert obj.shape == () and tel.shape == (512,) and stat.shape == (512,) and count.shape == (1,)
-        dh, de = torch.ops.algx.fused_head_bwd(h, e, t, stat, count, [L.ALGX_HEAD_CE, 16, 0, 0], [1.0, 0.0])
+        dh, de = torch.ops.algx.fused_head_bwd(h, e, t, stat, count, [L.ALGX_HEAD_CE, 16, 0, 0], [1.0, 0.0, 1.0])
         assert dh.shape == h.shape and dh.dtype == h.dtype
         assert de.shape == e.shape and de.dtype == torch.float32
+
+
+def test_export_keeps_opaque_nodes():
+    """torch.export (dynamo) traces the wrappers on fake CUDA tensors, no GPU needed:
+    each call stays one algx node and the configuration becomes constants."""
+
+    class Block(torch.nn.Module):
+        def forward(self, q, k, v, g, h, e, t):
+            o = T.flash_attention(T.qk_rms_norm(q, g), k, v, kind="asinh", n=16, c=8., range_guard=True)
+            obj, _ = T.fused_head(h, e, t, kind="alg_ce", n=8, c=2.)
+            return o, obj
+
+    with FakeTensorMode():
+        qkv = [torch.empty((2, 3, 512, 64), dtype=torch.bfloat16, device="cuda") for _ in range(3)]
+        args = (*qkv, torch.empty(64, device="cuda"), torch.empty((512, 128), device="cuda"),
+                torch.empty((1000, 128), device="cuda"), torch.empty(512, dtype=torch.int64, device="cuda"))
+    ep = torch.export.export(Block(), args)
+    algx_nodes = [n for n in ep.graph.nodes if n.op == "call_function" and "algx" in str(n.target)]
+    assert [str(n.target) for n in algx_nodes] == ["algx.qk_rms_norm.default", "algx.flash_attention_fwd.default",
+                                                   "algx.fused_head_fwd.default"]
+    ints, floats = algx_nodes[1].args[4], algx_nodes[1].args[5]
+    assert ints == [L.ALGX_ATTN_ASINH, L.ALGX_MODE_GUARDED, 16, 1, 1, 0]
+    assert floats[1] == 1.0 / (8.0 * 8.0)
+    assert algx_nodes[2].args[4][2] == 8 / 2.
 
 
 def test_errors_match_eager_wrappers():
@@ -70,7 +94,7 @@ def test_ops_match_eager_and_trace():
     from algx.kernels.fused_head import fused_head as eager_head
     from algx.kernels.qk_norm import qk_rms_norm as eager_norm
     g = torch.Generator(device="cuda").manual_seed(7)
-    q, k, v, do = (torch.randn((2, 3, 256, 64), device="cuda", generator=g).to(torch.bfloat16) for _ in range(4))
+    q, k, v, do = (torch.randn((2, 3, 512, 64), device="cuda", generator=g).to(torch.bfloat16) for _ in range(4))
     gq = 1 + 0.02 * torch.randn(64, device="cuda", generator=g)
 
     def block(ops, q_, k_, v_, g_):
