@@ -49,7 +49,7 @@ constexpr int kFwdVStages = 2;  // ... so K tiles are needed earlier than V tile
 constexpr int kFwdThreads = 352;  // 8 weight warps, producer, P.V issuer, S issuer
 constexpr int kFwdProducer = 8;
 constexpr int kFwdSmem = kTileBytes * (1 + kFwdKStages + kFwdVStages) + 1024;
-constexpr int kBwdThreads = 768;
+constexpr int kBwdThreads = 800;
 constexpr int kHalfBytes = kTileBytes / 2;  // 64 rows x 64 bf16
 constexpr int kBwdStages = 4;               // Q / dO ring of 64-query halves
 // K x2, V, the Q / dO ring, dS^T x2 tiles, dQ boxes x2, stat / di, alignment slack
@@ -428,7 +428,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   __shared__ uint64_t bar_k_full[2], bar_k_free[2], bar_v_full, bar_v_free, bar_fin, bar_acc_free;
   __shared__ uint64_t bar_dq_full, bar_dq_free, bar_stage_full[2], bar_stage_free[2];
   __shared__ uint64_t bar_st_full[2], bar_st_free[2], bar_ps_ready[2], bar_p_free[2], bar_ds_free[2], bar_ds_ready[2];
-  __shared__ uint64_t bar_qd_full[kBwdStages], bar_qd_empty[kBwdStages], bar_issued[3];
+  __shared__ uint64_t bar_qd_full[kBwdStages], bar_qd_empty[kBwdStages], bar_issued[4];
   __shared__ uint64_t bar_item_full[4], bar_item_empty[4];
   __shared__ int item_q[4];
   __shared__ uint32_t tmem_base;
@@ -443,8 +443,8 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     mbar_wait(&bar_issued[i], 0, &quiet, dev_err);
   };
   // Consumers of the item queue: one arrival per consumer warp on
-  // bar_item_empty (16 gradient + 4 drain warps + 3 issuers).
-  constexpr int kItemConsumers = kBwdGradWarps + 4 + 3;
+  // bar_item_empty (16 gradient + 4 drain warps + 4 issuers).
+  constexpr int kItemConsumers = kBwdGradWarps + 4 + 4;
   auto next_item = [&](int j, bool whole_warp) -> int {
     const int slot = j & 3;
     bool ok = whole_warp ? mbar_wait_warp(&bar_item_full[slot], (j >> 2) & 1, abort_v, dev_err)
@@ -458,7 +458,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   // warps 0-15: score gradients; warp w takes the sub-tiles u with u % 2 == w / 8 (TMEM buffer w / 8),
   //   TMEM lanes 32 (w % 4).. and query columns 32 ((w / 4) % 2).. of each
   // warps 16-19: dQ drain and the dK / dV write-out; warp 20: item queue + TMA producer (+ TMEM owner);
-  // warps 21-23: MMA issuers (21: S^T and dP^T, 22: dV and dK, 23: dQ)
+  // warps 21-24: MMA issuers (21: S^T, 22: dV and dK, 23: dQ, 24: dP^T). A
+  // thread spends ~100 cycles issuing one tcgen05.mma, so S^T and dP^T of the
+  // next sub-tile come from two threads in parallel.
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nq = T / kTile;
   const int total_items = BH * nq;
@@ -467,7 +469,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(&bar_k_full[b], 1);
       mbar_init(&bar_k_free[b], 1);
-      mbar_init(&bar_st_full[b], 1);
+      mbar_init(&bar_st_full[b], 2);  // S^T and dP^T issuers
       mbar_init(&bar_st_free[b], 8);
       mbar_init(&bar_ps_ready[b], 8);
       mbar_init(&bar_p_free[b], 1);
@@ -482,7 +484,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
       mbar_init(&bar_item_full[i], 1);
       mbar_init(&bar_item_empty[i], kItemConsumers);
     }
-    for (int i = 0; i < 3; ++i) mbar_init(&bar_issued[i], 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&bar_issued[i], 1);
     mbar_init(&bar_v_full, 1);
     mbar_init(&bar_v_free, 1);
     mbar_init(&bar_fin, 1);
@@ -563,11 +565,13 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           if (pending_qd[i] >= 0) mbar_wait(&bar_qd_full[i], (pending_qd[i] / kBwdStages) & 1, &quiet, nullptr);
       }
     }
-  } else if (warp == kBwdProducer + 1) {
-    // ----- S^T = K Q^T and dP^T = V dO^T of sub-tile u into buffer u & 1
+  } else if (warp == kBwdProducer + 1 || warp == kBwdProducer + 4) {
+    // ----- S^T = K Q^T (warp 21) or dP^T = V dO^T (warp 24) of sub-tile u into buffer u & 1
     if (lane == 0) {
+      const bool dp = warp == kBwdProducer + 4;
       const uint32_t idS = idesc_bf16_f32(128, 64, 0, 0);
-      const uint32_t k0 = smem_u32(sK), v0 = smem_u32(sV), q0 = smem_u32(sQ), do0 = smem_u32(sdO);
+      const uint32_t a0 = smem_u32(dp ? sV : sK), b0 = smem_u32(dp ? sdO : sQ);
+      const uint32_t tacc = dp ? tdP : tS;
       int U = 0;
       bool ok = true;
       for (int j = 0; ok; ++j) {
@@ -575,29 +579,25 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
         if (it < 0) break;
         const BwdItem w = bwd_item(it, BH, nq);
         const int kb = j & 1;
-        ok = mbar_wait(&bar_k_full[kb], (j >> 1) & 1, abort_v, dev_err) &&
-             mbar_wait(&bar_v_full, j & 1, abort_v, dev_err);
-        const uint32_t kbase = k0 + kb * kTileBytes;
+        ok = dp ? mbar_wait(&bar_v_full, j & 1, abort_v, dev_err)
+                : mbar_wait(&bar_k_full[kb], (j >> 1) & 1, abort_v, dev_err);
+        const uint32_t abase = dp ? a0 : a0 + kb * kTileBytes;  // K double-buffered, V single
         for (int u = 0; ok && u < 2 * w.ni; ++u, ++U) {
           const int b = U & 1, hs = U % kBwdStages;
           if (!mbar_wait(&bar_qd_full[hs], (U / kBwdStages) & 1, abort_v, dev_err)) ok = false;
           if (ok && U >= 2 && !mbar_wait(&bar_st_free[b], ((U >> 1) - 1) & 1, abort_v, dev_err)) ok = false;
           if (!ok) break;
           tc_fence_after();
-          const uint32_t qb = q0 + hs * kHalfBytes;
-          const uint32_t db = do0 + hs * kHalfBytes;
+          const uint32_t bb = b0 + hs * kHalfBytes;
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            mma_ss(tS + 64 * b, desc_sw128(kbase + k * 32, 16, 1024), desc_sw128(qb + k * 32, 16, 1024), idS,
+            mma_ss(tacc + 64 * b, desc_sw128(abase + k * 32, 16, 1024), desc_sw128(bb + k * 32, 16, 1024), idS,
                    k > 0);
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            mma_ss(tdP + 64 * b, desc_sw128(v0 + k * 32, 16, 1024), desc_sw128(db + k * 32, 16, 1024), idS, k > 0);
           mma_commit(&bar_st_full[b]);
         }
-        if (ok) mma_commit(&bar_v_free);  // every dP^T of the item has read V
+        if (ok && dp) mma_commit(&bar_v_free);  // every dP^T of the item has read V
       }
-      settle_issuer(0);
+      settle_issuer(dp ? 3 : 0);
     }
   } else if (warp == kBwdProducer + 2) {
     // ----- dV += P^T dO and dK += dS^T Q of sub-tile w. S^T and dP^T of the
@@ -719,17 +719,18 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           ok = false;
           break;
         }
-        {  // bf16 P^T pairs of this warp's 32 query columns -> 16 TMEM columns of P^T[b]
-          uint32_t pv16[16];
+        // bf16 P^T pairs of this warp's 32 query columns -> 16 TMEM columns of
+        // P^T[b]; the store completes while dS^T goes to shared memory.
+        uint32_t pv16[16];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            pv16[i] = pk[0][i];
-            pv16[8 + i] = pk[1][i];
-          }
-          tmem_st16(tPT + 32 * b + 16 * hc + lane_off, pv16);
+        for (int i = 0; i < 8; ++i) {
+          pv16[i] = pk[0][i];
+          pv16[8 + i] = pk[1][i];
         }
+        tmem_st16_nowait(tPT + 32 * b + 16 * hc + lane_off, pv16);
         const int c16 = 8 * b + 4 * hc;  // first 16-byte unit of this warp's 32 columns
         if (Ig >= 2 && !mbar_wait_warp(&bar_ds_free[s], ((Ig >> 1) - 1) & 1, abort_v, dev_err)) {
+          tmem_wait_st(pv16);
           ok = false;
           break;
         }
@@ -739,6 +740,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const uint32_t* v = dk2[un >> 1] + 4 * (un & 1);
           *reinterpret_cast<uint4*>(ds_tile + sw128_off(r, c16 + un)) = make_uint4(v[0], v[1], v[2], v[3]);
         }
+        tmem_wait_st(pv16);
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
