@@ -21,7 +21,6 @@ from typing import Optional
 import torch
 
 from .. import _lib as L
-from .qk_norm import qknorm_backward
 
 
 def _root(value: float, n: int) -> float:
@@ -130,6 +129,32 @@ def attn_backward(saved, cfg: L.AttnConfig, do, workspace=None):
                                   B, H, T, D, L.dtype_code(q_s.dtype), workspace.data_ptr(), nbytes,
                                   L.stream_of(q_s)), "algx_attn_bwd")
     return dq, dk, dv, dsink
+
+
+def qknorm_attn_backward(q, k, gain_q, gain_k, saved, cfg: L.AttnConfig, do, eps: float, workspace=None):
+    """Backward launch group of :func:`attn_forward_qknorm`: the attention
+    backward and the QK-norm backward of q and k with the latter fused into
+    one epilogue launch; returns (dq, dk, dv, dgain_q, dgain_k, dsink) with
+    dq, dk the gradients of the raw (pre-norm) q, k."""
+    q_s, k_n, v, sink, o, o_prec, stat, guard = saved
+    B, H, T, D = q_s.shape
+    do = do.to(q_s.dtype).contiguous()
+    dq = torch.empty_like(q_s)
+    dk = torch.empty_like(k_n)
+    dv = torch.empty_like(v)
+    dgq = torch.empty(D, dtype=torch.float32, device=q_s.device)
+    dgk = torch.empty(D, dtype=torch.float32, device=q_s.device)
+    dsink = torch.empty(H, dtype=torch.float32, device=q_s.device) if sink is not None else None
+    nbytes = L.lib().algx_qknorm_attn_bwd_workspace_size(B, H, T, D)
+    if workspace is None or workspace.numel() < nbytes:
+        workspace = torch.empty(nbytes, dtype=torch.uint8, device=q_s.device)
+    L.check(L.lib().algx_qknorm_attn_bwd(cfg, q.data_ptr(), k.data_ptr(), gain_q.data_ptr(), gain_k.data_ptr(),
+                                         q_s.data_ptr(), k_n.data_ptr(), v.data_ptr(), L.ptr(sink), guard.data_ptr(),
+                                         o.data_ptr(), L.ptr(o_prec), stat.data_ptr(), do.data_ptr(), dq.data_ptr(),
+                                         dk.data_ptr(), dv.data_ptr(), dgq.data_ptr(), dgk.data_ptr(), L.ptr(dsink),
+                                         B, H, T, D, L.dtype_code(q_s.dtype), float(eps), workspace.data_ptr(),
+                                         nbytes, L.stream_of(q_s)), "algx_qknorm_attn_bwd")
+    return dq, dk, dv, dgq, dgk, dsink
 
 
 class _Flash(torch.autograd.Function):
@@ -261,9 +286,7 @@ class _QKNormFlash(torch.autograd.Function):
     @staticmethod
     def backward(ctx, do):
         q, k, gain_q, gain_k, *saved = ctx.saved_tensors
-        dq, dk, dv, dsink = attn_backward(saved, ctx.cfg, do)
-        dxq, dgq = qknorm_backward(q, gain_q, dq, ctx.eps)
-        dxk, dgk = qknorm_backward(k, gain_k, dk, ctx.eps)
+        dxq, dxk, dv, dgq, dgk, dsink = qknorm_attn_backward(q, k, gain_q, gain_k, saved, ctx.cfg, do, ctx.eps)
         return dxq, dxk, dv, dgq, dgk, dsink, None, None
 
 

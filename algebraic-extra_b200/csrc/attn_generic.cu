@@ -605,6 +605,142 @@ int check_attn(const algx_attn_config* cfg, int64_t B, int64_t H, int64_t T, int
   return ALGX_OK;
 }
 
+// ------------------------------------------------------------------ fused QK-norm backward
+// Backward of the QK RMS norm (kernels/qk_norm.py:45-56) applied to the
+// attention's dq and dk, in place: dq_x holds dq (bf16 from the generic
+// kernels) or, when the fast path ran the unshifted branch, dq is read from
+// the fp32 accumulator as bf16(acc * n * scale), the rounding of
+// dq_finish_kernel; dk_x holds dk. Per row the arithmetic is that of
+// qknorm_bwd_kernel, so dx is bit-identical to the composed calls. dgain:
+// per-CTA column partials, then the last CTA to finish sums them in a fixed
+// order (deterministic for a given grid) and resets the arrival counter.
+constexpr int kEpiThreads = 512;
+constexpr int kEpiUnroll = 4;
+
+// All loads of a thread's kEpiUnroll rows are issued before any is used, so
+// that enough bytes are in flight to keep HBM busy at one CTA per SM.
+template <typename T, bool FROM_ACC>
+__device__ __forceinline__ void qk_rows_bwd(const T* __restrict__ x, const float* __restrict__ gain, T* dxy,
+                                            const float* __restrict__ acc, float f, int64_t rows, float eps,
+                                            float (&part)[Vec<T>::N]) {
+  using V = Vec<T>;
+  constexpr int kA = FROM_ACC ? V::N / 4 : 1;  // 16-byte chunks of fp32 accumulator per thread and row
+  const int lane = threadIdx.x & 31, sub = lane % V::TPR, rl = lane / V::TPR;
+  float g[V::N];
+#pragma unroll
+  for (int i = 0; i < V::N; ++i) g[i] = gain[sub * V::N + i];
+  const int64_t warps = (int64_t)gridDim.x * (kEpiThreads / 32);
+  const int64_t w = (int64_t)blockIdx.x * (kEpiThreads / 32) + (threadIdx.x >> 5);
+  for (int64_t r0 = w * V::RPW * kEpiUnroll; r0 < rows; r0 += warps * V::RPW * kEpiUnroll) {
+    uint4 rx[kEpiUnroll], rd[kEpiUnroll][kA];
+#pragma unroll
+    for (int u = 0; u < kEpiUnroll; ++u) {
+      const int64_t row = r0 + u * V::RPW + rl;
+      const bool ok = row < rows;
+      rx[u] = ok ? ld_stream(x + row * kD + sub * V::N) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+      for (int c = 0; c < kA; ++c) {
+        if constexpr (FROM_ACC)
+          rd[u][c] = ok ? ld_stream(acc + row * kD + sub * V::N + 4 * c) : make_uint4(0, 0, 0, 0);
+        else
+          rd[u][c] = ok ? *reinterpret_cast<const uint4*>(dxy + row * kD + sub * V::N) : make_uint4(0, 0, 0, 0);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < kEpiUnroll; ++u) {
+      const int64_t row = r0 + u * V::RPW + rl;
+      float xv[V::N], dv[V::N];
+      unpack<T>(rx[u], xv);
+      if constexpr (FROM_ACC) {
+#pragma unroll
+        for (int c = 0; c < kA; ++c) {
+          dv[4 * c + 0] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(rd[u][c].x) * f));
+          dv[4 * c + 1] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(rd[u][c].y) * f));
+          dv[4 * c + 2] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(rd[u][c].z) * f));
+          dv[4 * c + 3] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(rd[u][c].w) * f));
+        }
+      } else {
+        unpack<T>(rd[u][0], dv);
+      }
+      float ss = 0.f, sdg = 0.f;
+#pragma unroll
+      for (int i = 0; i < V::N; ++i) {
+        ss = fmaf(xv[i], xv[i], ss);
+        sdg = fmaf(dv[i] * g[i], xv[i], sdg);
+      }
+      ss = row_sum<V::TPR>(ss);
+      sdg = row_sum<V::TPR>(sdg);
+      const float tau = rsqrtf(ss * (1.0f / kD) + eps);
+      const float corr = tau * tau * tau * sdg * (1.0f / kD);
+      float out[V::N];
+#pragma unroll
+      for (int i = 0; i < V::N; ++i) {
+        out[i] = (dv[i] * g[i]) * tau - xv[i] * corr;
+        part[i] = fmaf(dv[i], xv[i] * tau, part[i]);
+      }
+      if (row < rows) *reinterpret_cast<uint4*>(dxy + row * kD + sub * V::N) = pack<T>(out);
+    }
+  }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kEpiThreads) qknorm_attn_bwd_kernel(
+    algx_attn_config cfg, const float* __restrict__ guard, int fast, const float* __restrict__ dq_acc,
+    const T* __restrict__ q, const float* __restrict__ gain_q, const T* __restrict__ k,
+    const float* __restrict__ gain_k, T* dq_x, T* dk_x, float* __restrict__ partial, unsigned* counter,
+    float* __restrict__ dgain_q, float* __restrict__ dgain_k, int64_t rows, float eps) {
+  using V = Vec<T>;
+  __shared__ float red[kEpiThreads / 32 * V::RPW][2 * kD];  // per row slot of a warp: q and k column sums
+  __shared__ float fin[kEpiThreads / (2 * kD)][2 * kD];
+  __shared__ bool last;
+  const bool use_acc = fast && resolve_variant(cfg, guard).branch == BR_UNSHIFTED;
+  float pq[V::N], pk[V::N];
+#pragma unroll
+  for (int i = 0; i < V::N; ++i) pq[i] = pk[i] = 0.f;
+  if (use_acc)
+    qk_rows_bwd<T, true>(q, gain_q, dq_x, dq_acc, (float)cfg.n * cfg.scale, rows, eps, pq);
+  else
+    qk_rows_bwd<T, false>(q, gain_q, dq_x, nullptr, 1.f, rows, eps, pq);
+  qk_rows_bwd<T, false>(k, gain_k, dk_x, nullptr, 1.f, rows, eps, pk);
+  // CTA column sums: slot (warp, row-in-warp) holds its threads' columns
+  const int lane = threadIdx.x & 31, sub = lane % V::TPR, rl = lane / V::TPR;
+  const int slot = (threadIdx.x >> 5) * V::RPW + rl;
+#pragma unroll
+  for (int i = 0; i < V::N; ++i) {
+    red[slot][sub * V::N + i] = pq[i];
+    red[slot][kD + sub * V::N + i] = pk[i];
+  }
+  __syncthreads();
+  if (threadIdx.x < 2 * kD) {
+    float sum = 0.f;
+    for (int r = 0; r < kEpiThreads / 32 * V::RPW; ++r) sum += red[r][threadIdx.x];
+    partial[(int64_t)blockIdx.x * 2 * kD + threadIdx.x] = sum;
+    __threadfence();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(counter, 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  const int c = threadIdx.x % (2 * kD), part = threadIdx.x / (2 * kD);
+  constexpr int kParts = kEpiThreads / (2 * kD);
+  float sum = 0.f;
+#pragma unroll 8
+  for (int b = part; b < (int)gridDim.x; b += kParts) sum += __ldcg(partial + (int64_t)b * 2 * kD + c);
+  fin[part][c] = sum;
+  __syncthreads();
+  if (threadIdx.x < 2 * kD) {
+    float t = 0.f;
+#pragma unroll
+    for (int i = 0; i < kParts; ++i) t += fin[i][threadIdx.x];
+    if (threadIdx.x < kD)
+      dgain_q[threadIdx.x] = t;
+    else
+      dgain_k[threadIdx.x - kD] = t;
+  }
+  if (threadIdx.x == 0) *counter = 0u;
+}
+
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 // Grid of the generic kernels: every (row block, head) tile when they do the
@@ -623,6 +759,13 @@ size_t ws_off_tc(int64_t B, int64_t H, int64_t T) {
   const int64_t nblk = (T + kRows - 1) / kRows;
   return ws_off_sink(B, H, T) + align256((size_t)B * H * nblk * sizeof(float));
 }
+// The fused QK-norm backward appends its dgain partials and, for calls where
+// the fast path does not zero its spare bytes, its own arrival counter.
+constexpr int kEpiBlocks = 148;
+size_t ws_off_epi(int64_t B, int64_t H, int64_t T, int64_t D) {
+  return align256(ws_off_tc(B, H, T) + tc_attn_bwd_workspace(B, H, T, D));
+}
+size_t epi_bytes() { return align256((size_t)kEpiBlocks * 2 * kD * sizeof(float)) + 256; }
 
 }  // namespace algx
 
@@ -718,16 +861,14 @@ size_t algx_attn_bwd_workspace_size(int64_t B, int64_t H, int64_t T, int64_t D) 
   return ws_off_tc(B, H, T) + tc_attn_bwd_workspace(B, H, T, D);
 }
 
-int algx_attn_bwd(const algx_attn_config* cfg, const void* q_scaled, const void* k, const void* v, const float* sink,
-                  const float* guard, const void* o, const float* o_precise, const float* stat, const void* dout,
-                  void* dq, void* dk, void* dv, float* dsink, int64_t B, int64_t H, int64_t T, int64_t D,
-                  int32_t dtype, void* workspace, size_t workspace_bytes, void* stream) {
-  if (int s = check_attn(cfg, B, H, T, D, dtype)) return s;
-  ALGX_REQUIRE(q_scaled && k && v && guard && o && stat && dout && dq && dk && dv, "attn_bwd: NULL pointer");
-  ALGX_REQUIRE(!cfg->has_sink || (sink && dsink), "attn_bwd: has_sink needs sink and dsink");
-  ALGX_REQUIRE(workspace && workspace_bytes >= algx_attn_bwd_workspace_size(B, H, T, D),
-               "attn_bwd: workspace too small (see algx_attn_bwd_workspace_size)");
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
+// The attention backward launch group. With finish_dq false and the fast
+// path taken (*fast), dq holds the generic kernels' result only if the guard
+// chose the shifted branch; otherwise the fp32 accumulator holds it unscaled.
+static int attn_bwd_core(const algx_attn_config* cfg, const void* q_scaled, const void* k, const void* v,
+                         const float* sink, const float* guard, const void* o, const float* o_precise,
+                         const float* stat, const void* dout, void* dq, void* dk, void* dv, float* dsink, int64_t B,
+                         int64_t H, int64_t T, int32_t dtype, void* workspace, cudaStream_t st, bool finish_dq,
+                         bool* fast_out) {
   char* ws = static_cast<char*>(workspace);
   float* di = reinterpret_cast<float*>(ws);
   float* sink_part = reinterpret_cast<float*>(ws + ws_off_sink(B, H, T));
@@ -750,8 +891,9 @@ int algx_attn_bwd(const algx_attn_config* cfg, const void* q_scaled, const void*
   int mask = 7;
   bool fast = false;
   if (int s = tc_attn_bwd(*cfg, q_scaled, k, v, dout, stat, di, guard, dq, dk, dv, tc_ws, B, H, T, dtype, st,
-                          &fast))
+                          finish_dq, &fast))
     return s;
+  *fast_out = fast;
   if (fast) {
     if (cfg->mode == ALGX_MODE_CLIPPED) return ALGX_OK;  // see algx_attn_fwd
     mask = 1 << BR_SHIFTED | 1 << BR_SOFTMAX;
@@ -792,6 +934,66 @@ int algx_attn_bwd(const algx_attn_config* cfg, const void* q_scaled, const void*
   }
   count_launches(1);  // two kernels above, one counted by the macro
   ALGX_LAUNCHED("attn_bwd_generic launch");
+  return ALGX_OK;
+}
+
+int algx_attn_bwd(const algx_attn_config* cfg, const void* q_scaled, const void* k, const void* v, const float* sink,
+                  const float* guard, const void* o, const float* o_precise, const float* stat, const void* dout,
+                  void* dq, void* dk, void* dv, float* dsink, int64_t B, int64_t H, int64_t T, int64_t D,
+                  int32_t dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int s = check_attn(cfg, B, H, T, D, dtype)) return s;
+  ALGX_REQUIRE(q_scaled && k && v && guard && o && stat && dout && dq && dk && dv, "attn_bwd: NULL pointer");
+  ALGX_REQUIRE(!cfg->has_sink || (sink && dsink), "attn_bwd: has_sink needs sink and dsink");
+  ALGX_REQUIRE(workspace && workspace_bytes >= algx_attn_bwd_workspace_size(B, H, T, D),
+               "attn_bwd: workspace too small (see algx_attn_bwd_workspace_size)");
+  bool fast = false;
+  return attn_bwd_core(cfg, q_scaled, k, v, sink, guard, o, o_precise, stat, dout, dq, dk, dv, dsink, B, H, T, dtype,
+                       workspace, static_cast<cudaStream_t>(stream), true, &fast);
+}
+
+size_t algx_qknorm_attn_bwd_workspace_size(int64_t B, int64_t H, int64_t T, int64_t D) {
+  return ws_off_epi(B, H, T, D) + epi_bytes();
+}
+
+int algx_qknorm_attn_bwd(const algx_attn_config* cfg, const void* q, const void* k, const float* gain_q,
+                         const float* gain_k, const void* q_scaled, const void* k_norm, const void* v,
+                         const float* sink, const float* guard, const void* o, const float* o_precise,
+                         const float* stat, const void* dout, void* dq, void* dk, void* dv, float* dgain_q,
+                         float* dgain_k, float* dsink, int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype,
+                         float eps, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int s = check_attn(cfg, B, H, T, D, dtype)) return s;
+  ALGX_REQUIRE(q && k && gain_q && gain_k && q_scaled && k_norm && v && guard && o && stat && dout && dq && dk && dv &&
+                   dgain_q && dgain_k,
+               "qknorm_attn_bwd: NULL pointer");
+  ALGX_REQUIRE(!cfg->has_sink || (sink && dsink), "qknorm_attn_bwd: has_sink needs sink and dsink");
+  ALGX_REQUIRE(eps > 0.f, "qknorm_attn_bwd: epsilon must be positive");
+  ALGX_REQUIRE(workspace && workspace_bytes >= algx_qknorm_attn_bwd_workspace_size(B, H, T, D),
+               "qknorm_attn_bwd: workspace too small (see algx_qknorm_attn_bwd_workspace_size)");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  bool fast = false;
+  if (int s = attn_bwd_core(cfg, q_scaled, k_norm, v, sink, guard, o, o_precise, stat, dout, dq, dk, dv, dsink, B, H,
+                            T, dtype, workspace, st, false, &fast))
+    return s;
+  char* ws = static_cast<char*>(workspace);
+  const float* acc = reinterpret_cast<const float*>(ws + ws_off_tc(B, H, T));
+  float* partial = reinterpret_cast<float*>(ws + ws_off_epi(B, H, T, D));
+  unsigned* counter;
+  if (fast) {  // zeroed with the accumulator
+    counter = reinterpret_cast<unsigned*>(ws + ws_off_tc(B, H, T) + tc_attn_bwd_spare_offset(B, H, T, D));
+  } else {
+    counter = reinterpret_cast<unsigned*>(ws + ws_off_epi(B, H, T, D) + epi_bytes() - 256);
+    ALGX_CUDA(cudaMemsetAsync(counter, 0, sizeof(unsigned), st));
+  }
+  const int64_t rows = B * H * T;
+  if (dtype == ALGX_BF16)
+    qknorm_attn_bwd_kernel<__nv_bfloat16><<<kEpiBlocks, kEpiThreads, 0, st>>>(
+        *cfg, guard, fast ? 1 : 0, acc, (const __nv_bfloat16*)q, gain_q, (const __nv_bfloat16*)k, gain_k,
+        (__nv_bfloat16*)dq, (__nv_bfloat16*)dk, partial, counter, dgain_q, dgain_k, rows, eps);
+  else
+    qknorm_attn_bwd_kernel<float><<<kEpiBlocks, kEpiThreads, 0, st>>>(
+        *cfg, guard, 0, acc, (const float*)q, gain_q, (const float*)k, gain_k, (float*)dq, (float*)dk, partial,
+        counter, dgain_q, dgain_k, rows, eps);
+  ALGX_LAUNCHED("qknorm_attn_bwd launch");
   return ALGX_OK;
 }
 

@@ -966,15 +966,18 @@ int tc_attn_fwd(const algx_attn_config& cfg, const void* q_scaled, const void* k
   return ALGX_OK;
 }
 
-// fp32 dQ accumulator, then the persistent kernel's work-item counter (both
-// zeroed by one memset per call).
+// fp32 dQ accumulator, then the persistent kernel's work-item counter and
+// spare bytes for the caller (all zeroed by one memset per call).
 size_t tc_attn_bwd_workspace(int64_t B, int64_t H, int64_t T, int64_t D) {
   return (size_t)B * H * T * D * sizeof(float) + 256;
+}
+size_t tc_attn_bwd_spare_offset(int64_t B, int64_t H, int64_t T, int64_t D) {
+  return (size_t)B * H * T * D * sizeof(float) + 128;
 }
 
 int tc_attn_bwd(const algx_attn_config& cfg, const void* q_scaled, const void* k, const void* v, const void* dout,
                 const float* stat, const float* di, const float* guard, void* dq, void* dk, void* dv, void* workspace,
-                int64_t B, int64_t H, int64_t T, int32_t dtype, cudaStream_t st, bool* launched) {
+                int64_t B, int64_t H, int64_t T, int32_t dtype, cudaStream_t st, bool finish_dq, bool* launched) {
   *launched = false;
   if (!fast_eligible(cfg, T, dtype)) return ALGX_OK;
   CUtensorMap maps[6];  // q, k, v, dO (loads), dK, dV (stores)
@@ -1004,11 +1007,13 @@ int tc_attn_bwd(const algx_attn_config& cfg, const void* q_scaled, const void* k
     s = clip ? (inv ? ALGX_BWD(32, true, true) : ALGX_BWD(32, true, false)) : ALGX_BWD(32, false, true);
 #undef ALGX_BWD
   if (s) return s;
-  const int64_t n4 = (int64_t)(nacc / 4);
-  const int grid = (int)std::min<int64_t>((n4 + 255) / 256, 148 * 16);
-  dq_finish_kernel<<<grid, 256, 0, st>>>(cfg, guard, reinterpret_cast<const float4*>(acc),
-                                          static_cast<__nv_bfloat16*>(dq), n4);
-  ALGX_LAUNCHED("dq_finish launch");
+  if (finish_dq) {
+    const int64_t n4 = (int64_t)(nacc / 4);
+    const int grid = (int)std::min<int64_t>((n4 + 255) / 256, 148 * 16);
+    dq_finish_kernel<<<grid, 256, 0, st>>>(cfg, guard, reinterpret_cast<const float4*>(acc),
+                                            static_cast<__nv_bfloat16*>(dq), n4);
+    ALGX_LAUNCHED("dq_finish launch");
+  }
   *launched = true;
   return ALGX_OK;
 }

@@ -15,10 +15,17 @@ int tc_attn_fwd(const algx_attn_config& cfg, const void* q_scaled, const void* k
                 const float* sink, const float* guard, void* o, float* stat, int64_t B, int64_t H, int64_t T,
                 int32_t dtype, cudaStream_t st, bool* launched);
 
+// With finish_dq false the fp32 dQ accumulator (the first B*H*T*64 floats of
+// the workspace, unscaled) is left for the caller instead of being rounded
+// into dq.
 int tc_attn_bwd(const algx_attn_config& cfg, const void* q_scaled, const void* k, const void* v,
                 const void* dout, const float* stat, const float* di, const float* guard, void* dq, void* dk,
                 void* dv, void* workspace, int64_t B, int64_t H, int64_t T, int32_t dtype, cudaStream_t st,
-                bool* launched);
+                bool finish_dq, bool* launched);
+
+// Byte offset, within the fast-path workspace, of 64 spare bytes that the
+// launch zeroes along with the dQ accumulator.
+size_t tc_attn_bwd_spare_offset(int64_t B, int64_t H, int64_t T, int64_t D);
 
 size_t tc_attn_bwd_workspace(int64_t B, int64_t H, int64_t T, int64_t D);
 

@@ -2,8 +2,8 @@
 """Hot-path benchmark: BASELINE config 2 (asinh-power attention + QK-norm, fwd+bwd).
 
 One step = QK-norm forward of q and k fused into the attention prologue,
-guarded asinh-power causal flash attention forward (n=16, c=8), its
-backward, and the QK-norm backward, on
+guarded asinh-power causal flash attention forward (n=16, c=8), and its
+backward with the QK-norm backward of q and k fused into one epilogue, on
 B=8, H=12, S=2048, D=64 bf16 per GPU (weak scaling: every rank runs its own
 batch; no collective sits on the data path). FLOPs per step follow the
 reference's convention (scripts/bench_attention.py:50,65): 3.5 x 4*B*H*T^2*D/2.
@@ -36,7 +36,7 @@ B, H, T, D = 8, 12, 2048, 64
 N_POW, C_SCALE, EPS = 16, 8.0, 1e-5
 FWD_FLOP = 4 * B * H * T * T * D / 2          # causal forward, per GPU
 STEP_FLOP = 3.5 * FWD_FLOP                    # forward + backward
-BWD_FLOP = 2.5 * FWD_FLOP                     # the backward launch group alone
+BWD_FLOP = 2.5 * FWD_FLOP                     # the attention backward of the backward launch group
 WORKLOAD = ("BASELINE config 2: QK-norm(q,k) -> causal asinh-power flash attention (n=16, c=8, "
             "range guard) fwd+bwd, B=8 H=12 S=2048 D=64 bf16, fp32 accumulation")
 # BASELINE config 3 (and the 350M shapes of config 4): fused LM head + likelihood
@@ -284,9 +284,8 @@ def run_algx(args, rank, world, local_rank):
     import torch.distributed as dist
 
     from algx import _lib as L
-    from algx.kernels.flash import attn_backward, attn_forward_qknorm, build_config, make_variant, \
+    from algx.kernels.flash import attn_forward_qknorm, build_config, make_variant, qknorm_attn_backward, \
         qknorm_flash_attention
-    from algx.kernels.qk_norm import qknorm_backward
 
     dev = torch.device("cuda", local_rank)
     torch.cuda.set_device(dev)
@@ -296,8 +295,7 @@ def run_algx(args, rank, world, local_rank):
     gq = 1 + 0.02 * torch.randn(D, device=dev, generator=gen)
     gk = 1 + 0.02 * torch.randn(D, device=dev, generator=gen)
     cfg = build_config("asinh", make_variant("asinh", N_POW, C_SCALE, T), T, D, C_SCALE, False, True)
-    ws_attn = torch.empty(lib.algx_attn_bwd_workspace_size(B, H, T, D), dtype=torch.uint8, device=dev)
-    ws_norm = torch.empty(lib.algx_qknorm_bwd_workspace_size(B * H * T, D), dtype=torch.uint8, device=dev)
+    ws_bwd = torch.empty(lib.algx_qknorm_attn_bwd_workspace_size(B, H, T, D), dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
     bwd_events = []
 
@@ -306,12 +304,10 @@ def run_algx(args, rank, world, local_rank):
         if record:
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-        dq, dk, dv, _ = attn_backward(saved, cfg, do, ws_attn)
+        dq, dk, dv, dgq, dgk, _ = qknorm_attn_backward(q, k, gq, gk, saved, cfg, do, EPS, ws_bwd)
         if record:
             e1.record(stream)
             bwd_events.append((e0, e1))
-        qknorm_backward(q, gq, dq, EPS, ws_norm)
-        qknorm_backward(k, gk, dk, EPS, ws_norm)
         return o, dv
 
     def sync_all():
@@ -445,7 +441,7 @@ def run_algx(args, rank, world, local_rank):
                         "streams"},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                      "frac": achieved / peak_tf, "traffic": _traffic(),
-                     "kernel": "attention backward launch group (di, tcgen05 bwd, dq finish)",
+                     "kernel": "backward launch group (di, tcgen05 attention bwd, fused QK-norm bwd epilogue)",
                      "algorithmic": "2.5 x 4*B*H*T^2*D/2 FLOP per launch", "ms_per_launch": bwd_ms,
                      "peak_source": f"{peak_src} bf16 dense (burst)"},
         "gpu_launches": int(launches),

@@ -142,6 +142,27 @@ ALGX_API int algx_attn_bwd(const algx_attn_config* cfg, const void* q_scaled, co
                   int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype, void* workspace,
                   size_t workspace_bytes, void* stream);
 
+/* Bytes of workspace algx_qknorm_attn_bwd needs. */
+ALGX_API size_t algx_qknorm_attn_bwd_workspace_size(int64_t B, int64_t H, int64_t T, int64_t D);
+
+/* Backward of attention over QK-normed inputs, the counterpart of
+ * algx_qknorm_attn_prepare: the attention backward of algx_attn_bwd on
+ * (q_scaled, k_norm) followed by the QK RMS norm backward of q and k
+ * (kernels/qk_norm.py:45-56) in one launch group. dq, dk receive d/dq and
+ * d/dk of the raw (pre-norm) q, k; dgain_q, dgain_k (64,) fp32 the gain
+ * gradients; dv and dsink as algx_attn_bwd. dk equals, bit for bit,
+ * algx_attn_bwd followed by algx_qknorm_bwd, and so does dq up to the order
+ * of the fast path's dQ reduce-adds (which varies between any two calls);
+ * dgain differs only by the order of its fp32 sums. Replaces the VJP of the model's qk-norm ->
+ * flash_attention prologue (model.py:170-174: qk_norm.py:45-56 after
+ * flash.py:630-642). */
+ALGX_API int algx_qknorm_attn_bwd(const algx_attn_config* cfg, const void* q, const void* k, const float* gain_q,
+                  const float* gain_k, const void* q_scaled, const void* k_norm, const void* v,
+                  const float* sink, const float* guard, const void* o, const float* o_precise,
+                  const float* stat, const void* dout, void* dq, void* dk, void* dv, float* dgain_q,
+                  float* dgain_k, float* dsink, int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype,
+                  float eps, void* workspace, size_t workspace_bytes, void* stream);
+
 /* --------------------------------------------------------------- fused head */
 
 /* kernels/fused_head.py:260-275 (+ the ignore_index extension). */

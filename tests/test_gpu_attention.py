@@ -264,3 +264,48 @@ def test_fused_qknorm_prologue_matches_composed(dtype, with_sink):
     lim = 1e-2 if dtype == torch.bfloat16 else 1e-5
     for a, b in zip(g_f, g_c):
         assert rel_l2(a, b) < lim
+
+
+@pytest.mark.parametrize("dtype,guard,gain,with_sink", [
+    (torch.bfloat16, True, 1., False), (torch.bfloat16, True, 1., True), (torch.bfloat16, True, 20., True),
+    (torch.bfloat16, False, 1., False), (torch.float32, True, 1., True)])
+def test_fused_qknorm_backward_matches_composed(dtype, guard, gain, with_sink):
+    """algx_qknorm_attn_bwd == algx_attn_bwd then algx_qknorm_bwd on q and k, on the same residuals.
+
+    gain 20 makes the scores exceed the guard bound, so the shifted fallback
+    supplies dq (bf16) instead of the fast path's fp32 accumulator. dk, dv and
+    dsink are computed in a fixed order and must match bit for bit, as must dq
+    wherever it does not come from the dQ reduce-adds (whose order varies
+    between any two calls); dgain differs only by the order of its sums.
+    """
+    from algx.kernels import flash as F
+    from algx.kernels.qk_norm import qknorm_backward
+    B, H, T, D = 2, 3, 512, 64
+    q, k, v, do = (_randn(60 + i, (B, H, T, D), dtype).cuda() for i in range(4))
+    gq = (gain + 0.02 * _randn(70, (D,))).cuda()
+    gk = (gain + 0.02 * _randn(71, (D,))).cuda()
+    sink_logit = _randn(72, (H,)).cuda() if with_sink else None
+    var = F.make_variant("asinh", 16, 8., T)
+    sink = F.check_inputs(q, k, v, sink_logit, "asinh", 8.)
+    cfg = F.build_config("asinh", var, T, D, 8., with_sink, guard)
+    o, saved = F.attn_forward_qknorm(q, k, v, gq, gk, sink, cfg, 1e-5)
+    fused = F.qknorm_attn_backward(q, k, gq, gk, saved, cfg, do, 1e-5)
+    dq, dk, dv, dsink = F.attn_backward(saved, cfg, do)
+    dxq, dgq = qknorm_backward(q, gq, dq, 1e-5)
+    dxk, dgk = qknorm_backward(k, gk, dk, 1e-5)
+    torch.cuda.synchronize()
+    g = saved[7].cpu().tolist()  # max||q_s||^2, max||k||^2, max|v|, max|sink| (attn_common.cuh)
+    low = g[0] * g[1] <= cfg.guard_qk and g[2] <= cfg.guard_v and (not with_sink or g[3] <= cfg.guard_sink)
+    shifted = guard and not low
+    fast_dq = dtype == torch.bfloat16 and not shifted
+    assert torch.equal(fused[1], dxk) and torch.equal(fused[2], dv)
+    if with_sink:
+        assert torch.equal(fused[5], dsink)
+    if fast_dq:
+        assert rel_l2(fused[0], dxq) < 2e-3
+    else:
+        assert torch.equal(fused[0], dxq)
+    for a, b in ((fused[3], dgq), (fused[4], dgk)):
+        assert rel_l2(a, b) < (1e-3 if fast_dq else 1e-5)
+    if gain == 20.:
+        assert shifted, "the large gains should have selected the shifted branch"
