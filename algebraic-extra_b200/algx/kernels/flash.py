@@ -75,13 +75,11 @@ def attn_forward(q, k, v, sink, cfg: L.AttnConfig):
     L.check(L.lib().algx_attn_prepare(cfg, q.data_ptr(), k.data_ptr(), v.data_ptr(), sp, q_s.data_ptr(),
                                       guard.data_ptr(), B, H, T, D, L.dtype_code(q.dtype), L.stream_of(q)),
             "algx_attn_prepare")
-    return _attn_forward_prepared(q_s, k, v, sink, guard, cfg)
+    return attn_forward_prepared(q_s, k, v, sink, guard, cfg)
 
 
-def attn_forward_qknorm(q, k, v, gain_q, gain_k, sink, cfg: L.AttnConfig, eps: float):
-    """Forward launch group with the fused QK-norm prologue: attention of
-    (rms_norm(q) * gain_q, rms_norm(k) * gain_k, v) with the QK norm, the
-    scale fold and the guard maxima in one launch; returns (o, saved)."""
+def qknorm_attn_prepare(q, k, v, gain_q, gain_k, sink, cfg: L.AttnConfig, eps: float):
+    """The fused QK-norm prologue alone: (q_scaled, k_norm, guard maxima)."""
     B, H, T, D = q.shape
     q_s = torch.empty_like(q)
     k_n = torch.empty_like(k)
@@ -91,10 +89,19 @@ def attn_forward_qknorm(q, k, v, gain_q, gain_k, sink, cfg: L.AttnConfig, eps: f
                                              gain_k.data_ptr(), sp, q_s.data_ptr(), k_n.data_ptr(),
                                              guard.data_ptr(), B, H, T, D, L.dtype_code(q.dtype), float(eps),
                                              L.stream_of(q)), "algx_qknorm_attn_prepare")
-    return _attn_forward_prepared(q_s, k_n, v, sink, guard, cfg)
+    return q_s, k_n, guard
 
 
-def _attn_forward_prepared(q_s, k, v, sink, guard, cfg: L.AttnConfig):
+def attn_forward_qknorm(q, k, v, gain_q, gain_k, sink, cfg: L.AttnConfig, eps: float):
+    """Forward launch group with the fused QK-norm prologue: attention of
+    (rms_norm(q) * gain_q, rms_norm(k) * gain_k, v) with the QK norm, the
+    scale fold and the guard maxima in one launch; returns (o, saved)."""
+    q_s, k_n, guard = qknorm_attn_prepare(q, k, v, gain_q, gain_k, sink, cfg, eps)
+    return attn_forward_prepared(q_s, k_n, v, sink, guard, cfg)
+
+
+def attn_forward_prepared(q_s, k, v, sink, guard, cfg: L.AttnConfig):
+    """Forward kernels on prepared inputs (q_scaled, the guard maxima); (o, saved)."""
     B, H, T, D = q_s.shape
     q = q_s
     dt = L.dtype_code(q.dtype)
@@ -300,6 +307,14 @@ def qknorm_flash_attention(q, k, v, gain_q, gain_k, sink_logit=None, *, eps: flo
     gradients (q, k, v, both gains and the sink) as the two calls composed;
     the reference has no fused entry of this kind.
     """
+    cfg, sink, gq, gk = qknorm_call_args(q, k, v, gain_q, gain_k, sink_logit, eps, kind, n, c, block, range_guard,
+                                         shift, fast_rho, inv_stat)
+    return _QKNormFlash.apply(q.contiguous(), k.contiguous(), v.contiguous(), gq, gk, sink, cfg, float(eps))
+
+
+def qknorm_call_args(q, k, v, gain_q, gain_k, sink_logit, eps, kind, n, c, block, range_guard, shift, fast_rho,
+                     inv_stat):
+    """Validation and configuration shared by the QK-norm attention entries: (cfg, sink, gain_q, gain_k)."""
     B, H, T, D = q.shape
     bq = min(block, T)
     if T % bq:
@@ -312,4 +327,4 @@ def qknorm_flash_attention(q, k, v, gain_q, gain_k, sink_logit=None, *, eps: flo
     gk = gain_k.to(device=q.device, dtype=torch.float32).contiguous()
     if gq.shape != (64,) or gk.shape != (64,):
         raise ValueError("gains must have shape (64,)")
-    return _QKNormFlash.apply(q.contiguous(), k.contiguous(), v.contiguous(), gq, gk, sink, cfg, float(eps))
+    return cfg, sink, gq, gk

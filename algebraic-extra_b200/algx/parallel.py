@@ -1,8 +1,12 @@
 """Multi-GPU pieces of the hot path (one process per GPU, torch.distributed).
 
-* Attention and QK-norm shard by (batch x heads) with no exchange: each rank
-  calls the single-GPU API on its own heads.
-* The fused head is vocabulary-parallel (SURVEY row E2): rank r holds a
+* Attention and QK-norm shard by (batch x heads) with no exchange on the data
+  path: each rank runs its own slice of one logical batch. For branch parity
+  with a single call on the whole batch, the range guard's maxima are
+  all-reduced (MAX, 4 floats) between the prologue and the forward kernels,
+  and the gradients of the shared parameters (QK-norm gains, and the sink
+  when the batch rather than the heads is split) are all-reduced (SUM).
+* The fused head is vocabulary-parallel: rank r holds a
   contiguous slice of the embedding rows. The forward computes per-token
   (max, sum, target logit) over the local slice, then all-reduces them
   (MAX then SUM for "ce"; SUM only for the additive "alg_ce"); the backward
@@ -16,6 +20,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib as L
+from .kernels import flash as F
 from .kernels import fused_head as FH
 
 
@@ -86,3 +91,71 @@ def vocab_parallel_fused_head(h, embed_shard, targets, *, vocab_offset: int, voc
     obj, tel = _VocabParallelHead.apply(h, embed_shard, targets, cfg, slope, kind, vocab_offset, vocab_total,
                                         group)
     return obj, tel.detach()
+
+
+# ------------------------------------------------------------------ attention
+def combine_guard(guard: torch.Tensor, group=None) -> torch.Tensor:
+    """This rank's range-guard maxima -> the maxima over all ranks, in place.
+
+    The reference takes them over the whole batch (kernels/flash.py:841-849).
+    NaN becomes +inf first: both fail every guard comparison (the shifted
+    branch), and a MAX reduction need not propagate NaN.
+    """
+    torch.nan_to_num_(guard, nan=float("inf"))
+    dist.all_reduce(guard, op=dist.ReduceOp.MAX, group=group)
+    return guard
+
+
+def sum_shared_grads(grads, group=None):
+    """All-reduce (SUM) a list of gradient tensors as one flat buffer; returns new tensors."""
+    flat = torch.cat([g.reshape(-1) for g in grads])
+    dist.all_reduce(flat, op=dist.ReduceOp.SUM, group=group)
+    out, i = [], 0
+    for g in grads:
+        out.append(flat[i:i + g.numel()].view_as(g))
+        i += g.numel()
+    return out
+
+
+class _ShardedQKNormFlash(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, gain_q, gain_k, sink, cfg, eps, group, sum_sink):
+        q_s, k_n, guard = F.qknorm_attn_prepare(q, k, v, gain_q, gain_k, sink, cfg, eps)
+        combine_guard(guard, group)
+        o, saved = F.attn_forward_prepared(q_s, k_n, v, sink, guard, cfg)
+        ctx.cfg, ctx.eps, ctx.group, ctx.sum_sink = cfg, eps, group, sum_sink
+        ctx.save_for_backward(q, k, gain_q, gain_k, *saved)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, gain_q, gain_k, *saved = ctx.saved_tensors
+        dxq, dxk, dv, dgq, dgk, dsink = F.qknorm_attn_backward(q, k, gain_q, gain_k, saved, ctx.cfg, do, ctx.eps)
+        shared = [dgq, dgk] + ([dsink] if ctx.sum_sink and dsink is not None else [])
+        shared = sum_shared_grads(shared, ctx.group)
+        dgq, dgk = shared[0], shared[1]
+        if ctx.sum_sink and dsink is not None:
+            dsink = shared[2]
+        return dxq, dxk, dv, dgq, dgk, dsink, None, None, None, None
+
+
+def sharded_qknorm_flash_attention(q, k, v, gain_q, gain_k, sink_logit=None, *, shard: str = "batch",
+                                   group=None, eps: float = 1e-5, kind: str = "asinh", n: int = 16,
+                                   c: float = 16.0, block: int = 512, range_guard: bool = False, shift=None,
+                                   fast_rho=None, inv_stat=None):
+    """``qknorm_flash_attention`` on this rank's slice of one logical batch.
+
+    ``shard="batch"``: every rank holds some of the sequences with all heads,
+    and the same ``sink_logit`` (its gradient is summed over the ranks).
+    ``shard="heads"``: every rank holds some of the heads of every sequence,
+    and the matching slice of ``sink_logit`` (its gradient stays local).
+    The QK-norm gains are shared in both cases (their gradients are summed).
+    Outputs and gradients equal those of one call on the whole batch, with
+    the range guard decided on the maxima over all ranks.
+    """
+    if shard not in ("batch", "heads"):
+        raise ValueError(f"shard must be 'batch' or 'heads', got {shard!r}")
+    cfg, sink, gq, gk = F.qknorm_call_args(q, k, v, gain_q, gain_k, sink_logit, eps, kind, n, c, block, range_guard,
+                                           shift, fast_rho, inv_stat)
+    return _ShardedQKNormFlash.apply(q.contiguous(), k.contiguous(), v.contiguous(), gq, gk, sink, cfg, float(eps),
+                                     group, shard == "batch")

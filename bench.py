@@ -1,5 +1,5 @@
 #!/usr/bin/env python3
-"""Hot-path benchmark: BASELINE config 2 (asinh-power attention + QK-norm, fwd+bwd).
+"""Hot-path benchmark: asinh-power attention + QK-norm, fwd+bwd, B8 H12 S2048 D64 bf16 (the headline workload).
 
 One step = QK-norm forward of q and k fused into the attention prologue,
 guarded asinh-power causal flash attention forward (n=16, c=8), and its
@@ -39,7 +39,7 @@ STEP_FLOP = 3.5 * FWD_FLOP                    # forward + backward
 BWD_FLOP = 2.5 * FWD_FLOP                     # the attention backward of the backward launch group
 WORKLOAD = ("BASELINE config 2: QK-norm(q,k) -> causal asinh-power flash attention (n=16, c=8, "
             "range guard) fwd+bwd, B=8 H=12 S=2048 D=64 bf16, fp32 accumulation")
-# BASELINE config 3 (and the 350M shapes of config 4): fused LM head + likelihood
+# fused LM head + likelihood: N=16384 tokens, V=50304, d=768 (and d=1024, the 350M shapes)
 HEAD_N, HEAD_V = 16384, 50304
 
 
@@ -214,7 +214,7 @@ def time_cuda(fn, steps, warmup, stream, sync_all, max_over_ranks):
 
 
 def secondary(dev, rank, world, stream, sync_all, max_over_ranks, steps=5, warmup=3):
-    """The other BASELINE lines: fused head tok/s (config 3, ce and alg_ce n=8 c=2;
+    """The other headline lines: fused head tok/s (d=768, ce and alg_ce n=8 c=2;
     vocabulary-parallel over the ranks when N > 1) and the 350M shapes (config 4)."""
     from algx.kernels.flash import qknorm_flash_attention
     from algx.kernels.fused_head import fused_head

@@ -114,7 +114,7 @@ ALGX_API int algx_attn_prepare(const algx_attn_config* cfg, const void* q, const
  * algx_qknorm_fwd on q and k followed by algx_attn_prepare; guard as there.
  * Replaces the model's qk-norm -> flash_attention prologue (model.py:170-174,
  * qk_norm.py:29-43, flash.py:823-849); no rotary is applied (the attention
- * block of BASELINE config 2 has none). */
+ * block benchmarked at B8 H12 S2048 has none). */
 ALGX_API int algx_qknorm_attn_prepare(const algx_attn_config* cfg, const void* q, const void* k,
                                       const void* v, const float* gain_q, const float* gain_k,
                                       const float* sink, void* q_scaled, void* k_norm, float* guard,

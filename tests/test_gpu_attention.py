@@ -2,7 +2,7 @@
 
 Cases and tolerances port tests/test_flash_kernel_tpu.py of the reference
 (file:line cited per test), plus the golden fixtures made from the
-reference's own dense code and the BASELINE fp32 bar (1e-3 relative).
+reference's own dense code and the fp32 bar of 1e-3 relative.
 """
 
 import math
@@ -184,7 +184,7 @@ def test_against_reference_goldens(case, prec):
 
 
 def test_baseline_config1_qknorm_then_attention():
-    """B2 H4 S512 D64 fp32, QK-norm (gain 1) then guarded asinh n16 c8.
+    """The CPU-runnable configuration: B2 H4 S512 D64 fp32, QK-norm (gain 1) then guarded asinh n16 c8.
 
     The fp32 bar of the north star: outputs and grads within 1e-3 relative.
     """
@@ -309,3 +309,94 @@ def test_fused_qknorm_backward_matches_composed(dtype, guard, gain, with_sink):
         assert rel_l2(a, b) < (1e-3 if fast_dq else 1e-5)
     if gain == 20.:
         assert shifted, "the large gains should have selected the shifted branch"
+
+
+def _sharded_vs_single(rank, world, init_file, q_out):
+    """Rank r runs batch slice r of a logical batch through the sharded API and
+    compares with one single-GPU call on the whole batch (on its own GPU)."""
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [root, os.path.join(root, "algebraic-extra_b200")]
+    import torch.distributed as dist
+    from algx.kernels.flash import qknorm_flash_attention
+    from algx.parallel import sharded_qknorm_flash_attention
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"file://{init_file}", rank=rank, world_size=world,
+                            device_id=torch.device("cuda", rank))
+    try:
+        B, H, T, D = 2 * world, 3, 256, 64
+        g = torch.Generator().manual_seed(81)
+        q, k, v, do = (torch.randn((B, H, T, D), generator=g).to(torch.bfloat16).cuda() for _ in range(4))
+        v[-1, 0, 5, 7] = 3e8  # the last slice alone exceeds the guard's max|v|: the shifted branch everywhere
+        gq0, gk0 = (1 + 0.02 * torch.randn(64, generator=g)).cuda(), (1 + 0.02 * torch.randn(64, generator=g)).cuda()
+        sink0 = torch.randn(H, generator=g).cuda()
+        opts = dict(kind="asinh", n=16, c=8., range_guard=True)
+
+        def run(sharded):
+            lo = 2 * rank if sharded else 0
+            hi = lo + 2 if sharded else B
+            leaves = [t[lo:hi].clone().requires_grad_(True) for t in (q, k, v)]
+            gains = [x.clone().requires_grad_(True) for x in (gq0, gk0)]
+            sink = sink0.clone().requires_grad_(True)
+            fn = partial(sharded_qknorm_flash_attention, shard="batch") if sharded else qknorm_flash_attention
+            o = fn(*leaves, *gains, sink, **opts)
+            torch.sum(o.float() * do[lo:hi].float()).backward()
+            return o.detach(), [t.grad for t in leaves], [x.grad for x in gains] + [sink.grad]
+
+        o_s, g_s, shared_s = run(True)
+        o_f, g_f, shared_f = run(False)
+        sl = slice(2 * rank, 2 * rank + 2)
+        ok_o = torch.equal(o_s, o_f[sl])
+        ok_g = all(rel_l2(a, b[sl]) < 1e-2 for a, b in zip(g_s, g_f))
+        ok_shared = all(rel_l2(a, b) < 1e-3 for a, b in zip(shared_s, shared_f))
+        q_out.put((rank, bool(ok_o), bool(ok_g), bool(ok_shared)))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_sharded_qknorm_attention_two_gpus():
+    """Batch split over two GPUs == one call on the whole batch, including the
+    range guard's branch (decided on the maxima over both ranks) and the
+    summed gain and sink gradients."""
+    import tempfile
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q_out = ctx.Queue()
+    with tempfile.TemporaryDirectory() as tmp:
+        procs = [ctx.Process(target=_sharded_vs_single, args=(r, 2, os.path.join(tmp, "pg"), q_out))
+                 for r in range(2)]
+        for p in procs:
+            p.start()
+        results = [q_out.get(timeout=300) for _ in range(2)]
+        for p in procs:
+            p.join(timeout=120)
+            assert p.exitcode == 0
+    for rank, ok_o, ok_g, ok_shared in results:
+        assert ok_o and ok_g and ok_shared, (rank, ok_o, ok_g, ok_shared)
+
+
+def test_sharded_qknorm_attention_one_rank_matches_single():
+    """With one rank the sharded entry is the single-GPU entry (same branch, same values)."""
+    import tempfile
+    import torch.distributed as dist
+    from algx.kernels.flash import qknorm_flash_attention
+    from algx.parallel import sharded_qknorm_flash_attention
+    shape = (2, 3, 256, 64)
+    q, k, v, do = (_randn(90 + i, shape, torch.bfloat16).cuda() for i in range(4))
+    gq0, gk0 = (1 + 0.02 * _randn(95, (64,))).cuda(), (1 + 0.02 * _randn(96, (64,))).cuda()
+    with tempfile.TemporaryDirectory() as tmp:
+        dist.init_process_group("nccl", init_method=f"file://{os.path.join(tmp, 'pg')}", rank=0, world_size=1,
+                                device_id=torch.device("cuda", torch.cuda.current_device()))
+        try:
+            outs = []
+            for fn in (qknorm_flash_attention, partial(sharded_qknorm_flash_attention, shard="heads")):
+                leaves = [t.clone().requires_grad_(True) for t in (q, k, v, gq0, gk0)]
+                o = fn(*leaves, kind="asinh", n=16, c=8., range_guard=True)
+                torch.sum(o.float() * do.float()).backward()
+                outs.append((o.detach(), [t.grad for t in leaves]))
+        finally:
+            dist.destroy_process_group()
+    assert torch.equal(outs[0][0], outs[1][0])
+    for a, b in zip(outs[0][1], outs[1][1]):
+        assert rel_l2(a, b) < 1e-2

@@ -1,5 +1,5 @@
 """Fused head kernels vs the oracle (cases of tests/test_fused_head_tpu.py:13-67, plus ce,
-ignore_index, golden fixtures and BASELINE config 3 at full size)."""
+ignore_index, golden fixtures and the benchmark head (N=16384, d=768, V=50304) at full size)."""
 
 import os
 
@@ -77,7 +77,7 @@ def test_production_head_tiles_at_model_widths(width):
 @pytest.mark.parametrize("ignore", [None, -100])
 @pytest.mark.parametrize("V", [5000, 50304])
 def test_ce_head_with_padded_vocab_and_ignore_index(ignore, V):
-    """ce head (BASELINE config 3 semantics): loss within 1e-4 absolute, labels bit-exact.
+    """ce head at the benchmark shapes: loss within 1e-4 absolute, labels bit-exact.
 
     With ignore=None a -100 label matches no column, as the reference kernel's
     compare does; with ignore=-100 those rows leave the loss and the mean.

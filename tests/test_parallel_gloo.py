@@ -103,3 +103,43 @@ def test_shard_rows_cover_vocabulary_once():
             assert sum(c for _, c in parts) == V
             for (o1, c1), (o2, _) in zip(parts, parts[1:]):
                 assert o1 + c1 == o2
+
+
+def _guard_worker(rank, init_file, q):
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [root, os.path.join(root, "algebraic-extra_b200")]
+    from algx.parallel import combine_guard, sum_shared_grads
+    dist.init_process_group("gloo", init_method=f"file://{init_file}", rank=rank, world_size=WORLD)
+    try:
+        # per-rank maxima (max||q_s||^2, max||k||^2, max|v|, max|sink|); rank 1 saw a NaN
+        mine = [torch.tensor([0.2, 7.0, 1.5, 0.3]), torch.tensor([0.4, float("nan"), 0.5, 0.1])][rank]
+        g = combine_guard(mine.clone())
+        ok_guard = torch.equal(g, torch.tensor([0.4, float("inf"), 1.5, 0.3]))
+        dg = [torch.full((64,), 1.0 + rank, dtype=torch.float32), torch.arange(64, dtype=torch.float32) * rank,
+              torch.full((3,), 0.5)]
+        s = sum_shared_grads(dg)
+        ok_sum = (torch.equal(s[0], torch.full((64,), 3.0)) and torch.equal(s[1], torch.arange(64.0))
+                  and torch.equal(s[2], torch.ones(3)) and all(a.shape == b.shape for a, b in zip(s, dg)))
+        q.put((rank, bool(ok_guard), bool(ok_sum)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_attention_guard_and_shared_grads():
+    """Sharded attention: the range guard's maxima become global maxima on every rank
+    (NaN as +inf, the same shifted-branch decision), and the shared gains'
+    gradients are summed over the ranks."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with tempfile.TemporaryDirectory() as tmp:
+        init_file = os.path.join(tmp, "pg")
+        procs = [ctx.Process(target=_guard_worker, args=(r, init_file, q)) for r in range(WORLD)]
+        for p in procs:
+            p.start()
+        results = [q.get(timeout=120) for _ in range(WORLD)]
+        for p in procs:
+            p.join(timeout=60)
+            assert p.exitcode == 0
+    for rank, ok_guard, ok_sum in results:
+        assert ok_guard and ok_sum, (rank, ok_guard, ok_sum)
