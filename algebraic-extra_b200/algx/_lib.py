@@ -70,16 +70,16 @@ SIGNATURES = {
     "algx_qknorm_bwd_noalloc": ([_P, _P, _P, _P, _P, _I64, _I64, _I32, _F, _P], ctypes.c_int),
     "algx_attn_prepare": ([ctypes.POINTER(AttnConfig), _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _P],
                           ctypes.c_int),
-    "algx_qknorm_attn_prepare": ([ctypes.POINTER(AttnConfig), _P, _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64,
-                                  _I64, _I32, _F, _P], ctypes.c_int),
+    "algx_qknorm_attn_prepare": ([ctypes.POINTER(AttnConfig)] + [_P] * 7 + [_I64] + [_P] * 4 +
+                                 [_I64, _I64, _I64, _I64, _I32, _F, _P], ctypes.c_int),
     "algx_attn_fwd": ([ctypes.POINTER(AttnConfig), _P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _P],
                       ctypes.c_int),
     "algx_attn_bwd_workspace_size": ([_I64, _I64, _I64, _I64], _SZ),
     "algx_attn_bwd": ([ctypes.POINTER(AttnConfig), _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
                        _I64, _I64, _I64, _I64, _I32, _P, _SZ, _P], ctypes.c_int),
     "algx_qknorm_attn_bwd_workspace_size": ([_I64, _I64, _I64, _I64], _SZ),
-    "algx_qknorm_attn_bwd": ([ctypes.POINTER(AttnConfig)] + [_P] * 19 + [_I64, _I64, _I64, _I64, _I32, _F, _P, _SZ,
-                                                                         _P], ctypes.c_int),
+    "algx_qknorm_attn_bwd": ([ctypes.POINTER(AttnConfig)] + [_P] * 6 + [_I64] + [_P] * 15 +
+                             [_I64, _I64, _I64, _I64, _I32, _F, _P, _SZ, _P], ctypes.c_int),
     "algx_head_fwd_splits": ([_I64, _I64], ctypes.c_int),
     "algx_head_fwd": ([ctypes.POINTER(HeadConfig), _P, _P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, _I32, _I32, _P],
                       ctypes.c_int),

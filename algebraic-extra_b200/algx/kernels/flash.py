@@ -78,25 +78,34 @@ def attn_forward(q, k, v, sink, cfg: L.AttnConfig):
     return attn_forward_prepared(q_s, k, v, sink, guard, cfg)
 
 
-def qknorm_attn_prepare(q, k, v, gain_q, gain_k, sink, cfg: L.AttnConfig, eps: float):
-    """The fused QK-norm prologue alone: (q_scaled, k_norm, guard maxima)."""
+def _rot_args(rotary):
+    if rotary is None:
+        return None, None, 0
+    cos, sin = rotary
+    return cos.data_ptr(), sin.data_ptr(), cos.shape[0]
+
+
+def qknorm_attn_prepare(q, k, v, gain_q, gain_k, sink, cfg: L.AttnConfig, eps: float, rotary=None):
+    """The fused QK-norm (-> rotary) prologue alone: (q_scaled, k_norm, guard maxima).
+    ``rotary``: None or (cos, sin), contiguous fp32 (>= T, 32) on q's device."""
     B, H, T, D = q.shape
     q_s = torch.empty_like(q)
     k_n = torch.empty_like(k)
     guard = torch.empty(4, dtype=torch.float32, device=q.device)
     sp = sink.data_ptr() if sink is not None else None
     L.check(L.lib().algx_qknorm_attn_prepare(cfg, q.data_ptr(), k.data_ptr(), v.data_ptr(), gain_q.data_ptr(),
-                                             gain_k.data_ptr(), sp, q_s.data_ptr(), k_n.data_ptr(),
-                                             guard.data_ptr(), B, H, T, D, L.dtype_code(q.dtype), float(eps),
-                                             L.stream_of(q)), "algx_qknorm_attn_prepare")
+                                             gain_k.data_ptr(), *_rot_args(rotary), sp, q_s.data_ptr(),
+                                             k_n.data_ptr(), guard.data_ptr(), B, H, T, D, L.dtype_code(q.dtype),
+                                             float(eps), L.stream_of(q)), "algx_qknorm_attn_prepare")
     return q_s, k_n, guard
 
 
-def attn_forward_qknorm(q, k, v, gain_q, gain_k, sink, cfg: L.AttnConfig, eps: float):
+def attn_forward_qknorm(q, k, v, gain_q, gain_k, sink, cfg: L.AttnConfig, eps: float, rotary=None):
     """Forward launch group with the fused QK-norm prologue: attention of
-    (rms_norm(q) * gain_q, rms_norm(k) * gain_k, v) with the QK norm, the
-    scale fold and the guard maxima in one launch; returns (o, saved)."""
-    q_s, k_n, guard = qknorm_attn_prepare(q, k, v, gain_q, gain_k, sink, cfg, eps)
+    (rms_norm(q) * gain_q, rms_norm(k) * gain_k, v), rotated by ``rotary``
+    when given, with the QK norm, the rotation, the scale fold and the guard
+    maxima in one launch; returns (o, saved)."""
+    q_s, k_n, guard = qknorm_attn_prepare(q, k, v, gain_q, gain_k, sink, cfg, eps, rotary)
     return attn_forward_prepared(q_s, k_n, v, sink, guard, cfg)
 
 
@@ -138,7 +147,8 @@ def attn_backward(saved, cfg: L.AttnConfig, do, workspace=None):
     return dq, dk, dv, dsink
 
 
-def qknorm_attn_backward(q, k, gain_q, gain_k, saved, cfg: L.AttnConfig, do, eps: float, workspace=None):
+def qknorm_attn_backward(q, k, gain_q, gain_k, saved, cfg: L.AttnConfig, do, eps: float, workspace=None,
+                         rotary=None):
     """Backward launch group of :func:`attn_forward_qknorm`: the attention
     backward and the QK-norm backward of q and k with the latter fused into
     one epilogue launch; returns (dq, dk, dv, dgain_q, dgain_k, dsink) with
@@ -156,7 +166,7 @@ def qknorm_attn_backward(q, k, gain_q, gain_k, saved, cfg: L.AttnConfig, do, eps
     if workspace is None or workspace.numel() < nbytes:
         workspace = torch.empty(nbytes, dtype=torch.uint8, device=q_s.device)
     L.check(L.lib().algx_qknorm_attn_bwd(cfg, q.data_ptr(), k.data_ptr(), gain_q.data_ptr(), gain_k.data_ptr(),
-                                         q_s.data_ptr(), k_n.data_ptr(), v.data_ptr(), L.ptr(sink), guard.data_ptr(),
+                                         *_rot_args(rotary), q_s.data_ptr(), k_n.data_ptr(), v.data_ptr(), L.ptr(sink), guard.data_ptr(),
                                          o.data_ptr(), L.ptr(o_prec), stat.data_ptr(), do.data_ptr(), dq.data_ptr(),
                                          dk.data_ptr(), dv.data_ptr(), dgq.data_ptr(), dgk.data_ptr(), L.ptr(dsink),
                                          B, H, T, D, L.dtype_code(q_s.dtype), float(eps), workspace.data_ptr(),
@@ -284,32 +294,51 @@ def _checked_call(q, k, v, sink_logit, kind, var, c, range_guard):
 
 class _QKNormFlash(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v, gain_q, gain_k, sink, cfg: L.AttnConfig, eps: float):
-        o, saved = attn_forward_qknorm(q, k, v, gain_q, gain_k, sink, cfg, eps)
-        ctx.cfg, ctx.eps = cfg, eps
+    def forward(ctx, q, k, v, gain_q, gain_k, sink, cfg: L.AttnConfig, eps: float, rotary):
+        o, saved = attn_forward_qknorm(q, k, v, gain_q, gain_k, sink, cfg, eps, rotary)
+        ctx.cfg, ctx.eps, ctx.rotary = cfg, eps, rotary
         ctx.save_for_backward(q, k, gain_q, gain_k, *saved)
         return o
 
     @staticmethod
     def backward(ctx, do):
         q, k, gain_q, gain_k, *saved = ctx.saved_tensors
-        dxq, dxk, dv, dgq, dgk, dsink = qknorm_attn_backward(q, k, gain_q, gain_k, saved, ctx.cfg, do, ctx.eps)
-        return dxq, dxk, dv, dgq, dgk, dsink, None, None
+        dxq, dxk, dv, dgq, dgk, dsink = qknorm_attn_backward(q, k, gain_q, gain_k, saved, ctx.cfg, do, ctx.eps,
+                                                             rotary=ctx.rotary)
+        return dxq, dxk, dv, dgq, dgk, dsink, None, None, None
 
 
 def qknorm_flash_attention(q, k, v, gain_q, gain_k, sink_logit=None, *, eps: float = 1e-5,
                            kind: str = "asinh", n: int = 16, c: float = 16.0, block: int = 512,
                            range_guard: bool = False, shift: Optional[bool] = None,
-                           fast_rho: Optional[bool] = None, inv_stat: Optional[bool] = None):
-    """``flash_attention(qk_rms_norm(q, gain_q, eps), qk_rms_norm(k, gain_k, eps), v, sink_logit, ...)``
-    with the QK norm, the scale fold and the range-guard maxima fused into one
-    prologue launch (model.py:170-174; no rotary in between). Same values and
-    gradients (q, k, v, both gains and the sink) as the two calls composed;
-    the reference has no fused entry of this kind.
+                           fast_rho: Optional[bool] = None, inv_stat: Optional[bool] = None, rotary=None):
+    """``flash_attention(rot(qk_rms_norm(q, gain_q, eps)), rot(qk_rms_norm(k, gain_k, eps)), v, sink_logit, ...)``
+    with the QK norm, the rotation, the scale fold and the range-guard maxima
+    fused into one prologue launch (model.py:170-174), and the QK-norm (and
+    rotation) backward fused into one epilogue launch after the attention
+    backward. ``rotary``: None (no rotation) or the (cos, sin) tables of
+    ``apply_rotary`` (algebraic.py:172-179), each (>= T, 32); they are constants
+    (no gradient). Same values and gradients (q, k, v, both gains and the sink)
+    as the calls composed; the reference has no fused entry of this kind.
     """
     cfg, sink, gq, gk = qknorm_call_args(q, k, v, gain_q, gain_k, sink_logit, eps, kind, n, c, block, range_guard,
                                          shift, fast_rho, inv_stat)
-    return _QKNormFlash.apply(q.contiguous(), k.contiguous(), v.contiguous(), gq, gk, sink, cfg, float(eps))
+    rot = rotary_tables(rotary, q)
+    return _QKNormFlash.apply(q.contiguous(), k.contiguous(), v.contiguous(), gq, gk, sink, cfg, float(eps), rot)
+
+
+def rotary_tables(rotary, q):
+    """Validate (cos, sin) rotary tables for q (B, H, T, 64): fp32, contiguous, on q's device."""
+    if rotary is None:
+        return None
+    cos, sin = rotary
+    T, D = q.shape[-2], q.shape[-1]
+    cos = torch.as_tensor(cos).to(device=q.device, dtype=torch.float32).contiguous()
+    sin = torch.as_tensor(sin).to(device=q.device, dtype=torch.float32).contiguous()
+    if cos.ndim != 2 or cos.shape != sin.shape or cos.shape[1] != D // 2 or cos.shape[0] < T:
+        raise ValueError(f"rotary tables must both have shape (>= {T}, {D // 2}), got {tuple(cos.shape)} and "
+                         f"{tuple(sin.shape)}")
+    return cos, sin
 
 
 def qknorm_call_args(q, k, v, gain_q, gain_k, sink_logit, eps, kind, n, c, block, range_guard, shift, fast_rho,

@@ -119,30 +119,31 @@ def sum_shared_grads(grads, group=None):
 
 class _ShardedQKNormFlash(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, q, k, v, gain_q, gain_k, sink, cfg, eps, group, sum_sink):
-        q_s, k_n, guard = F.qknorm_attn_prepare(q, k, v, gain_q, gain_k, sink, cfg, eps)
+    def forward(ctx, q, k, v, gain_q, gain_k, sink, cfg, eps, group, sum_sink, rotary):
+        q_s, k_n, guard = F.qknorm_attn_prepare(q, k, v, gain_q, gain_k, sink, cfg, eps, rotary)
         combine_guard(guard, group)
         o, saved = F.attn_forward_prepared(q_s, k_n, v, sink, guard, cfg)
-        ctx.cfg, ctx.eps, ctx.group, ctx.sum_sink = cfg, eps, group, sum_sink
+        ctx.cfg, ctx.eps, ctx.group, ctx.sum_sink, ctx.rotary = cfg, eps, group, sum_sink, rotary
         ctx.save_for_backward(q, k, gain_q, gain_k, *saved)
         return o
 
     @staticmethod
     def backward(ctx, do):
         q, k, gain_q, gain_k, *saved = ctx.saved_tensors
-        dxq, dxk, dv, dgq, dgk, dsink = F.qknorm_attn_backward(q, k, gain_q, gain_k, saved, ctx.cfg, do, ctx.eps)
+        dxq, dxk, dv, dgq, dgk, dsink = F.qknorm_attn_backward(q, k, gain_q, gain_k, saved, ctx.cfg, do, ctx.eps,
+                                                               rotary=ctx.rotary)
         shared = [dgq, dgk] + ([dsink] if ctx.sum_sink and dsink is not None else [])
         shared = sum_shared_grads(shared, ctx.group)
         dgq, dgk = shared[0], shared[1]
         if ctx.sum_sink and dsink is not None:
             dsink = shared[2]
-        return dxq, dxk, dv, dgq, dgk, dsink, None, None, None, None
+        return dxq, dxk, dv, dgq, dgk, dsink, None, None, None, None, None
 
 
 def sharded_qknorm_flash_attention(q, k, v, gain_q, gain_k, sink_logit=None, *, shard: str = "batch",
                                    group=None, eps: float = 1e-5, kind: str = "asinh", n: int = 16,
                                    c: float = 16.0, block: int = 512, range_guard: bool = False, shift=None,
-                                   fast_rho=None, inv_stat=None):
+                                   fast_rho=None, inv_stat=None, rotary=None):
     """``qknorm_flash_attention`` on this rank's slice of one logical batch.
 
     ``shard="batch"``: every rank holds some of the sequences with all heads,
@@ -158,4 +159,4 @@ def sharded_qknorm_flash_attention(q, k, v, gain_q, gain_k, sink_logit=None, *, 
     cfg, sink, gq, gk = F.qknorm_call_args(q, k, v, gain_q, gain_k, sink_logit, eps, kind, n, c, block, range_guard,
                                            shift, fast_rho, inv_stat)
     return _ShardedQKNormFlash.apply(q.contiguous(), k.contiguous(), v.contiguous(), gq, gk, sink, cfg, float(eps),
-                                     group, shard == "batch")
+                                     group, shard == "batch", F.rotary_tables(rotary, q))

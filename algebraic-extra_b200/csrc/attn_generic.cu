@@ -87,11 +87,38 @@ __global__ void __launch_bounds__(kPrepThreads) attn_prepare_kernel(const T* __r
 // rounding points as the separate launches: y = bf16((x * tau) * gain), then
 // q_scaled = bf16(y * scale); the guard maxima are taken over the rounded
 // q_scaled and normalised k rows, and over v and the sink as in prepare.
-template <typename T>
+// Rotate-half rotation of one D = 64 row by the (T, 32) tables cos, sin
+// (algebraic.py:172-179): y1 = x1 c - x2 s, y2 = x1 s + x2 c, with the table
+// entries rounded to the I/O dtype first and the products and sum taken in
+// fp32 (no contraction), rounded once. INVERSE applies the transpose
+// (dx1 = dy1 c + dy2 s, dx2 = dy2 c - dy1 s), the rotation's VJP. The thread
+// holding elements j.. of one half swaps values with the thread holding j + 32
+// of the other (lane ^ TPR/2), so every lane of the warp must call it.
+template <typename T, bool INVERSE>
+__device__ __forceinline__ void rotate_half(float (&x)[Vec<T>::N], const float* __restrict__ cosv,
+                                            const float* __restrict__ sinv, int64_t t, int sub) {
+  using V = Vec<T>;
+  constexpr int kHalfT = V::TPR / 2;
+  const bool first = sub < kHalfT;
+  const int j0 = (sub % kHalfT) * V::N;
+  const float* cr = cosv + t * (kD / 2) + j0;
+  const float* sr = sinv + t * (kD / 2) + j0;
+#pragma unroll
+  for (int i = 0; i < V::N; ++i) {
+    const float other = __shfl_xor_sync(0xffffffffu, x[i], kHalfT);
+    const float c = round_io<T>(cr[i]), s = round_io<T>(sr[i]);
+    const float own_c = __fmul_rn(x[i], c), other_s = __fmul_rn(other, s);
+    const bool minus = INVERSE ? !first : first;  // own * c - other * s, else own * c + other * s
+    x[i] = round_io<T>(minus ? __fsub_rn(own_c, other_s) : __fadd_rn(own_c, other_s));
+  }
+}
+
+template <typename T, bool ROT>
 __global__ void __launch_bounds__(kPrepThreads) qknorm_attn_prepare_kernel(
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v, const float* __restrict__ gain_q,
-    const float* __restrict__ gain_k, const float* __restrict__ sink, int H, T* __restrict__ qs,
-    T* __restrict__ kn, float* guard, int64_t rows, float scale, float eps) {
+    const float* __restrict__ gain_k, const float* __restrict__ rot_cos, const float* __restrict__ rot_sin,
+    const float* __restrict__ sink, int H, int T_, T* __restrict__ qs, T* __restrict__ kn, float* guard,
+    int64_t rows, float scale, float eps) {
   using V = Vec<T>;
   constexpr int kUnroll = 4;
   const int which = blockIdx.y;  // 0: q (normalised, scaled, written), 1: k (normalised, written), 2: v
@@ -132,6 +159,7 @@ __global__ void __launch_bounds__(kPrepThreads) qknorm_attn_prepare_kernel(
       const float tau = rsqrtf(ss * (1.0f / kD) + eps);
 #pragma unroll
       for (int i = 0; i < V::N; ++i) x[i] = round_io<T>((x[i] * tau) * g[i]);
+      if constexpr (ROT) rotate_half<T, false>(x, rot_cos, rot_sin, row % T_, sub);
       if (which == 0) {
 #pragma unroll
         for (int i = 0; i < V::N; ++i) x[i] = round_io<T>(x[i] * scale);
@@ -621,7 +649,8 @@ constexpr int kEpiUnroll = 4;
 // that enough bytes are in flight to keep HBM busy at one CTA per SM.
 template <typename T, bool FROM_ACC>
 __device__ __forceinline__ void qk_rows_bwd(const T* __restrict__ x, const float* __restrict__ gain, T* dxy,
-                                            const float* __restrict__ acc, float f, int64_t rows, float eps,
+                                            const float* __restrict__ acc, float f, const float* __restrict__ rot_cos,
+                                            const float* __restrict__ rot_sin, int T_, int64_t rows, float eps,
                                             float (&part)[Vec<T>::N]) {
   using V = Vec<T>;
   constexpr int kA = FROM_ACC ? V::N / 4 : 1;  // 16-byte chunks of fp32 accumulator per thread and row
@@ -662,6 +691,7 @@ __device__ __forceinline__ void qk_rows_bwd(const T* __restrict__ x, const float
       } else {
         unpack<T>(rd[u][0], dv);
       }
+      if (rot_cos) rotate_half<T, true>(dv, rot_cos, rot_sin, row % T_, sub);
       float ss = 0.f, sdg = 0.f;
 #pragma unroll
       for (int i = 0; i < V::N; ++i) {
@@ -687,8 +717,9 @@ template <typename T>
 __global__ void __launch_bounds__(kEpiThreads) qknorm_attn_bwd_kernel(
     algx_attn_config cfg, const float* __restrict__ guard, int fast, const float* __restrict__ dq_acc,
     const T* __restrict__ q, const float* __restrict__ gain_q, const T* __restrict__ k,
-    const float* __restrict__ gain_k, T* dq_x, T* dk_x, float* __restrict__ partial, unsigned* counter,
-    float* __restrict__ dgain_q, float* __restrict__ dgain_k, int64_t rows, float eps) {
+    const float* __restrict__ gain_k, const float* __restrict__ rot_cos, const float* __restrict__ rot_sin, int T_,
+    T* dq_x, T* dk_x, float* __restrict__ partial, unsigned* counter, float* __restrict__ dgain_q,
+    float* __restrict__ dgain_k, int64_t rows, float eps) {
   using V = Vec<T>;
   __shared__ float red[kEpiThreads / 32 * V::RPW][2 * kD];  // per row slot of a warp: q and k column sums
   __shared__ float fin[kEpiThreads / (2 * kD)][2 * kD];
@@ -698,10 +729,10 @@ __global__ void __launch_bounds__(kEpiThreads) qknorm_attn_bwd_kernel(
 #pragma unroll
   for (int i = 0; i < V::N; ++i) pq[i] = pk[i] = 0.f;
   if (use_acc)
-    qk_rows_bwd<T, true>(q, gain_q, dq_x, dq_acc, (float)cfg.n * cfg.scale, rows, eps, pq);
+    qk_rows_bwd<T, true>(q, gain_q, dq_x, dq_acc, (float)cfg.n * cfg.scale, rot_cos, rot_sin, T_, rows, eps, pq);
   else
-    qk_rows_bwd<T, false>(q, gain_q, dq_x, nullptr, 1.f, rows, eps, pq);
-  qk_rows_bwd<T, false>(k, gain_k, dk_x, nullptr, 1.f, rows, eps, pk);
+    qk_rows_bwd<T, false>(q, gain_q, dq_x, nullptr, 1.f, rot_cos, rot_sin, T_, rows, eps, pq);
+  qk_rows_bwd<T, false>(k, gain_k, dk_x, nullptr, 1.f, rot_cos, rot_sin, T_, rows, eps, pk);
   // CTA column sums: slot (warp, row-in-warp) holds its threads' columns
   const int lane = threadIdx.x & 31, sub = lane % V::TPR, rl = lane / V::TPR;
   const int slot = (threadIdx.x >> 5) * V::RPW + rl;
@@ -799,11 +830,13 @@ int algx_attn_prepare(const algx_attn_config* cfg, const void* q, const void* k,
 }
 
 int algx_qknorm_attn_prepare(const algx_attn_config* cfg, const void* q, const void* k, const void* v,
-                             const float* gain_q, const float* gain_k, const float* sink, void* q_scaled,
-                             void* k_norm, float* guard, int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype,
-                             float eps, void* stream) {
+                             const float* gain_q, const float* gain_k, const float* rope_cos, const float* rope_sin,
+                             int64_t rope_rows, const float* sink, void* q_scaled, void* k_norm, float* guard,
+                             int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype, float eps, void* stream) {
   if (int s = check_attn(cfg, B, H, T, D, dtype)) return s;
   ALGX_REQUIRE(q && k && v && gain_q && gain_k && q_scaled && k_norm && guard, "qknorm_attn_prepare: NULL pointer");
+  ALGX_REQUIRE((rope_cos == nullptr) == (rope_sin == nullptr), "qknorm_attn_prepare: give both rotary tables or none");
+  ALGX_REQUIRE(!rope_cos || rope_rows >= T, "qknorm_attn_prepare: rotary tables need at least T rows");
   ALGX_REQUIRE(!cfg->has_sink || sink, "qknorm_attn_prepare: has_sink without a sink pointer");
   ALGX_REQUIRE(eps > 0.f, "qknorm_attn_prepare: eps must be positive");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -813,14 +846,17 @@ int algx_qknorm_attn_prepare(const algx_attn_config* cfg, const void* q, const v
   const int gx = (int)std::min<int64_t>((rows + rows_per_block - 1) / rows_per_block, 148 * 8);
   dim3 grid(gx, 3);
   const float* sk = cfg->has_sink ? sink : nullptr;
+  auto launch = [&](auto kern, auto tag) {
+    using TT = decltype(tag);
+    kern<<<grid, kPrepThreads, 0, st>>>((const TT*)q, (const TT*)k, (const TT*)v, gain_q, gain_k, rope_cos, rope_sin,
+                                        sk, (int)H, (int)T, (TT*)q_scaled, (TT*)k_norm, guard, rows, cfg->scale, eps);
+  };
   if (dtype == ALGX_BF16)
-    qknorm_attn_prepare_kernel<__nv_bfloat16><<<grid, kPrepThreads, 0, st>>>(
-        (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, gain_q, gain_k, sk, (int)H,
-        (__nv_bfloat16*)q_scaled, (__nv_bfloat16*)k_norm, guard, rows, cfg->scale, eps);
+    rope_cos ? launch(qknorm_attn_prepare_kernel<__nv_bfloat16, true>, __nv_bfloat16{})
+             : launch(qknorm_attn_prepare_kernel<__nv_bfloat16, false>, __nv_bfloat16{});
   else
-    qknorm_attn_prepare_kernel<float><<<grid, kPrepThreads, 0, st>>>(
-        (const float*)q, (const float*)k, (const float*)v, gain_q, gain_k, sk, (int)H, (float*)q_scaled,
-        (float*)k_norm, guard, rows, cfg->scale, eps);
+    rope_cos ? launch(qknorm_attn_prepare_kernel<float, true>, float{})
+             : launch(qknorm_attn_prepare_kernel<float, false>, float{});
   ALGX_LAUNCHED("qknorm_attn_prepare launch");
   return ALGX_OK;
 }
@@ -956,7 +992,8 @@ size_t algx_qknorm_attn_bwd_workspace_size(int64_t B, int64_t H, int64_t T, int6
 }
 
 int algx_qknorm_attn_bwd(const algx_attn_config* cfg, const void* q, const void* k, const float* gain_q,
-                         const float* gain_k, const void* q_scaled, const void* k_norm, const void* v,
+                         const float* gain_k, const float* rope_cos, const float* rope_sin, int64_t rope_rows,
+                         const void* q_scaled, const void* k_norm, const void* v,
                          const float* sink, const float* guard, const void* o, const float* o_precise,
                          const float* stat, const void* dout, void* dq, void* dk, void* dv, float* dgain_q,
                          float* dgain_k, float* dsink, int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype,
@@ -967,6 +1004,8 @@ int algx_qknorm_attn_bwd(const algx_attn_config* cfg, const void* q, const void*
                "qknorm_attn_bwd: NULL pointer");
   ALGX_REQUIRE(!cfg->has_sink || (sink && dsink), "qknorm_attn_bwd: has_sink needs sink and dsink");
   ALGX_REQUIRE(eps > 0.f, "qknorm_attn_bwd: epsilon must be positive");
+  ALGX_REQUIRE((rope_cos == nullptr) == (rope_sin == nullptr), "qknorm_attn_bwd: give both rotary tables or none");
+  ALGX_REQUIRE(!rope_cos || rope_rows >= T, "qknorm_attn_bwd: rotary tables need at least T rows");
   ALGX_REQUIRE(workspace && workspace_bytes >= algx_qknorm_attn_bwd_workspace_size(B, H, T, D),
                "qknorm_attn_bwd: workspace too small (see algx_qknorm_attn_bwd_workspace_size)");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -987,12 +1026,12 @@ int algx_qknorm_attn_bwd(const algx_attn_config* cfg, const void* q, const void*
   const int64_t rows = B * H * T;
   if (dtype == ALGX_BF16)
     qknorm_attn_bwd_kernel<__nv_bfloat16><<<kEpiBlocks, kEpiThreads, 0, st>>>(
-        *cfg, guard, fast ? 1 : 0, acc, (const __nv_bfloat16*)q, gain_q, (const __nv_bfloat16*)k, gain_k,
-        (__nv_bfloat16*)dq, (__nv_bfloat16*)dk, partial, counter, dgain_q, dgain_k, rows, eps);
+        *cfg, guard, fast ? 1 : 0, acc, (const __nv_bfloat16*)q, gain_q, (const __nv_bfloat16*)k, gain_k, rope_cos,
+        rope_sin, (int)T, (__nv_bfloat16*)dq, (__nv_bfloat16*)dk, partial, counter, dgain_q, dgain_k, rows, eps);
   else
     qknorm_attn_bwd_kernel<float><<<kEpiBlocks, kEpiThreads, 0, st>>>(
-        *cfg, guard, 0, acc, (const float*)q, gain_q, (const float*)k, gain_k, (float*)dq, (float*)dk, partial,
-        counter, dgain_q, dgain_k, rows, eps);
+        *cfg, guard, 0, acc, (const float*)q, gain_q, (const float*)k, gain_k, rope_cos, rope_sin, (int)T,
+        (float*)dq, (float*)dk, partial, counter, dgain_q, dgain_k, rows, eps);
   ALGX_LAUNCHED("qknorm_attn_bwd launch");
   return ALGX_OK;
 }

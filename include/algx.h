@@ -112,11 +112,15 @@ ALGX_API int algx_attn_prepare(const algx_attn_config* cfg, const void* q, const
  * algx_attn_prepare, in one pass. k_norm = round(rmsnorm(k) * gain_k) and
  * q_scaled = round(round(rmsnorm(q) * gain_q) * scale) are bit-identical to
  * algx_qknorm_fwd on q and k followed by algx_attn_prepare; guard as there.
- * Replaces the model's qk-norm -> flash_attention prologue (model.py:170-174,
- * qk_norm.py:29-43, flash.py:823-849); no rotary is applied (the attention
- * block benchmarked at B8 H12 S2048 has none). */
+ * Replaces the model's qk-norm -> rotary -> flash_attention prologue
+ * (model.py:170-174, qk_norm.py:29-43, algebraic.py:172-179,
+ * flash.py:823-849). rope_cos, rope_sin: NULL (no rotary) or (rope_rows >= T,
+ * 32) fp32 tables, row t for position t (RoPE, standard.py:16-21, or Cayley,
+ * algebraic.py:124-169); the rotation runs between the norm and the scale
+ * fold, rounded to the I/O dtype once. */
 ALGX_API int algx_qknorm_attn_prepare(const algx_attn_config* cfg, const void* q, const void* k,
                                       const void* v, const float* gain_q, const float* gain_k,
+                                      const float* rope_cos, const float* rope_sin, int64_t rope_rows,
                                       const float* sink, void* q_scaled, void* k_norm, float* guard,
                                       int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype, float eps,
                                       void* stream);
@@ -149,7 +153,9 @@ ALGX_API size_t algx_qknorm_attn_bwd_workspace_size(int64_t B, int64_t H, int64_
  * algx_qknorm_attn_prepare: the attention backward of algx_attn_bwd on
  * (q_scaled, k_norm) followed by the QK RMS norm backward of q and k
  * (kernels/qk_norm.py:45-56) in one launch group. dq, dk receive d/dq and
- * d/dk of the raw (pre-norm) q, k; dgain_q, dgain_k (64,) fp32 the gain
+ * d/dk of the raw (pre-norm) q, k (through the inverse rotation when
+ * rope_cos, rope_sin are given, as in algx_qknorm_attn_prepare); dgain_q,
+ * dgain_k (64,) fp32 the gain
  * gradients; dv and dsink as algx_attn_bwd. dk equals, bit for bit,
  * algx_attn_bwd followed by algx_qknorm_bwd, and so does dq up to the order
  * of the fast path's dQ reduce-adds (which varies between any two calls);
@@ -157,7 +163,8 @@ ALGX_API size_t algx_qknorm_attn_bwd_workspace_size(int64_t B, int64_t H, int64_
  * flash_attention prologue (model.py:170-174: qk_norm.py:45-56 after
  * flash.py:630-642). */
 ALGX_API int algx_qknorm_attn_bwd(const algx_attn_config* cfg, const void* q, const void* k, const float* gain_q,
-                  const float* gain_k, const void* q_scaled, const void* k_norm, const void* v,
+                  const float* gain_k, const float* rope_cos, const float* rope_sin, int64_t rope_rows,
+                  const void* q_scaled, const void* k_norm, const void* v,
                   const float* sink, const float* guard, const void* o, const float* o_precise,
                   const float* stat, const void* dout, void* dq, void* dk, void* dv, float* dgain_q,
                   float* dgain_k, float* dsink, int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype,

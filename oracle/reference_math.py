@@ -161,6 +161,73 @@ def qk_norm_backward(x: torch.Tensor, gain: torch.Tensor, dy: torch.Tensor, eps:
 
 
 # ---------------------------------------------------------------------------
+# rotary position tables (model.py:128-134) and the rotation (model.py:173-174)
+# ---------------------------------------------------------------------------
+
+def rope_table(head_dim: int, seq_len: int, base: float = 10000.0, dtype=torch.float32):
+    """Trigonometric RoPE tables (standard.py:16-21): theta_i = base^(-i/half),
+    angle = t * theta_i, all in ``dtype`` (the reference uses float32)."""
+    half = head_dim // 2
+    theta = 1.0 / (torch.tensor(base, dtype=dtype) ** (torch.arange(half, dtype=dtype) / half))
+    angles = torch.arange(seq_len, dtype=dtype)[:, None] * theta[None, :]
+    return torch.cos(angles), torch.sin(angles)
+
+
+def cayley_powers(w: torch.Tensor, seq_len: int):
+    """Rows ((1 + i w)^2 / (1 + w^2))^m for m < seq_len (algebraic.py:124-149):
+    binary exponentiation over the bits of m with a renormalised squaring per
+    bit, then a final renormalisation; in the dtype of ``w``."""
+    w2 = w * w
+    c = (1.0 - w2) / (1.0 + w2)
+    s = (2.0 * w) / (1.0 + w2)
+    positions = torch.arange(seq_len)
+    out_c = torch.ones((seq_len, w.shape[0]), dtype=w.dtype)
+    out_s = torch.zeros((seq_len, w.shape[0]), dtype=w.dtype)
+    bit = 0
+    while (1 << bit) < seq_len:
+        take = ((positions >> bit) & 1).bool()[:, None]
+        new_c = out_c * c - out_s * s
+        new_s = out_c * s + out_s * c
+        out_c = torch.where(take, new_c, out_c)
+        out_s = torch.where(take, new_s, out_s)
+        c, s = c * c - s * s, 2.0 * c * s
+        inv = torch.rsqrt(c * c + s * s)
+        c, s = c * inv, s * inv
+        bit += 1
+    inv = torch.rsqrt(out_c * out_c + out_s * out_s)
+    return out_c * inv, out_s * inv
+
+
+def cayley_table_geometric(head_dim: int, seq_len: int, base: float = 10000.0, w0: float = 0.5,
+                           fraction: float = 1.0, dtype=torch.float32):
+    """Geometric Cayley grid w_k = w0 * base^(-k/half) (algebraic.py:152-169)."""
+    half = head_dim // 2
+    levels = int(round(math.log2(half)))
+    if 1 << levels != half:
+        raise ValueError("geometric Cayley grid needs head_dim/2 to be a power of two")
+    ratio = 1.0 / root(base, half)
+    active = int(round(fraction * half))
+    w = torch.tensor([w0 * ratio ** i if i < active else 0.0 for i in range(half)], dtype=dtype)
+    return cayley_powers(w, seq_len)
+
+
+def apply_rotary(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor,
+                 io_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """Rotate-half rotation of (..., T, D) by (>= T, D/2) tables (algebraic.py:172-179).
+
+    With ``io_dtype`` the tables are first rounded to it (``cos.astype(x.dtype)``)
+    and the rotated value is rounded to it once, the arithmetic in between
+    staying in x's (wider) dtype.
+    """
+    half = x.shape[-1] // 2
+    t = x.shape[-2]
+    c = _round(cos[:t].to(x.dtype), io_dtype)
+    s = _round(sin[:t].to(x.dtype), io_dtype)
+    x1, x2 = x[..., :half], x[..., half:]
+    return _round(torch.cat([x1 * c - x2 * s, x1 * s + x2 * c], dim=-1), io_dtype)
+
+
+# ---------------------------------------------------------------------------
 # attention
 # ---------------------------------------------------------------------------
 

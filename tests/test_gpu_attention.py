@@ -400,3 +400,77 @@ def test_sharded_qknorm_attention_one_rank_matches_single():
     assert torch.equal(outs[0][0], outs[1][0])
     for a, b in zip(outs[0][1], outs[1][1]):
         assert rel_l2(a, b) < 1e-2
+
+
+def _torch_rotary(x, cos, sin):
+    """The fused prologue's rotation restated with torch ops: tables rounded to
+    x's dtype, products and sums in fp32 (separate roundings), one rounding back."""
+    half = x.shape[-1] // 2
+    t = x.shape[-2]
+    c = cos[:t].to(x.dtype).float()
+    s = sin[:t].to(x.dtype).float()
+    x1, x2 = x[..., :half].float(), x[..., half:].float()
+    return torch.cat([x1 * c - x2 * s, x1 * s + x2 * c], dim=-1).to(x.dtype)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("table", ["rope", "cayley"])
+@pytest.mark.parametrize("with_sink", [False, True])
+def test_fused_rotary_prologue_matches_composed(dtype, table, with_sink):
+    """qknorm_flash_attention(rotary=...) == flash_attention(rot(qk_rms_norm(q)), rot(qk_rms_norm(k)), v)
+    (model.py:170-174): the output bit for bit; gradients up to the order of the dQ reduce-adds."""
+    from algx import rotary as P
+    from algx.kernels.flash import qknorm_flash_attention
+    from algx.kernels.qk_norm import qk_rms_norm
+    B, H, T, D = 2, 3, 512, 64
+    q, k, v, do = (_randn(110 + i, (B, H, T, D), dtype) for i in range(4))
+    gq0, gk0 = 1 + 0.02 * _randn(115, (64,)), 1 + 0.02 * _randn(116, (64,))
+    sink0 = _randn(117, (H,)) if with_sink else None
+    tabs = P.rope_table(64, 640) if table == "rope" else P.cayley_table_geometric(64, 640)
+    tabs = tuple(t.cuda() for t in tabs)
+
+    def run(fused):
+        leaves = [t.cuda().requires_grad_(True) for t in (q, k, v)]
+        gains = [g.cuda().requires_grad_(True) for g in (gq0, gk0)]
+        sink = sink0.cuda().requires_grad_(True) if with_sink else None
+        opts = dict(kind="asinh", n=16, c=8., range_guard=True)
+        if fused:
+            o = qknorm_flash_attention(*leaves, *gains, sink, eps=1e-5, rotary=tabs, **opts)
+        else:
+            rq = _torch_rotary(qk_rms_norm(leaves[0], gains[0]), *tabs)
+            rk = _torch_rotary(qk_rms_norm(leaves[1], gains[1]), *tabs)
+            o = flash_attention(rq, rk, leaves[2], sink, **opts)
+        torch.sum(o.float() * do.cuda().float()).backward()
+        return o.detach(), [t.grad for t in leaves + gains] + ([sink.grad] if with_sink else [])
+
+    o_f, g_f = run(True)
+    o_c, g_c = run(False)
+    assert torch.equal(o_f, o_c)
+    lim = 1e-2 if dtype == torch.bfloat16 else 1e-5
+    for a, b in zip(g_f, g_c):
+        assert rel_l2(a, b) < lim
+
+
+@pytest.mark.parametrize("dtype,tol", [(torch.float32, 1e-3), (torch.bfloat16, 2e-2)])
+def test_fused_rotary_attention_vs_oracle(dtype, tol):
+    """QK-norm -> RoPE -> guarded asinh attention against the float64 oracle
+    (rms_norm, apply_rotary, flash_attention of oracle/reference_math.py)."""
+    from algx import rotary as P
+    from algx.kernels.flash import qknorm_flash_attention
+    B, H, T, D = 1, 2, 256, 64
+    q, k, v, do = (_randn(120 + i, (B, H, T, D), dtype) for i in range(4))
+    gq0 = 1 + 0.02 * _randn(125, (64,))
+    gk0 = 1 + 0.02 * _randn(126, (64,))
+    cos, sin = P.rope_table(64, T)
+    leaves = [t.cuda().requires_grad_(True) for t in (q, k, v, gq0, gk0)]
+    o = qknorm_flash_attention(*leaves, kind="asinh", n=16, c=8., range_guard=True, rotary=(cos.cuda(), sin.cuda()))
+    torch.sum(o.float() * do.cuda().float()).backward()
+    io = None if dtype == torch.float32 else dtype
+    ref = [t.double().requires_grad_(True) for t in (q, k, v, gq0, gk0)]
+    rq = R.apply_rotary(R.rms_norm(ref[0], ref[3], 1e-5, io), cos.double(), sin.double(), io)
+    rk = R.apply_rotary(R.rms_norm(ref[1], ref[4], 1e-5, io), cos.double(), sin.double(), io)
+    ro = R.flash_attention(rq, rk, ref[2], kind="asinh", n=16, c=8., range_guard=True, io_dtype=io)
+    torch.sum(ro * do.double()).backward()
+    assert rel_l2(o.detach(), ro.detach()) < tol
+    for a, b in zip(leaves, ref):
+        assert rel_l2(a.grad, b.grad) < tol

@@ -76,3 +76,35 @@ def test_clipped_vjp_is_zero_above_cap():
 
     _, dq, dk, _, ds = R.attention_grads(fn, q, q.clone(), v, g, sink)
     assert torch.all(dq == 0) and torch.all(dk == 0) and torch.all(ds == 0)
+
+
+def test_cayley_powers_closed_form():
+    """((1 + i w)^2 / (1 + w^2))^m = exp(2 i m atan w): the binary exponentiation of
+    algebraic.py:124-149 (float64 here) against the closed form."""
+    w = torch.tensor([0.5, 0.1, 0.003, 0.0], dtype=torch.float64)
+    c, s = R.cayley_powers(w, 2048)
+    ang = 2 * torch.arange(2048, dtype=torch.float64)[:, None] * torch.atan(w)[None, :]
+    assert torch.allclose(c, torch.cos(ang), atol=1e-11) and torch.allclose(s, torch.sin(ang), atol=1e-11)
+
+
+def test_rotary_is_a_rotation():
+    """apply_rotary keeps row norms and its transpose undoes it (the VJP the fused epilogue applies)."""
+    g = torch.Generator().manual_seed(3)
+    x = torch.randn((2, 3, 64, 64), generator=g, dtype=torch.float64)
+    cos, sin = R.rope_table(64, 80, dtype=torch.float64)
+    y = R.apply_rotary(x, cos, sin)
+    assert torch.allclose(y.norm(dim=-1), x.norm(dim=-1), rtol=1e-12)
+    back = R.apply_rotary(y, cos, -sin)
+    assert torch.allclose(back, x, atol=1e-12)
+
+
+def test_product_tables_match_oracle():
+    """algx.rotary builds the same fp32 tables as the oracle's restatement."""
+    from algx import rotary as P
+    for got, want in ((P.rope_table(64, 2048), R.rope_table(64, 2048)),
+                      (P.cayley_table_geometric(64, 2048), R.cayley_table_geometric(64, 2048)),
+                      (P.cayley_table_geometric(64, 512, fraction=0.5), R.cayley_table_geometric(64, 512,
+                                                                                                 fraction=0.5))):
+        for a, b in zip(got, want):
+            assert a.dtype == torch.float32 and a.shape == b.shape
+            assert torch.allclose(a, b, atol=2e-6, rtol=0)
