@@ -320,6 +320,10 @@ __global__ void __launch_bounds__(kRows) attn_fwd_generic(algx_attn_config cfg, 
                                                           const float* __restrict__ guard, T* __restrict__ o,
                                                           float* __restrict__ o_prec, float* __restrict__ stat,
                                                           int H, int T_, int branch_mask, int BH) {
+  // As the fast path's fallback this kernel may start before the fast kernel
+  // ends (launch_dependent): wait for it, then let the next launch go.
+  pdl_wait();
+  pdl_trigger();
   const Eff e = resolve_variant(cfg, guard);
   if (!((branch_mask >> e.branch) & 1)) return;
   const int nblk = (T_ + kRows - 1) / kRows;
@@ -528,6 +532,8 @@ __global__ void __launch_bounds__(kRows) attn_dkdv_generic(algx_attn_config cfg,
                                                            const float* __restrict__ di,
                                                            const float* __restrict__ guard, T* __restrict__ dk,
                                                            T* __restrict__ dv, int T_, int branch_mask, int BH) {
+  pdl_wait();  // see attn_fwd_generic
+  pdl_trigger();
   const Eff e = resolve_variant(cfg, guard);
   if (!((branch_mask >> e.branch) & 1)) return;
   const int nblk = (T_ + kRows - 1) / kRows;
@@ -607,6 +613,8 @@ __global__ void __launch_bounds__(kRows) attn_dq_generic(algx_attn_config cfg, c
                                                          const float* __restrict__ di,
                                                          const float* __restrict__ guard, T* __restrict__ dq,
                                                          int T_, int branch_mask, int BH) {
+  pdl_wait();  // see attn_fwd_generic
+  pdl_trigger();
   const Eff e = resolve_variant(cfg, guard);
   if (!((branch_mask >> e.branch) & 1)) return;
   const int nblk = (T_ + kRows - 1) / kRows;
@@ -880,7 +888,11 @@ int algx_attn_fwd(const algx_attn_config* cfg, const void* q_scaled, const void*
     mask = 1 << BR_SHIFTED | 1 << BR_SOFTMAX;
   }
   const unsigned grid = generic_grid(B * H, T, fast);
-  if (dtype == ALGX_BF16)
+  if (fast)  // only the fast path's bf16 fallback: overlaps the fast kernel's tail
+    ALGX_CUDA(launch_dependent(attn_fwd_generic<__nv_bfloat16>, grid, kRows, 0, st, *cfg,
+                               (const __nv_bfloat16*)q_scaled, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v,
+                               sink, guard, (__nv_bfloat16*)o, o_precise, stat, (int)H, (int)T, mask, (int)(B * H)));
+  else if (dtype == ALGX_BF16)
     attn_fwd_generic<__nv_bfloat16><<<grid, kRows, 0, st>>>(*cfg, (const __nv_bfloat16*)q_scaled,
                                                              (const __nv_bfloat16*)k, (const __nv_bfloat16*)v,
                                                              sink, guard, (__nv_bfloat16*)o, o_precise, stat,
@@ -953,7 +965,15 @@ static int attn_bwd_core(const algx_attn_config* cfg, const void* q_scaled, cons
     attr_set[dev][dtype] = true;
   }
   const int bh = (int)(B * H);
-  if (dtype == ALGX_BF16) {
+  if (fast) {  // only the fast path's bf16 fallback: overlaps the fast kernel's tail
+    ALGX_CUDA(launch_dependent(attn_dkdv_generic<__nv_bfloat16>, ggrid, kRows, kGenericBwdSmem, st, *cfg,
+                               (const __nv_bfloat16*)q_scaled, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v,
+                               (const __nv_bfloat16*)dout, stat, di, guard, (__nv_bfloat16*)dk, (__nv_bfloat16*)dv,
+                               (int)T, mask, bh));
+    ALGX_CUDA(launch_dependent(attn_dq_generic<__nv_bfloat16>, ggrid, kRows, kGenericBwdSmem, st, *cfg,
+                               (const __nv_bfloat16*)q_scaled, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v,
+                               (const __nv_bfloat16*)dout, stat, di, guard, (__nv_bfloat16*)dq, (int)T, mask, bh));
+  } else if (dtype == ALGX_BF16) {
     attn_dkdv_generic<__nv_bfloat16><<<ggrid, kRows, kGenericBwdSmem, st>>>(
         *cfg, (const __nv_bfloat16*)q_scaled, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v,
         (const __nv_bfloat16*)dout, stat, di, guard, (__nv_bfloat16*)dk, (__nv_bfloat16*)dv, (int)T, mask, bh);

@@ -162,6 +162,7 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
                        int H, int T, int* dev_err) {
   const Eff e = resolve_variant(cfg, guard);
   if (e.branch != BR_UNSHIFTED) return;  // the generic kernel runs the shifted fallback
+  pdl_trigger();  // the fallback kernel may be scheduled behind this grid's last blocks
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sQ = smem;
@@ -415,6 +416,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                        int BH, int T, int* dev_err) {
   const Eff e = resolve_variant(cfg, guard);
   if (e.branch != BR_UNSHIFTED) return;
+  pdl_trigger();  // the fallback kernels may be scheduled behind this grid
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sK = smem;                     // 2 buffers
@@ -882,6 +884,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 // dq = bf16(acc * n * scale), only when the fast path ran (unshifted branch).
 __global__ void dq_finish_kernel(algx_attn_config cfg, const float* __restrict__ guard,
                                  const float4* __restrict__ acc, __nv_bfloat16* __restrict__ dq, int64_t n4) {
+  pdl_trigger();  // the fallback kernels may be scheduled behind this grid
   const Eff e = resolve_variant(cfg, guard);
   if (e.branch != BR_UNSHIFTED) return;
   const float f = (float)cfg.n * cfg.scale;
