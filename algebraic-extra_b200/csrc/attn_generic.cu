@@ -341,8 +341,14 @@ __global__ void __launch_bounds__(256) attn_di_kernel(algx_attn_config cfg, cons
                                                       const T* __restrict__ o, const float* __restrict__ o_prec,
                                                       const T* __restrict__ dout, const float* __restrict__ stat,
                                                       const float* __restrict__ sink, float* __restrict__ di,
-                                                      float* __restrict__ sink_part, int H, int T_) {
+                                                      float* __restrict__ sink_part, int H, int T_,
+                                                      float* __restrict__ zero_acc, int* __restrict__ zero_tail) {
   const Eff e = resolve_variant(cfg, guard);
+  // The fast backward's fp32 dQ accumulator (zero_acc, rows of 64) and its
+  // 256-byte counter area (zero_tail) are zeroed here, alongside the o / dO
+  // reads, instead of by a separate memset; the shifted branch never reads
+  // the accumulator, the counters are used in both branches.
+  if (zero_tail && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x < 64) zero_tail[threadIdx.x] = 0;
   const int bh = blockIdx.y, h = bh % H;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = blockIdx.x * kRows;
@@ -377,21 +383,37 @@ __global__ void __launch_bounds__(256) attn_di_kernel(algx_attn_config cfg, cons
       if (lane == 0) accumulate(row, s);
     }
   } else {
-    // 128-bit row loads: Vec<T>::TPR threads per row
+    // 128-bit row loads, Vec<T>::TPR threads per row; all of a thread's rows
+    // are loaded before any is used
     using V = Vec<T>;
+    constexpr int kIt = kRows / (8 * V::RPW);
     const int sub = lane % V::TPR, rl = lane / V::TPR;
-    for (int i0 = warp * V::RPW; i0 < kRows; i0 += 8 * V::RPW) {
-      const int row = row0 + i0 + rl;
+    uint4 ro[kIt], rd[kIt];
+#pragma unroll
+    for (int it = 0; it < kIt; ++it) {
+      const int row = row0 + (warp + 8 * it) * V::RPW + rl;
       const bool ok = row < T_;
       const size_t off = ((size_t)bh * T_ + row) * kD + sub * V::N;
+      ro[it] = ok ? ld_stream(o + off) : make_uint4(0, 0, 0, 0);
+      rd[it] = ok ? ld_stream(dout + off) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int it = 0; it < kIt; ++it) {
+      const int row = row0 + (warp + 8 * it) * V::RPW + rl;
+      const bool ok = row < T_;
       float ov[V::N], dv[V::N];
-      unpack<T>(ok ? ld_stream(o + off) : make_uint4(0, 0, 0, 0), ov);
-      unpack<T>(ok ? ld_stream(dout + off) : make_uint4(0, 0, 0, 0), dv);
+      unpack<T>(ro[it], ov);
+      unpack<T>(rd[it], dv);
       float s = 0.f;
 #pragma unroll
       for (int i = 0; i < V::N; ++i) s = fmaf(dv[i], ov[i], s);
       s = row_sum<V::TPR>(s);
       if (ok && sub == 0) accumulate(row, s);
+      if (zero_acc && ok) {
+        float4* z = reinterpret_cast<float4*>(zero_acc + ((size_t)bh * T_ + row) * kD + sub * V::N);
+#pragma unroll
+        for (int c = 0; c < V::N / 4; ++c) z[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
     }
   }
 #pragma unroll
@@ -923,13 +945,18 @@ static int attn_bwd_core(const algx_attn_config* cfg, const void* q_scaled, cons
   void* tc_ws = ws + ws_off_tc(B, H, T);
   const int nblk = (int)((T + kRows - 1) / kRows);
   dim3 grid((unsigned)nblk, (unsigned)(B * H));
+  // when the fast backward will run, the di pass zeroes its accumulator too
+  const bool fast_next = tc_attn_bwd_eligible(*cfg, T, dtype);
+  float* zero_acc = fast_next ? static_cast<float*>(tc_ws) : nullptr;
+  int* zero_tail =  // the 256 bytes after the accumulator
+      fast_next ? reinterpret_cast<int*>(static_cast<char*>(tc_ws) + tc_attn_bwd_workspace(B, H, T, kD) - 256) : nullptr;
   if (dtype == ALGX_BF16)
     attn_di_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(*cfg, guard, (const __nv_bfloat16*)o, o_precise,
                                                         (const __nv_bfloat16*)dout, stat, sink, di, sink_part,
-                                                        (int)H, (int)T);
+                                                        (int)H, (int)T, zero_acc, zero_tail);
   else
     attn_di_kernel<float><<<grid, 256, 0, st>>>(*cfg, guard, (const float*)o, o_precise, (const float*)dout, stat,
-                                                sink, di, sink_part, (int)H, (int)T);
+                                                sink, di, sink_part, (int)H, (int)T, zero_acc, zero_tail);
   ALGX_LAUNCHED("attn_di launch");
   if (cfg->has_sink) {
     attn_dsink_kernel<<<1, (unsigned)((H + 31) / 32 * 32), 0, st>>>(*cfg, guard, sink, sink_part, (int)B, (int)H,
@@ -939,7 +966,7 @@ static int attn_bwd_core(const algx_attn_config* cfg, const void* q_scaled, cons
   int mask = 7;
   bool fast = false;
   if (int s = tc_attn_bwd(*cfg, q_scaled, k, v, dout, stat, di, guard, dq, dk, dv, tc_ws, B, H, T, dtype, st,
-                          finish_dq, &fast))
+                          finish_dq, fast_next, &fast))
     return s;
   *fast_out = fast;
   if (fast) {

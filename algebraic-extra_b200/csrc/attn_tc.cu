@@ -974,13 +974,17 @@ int tc_attn_fwd(const algx_attn_config& cfg, const void* q_scaled, const void* k
 size_t tc_attn_bwd_workspace(int64_t B, int64_t H, int64_t T, int64_t D) {
   return (size_t)B * H * T * D * sizeof(float) + 256;
 }
+bool tc_attn_bwd_eligible(const algx_attn_config& cfg, int64_t T, int32_t dtype) {
+  return fast_eligible(cfg, T, dtype);
+}
 size_t tc_attn_bwd_spare_offset(int64_t B, int64_t H, int64_t T, int64_t D) {
   return (size_t)B * H * T * D * sizeof(float) + 128;
 }
 
 int tc_attn_bwd(const algx_attn_config& cfg, const void* q_scaled, const void* k, const void* v, const void* dout,
                 const float* stat, const float* di, const float* guard, void* dq, void* dk, void* dv, void* workspace,
-                int64_t B, int64_t H, int64_t T, int32_t dtype, cudaStream_t st, bool finish_dq, bool* launched) {
+                int64_t B, int64_t H, int64_t T, int32_t dtype, cudaStream_t st, bool finish_dq, bool pre_zeroed,
+                bool* launched) {
   *launched = false;
   if (!fast_eligible(cfg, T, dtype)) return ALGX_OK;
   CUtensorMap maps[6];  // q, k, v, dO (loads), dK, dV (stores)
@@ -994,7 +998,7 @@ int tc_attn_bwd(const algx_attn_config& cfg, const void* q_scaled, const void* k
   CUtensorMap tdq;  // fp32 accumulator, reduce-added in 128-row x 32-column boxes
   if (int s = make_tmap_2d(&tdq, acc, ALGX_F32, 64, (uint64_t)(B * H * T), 256, 32, kTile, true)) return s;
   int* item_counter = reinterpret_cast<int*>(acc + nacc);
-  ALGX_CUDA(cudaMemsetAsync(acc, 0, nacc * sizeof(float) + 256, st));
+  if (!pre_zeroed) ALGX_CUDA(cudaMemsetAsync(acc, 0, nacc * sizeof(float) + 256, st));
   const bool clip = cfg.mode == ALGX_MODE_CLIPPED;
   // The guarded low branch uses the 1/Z statistic; the clipped link follows cfg.inv_stat.
   const bool inv = clip ? cfg.inv_stat != 0 : true;

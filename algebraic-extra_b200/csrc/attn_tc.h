@@ -18,10 +18,15 @@ int tc_attn_fwd(const algx_attn_config& cfg, const void* q_scaled, const void* k
 // With finish_dq false the fp32 dQ accumulator (the first B*H*T*64 floats of
 // the workspace, unscaled) is left for the caller instead of being rounded
 // into dq.
+// pre_zeroed: the caller has already zeroed the accumulator and the 256-byte
+// counter area that follows it (the di pass does), so no memset is issued.
 int tc_attn_bwd(const algx_attn_config& cfg, const void* q_scaled, const void* k, const void* v,
                 const void* dout, const float* stat, const float* di, const float* guard, void* dq, void* dk,
                 void* dv, void* workspace, int64_t B, int64_t H, int64_t T, int32_t dtype, cudaStream_t st,
-                bool finish_dq, bool* launched);
+                bool finish_dq, bool pre_zeroed, bool* launched);
+
+// Whether tc_attn_bwd takes a call with this configuration.
+bool tc_attn_bwd_eligible(const algx_attn_config& cfg, int64_t T, int32_t dtype);
 
 // Byte offset, within the fast-path workspace, of 64 spare bytes that the
 // launch zeroes along with the dQ accumulator.
