@@ -119,6 +119,7 @@ __global__ void __launch_bounds__(kPrepThreads) qknorm_attn_prepare_kernel(
     const float* __restrict__ gain_k, const float* __restrict__ rot_cos, const float* __restrict__ rot_sin,
     const float* __restrict__ sink, int H, int T_, T* __restrict__ qs, T* __restrict__ kn, float* guard,
     int64_t rows, float scale, float eps) {
+  pdl_trigger();  // the forward kernel may be scheduled behind this grid (it waits for it)
   using V = Vec<T>;
   constexpr int kUnroll = 4;
   const int which = blockIdx.y;  // 0: q (normalised, scaled, written), 1: k (normalised, written), 2: v
@@ -343,6 +344,8 @@ __global__ void __launch_bounds__(256) attn_di_kernel(algx_attn_config cfg, cons
                                                       const float* __restrict__ sink, float* __restrict__ di,
                                                       float* __restrict__ sink_part, int H, int T_,
                                                       float* __restrict__ zero_acc, int* __restrict__ zero_tail) {
+  pdl_wait();  // launched as a dependent: the forward's outputs are complete after this
+  pdl_trigger();
   const Eff e = resolve_variant(cfg, guard);
   // The fast backward's fp32 dQ accumulator (zero_acc, rows of 64) and its
   // 256-byte counter area (zero_tail) are zeroed here, alongside the o / dO
@@ -750,6 +753,7 @@ __global__ void __launch_bounds__(kEpiThreads) qknorm_attn_bwd_kernel(
     const float* __restrict__ gain_k, const float* __restrict__ rot_cos, const float* __restrict__ rot_sin, int T_,
     T* dq_x, T* dk_x, float* __restrict__ partial, unsigned* counter, float* __restrict__ dgain_q,
     float* __restrict__ dgain_k, int64_t rows, float eps) {
+  pdl_wait();  // launched as a dependent of the attention backward
   using V = Vec<T>;
   __shared__ float red[kEpiThreads / 32 * V::RPW][2 * kD];  // per row slot of a warp: q and k column sums
   __shared__ float fin[kEpiThreads / (2 * kD)][2 * kD];
@@ -951,12 +955,13 @@ static int attn_bwd_core(const algx_attn_config* cfg, const void* q_scaled, cons
   int* zero_tail =  // the 256 bytes after the accumulator
       fast_next ? reinterpret_cast<int*>(static_cast<char*>(tc_ws) + tc_attn_bwd_workspace(B, H, T, kD) - 256) : nullptr;
   if (dtype == ALGX_BF16)
-    attn_di_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(*cfg, guard, (const __nv_bfloat16*)o, o_precise,
-                                                        (const __nv_bfloat16*)dout, stat, sink, di, sink_part,
-                                                        (int)H, (int)T, zero_acc, zero_tail);
+    ALGX_CUDA(launch_dependent(attn_di_kernel<__nv_bfloat16>, grid, 256, 0, st, *cfg, guard,
+                               (const __nv_bfloat16*)o, o_precise, (const __nv_bfloat16*)dout, stat, sink, di,
+                               sink_part, (int)H, (int)T, zero_acc, zero_tail));
   else
-    attn_di_kernel<float><<<grid, 256, 0, st>>>(*cfg, guard, (const float*)o, o_precise, (const float*)dout, stat,
-                                                sink, di, sink_part, (int)H, (int)T, zero_acc, zero_tail);
+    ALGX_CUDA(launch_dependent(attn_di_kernel<float>, grid, 256, 0, st, *cfg, guard, (const float*)o, o_precise,
+                               (const float*)dout, stat, sink, di, sink_part, (int)H, (int)T, zero_acc,
+                               zero_tail));
   ALGX_LAUNCHED("attn_di launch");
   if (cfg->has_sink) {
     attn_dsink_kernel<<<1, (unsigned)((H + 31) / 32 * 32), 0, st>>>(*cfg, guard, sink, sink_part, (int)B, (int)H,
@@ -1072,13 +1077,14 @@ int algx_qknorm_attn_bwd(const algx_attn_config* cfg, const void* q, const void*
   }
   const int64_t rows = B * H * T;
   if (dtype == ALGX_BF16)
-    qknorm_attn_bwd_kernel<__nv_bfloat16><<<kEpiBlocks, kEpiThreads, 0, st>>>(
-        *cfg, guard, fast ? 1 : 0, acc, (const __nv_bfloat16*)q, gain_q, (const __nv_bfloat16*)k, gain_k, rope_cos,
-        rope_sin, (int)T, (__nv_bfloat16*)dq, (__nv_bfloat16*)dk, partial, counter, dgain_q, dgain_k, rows, eps);
+    ALGX_CUDA(launch_dependent(qknorm_attn_bwd_kernel<__nv_bfloat16>, kEpiBlocks, kEpiThreads, 0, st, *cfg, guard,
+                               fast ? 1 : 0, acc, (const __nv_bfloat16*)q, gain_q, (const __nv_bfloat16*)k, gain_k,
+                               rope_cos, rope_sin, (int)T, (__nv_bfloat16*)dq, (__nv_bfloat16*)dk, partial, counter,
+                               dgain_q, dgain_k, rows, eps));
   else
-    qknorm_attn_bwd_kernel<float><<<kEpiBlocks, kEpiThreads, 0, st>>>(
-        *cfg, guard, 0, acc, (const float*)q, gain_q, (const float*)k, gain_k, rope_cos, rope_sin, (int)T,
-        (float*)dq, (float*)dk, partial, counter, dgain_q, dgain_k, rows, eps);
+    ALGX_CUDA(launch_dependent(qknorm_attn_bwd_kernel<float>, kEpiBlocks, kEpiThreads, 0, st, *cfg, guard, 0, acc,
+                               (const float*)q, gain_q, (const float*)k, gain_k, rope_cos, rope_sin, (int)T,
+                               (float*)dq, (float*)dk, partial, counter, dgain_q, dgain_k, rows, eps));
   ALGX_LAUNCHED("qknorm_attn_bwd launch");
   return ALGX_OK;
 }

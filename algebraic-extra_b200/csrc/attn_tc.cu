@@ -160,6 +160,7 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
                        const __grid_constant__ CUtensorMap tv, algx_attn_config cfg, const float* __restrict__ sink,
                        const float* __restrict__ guard, __nv_bfloat16* __restrict__ o, float* __restrict__ stat,
                        int H, int T, int* dev_err) {
+  pdl_wait();  // launched as a dependent of the prologue, which writes q_scaled and the guard maxima
   const Eff e = resolve_variant(cfg, guard);
   if (e.branch != BR_UNSHIFTED) return;  // the generic kernel runs the shifted fallback
   pdl_trigger();  // the fallback kernel may be scheduled behind this grid's last blocks
@@ -414,6 +415,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                        const __grid_constant__ CUtensorMap tdv, algx_attn_config cfg, const float* __restrict__ stat,
                        const float* __restrict__ di, const float* __restrict__ guard, int* __restrict__ item_counter,
                        int BH, int T, int* dev_err) {
+  pdl_wait();  // launched as a dependent of the di pass, which writes di and zeroes the accumulator
   const Eff e = resolve_variant(cfg, guard);
   if (e.branch != BR_UNSHIFTED) return;
   pdl_trigger();  // the fallback kernels may be scheduled behind this grid
@@ -884,6 +886,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 // dq = bf16(acc * n * scale), only when the fast path ran (unshifted branch).
 __global__ void dq_finish_kernel(algx_attn_config cfg, const float* __restrict__ guard,
                                  const float4* __restrict__ acc, __nv_bfloat16* __restrict__ dq, int64_t n4) {
+  pdl_wait();  // launched as a dependent of the fast backward
   pdl_trigger();  // the fallback kernels may be scheduled behind this grid
   const Eff e = resolve_variant(cfg, guard);
   if (e.branch != BR_UNSHIFTED) return;
@@ -913,8 +916,8 @@ int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& 
   auto kern = attn_fwd_tc_kernel<N, CLIP>;
   ALGX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem));
   dim3 grid((unsigned)(B * H), (unsigned)(T / kTile));
-  kern<<<grid, kFwdThreads, kFwdSmem, st>>>(tq, tk, tv, cfg, sink, guard, static_cast<__nv_bfloat16*>(o), stat,
-                                            (int)H, (int)T, device_error_word());
+  ALGX_CUDA(launch_dependent(kern, grid, kFwdThreads, kFwdSmem, st, tq, tk, tv, cfg, sink, guard,
+                             static_cast<__nv_bfloat16*>(o), stat, (int)H, (int)T, device_error_word()));
   ALGX_LAUNCHED("attn_fwd_tc launch");
   return ALGX_OK;
 }
@@ -931,8 +934,8 @@ int launch_bwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& 
   ALGX_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int64_t items = B * H * (T / kTile);
   const unsigned grid = (unsigned)std::min<int64_t>(items, sms);  // persistent: one CTA per SM
-  kern<<<grid, kBwdThreads, kBwdSmem, st>>>(tq, tk, tv, tdo, tdq, tdk, tdv, cfg, stat, di, guard, item_counter,
-                                            (int)(B * H), (int)T, device_error_word());
+  ALGX_CUDA(launch_dependent(kern, grid, kBwdThreads, kBwdSmem, st, tq, tk, tv, tdo, tdq, tdk, tdv, cfg, stat, di,
+                             guard, item_counter, (int)(B * H), (int)T, device_error_word()));
   ALGX_LAUNCHED("attn_bwd_tc launch");
   return ALGX_OK;
 }
@@ -1017,8 +1020,8 @@ int tc_attn_bwd(const algx_attn_config& cfg, const void* q_scaled, const void* k
   if (finish_dq) {
     const int64_t n4 = (int64_t)(nacc / 4);
     const int grid = (int)std::min<int64_t>((n4 + 255) / 256, 148 * 16);
-    dq_finish_kernel<<<grid, 256, 0, st>>>(cfg, guard, reinterpret_cast<const float4*>(acc),
-                                            static_cast<__nv_bfloat16*>(dq), n4);
+    ALGX_CUDA(launch_dependent(dq_finish_kernel, grid, 256, 0, st, cfg, guard, reinterpret_cast<const float4*>(acc),
+                               static_cast<__nv_bfloat16*>(dq), n4));
     ALGX_LAUNCHED("dq_finish launch");
   }
   *launched = true;
