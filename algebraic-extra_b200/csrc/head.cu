@@ -247,13 +247,17 @@ struct DzArgs {
   int N, d, V, voff;
   int tile0;           // first (local) vocabulary tile of the slab
   int ntiles;          // tiles in the slab
-  int splits;          // CTAs per 128-token block
+  int items;           // (128-token block, tile) work items of the slab: blocks x ntiles
   int ldz;             // row stride of the dz slab (elements)
 };
 
 // Logits of one slab with the forward's load / MMA pipeline; the epilogue
 // (thread = token) turns each fp32 logit into bf16 dz and stores its row
 // segment of the slab. Columns past the vocabulary and ignored rows give 0.
+// Persistent: one CTA per SM takes the work items blockIdx.x, +gridDim.x, ...
+// (item i = token block i / ntiles, tile i % ntiles), so the load ring and
+// the two TMEM accumulators run on across items and every SM gets an equal
+// share of the slab's items.
 template <int KIND, int NPOW>
 __global__ void __launch_bounds__(kHeadThreads, 1)
     head_dz_tc_kernel(const __grid_constant__ CUtensorMap th, const __grid_constant__ CUtensorMap te, DzArgs a,
@@ -265,10 +269,8 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
   __shared__ int abort_flag;
   volatile int* abort_v = &abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tb = blockIdx.x, split = blockIdx.y;
-  const int per = (a.ntiles + a.splits - 1) / a.splits;
-  const int t0 = a.tile0 + split * per, t1 = a.tile0 + min(a.ntiles, (split + 1) * per);
   const int nk = a.d / 64;
+  const int first = blockIdx.x, stride = gridDim.x;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kFwdStages; ++s) {
@@ -291,12 +293,13 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
   tc_fence_after();
 
   if (warp == kHeadTma) {
-    if (lane == 0 && t0 < t1) {
+    if (lane == 0 && first < a.items) {
       prefetch_tmap(&th);
       prefetch_tmap(&te);
       int it = 0;
       int last_stage_it[kFwdStages] = {-1, -1, -1, -1};
-      for (int t = t0; t < t1 && !*abort_v; ++t)
+      for (int i = first; i < a.items && !*abort_v; i += stride) {
+        const int tb = i / a.ntiles, t = a.tile0 + i % a.ntiles;
         for (int kc = 0; kc < nk; ++kc, ++it) {
           const int s = it % kFwdStages;
           if (it >= kFwdStages && !mbar_wait(&empty[s], ((it / kFwdStages) - 1) & 1, abort_v, dev_err)) break;
@@ -306,6 +309,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
           tma_load_2d(st + kChunkBytes, &te, &full[s], kc * 64, t * kFwdNT);
           last_stage_it[s] = it;
         }
+      }
       if (*abort_v)
         for (int s = 0; s < kFwdStages; ++s)
           if (last_stage_it[s] >= 0) {
@@ -314,13 +318,13 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
           }
     }
   } else if (warp == kHeadTma + 1) {
-    if (lane == 0 && t0 < t1) {
+    if (lane == 0 && first < a.items) {
       const uint32_t id = idesc_bf16_f32(128, kFwdNT, 0, 0);
       const uint32_t s0 = smem_u32(smem);
       int it = 0;
       bool ok = true;
-      for (int t = t0; ok && t < t1; ++t) {
-        const int buf = (t - t0) & 1, use = (t - t0) >> 1;
+      for (int i = first, li = 0; ok && i < a.items; i += stride, ++li) {
+        const int buf = li & 1, use = li >> 1;
         if (use > 0 && !mbar_wait(&acc_empty[buf], (use - 1) & 1, abort_v, dev_err)) break;
         tc_fence_after();
         const uint32_t acc = tmem_base + buf * kFwdNT;
@@ -341,23 +345,25 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
       }
     }
   } else {
-    // epilogue: two groups of four warps take alternate tiles (group g owns
-    // accumulator buffer g); thread r of a group owns token tb*128 + r
+    // epilogue: two groups of four warps take alternate items (group g owns
+    // accumulator buffer g); thread r of a group owns row r of the item's
+    // 128-token block
     const int g = warp >> 2;
     const int r = (warp & 3) * 32 + lane;
-    const int tok = tb * kRowsT + r;
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     const algx_head_config& c = a.cfg;
-    const int tgt = tok < a.N ? a.targets[tok] : -2147483647 - 1;
-    const bool row_ok = tok < a.N && !(c.has_ignore && tgt == c.ignore_index);
-    const int tloc = tgt - a.voff;  // local column of the target, may be out of range
-    const float st = tok < a.N ? a.stat[tok] : 0.f;
     const float scale = *a.scale;
     const float log2e = 1.4426950408889634f;
-    const float stl = st * log2e;
-    __nv_bfloat16* drow = dz + (size_t)tok * a.ldz - (size_t)a.tile0 * kFwdNT;
-    for (int t = t0 + g; t < t1; t += 2) {
-      const int buf = g, use = (t - t0) >> 1;
+    for (int i = first + g * stride, li = g; i < a.items; i += 2 * stride, li += 2) {
+      const int tb = i / a.ntiles, t = a.tile0 + i % a.ntiles;
+      const int tok = tb * kRowsT + r;
+      const int tgt = tok < a.N ? a.targets[tok] : -2147483647 - 1;
+      const bool row_ok = tok < a.N && !(c.has_ignore && tgt == c.ignore_index);
+      const int tloc = tgt - a.voff;  // local column of the target, may be out of range
+      const float st = tok < a.N ? a.stat[tok] : 0.f;
+      const float stl = st * log2e;
+      __nv_bfloat16* drow = dz + (size_t)tok * a.ldz - (size_t)a.tile0 * kFwdNT;
+      const int buf = g, use = li >> 1;
       if (!mbar_wait_warp(&acc_full[buf], use & 1, abort_v, dev_err)) break;
       tc_fence_after();
       const uint32_t acc = tmem_base + buf * kFwdNT + lane_off;
@@ -368,25 +374,25 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
         const int col0 = t * kFwdNT + cc * 32;
         uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
+        for (int i2 = 0; i2 < 16; ++i2) {
           float g2[2];
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const int col = col0 + 2 * i + h;
-            const float z = __uint_as_float(zr[2 * i + h]);
+            const int col = col0 + 2 * i2 + h;
+            const float z = __uint_as_float(zr[2 * i2 + h]);
             const float y = col == tloc ? 1.f : 0.f;
-            float g;
+            float gr;
             if constexpr (KIND == ALGX_HEAD_CE) {
-              g = exp2f(fmaf(z, log2e, -stl)) - y;
+              gr = exp2f(fmaf(z, log2e, -stl)) - y;
             } else {
               const float x = fminf(z * c.inv_c, c.clamp);
               const float rad = fmaf(x, x, 1.f);
               const float rr = rsqrt_fast(rad);
-              g = (ipow_t<NPOW>(fmaf(rad, rr, x) * st) - y) * rr;
+              gr = (ipow_t<NPOW>(fmaf(rad, rr, x) * st) - y) * rr;
             }
-            g2[h] = (row_ok && col < a.V) ? g * scale : 0.f;
+            g2[h] = (row_ok && col < a.V) ? gr * scale : 0.f;
           }
-          pk[i] = pack_bf16x2(g2[0], g2[1]);
+          pk[i2] = pack_bf16x2(g2[0], g2[1]);
         }
         if (tok < a.N) {
           uint4* d4 = reinterpret_cast<uint4*>(drow + col0);
@@ -519,10 +525,13 @@ int launch_fwd_k(const CUtensorMap& th, const CUtensorMap& te, const HeadArgs& a
 
 template <int KIND>
 int launch_dz_k(const CUtensorMap& th, const CUtensorMap& te, const DzArgs& a, __nv_bfloat16* dz, cudaStream_t st) {
-  const int tb = (a.N + 127) / 128;
+  int dev = 0, sms = 0;
+  ALGX_CUDA(cudaGetDevice(&dev));
+  ALGX_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const unsigned grid = (unsigned)std::max(1, std::min(a.items, sms));  // persistent: one CTA per SM
   auto run = [&](auto kern) -> int {
     ALGX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem));
-    kern<<<dim3(tb, a.splits), kHeadThreads, kFwdSmem, st>>>(th, te, a, dz, device_error_word());
+    kern<<<grid, kHeadThreads, kFwdSmem, st>>>(th, te, a, dz, device_error_word());
     ALGX_LAUNCHED("head_dz_tc launch");
     return ALGX_OK;
   };
@@ -654,10 +663,9 @@ int algx_head_bwd(const algx_head_config* cfg, const void* h, const void* embed,
   const float one = 1.f, zero = 0.f;
   for (int64_t c0 = 0; c0 < V; c0 += vs) {
     const int64_t vc = std::min<int64_t>(vs, V - c0);  // valid columns of this slab
-    DzArgs a{*cfg, targets, stat, scale, (int)N, (int)d, (int)V, (int)vocab_offset, (int)(c0 / kFwdNT), 0, 1, (int)vs};
+    DzArgs a{*cfg, targets, stat, scale, (int)N, (int)d, (int)V, (int)vocab_offset, (int)(c0 / kFwdNT), 0, 0, (int)vs};
     a.ntiles = std::min<int>((int)(vs / kFwdNT), ntiles_total - a.tile0);
-    // enough CTAs for a few waves: 128-token blocks x tile groups
-    a.splits = std::max(1, std::min(a.ntiles, (4 * 148 + tb - 1) / tb));
+    a.items = tb * a.ntiles;
     int s = cfg->kind == ALGX_HEAD_CE ? launch_dz_k<ALGX_HEAD_CE>(th, te, a, dz, st)
                                       : launch_dz_k<ALGX_HEAD_ALG_CE>(th, te, a, dz, st);
     if (s) return s;
