@@ -1,0 +1,111 @@
+"""Row RMS norm and SwiGLU over libalgx, as autograd functions.
+
+These are the model's own elementwise layers around the three hot kernels
+(model.py:158-159 ``_norm`` and model.py:193-198 ``gate * silu(up)``), each
+one fused launch forward and one backward, for the config-5 training step in
+``algx.model``. Like the hot kernels they run on CUDA tensors only.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib as L
+
+
+def rmsnorm_forward(x: torch.Tensor, gain, eps: float) -> torch.Tensor:
+    """y = rms_norm(x) * gain over the last axis (algebraic.py:76-83), one launch."""
+    dim = x.shape[-1]
+    y = torch.empty_like(x)
+    L.check(L.lib().algx_rmsnorm_fwd(x.data_ptr(), L.ptr(gain), y.data_ptr(), x.numel() // dim, dim,
+                                     L.dtype_code(x.dtype), float(eps), L.stream_of(x)), "algx_rmsnorm_fwd")
+    return y
+
+
+def rmsnorm_backward(x: torch.Tensor, gain, dy: torch.Tensor, eps: float):
+    """(dx, dgain) of ``rmsnorm_forward``; dgain is None without a gain."""
+    dim = x.shape[-1]
+    rows = x.numel() // dim
+    dy = dy.to(x.dtype).contiguous()
+    dx = torch.empty_like(x)
+    lib = L.lib()
+    dgain = None
+    ws, nbytes = None, 0
+    if gain is not None:
+        dgain = torch.empty(dim, dtype=torch.float32, device=x.device)
+        nbytes = lib.algx_rmsnorm_bwd_workspace_size(rows, dim)
+        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=x.device)
+    L.check(lib.algx_rmsnorm_bwd(x.data_ptr(), L.ptr(gain), dy.data_ptr(), dx.data_ptr(), L.ptr(dgain), rows, dim,
+                                 L.dtype_code(x.dtype), float(eps), L.ptr(ws), nbytes, L.stream_of(x)),
+            "algx_rmsnorm_bwd")
+    return dx, dgain
+
+
+class _RMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, gain, eps):
+        xc = x.contiguous()
+        ctx.eps = float(eps)
+        ctx.has_gain = gain is not None
+        ctx.save_for_backward(xc, gain)
+        return rmsnorm_forward(xc, gain, eps)
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, gain = ctx.saved_tensors
+        dx, dgain = rmsnorm_backward(x, gain if ctx.has_gain else None, dy, ctx.eps)
+        return dx, (dgain.to(gain.dtype) if dgain is not None else None), None
+
+
+def rms_norm(x: torch.Tensor, gain, eps: float = 1e-5) -> torch.Tensor:
+    """``algebraic.rms_norm`` (algebraic.py:76-83): fp32 maths, result in x's dtype.
+
+    ``gain`` is a float32 vector of the last axis' length, or None for the
+    parameter-free form. The width must be a multiple of 16 bytes and at most
+    4096 (bf16) / 2048 (float32).
+    """
+    if x.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("rms_norm needs float32 or bfloat16 input")
+    if gain is not None and (gain.dtype != torch.float32 or tuple(gain.shape) != (x.shape[-1],)):
+        raise ValueError("rms_norm gain must be float32 with the width of x's last axis")
+    if eps <= 0:
+        raise ValueError("rms_norm epsilon must be positive")
+    L.require_cuda(x, gain)
+    return _RMSNorm.apply(x, gain, float(eps))
+
+
+class _SwiGLU(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, gu):
+        gu = gu.contiguous()
+        ff = gu.shape[-1] // 2
+        rows = gu.numel() // gu.shape[-1]
+        y = torch.empty(gu.shape[:-1] + (ff,), dtype=gu.dtype, device=gu.device)
+        L.check(L.lib().algx_swiglu_fwd(gu.data_ptr(), y.data_ptr(), rows, ff, L.stream_of(gu)), "algx_swiglu_fwd")
+        ctx.save_for_backward(gu)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        (gu,) = ctx.saved_tensors
+        ff = gu.shape[-1] // 2
+        rows = gu.numel() // gu.shape[-1]
+        dy = dy.to(gu.dtype).contiguous()
+        dgu = torch.empty_like(gu)
+        L.check(L.lib().algx_swiglu_bwd(gu.data_ptr(), dy.data_ptr(), dgu.data_ptr(), rows, ff, L.stream_of(gu)),
+                "algx_swiglu_bwd")
+        return dgu
+
+
+def swiglu(gu: torch.Tensor) -> torch.Tensor:
+    """``gate * silu(up)`` for ``gu = [gate | up]`` on the last axis (model.py:193-198), bf16.
+
+    ``gu`` is the output of one GEMM against ``[w_g | w_u]``; the result has
+    half its last axis.
+    """
+    if gu.dtype != torch.bfloat16:
+        raise ValueError("swiglu needs bfloat16 input")
+    if gu.shape[-1] % 16:
+        raise ValueError("swiglu needs an even hidden width that is a multiple of 8")
+    L.require_cuda(gu)
+    return _SwiGLU.apply(gu)

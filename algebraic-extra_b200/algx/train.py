@@ -1,0 +1,188 @@
+"""Data-parallel training step: micro-batch accumulation, gradient all-reduce,
+global-norm clipping and AdamW (train.py:265-290 of the reference).
+
+One process per GPU. Each rank runs its share of the global batch as
+micro-batches, accumulating float32 gradients in the model's flat gradient
+buffers. During the last micro-batch's backward, each contiguous bucket of a
+flat buffer is all-reduced (NCCL, asynchronously) as soon as autograd has
+finished every parameter in it, so the exchange overlaps the rest of the
+backward; the buffers are laid out in the order the backward finishes them.
+Then, on the device and without a host synchronisation:
+
+    g      = sum_ranks(g) / world                       (lax.pmean, train.py:281)
+    gnorm  = ||g||_2
+    g     *= min(1, clip / max(gnorm, 1e-12))           (train.py:283-285)
+    AdamW on the two flat master buffers, weight decay on the decayed one only
+    (model.py:120-125 mask)
+
+The step works for any module that exposes ``flat`` (``algx.model.FlatParams``)
+and ``loss(tokens, targets) -> (objective, telemetry)``; ``algx.model.AlgebraicLM``
+is the one this package ships.
+"""
+
+from __future__ import annotations
+
+from typing import Dict, List, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+
+
+class DataParallelTrainer:
+    """Train step over the ranks of ``group`` (all ranks when None).
+
+    ``micro_batch``: sequences per forward/backward pass; the rank's share of
+    the batch must be a multiple of it. ``bucket_bytes``: target size of one
+    all-reduce.
+    """
+
+    def __init__(self, model, *, lr: float = 2e-3, betas=(0.9, 0.95), eps: float = 1e-8,
+                 weight_decay: float = 0.1, clip: float = 1.0, micro_batch: int = 8,
+                 bucket_bytes: int = 32 << 20, group=None):
+        self.model = model
+        self.flat = model.flat
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+        self.clip = float(clip)
+        self.micro_batch = int(micro_batch)
+        dev = self.flat.data[True].device
+        groups = [{"params": [self.flat.flat[True]], "weight_decay": weight_decay},
+                  {"params": [self.flat.flat[False]], "weight_decay": 0.0}]
+        self.opt = torch.optim.AdamW(groups, lr=lr, betas=tuple(betas), eps=eps,
+                                     fused=dev.type == "cuda")
+        self._works: List = []
+        self._last = False
+        self._buckets = self._make_buckets(bucket_bytes) if self.world > 1 else []
+        self._pending: Dict[int, int] = {}
+        self._hooks = []
+        if self._buckets:
+            owner = {}
+            for bi, (_, _, _, names) in enumerate(self._buckets):
+                for n in names:
+                    owner[n] = bi
+            for name, p in self.flat.params.items():
+                self._hooks.append(p.register_post_accumulate_grad_hook(self._on_grad(owner[name])))
+
+    # ------------------------------------------------------------ buckets
+    def _make_buckets(self, bucket_bytes: int) -> List[Tuple[bool, int, int, List[str]]]:
+        """Consecutive parameters of each flat buffer, grouped up to
+        ``bucket_bytes`` (a parameter larger than that is a bucket alone)."""
+        limit = max(1, bucket_bytes // 4)
+        buckets = []
+        for decay in (True, False):
+            cur, start, end = [], None, None
+            for sp in self.flat.specs:
+                d, a, b = self.flat.slices[sp.name]
+                if d != decay:
+                    continue
+                if cur and b - start > limit:
+                    buckets.append((decay, start, end, cur))
+                    cur = []
+                if not cur:
+                    start = a
+                cur.append(sp.name)
+                end = b
+            if cur:
+                buckets.append((decay, start, end, cur))
+        return buckets
+
+    def _on_grad(self, bi: int):
+        def hook(_p):
+            if not self._last:
+                return
+            left = self._pending.get(bi, len(self._buckets[bi][3])) - 1
+            self._pending[bi] = left
+            if left == 0:
+                decay, a, b, _ = self._buckets[bi]
+                self._works.append(dist.all_reduce(self.flat.grad[decay][a:b], group=self.group, async_op=True))
+        return hook
+
+    # ------------------------------------------------------------ step
+    def step(self, tokens: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
+        """One optimizer step on this rank's (b, T) tokens and targets.
+
+        Returns the mean objective over the global batch as a device tensor
+        (no host synchronisation).
+        """
+        b = tokens.shape[0]
+        m = min(self.micro_batch, b)
+        if b % m:
+            raise ValueError(f"rank batch {b} is not a multiple of the micro-batch {m}")
+        n_micro = b // m
+        self.flat.zero_grad()
+        self._pending = {}
+        self._works = []
+        loss_sum = torch.zeros((), dtype=torch.float32, device=tokens.device)
+        for i in range(n_micro):
+            self._last = i == n_micro - 1
+            obj, _ = self.model.loss(tokens[i * m:(i + 1) * m], targets[i * m:(i + 1) * m])
+            (obj / n_micro).backward()
+            loss_sum += obj.detach()
+        self._last = False
+        if self.world > 1:
+            if len(self._works) != len(self._buckets):
+                raise RuntimeError(f"{len(self._buckets) - len(self._works)} gradient buckets were not "
+                                   "all-reduced: some parameters received no gradient")
+            for w in self._works:
+                w.wait()
+            self._works = []
+            dist.all_reduce(loss_sum, group=self.group)
+        self._clip_and_scale()
+        self.opt.step()
+        return loss_sum / (n_micro * self.world)
+
+    def _clip_and_scale(self) -> None:
+        grads = list(self.flat.grad.values())
+        norms = torch.stack([torch.linalg.vector_norm(g) for g in grads])
+        gnorm = torch.linalg.vector_norm(norms) / self.world
+        scale = torch.clamp(self.clip / torch.clamp(gnorm, min=1e-12), max=1.0) / self.world
+        torch._foreach_mul_(grads, scale)
+        self.last_gnorm = gnorm
+
+    def close(self) -> None:
+        for h in self._hooks:
+            h.remove()
+        self._hooks = []
+
+
+def main(argv=None) -> None:
+    """``python -m algx.train --profile-steps N``: time N config-5 training
+    steps on one GPU on synthetic token ids and print tok/s (the reference
+    trainer's ``--profile-steps`` mode, train.py:96)."""
+    import argparse
+    import json
+
+    from .model import AlgebraicLM, config_125m, train_flops_per_token
+
+    ap = argparse.ArgumentParser(description=main.__doc__)
+    ap.add_argument("--profile-steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=2)
+    ap.add_argument("--batch", type=int, default=64, help="sequences per optimizer step")
+    ap.add_argument("--micro", type=int, default=8, help="sequences per micro-batch")
+    ap.add_argument("--layers", type=int, default=None, help="override n_layers")
+    args = ap.parse_args(argv)
+    cfg = config_125m() if args.layers is None else config_125m(n_layers=args.layers)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    model = AlgebraicLM(cfg, device=dev, seed=0)
+    tr = DataParallelTrainer(model, micro_batch=args.micro)
+    g = torch.Generator(device=dev).manual_seed(777)
+    seq = torch.randint(0, cfg.vocab_size, (args.batch, cfg.seq_len + 1), device=dev, generator=g)
+    tok, tgt = seq[:, :-1].contiguous(), seq[:, 1:].contiguous()
+    for _ in range(args.warmup):
+        tr.step(tok, tgt)
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    losses = [tr.step(tok, tgt) for _ in range(args.profile_steps)]
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / max(args.profile_steps, 1)
+    tokens = args.batch * cfg.seq_len
+    print(json.dumps({"tok_per_s": tokens / (ms / 1e3), "ms_per_step": ms,
+                      "tflops_6P": train_flops_per_token(cfg) * tokens / (ms / 1e3) / 1e12,
+                      "loss": [float(x) for x in losses], "batch": args.batch, "micro": args.micro,
+                      "layers": cfg.n_layers}))
+
+
+if __name__ == "__main__":
+    main()

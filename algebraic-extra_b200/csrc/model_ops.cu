@@ -1,0 +1,403 @@
+// Row RMS norm of any width and the SwiGLU gate, the two memory-bound
+// elementwise families of the training step around the hot kernels
+// (model.py:184-200): the ln1 / ln2 / embed / final norms (algebraic.py:76-83
+// through model.py:158-159) and gate * silu(up) (model.py:193-198,
+// standard.py:12-13).
+//
+// RMS norm: one warp per row, 128-bit loads, C 16-byte chunks per lane, the
+// row's sum of squares by warp shuffles. The backward writes one fp32 row of
+// dgain partials per CTA into the caller's workspace and a second launch sums
+// them in a fixed order (deterministic for a given grid).
+//
+// SwiGLU: the gate and up projections come out of one GEMM as rows of
+// [gate (f) | up (f)]; the forward reads both halves and writes y (rows, f),
+// the backward reads the pair and dy and writes [dgate | dup]. Everything in
+// fp32 between one bf16 load and one bf16 store per output, which is how XLA
+// evaluates the fused bf16 chain (excess precision) in the reference.
+#include "algx_common.cuh"
+#include "vec_io.cuh"
+
+namespace algx {
+namespace {
+
+constexpr int kNormThreads = 256;  // 8 warps: one row per warp per pass
+constexpr int kNormWarps = kNormThreads / 32;
+constexpr int kNormMaxBlocks = 148 * 4;
+
+template <typename T, int C>
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_fwd_kernel(const T* __restrict__ x,
+                                                                   const float* __restrict__ gain,
+                                                                   T* __restrict__ y, int64_t rows, int dim,
+                                                                   float eps) {
+  using V = Vec<T>;
+  const int lane = threadIdx.x & 31;
+  const int chunks = dim / V::N;
+  float g[C][V::N];
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    const int idx = lane + 32 * c;
+#pragma unroll
+    for (int i = 0; i < V::N; ++i) g[c][i] = (gain && idx < chunks) ? gain[idx * V::N + i] : 1.f;
+  }
+  const int64_t warps = (int64_t)gridDim.x * kNormWarps;
+  for (int64_t row = (int64_t)blockIdx.x * kNormWarps + (threadIdx.x >> 5); row < rows; row += warps) {
+    const T* xr = x + row * dim;
+    uint4 raw[C];
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      const int idx = lane + 32 * c;
+      raw[c] = idx < chunks ? ld_stream(xr + idx * V::N) : make_uint4(0, 0, 0, 0);
+    }
+    float v[C][V::N];
+    float ss = 0.f;
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      unpack<T>(raw[c], v[c]);
+#pragma unroll
+      for (int i = 0; i < V::N; ++i) ss = fmaf(v[c][i], v[c][i], ss);
+    }
+    ss = row_sum<32>(ss);
+    // mean = sum / dim, as jnp.mean divides (algebraic.py:79)
+    const float tau = rsqrtf(ss / (float)dim + eps);
+    T* yr = y + row * dim;
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      const int idx = lane + 32 * c;
+      float o[V::N];
+#pragma unroll
+      for (int i = 0; i < V::N; ++i) o[i] = gain ? (v[c][i] * tau) * g[c][i] : v[c][i] * tau;
+      if (idx < chunks) *reinterpret_cast<uint4*>(yr + idx * V::N) = pack<T>(o);
+    }
+  }
+}
+
+// dx = tau (g dy) - x tau^3 mean(x g dy) (AD of the forward, the operation
+// order of kernels/qk_norm.py:39-40); dgain partials = sum_rows dy (x tau).
+template <typename T, int C>
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(const T* __restrict__ x,
+                                                                   const float* __restrict__ gain,
+                                                                   const T* __restrict__ dy, T* __restrict__ dx,
+                                                                   float* __restrict__ partial, int64_t rows,
+                                                                   int dim, float eps) {
+  using V = Vec<T>;
+  extern __shared__ float red[];  // [kNormWarps][dim]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int chunks = dim / V::N;
+  float g[C][V::N], acc[C][V::N];
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    const int idx = lane + 32 * c;
+#pragma unroll
+    for (int i = 0; i < V::N; ++i) {
+      g[c][i] = (gain && idx < chunks) ? gain[idx * V::N + i] : 1.f;
+      acc[c][i] = 0.f;
+    }
+  }
+  const int64_t warps = (int64_t)gridDim.x * kNormWarps;
+  for (int64_t row = (int64_t)blockIdx.x * kNormWarps + warp; row < rows; row += warps) {
+    uint4 rx[C], rd[C];
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      const int idx = lane + 32 * c;
+      const bool ok = idx < chunks;
+      rx[c] = ok ? ld_stream(x + row * dim + idx * V::N) : make_uint4(0, 0, 0, 0);
+      rd[c] = ok ? ld_stream(dy + row * dim + idx * V::N) : make_uint4(0, 0, 0, 0);
+    }
+    float xv[C][V::N], dv[C][V::N];
+    float ss = 0.f, sdg = 0.f;
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      unpack<T>(rx[c], xv[c]);
+      unpack<T>(rd[c], dv[c]);
+#pragma unroll
+      for (int i = 0; i < V::N; ++i) {
+        ss = fmaf(xv[c][i], xv[c][i], ss);
+        sdg = fmaf(dv[c][i] * g[c][i], xv[c][i], sdg);
+      }
+    }
+    ss = row_sum<32>(ss);
+    sdg = row_sum<32>(sdg);
+    const float tau = rsqrtf(ss / (float)dim + eps);
+    const float corr = tau * tau * tau * (sdg / (float)dim);
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+      const int idx = lane + 32 * c;
+      float o[V::N];
+#pragma unroll
+      for (int i = 0; i < V::N; ++i) {
+        o[i] = (dv[c][i] * g[c][i]) * tau - xv[c][i] * corr;
+        acc[c][i] = fmaf(dv[c][i], xv[c][i] * tau, acc[c][i]);
+      }
+      if (idx < chunks) *reinterpret_cast<uint4*>(dx + row * dim + idx * V::N) = pack<T>(o);
+    }
+  }
+  if (!partial) return;  // no gain: no dgain
+#pragma unroll
+  for (int c = 0; c < C; ++c) {
+    const int idx = lane + 32 * c;
+    if (idx < chunks) {
+#pragma unroll
+      for (int i = 0; i < V::N; ++i) red[warp * dim + idx * V::N + i] = acc[c][i];
+    }
+  }
+  __syncthreads();
+  for (int col = threadIdx.x; col < dim; col += kNormThreads) {
+    float s = 0.f;
+#pragma unroll
+    for (int w = 0; w < kNormWarps; ++w) s += red[w * dim + col];
+    partial[(int64_t)blockIdx.x * dim + col] = s;
+  }
+}
+
+// dgain[col] = sum over the nb partial rows, in a fixed order: warp w sums rows
+// w, w + 8, ... of 32 columns; the 8 warp sums are added in warp order.
+__global__ void __launch_bounds__(256) rmsnorm_dgain_reduce(const float* __restrict__ partial, int nb, int dim,
+                                                           float* __restrict__ dgain) {
+  __shared__ float red[8][32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int col = blockIdx.x * 32 + lane;
+  float s = 0.f;
+  if (col < dim)
+    for (int b = warp; b < nb; b += 8) s += partial[(int64_t)b * dim + col];
+  red[warp][lane] = s;
+  __syncthreads();
+  if (warp == 0 && col < dim) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += red[w][lane];
+    dgain[col] = t;
+  }
+}
+
+int norm_chunks(int64_t dim, int32_t dtype) {
+  const int n = dtype == ALGX_BF16 ? 8 : 4;
+  const int64_t per_lane = (dim / n + 31) / 32;
+  // instantiated chunk counts per lane: dim <= 4096 (bf16), 2048 (float32)
+  static const int kC[] = {1, 2, 3, 4, 6, 8, 12, 16};
+  for (int c : kC)
+    if (per_lane <= c) return c;
+  return -1;
+}
+
+int norm_grid(int64_t rows) {
+  int64_t g = (rows + kNormWarps - 1) / kNormWarps;
+  if (g > kNormMaxBlocks) g = kNormMaxBlocks;
+  return (int)(g < 1 ? 1 : g);
+}
+
+// Pointers may be NULL only when there are no rows (empty tensors).
+int check_norm(const void* x, const void* y, int64_t rows, int64_t dim, int32_t dtype, float eps, const char* who) {
+  ALGX_REQUIRE(rows >= 0, std::string(who) + ": negative row count");
+  ALGX_REQUIRE(rows == 0 || (x && y), std::string(who) + ": NULL pointer");
+  ALGX_REQUIRE(dtype == ALGX_F32 || dtype == ALGX_BF16, std::string(who) + ": dtype must be float32 or bfloat16");
+  ALGX_REQUIRE(eps > 0.f, std::string(who) + ": epsilon must be positive");
+  const int n = dtype == ALGX_BF16 ? 8 : 4;
+  ALGX_REQUIRE(dim > 0 && dim % n == 0, std::string(who) + ": width must be a positive multiple of 16 bytes");
+  ALGX_REQUIRE(norm_chunks(dim, dtype) > 0,
+               std::string(who) + ": width above the supported maximum (4096 bf16, 2048 float32)");
+  ALGX_REQUIRE((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0,
+               std::string(who) + ": tensors must be 16-byte aligned");
+  return ALGX_OK;
+}
+
+template <typename T, int C>
+void launch_norm_fwd(const void* x, const float* gain, void* y, int64_t rows, int dim, float eps, cudaStream_t st) {
+  rmsnorm_fwd_kernel<T, C><<<norm_grid(rows), kNormThreads, 0, st>>>(static_cast<const T*>(x), gain,
+                                                                      static_cast<T*>(y), rows, dim, eps);
+}
+
+template <typename T, int C>
+cudaError_t launch_norm_bwd(const void* x, const float* gain, const void* dy, void* dx, float* partial,
+                            int64_t rows, int dim, float eps, cudaStream_t st) {
+  const size_t smem = (size_t)kNormWarps * dim * sizeof(float);
+  auto kern = rmsnorm_bwd_kernel<T, C>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  kern<<<norm_grid(rows), kNormThreads, smem, st>>>(static_cast<const T*>(x), gain, static_cast<const T*>(dy),
+                                                    static_cast<T*>(dx), partial, rows, dim, eps);
+  return cudaSuccess;
+}
+
+template <typename T>
+void dispatch_norm_fwd(int C, const void* x, const float* gain, void* y, int64_t rows, int dim, float eps,
+                       cudaStream_t st) {
+  switch (C) {
+    case 1: launch_norm_fwd<T, 1>(x, gain, y, rows, dim, eps, st); break;
+    case 2: launch_norm_fwd<T, 2>(x, gain, y, rows, dim, eps, st); break;
+    case 3: launch_norm_fwd<T, 3>(x, gain, y, rows, dim, eps, st); break;
+    case 4: launch_norm_fwd<T, 4>(x, gain, y, rows, dim, eps, st); break;
+    case 6: launch_norm_fwd<T, 6>(x, gain, y, rows, dim, eps, st); break;
+    case 8: launch_norm_fwd<T, 8>(x, gain, y, rows, dim, eps, st); break;
+    case 12: launch_norm_fwd<T, 12>(x, gain, y, rows, dim, eps, st); break;
+    default: launch_norm_fwd<T, 16>(x, gain, y, rows, dim, eps, st); break;
+  }
+}
+
+template <typename T>
+cudaError_t dispatch_norm_bwd(int C, const void* x, const float* gain, const void* dy, void* dx, float* partial,
+                              int64_t rows, int dim, float eps, cudaStream_t st) {
+  switch (C) {
+    case 1: return launch_norm_bwd<T, 1>(x, gain, dy, dx, partial, rows, dim, eps, st);
+    case 2: return launch_norm_bwd<T, 2>(x, gain, dy, dx, partial, rows, dim, eps, st);
+    case 3: return launch_norm_bwd<T, 3>(x, gain, dy, dx, partial, rows, dim, eps, st);
+    case 4: return launch_norm_bwd<T, 4>(x, gain, dy, dx, partial, rows, dim, eps, st);
+    case 6: return launch_norm_bwd<T, 6>(x, gain, dy, dx, partial, rows, dim, eps, st);
+    case 8: return launch_norm_bwd<T, 8>(x, gain, dy, dx, partial, rows, dim, eps, st);
+    case 12: return launch_norm_bwd<T, 12>(x, gain, dy, dx, partial, rows, dim, eps, st);
+    default: return launch_norm_bwd<T, 16>(x, gain, dy, dx, partial, rows, dim, eps, st);
+  }
+}
+
+// ------------------------------------------------------------------ SwiGLU
+constexpr int kGluThreads = 256;
+constexpr int kGluMaxBlocks = 148 * 8;
+
+__device__ __forceinline__ float sigmoid_f(float u) { return 1.f / (1.f + __expf(-u)); }
+
+// y[r, j] = gate[r, j] * up[r, j] * sigmoid(up[r, j]), gu[r] = [gate | up]
+__global__ void __launch_bounds__(kGluThreads) swiglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu,
+                                                                 __nv_bfloat16* __restrict__ y, int64_t rows,
+                                                                 int ff) {
+  const int cpr = ff / 8;  // 16-byte chunks per output row
+  const int64_t total = rows * cpr;
+  for (int64_t i = (int64_t)blockIdx.x * kGluThreads + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * kGluThreads) {
+    const int64_t r = i / cpr;
+    const int c = (int)(i - r * cpr);
+    const __nv_bfloat16* src = gu + r * 2 * ff + c * 8;
+    float g[8], u[8], o[8];
+    unpack<__nv_bfloat16>(ld_stream(src), g);
+    unpack<__nv_bfloat16>(ld_stream(src + ff), u);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) o[k] = g[k] * (u[k] * sigmoid_f(u[k]));
+    *reinterpret_cast<uint4*>(y + r * ff + c * 8) = pack<__nv_bfloat16>(o);
+  }
+}
+
+// dgate = dy silu(up); dup = dy gate (s + up s (1 - s)), s = sigmoid(up)
+__global__ void __launch_bounds__(kGluThreads) swiglu_bwd_kernel(const __nv_bfloat16* __restrict__ gu,
+                                                                 const __nv_bfloat16* __restrict__ dy,
+                                                                 __nv_bfloat16* __restrict__ dgu, int64_t rows,
+                                                                 int ff) {
+  const int cpr = ff / 8;
+  const int64_t total = rows * cpr;
+  for (int64_t i = (int64_t)blockIdx.x * kGluThreads + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * kGluThreads) {
+    const int64_t r = i / cpr;
+    const int c = (int)(i - r * cpr);
+    const __nv_bfloat16* src = gu + r * 2 * ff + c * 8;
+    float g[8], u[8], d[8], dg[8], du[8];
+    unpack<__nv_bfloat16>(ld_stream(src), g);
+    unpack<__nv_bfloat16>(ld_stream(src + ff), u);
+    unpack<__nv_bfloat16>(ld_stream(dy + r * ff + c * 8), d);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float s = sigmoid_f(u[k]);
+      dg[k] = d[k] * (u[k] * s);
+      du[k] = (d[k] * g[k]) * (s + u[k] * s * (1.f - s));
+    }
+    __nv_bfloat16* dst = dgu + r * 2 * ff + c * 8;
+    *reinterpret_cast<uint4*>(dst) = pack<__nv_bfloat16>(dg);
+    *reinterpret_cast<uint4*>(dst + ff) = pack<__nv_bfloat16>(du);
+  }
+}
+
+int glu_grid(int64_t rows, int64_t ff) {
+  const int64_t total = rows * (ff / 8);
+  int64_t g = (total + kGluThreads - 1) / kGluThreads;
+  if (g > kGluMaxBlocks) g = kGluMaxBlocks;
+  return (int)(g < 1 ? 1 : g);
+}
+
+int check_glu(const void* a, const void* b, int64_t rows, int64_t ff, const char* who) {
+  ALGX_REQUIRE(rows >= 0, std::string(who) + ": negative row count");
+  ALGX_REQUIRE(rows == 0 || (a && b), std::string(who) + ": NULL pointer");
+  ALGX_REQUIRE(ff > 0 && ff % 8 == 0, std::string(who) + ": hidden width must be a positive multiple of 8");
+  ALGX_REQUIRE((reinterpret_cast<uintptr_t>(a) & 15) == 0 && (reinterpret_cast<uintptr_t>(b) & 15) == 0,
+               std::string(who) + ": tensors must be 16-byte aligned");
+  return ALGX_OK;
+}
+
+}  // namespace
+}  // namespace algx
+
+using namespace algx;
+
+extern "C" {
+
+int algx_rmsnorm_fwd(const void* x, const float* gain, void* y, int64_t rows, int64_t dim, int32_t dtype, float eps,
+                     void* stream) {
+  if (int s = check_norm(x, y, rows, dim, dtype, eps, "rmsnorm_fwd")) return s;
+  if (rows == 0) return ALGX_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int C = norm_chunks(dim, dtype);
+  if (dtype == ALGX_BF16)
+    dispatch_norm_fwd<__nv_bfloat16>(C, x, gain, y, rows, (int)dim, eps, st);
+  else
+    dispatch_norm_fwd<float>(C, x, gain, y, rows, (int)dim, eps, st);
+  ALGX_LAUNCHED("rmsnorm_fwd launch");
+  return ALGX_OK;
+}
+
+size_t algx_rmsnorm_bwd_workspace_size(int64_t rows, int64_t dim) {
+  if (rows <= 0 || dim <= 0) return 0;
+  return (size_t)norm_grid(rows) * (size_t)dim * sizeof(float);
+}
+
+int algx_rmsnorm_bwd(const void* x, const float* gain, const void* dy, void* dx, float* dgain, int64_t rows,
+                     int64_t dim, int32_t dtype, float eps, void* workspace, size_t workspace_bytes, void* stream) {
+  if (int s = check_norm(x, dx, rows, dim, dtype, eps, "rmsnorm_bwd")) return s;
+  ALGX_REQUIRE(rows == 0 || dy, "rmsnorm_bwd: NULL pointer");
+  ALGX_REQUIRE((reinterpret_cast<uintptr_t>(dy) & 15) == 0, "rmsnorm_bwd: tensors must be 16-byte aligned");
+  ALGX_REQUIRE(!gain || dgain, "rmsnorm_bwd: a gain needs a dgain output");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (rows == 0) {
+    if (gain) ALGX_CUDA(cudaMemsetAsync(dgain, 0, (size_t)dim * sizeof(float), st));
+    return ALGX_OK;
+  }
+  const int grid = norm_grid(rows);
+  float* partial = nullptr;
+  if (gain) {
+    ALGX_REQUIRE(workspace && workspace_bytes >= (size_t)grid * (size_t)dim * sizeof(float),
+                 "rmsnorm_bwd: workspace too small (see algx_rmsnorm_bwd_workspace_size)");
+    partial = static_cast<float*>(workspace);
+  }
+  const int C = norm_chunks(dim, dtype);
+  if (dtype == ALGX_BF16)
+    ALGX_CUDA(dispatch_norm_bwd<__nv_bfloat16>(C, x, gain, dy, dx, partial, rows, (int)dim, eps, st));
+  else
+    ALGX_CUDA(dispatch_norm_bwd<float>(C, x, gain, dy, dx, partial, rows, (int)dim, eps, st));
+  ALGX_LAUNCHED("rmsnorm_bwd launch");
+  if (gain) {
+    rmsnorm_dgain_reduce<<<(unsigned)((dim + 31) / 32), 256, 0, st>>>(partial, grid, (int)dim, dgain);
+    ALGX_LAUNCHED("rmsnorm_dgain_reduce launch");
+  }
+  return ALGX_OK;
+}
+
+int algx_swiglu_fwd(const void* gu, void* y, int64_t rows, int64_t ff, void* stream) {
+  if (int s = check_glu(gu, y, rows, ff, "swiglu_fwd")) return s;
+  if (rows == 0) return ALGX_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  swiglu_fwd_kernel<<<glu_grid(rows, ff), kGluThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(gu),
+                                                                static_cast<__nv_bfloat16*>(y), rows, (int)ff);
+  ALGX_LAUNCHED("swiglu_fwd launch");
+  return ALGX_OK;
+}
+
+int algx_swiglu_bwd(const void* gu, const void* dy, void* dgu, int64_t rows, int64_t ff, void* stream) {
+  if (int s = check_glu(gu, dgu, rows, ff, "swiglu_bwd")) return s;
+  ALGX_REQUIRE((rows == 0 || dy) && (reinterpret_cast<uintptr_t>(dy) & 15) == 0,
+               "swiglu_bwd: dy NULL or not 16-byte aligned");
+  if (rows == 0) return ALGX_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  swiglu_bwd_kernel<<<glu_grid(rows, ff), kGluThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(gu),
+                                                                static_cast<const __nv_bfloat16*>(dy),
+                                                                static_cast<__nv_bfloat16*>(dgu), rows, (int)ff);
+  ALGX_LAUNCHED("swiglu_bwd launch");
+  return ALGX_OK;
+}
+
+}  // extern "C"

@@ -43,14 +43,17 @@ WORKLOAD = ("BASELINE config 2: QK-norm(q,k) -> causal asinh-power flash attenti
 HEAD_N, HEAD_V = 16384, 50304
 
 
-def _peaks():
+def _peaks(sustained=False):
+    """(bf16 TFLOP/s, HBM GB/s, source): the burst GEMM figure for a kernel timed
+    alone, the sustained one (power-capped loop) for a seconds-long step."""
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
         with open(path) as f:
             p = json.load(f)
-        return float(p["bf16_tflops"]), float(p["hbm_gbs"]), "measured"
+        tf = float(p["bf16_tflops_sustained"] if sustained else p["bf16_tflops"])
+        return tf, float(p["hbm_gbs"]), "measured"
     except (OSError, KeyError, ValueError):
-        return 1590.0, 6650.0, "fallback"
+        return (1400.0 if sustained else 1590.0), 6650.0, "fallback"
 
 
 def _traffic():
@@ -277,7 +280,52 @@ def secondary(dev, rank, world, stream, sync_all, max_over_ranks, steps=5, warmu
                         "unit": "TFLOP/s", "ms_per_step": ms,
                         "config": f"B={B4} H={H4} S={T} D={D} bf16 per GPU, QK-norm + guarded asinh n=16 c=8, "
                                   "public API (autograd)", "scaling": "weak"}
+    del q, k, v, do, gq, gk, leaves
+    trace("secondary: train cfg5")
+    out["train_cfg5"] = train_line(dev, rank, world, stream, sync_all, max_over_ranks)
     return out
+
+
+TRAIN_GLOBAL_BATCH = 64  # sequences per optimizer step, split over the ranks (config 5)
+
+
+def train_line(dev, rank, world, stream, sync_all, max_over_ranks, steps=3, warmup=3):
+    """Config 5: the 125M training step (fwd + bwd + clip + AdamW) on synthetic
+    uniform token ids, global batch 64 x 2048 split over the ranks, micro-batches
+    of 8 sequences, gradient all-reduce overlapped with the last backward."""
+    from algx.model import AlgebraicLM, config_125m, count_params, train_flops_per_token
+    from algx.train import DataParallelTrainer
+
+    cfg = config_125m()
+    per = TRAIN_GLOBAL_BATCH // world
+    micro = min(8, per)
+    model = AlgebraicLM(cfg, device=dev, seed=0)  # same initial replica on every rank
+    tr = DataParallelTrainer(model, micro_batch=micro)
+    g = torch.Generator(device=dev).manual_seed(777 + rank)
+    seq = torch.randint(0, cfg.vocab_size, (per, cfg.seq_len + 1), device=dev, generator=g)
+    tok, tgt = seq[:, :-1].contiguous(), seq[:, 1:].contiguous()
+    losses = []
+
+    def step():
+        losses.append(tr.step(tok, tgt))
+
+    ms = time_cuda(step, steps, warmup, stream, sync_all, max_over_ranks)
+    tokens = TRAIN_GLOBAL_BATCH * cfg.seq_len
+    tflops = train_flops_per_token(cfg) * tokens / (ms / 1e3) / 1e12
+    peak_tf, _, peak_src = _peaks(sustained=True)
+    line = {"metric": "125M train tok/s", "value": tokens / (ms / 1e3), "unit": "tok/s", "ms_per_step": ms,
+            "steps": steps, "warmup": warmup, "tflops_6P": tflops, "mfu": tflops / peak_tf,
+            "mfu_peak": f"{peak_tf:.1f} TFLOP/s {peak_src} bf16 dense (sustained)",
+            "loss_first": float(losses[0]), "loss_last": float(losses[-1]),
+            "params": count_params(cfg), "flop_per_token": train_flops_per_token(cfg),
+            "config": f"L={cfg.n_layers} d={cfg.d_model} H={cfg.n_heads} ff={cfg.d_ff} V={cfg.vocab_size} "
+                      f"S={cfg.seq_len}; QK-norm + RoPE + asinh n={cfg.attn_n} c={cfg.attn_c}, SwiGLU, "
+                      f"ce head; fp32 masters, bf16 compute; global batch {TRAIN_GLOBAL_BATCH} sequences, "
+                      f"{per} per rank in micro-batches of {micro}; clip 1.0; fused AdamW",
+            "data": "synthetic uniform token ids, seeded per rank",
+            "scaling": "strong (global batch fixed, split over the ranks)" if world > 1 else "single GPU"}
+    tr.close()
+    return line
 
 
 def run_algx(args, rank, world, local_rank):

@@ -237,6 +237,37 @@ ALGX_API int algx_head_bwd(const algx_head_config* cfg, const void* h, const voi
  * out: fp32 128 x nout. No counterpart in the reference (hardware check). */
 ALGX_API int algx_selftest_tcgen05(int32_t mode, const void* a, const void* b, float* out, void* stream);
 
+/* ------------------------------------------------ training-step elementwise */
+/* The model's own row norms and gate around the hot kernels, used by the
+ * config-5 training step (algx.model). bf16 or fp32 rows, fp32 maths. */
+
+/* y = rms_norm(x) * gain over rows of `dim` elements (dim a multiple of 16
+ * bytes, at most 4096 bf16 / 2048 fp32); gain NULL gives the parameter-free
+ * form. Replaces algebraic.py:76-83 `rms_norm` as the model calls it
+ * (model.py:158-159 `_norm`: ln1, ln2, embed_gain, final_gain). */
+ALGX_API int algx_rmsnorm_fwd(const void* x, const float* gain, void* y, int64_t rows, int64_t dim,
+                              int32_t dtype, float eps, void* stream);
+
+/* Bytes of workspace algx_rmsnorm_bwd needs (one fp32 row of dgain partials
+ * per CTA). */
+ALGX_API size_t algx_rmsnorm_bwd_workspace_size(int64_t rows, int64_t dim);
+
+/* dx and dgain of algx_rmsnorm_fwd (JAX AD of algebraic.py:76-83 in the
+ * reference's training step, model.py:158-159). dgain is summed in a fixed
+ * order (deterministic). gain NULL: no dgain, no workspace needed. */
+ALGX_API int algx_rmsnorm_bwd(const void* x, const float* gain, const void* dy, void* dx, float* dgain,
+                              int64_t rows, int64_t dim, int32_t dtype, float eps, void* workspace,
+                              size_t workspace_bytes, void* stream);
+
+/* y = gate * silu(up), bf16, for rows of gu = [gate (ff) | up (ff)]; y is
+ * (rows, ff). ff a multiple of 8. Replaces model.py:193-198 (`gate * act`,
+ * act = S.silu(up), standard.py:12-13), evaluated in fp32 and rounded once. */
+ALGX_API int algx_swiglu_fwd(const void* gu, void* y, int64_t rows, int64_t ff, void* stream);
+
+/* dgu = [dgate | dup] of algx_swiglu_fwd for the upstream gradient dy
+ * (rows, ff); JAX AD of model.py:193-198. */
+ALGX_API int algx_swiglu_bwd(const void* gu, const void* dy, void* dgu, int64_t rows, int64_t ff, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,164 @@
+"""GPU parity of the config-5 training step pieces: the row RMS norm and SwiGLU
+kernels against the float64 oracle / fp32 formulas, the model's loss and
+gradients against a float64 restatement of model.py with the same bf16
+rounding points, and the data-parallel step itself.
+
+Tolerances: RMS norm outputs within one bf16 ulp (fp32 I/O: 2e-6 relative),
+gradients within 1e-2 relative L2 (bf16) / 1e-5 (fp32); SwiGLU within one
+bf16 ulp forward and 1e-2 relative L2 backward; the 2-layer model's loss
+within 2e-3 relative and each parameter gradient within 3e-2 relative L2 of
+the restatement (bf16 activations through two blocks and the head).
+"""
+
+import math
+
+import pytest
+import torch
+
+from oracle import reference_math as R
+
+pytestmark = pytest.mark.gpu
+
+F64 = torch.float64
+
+
+def _rel_l2(a, b):
+    a, b = a.double(), b.double()
+    return float(torch.linalg.vector_norm(a - b) / torch.linalg.vector_norm(b).clamp_min(1e-300))
+
+
+@pytest.mark.parametrize("dtype,dim,rows", [(torch.bfloat16, 768, 1000), (torch.bfloat16, 1024, 37),
+                                            (torch.float32, 768, 515), (torch.bfloat16, 136, 64)])
+def test_rmsnorm_matches_oracle(dtype, dim, rows):
+    from algx.layers import rms_norm
+    g = torch.Generator().manual_seed(dim + rows)
+    x = (torch.randn((rows, dim), generator=g) * 3).to(dtype)
+    gain = 1 + 0.1 * torch.randn(dim, generator=g)
+    dy = torch.randn((rows, dim), generator=g).to(dtype)
+    xc, gc = x.cuda().requires_grad_(True), gain.cuda().requires_grad_(True)
+    y = rms_norm(xc, gc, 1e-5)
+    y.backward(dy.cuda())
+    ref = R.rms_norm(x.double(), gain.double(), 1e-5, io_dtype=dtype)
+    ulp = 2.0 ** -7 if dtype == torch.bfloat16 else 2e-6
+    assert torch.all((y.cpu().double() - ref).abs() <= ulp * ref.abs() + 1e-30)
+    dx, dgain = R.qk_norm_backward(x.double(), gain.double(), dy.double(), 1e-5)
+    tol = 1e-2 if dtype == torch.bfloat16 else 1e-5
+    assert _rel_l2(xc.grad.cpu(), dx) < tol
+    assert _rel_l2(gc.grad.cpu(), dgain) < 1e-5
+
+
+def test_rmsnorm_without_gain_and_empty():
+    from algx.layers import rms_norm
+    x = torch.randn((64, 256), device="cuda").to(torch.bfloat16).requires_grad_(True)
+    y = rms_norm(x, None)
+    ref = R.rms_norm(x.detach().cpu().double(), None, 1e-5, io_dtype=torch.bfloat16)
+    assert torch.all((y.detach().cpu().double() - ref).abs() <= 2.0 ** -7 * ref.abs())
+    y.sum().backward()
+    assert torch.isfinite(x.grad.float()).all()
+    e = torch.empty((0, 768), device="cuda", dtype=torch.bfloat16)
+    assert rms_norm(e, torch.ones(768, device="cuda")).shape == (0, 768)
+
+
+def test_swiglu_matches_fp32_formula():
+    from algx.layers import swiglu
+    g = torch.Generator().manual_seed(11)
+    rows, ff = 300, 2048
+    gu = (torch.randn((rows, 2 * ff), generator=g) * 2).to(torch.bfloat16)
+    dy = torch.randn((rows, ff), generator=g).to(torch.bfloat16)
+    x = gu.cuda().requires_grad_(True)
+    y = swiglu(x)
+    y.backward(dy.cuda())
+    gf = gu.double().requires_grad_(True)
+    gate, up = gf[:, :ff], gf[:, ff:]
+    ref = gate * (up * torch.sigmoid(up))
+    ref.backward(dy.double())
+    yr = ref.detach().to(torch.bfloat16).double()
+    assert torch.all((y.detach().cpu().double() - yr).abs() <= 2.0 ** -7 * yr.abs() + 1e-6)
+    assert _rel_l2(x.grad.cpu(), gf.grad) < 1e-2
+
+
+def _tiny_cfg(**kw):
+    from algx.model import LMConfig
+    base = dict(vocab_size=1000, d_model=128, n_layers=2, n_heads=2, d_ff=256, seq_len=256)
+    base.update(kw)
+    return LMConfig(**base)
+
+
+def _rb(x):
+    """Straight-through bf16 rounding (the reference's .astype(bf16) points)."""
+    return x + (x.to(torch.bfloat16).to(x.dtype) - x).detach()
+
+
+def _restated_loss(cfg, params, tokens, targets):
+    """model.py:184-226 in float64 with bf16 rounding of every stored activation."""
+    B, T = tokens.shape
+    d, H, D = cfg.d_model, cfg.n_heads, cfg.head_dim
+    P = lambda n: params[n]  # noqa: E731
+    cos, sin = R.rope_table(D, T, cfg.rope_base, dtype=F64)
+    x = _rb(P("embed")[tokens])
+    x = R.rms_norm(x, P("embed_gain"), cfg.eps, io_dtype=torch.bfloat16)
+    for i in range(cfg.n_layers):
+        p = lambda n: P(f"layers.{i}.{n}")  # noqa: E731
+        h = R.rms_norm(x, p("ln1"), cfg.eps, io_dtype=torch.bfloat16)
+        qkv = _rb(h @ _rb(p("w_qkv")))
+        q, k, v = (qkv[..., j * d:(j + 1) * d].reshape(B, T, H, D).transpose(1, 2) for j in range(3))
+        q = R.rms_norm(q, p("q_gain"), cfg.eps, io_dtype=torch.bfloat16)
+        k = R.rms_norm(k, p("k_gain"), cfg.eps, io_dtype=torch.bfloat16)
+        q = R.apply_rotary(q, cos, sin, io_dtype=torch.bfloat16)
+        k = R.apply_rotary(k, cos, sin, io_dtype=torch.bfloat16)
+        a = R.asinh_attention(q, k, v, n=cfg.attn_n, c=cfg.attn_c, io_dtype=torch.bfloat16)
+        a = a.transpose(1, 2).reshape(B, T, d)
+        x = _rb(x + _rb(a @ _rb(p("w_o"))))
+        h2 = R.rms_norm(x, p("ln2"), cfg.eps, io_dtype=torch.bfloat16)
+        gu = _rb(h2 @ _rb(p("w_gu")))
+        gate, up = gu[..., :cfg.d_ff], gu[..., cfg.d_ff:]
+        act = _rb(gate * (up * torch.sigmoid(up)))
+        x = _rb(x + _rb(act @ _rb(p("w_d"))))
+    hid = R.rms_norm(x, P("final_gain"), cfg.eps, io_dtype=torch.bfloat16)
+    z = hid.reshape(B * T, d) @ _rb(P("embed")).T
+    obj, _ = R.cross_entropy(z, targets.reshape(-1))
+    return obj
+
+
+def test_model_matches_float64_restatement():
+    from algx.model import AlgebraicLM
+    cfg = _tiny_cfg()
+    model = AlgebraicLM(cfg, device="cuda", seed=0)
+    g = torch.Generator().manual_seed(5)
+    seq = torch.randint(0, cfg.vocab_size, (2, cfg.seq_len + 1), generator=g)
+    tok, tgt = seq[:, :-1].contiguous(), seq[:, 1:].contiguous()
+    model.flat.zero_grad()
+    obj, _ = model.loss(tok.cuda(), tgt.cuda())
+    obj.backward()
+    torch.cuda.synchronize()
+    params = {n: p.detach().cpu().double().requires_grad_(True) for n, p in model.flat.params.items()}
+    ref = _restated_loss(cfg, params, tok, tgt)
+    ref.backward()
+    assert abs(float(obj) - float(ref)) <= 2e-3 * abs(float(ref)), (float(obj), float(ref))
+    bad = {}
+    for n, p in model.flat.params.items():
+        err = _rel_l2(p.grad.cpu(), params[n].grad)
+        if err > 3e-2:
+            bad[n] = err
+    assert not bad, bad
+    from algx import _lib as L
+    assert L.device_error() == 0
+
+
+def test_train_step_reduces_loss_on_a_fixed_batch():
+    from algx.model import AlgebraicLM
+    from algx.train import DataParallelTrainer
+    cfg = _tiny_cfg(sink="learned")
+    model = AlgebraicLM(cfg, device="cuda", seed=1)
+    tr = DataParallelTrainer(model, lr=3e-3, micro_batch=2)
+    g = torch.Generator(device="cuda").manual_seed(2)
+    seq = torch.randint(0, cfg.vocab_size, (4, cfg.seq_len + 1), device="cuda", generator=g)
+    tok, tgt = seq[:, :-1].contiguous(), seq[:, 1:].contiguous()
+    before = model.flat.data[True].clone()
+    losses = [float(tr.step(tok, tgt)) for _ in range(6)]
+    assert all(math.isfinite(l) for l in losses)
+    assert losses[-1] < losses[0] - 0.05, losses
+    assert not torch.equal(before, model.flat.data[True])
+    assert math.isfinite(float(tr.last_gnorm))
+    from algx import _lib as L
+    assert L.device_error() == 0
