@@ -89,11 +89,20 @@ SIGNATURES = {
     "algx_head_bwd_workspace_size": ([_I64, _I64, _I64, _I32], ctypes.c_size_t),
     "algx_head_bwd": ([ctypes.POINTER(HeadConfig), _P, _P, _P, _P, _P, _P, _I32, _P, _I64, _I64, _I64, _I64, _I32,
                        _P, ctypes.c_size_t, _P], ctypes.c_int),
+    "algx_qknorm_attn_prepare_packed": ([ctypes.POINTER(AttnConfig)] + [_P] * 5 + [_I64] + [_P] * 5 +
+                                        [_I64, _I64, _I64, _I64, _I32, _F, _P], ctypes.c_int),
+    "algx_qknorm_attn_bwd_packed_workspace_size": ([_I64, _I64, _I64, _I64, _I32], _SZ),
+    "algx_qknorm_attn_bwd_packed": ([ctypes.POINTER(AttnConfig)] + [_P] * 5 + [_I64] + [_P] * 13 +
+                                    [_I64, _I64, _I64, _I64, _I32, _F, _P, _SZ, _P], ctypes.c_int),
+    "algx_heads_to_tokens": ([_P, _P, _I64, _I64, _I64, _I64, _I32, _P], ctypes.c_int),
+    "algx_tokens_to_heads": ([_P, _P, _I64, _I64, _I64, _I64, _I32, _P], ctypes.c_int),
     "algx_rmsnorm_fwd": ([_P, _P, _P, _I64, _I64, _I32, _F, _P], ctypes.c_int),
     "algx_rmsnorm_bwd_workspace_size": ([_I64, _I64], _SZ),
     "algx_rmsnorm_bwd": ([_P, _P, _P, _P, _P, _I64, _I64, _I32, _F, _P, _SZ, _P], ctypes.c_int),
     "algx_swiglu_fwd": ([_P, _P, _I64, _I64, _P], ctypes.c_int),
     "algx_swiglu_bwd": ([_P, _P, _P, _I64, _I64, _P], ctypes.c_int),
+    "algx_aluglu_fwd": ([_P, _P, _I64, _I64, _F, _P], ctypes.c_int),
+    "algx_aluglu_bwd": ([_P, _P, _P, _I64, _I64, _F, _P], ctypes.c_int),
     "algx_selftest_tcgen05": ([_I32, _P, _P, _P, _P], ctypes.c_int),
 }
 

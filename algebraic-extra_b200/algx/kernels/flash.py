@@ -357,3 +357,88 @@ def qknorm_call_args(q, k, v, gain_q, gain_k, sink_logit, eps, kind, n, c, block
     if gq.shape != (64,) or gk.shape != (64,):
         raise ValueError("gains must have shape (64,)")
     return cfg, sink, gq, gk
+
+
+# ------------------------------------------------------------ packed layout
+def qknorm_attn_forward_packed(qkv, gain_q, gain_k, sink, cfg: L.AttnConfig, eps: float, rotary=None):
+    """Forward launch group on the packed token-major qkv (B, T, 3, H, D):
+    the prologue reads q, k, v in place and writes head-major q_scaled, k_norm
+    and v; the attention kernels run head-major; the output is permuted to
+    token-major (B, T, H, D). Returns (o_tokens, saved)."""
+    B, T, _, H, D = qkv.shape
+    lib = L.lib()
+    dt = L.dtype_code(qkv.dtype)
+    st = L.stream_of(qkv)
+    q_s = torch.empty((B, H, T, D), dtype=qkv.dtype, device=qkv.device)
+    k_n = torch.empty_like(q_s)
+    v_h = torch.empty_like(q_s)
+    guard = torch.empty(4, dtype=torch.float32, device=qkv.device)
+    L.check(lib.algx_qknorm_attn_prepare_packed(cfg, qkv.data_ptr(), gain_q.data_ptr(), gain_k.data_ptr(),
+                                                *_rot_args(rotary), L.ptr(sink), q_s.data_ptr(), k_n.data_ptr(),
+                                                v_h.data_ptr(), guard.data_ptr(), B, H, T, D, dt, float(eps), st),
+            "algx_qknorm_attn_prepare_packed")
+    o, saved = attn_forward_prepared(q_s, k_n, v_h, sink, guard, cfg)
+    o_tok = torch.empty((B, T, H, D), dtype=qkv.dtype, device=qkv.device)
+    L.check(lib.algx_heads_to_tokens(o.data_ptr(), o_tok.data_ptr(), B, H, T, D, dt, st), "algx_heads_to_tokens")
+    return o_tok, saved
+
+
+def qknorm_attn_backward_packed(qkv, gain_q, gain_k, saved, cfg: L.AttnConfig, do_tok, eps: float, rotary=None):
+    """Backward of :func:`qknorm_attn_forward_packed`: (dqkv, dgain_q, dgain_k, dsink)."""
+    q_s, k_n, v_h, sink, o, o_prec, stat, guard = saved
+    B, H, T, D = q_s.shape
+    lib = L.lib()
+    dt = L.dtype_code(q_s.dtype)
+    st = L.stream_of(q_s)
+    do_tok = do_tok.to(q_s.dtype).contiguous()
+    do = torch.empty_like(q_s)
+    L.check(lib.algx_tokens_to_heads(do_tok.data_ptr(), do.data_ptr(), B, H, T, D, dt, st), "algx_tokens_to_heads")
+    dqkv = torch.empty_like(qkv)
+    dgq = torch.empty(D, dtype=torch.float32, device=q_s.device)
+    dgk = torch.empty(D, dtype=torch.float32, device=q_s.device)
+    dsink = torch.empty(H, dtype=torch.float32, device=q_s.device) if sink is not None else None
+    nbytes = lib.algx_qknorm_attn_bwd_packed_workspace_size(B, H, T, D, dt)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=q_s.device)
+    L.check(lib.algx_qknorm_attn_bwd_packed(cfg, qkv.data_ptr(), gain_q.data_ptr(), gain_k.data_ptr(),
+                                            *_rot_args(rotary), q_s.data_ptr(), k_n.data_ptr(), v_h.data_ptr(),
+                                            L.ptr(sink), guard.data_ptr(), o.data_ptr(), L.ptr(o_prec),
+                                            stat.data_ptr(), do.data_ptr(), dqkv.data_ptr(), dgq.data_ptr(),
+                                            dgk.data_ptr(), L.ptr(dsink), B, H, T, D, dt, float(eps), ws.data_ptr(),
+                                            nbytes, st), "algx_qknorm_attn_bwd_packed")
+    return dqkv, dgq, dgk, dsink
+
+
+class _QKNormFlashPacked(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv, gain_q, gain_k, sink, cfg: L.AttnConfig, eps: float, rotary):
+        o, saved = qknorm_attn_forward_packed(qkv, gain_q, gain_k, sink, cfg, eps, rotary)
+        ctx.cfg, ctx.eps, ctx.rotary = cfg, eps, rotary
+        ctx.save_for_backward(qkv, gain_q, gain_k, *saved)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        qkv, gain_q, gain_k, *saved = ctx.saved_tensors
+        dqkv, dgq, dgk, dsink = qknorm_attn_backward_packed(qkv, gain_q, gain_k, saved, ctx.cfg, do, ctx.eps,
+                                                            rotary=ctx.rotary)
+        return dqkv, dgq, dgk, dsink, None, None, None
+
+
+def qknorm_flash_attention_packed(qkv, gain_q, gain_k, sink_logit=None, *, eps: float = 1e-5, kind: str = "asinh",
+                                  n: int = 16, c: float = 16.0, block: int = 512, range_guard: bool = False,
+                                  shift: Optional[bool] = None, fast_rho: Optional[bool] = None,
+                                  inv_stat: Optional[bool] = None, rotary=None):
+    """:func:`qknorm_flash_attention` on the token-major output of one QKV
+    projection: ``qkv`` (B, T, 3, H, D) holds [q | k | v] per token; returns
+    the attention output token-major (B, T, H, D), ready for the output
+    projection (model.py:166-180 without the transposes). Same values and
+    gradients as transposing q, k, v to (B, H, T, D), calling
+    :func:`qknorm_flash_attention` and transposing back."""
+    if qkv.ndim != 5 or qkv.shape[2] != 3:
+        raise ValueError(f"qkv must have shape (B, T, 3, H, D), got {tuple(qkv.shape)}")
+    qkv = qkv.contiguous()
+    q_view = qkv[:, :, 0].permute(0, 2, 1, 3)  # shapes and dtypes for validation only
+    cfg, sink, gq, gk = qknorm_call_args(q_view, q_view, q_view, gain_q, gain_k, sink_logit, eps, kind, n, c, block,
+                                         range_guard, shift, fast_rho, inv_stat)
+    rot = rotary_tables(rotary, q_view)
+    return _QKNormFlashPacked.apply(qkv, gq, gk, sink, cfg, float(eps), rot)

@@ -1,9 +1,10 @@
-"""Row RMS norm and SwiGLU over libalgx, as autograd functions.
+"""Row RMS norm, SwiGLU and ALU-GLU over libalgx, as autograd functions.
 
 These are the model's own elementwise layers around the three hot kernels
-(model.py:158-159 ``_norm`` and model.py:193-198 ``gate * silu(up)``), each
-one fused launch forward and one backward, for the config-5 training step in
-``algx.model``. Like the hot kernels they run on CUDA tensors only.
+(model.py:158-159 ``_norm``; model.py:193-198 ``gate * silu(up)`` or
+``gate * alu(up)``), each one fused launch forward and one backward, for the
+config-5 training step in ``algx.model``. Like the hot kernels they run on
+CUDA tensors only.
 """
 
 from __future__ import annotations
@@ -109,3 +110,39 @@ def swiglu(gu: torch.Tensor) -> torch.Tensor:
         raise ValueError("swiglu needs an even hidden width that is a multiple of 8")
     L.require_cuda(gu)
     return _SwiGLU.apply(gu)
+
+
+class _ALUGLU(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, gu, beta):
+        gu = gu.contiguous()
+        ff = gu.shape[-1] // 2
+        rows = gu.numel() // gu.shape[-1]
+        y = torch.empty(gu.shape[:-1] + (ff,), dtype=gu.dtype, device=gu.device)
+        L.check(L.lib().algx_aluglu_fwd(gu.data_ptr(), y.data_ptr(), rows, ff, float(beta), L.stream_of(gu)),
+                "algx_aluglu_fwd")
+        ctx.save_for_backward(gu)
+        ctx.beta = float(beta)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        (gu,) = ctx.saved_tensors
+        ff = gu.shape[-1] // 2
+        rows = gu.numel() // gu.shape[-1]
+        dy = dy.to(gu.dtype).contiguous()
+        dgu = torch.empty_like(gu)
+        L.check(L.lib().algx_aluglu_bwd(gu.data_ptr(), dy.data_ptr(), dgu.data_ptr(), rows, ff, ctx.beta,
+                                        L.stream_of(gu)), "algx_aluglu_bwd")
+        return dgu, None
+
+
+def aluglu(gu: torch.Tensor, beta: float = 1.0) -> torch.Tensor:
+    """``gate * alu(up, beta)`` for ``gu = [gate | up]`` on the last axis (model.py:196-197,
+    algebraic.py:86-113), bf16: the algebraic preset's gate (``ffn="alu_glu"``)."""
+    if gu.dtype != torch.bfloat16:
+        raise ValueError("aluglu needs bfloat16 input")
+    if gu.shape[-1] % 16:
+        raise ValueError("aluglu needs an even hidden width that is a multiple of 8")
+    L.require_cuda(gu)
+    return _ALUGLU.apply(gu, float(beta))

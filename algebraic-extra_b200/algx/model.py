@@ -2,16 +2,17 @@
 
 Mirrors the reference's ``LMConfig`` / ``init_params`` / ``forward_hidden`` /
 ``head_loss`` (model.py:25-226) for the configuration its training-step
-benchmark names: learned RMS gains, SwiGLU, RoPE (or geometric Cayley)
-rotations, QK norm, causal asinh-power attention with the range guard, an
-optional learned per-head sink, and a tied-embedding ``ce`` or ``alg_ce``
-head. Per block (model.py:184-200):
+benchmark names: learned RMS gains, SwiGLU, RoPE, QK norm, causal
+asinh-power attention with the range guard and a tied-embedding ``ce`` head;
+and the reference's pure algebraic preset (ALU-GLU, geometric Cayley
+rotations, a learned per-head sink, the ``alg_ce`` head). Per block (model.py:184-200):
 
     h  = rms_norm(x, ln1)
-    q, k, v = h @ [w_q | w_k | w_v]               one GEMM, (B,T,3,H,D) -> (3,B,H,T,D)
-    a  = attention(rot(qk_norm(q)), rot(qk_norm(k)), v)   fused prologue + tcgen05 kernels
+    qkv = h @ [w_q | w_k | w_v]                   one GEMM, token-major (B, T, 3, H, D)
+    a  = attention(rot(qk_norm(q)), rot(qk_norm(k)), v)   read from qkv in place by the fused
+                                                  prologue; tcgen05 kernels; output (B, T, H, D)
     x  = x + a @ w_o
-    x  = x + swiglu(rms_norm(x, ln2) @ [w_g | w_u]) @ w_d
+    x  = x + glu(rms_norm(x, ln2) @ [w_g | w_u]) @ w_d      glu: SwiGLU or ALU-GLU
 
 Parameters are float32 masters; every matmul casts its weight to bfloat16
 (``.astype(dt)`` in model.py:167-196), so gradients reach the masters in
@@ -37,9 +38,9 @@ import torch
 from torch import nn
 
 from . import rotary as R
-from .kernels.flash import qknorm_flash_attention
+from .kernels.flash import qknorm_flash_attention_packed
 from .kernels.fused_head import fused_head
-from .layers import rms_norm, swiglu
+from .layers import aluglu, rms_norm, swiglu
 
 BF16 = torch.bfloat16
 
@@ -55,6 +56,8 @@ class LMConfig:
     d_ff: int = 2048
     seq_len: int = 2048
     eps: float = 1e-5
+    ffn: str = "swiglu"          # "swiglu" or "alu_glu"
+    alu_beta: float = 1.0
     pos: str = "rope"            # "rope" or "cayley_geo"
     rope_base: float = 10000.0
     rope_fraction: float = 1.0
@@ -77,6 +80,8 @@ class LMConfig:
             raise ValueError("d_model must be divisible by n_heads")
         if self.head_dim != 64:
             raise ValueError("the algx attention kernels need head_dim = 64")
+        if self.ffn not in ("swiglu", "alu_glu"):
+            raise ValueError(f"unknown ffn {self.ffn!r}")
         if self.pos not in ("rope", "cayley_geo"):
             raise ValueError(f"unknown position kind {self.pos!r}")
         if self.sink not in ("none", "const", "learned"):
@@ -90,6 +95,14 @@ def config_125m(**overrides) -> LMConfig:
     asinh-power attention n=16, c=8 (config.py:33), RoPE, SwiGLU, the ``ce``
     head and a 50304-token vocabulary."""
     return replace(LMConfig(), **overrides)
+
+
+def config_algebraic_125m(**overrides) -> LMConfig:
+    """The reference's pure algebraic preset at the 125M size (config.py:25-36):
+    ALU-GLU with beta 1/2, geometric Cayley rotations, QK norm, rho(s/8)^16
+    attention with a learned per-head sink, and the rho(z/2)^8 likelihood head."""
+    return replace(LMConfig(ffn="alu_glu", alu_beta=0.5, pos="cayley_geo", sink="learned", sink_init=0.0,
+                            head="alg_ce", head_n=8, head_c=2.0), **overrides)
 
 
 @dataclass(frozen=True)
@@ -211,21 +224,21 @@ class AlgebraicLM(nn.Module):
         H, D = cfg.n_heads, cfg.head_dim
         p = lambda n: self.flat[f"layers.{i}.{n}"]  # noqa: E731
         h = rms_norm(x, p("ln1"), cfg.eps)
-        qkv = (h @ p("w_qkv").to(BF16)).view(B, T, 3, H, D).permute(2, 0, 3, 1, 4).contiguous()
-        q, k, v = torch.unbind(qkv, 0)
+        qkv = (h @ p("w_qkv").to(BF16)).view(B, T, 3, H, D)  # token-major [q | k | v], no copy
         if cfg.sink == "learned":
             sink = p("sink")
         elif cfg.sink == "const":
             sink = torch.full((H,), cfg.sink_init, dtype=torch.float32, device=x.device)
         else:
             sink = None
-        a = qknorm_flash_attention(q, k, v, p("q_gain"), p("k_gain"), sink, eps=cfg.eps, kind="asinh",
-                                   n=cfg.attn_n, c=cfg.attn_c, range_guard=True,
-                                   rotary=(self.rot_cos, self.rot_sin))
-        a = a.permute(0, 2, 1, 3).reshape(B, T, d)
-        x = x + a @ p("w_o").to(BF16)
+        a = qknorm_flash_attention_packed(qkv, p("q_gain"), p("k_gain"), sink, eps=cfg.eps, kind="asinh",
+                                          n=cfg.attn_n, c=cfg.attn_c, range_guard=True,
+                                          rotary=(self.rot_cos, self.rot_sin))
+        x = x + a.view(B, T, d) @ p("w_o").to(BF16)
         h2 = rms_norm(x, p("ln2"), cfg.eps)
-        return x + swiglu(h2 @ p("w_gu").to(BF16)) @ p("w_d").to(BF16)
+        gu = h2 @ p("w_gu").to(BF16)
+        act = swiglu(gu) if cfg.ffn == "swiglu" else aluglu(gu, cfg.alu_beta)
+        return x + act @ p("w_d").to(BF16)
 
     def forward_hidden(self, tokens: torch.Tensor) -> torch.Tensor:
         """Final normalised hidden states (B, T, d) in bf16 (model.py:203-215)."""

@@ -113,12 +113,28 @@ __device__ __forceinline__ void rotate_half(float (&x)[Vec<T>::N], const float* 
   }
 }
 
+// Row of head-major index row = (b*H + h)*T + t in a token-major tensor whose
+// rows (b, t) hold `stride` rows of 64 elements, head h at offset h (the
+// caller offsets the base pointer to the q, k or v block). stride 0: the
+// tensor is head-major itself.
+__device__ __forceinline__ int64_t tok_row(int64_t row, int T_, int H, int stride) {
+  if (stride == 0) return row;
+  const int64_t bh = row / T_;
+  const int64_t t = row - bh * T_;
+  const int64_t b = bh / H;
+  const int64_t h = bh - b * H;
+  return (b * T_ + t) * stride + h;
+}
+
+// in_stride > 0: q, k, v are the blocks of one token-major (B, T, 3, H, D)
+// tensor (row stride in_stride = 3H), and vh (when not NULL) receives v in
+// head-major order for the TMA-fed attention kernels.
 template <typename T, bool ROT>
 __global__ void __launch_bounds__(kPrepThreads) qknorm_attn_prepare_kernel(
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v, const float* __restrict__ gain_q,
     const float* __restrict__ gain_k, const float* __restrict__ rot_cos, const float* __restrict__ rot_sin,
     const float* __restrict__ sink, int H, int T_, T* __restrict__ qs, T* __restrict__ kn, float* guard,
-    int64_t rows, float scale, float eps) {
+    int64_t rows, float scale, float eps, int in_stride, T* __restrict__ vh) {
   pdl_trigger();  // the forward kernel may be scheduled behind this grid (it waits for it)
   using V = Vec<T>;
   constexpr int kUnroll = 4;
@@ -140,7 +156,8 @@ __global__ void __launch_bounds__(kPrepThreads) qknorm_attn_prepare_kernel(
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
       const int64_t row = r0 + u * V::RPW + rl;
-      raw[u] = row < rows ? ld_stream(src + row * kD + sub * V::N) : make_uint4(0, 0, 0, 0);
+      raw[u] = row < rows ? ld_stream(src + tok_row(row, T_, H, in_stride) * kD + sub * V::N)
+                          : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
@@ -151,6 +168,7 @@ __global__ void __launch_bounds__(kPrepThreads) qknorm_attn_prepare_kernel(
       if (which == 2) {
 #pragma unroll
         for (int i = 0; i < V::N; ++i) local = nan_max(local, fabsf(x[i]));
+        if (vh != nullptr && ok) *reinterpret_cast<uint4*>(vh + row * kD + sub * V::N) = raw[u];
         continue;
       }
       float ss = 0.f;
@@ -680,10 +698,14 @@ constexpr int kEpiUnroll = 4;
 
 // All loads of a thread's kEpiUnroll rows are issued before any is used, so
 // that enough bytes are in flight to keep HBM busy at one CTA per SM.
+// x and dx_out are head-major (tok_stride 0) or blocks of a token-major
+// (B, T, 3, H, D) tensor (tok_stride 3H); dy_in (when not FROM_ACC) and acc
+// are head-major. dy_in may equal dx_out (the in-place head-major call).
 template <typename T, bool FROM_ACC>
-__device__ __forceinline__ void qk_rows_bwd(const T* __restrict__ x, const float* __restrict__ gain, T* dxy,
-                                            const float* __restrict__ acc, float f, const float* __restrict__ rot_cos,
-                                            const float* __restrict__ rot_sin, int T_, int64_t rows, float eps,
+__device__ __forceinline__ void qk_rows_bwd(const T* __restrict__ x, const float* __restrict__ gain, const T* dy_in,
+                                            T* dx_out, const float* __restrict__ acc, float f,
+                                            const float* __restrict__ rot_cos, const float* __restrict__ rot_sin,
+                                            int T_, int H, int tok_stride, int64_t rows, float eps,
                                             float (&part)[Vec<T>::N]) {
   using V = Vec<T>;
   constexpr int kA = FROM_ACC ? V::N / 4 : 1;  // 16-byte chunks of fp32 accumulator per thread and row
@@ -699,13 +721,13 @@ __device__ __forceinline__ void qk_rows_bwd(const T* __restrict__ x, const float
     for (int u = 0; u < kEpiUnroll; ++u) {
       const int64_t row = r0 + u * V::RPW + rl;
       const bool ok = row < rows;
-      rx[u] = ok ? ld_stream(x + row * kD + sub * V::N) : make_uint4(0, 0, 0, 0);
+      rx[u] = ok ? ld_stream(x + tok_row(row, T_, H, tok_stride) * kD + sub * V::N) : make_uint4(0, 0, 0, 0);
 #pragma unroll
       for (int c = 0; c < kA; ++c) {
         if constexpr (FROM_ACC)
           rd[u][c] = ok ? ld_stream(acc + row * kD + sub * V::N + 4 * c) : make_uint4(0, 0, 0, 0);
         else
-          rd[u][c] = ok ? *reinterpret_cast<const uint4*>(dxy + row * kD + sub * V::N) : make_uint4(0, 0, 0, 0);
+          rd[u][c] = ok ? *reinterpret_cast<const uint4*>(dy_in + row * kD + sub * V::N) : make_uint4(0, 0, 0, 0);
       }
     }
 #pragma unroll
@@ -741,7 +763,31 @@ __device__ __forceinline__ void qk_rows_bwd(const T* __restrict__ x, const float
         out[i] = (dv[i] * g[i]) * tau - xv[i] * corr;
         part[i] = fmaf(dv[i], xv[i] * tau, part[i]);
       }
-      if (row < rows) *reinterpret_cast<uint4*>(dxy + row * kD + sub * V::N) = pack<T>(out);
+      if (row < rows)
+        *reinterpret_cast<uint4*>(dx_out + tok_row(row, T_, H, tok_stride) * kD + sub * V::N) = pack<T>(out);
+    }
+  }
+}
+
+// dv_out (token-major block, tok_stride) = dv_in (head-major), row by row.
+template <typename T>
+__device__ __forceinline__ void copy_rows_to_tokens(const T* __restrict__ dv_in, T* __restrict__ dv_out, int T_, int H,
+                                                    int tok_stride, int64_t rows) {
+  using V = Vec<T>;
+  const int lane = threadIdx.x & 31, sub = lane % V::TPR, rl = lane / V::TPR;
+  const int64_t warps = (int64_t)gridDim.x * (kEpiThreads / 32);
+  const int64_t w = (int64_t)blockIdx.x * (kEpiThreads / 32) + (threadIdx.x >> 5);
+  for (int64_t r0 = w * V::RPW * kEpiUnroll; r0 < rows; r0 += warps * V::RPW * kEpiUnroll) {
+    uint4 raw[kEpiUnroll];
+#pragma unroll
+    for (int u = 0; u < kEpiUnroll; ++u) {
+      const int64_t row = r0 + u * V::RPW + rl;
+      raw[u] = row < rows ? ld_stream(dv_in + row * kD + sub * V::N) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < kEpiUnroll; ++u) {
+      const int64_t row = r0 + u * V::RPW + rl;
+      if (row < rows) *reinterpret_cast<uint4*>(dv_out + tok_row(row, T_, H, tok_stride) * kD + sub * V::N) = raw[u];
     }
   }
 }
@@ -752,7 +798,8 @@ __global__ void __launch_bounds__(kEpiThreads) qknorm_attn_bwd_kernel(
     const T* __restrict__ q, const float* __restrict__ gain_q, const T* __restrict__ k,
     const float* __restrict__ gain_k, const float* __restrict__ rot_cos, const float* __restrict__ rot_sin, int T_,
     T* dq_x, T* dk_x, float* __restrict__ partial, unsigned* counter, float* __restrict__ dgain_q,
-    float* __restrict__ dgain_k, int64_t rows, float eps) {
+    float* __restrict__ dgain_k, int64_t rows, float eps, int H, int tok_stride, const T* dq_in, const T* dk_in,
+    const T* __restrict__ dv_in, T* __restrict__ dv_out) {
   pdl_wait();  // launched as a dependent of the attention backward
   using V = Vec<T>;
   __shared__ float red[kEpiThreads / 32 * V::RPW][2 * kD];  // per row slot of a warp: q and k column sums
@@ -763,10 +810,12 @@ __global__ void __launch_bounds__(kEpiThreads) qknorm_attn_bwd_kernel(
 #pragma unroll
   for (int i = 0; i < V::N; ++i) pq[i] = pk[i] = 0.f;
   if (use_acc)
-    qk_rows_bwd<T, true>(q, gain_q, dq_x, dq_acc, (float)cfg.n * cfg.scale, rot_cos, rot_sin, T_, rows, eps, pq);
+    qk_rows_bwd<T, true>(q, gain_q, nullptr, dq_x, dq_acc, (float)cfg.n * cfg.scale, rot_cos, rot_sin, T_, H,
+                         tok_stride, rows, eps, pq);
   else
-    qk_rows_bwd<T, false>(q, gain_q, dq_x, nullptr, 1.f, rot_cos, rot_sin, T_, rows, eps, pq);
-  qk_rows_bwd<T, false>(k, gain_k, dk_x, nullptr, 1.f, rot_cos, rot_sin, T_, rows, eps, pk);
+    qk_rows_bwd<T, false>(q, gain_q, dq_in, dq_x, nullptr, 1.f, rot_cos, rot_sin, T_, H, tok_stride, rows, eps, pq);
+  qk_rows_bwd<T, false>(k, gain_k, dk_in, dk_x, nullptr, 1.f, rot_cos, rot_sin, T_, H, tok_stride, rows, eps, pk);
+  if (dv_in != nullptr) copy_rows_to_tokens<T>(dv_in, dv_out, T_, H, tok_stride, rows);
   // CTA column sums: slot (warp, row-in-warp) holds its threads' columns
   const int lane = threadIdx.x & 31, sub = lane % V::TPR, rl = lane / V::TPR;
   const int slot = (threadIdx.x >> 5) * V::RPW + rl;
@@ -863,10 +912,17 @@ int algx_attn_prepare(const algx_attn_config* cfg, const void* q, const void* k,
   return ALGX_OK;
 }
 
-int algx_qknorm_attn_prepare(const algx_attn_config* cfg, const void* q, const void* k, const void* v,
-                             const float* gain_q, const float* gain_k, const float* rope_cos, const float* rope_sin,
-                             int64_t rope_rows, const float* sink, void* q_scaled, void* k_norm, float* guard,
-                             int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype, float eps, void* stream) {
+}  // extern "C"
+
+namespace algx {
+namespace {
+// Shared body of the head-major and packed prologues: q, k, v point at the
+// first row of each block, in_stride as in qknorm_attn_prepare_kernel.
+int qknorm_prepare_impl(const algx_attn_config* cfg, const void* q, const void* k, const void* v,
+                        const float* gain_q, const float* gain_k, const float* rope_cos, const float* rope_sin,
+                        int64_t rope_rows, const float* sink, void* q_scaled, void* k_norm, void* v_heads,
+                        float* guard, int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype, float eps,
+                        int in_stride, void* stream) {
   if (int s = check_attn(cfg, B, H, T, D, dtype)) return s;
   ALGX_REQUIRE(q && k && v && gain_q && gain_k && q_scaled && k_norm && guard, "qknorm_attn_prepare: NULL pointer");
   ALGX_REQUIRE((rope_cos == nullptr) == (rope_sin == nullptr), "qknorm_attn_prepare: give both rotary tables or none");
@@ -883,7 +939,8 @@ int algx_qknorm_attn_prepare(const algx_attn_config* cfg, const void* q, const v
   auto launch = [&](auto kern, auto tag) {
     using TT = decltype(tag);
     kern<<<grid, kPrepThreads, 0, st>>>((const TT*)q, (const TT*)k, (const TT*)v, gain_q, gain_k, rope_cos, rope_sin,
-                                        sk, (int)H, (int)T, (TT*)q_scaled, (TT*)k_norm, guard, rows, cfg->scale, eps);
+                                        sk, (int)H, (int)T, (TT*)q_scaled, (TT*)k_norm, guard, rows, cfg->scale, eps,
+                                        in_stride, (TT*)v_heads);
   };
   if (dtype == ALGX_BF16)
     rope_cos ? launch(qknorm_attn_prepare_kernel<__nv_bfloat16, true>, __nv_bfloat16{})
@@ -893,6 +950,32 @@ int algx_qknorm_attn_prepare(const algx_attn_config* cfg, const void* q, const v
              : launch(qknorm_attn_prepare_kernel<float, false>, float{});
   ALGX_LAUNCHED("qknorm_attn_prepare launch");
   return ALGX_OK;
+}
+}  // namespace
+}  // namespace algx
+
+extern "C" {
+
+int algx_qknorm_attn_prepare(const algx_attn_config* cfg, const void* q, const void* k, const void* v,
+                             const float* gain_q, const float* gain_k, const float* rope_cos, const float* rope_sin,
+                             int64_t rope_rows, const float* sink, void* q_scaled, void* k_norm, float* guard,
+                             int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype, float eps, void* stream) {
+  return qknorm_prepare_impl(cfg, q, k, v, gain_q, gain_k, rope_cos, rope_sin, rope_rows, sink, q_scaled, k_norm,
+                             nullptr, guard, B, H, T, D, dtype, eps, 0, stream);
+}
+
+int algx_qknorm_attn_prepare_packed(const algx_attn_config* cfg, const void* qkv, const float* gain_q,
+                                    const float* gain_k, const float* rope_cos, const float* rope_sin,
+                                    int64_t rope_rows, const float* sink, void* q_scaled, void* k_norm, void* v_heads,
+                                    float* guard, int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype,
+                                    float eps, void* stream) {
+  ALGX_REQUIRE(qkv && v_heads, "qknorm_attn_prepare_packed: NULL pointer");
+  ALGX_REQUIRE(H > 0 && 3 * H <= INT32_MAX, "qknorm_attn_prepare_packed: bad head count");
+  const size_t es = dtype == ALGX_BF16 ? 2 : 4;
+  const char* base = static_cast<const char*>(qkv);
+  const size_t blk = (size_t)H * (size_t)D * es;  // bytes between the q, k and v blocks of a token row
+  return qknorm_prepare_impl(cfg, base, base + blk, base + 2 * blk, gain_q, gain_k, rope_cos, rope_sin, rope_rows,
+                             sink, q_scaled, k_norm, v_heads, guard, B, H, T, D, dtype, eps, (int)(3 * H), stream);
 }
 
 int algx_attn_fwd(const algx_attn_config* cfg, const void* q_scaled, const void* k, const void* v, const float* sink,
@@ -1043,16 +1126,26 @@ size_t algx_qknorm_attn_bwd_workspace_size(int64_t B, int64_t H, int64_t T, int6
   return ws_off_epi(B, H, T, D) + epi_bytes();
 }
 
-int algx_qknorm_attn_bwd(const algx_attn_config* cfg, const void* q, const void* k, const float* gain_q,
+}  // extern "C"
+
+namespace algx {
+namespace {
+// Shared body of the head-major and packed backward calls. q_src/k_src: the
+// raw (pre-norm) q and k, head-major (tok_stride 0) or blocks of the packed
+// (B, T, 3, H, D) input (tok_stride 3H); dq_out/dk_out likewise. The
+// attention backward writes its dq, dk, dv into dq_h, dk_h, dv_h (head-major);
+// with dv_out set, the epilogue also copies dv_h into it.
+int qknorm_attn_bwd_impl(const algx_attn_config* cfg, const void* q_src, const void* k_src, const float* gain_q,
                          const float* gain_k, const float* rope_cos, const float* rope_sin, int64_t rope_rows,
-                         const void* q_scaled, const void* k_norm, const void* v,
-                         const float* sink, const float* guard, const void* o, const float* o_precise,
-                         const float* stat, const void* dout, void* dq, void* dk, void* dv, float* dgain_q,
-                         float* dgain_k, float* dsink, int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype,
-                         float eps, void* workspace, size_t workspace_bytes, void* stream) {
+                         const void* q_scaled, const void* k_norm, const void* v, const float* sink,
+                         const float* guard, const void* o, const float* o_precise, const float* stat,
+                         const void* dout, void* dq_h, void* dk_h, void* dv_h, void* dq_out, void* dk_out,
+                         void* dv_out, int tok_stride, float* dgain_q, float* dgain_k, float* dsink, int64_t B,
+                         int64_t H, int64_t T, int64_t D, int32_t dtype, float eps, void* workspace,
+                         size_t workspace_bytes, void* stream) {
   if (int s = check_attn(cfg, B, H, T, D, dtype)) return s;
-  ALGX_REQUIRE(q && k && gain_q && gain_k && q_scaled && k_norm && v && guard && o && stat && dout && dq && dk && dv &&
-                   dgain_q && dgain_k,
+  ALGX_REQUIRE(q_src && k_src && gain_q && gain_k && q_scaled && k_norm && v && guard && o && stat && dout && dq_h &&
+                   dk_h && dv_h && dq_out && dk_out && dgain_q && dgain_k,
                "qknorm_attn_bwd: NULL pointer");
   ALGX_REQUIRE(!cfg->has_sink || (sink && dsink), "qknorm_attn_bwd: has_sink needs sink and dsink");
   ALGX_REQUIRE(eps > 0.f, "qknorm_attn_bwd: epsilon must be positive");
@@ -1062,8 +1155,8 @@ int algx_qknorm_attn_bwd(const algx_attn_config* cfg, const void* q, const void*
                "qknorm_attn_bwd: workspace too small (see algx_qknorm_attn_bwd_workspace_size)");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   bool fast = false;
-  if (int s = attn_bwd_core(cfg, q_scaled, k_norm, v, sink, guard, o, o_precise, stat, dout, dq, dk, dv, dsink, B, H,
-                            T, dtype, workspace, st, false, &fast))
+  if (int s = attn_bwd_core(cfg, q_scaled, k_norm, v, sink, guard, o, o_precise, stat, dout, dq_h, dk_h, dv_h, dsink,
+                            B, H, T, dtype, workspace, st, false, &fast))
     return s;
   char* ws = static_cast<char*>(workspace);
   const float* acc = reinterpret_cast<const float*>(ws + ws_off_tc(B, H, T));
@@ -1076,17 +1169,70 @@ int algx_qknorm_attn_bwd(const algx_attn_config* cfg, const void* q, const void*
     ALGX_CUDA(cudaMemsetAsync(counter, 0, sizeof(unsigned), st));
   }
   const int64_t rows = B * H * T;
+  auto launch = [&](auto tag) {
+    using TT = decltype(tag);
+    return launch_dependent(qknorm_attn_bwd_kernel<TT>, kEpiBlocks, kEpiThreads, 0, st, *cfg, guard,
+                            (dtype == ALGX_BF16 && fast) ? 1 : 0, acc, (const TT*)q_src, gain_q, (const TT*)k_src,
+                            gain_k, rope_cos, rope_sin, (int)T, (TT*)dq_out, (TT*)dk_out, partial, counter, dgain_q,
+                            dgain_k, rows, eps, (int)H, tok_stride, (const TT*)dq_h, (const TT*)dk_h,
+                            (const TT*)(dv_out ? dv_h : nullptr), (TT*)dv_out);
+  };
   if (dtype == ALGX_BF16)
-    ALGX_CUDA(launch_dependent(qknorm_attn_bwd_kernel<__nv_bfloat16>, kEpiBlocks, kEpiThreads, 0, st, *cfg, guard,
-                               fast ? 1 : 0, acc, (const __nv_bfloat16*)q, gain_q, (const __nv_bfloat16*)k, gain_k,
-                               rope_cos, rope_sin, (int)T, (__nv_bfloat16*)dq, (__nv_bfloat16*)dk, partial, counter,
-                               dgain_q, dgain_k, rows, eps));
+    ALGX_CUDA(launch(__nv_bfloat16{}));
   else
-    ALGX_CUDA(launch_dependent(qknorm_attn_bwd_kernel<float>, kEpiBlocks, kEpiThreads, 0, st, *cfg, guard, 0, acc,
-                               (const float*)q, gain_q, (const float*)k, gain_k, rope_cos, rope_sin, (int)T,
-                               (float*)dq, (float*)dk, partial, counter, dgain_q, dgain_k, rows, eps));
+    ALGX_CUDA(launch(float{}));
   ALGX_LAUNCHED("qknorm_attn_bwd launch");
   return ALGX_OK;
+}
+
+size_t packed_scratch_off(int64_t B, int64_t H, int64_t T, int64_t D) {
+  return align256(algx_qknorm_attn_bwd_workspace_size(B, H, T, D));
+}
+size_t packed_scratch_bytes(int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype) {
+  return align256((size_t)B * H * T * D * (dtype == ALGX_BF16 ? 2 : 4));
+}
+}  // namespace
+}  // namespace algx
+
+extern "C" {
+
+int algx_qknorm_attn_bwd(const algx_attn_config* cfg, const void* q, const void* k, const float* gain_q,
+                         const float* gain_k, const float* rope_cos, const float* rope_sin, int64_t rope_rows,
+                         const void* q_scaled, const void* k_norm, const void* v,
+                         const float* sink, const float* guard, const void* o, const float* o_precise,
+                         const float* stat, const void* dout, void* dq, void* dk, void* dv, float* dgain_q,
+                         float* dgain_k, float* dsink, int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype,
+                         float eps, void* workspace, size_t workspace_bytes, void* stream) {
+  return qknorm_attn_bwd_impl(cfg, q, k, gain_q, gain_k, rope_cos, rope_sin, rope_rows, q_scaled, k_norm, v, sink,
+                              guard, o, o_precise, stat, dout, dq, dk, dv, dq, dk, nullptr, 0, dgain_q, dgain_k, dsink,
+                              B, H, T, D, dtype, eps, workspace, workspace_bytes, stream);
+}
+
+size_t algx_qknorm_attn_bwd_packed_workspace_size(int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype) {
+  return packed_scratch_off(B, H, T, D) + 3 * packed_scratch_bytes(B, H, T, D, dtype);
+}
+
+int algx_qknorm_attn_bwd_packed(const algx_attn_config* cfg, const void* qkv, const float* gain_q,
+                                const float* gain_k, const float* rope_cos, const float* rope_sin, int64_t rope_rows,
+                                const void* q_scaled, const void* k_norm, const void* v_heads, const float* sink,
+                                const float* guard, const void* o, const float* o_precise, const float* stat,
+                                const void* dout, void* dqkv, float* dgain_q, float* dgain_k, float* dsink,
+                                int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype, float eps,
+                                void* workspace, size_t workspace_bytes, void* stream) {
+  ALGX_REQUIRE(qkv && dqkv, "qknorm_attn_bwd_packed: NULL pointer");
+  ALGX_REQUIRE(H > 0 && 3 * H <= INT32_MAX, "qknorm_attn_bwd_packed: bad head count");
+  ALGX_REQUIRE(workspace && workspace_bytes >= algx_qknorm_attn_bwd_packed_workspace_size(B, H, T, D, dtype),
+               "qknorm_attn_bwd_packed: workspace too small (see algx_qknorm_attn_bwd_packed_workspace_size)");
+  const size_t es = dtype == ALGX_BF16 ? 2 : 4;
+  const size_t blk = (size_t)H * (size_t)D * es;
+  const char* in = static_cast<const char*>(qkv);
+  char* out = static_cast<char*>(dqkv);
+  char* scratch = static_cast<char*>(workspace) + packed_scratch_off(B, H, T, D);
+  const size_t sb = packed_scratch_bytes(B, H, T, D, dtype);
+  return qknorm_attn_bwd_impl(cfg, in, in + blk, gain_q, gain_k, rope_cos, rope_sin, rope_rows, q_scaled, k_norm,
+                              v_heads, sink, guard, o, o_precise, stat, dout, scratch, scratch + sb, scratch + 2 * sb,
+                              out, out + blk, out + 2 * blk, (int)(3 * H), dgain_q, dgain_k, dsink, B, H, T, D, dtype,
+                              eps, workspace, workspace_bytes, stream);
 }
 
 }  // extern "C"

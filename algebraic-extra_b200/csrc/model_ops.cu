@@ -14,6 +14,8 @@
 // the backward reads the pair and dy and writes [dgate | dup]. Everything in
 // fp32 between one bf16 load and one bf16 store per output, which is how XLA
 // evaluates the fused bf16 chain (excess precision) in the reference.
+#include <algorithm>
+
 #include "algx_common.cuh"
 #include "vec_io.cuh"
 
@@ -22,113 +24,138 @@ namespace {
 
 constexpr int kNormThreads = 256;  // 8 warps: one row per warp per pass
 constexpr int kNormWarps = kNormThreads / 32;
-constexpr int kNormMaxBlocks = 148 * 4;
+constexpr int kNormMaxBlocks = 148 * 3;
 
+// Forward: two rows per warp in flight (both rows' loads issued before
+// either is used), the gain in shared memory.
 template <typename T, int C>
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_fwd_kernel(const T* __restrict__ x,
                                                                    const float* __restrict__ gain,
                                                                    T* __restrict__ y, int64_t rows, int dim,
                                                                    float eps) {
   using V = Vec<T>;
+  extern __shared__ float sg[];  // [dim] gain
   const int lane = threadIdx.x & 31;
   const int chunks = dim / V::N;
-  float g[C][V::N];
-#pragma unroll
-  for (int c = 0; c < C; ++c) {
-    const int idx = lane + 32 * c;
-#pragma unroll
-    for (int i = 0; i < V::N; ++i) g[c][i] = (gain && idx < chunks) ? gain[idx * V::N + i] : 1.f;
-  }
+  for (int i = threadIdx.x; i < dim; i += kNormThreads) sg[i] = gain ? gain[i] : 1.f;
+  __syncthreads();
   const int64_t warps = (int64_t)gridDim.x * kNormWarps;
-  for (int64_t row = (int64_t)blockIdx.x * kNormWarps + (threadIdx.x >> 5); row < rows; row += warps) {
-    const T* xr = x + row * dim;
-    uint4 raw[C];
+  for (int64_t r0 = (int64_t)blockIdx.x * kNormWarps + (threadIdx.x >> 5); r0 < rows; r0 += 2 * warps) {
+    uint4 raw[2][C];
 #pragma unroll
-    for (int c = 0; c < C; ++c) {
-      const int idx = lane + 32 * c;
-      raw[c] = idx < chunks ? ld_stream(xr + idx * V::N) : make_uint4(0, 0, 0, 0);
+    for (int k = 0; k < 2; ++k) {
+      const int64_t row = r0 + k * warps;
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        const int idx = lane + 32 * c;
+        raw[k][c] = (idx < chunks && row < rows) ? ld_stream(x + row * dim + idx * V::N) : make_uint4(0, 0, 0, 0);
+      }
     }
-    float v[C][V::N];
-    float ss = 0.f;
 #pragma unroll
-    for (int c = 0; c < C; ++c) {
-      unpack<T>(raw[c], v[c]);
+    for (int k = 0; k < 2; ++k) {
+      const int64_t row = r0 + k * warps;
+      float ss = 0.f;
 #pragma unroll
-      for (int i = 0; i < V::N; ++i) ss = fmaf(v[c][i], v[c][i], ss);
-    }
-    ss = row_sum<32>(ss);
-    // mean = sum / dim, as jnp.mean divides (algebraic.py:79)
-    const float tau = rsqrtf(ss / (float)dim + eps);
-    T* yr = y + row * dim;
+      for (int c = 0; c < C; ++c) {
+        float v[V::N];
+        unpack<T>(raw[k][c], v);
 #pragma unroll
-    for (int c = 0; c < C; ++c) {
-      const int idx = lane + 32 * c;
-      float o[V::N];
+        for (int i = 0; i < V::N; ++i) ss = fmaf(v[i], v[i], ss);
+      }
+      ss = row_sum<32>(ss);
+      // mean = sum / dim, as jnp.mean divides (algebraic.py:79)
+      const float tau = rsqrtf(ss / (float)dim + eps);
 #pragma unroll
-      for (int i = 0; i < V::N; ++i) o[i] = gain ? (v[c][i] * tau) * g[c][i] : v[c][i] * tau;
-      if (idx < chunks) *reinterpret_cast<uint4*>(yr + idx * V::N) = pack<T>(o);
+      for (int c = 0; c < C; ++c) {
+        const int idx = lane + 32 * c;
+        float v[V::N], o[V::N];
+        unpack<T>(raw[k][c], v);
+#pragma unroll
+        for (int i = 0; i < V::N; ++i) {
+          const float g = idx < chunks ? sg[idx * V::N + i] : 0.f;
+          o[i] = gain ? (v[i] * tau) * g : v[i] * tau;
+        }
+        if (idx < chunks && row < rows) *reinterpret_cast<uint4*>(y + row * dim + idx * V::N) = pack<T>(o);
+      }
     }
   }
 }
 
 // dx = tau (g dy) - x tau^3 mean(x g dy) (AD of the forward, the operation
 // order of kernels/qk_norm.py:39-40); dgain partials = sum_rows dy (x tau).
+// Two rows per warp are in flight (their loads issued before either is
+// used); rows stay packed in registers and the gain sits in shared memory, so
+// two CTAs fit on an SM.
+constexpr int kNormBwdRows = 2;
+constexpr int kNormBwdBlocks = 148 * 2;
+
 template <typename T, int C>
-__global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(const T* __restrict__ x,
-                                                                   const float* __restrict__ gain,
-                                                                   const T* __restrict__ dy, T* __restrict__ dx,
-                                                                   float* __restrict__ partial, int64_t rows,
-                                                                   int dim, float eps) {
+__global__ void __launch_bounds__(kNormThreads, 2) rmsnorm_bwd_kernel(const T* __restrict__ x,
+                                                                      const float* __restrict__ gain,
+                                                                      const T* __restrict__ dy, T* __restrict__ dx,
+                                                                      float* __restrict__ partial, int64_t rows,
+                                                                      int dim, float eps) {
   using V = Vec<T>;
-  extern __shared__ float red[];  // [kNormWarps][dim]
+  extern __shared__ float red[];  // [kNormWarps][dim] partial sums, then [dim] gain
+  float* sg = red + kNormWarps * dim;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int chunks = dim / V::N;
-  float g[C][V::N], acc[C][V::N];
+  for (int i = threadIdx.x; i < dim; i += kNormThreads) sg[i] = gain ? gain[i] : 1.f;
+  __syncthreads();
+  float acc[C][V::N];
 #pragma unroll
-  for (int c = 0; c < C; ++c) {
-    const int idx = lane + 32 * c;
+  for (int c = 0; c < C; ++c)
 #pragma unroll
-    for (int i = 0; i < V::N; ++i) {
-      g[c][i] = (gain && idx < chunks) ? gain[idx * V::N + i] : 1.f;
-      acc[c][i] = 0.f;
-    }
-  }
+    for (int i = 0; i < V::N; ++i) acc[c][i] = 0.f;
   const int64_t warps = (int64_t)gridDim.x * kNormWarps;
-  for (int64_t row = (int64_t)blockIdx.x * kNormWarps + warp; row < rows; row += warps) {
-    uint4 rx[C], rd[C];
+  for (int64_t r0 = (int64_t)blockIdx.x * kNormWarps + warp; r0 < rows; r0 += kNormBwdRows * warps) {
+    uint4 rx[kNormBwdRows][C], rd[kNormBwdRows][C];
 #pragma unroll
-    for (int c = 0; c < C; ++c) {
-      const int idx = lane + 32 * c;
-      const bool ok = idx < chunks;
-      rx[c] = ok ? ld_stream(x + row * dim + idx * V::N) : make_uint4(0, 0, 0, 0);
-      rd[c] = ok ? ld_stream(dy + row * dim + idx * V::N) : make_uint4(0, 0, 0, 0);
-    }
-    float xv[C][V::N], dv[C][V::N];
-    float ss = 0.f, sdg = 0.f;
+    for (int k = 0; k < kNormBwdRows; ++k) {
+      const int64_t row = r0 + k * warps;
 #pragma unroll
-    for (int c = 0; c < C; ++c) {
-      unpack<T>(rx[c], xv[c]);
-      unpack<T>(rd[c], dv[c]);
-#pragma unroll
-      for (int i = 0; i < V::N; ++i) {
-        ss = fmaf(xv[c][i], xv[c][i], ss);
-        sdg = fmaf(dv[c][i] * g[c][i], xv[c][i], sdg);
+      for (int c = 0; c < C; ++c) {
+        const int idx = lane + 32 * c;
+        const bool ok = idx < chunks && row < rows;
+        rx[k][c] = ok ? ld_stream(x + row * dim + idx * V::N) : make_uint4(0, 0, 0, 0);
+        rd[k][c] = ok ? ld_stream(dy + row * dim + idx * V::N) : make_uint4(0, 0, 0, 0);
       }
     }
-    ss = row_sum<32>(ss);
-    sdg = row_sum<32>(sdg);
-    const float tau = rsqrtf(ss / (float)dim + eps);
-    const float corr = tau * tau * tau * (sdg / (float)dim);
 #pragma unroll
-    for (int c = 0; c < C; ++c) {
-      const int idx = lane + 32 * c;
-      float o[V::N];
+    for (int k = 0; k < kNormBwdRows; ++k) {
+      const int64_t row = r0 + k * warps;
+      float ss = 0.f, sdg = 0.f;
 #pragma unroll
-      for (int i = 0; i < V::N; ++i) {
-        o[i] = (dv[c][i] * g[c][i]) * tau - xv[c][i] * corr;
-        acc[c][i] = fmaf(dv[c][i], xv[c][i] * tau, acc[c][i]);
+      for (int c = 0; c < C; ++c) {
+        const int idx = lane + 32 * c;
+        float xv[V::N], dv[V::N];
+        unpack<T>(rx[k][c], xv);
+        unpack<T>(rd[k][c], dv);
+#pragma unroll
+        for (int i = 0; i < V::N; ++i) {
+          const float g = idx < chunks ? sg[idx * V::N + i] : 0.f;
+          ss = fmaf(xv[i], xv[i], ss);
+          sdg = fmaf(dv[i] * g, xv[i], sdg);
+        }
       }
-      if (idx < chunks) *reinterpret_cast<uint4*>(dx + row * dim + idx * V::N) = pack<T>(o);
+      ss = row_sum<32>(ss);
+      sdg = row_sum<32>(sdg);
+      const float tau = rsqrtf(ss / (float)dim + eps);
+      const float corr = tau * tau * tau * (sdg / (float)dim);
+#pragma unroll
+      for (int c = 0; c < C; ++c) {
+        const int idx = lane + 32 * c;
+        float xv[V::N], dv[V::N], o[V::N];
+        unpack<T>(rx[k][c], xv);
+        unpack<T>(rd[k][c], dv);
+#pragma unroll
+        for (int i = 0; i < V::N; ++i) {
+          const float g = idx < chunks ? sg[idx * V::N + i] : 0.f;
+          o[i] = (dv[i] * g) * tau - xv[i] * corr;
+          acc[c][i] = fmaf(dv[i], xv[i] * tau, acc[c][i]);
+        }
+        if (idx < chunks && row < rows) *reinterpret_cast<uint4*>(dx + row * dim + idx * V::N) = pack<T>(o);
+      }
     }
   }
   if (!partial) return;  // no gain: no dgain
@@ -150,16 +177,23 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_bwd_kernel(const T* __re
 }
 
 // dgain[col] = sum over the nb partial rows, in a fixed order: warp w sums rows
-// w, w + 8, ... of 32 columns; the 8 warp sums are added in warp order.
+// w, w + 8, ... of 32 columns in four interleaved accumulators (so four loads
+// are in flight), added in a fixed order; the 8 warp sums in warp order.
 __global__ void __launch_bounds__(256) rmsnorm_dgain_reduce(const float* __restrict__ partial, int nb, int dim,
                                                            float* __restrict__ dgain) {
   __shared__ float red[8][32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int col = blockIdx.x * 32 + lane;
-  float s = 0.f;
-  if (col < dim)
-    for (int b = warp; b < nb; b += 8) s += partial[(int64_t)b * dim + col];
-  red[warp][lane] = s;
+  float s[4] = {0.f, 0.f, 0.f, 0.f};
+  if (col < dim) {
+    int b = warp;
+    for (; b + 24 < nb; b += 32) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) s[j] += partial[(int64_t)(b + 8 * j) * dim + col];
+    }
+    for (int j = 0; b < nb; b += 8, ++j) s[j & 3] += partial[(int64_t)b * dim + col];
+  }
+  red[warp][lane] = (s[0] + s[1]) + (s[2] + s[3]);
   __syncthreads();
   if (warp == 0 && col < dim) {
     float t = 0.f;
@@ -179,9 +213,18 @@ int norm_chunks(int64_t dim, int32_t dtype) {
   return -1;
 }
 
+// Forward: one wave at three CTAs per SM (80 registers a thread at d = 768),
+// two rows per warp per pass.
 int norm_grid(int64_t rows) {
-  int64_t g = (rows + kNormWarps - 1) / kNormWarps;
+  int64_t g = (rows + 2 * kNormWarps - 1) / (2 * kNormWarps);
   if (g > kNormMaxBlocks) g = kNormMaxBlocks;
+  return (int)(g < 1 ? 1 : g);
+}
+
+// One wave at two CTAs per SM; every warp keeps two rows in flight.
+int norm_bwd_grid(int64_t rows) {
+  int64_t g = (rows + kNormWarps * kNormBwdRows - 1) / (kNormWarps * kNormBwdRows);
+  if (g > kNormBwdBlocks) g = kNormBwdBlocks;
   return (int)(g < 1 ? 1 : g);
 }
 
@@ -202,21 +245,22 @@ int check_norm(const void* x, const void* y, int64_t rows, int64_t dim, int32_t 
 
 template <typename T, int C>
 void launch_norm_fwd(const void* x, const float* gain, void* y, int64_t rows, int dim, float eps, cudaStream_t st) {
-  rmsnorm_fwd_kernel<T, C><<<norm_grid(rows), kNormThreads, 0, st>>>(static_cast<const T*>(x), gain,
-                                                                      static_cast<T*>(y), rows, dim, eps);
+  // dim <= 4096 floats of gain: at most 16 KB of shared memory
+  rmsnorm_fwd_kernel<T, C><<<norm_grid(rows), kNormThreads, (size_t)dim * sizeof(float), st>>>(
+      static_cast<const T*>(x), gain, static_cast<T*>(y), rows, dim, eps);
 }
 
 template <typename T, int C>
 cudaError_t launch_norm_bwd(const void* x, const float* gain, const void* dy, void* dx, float* partial,
                             int64_t rows, int dim, float eps, cudaStream_t st) {
-  const size_t smem = (size_t)kNormWarps * dim * sizeof(float);
+  const size_t smem = (size_t)(kNormWarps + 1) * dim * sizeof(float);
   auto kern = rmsnorm_bwd_kernel<T, C>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
-  kern<<<norm_grid(rows), kNormThreads, smem, st>>>(static_cast<const T*>(x), gain, static_cast<const T*>(dy),
-                                                    static_cast<T*>(dx), partial, rows, dim, eps);
+  kern<<<norm_bwd_grid(rows), kNormThreads, smem, st>>>(static_cast<const T*>(x), gain, static_cast<const T*>(dy),
+                                                        static_cast<T*>(dx), partial, rows, dim, eps);
   return cudaSuccess;
 }
 
@@ -304,6 +348,73 @@ __global__ void __launch_bounds__(kGluThreads) swiglu_bwd_kernel(const __nv_bflo
   }
 }
 
+// ALU-GLU (algebraic.py:86-117, model.py:196-197): act = alu(up, beta)
+// rounded to bf16 (_alu_parts' astype), y = bf16(gate * act). alu(z) =
+// z/2 (1 + u), u = bz / sqrt(1 + b^2 z^2); for bz < 0 the factor 1 + u is
+// formed as r^2 / (1 - u) so the negative tail keeps its precision.
+__device__ __forceinline__ void alu_parts(float z, float beta, float& act, float& u, float& r) {
+  const float bz = beta * z;
+  r = rsqrtf(1.f + bz * bz);
+  u = bz * r;
+  const float opu = bz < 0.f ? (r * r) / (1.f - u) : 1.f + u;
+  act = round_io<__nv_bfloat16>(0.5f * z * opu);
+}
+
+__global__ void __launch_bounds__(kGluThreads) aluglu_fwd_kernel(const __nv_bfloat16* __restrict__ gu,
+                                                                 __nv_bfloat16* __restrict__ y, int64_t rows, int ff,
+                                                                 float beta) {
+  const int cpr = ff / 8;
+  const int64_t total = rows * cpr;
+  for (int64_t i = (int64_t)blockIdx.x * kGluThreads + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * kGluThreads) {
+    const int64_t r = i / cpr;
+    const int c = (int)(i - r * cpr);
+    const __nv_bfloat16* src = gu + r * 2 * ff + c * 8;
+    float g[8], z[8], o[8];
+    unpack<__nv_bfloat16>(ld_stream(src), g);
+    unpack<__nv_bfloat16>(ld_stream(src + ff), z);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float act, u, rr;
+      alu_parts(z[k], beta, act, u, rr);
+      o[k] = g[k] * act;
+    }
+    *reinterpret_cast<uint4*>(y + r * ff + c * 8) = pack<__nv_bfloat16>(o);
+  }
+}
+
+// The reference's custom VJP (algebraic.py:109-113): the cotangent of act is
+// bf16(dy * gate); dup = bf16(g * (0.5 (1 + u) + 0.5 u r^2)); dgate = bf16(dy * act).
+__global__ void __launch_bounds__(kGluThreads) aluglu_bwd_kernel(const __nv_bfloat16* __restrict__ gu,
+                                                                 const __nv_bfloat16* __restrict__ dy,
+                                                                 __nv_bfloat16* __restrict__ dgu, int64_t rows,
+                                                                 int ff, float beta) {
+  const int cpr = ff / 8;
+  const int64_t total = rows * cpr;
+  for (int64_t i = (int64_t)blockIdx.x * kGluThreads + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * kGluThreads) {
+    const int64_t r = i / cpr;
+    const int c = (int)(i - r * cpr);
+    const __nv_bfloat16* src = gu + r * 2 * ff + c * 8;
+    float g[8], z[8], d[8], dg[8], dz[8];
+    unpack<__nv_bfloat16>(ld_stream(src), g);
+    unpack<__nv_bfloat16>(ld_stream(src + ff), z);
+    unpack<__nv_bfloat16>(ld_stream(dy + r * ff + c * 8), d);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float act, u, rr;
+      alu_parts(z[k], beta, act, u, rr);
+      const float gact = round_io<__nv_bfloat16>(d[k] * g[k]);
+      const float deriv = 0.5f * (1.f + u) + 0.5f * u * (rr * rr);
+      dg[k] = d[k] * act;
+      dz[k] = gact * deriv;
+    }
+    __nv_bfloat16* dst = dgu + r * 2 * ff + c * 8;
+    *reinterpret_cast<uint4*>(dst) = pack<__nv_bfloat16>(dg);
+    *reinterpret_cast<uint4*>(dst + ff) = pack<__nv_bfloat16>(dz);
+  }
+}
+
 int glu_grid(int64_t rows, int64_t ff) {
   const int64_t total = rows * (ff / 8);
   int64_t g = (total + kGluThreads - 1) / kGluThreads;
@@ -317,6 +428,65 @@ int check_glu(const void* a, const void* b, int64_t rows, int64_t ff, const char
   ALGX_REQUIRE(ff > 0 && ff % 8 == 0, std::string(who) + ": hidden width must be a positive multiple of 8");
   ALGX_REQUIRE((reinterpret_cast<uintptr_t>(a) & 15) == 0 && (reinterpret_cast<uintptr_t>(b) & 15) == 0,
                std::string(who) + ": tensors must be 16-byte aligned");
+  return ALGX_OK;
+}
+
+// ------------------------------------------------------- head/token order
+// Attention tensors are head-major (B, H, T, 64) for the TMA-fed kernels;
+// the model's projections produce and consume token-major (B, T, H, 64).
+// One 64-element row moves per TPR threads with 16-byte accesses; the rows
+// are read in one order and written in the other.
+constexpr int kPermThreads = 256;
+constexpr int kPermUnroll = 4;
+
+template <typename T>
+__global__ void __launch_bounds__(kPermThreads) permute_rows_kernel(const T* __restrict__ src, T* __restrict__ dst,
+                                                                   int64_t rows, int T_, int H, int to_tokens) {
+  using V = Vec<T>;
+  const int lane = threadIdx.x & 31, sub = lane % V::TPR, rl = lane / V::TPR;
+  const int64_t warps = (int64_t)gridDim.x * (kPermThreads / 32);
+  const int64_t w = (int64_t)blockIdx.x * (kPermThreads / 32) + (threadIdx.x >> 5);
+  for (int64_t r0 = w * V::RPW * kPermUnroll; r0 < rows; r0 += warps * V::RPW * kPermUnroll) {
+    uint4 raw[kPermUnroll];
+    int64_t other[kPermUnroll];
+#pragma unroll
+    for (int u = 0; u < kPermUnroll; ++u) {
+      const int64_t row = r0 + u * V::RPW + rl;  // head-major index (b*H + h)*T + t
+      const int64_t bh = row / T_, t = row - bh * T_, b = bh / H, h = bh - b * H;
+      other[u] = (b * T_ + t) * H + h;          // token-major index
+      const int64_t from = to_tokens ? row : other[u];
+      raw[u] = row < rows ? ld_stream(src + from * kRowDim + sub * V::N) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < kPermUnroll; ++u) {
+      const int64_t row = r0 + u * V::RPW + rl;
+      const int64_t to = to_tokens ? other[u] : row;
+      if (row < rows) *reinterpret_cast<uint4*>(dst + to * kRowDim + sub * V::N) = raw[u];
+    }
+  }
+}
+
+int permute_rows(const void* src, void* dst, int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype,
+                 int to_tokens, void* stream, const char* who) {
+  ALGX_REQUIRE(B >= 0 && H > 0 && T > 0 && D == kRowDim, std::string(who) + ": needs D = 64 and positive H, T");
+  ALGX_REQUIRE(dtype == ALGX_F32 || dtype == ALGX_BF16, std::string(who) + ": dtype must be float32 or bfloat16");
+  const int64_t rows = B * H * T;
+  if (rows == 0) return ALGX_OK;
+  ALGX_REQUIRE(src && dst && src != dst, std::string(who) + ": NULL or aliased pointers");
+  ALGX_REQUIRE((reinterpret_cast<uintptr_t>(src) & 15) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0,
+               std::string(who) + ": tensors must be 16-byte aligned");
+  ALGX_REQUIRE(T <= INT32_MAX && H <= INT32_MAX, std::string(who) + ": T or H out of range");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int rpw = dtype == ALGX_BF16 ? Vec<__nv_bfloat16>::RPW : Vec<float>::RPW;
+  const int64_t per_block = (int64_t)(kPermThreads / 32) * rpw * kPermUnroll;
+  const int grid = (int)std::min<int64_t>((rows + per_block - 1) / per_block, 148 * 8);
+  if (dtype == ALGX_BF16)
+    permute_rows_kernel<__nv_bfloat16><<<grid, kPermThreads, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(src), static_cast<__nv_bfloat16*>(dst), rows, (int)T, (int)H, to_tokens);
+  else
+    permute_rows_kernel<float><<<grid, kPermThreads, 0, st>>>(static_cast<const float*>(src), static_cast<float*>(dst),
+                                                              rows, (int)T, (int)H, to_tokens);
+  ALGX_LAUNCHED("permute_rows launch");
   return ALGX_OK;
 }
 
@@ -343,7 +513,7 @@ int algx_rmsnorm_fwd(const void* x, const float* gain, void* y, int64_t rows, in
 
 size_t algx_rmsnorm_bwd_workspace_size(int64_t rows, int64_t dim) {
   if (rows <= 0 || dim <= 0) return 0;
-  return (size_t)norm_grid(rows) * (size_t)dim * sizeof(float);
+  return (size_t)norm_bwd_grid(rows) * (size_t)dim * sizeof(float);
 }
 
 int algx_rmsnorm_bwd(const void* x, const float* gain, const void* dy, void* dx, float* dgain, int64_t rows,
@@ -357,7 +527,7 @@ int algx_rmsnorm_bwd(const void* x, const float* gain, const void* dy, void* dx,
     if (gain) ALGX_CUDA(cudaMemsetAsync(dgain, 0, (size_t)dim * sizeof(float), st));
     return ALGX_OK;
   }
-  const int grid = norm_grid(rows);
+  const int grid = norm_bwd_grid(rows);
   float* partial = nullptr;
   if (gain) {
     ALGX_REQUIRE(workspace && workspace_bytes >= (size_t)grid * (size_t)dim * sizeof(float),
@@ -398,6 +568,39 @@ int algx_swiglu_bwd(const void* gu, const void* dy, void* dgu, int64_t rows, int
                                                                 static_cast<__nv_bfloat16*>(dgu), rows, (int)ff);
   ALGX_LAUNCHED("swiglu_bwd launch");
   return ALGX_OK;
+}
+
+int algx_aluglu_fwd(const void* gu, void* y, int64_t rows, int64_t ff, float beta, void* stream) {
+  if (int s = check_glu(gu, y, rows, ff, "aluglu_fwd")) return s;
+  if (rows == 0) return ALGX_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  aluglu_fwd_kernel<<<glu_grid(rows, ff), kGluThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(gu),
+                                                                static_cast<__nv_bfloat16*>(y), rows, (int)ff, beta);
+  ALGX_LAUNCHED("aluglu_fwd launch");
+  return ALGX_OK;
+}
+
+int algx_aluglu_bwd(const void* gu, const void* dy, void* dgu, int64_t rows, int64_t ff, float beta, void* stream) {
+  if (int s = check_glu(gu, dgu, rows, ff, "aluglu_bwd")) return s;
+  ALGX_REQUIRE((rows == 0 || dy) && (reinterpret_cast<uintptr_t>(dy) & 15) == 0,
+               "aluglu_bwd: dy NULL or not 16-byte aligned");
+  if (rows == 0) return ALGX_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  aluglu_bwd_kernel<<<glu_grid(rows, ff), kGluThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(gu),
+                                                                static_cast<const __nv_bfloat16*>(dy),
+                                                                static_cast<__nv_bfloat16*>(dgu), rows, (int)ff, beta);
+  ALGX_LAUNCHED("aluglu_bwd launch");
+  return ALGX_OK;
+}
+
+int algx_heads_to_tokens(const void* src, void* dst, int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype,
+                         void* stream) {
+  return permute_rows(src, dst, B, H, T, D, dtype, 1, stream, "heads_to_tokens");
+}
+
+int algx_tokens_to_heads(const void* src, void* dst, int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype,
+                         void* stream) {
+  return permute_rows(src, dst, B, H, T, D, dtype, 0, stream, "tokens_to_heads");
 }
 
 }  // extern "C"

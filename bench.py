@@ -283,20 +283,25 @@ def secondary(dev, rank, world, stream, sync_all, max_over_ranks, steps=5, warmu
     del q, k, v, do, gq, gk, leaves
     trace("secondary: train cfg5")
     out["train_cfg5"] = train_line(dev, rank, world, stream, sync_all, max_over_ranks)
+    trace("secondary: train cfg5, algebraic preset")
+    out["train_cfg5_algebraic"] = train_line(dev, rank, world, stream, sync_all, max_over_ranks, preset="algebraic")
     return out
 
 
 TRAIN_GLOBAL_BATCH = 64  # sequences per optimizer step, split over the ranks (config 5)
 
 
-def train_line(dev, rank, world, stream, sync_all, max_over_ranks, steps=3, warmup=3):
+def train_line(dev, rank, world, stream, sync_all, max_over_ranks, steps=3, warmup=3, preset="standard"):
     """Config 5: the 125M training step (fwd + bwd + clip + AdamW) on synthetic
     uniform token ids, global batch 64 x 2048 split over the ranks, micro-batches
-    of 8 sequences, gradient all-reduce overlapped with the last backward."""
-    from algx.model import AlgebraicLM, config_125m, count_params, train_flops_per_token
+    of 8 sequences, gradient all-reduce overlapped with the last backward.
+    preset "standard": SwiGLU, RoPE, ce head; "algebraic":
+    the reference's algebraic preset at the same size (ALU-GLU, Cayley
+    rotations, learned sink, alg_ce head n=8 c=2)."""
+    from algx.model import AlgebraicLM, config_125m, config_algebraic_125m, count_params, train_flops_per_token
     from algx.train import DataParallelTrainer
 
-    cfg = config_125m()
+    cfg = config_125m() if preset == "standard" else config_algebraic_125m()
     per = TRAIN_GLOBAL_BATCH // world
     micro = min(8, per)
     model = AlgebraicLM(cfg, device=dev, seed=0)  # same initial replica on every rank
@@ -319,8 +324,9 @@ def train_line(dev, rank, world, stream, sync_all, max_over_ranks, steps=3, warm
             "loss_first": float(losses[0]), "loss_last": float(losses[-1]),
             "params": count_params(cfg), "flop_per_token": train_flops_per_token(cfg),
             "config": f"L={cfg.n_layers} d={cfg.d_model} H={cfg.n_heads} ff={cfg.d_ff} V={cfg.vocab_size} "
-                      f"S={cfg.seq_len}; QK-norm + RoPE + asinh n={cfg.attn_n} c={cfg.attn_c}, SwiGLU, "
-                      f"ce head; fp32 masters, bf16 compute; global batch {TRAIN_GLOBAL_BATCH} sequences, "
+                      f"S={cfg.seq_len}; QK-norm + {cfg.pos} + asinh n={cfg.attn_n} c={cfg.attn_c}, sink "
+                      f"{cfg.sink}, {cfg.ffn}, {cfg.head} head; fp32 masters, bf16 compute; "
+                      f"global batch {TRAIN_GLOBAL_BATCH} sequences, "
                       f"{per} per rank in micro-batches of {micro}; clip 1.0; fused AdamW",
             "data": "synthetic uniform token ids, seeded per rank",
             "scaling": "strong (global batch fixed, split over the ranks)" if world > 1 else "single GPU"}

@@ -237,6 +237,47 @@ ALGX_API int algx_head_bwd(const algx_head_config* cfg, const void* h, const voi
  * out: fp32 128 x nout. No counterpart in the reference (hardware check). */
 ALGX_API int algx_selftest_tcgen05(int32_t mode, const void* a, const void* b, float* out, void* stream);
 
+/* --------------------------------------------- packed (token-major) attention */
+/* The model's QKV projection writes one token-major tensor qkv (B, T, 3, H, D)
+ * ([q | k | v] per token, each H x D); its output projection reads the
+ * attention output token-major (B, T, H, D). These entries read and write
+ * those layouts directly, so no head-major copy of q, k, v or of their
+ * gradients is made outside the kernels. No counterpart in the reference:
+ * XLA fuses its transposes (model.py:166-169, 180) into neighbouring ops. */
+
+/* algx_qknorm_attn_prepare on the packed qkv: q_scaled and k_norm as there,
+ * v_heads = v in head-major order (B, H, T, D) for algx_attn_fwd. */
+ALGX_API int algx_qknorm_attn_prepare_packed(const algx_attn_config* cfg, const void* qkv, const float* gain_q,
+                                             const float* gain_k, const float* rope_cos, const float* rope_sin,
+                                             int64_t rope_rows, const float* sink, void* q_scaled, void* k_norm,
+                                             void* v_heads, float* guard, int64_t B, int64_t H, int64_t T, int64_t D,
+                                             int32_t dtype, float eps, void* stream);
+
+/* Workspace bytes of algx_qknorm_attn_bwd_packed: that of
+ * algx_qknorm_attn_bwd plus head-major dq, dk, dv scratch. */
+ALGX_API size_t algx_qknorm_attn_bwd_packed_workspace_size(int64_t B, int64_t H, int64_t T, int64_t D,
+                                                           int32_t dtype);
+
+/* algx_qknorm_attn_bwd for a forward run by algx_qknorm_attn_prepare_packed:
+ * dout head-major (B, H, T, D); dqkv (B, T, 3, H, D) receives the gradients of
+ * the raw q and k and of v in the packed layout. */
+ALGX_API int algx_qknorm_attn_bwd_packed(const algx_attn_config* cfg, const void* qkv, const float* gain_q,
+                                         const float* gain_k, const float* rope_cos, const float* rope_sin,
+                                         int64_t rope_rows, const void* q_scaled, const void* k_norm,
+                                         const void* v_heads, const float* sink, const float* guard, const void* o,
+                                         const float* o_precise, const float* stat, const void* dout, void* dqkv,
+                                         float* dgain_q, float* dgain_k, float* dsink, int64_t B, int64_t H,
+                                         int64_t T, int64_t D, int32_t dtype, float eps, void* workspace,
+                                         size_t workspace_bytes, void* stream);
+
+/* dst (B, T, H, D) = src (B, H, T, D) and back, D = 64, src != dst: the
+ * attention output into the output projection and its gradient out of it
+ * (model.py:180). No counterpart in the reference (an XLA transpose). */
+ALGX_API int algx_heads_to_tokens(const void* src, void* dst, int64_t B, int64_t H, int64_t T, int64_t D,
+                                  int32_t dtype, void* stream);
+ALGX_API int algx_tokens_to_heads(const void* src, void* dst, int64_t B, int64_t H, int64_t T, int64_t D,
+                                  int32_t dtype, void* stream);
+
 /* ------------------------------------------------ training-step elementwise */
 /* The model's own row norms and gate around the hot kernels, used by the
  * config-5 training step (algx.model). bf16 or fp32 rows, fp32 maths. */
@@ -267,6 +308,17 @@ ALGX_API int algx_swiglu_fwd(const void* gu, void* y, int64_t rows, int64_t ff, 
 /* dgu = [dgate | dup] of algx_swiglu_fwd for the upstream gradient dy
  * (rows, ff); JAX AD of model.py:193-198. */
 ALGX_API int algx_swiglu_bwd(const void* gu, const void* dy, void* dgu, int64_t rows, int64_t ff, void* stream);
+
+/* y = gate * alu(up, beta), bf16, for rows of gu = [gate (ff) | up (ff)]:
+ * the algebraic preset's feed-forward gate (model.py:196-197). alu is
+ * algebraic.py:86-101 (rounded to bf16 as `_alu_parts` does), the product
+ * is rounded once more. */
+ALGX_API int algx_aluglu_fwd(const void* gu, void* y, int64_t rows, int64_t ff, float beta, void* stream);
+
+/* dgu = [dgate | dup] of algx_aluglu_fwd with the reference's custom VJP of
+ * alu (algebraic.py:104-113). */
+ALGX_API int algx_aluglu_bwd(const void* gu, const void* dy, void* dgu, int64_t rows, int64_t ff, float beta,
+                             void* stream);
 
 #ifdef __cplusplus
 }

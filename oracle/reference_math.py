@@ -151,6 +151,33 @@ def rms_norm(x: torch.Tensor, gain: Optional[torch.Tensor], eps: float = 1e-5,
     return _round(y, io_dtype)
 
 
+class _Alu(torch.autograd.Function):
+    """alu with the reference's own VJP rule (algebraic.py:104-113)."""
+
+    @staticmethod
+    def forward(ctx, x, beta, io_dtype):
+        bz = beta * x
+        r = torch.rsqrt(1.0 + bz * bz)
+        u = bz * r
+        one_plus_u = torch.where(bz < 0, (r * r) / (1.0 - u), 1.0 + u)
+        ctx.save_for_backward(u, r)
+        ctx.io = io_dtype
+        return _round(0.5 * x * one_plus_u, io_dtype)
+
+    @staticmethod
+    def backward(ctx, g):
+        u, r = ctx.saved_tensors
+        derivative = 0.5 * (1.0 + u) + 0.5 * u * (r * r)
+        return _round(g * derivative, ctx.io), None, None
+
+
+def alu(x: torch.Tensor, beta: float = 1.0, io_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """Algebraic linear unit x/2 (1 + bx / sqrt(1 + b^2 x^2)) (algebraic.py:86-101):
+    for bx < 0 the factor 1 + u is r^2 / (1 - u); the result is rounded to
+    ``io_dtype`` (``.astype(x.dtype)``), and so is the gradient."""
+    return _Alu.apply(x, float(beta), io_dtype)
+
+
 def qk_norm_backward(x: torch.Tensor, gain: torch.Tensor, dy: torch.Tensor, eps: float):
     """(dx, dgain) of ``rms_norm`` by autograd (kernels/qk_norm.py:41-55)."""
     xx = x.detach().clone().requires_grad_(True)

@@ -14,7 +14,8 @@ Two precisions per case:
     reference's rounding points (``p.astype(v.dtype)``, ``out.astype(q.dtype)``).
 
 Usage: python tests/golden/make_golden.py --reference <path-to-reference-checkout>
-Outputs: tests/golden/*.npz (small; inputs are regenerated from seeds).
+Outputs: tests/golden/reference_dense.npz and reference_alu.npz (small; inputs
+are regenerated from seeds; ``--which`` writes one of them).
 """
 
 import argparse
@@ -135,9 +136,30 @@ def head_goldens(RA, RS, out):
                                       float(np.sum(e, dtype=np.float64)) + float(t.sum()))
 
 
+def alu_goldens(RA, out):
+    """alu(x, beta) (algebraic.py:86-101) and its custom VJP (algebraic.py:104-113)
+    through the reference's own code, float64 and bf16 I/O, both signs and the
+    far negative tail that the r^2 / (1 - u) branch protects."""
+    x = cases.normal(41, (6, 256), 4.0)
+    x[0, :8] = np.array([0.0, -1e-3, 1e-3, -30.0, 30.0, -300.0, 300.0, -3000.0], dtype=np.float32)
+    g = cases.normal(42, (6, 256))
+    for beta in (0.5, 1.0):
+        for prec in ("f64", "bf16"):
+            io = torch.bfloat16 if prec == "bf16" else torch.float64
+            xt = torch.from_numpy(x).to(io).requires_grad_(True)
+            y = RA.alu(xt, beta)
+            y.backward(torch.from_numpy(g).to(io))
+            key = f"alu_b{beta:g}_{prec}"
+            out[key + "_y"] = _np(y)
+            out[key + "_dx"] = _np(xt.grad)
+    out["alu_checksum"] = np.float64(float(np.sum(x, dtype=np.float64)) + float(np.sum(g, dtype=np.float64)))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="root of the reference checkout")
+    ap.add_argument("--which", choices=("all", "dense", "alu"), default="all",
+                    help="dense: reference_dense.npz; alu: reference_alu.npz")
     args = ap.parse_args()
     src = os.path.join(args.reference, "src")
     sys.path.insert(0, src)
@@ -147,14 +169,21 @@ def main():
     prov = {name: _sha(os.path.join(src, "algebraic", name))
             for name in ("algebraic.py", "standard.py", "evaluation.py")}
     torch.set_num_threads(8)
-    out = {"provenance": np.array(repr(prov))}
-    attention_goldens(RA, out)
-    norm_goldens(RA, out)
-    likelihood_goldens(RA, RS, RE, out)
-    head_goldens(RA, RS, out)
-    path = os.path.join(HERE, "reference_dense.npz")
-    np.savez_compressed(path, **out)
-    print(f"wrote {path}: {len(out)} arrays, {os.path.getsize(path) / 1e6:.2f} MB; {prov}")
+    if args.which in ("all", "dense"):
+        out = {"provenance": np.array(repr(prov))}
+        attention_goldens(RA, out)
+        norm_goldens(RA, out)
+        likelihood_goldens(RA, RS, RE, out)
+        head_goldens(RA, RS, out)
+        path = os.path.join(HERE, "reference_dense.npz")
+        np.savez_compressed(path, **out)
+        print(f"wrote {path}: {len(out)} arrays, {os.path.getsize(path) / 1e6:.2f} MB; {prov}")
+    if args.which in ("all", "alu"):
+        out = {"provenance": np.array(repr(prov))}
+        alu_goldens(RA, out)
+        path = os.path.join(HERE, "reference_alu.npz")
+        np.savez_compressed(path, **out)
+        print(f"wrote {path}: {len(out)} arrays, {os.path.getsize(path) / 1e6:.2f} MB; {prov}")
 
 
 if __name__ == "__main__":

@@ -141,3 +141,30 @@ def test_fused_head_oracle_matches_reference(kind, n, c, prec):
         assert rel_l2(tel, GOLD[key + "_tel"]) < 2e-2
         assert rel_l2(dh, GOLD[key + "_dh"]) < 1e-2
         assert rel_l2(de, GOLD[key + "_de"]) < 1e-2
+
+
+ALU = np.load(__import__("os").path.join(__import__("os").path.dirname(__file__), "golden", "reference_alu.npz"))
+
+
+def _alu_inputs():
+    x = cases.normal(41, (6, 256), 4.0)
+    x[0, :8] = np.array([0.0, -1e-3, 1e-3, -30.0, 30.0, -300.0, 300.0, -3000.0], dtype=np.float32)
+    return x, cases.normal(42, (6, 256))
+
+
+@pytest.mark.parametrize("beta", [0.5, 1.0])
+@pytest.mark.parametrize("prec", ["f64", "bf16"])
+def test_alu_oracle_matches_reference(beta, prec):
+    """ALU-GLU's activation and its custom VJP (algebraic.py:86-113) against the reference's own code."""
+    x, g = _alu_inputs()
+    assert float(np.sum(x, dtype=np.float64)) + float(np.sum(g, dtype=np.float64)) == float(ALU["alu_checksum"])
+    io = torch.bfloat16 if prec == "bf16" else None
+    xt = cases.to_io(x, io if io else torch.float64).requires_grad_(True)
+    y = R.alu(xt, beta, io_dtype=io)
+    y.backward(cases.to_io(g, io if io else torch.float64))
+    key = f"alu_b{beta:g}_{prec}"
+    tol = 1e-6 if prec == "f64" else 1e-2
+    assert rel_l2(y.detach().numpy(), ALU[key + "_y"]) < tol
+    assert rel_l2(xt.grad.numpy(), ALU[key + "_dx"]) < tol
+    # the far negative tail keeps its precision (r^2 / (1 - u) branch)
+    assert np.all(np.isfinite(ALU[key + "_y"]))
