@@ -117,13 +117,17 @@ __device__ __forceinline__ void rotate_half(float (&x)[Vec<T>::N], const float* 
 // rows (b, t) hold `stride` rows of 64 elements, head h at offset h (the
 // caller offsets the base pointer to the q, k or v block). stride 0: the
 // tensor is head-major itself.
+// The packed entry points require B*H*T < 2^31, so the index splits use
+// 32-bit division (a 64-bit division costs several times as many instructions,
+// once per row and thread).
 __device__ __forceinline__ int64_t tok_row(int64_t row, int T_, int H, int stride) {
   if (stride == 0) return row;
-  const int64_t bh = row / T_;
-  const int64_t t = row - bh * T_;
-  const int64_t b = bh / H;
-  const int64_t h = bh - b * H;
-  return (b * T_ + t) * stride + h;
+  const unsigned r = (unsigned)row;
+  const unsigned bh = r / (unsigned)T_;
+  const unsigned t = r - bh * (unsigned)T_;
+  const unsigned b = bh / (unsigned)H;
+  const unsigned h = bh - b * (unsigned)H;
+  return ((int64_t)b * T_ + t) * stride + h;
 }
 
 // in_stride > 0: q, k, v are the blocks of one token-major (B, T, 3, H, D)
@@ -971,6 +975,7 @@ int algx_qknorm_attn_prepare_packed(const algx_attn_config* cfg, const void* qkv
                                     float eps, void* stream) {
   ALGX_REQUIRE(qkv && v_heads, "qknorm_attn_prepare_packed: NULL pointer");
   ALGX_REQUIRE(H > 0 && 3 * H <= INT32_MAX, "qknorm_attn_prepare_packed: bad head count");
+  ALGX_REQUIRE(B >= 0 && T > 0 && B * H * T <= INT32_MAX, "qknorm_attn_prepare_packed: B*H*T must be below 2^31");
   const size_t es = dtype == ALGX_BF16 ? 2 : 4;
   const char* base = static_cast<const char*>(qkv);
   const size_t blk = (size_t)H * (size_t)D * es;  // bytes between the q, k and v blocks of a token row
@@ -1221,6 +1226,7 @@ int algx_qknorm_attn_bwd_packed(const algx_attn_config* cfg, const void* qkv, co
                                 void* workspace, size_t workspace_bytes, void* stream) {
   ALGX_REQUIRE(qkv && dqkv, "qknorm_attn_bwd_packed: NULL pointer");
   ALGX_REQUIRE(H > 0 && 3 * H <= INT32_MAX, "qknorm_attn_bwd_packed: bad head count");
+  ALGX_REQUIRE(B >= 0 && T > 0 && B * H * T <= INT32_MAX, "qknorm_attn_bwd_packed: B*H*T must be below 2^31");
   ALGX_REQUIRE(workspace && workspace_bytes >= algx_qknorm_attn_bwd_packed_workspace_size(B, H, T, D, dtype),
                "qknorm_attn_bwd_packed: workspace too small (see algx_qknorm_attn_bwd_packed_workspace_size)");
   const size_t es = dtype == ALGX_BF16 ? 2 : 4;

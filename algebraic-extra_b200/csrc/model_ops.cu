@@ -34,10 +34,16 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_fwd_kernel(const T* __re
                                                                    T* __restrict__ y, int64_t rows, int dim,
                                                                    float eps) {
   using V = Vec<T>;
-  extern __shared__ float sg[];  // [dim] gain
+  // gain, transposed to [element i of a chunk][chunk]: the lanes of a warp read
+  // consecutive words (no bank conflicts)
+  extern __shared__ float sg[];
+  constexpr int CP = 32 * C;
   const int lane = threadIdx.x & 31;
   const int chunks = dim / V::N;
-  for (int i = threadIdx.x; i < dim; i += kNormThreads) sg[i] = gain ? gain[i] : 1.f;
+  for (int j = threadIdx.x; j < V::N * CP; j += kNormThreads) {
+    const int i = j / CP, idx = j - i * CP;
+    sg[j] = idx < chunks ? (gain ? gain[idx * V::N + i] : 1.f) : 0.f;
+  }
   __syncthreads();
   const int64_t warps = (int64_t)gridDim.x * kNormWarps;
   for (int64_t r0 = (int64_t)blockIdx.x * kNormWarps + (threadIdx.x >> 5); r0 < rows; r0 += 2 * warps) {
@@ -71,10 +77,7 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_fwd_kernel(const T* __re
         float v[V::N], o[V::N];
         unpack<T>(raw[k][c], v);
 #pragma unroll
-        for (int i = 0; i < V::N; ++i) {
-          const float g = idx < chunks ? sg[idx * V::N + i] : 0.f;
-          o[i] = gain ? (v[i] * tau) * g : v[i] * tau;
-        }
+        for (int i = 0; i < V::N; ++i) o[i] = gain ? (v[i] * tau) * sg[i * CP + idx] : v[i] * tau;
         if (idx < chunks && row < rows) *reinterpret_cast<uint4*>(y + row * dim + idx * V::N) = pack<T>(o);
       }
     }
@@ -84,8 +87,8 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_fwd_kernel(const T* __re
 // dx = tau (g dy) - x tau^3 mean(x g dy) (AD of the forward, the operation
 // order of kernels/qk_norm.py:39-40); dgain partials = sum_rows dy (x tau).
 // Two rows per warp are in flight (their loads issued before either is
-// used); rows stay packed in registers and the gain sits in shared memory, so
-// two CTAs fit on an SM.
+// used); rows stay packed in registers, and the gain and the dgain
+// accumulator sit in shared memory, so two CTAs fit on an SM.
 constexpr int kNormBwdRows = 2;
 constexpr int kNormBwdBlocks = 148 * 2;
 
@@ -96,22 +99,28 @@ __global__ void __launch_bounds__(kNormThreads, 2) rmsnorm_bwd_kernel(const T* _
                                                                       float* __restrict__ partial, int64_t rows,
                                                                       int dim, float eps) {
   using V = Vec<T>;
-  extern __shared__ float red[];  // [kNormWarps][dim] partial sums, then [dim] gain
-  float* sg = red + kNormWarps * dim;
+  // Shared memory, all in the transposed [element i of a chunk][chunk] layout
+  // so that the lanes of a warp touch consecutive words: each warp's dgain
+  // accumulator [kNormWarps][N][32C], then the gain [N][32C].
+  extern __shared__ float red[];
+  constexpr int CP = 32 * C;
+  constexpr int WS = V::N * CP;                  // floats per warp accumulator
+  constexpr int R = C <= 3 ? kNormBwdRows : 1;  // rows in flight per warp (wider rows: one, no spills)
+  float* sg = red + kNormWarps * WS;
+  float* acc = red + (threadIdx.x >> 5) * WS;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int chunks = dim / V::N;
-  for (int i = threadIdx.x; i < dim; i += kNormThreads) sg[i] = gain ? gain[i] : 1.f;
+  for (int j = threadIdx.x; j < WS; j += kNormThreads) {
+    const int i = j / CP, idx = j - i * CP;
+    sg[j] = idx < chunks ? (gain ? gain[idx * V::N + i] : 1.f) : 0.f;
+  }
+  for (int j = threadIdx.x; j < kNormWarps * WS; j += kNormThreads) red[j] = 0.f;
   __syncthreads();
-  float acc[C][V::N];
-#pragma unroll
-  for (int c = 0; c < C; ++c)
-#pragma unroll
-    for (int i = 0; i < V::N; ++i) acc[c][i] = 0.f;
   const int64_t warps = (int64_t)gridDim.x * kNormWarps;
-  for (int64_t r0 = (int64_t)blockIdx.x * kNormWarps + warp; r0 < rows; r0 += kNormBwdRows * warps) {
-    uint4 rx[kNormBwdRows][C], rd[kNormBwdRows][C];
+  for (int64_t r0 = (int64_t)blockIdx.x * kNormWarps + warp; r0 < rows; r0 += R * warps) {
+    uint4 rx[R][C], rd[R][C];
 #pragma unroll
-    for (int k = 0; k < kNormBwdRows; ++k) {
+    for (int k = 0; k < R; ++k) {
       const int64_t row = r0 + k * warps;
 #pragma unroll
       for (int c = 0; c < C; ++c) {
@@ -122,7 +131,7 @@ __global__ void __launch_bounds__(kNormThreads, 2) rmsnorm_bwd_kernel(const T* _
       }
     }
 #pragma unroll
-    for (int k = 0; k < kNormBwdRows; ++k) {
+    for (int k = 0; k < R; ++k) {
       const int64_t row = r0 + k * warps;
       float ss = 0.f, sdg = 0.f;
 #pragma unroll
@@ -133,9 +142,8 @@ __global__ void __launch_bounds__(kNormThreads, 2) rmsnorm_bwd_kernel(const T* _
         unpack<T>(rd[k][c], dv);
 #pragma unroll
         for (int i = 0; i < V::N; ++i) {
-          const float g = idx < chunks ? sg[idx * V::N + i] : 0.f;
           ss = fmaf(xv[i], xv[i], ss);
-          sdg = fmaf(dv[i] * g, xv[i], sdg);
+          sdg = fmaf(dv[i] * sg[i * CP + idx], xv[i], sdg);
         }
       }
       ss = row_sum<32>(ss);
@@ -150,28 +158,20 @@ __global__ void __launch_bounds__(kNormThreads, 2) rmsnorm_bwd_kernel(const T* _
         unpack<T>(rd[k][c], dv);
 #pragma unroll
         for (int i = 0; i < V::N; ++i) {
-          const float g = idx < chunks ? sg[idx * V::N + i] : 0.f;
-          o[i] = (dv[i] * g) * tau - xv[i] * corr;
-          acc[c][i] = fmaf(dv[i], xv[i] * tau, acc[c][i]);
+          o[i] = (dv[i] * sg[i * CP + idx]) * tau - xv[i] * corr;
+          acc[i * CP + idx] = fmaf(dv[i], xv[i] * tau, acc[i * CP + idx]);
         }
         if (idx < chunks && row < rows) *reinterpret_cast<uint4*>(dx + row * dim + idx * V::N) = pack<T>(o);
       }
     }
   }
   if (!partial) return;  // no gain: no dgain
-#pragma unroll
-  for (int c = 0; c < C; ++c) {
-    const int idx = lane + 32 * c;
-    if (idx < chunks) {
-#pragma unroll
-      for (int i = 0; i < V::N; ++i) red[warp * dim + idx * V::N + i] = acc[c][i];
-    }
-  }
   __syncthreads();
   for (int col = threadIdx.x; col < dim; col += kNormThreads) {
+    const int idx = col / V::N, i = col - idx * V::N;
     float s = 0.f;
 #pragma unroll
-    for (int w = 0; w < kNormWarps; ++w) s += red[w * dim + col];
+    for (int w = 0; w < kNormWarps; ++w) s += red[w * WS + i * CP + idx];
     partial[(int64_t)blockIdx.x * dim + col] = s;
   }
 }
@@ -245,15 +245,15 @@ int check_norm(const void* x, const void* y, int64_t rows, int64_t dim, int32_t 
 
 template <typename T, int C>
 void launch_norm_fwd(const void* x, const float* gain, void* y, int64_t rows, int dim, float eps, cudaStream_t st) {
-  // dim <= 4096 floats of gain: at most 16 KB of shared memory
-  rmsnorm_fwd_kernel<T, C><<<norm_grid(rows), kNormThreads, (size_t)dim * sizeof(float), st>>>(
+  // the transposed gain: N x 32C floats (at most 16 KB)
+  rmsnorm_fwd_kernel<T, C><<<norm_grid(rows), kNormThreads, (size_t)Vec<T>::N * 32 * C * sizeof(float), st>>>(
       static_cast<const T*>(x), gain, static_cast<T*>(y), rows, dim, eps);
 }
 
 template <typename T, int C>
 cudaError_t launch_norm_bwd(const void* x, const float* gain, const void* dy, void* dx, float* partial,
                             int64_t rows, int dim, float eps, cudaStream_t st) {
-  const size_t smem = (size_t)(kNormWarps + 1) * dim * sizeof(float);
+  const size_t smem = (size_t)(kNormWarps + 1) * Vec<T>::N * 32 * C * sizeof(float);
   auto kern = rmsnorm_bwd_kernel<T, C>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -451,9 +451,10 @@ __global__ void __launch_bounds__(kPermThreads) permute_rows_kernel(const T* __r
     int64_t other[kPermUnroll];
 #pragma unroll
     for (int u = 0; u < kPermUnroll; ++u) {
-      const int64_t row = r0 + u * V::RPW + rl;  // head-major index (b*H + h)*T + t
-      const int64_t bh = row / T_, t = row - bh * T_, b = bh / H, h = bh - b * H;
-      other[u] = (b * T_ + t) * H + h;          // token-major index
+      const int64_t row = r0 + u * V::RPW + rl;  // head-major index (b*H + h)*T + t, below 2^31
+      const unsigned r = (unsigned)row, bh = r / (unsigned)T_, t = r - bh * (unsigned)T_;
+      const unsigned b = bh / (unsigned)H, h = bh - b * (unsigned)H;
+      other[u] = ((int64_t)b * T_ + t) * H + h;  // token-major index
       const int64_t from = to_tokens ? row : other[u];
       raw[u] = row < rows ? ld_stream(src + from * kRowDim + sub * V::N) : make_uint4(0, 0, 0, 0);
     }
@@ -475,7 +476,7 @@ int permute_rows(const void* src, void* dst, int64_t B, int64_t H, int64_t T, in
   ALGX_REQUIRE(src && dst && src != dst, std::string(who) + ": NULL or aliased pointers");
   ALGX_REQUIRE((reinterpret_cast<uintptr_t>(src) & 15) == 0 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0,
                std::string(who) + ": tensors must be 16-byte aligned");
-  ALGX_REQUIRE(T <= INT32_MAX && H <= INT32_MAX, std::string(who) + ": T or H out of range");
+  ALGX_REQUIRE(rows <= INT32_MAX, std::string(who) + ": B*H*T must be below 2^31");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int rpw = dtype == ALGX_BF16 ? Vec<__nv_bfloat16>::RPW : Vec<float>::RPW;
   const int64_t per_block = (int64_t)(kPermThreads / 32) * rpw * kPermUnroll;
