@@ -146,3 +146,28 @@ def aluglu(gu: torch.Tensor, beta: float = 1.0) -> torch.Tensor:
         raise ValueError("aluglu needs an even hidden width that is a multiple of 8")
     L.require_cuda(gu)
     return _ALUGLU.apply(gu, float(beta))
+
+
+class _Linear(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, w16):
+        ctx.save_for_backward(x, w16)
+        return x @ w16
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, w16 = ctx.saved_tensors
+        dx = dy @ w16.t()
+        x2 = x.reshape(-1, x.shape[-1])
+        dy2 = dy.reshape(-1, dy.shape[-1])
+        dw = torch.mm(x2.t(), dy2, out_dtype=torch.float32)
+        return dx, dw, None
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, w16: torch.Tensor) -> torch.Tensor:
+    """``x @ w.astype(bf16)`` (model.py:167-198) for a float32 master ``w`` whose
+    bf16 copy ``w16`` the caller keeps for a whole optimizer step: the weight is
+    not cast again per micro-batch, and the weight gradient comes out of its
+    GEMM in float32 (no bf16 rounding of it, no separate cast kernel) to be
+    accumulated into the master's gradient."""
+    return _Linear.apply(x, w, w16)

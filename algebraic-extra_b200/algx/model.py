@@ -40,7 +40,7 @@ from torch import nn
 from . import rotary as R
 from .kernels.flash import qknorm_flash_attention_packed
 from .kernels.fused_head import fused_head
-from .layers import aluglu, rms_norm, swiglu
+from .layers import aluglu, linear, rms_norm, swiglu
 
 BF16 = torch.bfloat16
 
@@ -214,9 +214,25 @@ class AlgebraicLM(nn.Module):
             cos, sin = R.cayley_table_geometric(cfg.head_dim, T, cfg.rope_base, fraction=cfg.rope_fraction)
         self.register_buffer("rot_cos", cos.to(device=device, dtype=torch.float32).contiguous(), persistent=False)
         self.register_buffer("rot_sin", sin.to(device=device, dtype=torch.float32).contiguous(), persistent=False)
+        self._w16 = {}
 
     def p(self, name: str) -> nn.Parameter:
         return self.flat[name]
+
+    def weights_changed(self) -> None:
+        """Drop the bf16 weight copies (the trainer calls this after each
+        optimizer step to release them early)."""
+        self._w16 = {}
+
+    def _mm(self, x: torch.Tensor, name: str) -> torch.Tensor:
+        """x @ bf16(w) with the bf16 copy made once per weight version: every
+        parameter view shares its version counter with the flat buffer, so an
+        optimizer step (or any in-place update) makes the next call recast."""
+        w = self.flat[name]
+        hit = self._w16.get(name)
+        if hit is None or hit[0] != w._version:
+            hit = self._w16[name] = (w._version, w.detach().to(BF16))
+        return linear(x, w, hit[1])
 
     def _block(self, i: int, x: torch.Tensor) -> torch.Tensor:
         cfg = self.cfg
@@ -224,7 +240,7 @@ class AlgebraicLM(nn.Module):
         H, D = cfg.n_heads, cfg.head_dim
         p = lambda n: self.flat[f"layers.{i}.{n}"]  # noqa: E731
         h = rms_norm(x, p("ln1"), cfg.eps)
-        qkv = (h @ p("w_qkv").to(BF16)).view(B, T, 3, H, D)  # token-major [q | k | v], no copy
+        qkv = self._mm(h, f"layers.{i}.w_qkv").view(B, T, 3, H, D)  # token-major [q | k | v], no copy
         if cfg.sink == "learned":
             sink = p("sink")
         elif cfg.sink == "const":
@@ -234,11 +250,11 @@ class AlgebraicLM(nn.Module):
         a = qknorm_flash_attention_packed(qkv, p("q_gain"), p("k_gain"), sink, eps=cfg.eps, kind="asinh",
                                           n=cfg.attn_n, c=cfg.attn_c, range_guard=True,
                                           rotary=(self.rot_cos, self.rot_sin))
-        x = x + a.view(B, T, d) @ p("w_o").to(BF16)
+        x = x + self._mm(a.view(B, T, d), f"layers.{i}.w_o")
         h2 = rms_norm(x, p("ln2"), cfg.eps)
-        gu = h2 @ p("w_gu").to(BF16)
+        gu = self._mm(h2, f"layers.{i}.w_gu")
         act = swiglu(gu) if cfg.ffn == "swiglu" else aluglu(gu, cfg.alu_beta)
-        return x + act @ p("w_d").to(BF16)
+        return x + self._mm(act, f"layers.{i}.w_d")
 
     def forward_hidden(self, tokens: torch.Tensor) -> torch.Tensor:
         """Final normalised hidden states (B, T, d) in bf16 (model.py:203-215)."""

@@ -129,6 +129,8 @@ class DataParallelTrainer:
             dist.all_reduce(loss_sum, group=self.group)
         self._clip_and_scale()
         self.opt.step()
+        if hasattr(self.model, "weights_changed"):
+            self.model.weights_changed()
         return loss_sum / (n_micro * self.world)
 
     def _clip_and_scale(self) -> None:

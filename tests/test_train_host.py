@@ -145,3 +145,16 @@ def test_two_ranks_match_one_process():
         assert all(abs(a - b) < 1e-6 for a, b in zip(losses, ref_losses)), (losses, ref_losses)
         for k in ref:
             torch.testing.assert_close(torch.from_numpy(params[k]), ref[k], rtol=1e-5, atol=1e-6)
+
+
+def test_optimizer_step_bumps_the_version_of_every_view():
+    """The model's bf16 weight copies are keyed on the master's version: an
+    optimizer update of the flat buffer must change each view's version."""
+    specs = M.param_specs(M.LMConfig(vocab_size=256, d_model=128, n_layers=1, n_heads=2, d_ff=256, seq_len=128))
+    fp = M.FlatParams(specs, "cpu", torch.Generator().manual_seed(0))
+    before = {n: p._version for n, p in fp.params.items()}
+    opt = torch.optim.AdamW([fp.flat[True], fp.flat[False]], lr=1e-3)
+    for k in (True, False):
+        fp.flat[k].grad = torch.ones_like(fp.flat[k])
+    opt.step()
+    assert all(fp.params[n]._version != v for n, v in before.items())
