@@ -302,8 +302,8 @@ def train_line(dev, rank, world, stream, sync_all, max_over_ranks, steps=3, warm
     from algx.train import DataParallelTrainer
 
     cfg = config_125m() if preset == "standard" else config_algebraic_125m()
-    per = TRAIN_GLOBAL_BATCH // world
-    micro = min(8, per)
+    per = max(1, TRAIN_GLOBAL_BATCH // world)
+    micro = max(m for m in range(1, 9) if per % m == 0)  # at most 8 sequences, dividing the rank's share
     model = AlgebraicLM(cfg, device=dev, seed=0)  # same initial replica on every rank
     tr = DataParallelTrainer(model, micro_batch=micro)
     g = torch.Generator(device=dev).manual_seed(777 + rank)
