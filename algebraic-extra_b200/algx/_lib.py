@@ -99,6 +99,8 @@ SIGNATURES = {
     "algx_rmsnorm_fwd": ([_P, _P, _P, _I64, _I64, _I32, _F, _P], ctypes.c_int),
     "algx_rmsnorm_bwd_workspace_size": ([_I64, _I64], _SZ),
     "algx_rmsnorm_bwd": ([_P, _P, _P, _P, _P, _I64, _I64, _I32, _F, _P, _SZ, _P], ctypes.c_int),
+    "algx_add_rmsnorm_fwd": ([_P, _P, _P, _P, _P, _I64, _I64, _I32, _F, _P], ctypes.c_int),
+    "algx_add_rmsnorm_bwd": ([_P, _P, _P, _P, _P, _P, _I64, _I64, _I32, _F, _P, _SZ, _P], ctypes.c_int),
     "algx_swiglu_fwd": ([_P, _P, _I64, _I64, _P], ctypes.c_int),
     "algx_swiglu_bwd": ([_P, _P, _P, _I64, _I64, _P], ctypes.c_int),
     "algx_aluglu_fwd": ([_P, _P, _I64, _I64, _F, _P], ctypes.c_int),

@@ -171,3 +171,59 @@ def linear(x: torch.Tensor, w: torch.Tensor, w16: torch.Tensor) -> torch.Tensor:
     GEMM in float32 (no bf16 rounding of it, no separate cast kernel) to be
     accumulated into the master's gradient."""
     return _Linear.apply(x, w, w16)
+
+
+class _AddRMSNorm(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, r, gain, eps):
+        x, r = x.contiguous(), r.contiguous()
+        dim = x.shape[-1]
+        s = torch.empty_like(x)
+        y = torch.empty_like(x)
+        L.check(L.lib().algx_add_rmsnorm_fwd(x.data_ptr(), r.data_ptr(), L.ptr(gain), s.data_ptr(), y.data_ptr(),
+                                             x.numel() // dim, dim, L.dtype_code(x.dtype), float(eps),
+                                             L.stream_of(x)), "algx_add_rmsnorm_fwd")
+        ctx.eps = float(eps)
+        ctx.has_gain = gain is not None
+        ctx.save_for_backward(s, gain)
+        return s, y
+
+    @staticmethod
+    def backward(ctx, ds, dy):
+        s, gain = ctx.saved_tensors
+        gain = gain if ctx.has_gain else None
+        if dy is None:
+            return ds, ds, None, None
+        if ds is None:
+            dx, dgain = rmsnorm_backward(s, gain, dy, ctx.eps)
+        else:
+            dim = s.shape[-1]
+            rows = s.numel() // dim
+            dy = dy.to(s.dtype).contiguous()
+            ds = ds.to(s.dtype).contiguous()
+            dx = torch.empty_like(s)
+            lib = L.lib()
+            dgain, ws, nbytes = None, None, 0
+            if gain is not None:
+                dgain = torch.empty(dim, dtype=torch.float32, device=s.device)
+                nbytes = lib.algx_rmsnorm_bwd_workspace_size(rows, dim)
+                ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=s.device)
+            L.check(lib.algx_add_rmsnorm_bwd(s.data_ptr(), L.ptr(gain), dy.data_ptr(), ds.data_ptr(), dx.data_ptr(),
+                                             L.ptr(dgain), rows, dim, L.dtype_code(s.dtype), ctx.eps, L.ptr(ws),
+                                             nbytes, L.stream_of(s)), "algx_add_rmsnorm_bwd")
+        return dx, dx, (dgain.to(gain.dtype) if dgain is not None else None), None
+
+
+def add_rms_norm(x: torch.Tensor, r: torch.Tensor, gain, eps: float = 1e-5):
+    """``s = x + r; (s, rms_norm(s, gain))`` in one launch each way (the residual
+    add and the norm that reads it, model.py:180-200); same values as the
+    composed ops, with the backward's two gradient contributions to ``s``
+    summed before one rounding."""
+    if x.shape != r.shape or x.dtype != r.dtype:
+        raise ValueError("add_rms_norm needs x and r of one shape and dtype")
+    if x.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("add_rms_norm needs float32 or bfloat16 input")
+    if gain is not None and (gain.dtype != torch.float32 or tuple(gain.shape) != (x.shape[-1],)):
+        raise ValueError("add_rms_norm gain must be float32 with the width of x's last axis")
+    L.require_cuda(x, r, gain)
+    return _AddRMSNorm.apply(x, r, gain, float(eps))

@@ -40,7 +40,7 @@ from torch import nn
 from . import rotary as R
 from .kernels.flash import qknorm_flash_attention_packed
 from .kernels.fused_head import fused_head
-from .layers import aluglu, linear, rms_norm, swiglu
+from .layers import add_rms_norm, aluglu, linear, rms_norm, swiglu
 
 BF16 = torch.bfloat16
 
@@ -234,12 +234,14 @@ class AlgebraicLM(nn.Module):
             hit = self._w16[name] = (w._version, w.detach().to(BF16))
         return linear(x, w, hit[1])
 
-    def _block(self, i: int, x: torch.Tensor) -> torch.Tensor:
+    def _block(self, i: int, x: torch.Tensor, h: torch.Tensor):
+        """Block i on the residual stream x with h = rms_norm(x, ln1) given;
+        returns (x', rms_norm(x', next gain)), each residual add fused into the
+        norm that follows it."""
         cfg = self.cfg
         B, T, d = x.shape
         H, D = cfg.n_heads, cfg.head_dim
         p = lambda n: self.flat[f"layers.{i}.{n}"]  # noqa: E731
-        h = rms_norm(x, p("ln1"), cfg.eps)
         qkv = self._mm(h, f"layers.{i}.w_qkv").view(B, T, 3, H, D)  # token-major [q | k | v], no copy
         if cfg.sink == "learned":
             sink = p("sink")
@@ -250,20 +252,21 @@ class AlgebraicLM(nn.Module):
         a = qknorm_flash_attention_packed(qkv, p("q_gain"), p("k_gain"), sink, eps=cfg.eps, kind="asinh",
                                           n=cfg.attn_n, c=cfg.attn_c, range_guard=True,
                                           rotary=(self.rot_cos, self.rot_sin))
-        x = x + self._mm(a.view(B, T, d), f"layers.{i}.w_o")
-        h2 = rms_norm(x, p("ln2"), cfg.eps)
+        x, h2 = add_rms_norm(x, self._mm(a.view(B, T, d), f"layers.{i}.w_o"), p("ln2"), cfg.eps)
         gu = self._mm(h2, f"layers.{i}.w_gu")
         act = swiglu(gu) if cfg.ffn == "swiglu" else aluglu(gu, cfg.alu_beta)
-        return x + self._mm(act, f"layers.{i}.w_d")
+        nxt = self.flat[f"layers.{i + 1}.ln1"] if i + 1 < cfg.n_layers else self.flat["final_gain"]
+        return add_rms_norm(x, self._mm(act, f"layers.{i}.w_d"), nxt, cfg.eps)
 
     def forward_hidden(self, tokens: torch.Tensor) -> torch.Tensor:
         """Final normalised hidden states (B, T, d) in bf16 (model.py:203-215)."""
         cfg = self.cfg
         x = nn.functional.embedding(tokens, self.flat["embed"]).to(BF16)
         x = rms_norm(x, self.flat["embed_gain"], cfg.eps)
+        h = rms_norm(x, self.flat["layers.0.ln1"], cfg.eps)
         for i in range(cfg.n_layers):
-            x = self._block(i, x)
-        return rms_norm(x, self.flat["final_gain"], cfg.eps)
+            x, h = self._block(i, x, h)
+        return h
 
     def loss(self, tokens: torch.Tensor, targets: torch.Tensor):
         """(objective, telemetry) of one micro-batch (model.py:218-226, fused head)."""

@@ -11,6 +11,8 @@
 // does not take.
 #include <algorithm>
 
+#include <type_traits>
+
 #include "attn_common.cuh"
 #include "attn_tc.h"
 #include "tmap.h"
@@ -133,7 +135,7 @@ __device__ __forceinline__ int64_t tok_row(int64_t row, int T_, int H, int strid
 // in_stride > 0: q, k, v are the blocks of one token-major (B, T, 3, H, D)
 // tensor (row stride in_stride = 3H), and vh (when not NULL) receives v in
 // head-major order for the TMA-fed attention kernels.
-template <typename T, bool ROT>
+template <typename T, bool ROT, bool PACKED>
 __global__ void __launch_bounds__(kPrepThreads) qknorm_attn_prepare_kernel(
     const T* __restrict__ q, const T* __restrict__ k, const T* __restrict__ v, const float* __restrict__ gain_q,
     const float* __restrict__ gain_k, const float* __restrict__ rot_cos, const float* __restrict__ rot_sin,
@@ -160,8 +162,8 @@ __global__ void __launch_bounds__(kPrepThreads) qknorm_attn_prepare_kernel(
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
       const int64_t row = r0 + u * V::RPW + rl;
-      raw[u] = row < rows ? ld_stream(src + tok_row(row, T_, H, in_stride) * kD + sub * V::N)
-                          : make_uint4(0, 0, 0, 0);
+      const int64_t srow = PACKED ? tok_row(row, T_, H, in_stride) : row;
+      raw[u] = row < rows ? ld_stream(src + srow * kD + sub * V::N) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
     for (int u = 0; u < kUnroll; ++u) {
@@ -172,7 +174,9 @@ __global__ void __launch_bounds__(kPrepThreads) qknorm_attn_prepare_kernel(
       if (which == 2) {
 #pragma unroll
         for (int i = 0; i < V::N; ++i) local = nan_max(local, fabsf(x[i]));
-        if (vh != nullptr && ok) *reinterpret_cast<uint4*>(vh + row * kD + sub * V::N) = raw[u];
+        if constexpr (PACKED) {
+          if (ok) *reinterpret_cast<uint4*>(vh + row * kD + sub * V::N) = raw[u];
+        }
         continue;
       }
       float ss = 0.f;
@@ -705,7 +709,7 @@ constexpr int kEpiUnroll = 4;
 // x and dx_out are head-major (tok_stride 0) or blocks of a token-major
 // (B, T, 3, H, D) tensor (tok_stride 3H); dy_in (when not FROM_ACC) and acc
 // are head-major. dy_in may equal dx_out (the in-place head-major call).
-template <typename T, bool FROM_ACC>
+template <typename T, bool FROM_ACC, bool PACKED>
 __device__ __forceinline__ void qk_rows_bwd(const T* __restrict__ x, const float* __restrict__ gain, const T* dy_in,
                                             T* dx_out, const float* __restrict__ acc, float f,
                                             const float* __restrict__ rot_cos, const float* __restrict__ rot_sin,
@@ -725,7 +729,8 @@ __device__ __forceinline__ void qk_rows_bwd(const T* __restrict__ x, const float
     for (int u = 0; u < kEpiUnroll; ++u) {
       const int64_t row = r0 + u * V::RPW + rl;
       const bool ok = row < rows;
-      rx[u] = ok ? ld_stream(x + tok_row(row, T_, H, tok_stride) * kD + sub * V::N) : make_uint4(0, 0, 0, 0);
+      const int64_t xrow = PACKED ? tok_row(row, T_, H, tok_stride) : row;
+      rx[u] = ok ? ld_stream(x + xrow * kD + sub * V::N) : make_uint4(0, 0, 0, 0);
 #pragma unroll
       for (int c = 0; c < kA; ++c) {
         if constexpr (FROM_ACC)
@@ -767,8 +772,8 @@ __device__ __forceinline__ void qk_rows_bwd(const T* __restrict__ x, const float
         out[i] = (dv[i] * g[i]) * tau - xv[i] * corr;
         part[i] = fmaf(dv[i], xv[i] * tau, part[i]);
       }
-      if (row < rows)
-        *reinterpret_cast<uint4*>(dx_out + tok_row(row, T_, H, tok_stride) * kD + sub * V::N) = pack<T>(out);
+      const int64_t orow = PACKED ? tok_row(row, T_, H, tok_stride) : row;
+      if (row < rows) *reinterpret_cast<uint4*>(dx_out + orow * kD + sub * V::N) = pack<T>(out);
     }
   }
 }
@@ -796,7 +801,7 @@ __device__ __forceinline__ void copy_rows_to_tokens(const T* __restrict__ dv_in,
   }
 }
 
-template <typename T>
+template <typename T, bool PACKED>
 __global__ void __launch_bounds__(kEpiThreads) qknorm_attn_bwd_kernel(
     algx_attn_config cfg, const float* __restrict__ guard, int fast, const float* __restrict__ dq_acc,
     const T* __restrict__ q, const float* __restrict__ gain_q, const T* __restrict__ k,
@@ -814,12 +819,14 @@ __global__ void __launch_bounds__(kEpiThreads) qknorm_attn_bwd_kernel(
 #pragma unroll
   for (int i = 0; i < V::N; ++i) pq[i] = pk[i] = 0.f;
   if (use_acc)
-    qk_rows_bwd<T, true>(q, gain_q, nullptr, dq_x, dq_acc, (float)cfg.n * cfg.scale, rot_cos, rot_sin, T_, H,
-                         tok_stride, rows, eps, pq);
+    qk_rows_bwd<T, true, PACKED>(q, gain_q, nullptr, dq_x, dq_acc, (float)cfg.n * cfg.scale, rot_cos, rot_sin, T_,
+                                 H, tok_stride, rows, eps, pq);
   else
-    qk_rows_bwd<T, false>(q, gain_q, dq_in, dq_x, nullptr, 1.f, rot_cos, rot_sin, T_, H, tok_stride, rows, eps, pq);
-  qk_rows_bwd<T, false>(k, gain_k, dk_in, dk_x, nullptr, 1.f, rot_cos, rot_sin, T_, H, tok_stride, rows, eps, pk);
-  if (dv_in != nullptr) copy_rows_to_tokens<T>(dv_in, dv_out, T_, H, tok_stride, rows);
+    qk_rows_bwd<T, false, PACKED>(q, gain_q, dq_in, dq_x, nullptr, 1.f, rot_cos, rot_sin, T_, H, tok_stride, rows,
+                                  eps, pq);
+  qk_rows_bwd<T, false, PACKED>(k, gain_k, dk_in, dk_x, nullptr, 1.f, rot_cos, rot_sin, T_, H, tok_stride, rows, eps,
+                                pk);
+  if constexpr (PACKED) copy_rows_to_tokens<T>(dv_in, dv_out, T_, H, tok_stride, rows);
   // CTA column sums: slot (warp, row-in-warp) holds its threads' columns
   const int lane = threadIdx.x & 31, sub = lane % V::TPR, rl = lane / V::TPR;
   const int slot = (threadIdx.x >> 5) * V::RPW + rl;
@@ -946,12 +953,23 @@ int qknorm_prepare_impl(const algx_attn_config* cfg, const void* q, const void* 
                                         sk, (int)H, (int)T, (TT*)q_scaled, (TT*)k_norm, guard, rows, cfg->scale, eps,
                                         in_stride, (TT*)v_heads);
   };
-  if (dtype == ALGX_BF16)
-    rope_cos ? launch(qknorm_attn_prepare_kernel<__nv_bfloat16, true>, __nv_bfloat16{})
-             : launch(qknorm_attn_prepare_kernel<__nv_bfloat16, false>, __nv_bfloat16{});
-  else
-    rope_cos ? launch(qknorm_attn_prepare_kernel<float, true>, float{})
-             : launch(qknorm_attn_prepare_kernel<float, false>, float{});
+  ALGX_REQUIRE(in_stride == 0 || v_heads, "qknorm_attn_prepare: the packed layout needs v_heads");
+  const bool packed = in_stride != 0;
+  if (dtype == ALGX_BF16) {
+    if (packed)
+      rope_cos ? launch(qknorm_attn_prepare_kernel<__nv_bfloat16, true, true>, __nv_bfloat16{})
+               : launch(qknorm_attn_prepare_kernel<__nv_bfloat16, false, true>, __nv_bfloat16{});
+    else
+      rope_cos ? launch(qknorm_attn_prepare_kernel<__nv_bfloat16, true, false>, __nv_bfloat16{})
+               : launch(qknorm_attn_prepare_kernel<__nv_bfloat16, false, false>, __nv_bfloat16{});
+  } else {
+    if (packed)
+      rope_cos ? launch(qknorm_attn_prepare_kernel<float, true, true>, float{})
+               : launch(qknorm_attn_prepare_kernel<float, false, true>, float{});
+    else
+      rope_cos ? launch(qknorm_attn_prepare_kernel<float, true, false>, float{})
+               : launch(qknorm_attn_prepare_kernel<float, false, false>, float{});
+  }
   ALGX_LAUNCHED("qknorm_attn_prepare launch");
   return ALGX_OK;
 }
@@ -1174,18 +1192,20 @@ int qknorm_attn_bwd_impl(const algx_attn_config* cfg, const void* q_src, const v
     ALGX_CUDA(cudaMemsetAsync(counter, 0, sizeof(unsigned), st));
   }
   const int64_t rows = B * H * T;
-  auto launch = [&](auto tag) {
+  auto launch = [&](auto tag, auto packed) {
     using TT = decltype(tag);
-    return launch_dependent(qknorm_attn_bwd_kernel<TT>, kEpiBlocks, kEpiThreads, 0, st, *cfg, guard,
+    return launch_dependent(qknorm_attn_bwd_kernel<TT, decltype(packed)::value>, kEpiBlocks, kEpiThreads, 0, st,
+                            *cfg, guard,
                             (dtype == ALGX_BF16 && fast) ? 1 : 0, acc, (const TT*)q_src, gain_q, (const TT*)k_src,
                             gain_k, rope_cos, rope_sin, (int)T, (TT*)dq_out, (TT*)dk_out, partial, counter, dgain_q,
                             dgain_k, rows, eps, (int)H, tok_stride, (const TT*)dq_h, (const TT*)dk_h,
                             (const TT*)(dv_out ? dv_h : nullptr), (TT*)dv_out);
   };
+  ALGX_REQUIRE((tok_stride == 0) == (dv_out == nullptr), "qknorm_attn_bwd: the packed layout needs dv_out");
   if (dtype == ALGX_BF16)
-    ALGX_CUDA(launch(__nv_bfloat16{}));
+    ALGX_CUDA(tok_stride ? launch(__nv_bfloat16{}, std::true_type{}) : launch(__nv_bfloat16{}, std::false_type{}));
   else
-    ALGX_CUDA(launch(float{}));
+    ALGX_CUDA(tok_stride ? launch(float{}, std::true_type{}) : launch(float{}, std::false_type{}));
   ALGX_LAUNCHED("qknorm_attn_bwd launch");
   return ALGX_OK;
 }

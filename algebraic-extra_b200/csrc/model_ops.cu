@@ -28,11 +28,14 @@ constexpr int kNormMaxBlocks = 148 * 3;
 
 // Forward: two rows per warp in flight (both rows' loads issued before
 // either is used), the gain in shared memory.
-template <typename T, int C>
+// ADD: the row is s = x + r rounded to T (the residual add before the norm,
+// model.py:180-200), written to s_out, then normalised.
+template <typename T, int C, bool ADD>
 __global__ void __launch_bounds__(kNormThreads) rmsnorm_fwd_kernel(const T* __restrict__ x,
                                                                    const float* __restrict__ gain,
                                                                    T* __restrict__ y, int64_t rows, int dim,
-                                                                   float eps) {
+                                                                   float eps, const T* __restrict__ r,
+                                                                   T* __restrict__ s_out) {
   using V = Vec<T>;
   // gain, transposed to [element i of a chunk][chunk]: the lanes of a warp read
   // consecutive words (no bank conflicts)
@@ -55,6 +58,25 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_fwd_kernel(const T* __re
       for (int c = 0; c < C; ++c) {
         const int idx = lane + 32 * c;
         raw[k][c] = (idx < chunks && row < rows) ? ld_stream(x + row * dim + idx * V::N) : make_uint4(0, 0, 0, 0);
+      }
+    }
+    if constexpr (ADD) {
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int64_t row = r0 + k * warps;
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+          const int idx = lane + 32 * c;
+          const uint4 rr =
+              (idx < chunks && row < rows) ? ld_stream(r + row * dim + idx * V::N) : make_uint4(0, 0, 0, 0);
+          float a[V::N], b[V::N];
+          unpack<T>(raw[k][c], a);
+          unpack<T>(rr, b);
+#pragma unroll
+          for (int i = 0; i < V::N; ++i) a[i] += b[i];
+          raw[k][c] = pack<T>(a);  // s = round(x + r)
+          if (idx < chunks && row < rows) *reinterpret_cast<uint4*>(s_out + row * dim + idx * V::N) = raw[k][c];
+        }
       }
     }
 #pragma unroll
@@ -92,12 +114,14 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_fwd_kernel(const T* __re
 constexpr int kNormBwdRows = 2;
 constexpr int kNormBwdBlocks = 148 * 2;
 
-template <typename T, int C>
+// ADD: dx = round(norm backward + ds), ds the gradient that reaches the
+// residual sum directly (the add's other consumer), in one rounding.
+template <typename T, int C, bool ADD>
 __global__ void __launch_bounds__(kNormThreads, 2) rmsnorm_bwd_kernel(const T* __restrict__ x,
                                                                       const float* __restrict__ gain,
                                                                       const T* __restrict__ dy, T* __restrict__ dx,
                                                                       float* __restrict__ partial, int64_t rows,
-                                                                      int dim, float eps) {
+                                                                      int dim, float eps, const T* __restrict__ ds) {
   using V = Vec<T>;
   // Shared memory, all in the transposed [element i of a chunk][chunk] layout
   // so that the lanes of a warp touch consecutive words: each warp's dgain
@@ -105,7 +129,7 @@ __global__ void __launch_bounds__(kNormThreads, 2) rmsnorm_bwd_kernel(const T* _
   extern __shared__ float red[];
   constexpr int CP = 32 * C;
   constexpr int WS = V::N * CP;                  // floats per warp accumulator
-  constexpr int R = C <= 3 ? kNormBwdRows : 1;  // rows in flight per warp (wider rows: one, no spills)
+  constexpr int R = (C <= 3 && !ADD) ? kNormBwdRows : 1;  // rows in flight per warp (else one, no spills)
   float* sg = red + kNormWarps * WS;
   float* acc = red + (threadIdx.x >> 5) * WS;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -160,6 +184,13 @@ __global__ void __launch_bounds__(kNormThreads, 2) rmsnorm_bwd_kernel(const T* _
         for (int i = 0; i < V::N; ++i) {
           o[i] = (dv[i] * sg[i * CP + idx]) * tau - xv[i] * corr;
           acc[i * CP + idx] = fmaf(dv[i], xv[i] * tau, acc[i * CP + idx]);
+        }
+        if constexpr (ADD) {
+          float dsv[V::N];
+          unpack<T>((idx < chunks && row < rows) ? ld_stream(ds + row * dim + idx * V::N) : make_uint4(0, 0, 0, 0),
+                    dsv);
+#pragma unroll
+          for (int i = 0; i < V::N; ++i) o[i] += dsv[i];
         }
         if (idx < chunks && row < rows) *reinterpret_cast<uint4*>(dx + row * dim + idx * V::N) = pack<T>(o);
       }
@@ -244,53 +275,61 @@ int check_norm(const void* x, const void* y, int64_t rows, int64_t dim, int32_t 
 }
 
 template <typename T, int C>
-void launch_norm_fwd(const void* x, const float* gain, void* y, int64_t rows, int dim, float eps, cudaStream_t st) {
+void launch_norm_fwd(const void* x, const float* gain, void* y, int64_t rows, int dim, float eps, cudaStream_t st,
+                     const void* r, void* s_out) {
   // the transposed gain: N x 32C floats (at most 16 KB)
-  rmsnorm_fwd_kernel<T, C><<<norm_grid(rows), kNormThreads, (size_t)Vec<T>::N * 32 * C * sizeof(float), st>>>(
-      static_cast<const T*>(x), gain, static_cast<T*>(y), rows, dim, eps);
+  const size_t smem = (size_t)Vec<T>::N * 32 * C * sizeof(float);
+  if (r)
+    rmsnorm_fwd_kernel<T, C, true><<<norm_grid(rows), kNormThreads, smem, st>>>(
+        static_cast<const T*>(x), gain, static_cast<T*>(y), rows, dim, eps, static_cast<const T*>(r),
+        static_cast<T*>(s_out));
+  else
+    rmsnorm_fwd_kernel<T, C, false><<<norm_grid(rows), kNormThreads, smem, st>>>(
+        static_cast<const T*>(x), gain, static_cast<T*>(y), rows, dim, eps, nullptr, nullptr);
 }
 
 template <typename T, int C>
 cudaError_t launch_norm_bwd(const void* x, const float* gain, const void* dy, void* dx, float* partial,
-                            int64_t rows, int dim, float eps, cudaStream_t st) {
+                            int64_t rows, int dim, float eps, cudaStream_t st, const void* ds) {
   const size_t smem = (size_t)(kNormWarps + 1) * Vec<T>::N * 32 * C * sizeof(float);
-  auto kern = rmsnorm_bwd_kernel<T, C>;
+  auto kern = ds ? rmsnorm_bwd_kernel<T, C, true> : rmsnorm_bwd_kernel<T, C, false>;
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
   }
   kern<<<norm_bwd_grid(rows), kNormThreads, smem, st>>>(static_cast<const T*>(x), gain, static_cast<const T*>(dy),
-                                                        static_cast<T*>(dx), partial, rows, dim, eps);
+                                                        static_cast<T*>(dx), partial, rows, dim, eps,
+                                                        static_cast<const T*>(ds));
   return cudaSuccess;
 }
 
 template <typename T>
 void dispatch_norm_fwd(int C, const void* x, const float* gain, void* y, int64_t rows, int dim, float eps,
-                       cudaStream_t st) {
+                       cudaStream_t st, const void* r = nullptr, void* s_out = nullptr) {
   switch (C) {
-    case 1: launch_norm_fwd<T, 1>(x, gain, y, rows, dim, eps, st); break;
-    case 2: launch_norm_fwd<T, 2>(x, gain, y, rows, dim, eps, st); break;
-    case 3: launch_norm_fwd<T, 3>(x, gain, y, rows, dim, eps, st); break;
-    case 4: launch_norm_fwd<T, 4>(x, gain, y, rows, dim, eps, st); break;
-    case 6: launch_norm_fwd<T, 6>(x, gain, y, rows, dim, eps, st); break;
-    case 8: launch_norm_fwd<T, 8>(x, gain, y, rows, dim, eps, st); break;
-    case 12: launch_norm_fwd<T, 12>(x, gain, y, rows, dim, eps, st); break;
-    default: launch_norm_fwd<T, 16>(x, gain, y, rows, dim, eps, st); break;
+    case 1: launch_norm_fwd<T, 1>(x, gain, y, rows, dim, eps, st, r, s_out); break;
+    case 2: launch_norm_fwd<T, 2>(x, gain, y, rows, dim, eps, st, r, s_out); break;
+    case 3: launch_norm_fwd<T, 3>(x, gain, y, rows, dim, eps, st, r, s_out); break;
+    case 4: launch_norm_fwd<T, 4>(x, gain, y, rows, dim, eps, st, r, s_out); break;
+    case 6: launch_norm_fwd<T, 6>(x, gain, y, rows, dim, eps, st, r, s_out); break;
+    case 8: launch_norm_fwd<T, 8>(x, gain, y, rows, dim, eps, st, r, s_out); break;
+    case 12: launch_norm_fwd<T, 12>(x, gain, y, rows, dim, eps, st, r, s_out); break;
+    default: launch_norm_fwd<T, 16>(x, gain, y, rows, dim, eps, st, r, s_out); break;
   }
 }
 
 template <typename T>
 cudaError_t dispatch_norm_bwd(int C, const void* x, const float* gain, const void* dy, void* dx, float* partial,
-                              int64_t rows, int dim, float eps, cudaStream_t st) {
+                              int64_t rows, int dim, float eps, cudaStream_t st, const void* ds = nullptr) {
   switch (C) {
-    case 1: return launch_norm_bwd<T, 1>(x, gain, dy, dx, partial, rows, dim, eps, st);
-    case 2: return launch_norm_bwd<T, 2>(x, gain, dy, dx, partial, rows, dim, eps, st);
-    case 3: return launch_norm_bwd<T, 3>(x, gain, dy, dx, partial, rows, dim, eps, st);
-    case 4: return launch_norm_bwd<T, 4>(x, gain, dy, dx, partial, rows, dim, eps, st);
-    case 6: return launch_norm_bwd<T, 6>(x, gain, dy, dx, partial, rows, dim, eps, st);
-    case 8: return launch_norm_bwd<T, 8>(x, gain, dy, dx, partial, rows, dim, eps, st);
-    case 12: return launch_norm_bwd<T, 12>(x, gain, dy, dx, partial, rows, dim, eps, st);
-    default: return launch_norm_bwd<T, 16>(x, gain, dy, dx, partial, rows, dim, eps, st);
+    case 1: return launch_norm_bwd<T, 1>(x, gain, dy, dx, partial, rows, dim, eps, st, ds);
+    case 2: return launch_norm_bwd<T, 2>(x, gain, dy, dx, partial, rows, dim, eps, st, ds);
+    case 3: return launch_norm_bwd<T, 3>(x, gain, dy, dx, partial, rows, dim, eps, st, ds);
+    case 4: return launch_norm_bwd<T, 4>(x, gain, dy, dx, partial, rows, dim, eps, st, ds);
+    case 6: return launch_norm_bwd<T, 6>(x, gain, dy, dx, partial, rows, dim, eps, st, ds);
+    case 8: return launch_norm_bwd<T, 8>(x, gain, dy, dx, partial, rows, dim, eps, st, ds);
+    case 12: return launch_norm_bwd<T, 12>(x, gain, dy, dx, partial, rows, dim, eps, st, ds);
+    default: return launch_norm_bwd<T, 16>(x, gain, dy, dx, partial, rows, dim, eps, st, ds);
   }
 }
 
@@ -541,6 +580,56 @@ int algx_rmsnorm_bwd(const void* x, const float* gain, const void* dy, void* dx,
   else
     ALGX_CUDA(dispatch_norm_bwd<float>(C, x, gain, dy, dx, partial, rows, (int)dim, eps, st));
   ALGX_LAUNCHED("rmsnorm_bwd launch");
+  if (gain) {
+    rmsnorm_dgain_reduce<<<(unsigned)((dim + 31) / 32), 256, 0, st>>>(partial, grid, (int)dim, dgain);
+    ALGX_LAUNCHED("rmsnorm_dgain_reduce launch");
+  }
+  return ALGX_OK;
+}
+
+int algx_add_rmsnorm_fwd(const void* x, const void* r, const float* gain, void* s_out, void* y, int64_t rows,
+                         int64_t dim, int32_t dtype, float eps, void* stream) {
+  if (int st = check_norm(x, y, rows, dim, dtype, eps, "add_rmsnorm_fwd")) return st;
+  ALGX_REQUIRE(rows == 0 || (r && s_out), "add_rmsnorm_fwd: NULL pointer");
+  ALGX_REQUIRE((reinterpret_cast<uintptr_t>(r) & 15) == 0 && (reinterpret_cast<uintptr_t>(s_out) & 15) == 0,
+               "add_rmsnorm_fwd: tensors must be 16-byte aligned");
+  if (rows == 0) return ALGX_OK;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int C = norm_chunks(dim, dtype);
+  if (dtype == ALGX_BF16)
+    dispatch_norm_fwd<__nv_bfloat16>(C, x, gain, y, rows, (int)dim, eps, st, r, s_out);
+  else
+    dispatch_norm_fwd<float>(C, x, gain, y, rows, (int)dim, eps, st, r, s_out);
+  ALGX_LAUNCHED("add_rmsnorm_fwd launch");
+  return ALGX_OK;
+}
+
+int algx_add_rmsnorm_bwd(const void* s, const float* gain, const void* dy, const void* ds, void* dx, float* dgain,
+                         int64_t rows, int64_t dim, int32_t dtype, float eps, void* workspace, size_t workspace_bytes,
+                         void* stream) {
+  if (int st = check_norm(s, dx, rows, dim, dtype, eps, "add_rmsnorm_bwd")) return st;
+  ALGX_REQUIRE(rows == 0 || (dy && ds), "add_rmsnorm_bwd: NULL pointer");
+  ALGX_REQUIRE((reinterpret_cast<uintptr_t>(dy) & 15) == 0 && (reinterpret_cast<uintptr_t>(ds) & 15) == 0,
+               "add_rmsnorm_bwd: tensors must be 16-byte aligned");
+  ALGX_REQUIRE(!gain || dgain, "add_rmsnorm_bwd: a gain needs a dgain output");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (rows == 0) {
+    if (gain) ALGX_CUDA(cudaMemsetAsync(dgain, 0, (size_t)dim * sizeof(float), st));
+    return ALGX_OK;
+  }
+  const int grid = norm_bwd_grid(rows);
+  float* partial = nullptr;
+  if (gain) {
+    ALGX_REQUIRE(workspace && workspace_bytes >= (size_t)grid * (size_t)dim * sizeof(float),
+                 "add_rmsnorm_bwd: workspace too small (see algx_rmsnorm_bwd_workspace_size)");
+    partial = static_cast<float*>(workspace);
+  }
+  const int C = norm_chunks(dim, dtype);
+  if (dtype == ALGX_BF16)
+    ALGX_CUDA(dispatch_norm_bwd<__nv_bfloat16>(C, s, gain, dy, dx, partial, rows, (int)dim, eps, st, ds));
+  else
+    ALGX_CUDA(dispatch_norm_bwd<float>(C, s, gain, dy, dx, partial, rows, (int)dim, eps, st, ds));
+  ALGX_LAUNCHED("add_rmsnorm_bwd launch");
   if (gain) {
     rmsnorm_dgain_reduce<<<(unsigned)((dim + 31) / 32), 256, 0, st>>>(partial, grid, (int)dim, dgain);
     ALGX_LAUNCHED("rmsnorm_dgain_reduce launch");

@@ -300,6 +300,19 @@ ALGX_API int algx_rmsnorm_bwd(const void* x, const float* gain, const void* dy, 
                               int64_t rows, int64_t dim, int32_t dtype, float eps, void* workspace,
                               size_t workspace_bytes, void* stream);
 
+/* Residual add fused into the following norm (model.py:180-200): s = x + r
+ * rounded to the I/O dtype, written to s_out, and y = rms_norm(s) * gain as
+ * algx_rmsnorm_fwd. No counterpart in the reference (XLA fuses the add). */
+ALGX_API int algx_add_rmsnorm_fwd(const void* x, const void* r, const float* gain, void* s_out, void* y,
+                                  int64_t rows, int64_t dim, int32_t dtype, float eps, void* stream);
+
+/* Backward of algx_add_rmsnorm_fwd: dx = (norm backward of dy at s) + ds,
+ * rounded once, where ds is the gradient reaching s from its other consumer;
+ * dx is the gradient of both x and r. Workspace as algx_rmsnorm_bwd. */
+ALGX_API int algx_add_rmsnorm_bwd(const void* s, const float* gain, const void* dy, const void* ds, void* dx,
+                                  float* dgain, int64_t rows, int64_t dim, int32_t dtype, float eps, void* workspace,
+                                  size_t workspace_bytes, void* stream);
+
 /* y = gate * silu(up), bf16, for rows of gu = [gate (ff) | up (ff)]; y is
  * (rows, ff). ff a multiple of 8. Replaces model.py:193-198 (`gate * act`,
  * act = S.silu(up), standard.py:12-13), evaluated in fp32 and rounded once. */

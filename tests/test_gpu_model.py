@@ -216,3 +216,27 @@ def test_packed_attention_matches_head_major(with_sink):
         assert _rel_l2(sa.grad, sb.grad) < 1e-3
     from algx import _lib as L
     assert L.device_error() == 0
+
+
+@pytest.mark.parametrize("dtype,dim", [(torch.bfloat16, 768), (torch.bfloat16, 1024), (torch.float32, 768)])
+def test_add_rms_norm_matches_composed(dtype, dim):
+    """The fused residual add + norm equals x + r followed by rms_norm: s and y
+    bit-identical, gradients within one rounding (1e-2 / 1e-5 relative L2)."""
+    from algx.layers import add_rms_norm, rms_norm
+    g = torch.Generator(device="cuda").manual_seed(dim)
+    x = torch.randn((777, dim), device="cuda", generator=g).to(dtype)
+    r = torch.randn((777, dim), device="cuda", generator=g).to(dtype)
+    gain = 1 + 0.1 * torch.randn(dim, device="cuda", generator=g)
+    ds = torch.randn((777, dim), device="cuda", generator=g).to(dtype)
+    dy = torch.randn((777, dim), device="cuda", generator=g).to(dtype)
+    a = [t.clone().requires_grad_(True) for t in (x, r, gain)]
+    s1, y1 = add_rms_norm(a[0], a[1], a[2], 1e-5)
+    torch.autograd.backward([s1, y1], [ds, dy])
+    b = [t.clone().requires_grad_(True) for t in (x, r, gain)]
+    s2 = b[0] + b[1]
+    y2 = rms_norm(s2, b[2], 1e-5)
+    torch.autograd.backward([s2, y2], [ds, dy])
+    assert torch.equal(s1, s2) and torch.equal(y1, y2)
+    tol = 1e-2 if dtype == torch.bfloat16 else 1e-5
+    assert _rel_l2(a[0].grad, b[0].grad) < tol and _rel_l2(a[1].grad, b[1].grad) < tol
+    assert _rel_l2(a[2].grad, b[2].grad) < 1e-5
