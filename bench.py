@@ -294,7 +294,7 @@ TRAIN_GLOBAL_BATCH = 64  # sequences per optimizer step, split over the ranks (c
 def train_line(dev, rank, world, stream, sync_all, max_over_ranks, steps=3, warmup=3, preset="standard"):
     """Config 5: the 125M training step (fwd + bwd + clip + AdamW) on synthetic
     uniform token ids, global batch 64 x 2048 split over the ranks, micro-batches
-    of 8 sequences, gradient all-reduce overlapped with the last backward.
+    of up to 32 sequences, gradient all-reduce overlapped with the last backward.
     preset "standard": SwiGLU, RoPE, ce head; "algebraic":
     the reference's algebraic preset at the same size (ALU-GLU, Cayley
     rotations, learned sink, alg_ce head n=8 c=2)."""
@@ -303,7 +303,10 @@ def train_line(dev, rank, world, stream, sync_all, max_over_ranks, steps=3, warm
 
     cfg = config_125m() if preset == "standard" else config_algebraic_125m()
     per = max(1, TRAIN_GLOBAL_BATCH // world)
-    micro = max(m for m in range(1, 9) if per % m == 0)  # at most 8 sequences, dividing the rank's share
+    # micro-batches of up to 32 sequences dividing the rank's share: 32 x 2048
+    # tokens per pass measured 6% faster than 8 on one B200 (larger GEMMs,
+    # fewer gradient accumulations); the global batch stays 64 sequences
+    micro = max(m for m in range(1, 33) if per % m == 0)
     model = AlgebraicLM(cfg, device=dev, seed=0)  # same initial replica on every rank
     tr = DataParallelTrainer(model, micro_batch=micro)
     g = torch.Generator(device=dev).manual_seed(777 + rank)
