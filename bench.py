@@ -322,8 +322,8 @@ def train_line(dev, rank, world, stream, sync_all, max_over_ranks, steps=3, warm
     tflops = train_flops_per_token(cfg) * tokens / (ms / 1e3) / 1e12
     peak_tf, _, peak_src = _peaks(sustained=True)
     line = {"metric": "125M train tok/s", "value": tokens / (ms / 1e3), "unit": "tok/s", "ms_per_step": ms,
-            "steps": steps, "warmup": warmup, "tflops_6P": tflops, "mfu": tflops / peak_tf,
-            "mfu_peak": f"{peak_tf:.1f} TFLOP/s {peak_src} bf16 dense (sustained)",
+            "steps": steps, "warmup": warmup, "tflops_6P": tflops, "mfu": tflops / (peak_tf * world),
+            "mfu_peak": f"{peak_tf:.1f} TFLOP/s {peak_src} bf16 dense (sustained) per GPU x {world}",
             "loss_first": float(losses[0]), "loss_last": float(losses[-1]),
             "params": count_params(cfg), "flop_per_token": train_flops_per_token(cfg),
             "config": f"L={cfg.n_layers} d={cfg.d_model} H={cfg.n_heads} ff={cfg.d_ff} V={cfg.vocab_size} "
