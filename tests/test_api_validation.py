@@ -60,3 +60,46 @@ def test_qk_norm_rejects_like_reference():
         qk_rms_norm(torch.ones((1024, 64)), g, eps=0.0)
     with pytest.raises(RuntimeError, match="CUDA tensors only"):
         qk_rms_norm(torch.ones((1024, 64)), g)
+
+
+def test_training_step_layers_validate_before_any_launch():
+    """The training-step layers reject bad arguments, and CPU tensors, before any kernel call."""
+    from algx._lib import AlgxError
+    from algx.layers import add_rms_norm, aluglu, rms_norm, swiglu
+    x = torch.ones((4, 768), dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="float32 or bfloat16"):
+        rms_norm(x.to(torch.float16), None)
+    with pytest.raises(ValueError, match="gain must be float32"):
+        rms_norm(x, torch.ones(767))
+    with pytest.raises(ValueError, match="epsilon must be positive"):
+        rms_norm(x, None, 0.0)
+    with pytest.raises(ValueError, match="one shape and dtype"):
+        add_rms_norm(x, torch.ones((4, 768)), None)
+    with pytest.raises(ValueError, match="bfloat16"):
+        swiglu(torch.ones((4, 64)))
+    with pytest.raises(ValueError, match="multiple of 8"):
+        aluglu(torch.ones((4, 24), dtype=torch.bfloat16))
+    with pytest.raises(AlgxError, match="CUDA tensors only"):
+        rms_norm(x, torch.ones(768))
+
+
+def test_packed_attention_validates_its_layout():
+    from algx.kernels.flash import qknorm_flash_attention_packed
+    g = torch.ones(64)
+    with pytest.raises(ValueError, match=r"\(B, T, 3, H, D\)"):
+        qknorm_flash_attention_packed(torch.ones((1, 128, 2, 2, 64), dtype=torch.bfloat16), g, g)
+    with pytest.raises(ValueError, match="head_dim 64"):
+        qknorm_flash_attention_packed(torch.ones((1, 128, 3, 2, 32), dtype=torch.bfloat16), torch.ones(32),
+                                      torch.ones(32))
+
+
+def test_model_config_rejects_unsupported_choices():
+    from algx.model import LMConfig
+    with pytest.raises(ValueError, match="head_dim = 64"):
+        LMConfig(d_model=768, n_heads=16).validate()
+    with pytest.raises(ValueError, match="unknown ffn"):
+        LMConfig(ffn="gelu").validate()
+    with pytest.raises(ValueError, match="unknown position"):
+        LMConfig(pos="none").validate()
+    with pytest.raises(ValueError, match="unknown head"):
+        LMConfig(head="mse").validate()
