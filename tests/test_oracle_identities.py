@@ -108,3 +108,26 @@ def test_product_tables_match_oracle():
         for a, b in zip(got, want):
             assert a.dtype == torch.float32 and a.shape == b.shape
             assert torch.allclose(a, b, atol=2e-6, rtol=0)
+
+
+@pytest.mark.parametrize("beta", [0.5, 0.8, 1.0])
+def test_alu_stable_form_and_custom_vjp_match_the_closed_form(beta):
+    """alu(x) = x/2 (1 + bx / sqrt(1 + b^2 x^2)) (algebraic.py:95-101): the oracle's
+    r^2 / (1 - u) branch for bx < 0 equals the direct formula where both are
+    accurate, and its custom VJP (algebraic.py:104-113) equals autograd of it."""
+    x = torch.linspace(-40.0, 40.0, 4001, dtype=torch.float64)
+    xa = x.clone().requires_grad_(True)
+    y = R.alu(xa, beta)
+    y.sum().backward()
+    xb = x.clone().requires_grad_(True)
+    bz = beta * xb
+    direct = 0.5 * xb * (1.0 + bz / torch.sqrt(1.0 + bz * bz))
+    direct.sum().backward()
+    torch.testing.assert_close(y.detach(), direct.detach(), rtol=1e-9, atol=1e-12)
+    torch.testing.assert_close(xa.grad, xb.grad, rtol=1e-9, atol=1e-12)
+    # far negative tail: the stable form keeps relative precision where 1 + u cancels
+    # (for bx < 0, with w = 1/(bx)^2: 1 + u = w / ((1 + w) + sqrt(1 + w)), no cancellation)
+    t = torch.tensor([-30.0, -1e4, -1e6], dtype=torch.float64)
+    w = 1.0 / (beta * beta * t * t)
+    exact = 0.5 * t * w / ((1.0 + w) + torch.sqrt(1.0 + w))
+    torch.testing.assert_close(R.alu(t, beta), exact, rtol=1e-12, atol=0.0)
