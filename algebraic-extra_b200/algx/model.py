@@ -14,9 +14,15 @@ rotations, a learned per-head sink, the ``alg_ce`` head). Per block (model.py:18
     x  = x + a @ w_o
     x  = x + glu(rms_norm(x, ln2) @ [w_g | w_u]) @ w_d      glu: SwiGLU or ALU-GLU
 
-Parameters are float32 masters; every matmul casts its weight to bfloat16
-(``.astype(dt)`` in model.py:167-196), so gradients reach the masters in
-float32. All parameters live in two flat float32 buffers (decayed weights and
+and each residual add runs fused into the RMS norm that reads its sum
+(``add_rms_norm``: ln2 inside the block, the next block's ln1 or the final
+gain after it).
+
+Parameters are float32 masters; every matmul reads a bfloat16 copy of its
+weight (``.astype(dt)`` in model.py:167-196), made once per weight version
+rather than once per micro-batch, and its weight gradient comes out of the
+GEMM in float32 and accumulates into the master's gradient. All parameters
+live in two flat float32 buffers (decayed weights and
 the embedding; gains and sinks), with every ``nn.Parameter`` a view into
 them and every ``.grad`` a view into matching flat gradient buffers. The
 optimizer then updates two tensors, the gradient all-reduce runs over
