@@ -103,6 +103,26 @@ def config_125m(**overrides) -> LMConfig:
     return replace(LMConfig(), **overrides)
 
 
+_FIELD_TYPES = {"int": int, "float": float, "str": str, "bool": bool}
+
+
+def parse_overrides(pairs) -> dict:
+    """``key=value`` strings to typed ``LMConfig`` field overrides (the
+    trainer's ``--set``, train.py:31-45): the value is converted by the
+    field's declared type; booleans accept 1/true/yes (any case) as true.
+    An unknown field raises ``ValueError``."""
+    from dataclasses import fields
+    types = {f.name: (f.type if isinstance(f.type, str) else f.type.__name__) for f in fields(LMConfig)}
+    out = {}
+    for item in pairs or []:
+        key, _, value = item.partition("=")
+        if key not in types:
+            raise ValueError(f"unknown config field {key!r}")
+        kind = _FIELD_TYPES[types[key]]
+        out[key] = value.lower() in ("1", "true", "yes") if kind is bool else kind(value)
+    return out
+
+
 def config_algebraic_125m(**overrides) -> LMConfig:
     """The reference's pure algebraic preset at the 125M size (config.py:25-36):
     ALU-GLU with beta 1/2, geometric Cayley rotations, QK norm, rho(s/8)^16

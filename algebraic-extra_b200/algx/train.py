@@ -33,13 +33,18 @@ class DataParallelTrainer:
 
     ``micro_batch``: sequences per forward/backward pass; the rank's share of
     the batch must be a multiple of it. ``bucket_bytes``: target size of one
-    all-reduce.
+    all-reduce. ``check_finite``: before each optimizer update, read the loss
+    and the gradient norm on the host and raise ``FloatingPointError`` if
+    either is not finite (the reference trainer's check, train.py:423-427),
+    leaving the master weights at their last finite values; it costs one host
+    synchronisation per step, so it is off by default.
     """
 
     def __init__(self, model, *, lr: float = 2e-3, betas=(0.9, 0.95), eps: float = 1e-8,
                  weight_decay: float = 0.1, clip: float = 1.0, micro_batch: int = 8,
-                 bucket_bytes: int = 32 << 20, group=None):
+                 bucket_bytes: int = 32 << 20, group=None, check_finite: bool = False):
         self.model = model
+        self.check_finite = bool(check_finite)
         self.flat = model.flat
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
@@ -128,10 +133,18 @@ class DataParallelTrainer:
             self._works = []
             dist.all_reduce(loss_sum, group=self.group)
         self._clip_and_scale()
+        loss = loss_sum / (n_micro * self.world)
+        if self.check_finite:
+            # loss and gnorm are already reduced over the ranks, so every rank
+            # takes the same decision and no collective is left unmatched
+            ok = bool(torch.isfinite(loss) & torch.isfinite(self.last_gnorm))
+            if not ok:
+                raise FloatingPointError(f"non-finite loss {float(loss)} or gradient norm "
+                                         f"{float(self.last_gnorm)}; the update was not applied")
         self.opt.step()
         if hasattr(self.model, "weights_changed"):
             self.model.weights_changed()
-        return loss_sum / (n_micro * self.world)
+        return loss
 
     def _clip_and_scale(self) -> None:
         grads = list(self.flat.grad.values())
@@ -154,19 +167,28 @@ def main(argv=None) -> None:
     import argparse
     import json
 
-    from .model import AlgebraicLM, config_125m, train_flops_per_token
+    from .model import AlgebraicLM, config_125m, config_algebraic_125m, parse_overrides, train_flops_per_token
 
     ap = argparse.ArgumentParser(description=main.__doc__)
     ap.add_argument("--profile-steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=2)
     ap.add_argument("--batch", type=int, default=64, help="sequences per optimizer step")
     ap.add_argument("--micro", type=int, default=8, help="sequences per micro-batch")
-    ap.add_argument("--layers", type=int, default=None, help="override n_layers")
+    ap.add_argument("--preset", choices=("standard", "algebraic"), default="standard",
+                    help="standard: BASELINE config 5 (SwiGLU, RoPE, ce); algebraic: the reference's algebraic preset")
+    ap.add_argument("--set", action="append", default=[], metavar="KEY=VALUE",
+                    help="override an LMConfig field, typed by the field (repeatable)")
+    ap.add_argument("--layers", type=int, default=None, help="override n_layers (same as --set n_layers=N)")
+    ap.add_argument("--check-finite", action="store_true",
+                    help="raise FloatingPointError on a non-finite loss or gradient norm (one host sync per step)")
     args = ap.parse_args(argv)
-    cfg = config_125m() if args.layers is None else config_125m(n_layers=args.layers)
+    over = parse_overrides(args.set)
+    if args.layers is not None:
+        over["n_layers"] = args.layers
+    cfg = (config_125m if args.preset == "standard" else config_algebraic_125m)(**over)
     dev = torch.device("cuda", torch.cuda.current_device())
     model = AlgebraicLM(cfg, device=dev, seed=0)
-    tr = DataParallelTrainer(model, micro_batch=args.micro)
+    tr = DataParallelTrainer(model, micro_batch=args.micro, check_finite=args.check_finite)
     g = torch.Generator(device=dev).manual_seed(777)
     seq = torch.randint(0, cfg.vocab_size, (args.batch, cfg.seq_len + 1), device=dev, generator=g)
     tok, tgt = seq[:, :-1].contiguous(), seq[:, 1:].contiguous()
@@ -182,8 +204,8 @@ def main(argv=None) -> None:
     tokens = args.batch * cfg.seq_len
     print(json.dumps({"tok_per_s": tokens / (ms / 1e3), "ms_per_step": ms,
                       "tflops_6P": train_flops_per_token(cfg) * tokens / (ms / 1e3) / 1e12,
-                      "loss": [float(x) for x in losses], "batch": args.batch, "micro": args.micro,
-                      "layers": cfg.n_layers}))
+                      "loss": [float(x) for x in losses], "gnorm": float(tr.last_gnorm), "batch": args.batch,
+                      "micro": args.micro, "layers": cfg.n_layers, "preset": args.preset}))
 
 
 if __name__ == "__main__":

@@ -158,3 +158,69 @@ def test_optimizer_step_bumps_the_version_of_every_view():
         fp.flat[k].grad = torch.ones_like(fp.flat[k])
     opt.step()
     assert all(fp.params[n]._version != v for n, v in before.items())
+
+
+def test_parse_overrides_types_values_like_the_reference_cli():
+    over = M.parse_overrides(["n_layers=2", "attn_c=4", "head=alg_ce", "d_model=128"])
+    assert over == {"n_layers": 2, "attn_c": 4.0, "head": "alg_ce", "d_model": 128}
+    assert isinstance(over["attn_c"], float) and isinstance(over["n_layers"], int)
+    cfg = M.config_125m(**over)
+    assert cfg.n_layers == 2 and cfg.head == "alg_ce"
+    with pytest.raises(ValueError, match="unknown config field"):
+        M.parse_overrides(["heads=3"])
+
+
+def test_check_finite_raises_before_the_update():
+    """A non-finite loss raises FloatingPointError and leaves the masters untouched."""
+    model = ToyLM()
+    tr = DataParallelTrainer(model, lr=1e-2, micro_batch=8, check_finite=True)
+    tok, tgt = _batch()
+    tr.step(tok, tgt)  # finite: applied
+    with torch.no_grad():
+        model.flat["out_gain"][0] = float("nan")
+    before = {k: v.clone() for k, v in model.flat.data.items()}
+    with pytest.raises(FloatingPointError, match="not applied"):
+        tr.step(tok, tgt)
+    for k, v in model.flat.data.items():
+        assert torch.allclose(v, before[k], equal_nan=True)
+
+
+def _leaving_worker(rank, init_file, q):
+    import datetime
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path[:0] = [root, os.path.join(root, "algebraic-extra_b200")]
+    dist.init_process_group("gloo", init_method=f"file://{init_file}", rank=rank, world_size=2,
+                            timeout=datetime.timedelta(seconds=10))
+    if rank == 1:  # leaves between steps, before joining any collective
+        dist.destroy_process_group()
+        q.put((rank, "left"))
+        return
+    try:
+        from algx.train import DataParallelTrainer as T
+        from tests.test_train_host import ToyLM, _batch
+        tr = T(ToyLM(), lr=1e-2, micro_batch=2, bucket_bytes=256)
+        tok, tgt = _batch()
+        tr.step(tok[:4], tgt[:4])
+        q.put((rank, "no error"))
+    except Exception as e:  # noqa: BLE001 - the failure is the expected outcome
+        q.put((rank, type(e).__name__))
+
+
+def test_step_fails_instead_of_hanging_when_a_rank_leaves():
+    """A rank that leaves before the step: the other rank's gradient all-reduce
+    errors out (peer gone or process-group timeout) rather than waiting forever."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    with tempfile.TemporaryDirectory() as tmp:
+        init = os.path.join(tmp, "init")
+        procs = [ctx.Process(target=_leaving_worker, args=(r, init, q)) for r in range(2)]
+        for p in procs:
+            p.start()
+        out = dict(q.get(timeout=120) for _ in procs)
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    assert out[1] == "left"
+    assert out[0] == "RuntimeError", out
