@@ -42,14 +42,18 @@ enum { ALGX_ATTN_ASINH = 0, ALGX_ATTN_SOFTMAX = 1 };
 enum { ALGX_MODE_CLIPPED = 0, ALGX_MODE_SHIFTED = 1, ALGX_MODE_GUARDED = 2 };
 enum { ALGX_HEAD_CE = 0, ALGX_HEAD_ALG_CE = 1 };
 
-/* Message of the last failed call on this thread. */
+/* Message of the last failed call on this thread. Library plumbing:
+ * no counterpart in the reference (its kernels raise Python exceptions). */
 ALGX_API const char* algx_last_error(void);
-/* Library version (major*10000 + minor*100 + patch). */
+/* Library version (major*10000 + minor*100 + patch).
+ * No counterpart in the reference. */
 ALGX_API int algx_version(void);
-/* Number of kernels this process launched through libalgx so far. */
+/* Number of kernels this process launched through libalgx so far.
+ * No counterpart in the reference. */
 ALGX_API uint64_t algx_launch_count(void);
 /* Reads and clears the device error word of the current device (bounded
- * waits that gave up set it). Synchronizes the device. */
+ * waits that gave up set it). Synchronizes the device. No counterpart in the
+ * reference (a Pallas kernel has no bounded device-side waits). */
 ALGX_API int algx_device_error(int32_t* code);
 
 /* ------------------------------------------------------------------ QK norm */
@@ -59,7 +63,7 @@ ALGX_API int algx_device_error(int32_t* code);
 ALGX_API int algx_qknorm_fwd(const void* x, const float* gain, void* y, int64_t rows, int64_t dim,
                     int32_t dtype, float eps, void* stream);
 
-/* Bytes of workspace algx_qknorm_bwd needs. */
+/* Bytes of workspace algx_qknorm_bwd needs. No counterpart in the reference: XLA sizes the Pallas kernels' scratch itself. */
 ALGX_API size_t algx_qknorm_bwd_workspace_size(int64_t rows, int64_t dim);
 
 /* dx and dgain of the QK norm. Replaces kernels/qk_norm.py:39-55 `_norm_bwd`
@@ -133,7 +137,7 @@ ALGX_API int algx_attn_fwd(const algx_attn_config* cfg, const void* q_scaled, co
                   const float* sink, const float* guard, void* o, float* o_precise, float* stat,
                   int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype, void* stream);
 
-/* Bytes of workspace algx_attn_bwd needs. */
+/* Bytes of workspace algx_attn_bwd needs. No counterpart in the reference: XLA sizes the Pallas kernels' scratch itself. */
 ALGX_API size_t algx_attn_bwd_workspace_size(int64_t B, int64_t H, int64_t T, int64_t D);
 
 /* Causal backward: dq (with the scale fold applied, i.e. d/dq of the
@@ -146,7 +150,7 @@ ALGX_API int algx_attn_bwd(const algx_attn_config* cfg, const void* q_scaled, co
                   int64_t B, int64_t H, int64_t T, int64_t D, int32_t dtype, void* workspace,
                   size_t workspace_bytes, void* stream);
 
-/* Bytes of workspace algx_qknorm_attn_bwd needs. */
+/* Bytes of workspace algx_qknorm_attn_bwd needs. No counterpart in the reference: XLA sizes the Pallas kernels' scratch itself. */
 ALGX_API size_t algx_qknorm_attn_bwd_workspace_size(int64_t B, int64_t H, int64_t T, int64_t D);
 
 /* Backward of attention over QK-normed inputs, the counterpart of
@@ -211,7 +215,8 @@ ALGX_API int algx_head_finalize(const algx_head_config* cfg, const int32_t* targ
                                 void* stream);
 
 /* Workspace bytes of algx_head_bwd: one bf16 dz slab of N x min(4096, V
- * rounded up to 256) plus, when dh is bf16, an fp32 dh accumulator. */
+ * rounded up to 256) plus, when dh is bf16, an fp32 dh accumulator. The
+ * reference writes dz for the whole vocabulary (fused_head.py:194-216). */
 ALGX_API size_t algx_head_bwd_workspace_size(int64_t N, int64_t d, int64_t V, int32_t dh_dtype);
 
 /* dh (N, d) in dh_dtype (partial over this rank's vocabulary rows) and
@@ -254,13 +259,14 @@ ALGX_API int algx_qknorm_attn_prepare_packed(const algx_attn_config* cfg, const 
                                              int32_t dtype, float eps, void* stream);
 
 /* Workspace bytes of algx_qknorm_attn_bwd_packed: that of
- * algx_qknorm_attn_bwd plus head-major dq, dk, dv scratch. */
+ * algx_qknorm_attn_bwd plus head-major dq, dk, dv scratch. No counterpart in the reference: XLA sizes the Pallas kernels' scratch itself. */
 ALGX_API size_t algx_qknorm_attn_bwd_packed_workspace_size(int64_t B, int64_t H, int64_t T, int64_t D,
                                                            int32_t dtype);
 
 /* algx_qknorm_attn_bwd for a forward run by algx_qknorm_attn_prepare_packed:
  * dout head-major (B, H, T, D); dqkv (B, T, 3, H, D) receives the gradients of
- * the raw q and k and of v in the packed layout. */
+ * the raw q and k and of v in the packed layout. Replaces the backward of
+ * model.py:166-180 (projections' transposes, QK norm, rotary, flash.py:718-726). */
 ALGX_API int algx_qknorm_attn_bwd_packed(const algx_attn_config* cfg, const void* qkv, const float* gain_q,
                                          const float* gain_k, const float* rope_cos, const float* rope_sin,
                                          int64_t rope_rows, const void* q_scaled, const void* k_norm,
@@ -275,6 +281,8 @@ ALGX_API int algx_qknorm_attn_bwd_packed(const algx_attn_config* cfg, const void
  * (model.py:180). No counterpart in the reference (an XLA transpose). */
 ALGX_API int algx_heads_to_tokens(const void* src, void* dst, int64_t B, int64_t H, int64_t T, int64_t D,
                                   int32_t dtype, void* stream);
+/* The inverse permutation: dO from the output projection back to head-major
+ * order. No counterpart in the reference (an XLA transpose). */
 ALGX_API int algx_tokens_to_heads(const void* src, void* dst, int64_t B, int64_t H, int64_t T, int64_t D,
                                   int32_t dtype, void* stream);
 
@@ -290,7 +298,7 @@ ALGX_API int algx_rmsnorm_fwd(const void* x, const float* gain, void* y, int64_t
                               int32_t dtype, float eps, void* stream);
 
 /* Bytes of workspace algx_rmsnorm_bwd needs (one fp32 row of dgain partials
- * per CTA). */
+ * per CTA). No counterpart in the reference (XLA reduces dgain itself). */
 ALGX_API size_t algx_rmsnorm_bwd_workspace_size(int64_t rows, int64_t dim);
 
 /* dx and dgain of algx_rmsnorm_fwd (JAX AD of algebraic.py:76-83 in the
@@ -308,7 +316,8 @@ ALGX_API int algx_add_rmsnorm_fwd(const void* x, const void* r, const float* gai
 
 /* Backward of algx_add_rmsnorm_fwd: dx = (norm backward of dy at s) + ds,
  * rounded once, where ds is the gradient reaching s from its other consumer;
- * dx is the gradient of both x and r. Workspace as algx_rmsnorm_bwd. */
+ * dx is the gradient of both x and r. Workspace as algx_rmsnorm_bwd. No
+ * counterpart in the reference (JAX AD of the add and norm, model.py:180-200). */
 ALGX_API int algx_add_rmsnorm_bwd(const void* s, const float* gain, const void* dy, const void* ds, void* dx,
                                   float* dgain, int64_t rows, int64_t dim, int32_t dtype, float eps, void* workspace,
                                   size_t workspace_bytes, void* stream);

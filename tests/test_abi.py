@@ -40,3 +40,18 @@ def test_workspace_queries_are_host_only():
     lib = L.lib()
     assert lib.algx_qknorm_bwd_workspace_size(196608, 64) > 0
     assert lib.algx_attn_bwd_workspace_size(8, 12, 2048, 64) >= 8 * 12 * 2048 * 4
+
+
+def test_every_declaration_cites_the_reference_or_says_it_has_none():
+    """Each entry point's comment names the reference function it replaces
+    (file.py:line) or states that it has no counterpart in the reference."""
+    text = open(os.path.join(ROOT, "include", "algx.h")).read()
+    decls = [(m.start(), text.index(";", m.start()), m.group(1))
+             for m in re.finditer(r"ALGX_API[^;]*?\b(algx_\w+)\s*\(", text)]
+    missing, prev_end = [], 0
+    for start, end, name in decls:
+        chunk = text[prev_end:start]
+        if not (re.search(r"\.py:\d", chunk) or re.search(r"[Nn]o counterpart", chunk)):
+            missing.append(name)
+        prev_end = end
+    assert len(decls) >= 30 and not missing, missing
