@@ -105,7 +105,6 @@ SIGNATURES = {
     "algx_swiglu_bwd": ([_P, _P, _P, _I64, _I64, _P], ctypes.c_int),
     "algx_aluglu_fwd": ([_P, _P, _I64, _I64, _F, _P], ctypes.c_int),
     "algx_aluglu_bwd": ([_P, _P, _P, _I64, _I64, _F, _P], ctypes.c_int),
-    "algx_selftest_tcgen05": ([_I32, _P, _P, _P, _P], ctypes.c_int),
 }
 
 _lib = None

@@ -248,11 +248,21 @@ def secondary(dev, rank, world, stream, sync_all, max_over_ranks, steps=5, warmu
 
         ms = time_cuda(step, steps, warmup, stream, sync_all, max_over_ranks)
         flop = 3 * 2 * HEAD_N * d * HEAD_V  # bench_head.py:36 convention (recompute excluded)
+        tflops = flop / (ms / 1e3) / 1e12
+        peak_tf, _, peak_src = _peaks()
         return {"metric": "fused CE head tok/s", "value": HEAD_N / (ms / 1e3), "unit": "tok/s",
-                "ms_per_step": ms, "tflops_3gemm": flop / (ms / 1e3) / 1e12, "kind": kind, "n": n, "c": c,
+                "ms_per_step": ms, "tflops_3gemm": tflops, "kind": kind, "n": n, "c": c,
+                "roofline": {"bound": "tensor", "achieved": tflops, "peak": peak_tf * world, "unit": "TFLOP/s",
+                             "frac": tflops / (peak_tf * world), "traffic": None,
+                             "algorithmic": "3 x 2*N*d*V FLOP per step (bench_head.py:36: forward GEMM, dh, dE; "
+                                            "the backward's logit recompute, a fourth GEMM, is not counted)",
+                             "frac_with_recompute": 4 / 3 * tflops / (peak_tf * world),
+                             "peak_source": f"{peak_src} bf16 dense (burst) x {world} GPU"},
                 "config": f"N={HEAD_N} d={d} V={HEAD_V} bf16, 5% labels = ignore_index -100, fwd+bwd",
                 "scaling": "strong (vocabulary rows split over the ranks)" if world > 1 else "single GPU"}
 
+    trace("secondary: qk norm cfg2")
+    out["qknorm_cfg2"] = qknorm_line(dev, gen, world, stream, sync_all, max_over_ranks)
     trace("secondary: head cfg3 ce")
     out["head_cfg3_ce"] = head_line(768, "ce", 16, 16.0)
     trace("secondary: head cfg3 alg_ce")
@@ -285,6 +295,53 @@ def secondary(dev, rank, world, stream, sync_all, max_over_ranks, steps=5, warmu
     out["train_cfg5"] = train_line(dev, rank, world, stream, sync_all, max_over_ranks)
     trace("secondary: train cfg5, algebraic preset")
     out["train_cfg5_algebraic"] = train_line(dev, rank, world, stream, sync_all, max_over_ranks, preset="algebraic")
+    return out
+
+
+def qknorm_line(dev, gen, world, stream, sync_all, max_over_ranks, steps=20, warmup=3, copies=4):
+    """QK RMS norm alone at config 2 (q and k, each (8, 12, 2048, 64) bf16), through
+    the public kernels of algx.kernels.qk_norm: forward of q and k, then the backward
+    (dx and dgain) of q and k. Bytes per the reference's convention: 4 B/elem forward
+    (read x, write y), 6 B/elem backward (read x, dy, write dx). Each timed call works
+    on one of ``copies`` input sets in turn (4 x 100 MB > L2), so a call never finds
+    its inputs in L2 from the previous use."""
+    from algx.kernels.qk_norm import qknorm_backward, qknorm_forward
+
+    shape = (B, H, T, D)
+    elems = 2 * B * H * T * D
+    sets = [[torch.randn(shape, device=dev, generator=gen).to(torch.bfloat16) for _ in range(4)]
+            for _ in range(copies)]  # q, k, dy_q, dy_k
+    gq = 1 + 0.02 * torch.randn(D, device=dev, generator=gen)
+    gk = 1 + 0.02 * torch.randn(D, device=dev, generator=gen)
+    from algx import _lib as L
+    ws = torch.empty(L.lib().algx_qknorm_bwd_workspace_size(B * H * T, D), dtype=torch.uint8, device=dev)
+    state = {"i": 0}
+
+    def fwd():
+        q, k, _, _ = sets[state["i"] % copies]
+        state["i"] += 1
+        qknorm_forward(q, gq, EPS)
+        qknorm_forward(k, gk, EPS)
+
+    def bwd():
+        q, k, dq, dk = sets[state["i"] % copies]
+        state["i"] += 1
+        qknorm_backward(q, gq, dq, EPS, ws)
+        qknorm_backward(k, gk, dk, EPS, ws)
+
+    peak_tf, hbm, peak_src = _peaks()
+    out = {"metric": "QK-norm GB/s", "unit": "GB/s",
+           "config": f"q and k of config 2, each (B={B}, H={H}, S={T}, D={D}) bf16, qk_rms_norm fwd / bwd kernels; "
+                     f"{copies} rotating input sets (L2 not reused between calls)"}
+    for name, fn, per_elem in (("fwd", fwd, 4), ("bwd", bwd, 6)):
+        ms = time_cuda(fn, steps, warmup, stream, sync_all, max_over_ranks)
+        nbytes = per_elem * elems
+        gbs = nbytes / (ms / 1e3) / 1e9
+        out[name] = {"value": gbs, "ms_per_call": ms, "bytes": nbytes,
+                     "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                                  "frac": gbs / hbm, "traffic": None,
+                                  "peak_source": f"{peak_src} HBM copy bandwidth"}}
+    del sets
     return out
 
 

@@ -233,15 +233,6 @@ ALGX_API int algx_head_bwd(const algx_head_config* cfg, const void* h, const voi
                            int64_t vocab_offset, int32_t dtype, void* workspace, size_t workspace_bytes,
                            void* stream);
 
-/* --------------------------------------------------------------- diagnostics */
-
-/* One-CTA tcgen05/TMA self-test: D = A*B for the operand layouts the
- * attention kernels use (mode 0: SS K-major x K-major, N=128; 1: B MN-major;
- * 2: A from TMEM; 3: A MN-major; 4: N=256). Inputs are bf16 device buffers:
- * a (128 x ka, row-major; for mode 3 the transpose 128 x 128), b (nb x kb).
- * out: fp32 128 x nout. No counterpart in the reference (hardware check). */
-ALGX_API int algx_selftest_tcgen05(int32_t mode, const void* a, const void* b, float* out, void* stream);
-
 /* --------------------------------------------- packed (token-major) attention */
 /* The model's QKV projection writes one token-major tensor qkv (B, T, 3, H, D)
  * ([q | k | v] per token, each H x D); its output projection reads the

@@ -1,5 +1,13 @@
-// One-CTA tcgen05 + TMA self-test of the operand layouts the attention and
-// head kernels use. The host compares the result with a reference GEMM.
+// TEST-ONLY. One-CTA tcgen05 + TMA self-test of the operand layouts the
+// attention and head kernels use; the host compares the result with a
+// reference GEMM. Built into tests/native/libalgx_selftest.so (with the
+// library's error and tensor-map helpers linked in privately), never into the
+// product libalgx.so, and not part of the C ABI in include/algx.h:
+//   int algx_selftest_tcgen05(int32_t mode, const void* a, const void* b,
+//                             float* out, void* stream);
+// a, b: bf16 device buffers, a (128 x ka, row-major; for mode 3 its
+// transpose), b (nb x kb); out: fp32 128 x nout. The kernel's bounded waits
+// report through this library's own algx_device_error().
 //   mode 0: D[128x128]  = A[128x64]  . B[128x64]^T   (A, B K-major, SW128)
 //   mode 1: D[128x64]   = A[128x128] . B[128x64]     (A K-major in two 64-wide
 //                                                     chunks, B MN-major)
@@ -125,7 +133,7 @@ __global__ void __launch_bounds__(128) tc_selftest_kernel(const __grid_constant_
 
 using namespace algx;
 
-extern "C" int algx_selftest_tcgen05(int32_t mode, const void* a, const void* b, float* out, void* stream) {
+extern "C" __attribute__((visibility("default"))) int algx_selftest_tcgen05(int32_t mode, const void* a, const void* b, float* out, void* stream) {
   ALGX_REQUIRE(mode >= 0 && mode <= 4, "selftest: mode must be 0..4");
   ALGX_REQUIRE(a && b && out, "selftest: NULL pointer");
   CUtensorMap ta, tb;

@@ -142,3 +142,24 @@ def test_baseline_config3_full_size_against_chunked_check():
     assert abs(obj.item() - loss_ref) < 1e-4
     assert rel_l2(hc.grad.float(), dh_ref) < 1e-2
     assert rel_l2(ec.grad.float(), de_ref) < 1e-2
+
+
+def test_out_of_range_label_sets_the_device_error_word():
+    """With ignore_index set, a label outside [0, V) other than ignore_index is an
+    error (the reference's kernel reads nothing for it, fused_head.py:86-87): the
+    head sets DEV_ERR_BAD_LABEL (4) in the device error word, which
+    algx_device_error() reads and clears; a following call with valid labels
+    leaves the word at 0. Host-visible status only, no fault."""
+    from algx import _lib as L
+    V = 1000
+    h, e, t = _inputs(256, 128, V, 0.05, 17)
+    t[3] = -100          # the ignore index: fine
+    L.device_error()     # start from a clear word
+    for bad in (V, -1, 2 ** 31 - 1):
+        tb = t.clone()
+        tb[7] = bad
+        _run(h, e, tb, kind="ce", ignore_index=-100)
+        assert L.device_error() == 4, bad
+        assert L.device_error() == 0  # read-and-clear
+    _run(h, e, t, kind="ce", ignore_index=-100)
+    assert L.device_error() == 0
