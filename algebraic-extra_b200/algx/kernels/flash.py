@@ -15,7 +15,7 @@ shifted (high) branch from them, so no host synchronisation happens.
 
 from __future__ import annotations
 
-import math
+import math  # noqa: F401
 from typing import Optional
 
 import torch
@@ -23,47 +23,9 @@ import torch
 from .. import _lib as L
 
 
-def _root(value: float, n: int) -> float:
-    """value^(1/n) for n a power of two by repeated sqrt (kernels/flash.py:117-123)."""
-    out = float(value)
-    while n > 1:
-        out = math.sqrt(out)
-        n //= 2
-    return out
-
-
-class Variant(dict):
-    """Resolved asinh/softmax variant (mirrors kernels/flash.py:59-73)."""
-
-
-def make_variant(kind: str, n: int = 16, c: float = 16.0, seq_len: int = 2048,
-                 shift: Optional[bool] = None, fast_rho: Optional[bool] = None,
-                 inv_stat: Optional[bool] = None, compact_stat: bool = True,
-                 poly_rho: bool = False) -> Variant:
-    """Variant resolution of kernels/flash.py:732-760."""
-    if kind == "softmax":
-        return Variant(kind="softmax", n=16, shift=True, fast_rho=False, clamp=0.0, inv_stat=False,
-                       compact_stat=bool(compact_stat), poly_rho=False)
-    if kind != "asinh":
-        raise ValueError(f"unknown attention kernel: {kind}")
-    if n < 2 or n & (n - 1):
-        raise ValueError("asinh kernel needs n to be a power of two")
-    if not math.isfinite(c) or c <= 0:
-        raise ValueError("asinh scale c must be positive and finite")
-    t = _root(1e37 / (seq_len + 1), n)
-    clamp = 0.5 * (t - 1.0 / t)
-    if shift is None:
-        shift = clamp < 20.0
-    if fast_rho is None:
-        fast_rho = True
-    if inv_stat is None:
-        inv_stat = not shift
-    if inv_stat and shift:
-        raise ValueError("inverse-denominator statistic requires shift=False")
-    if poly_rho and (shift or n != 16):
-        raise ValueError("bounded radical approximation requires shift=False and n=16")
-    return Variant(kind="asinh", n=int(n), shift=bool(shift), fast_rho=bool(fast_rho), clamp=float(clamp),
-                   inv_stat=bool(inv_stat), compact_stat=bool(compact_stat), poly_rho=bool(poly_rho))
+# Variant resolution, option checks and wrapper constants live in the
+# torch-free algx.variants (shared with the JAX front-end); re-exported here.
+from ..variants import Variant, check_flash_options, config_lists, make_variant  # noqa: E402,F401
 
 
 def attn_forward(q, k, v, sink, cfg: L.AttnConfig):
@@ -188,28 +150,6 @@ class _Flash(torch.autograd.Function):
         return dq, dk, dv, dsink, None
 
 
-def config_lists(kind, var: Variant, T: int, D: int, c: float, has_sink: bool, range_guard: bool):
-    """The resolved variant and the wrapper constants (kernels/flash.py:823-856)
-    as plain scalars: ints ``[kind, mode, n, fast_rho, inv_stat, has_sink]`` and
-    floats ``[clamp, scale, guard_qk, guard_sink, guard_v]``."""
-    unit = 1.0 if kind == "softmax" else float(c)
-    guard_qk = guard_sink = guard_v = 0.0
-    if kind == "asinh" and range_guard and var["n"] <= 32:
-        bound = min(16.0, var["clamp"] / 2)
-        mode = L.ALGX_MODE_GUARDED
-        guard_qk = (bound / 1.01) ** 2
-        guard_sink = bound / 1.01
-        guard_v = min(1e8, 1e37 / ((T + int(has_sink)) * (2 * bound + 1) ** var["n"]))
-    elif kind == "asinh":
-        mode = L.ALGX_MODE_SHIFTED if var["shift"] else L.ALGX_MODE_CLIPPED
-    else:
-        mode = L.ALGX_MODE_SHIFTED
-    ints = [L.ALGX_ATTN_SOFTMAX if kind == "softmax" else L.ALGX_ATTN_ASINH, mode, int(var["n"]),
-            int(var["fast_rho"]), int(var["inv_stat"]), int(has_sink)]
-    floats = [float(var["clamp"]), 1.0 / (math.sqrt(D) * unit), guard_qk, guard_sink, guard_v]
-    return ints, floats
-
-
 def config_from_lists(ints, floats) -> L.AttnConfig:
     """Pack :func:`config_lists` into the C ABI's ``AlgxAttnConfig``."""
     cfg = L.AttnConfig()
@@ -242,27 +182,11 @@ def flash_attention(q, k, v, sink_logit=None, *, kind: str = "softmax",
     the reference's own polynomial-mode tolerance). D must be 64.
     """
     B, H, T, D = q.shape
-    bq = min(block_q or block, T)
-    bk = min(block_k or block, T)
-    if T % bq or T % bk:
-        raise ValueError(f"sequence length {T} must be divisible by blocks ({bq}, {bk})")
-    var = make_variant(kind, n, c, T, shift, fast_rho, inv_stat, compact_stat, poly_rho)
-    resident_supported = (T in (512, 1024, 2048) and D == 64 and
-                          q.dtype == k.dtype == v.dtype == torch.bfloat16 and not poly_rho and
-                          (kind == "softmax" or n == 16))
-    if resident_bwd is True and not resident_supported:
-        raise ValueError("resident backward needs bfloat16, T=512/1024/2048, D=64, "
-                         "and softmax or exact asinh n=16")
-    use_resident = (resident_supported and T == 2048 and bq == bk == 512 and compact_stat
-                    if resident_bwd is None else bool(resident_bwd))
-    if diagonal_bwd is True and not use_resident:
-        raise ValueError("diagonal backward requires the resident backward backend")
-    head_supported = (use_resident and T == 2048 and bq == bk == 512 and compact_stat)
-    if head_resident is True and not head_supported:
-        raise ValueError("whole-head residency needs resident bfloat16 T=2048,D=64, "
-                         "512-square public tiles, and compact statistics")
-    if range_guard and kind == "asinh" and n <= 32 and poly_rho:
-        raise ValueError("range_guard is for exact radical evaluation")
+    var = check_flash_options(T, D, q.dtype == k.dtype == v.dtype == torch.bfloat16, kind=kind, n=n, c=c,
+                              block=block, block_q=block_q, block_k=block_k, shift=shift, fast_rho=fast_rho,
+                              inv_stat=inv_stat, compact_stat=compact_stat, poly_rho=poly_rho,
+                              range_guard=range_guard, resident_bwd=resident_bwd, diagonal_bwd=diagonal_bwd,
+                              head_resident=head_resident)
     cfg, sink = _checked_call(q, k, v, sink_logit, kind, var, c, range_guard)
     return _Flash.apply(q.contiguous(), k.contiguous(), v.contiguous(), sink, cfg)
 

@@ -20,29 +20,14 @@ which is what a TPU matmul at default precision does with float32 operands).
 
 from __future__ import annotations
 
-import math
-
 import torch
 
 from .. import _lib as L
 
 
-def _root(value: float, n: int) -> float:
-    out = float(value)
-    while n > 1:
-        out = math.sqrt(out)
-        n //= 2
-    return out
-
-
-def head_config_lists(kind: str, n: int, c: float, vocab: int, ignore_index=None):
-    """The objective's constants as plain scalars: ints ``[kind, n, has_ignore,
-    ignore_index]`` and floats ``[inv_c, clamp]``."""
-    ints = [L.ALGX_HEAD_CE if kind == "ce" else L.ALGX_HEAD_ALG_CE, int(n), int(ignore_index is not None),
-            int(ignore_index) if ignore_index is not None else 0]
-    floats = [1.0 / float(c) if kind == "alg_ce" else 1.0,
-              0.25 * _root(1e38 / vocab, n) if kind == "alg_ce" else 0.0]
-    return ints, floats
+# The objective's constants and argument checks live in the torch-free
+# algx.variants (shared with the JAX front-end); re-exported here.
+from ..variants import check_head_options, head_config_lists, head_slope  # noqa: E402,F401
 
 
 def head_config_from_lists(ints, floats) -> L.HeadConfig:
@@ -139,22 +124,11 @@ def fused_head(h, embed, targets, *, kind="ce", n=16, c=16.0, block_n=128, block
     telemetry)``. ``block_n``/``block_v`` are validated as the reference does
     (N divisible by min(block_n, N)) and do not change the result.
     """
-    if kind not in ("ce", "alg_ce"):
-        raise ValueError(kind)
-    if kind == "alg_ce" and (n & (n - 1)):
-        raise ValueError("n must be a power of two")
-    N, d = h.shape
-    bn = min(block_n, N)
-    if N % bn:
-        raise ValueError(f"token count {N} must be divisible by block {bn}")
-    if kind == "alg_ce" and n not in (2, 4, 8, 16, 32):
-        raise ValueError("algx fused head supports alg_ce powers n in {2, 4, 8, 16, 32}")
-    if d % 64:
-        raise ValueError(f"algx fused head needs d to be a multiple of 64, got {d}")
+    N, d = check_head_options(kind, n, h.shape, block_n)
     if embed.shape[1] != d or targets.shape != (N,):
         raise ValueError("h (N, d), embed (V, d) and targets (N,) shapes disagree")
     L.require_cuda(h, embed, targets)
     cfg = head_config(kind, n, c, embed.shape[0], ignore_index)
-    slope = 1.0 if kind == "ce" else n / c
+    slope = head_slope(kind, n, c)
     obj, tel = _Head.apply(h, embed, targets, cfg, slope)
     return obj, tel.detach()

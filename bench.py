@@ -329,12 +329,30 @@ def qknorm_line(dev, gen, world, stream, sync_all, max_over_ranks, steps=20, war
         qknorm_backward(q, gq, dq, EPS, ws)
         qknorm_backward(k, gk, dk, EPS, ws)
 
+    def graph_of(fn, n):
+        """n calls of fn captured in one CUDA graph: the timing then measures the
+        kernels, not the Python wrapper's per-call launch overhead."""
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                fn()
+        stream.wait_stream(side)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for _ in range(n):
+                fn()
+        return g
+
     peak_tf, hbm, peak_src = _peaks()
     out = {"metric": "QK-norm GB/s", "unit": "GB/s",
-           "config": f"q and k of config 2, each (B={B}, H={H}, S={T}, D={D}) bf16, qk_rms_norm fwd / bwd kernels; "
-                     f"{copies} rotating input sets (L2 not reused between calls)"}
+           "config": f"q and k of config 2, each (B={B}, H={H}, S={T}, D={D}) bf16, qk_rms_norm fwd / bwd kernels "
+                     f"(bwd: dx and the dgain reduction) through the public wrappers, {steps} calls captured in a "
+                     f"CUDA graph and replayed; {copies} rotating input sets (L2 not reused between calls)"}
     for name, fn, per_elem in (("fwd", fwd, 4), ("bwd", bwd, 6)):
-        ms = time_cuda(fn, steps, warmup, stream, sync_all, max_over_ranks)
+        g = graph_of(fn, steps)
+        ms = time_cuda(g.replay, 1, warmup, stream, sync_all, max_over_ranks) / steps
+        del g
         nbytes = per_elem * elems
         gbs = nbytes / (ms / 1e3) / 1e9
         out[name] = {"value": gbs, "ms_per_call": ms, "bytes": nbytes,
