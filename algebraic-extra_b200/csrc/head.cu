@@ -14,14 +14,13 @@
 // kSlabCols columns at a time, so the logits are never materialised in full:
 // head_dz_tc_kernel recomputes the slab's logits with the forward's pipeline
 // and its epilogue writes dz = (softmax - y) or (p - y) r, scaled and rounded
-// to bf16 (the reference's dzb), into a slab-sized workspace; two plain GEMMs
-// then consume the slab: dh += dz . E_slab (fp32 accumulation across slabs)
-// and dE_slab = dz^T . h. At config 3 a slab is 16384 x 4096 bf16 (134 MB,
-// about the size of L2), so both GEMMs read it mostly from L2.
-#include <cublas_v2.h>
-
+// to bf16 (the reference's dzb), into a slab-sized workspace; head_gemm_tc_kernel
+// then consumes the slab with both products on tcgen05 tensor cores in one
+// persistent launch: dE_slab = dz^T . h and dh += dz . E_slab (fp32
+// accumulation across slabs by TMA reduce-adds). At config 3 a slab is
+// 16384 x 4096 bf16 (134 MB, about the size of L2), so the products read it
+// mostly from L2.
 #include <algorithm>
-#include <mutex>
 #include <string>
 
 #include "algx_common.cuh"
@@ -410,6 +409,249 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
   if (warp == kHeadTma) tmem_dealloc(tmem_base, 512);
 }
 
+// ------------------------------------------------------------------ slab GEMMs
+// The two products of a backward slab on tcgen05 tensor cores, in one
+// persistent launch (one CTA per SM):
+//   problem 0: dE_slab (vc x d) = dz^T . h   (A = dz read MN-major, B = h MN-major, K = N tokens)
+//   problem 1: dh (N x d) (+)= dz . E_slab  (A = dz K-major, B = E_slab MN-major, K = vc columns)
+// Output tiles of 128 x 256 fp32 are handed out by a global counter, the large
+// dE tiles (the whole token reduction) first and the dh tiles after them, so
+// the SMs that finish early take the remaining small tiles. A TMA warp streams
+// 64-wide K chunks of A and B through a 4-stage ring; one thread issues the
+// M=128, N=256, K=16 MMAs into two TMEM accumulators; two groups of four
+// epilogue warps take alternate tiles and move each accumulator out in
+// 32-column boxes (fp32, 128B-swizzled shared memory) with TMA stores, or
+// TMA reduce-adds for dh after the first slab (the fp32 sum across slabs).
+constexpr int kGemmBM = 128, kGemmBN = 256, kGemmStages = 4;
+constexpr int kGemmABytes = kGemmBM * 64 * 2;  // 16 KB
+constexpr int kGemmBBytes = kGemmBN * 64 * 2;  // 32 KB
+constexpr int kGemmStageBytes = kGemmABytes + kGemmBBytes;
+constexpr int kGemmBoxBytes = 128 * 32 * 4;  // epilogue staging box: 128 rows x 32 fp32
+constexpr int kGemmSmem = kGemmStages * kGemmStageBytes + 2 * kGemmBoxBytes + 1024;
+constexpr int kGemmThreads = 320;  // 2 x 4 epilogue warps, TMA warp, MMA warp
+
+struct GemmProblem {
+  int a_mn, b_mn;  // operand read MN-major (MN contiguous in memory) or K-major
+  int add;         // epilogue: 0 = TMA store, 1 = TMA reduce-add
+  int tiles_n;     // 256-column tiles of the output
+  int tiles;       // output tiles
+  int kchunks;     // 64-wide chunks of the reduction
+};
+struct GemmArgs {
+  GemmProblem p[2];
+  int* counter;  // zeroed before the launch
+};
+
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    head_gemm_tc_kernel(const __grid_constant__ CUtensorMap ta0, const __grid_constant__ CUtensorMap tb0,
+                        const __grid_constant__ CUtensorMap tc0, const __grid_constant__ CUtensorMap ta1,
+                        const __grid_constant__ CUtensorMap tb1, const __grid_constant__ CUtensorMap tc1, GemmArgs g,
+                        int* dev_err) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1k(smem_raw);
+  uint8_t* sbox = smem + kGemmStages * kGemmStageBytes;  // two staging boxes, one per epilogue group
+  __shared__ uint64_t full[kGemmStages], empty[kGemmStages], acc_full[2], acc_empty[2];
+  __shared__ uint64_t item_full[4], item_empty[4], issued;
+  __shared__ int item_q[4];
+  __shared__ uint32_t tmem_base;
+  __shared__ int abort_flag;
+  volatile int* abort_v = &abort_flag;
+  volatile int* item_v = item_q;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int total = g.p[0].tiles + g.p[1].tiles;
+  constexpr int kItemConsumers = 1 + 8;  // the MMA thread and the eight epilogue warps
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGemmStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);
+    }
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(&item_full[i], 1);
+      mbar_init(&item_empty[i], kItemConsumers);
+    }
+    mbar_init(&issued, 1);
+    fence_mbar_init();
+    abort_flag = 0;
+  }
+  if (warp == kHeadTma) {
+    tmem_alloc(&tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  // the item queue: the TMA thread takes tiles from the global counter and
+  // publishes them in a 4-slot ring read by the MMA thread and the epilogues
+  auto next_item = [&](int j, bool whole_warp) -> int {
+    const int slot = j & 3;
+    const bool ok = whole_warp ? mbar_wait_warp(&item_full[slot], (j >> 2) & 1, abort_v, dev_err)
+                               : mbar_wait(&item_full[slot], (j >> 2) & 1, abort_v, dev_err);
+    const int it = ok ? item_v[slot] : -1;
+    if (whole_warp) __syncwarp();
+    if (!whole_warp || lane == 0) mbar_arrive(&item_empty[slot]);
+    return it;
+  };
+  auto decode = [&](int it, int& p, int& m0, int& n0) {
+    p = it < g.p[0].tiles ? 0 : 1;
+    const int t = it - (p ? g.p[0].tiles : 0);
+    m0 = (t / g.p[p].tiles_n) * kGemmBM;
+    n0 = (t % g.p[p].tiles_n) * kGemmBN;
+  };
+
+  if (warp == kHeadTma) {
+    if (lane == 0) {
+      prefetch_tmap(&ta0);
+      prefetch_tmap(&tb0);
+      prefetch_tmap(&ta1);
+      prefetch_tmap(&tb1);
+      int it_stage = 0;
+      int last_stage_it[kGemmStages] = {-1, -1, -1, -1};
+      bool ok = true;
+      for (int j = 0; ok; ++j) {
+        const int slot = j & 3;
+        if (j >= 4 && !mbar_wait(&item_empty[slot], ((j >> 2) - 1) & 1, abort_v, dev_err)) break;
+        int it = atomicAdd(g.counter, 1);
+        if (it >= total) it = -1;
+        item_v[slot] = it;
+        mbar_arrive(&item_full[slot]);  // release: the tile index is visible to the waiters
+        if (it < 0) break;
+        int p, m0, n0;
+        decode(it, p, m0, n0);
+        const GemmProblem& P = g.p[p];
+        const CUtensorMap* tA = p ? &ta1 : &ta0;
+        const CUtensorMap* tB = p ? &tb1 : &tb0;
+        for (int kc = 0; kc < P.kchunks; ++kc, ++it_stage) {
+          const int s = it_stage % kGemmStages;
+          if (it_stage >= kGemmStages &&
+              !mbar_wait(&empty[s], ((it_stage / kGemmStages) - 1) & 1, abort_v, dev_err)) {
+            ok = false;
+            break;
+          }
+          uint8_t* sa = smem + s * kGemmStageBytes;
+          uint8_t* sb = sa + kGemmABytes;
+          mbar_expect_tx(&full[s], kGemmStageBytes);
+          const int k0 = kc * 64;
+          if (P.a_mn) {  // [K][M] in memory: two 64-wide M chunks of 64 K rows
+            tma_load_2d(sa, tA, &full[s], m0, k0);
+            tma_load_2d(sa + kGemmABytes / 2, tA, &full[s], m0 + 64, k0);
+          } else {  // [M][K]: one box of 128 rows x 64 K
+            tma_load_2d(sa, tA, &full[s], k0, m0);
+          }
+          if (P.b_mn) {  // [K][N]: four 64-wide N chunks of 64 K rows
+#pragma unroll
+            for (int c = 0; c < 4; ++c) tma_load_2d(sb + c * (kGemmBBytes / 4), tB, &full[s], n0 + 64 * c, k0);
+          } else {
+            tma_load_2d(sb, tB, &full[s], k0, n0);
+          }
+          last_stage_it[s] = it_stage;
+        }
+      }
+      if (*abort_v)
+        for (int s = 0; s < kGemmStages; ++s)
+          if (last_stage_it[s] >= 0) {
+            volatile int quiet = 0;
+            mbar_wait(&full[s], (last_stage_it[s] / kGemmStages) & 1, &quiet, nullptr);
+          }
+    }
+  } else if (warp == kHeadTma + 1) {
+    if (lane == 0) {
+      const uint32_t s0 = smem_u32(smem);
+      int it_stage = 0;
+      bool ok = true;
+      for (int j = 0; ok; ++j) {
+        const int it = next_item(j, false);
+        if (it < 0) break;
+        int p, m0, n0;
+        decode(it, p, m0, n0);
+        const GemmProblem& P = g.p[p];
+        const uint32_t id = idesc_bf16_f32(kGemmBM, kGemmBN, P.a_mn, P.b_mn);
+        const int buf = j & 1, use = j >> 1;
+        if (use > 0 && !mbar_wait(&acc_empty[buf], (use - 1) & 1, abort_v, dev_err)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem_base + buf * kGemmBN;
+        for (int kc = 0; kc < P.kchunks; ++kc, ++it_stage) {
+          const int s = it_stage % kGemmStages;
+          if (!mbar_wait(&full[s], (it_stage / kGemmStages) & 1, abort_v, dev_err)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = s0 + s * kGemmStageBytes, sb = sa + kGemmABytes;
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint64_t ad = P.a_mn ? desc_sw128(sa + k * 2048, kGemmABytes / 2, 1024) : desc_sw128(sa + k * 32, 16, 1024);
+            const uint64_t bd = P.b_mn ? desc_sw128(sb + k * 2048, kGemmBBytes / 4, 1024) : desc_sw128(sb + k * 32, 16, 1024);
+            mma_ss(acc, ad, bd, id, (kc > 0 || k > 0));
+          }
+          mma_commit(&empty[s]);
+        }
+        if (ok) mma_commit(&acc_full[buf]);
+      }
+      mma_commit(&issued);  // settle: every product of this thread completed before TMEM is freed
+      volatile int quiet = 0;
+      mbar_wait(&issued, 0, &quiet, dev_err);
+    }
+  } else {
+    // epilogue group eg = warp / 4 takes the items j with j % 2 == eg; thread r owns row r
+    const int eg = warp >> 2;
+    const int r = (warp & 3) * 32 + lane;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    uint8_t* box = sbox + eg * kGemmBoxBytes;
+    const bool issuer = (warp & 3) == 0 && lane == 0;
+    for (int j = 0;; ++j) {
+      const int it = next_item(j, true);
+      if (it < 0) break;
+      if ((j & 1) != eg) continue;
+      int p, m0, n0;
+      decode(it, p, m0, n0);
+      const CUtensorMap* tC = p ? &tc1 : &tc0;
+      const bool add = g.p[p].add != 0;
+      const int use = j >> 1;
+      if (!mbar_wait_warp(&acc_full[eg], use & 1, abort_v, dev_err)) break;
+      tc_fence_after();
+      const uint32_t acc = tmem_base + eg * kGemmBN + lane_off;
+#pragma unroll 1
+      for (int c = 0; c < kGemmBN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(acc + 32 * c, v);
+        if (c == kGemmBN / 32 - 1) {  // the accumulator is read: the next tile may overwrite it
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[eg]);
+        }
+        if (issuer) bulk_wait_group_read0();  // the previous box has been read by its TMA
+        named_bar_sync(1 + eg, 128);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          *reinterpret_cast<uint4*>(box + r * 128 + ((u ^ (r & 7)) << 4)) =
+              make_uint4(v[4 * u], v[4 * u + 1], v[4 * u + 2], v[4 * u + 3]);
+        fence_proxy_async_smem();
+        named_bar_sync(1 + eg, 128);
+        if (issuer) {
+          if (add)
+            tma_reduce_add_2d(tC, box, n0 + 32 * c, m0);
+          else
+            tma_store_2d(tC, box, n0 + 32 * c, m0);
+          bulk_commit_group();
+        }
+      }
+    }
+    if (issuer) bulk_wait_group0();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kHeadTma) tmem_dealloc(tmem_base, 512);
+}
+
 __global__ void f32_to_bf16_kernel(const float4* __restrict__ in, uint2* __restrict__ out, int64_t n4) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
     const float4 v = in[i];
@@ -550,30 +792,18 @@ int64_t slab_cols(int64_t V) {
   return std::min<int64_t>(kSlabCols, vt);
 }
 
-// One cuBLAS handle per device, created on first use (the only allocation
-// the library makes for the head backward besides the caller's workspace).
-std::mutex g_blas_mu;
-cublasHandle_t g_blas[64] = {};
-int blas_handle(cublasHandle_t* out) {
-  int dev = 0;
+int launch_gemm(const CUtensorMap (&maps)[6], const GemmArgs& a, cudaStream_t st) {
+  int dev = 0, sms = 0;
   ALGX_CUDA(cudaGetDevice(&dev));
-  ALGX_REQUIRE(dev >= 0 && dev < 64, "head_bwd: device index out of range");
-  std::lock_guard<std::mutex> lock(g_blas_mu);
-  if (!g_blas[dev]) {
-    cublasHandle_t hnd = nullptr;
-    if (cublasCreate(&hnd) != CUBLAS_STATUS_SUCCESS) return fail(ALGX_ERR_CUDA, "cublasCreate failed");
-    g_blas[dev] = hnd;
-  }
-  *out = g_blas[dev];
+  ALGX_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+  const int total = a.p[0].tiles + a.p[1].tiles;
+  const unsigned grid = (unsigned)std::max(1, std::min(total, sms));  // persistent: one CTA per SM
+  ALGX_CUDA(cudaFuncSetAttribute(head_gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
+  head_gemm_tc_kernel<<<grid, kGemmThreads, kGemmSmem, st>>>(maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], a,
+                                                             device_error_word());
+  ALGX_LAUNCHED("head_gemm_tc launch");
   return ALGX_OK;
 }
-
-#define ALGX_BLAS(call)                                                                        \
-  do {                                                                                        \
-    cublasStatus_t _st = (call);                                                              \
-    if (_st != CUBLAS_STATUS_SUCCESS)                                                         \
-      return fail(ALGX_ERR_CUDA, std::string(#call) + " failed (" + std::to_string((int)_st) + ")"); \
-  } while (0)
 
 }  // namespace
 }  // namespace algx
@@ -634,7 +864,7 @@ size_t algx_head_bwd_workspace_size(int64_t N, int64_t d, int64_t V, int32_t dh_
   if (N < 1 || d < 1 || V < 1) return 0;
   size_t bytes = (size_t)N * (size_t)slab_cols(V) * 2;               // dz slab, bf16
   if (dh_dtype == ALGX_BF16) bytes += (size_t)N * (size_t)d * 4;     // fp32 dh accumulator
-  return bytes;
+  return bytes + 256;                                                // the GEMM's tile counter
 }
 
 int algx_head_bwd(const algx_head_config* cfg, const void* h, const void* embed, const int32_t* targets,
@@ -652,15 +882,14 @@ int algx_head_bwd(const algx_head_config* cfg, const void* h, const void* embed,
   if (int s = make_tmap_2d(&te, embed, ALGX_BF16, (uint64_t)d, (uint64_t)V, (uint64_t)d * 2, 64, kFwdNT, true))
     return s;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cublasHandle_t blas;
-  if (int s = blas_handle(&blas)) return s;
-  ALGX_BLAS(cublasSetStream(blas, st));
   __nv_bfloat16* dz = static_cast<__nv_bfloat16*>(workspace);
   float* dh_acc = dh_dtype == ALGX_F32 ? static_cast<float*>(dh)
                                        : reinterpret_cast<float*>(static_cast<char*>(workspace) + (size_t)N * vs * 2);
+  int* counter = reinterpret_cast<int*>(static_cast<char*>(workspace) + algx_head_bwd_workspace_size(N, d, V, dh_dtype) -
+                                        256);
   const int tb = (int)((N + 127) / 128);
   const int ntiles_total = (int)((V + kFwdNT - 1) / kFwdNT);
-  const float one = 1.f, zero = 0.f;
+  const int tiles_n = (int)((d + kGemmBN - 1) / kGemmBN);
   for (int64_t c0 = 0; c0 < V; c0 += vs) {
     const int64_t vc = std::min<int64_t>(vs, V - c0);  // valid columns of this slab
     DzArgs a{*cfg, targets, stat, scale, (int)N, (int)d, (int)V, (int)vocab_offset, (int)(c0 / kFwdNT), 0, 0, (int)vs};
@@ -669,17 +898,26 @@ int algx_head_bwd(const algx_head_config* cfg, const void* h, const void* embed,
     int s = cfg->kind == ALGX_HEAD_CE ? launch_dz_k<ALGX_HEAD_CE>(th, te, a, dz, st)
                                       : launch_dz_k<ALGX_HEAD_ALG_CE>(th, te, a, dz, st);
     if (s) return s;
-    // dh (row-major N x d) += dz (N x vc) . E[c0 : c0 + vc] (vc x d); column-major view:
-    // dh^T (d x N) = E_slab^T (d x vc) . dz^T (vc x N)
+    // problem 0: dE[c0 : c0 + vc] (vc x d) = dz^T . h; problem 1: dh (N x d) (+)= dz . E[c0 : c0 + vc]
+    CUtensorMap maps[6];
     const __nv_bfloat16* eslab = static_cast<const __nv_bfloat16*>(embed) + (size_t)c0 * d;
-    ALGX_BLAS(cublasGemmEx(blas, CUBLAS_OP_N, CUBLAS_OP_N, (int)d, (int)N, (int)vc, &one, eslab, CUDA_R_16BF, (int)d,
-                           dz, CUDA_R_16BF, (int)vs, c0 == 0 ? &zero : &one, dh_acc, CUDA_R_32F, (int)d,
-                           CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT));
-    // dE[c0 : c0 + vc] (row-major vc x d) = dz^T . h; column-major view:
-    // dE_slab^T (d x vc) = h^T (d x N) . dz (N x vc)
-    ALGX_BLAS(cublasGemmEx(blas, CUBLAS_OP_N, CUBLAS_OP_T, (int)d, (int)vc, (int)N, &one, h, CUDA_R_16BF, (int)d, dz,
-                           CUDA_R_16BF, (int)vs, &zero, dembed + (size_t)c0 * d, CUDA_R_32F, (int)d,
-                           CUBLAS_COMPUTE_32F, CUBLAS_GEMM_DEFAULT));
+    if ((s = make_tmap_2d(&maps[0], dz, ALGX_BF16, (uint64_t)vc, (uint64_t)N, (uint64_t)vs * 2, 64, 64, true))) return s;
+    if ((s = make_tmap_2d(&maps[1], h, ALGX_BF16, (uint64_t)d, (uint64_t)N, (uint64_t)d * 2, 64, 64, true))) return s;
+    if ((s = make_tmap_2d(&maps[2], dembed + (size_t)c0 * d, ALGX_F32, (uint64_t)d, (uint64_t)vc, (uint64_t)d * 4, 32,
+                          kGemmBM, true)))
+      return s;
+    if ((s = make_tmap_2d(&maps[3], dz, ALGX_BF16, (uint64_t)vc, (uint64_t)N, (uint64_t)vs * 2, 64, kGemmBM, true)))
+      return s;
+    if ((s = make_tmap_2d(&maps[4], eslab, ALGX_BF16, (uint64_t)d, (uint64_t)vc, (uint64_t)d * 2, 64, 64, true)))
+      return s;
+    if ((s = make_tmap_2d(&maps[5], dh_acc, ALGX_F32, (uint64_t)d, (uint64_t)N, (uint64_t)d * 4, 32, kGemmBM, true)))
+      return s;
+    GemmArgs ga;
+    ga.p[0] = GemmProblem{1, 1, 0, tiles_n, (int)((vc + kGemmBM - 1) / kGemmBM) * tiles_n, (int)((N + 63) / 64)};
+    ga.p[1] = GemmProblem{0, 1, c0 > 0 ? 1 : 0, tiles_n, tb * tiles_n, (int)((vc + 63) / 64)};
+    ga.counter = counter;
+    ALGX_CUDA(cudaMemsetAsync(counter, 0, sizeof(int), st));
+    if ((s = launch_gemm(maps, ga, st))) return s;
   }
   if (dh_dtype == ALGX_BF16) {
     const int64_t n4 = N * d / 4;

@@ -215,8 +215,9 @@ ALGX_API int algx_head_finalize(const algx_head_config* cfg, const int32_t* targ
                                 void* stream);
 
 /* Workspace bytes of algx_head_bwd: one bf16 dz slab of N x min(4096, V
- * rounded up to 256) plus, when dh is bf16, an fp32 dh accumulator. The
- * reference writes dz for the whole vocabulary (fused_head.py:194-216). */
+ * rounded up to 256), when dh is bf16 an fp32 dh accumulator, and 256 bytes
+ * for the slab GEMM's tile counter. The reference writes dz for the whole
+ * vocabulary (fused_head.py:194-216). */
 ALGX_API size_t algx_head_bwd_workspace_size(int64_t N, int64_t d, int64_t V, int32_t dh_dtype);
 
 /* dh (N, d) in dh_dtype (partial over this rank's vocabulary rows) and
@@ -224,8 +225,8 @@ ALGX_API size_t algx_head_bwd_workspace_size(int64_t N, int64_t d, int64_t V, in
  * memory. The logits are recomputed one vocabulary slab of at most 4096
  * columns at a time (never in full): a tcgen05 kernel writes the slab's
  * bf16 dz = scale * (softmax - y) or scale * (p - y) r into the workspace,
- * then cuBLAS computes dh += dz . E_slab and dE_slab = dz^T . h (fp32
- * accumulation). Replaces kernels/fused_head.py:120-156, 194-216
+ * then one persistent tcgen05 GEMM launch computes dE_slab = dz^T . h and
+ * dh += dz . E_slab (fp32 accumulation). Replaces kernels/fused_head.py:120-156, 194-216
  * (`_bwd_kernel`, `_backward`, including the XLA dE = dz^T h product). */
 ALGX_API int algx_head_bwd(const algx_head_config* cfg, const void* h, const void* embed,
                            const int32_t* targets, const float* stat, const float* scale, void* dh,
