@@ -9,7 +9,8 @@
 * The fused head is vocabulary-parallel: rank r holds a
   contiguous slice of the embedding rows. The forward computes per-token
   (max, sum, target logit) over the local slice, then all-reduces them
-  (MAX then SUM for "ce"; SUM only for the additive "alg_ce"); the backward
+  (one all-gather and a local combine for "ce"; a SUM for the additive
+  "alg_ce"); the backward
   computes the local dE slice with no communication and all-reduces the
   partial dh. Collectives go through NCCL on GPU (gloo in the CPU tests).
 """
@@ -38,12 +39,18 @@ def combine_vocab_stats(mlz: torch.Tensor, kind: str, group=None) -> torch.Tenso
     "ce": m_g = max_r m_r, l = sum_r l_r exp(m_r - m_g); "alg_ce": l = sum_r l_r.
     zt is a sum (only the rank owning the target column contributes).
     """
-    m, l = mlz[0], mlz[1]
     if kind == "ce":
-        mg = m.clone()
-        dist.all_reduce(mg, op=dist.ReduceOp.MAX, group=group)
-        l.mul_(torch.exp(m - mg))
-        m.copy_(mg)
+        # one collective: every rank gathers all ranks' (m, l, zt) and combines
+        # them in the same fixed order, so all ranks hold identical statistics
+        world = dist.get_world_size(group)
+        flat = torch.empty((world * mlz.shape[0],) + tuple(mlz.shape[1:]), dtype=mlz.dtype, device=mlz.device)
+        dist.all_gather_into_tensor(flat, mlz.contiguous(), group=group)  # rank blocks stacked along dim 0
+        parts = flat.view((world,) + tuple(mlz.shape))
+        mg = parts[:, 0].amax(dim=0)
+        mlz[1].copy_(torch.sum(parts[:, 1] * torch.exp(parts[:, 0] - mg), dim=0))
+        mlz[2].copy_(torch.sum(parts[:, 2], dim=0))
+        mlz[0].copy_(mg)
+        return mlz
     dist.all_reduce(mlz[1:], op=dist.ReduceOp.SUM, group=group)
     return mlz
 
