@@ -136,6 +136,7 @@ constexpr int kStagesB = 6;
 constexpr int kConsumerWarpsB = 16;
 constexpr int kThreadsB = (kConsumerWarpsB + 1) * 32;
 constexpr int kSmemB = 2 * kStagesB * kChunkBytesB;
+constexpr int kMaxBlocksB = 256;  // grid cap (one CTA per SM up to this many SMs); sizes the workspace
 
 template <typename T>
 __global__ void __launch_bounds__(kThreadsB, 1)
@@ -340,8 +341,9 @@ int algx_qknorm_fwd(const void* x, const float* gain, void* y, int64_t rows, int
 
 size_t algx_qknorm_bwd_workspace_size(int64_t rows, int64_t dim) {
   (void)dim;
-  const int g = grid_for<float>(rows) > grid_for<__nv_bfloat16>(rows) ? grid_for<float>(rows)
-                                                                      : grid_for<__nv_bfloat16>(rows);
+  // the staged kernel's grid: one CTA per chunk (fp32 chunks hold the fewest rows), at most kMaxBlocksB
+  const int64_t chunk_rows = kChunkBytesB / (kDim * (int64_t)sizeof(float));
+  const int64_t g = std::max<int64_t>(1, std::min<int64_t>((rows + chunk_rows - 1) / chunk_rows, kMaxBlocksB));
   return (size_t)g * kDim * sizeof(float);
 }
 
@@ -361,7 +363,8 @@ int algx_qknorm_bwd(const void* x, const float* gain, const void* dy, void* dx, 
   ALGX_CUDA(cudaGetDevice(&dev));
   ALGX_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int64_t chunk_rows = kChunkBytesB / (kDim * (dtype == ALGX_BF16 ? 2 : 4));
-  const int grid = (int)std::min<int64_t>((rows + chunk_rows - 1) / chunk_rows, sms);  // one CTA per SM
+  const int grid = (int)std::min<int64_t>(std::min<int64_t>((rows + chunk_rows - 1) / chunk_rows, sms),
+                                          kMaxBlocksB);  // one CTA per SM
   ALGX_REQUIRE(workspace && workspace_bytes >= (size_t)grid * kDim * sizeof(float),
                "qknorm_bwd: workspace too small (see algx_qknorm_bwd_workspace_size)");
   float* partial = static_cast<float*>(workspace);

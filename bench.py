@@ -216,7 +216,7 @@ def time_cuda(fn, steps, warmup, stream, sync_all, max_over_ranks):
     return max_over_ranks(a.elapsed_time(b)) / steps
 
 
-def secondary(dev, rank, world, stream, sync_all, max_over_ranks, steps=5, warmup=3):
+def secondary(dev, rank, world, stream, sync_all, max_over_ranks, steps=5, warmup=3, lines=None):
     """The other headline lines: fused head tok/s (d=768, ce and alg_ce n=8 c=2;
     vocabulary-parallel over the ranks when N > 1) and the 350M shapes (config 4)."""
     from algx.kernels.flash import qknorm_flash_attention
@@ -261,40 +261,42 @@ def secondary(dev, rank, world, stream, sync_all, max_over_ranks, steps=5, warmu
                 "config": f"N={HEAD_N} d={d} V={HEAD_V} bf16, 5% labels = ignore_index -100, fwd+bwd",
                 "scaling": "strong (vocabulary rows split over the ranks)" if world > 1 else "single GPU"}
 
-    trace("secondary: qk norm cfg2")
-    out["qknorm_cfg2"] = qknorm_line(dev, gen, world, stream, sync_all, max_over_ranks)
-    trace("secondary: head cfg3 ce")
-    out["head_cfg3_ce"] = head_line(768, "ce", 16, 16.0)
-    trace("secondary: head cfg3 alg_ce")
-    out["head_cfg3_alg_ce"] = head_line(768, "alg_ce", 8, 2.0)
-    trace("secondary: head cfg4 ce")
-    out["head_cfg4_ce"] = head_line(1024, "ce", 16, 16.0)
-    trace("secondary: attention cfg4")
-    # config 4 attention: B=8, H=16 per GPU (weak scaling like config 2)
-    B4, H4 = 8, 16
-    q, k, v, do = (torch.randn((B4, H4, T, D), device=dev, generator=gen).to(torch.bfloat16) for _ in range(4))
-    gq = 1 + 0.02 * torch.randn(D, device=dev, generator=gen)
-    gk = 1 + 0.02 * torch.randn(D, device=dev, generator=gen)
-    leaves = [x.requires_grad_(True) for x in (q, k, v, gq, gk)]
+    def attn_cfg4_line():
+        # config 4 attention: B=8, H=16 per GPU (weak scaling like config 2)
+        B4, H4 = 8, 16
+        q, k, v, do = (torch.randn((B4, H4, T, D), device=dev, generator=gen).to(torch.bfloat16) for _ in range(4))
+        gq = 1 + 0.02 * torch.randn(D, device=dev, generator=gen)
+        gk = 1 + 0.02 * torch.randn(D, device=dev, generator=gen)
+        leaves = [x.requires_grad_(True) for x in (q, k, v, gq, gk)]
 
-    def attn_step():
-        o = qknorm_flash_attention(leaves[0], leaves[1], leaves[2], leaves[3], leaves[4], eps=EPS, kind="asinh",
-                                   n=N_POW, c=C_SCALE, range_guard=True)
-        o.backward(do)
-        for x in leaves:
-            x.grad = None
+        def attn_step():
+            o = qknorm_flash_attention(leaves[0], leaves[1], leaves[2], leaves[3], leaves[4], eps=EPS, kind="asinh",
+                                       n=N_POW, c=C_SCALE, range_guard=True)
+            o.backward(do)
+            for x in leaves:
+                x.grad = None
 
-    ms = time_cuda(attn_step, steps, warmup, stream, sync_all, max_over_ranks)
-    flop = 3.5 * 4 * B4 * H4 * T * T * D / 2
-    out["attn_cfg4"] = {"metric": "asinh-attn fwd+bwd TFLOP/s", "value": world * flop / (ms / 1e3) / 1e12,
-                        "unit": "TFLOP/s", "ms_per_step": ms,
-                        "config": f"B={B4} H={H4} S={T} D={D} bf16 per GPU, QK-norm + guarded asinh n=16 c=8, "
-                                  "public API (autograd)", "scaling": "weak"}
-    del q, k, v, do, gq, gk, leaves
-    trace("secondary: train cfg5")
-    out["train_cfg5"] = train_line(dev, rank, world, stream, sync_all, max_over_ranks)
-    trace("secondary: train cfg5, algebraic preset")
-    out["train_cfg5_algebraic"] = train_line(dev, rank, world, stream, sync_all, max_over_ranks, preset="algebraic")
+        ms = time_cuda(attn_step, steps, warmup, stream, sync_all, max_over_ranks)
+        flop = 3.5 * 4 * B4 * H4 * T * T * D / 2
+        return {"metric": "asinh-attn fwd+bwd TFLOP/s", "value": world * flop / (ms / 1e3) / 1e12,
+                "unit": "TFLOP/s", "ms_per_step": ms,
+                "config": f"B={B4} H={H4} S={T} D={D} bf16 per GPU, QK-norm + guarded asinh n=16 c=8, "
+                          "public API (autograd)", "scaling": "weak"}
+
+    table = [
+        ("qknorm_cfg2", lambda: qknorm_line(dev, gen, world, stream, sync_all, max_over_ranks)),
+        ("head_cfg3_ce", lambda: head_line(768, "ce", 16, 16.0)),
+        ("head_cfg3_alg_ce", lambda: head_line(768, "alg_ce", 8, 2.0)),
+        ("head_cfg4_ce", lambda: head_line(1024, "ce", 16, 16.0)),
+        ("attn_cfg4", attn_cfg4_line),
+        ("train_cfg5", lambda: train_line(dev, rank, world, stream, sync_all, max_over_ranks)),
+        ("train_cfg5_algebraic",
+         lambda: train_line(dev, rank, world, stream, sync_all, max_over_ranks, preset="algebraic")),
+    ]
+    for name, fn in table:
+        if lines is None or name in lines:
+            trace(f"secondary: {name}")
+            out[name] = fn()
     return out
 
 
@@ -545,7 +547,8 @@ def run_algx(args, rank, world, local_rank):
     if clocks:
         clocks.mark(w2, w3)
     e2e_ms = max_over_ranks(ev2.elapsed_time(ev3))
-    extra = secondary(dev, rank, world, stream, sync_all, max_over_ranks) if not args.no_secondary else None
+    lines = None if not args.lines else set(args.lines.split(","))
+    extra = secondary(dev, rank, world, stream, sync_all, max_over_ranks, lines=lines) if not args.no_secondary else None
     trace("done")
     dev_err = L.device_error()
     clk = clocks.stop() if clocks else None
@@ -601,6 +604,8 @@ def main():
     ap.add_argument("--impl", choices=["algx", "reference"], default="algx")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true", help="skip the head and config 4 lines")
+    ap.add_argument("--lines", default="", help="comma-separated names of the secondary lines to run (default: all); "
+                                                "for profiling one of them")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
