@@ -95,6 +95,14 @@ __device__ __forceinline__ float rsqrt_fast(float x) {
   return y;
 }
 
+// 1/x on the MUFU pipe (approximate reciprocal, flushing denormals; the
+// arguments here are |x| + sqrt(1 + x^2) >= 1).
+__device__ __forceinline__ float rcp_fast(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // rho(x) = x + sqrt(1+x^2): fast form (kernels/flash.py:83-88) and stable
 // form with the reciprocal for x < 0 (kernels/flash.py:76-80). Both return
 // r = 1/sqrt(1+x^2) through the out-parameter.

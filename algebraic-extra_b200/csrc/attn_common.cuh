@@ -52,4 +52,12 @@ __host__ __device__ inline Eff resolve_variant(const algx_attn_config& c, const 
   return e;
 }
 
+// Whether the tcgen05 backward (when it was launched: bf16, D = 64, T % 128
+// == 0, asinh fast path) produced this branch's gradients in its fp32 dQ
+// accumulator: the unshifted branch always, the shifted one under the range
+// guard (kernels/flash.py:834-856), where both instantiations are launched.
+__host__ __device__ inline bool tc_bwd_covers(const algx_attn_config& c, const Eff& e) {
+  return e.branch == BR_UNSHIFTED || (e.branch == BR_SHIFTED && c.mode == ALGX_MODE_GUARDED);
+}
+
 }  // namespace algx

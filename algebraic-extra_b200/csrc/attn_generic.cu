@@ -375,8 +375,8 @@ __global__ void __launch_bounds__(256) attn_di_kernel(algx_attn_config cfg, cons
   const Eff e = resolve_variant(cfg, guard);
   // The fast backward's fp32 dQ accumulator (zero_acc, rows of 64) and its
   // 256-byte counter area (zero_tail) are zeroed here, alongside the o / dO
-  // reads, instead of by a separate memset; the shifted branch never reads
-  // the accumulator, the counters are used in both branches.
+  // reads, instead of by a separate memset (in both branches: under the range
+  // guard the shifted branch's backward also runs on the tcgen05 path).
   if (zero_tail && blockIdx.x == 0 && blockIdx.y == 0 && threadIdx.x < 64) zero_tail[threadIdx.x] = 0;
   const int bh = blockIdx.y, h = bh % H;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -410,6 +410,8 @@ __global__ void __launch_bounds__(256) attn_di_kernel(algx_attn_config cfg, cons
 #pragma unroll
       for (int x = 16; x > 0; x >>= 1) s += __shfl_xor_sync(0xffffffffu, s, x);
       if (lane == 0) accumulate(row, s);
+      // the tcgen05 backward of the shifted branch accumulates dQ here as well
+      if (zero_acc) *reinterpret_cast<float2*>(zero_acc + off) = make_float2(0.f, 0.f);
     }
   } else {
     // 128-bit row loads, Vec<T>::TPR threads per row; all of a thread's rows
@@ -695,8 +697,8 @@ int check_attn(const algx_attn_config* cfg, int64_t B, int64_t H, int64_t T, int
 // ------------------------------------------------------------------ fused QK-norm backward
 // Backward of the QK RMS norm (kernels/qk_norm.py:45-56) applied to the
 // attention's dq and dk, in place: dq_x holds dq (bf16 from the generic
-// kernels) or, when the fast path ran the unshifted branch, dq is read from
-// the fp32 accumulator as bf16(acc * n * scale), the rounding of
+// kernels) or, when the fast path ran the backward (tc_bwd_covers), dq is
+// read from the fp32 accumulator as bf16(acc * n * scale), the rounding of
 // dq_finish_kernel; dk_x holds dk. Per row the arithmetic is that of
 // qknorm_bwd_kernel, so dx is bit-identical to the composed calls. dgain:
 // per-CTA column partials, then the last CTA to finish sums them in a fixed
@@ -814,7 +816,7 @@ __global__ void __launch_bounds__(kEpiThreads) qknorm_attn_bwd_kernel(
   __shared__ float red[kEpiThreads / 32 * V::RPW][2 * kD];  // per row slot of a warp: q and k column sums
   __shared__ float fin[kEpiThreads / (2 * kD)][2 * kD];
   __shared__ bool last;
-  const bool use_acc = fast && resolve_variant(cfg, guard).branch == BR_UNSHIFTED;
+  const bool use_acc = fast && tc_bwd_covers(cfg, resolve_variant(cfg, guard));
   float pq[V::N], pk[V::N];
 #pragma unroll
   for (int i = 0; i < V::N; ++i) pq[i] = pk[i] = 0.f;
@@ -1042,8 +1044,8 @@ size_t algx_attn_bwd_workspace_size(int64_t B, int64_t H, int64_t T, int64_t D) 
 }
 
 // The attention backward launch group. With finish_dq false and the fast
-// path taken (*fast), dq holds the generic kernels' result only if the guard
-// chose the shifted branch; otherwise the fp32 accumulator holds it unscaled.
+// path taken (*fast), the fp32 accumulator holds dq unscaled whenever
+// tc_bwd_covers(cfg, branch); otherwise dq holds the generic kernels' result.
 static int attn_bwd_core(const algx_attn_config* cfg, const void* q_scaled, const void* k, const void* v,
                          const float* sink, const float* guard, const void* o, const float* o_precise,
                          const float* stat, const void* dout, void* dq, void* dk, void* dv, float* dsink, int64_t B,
@@ -1081,7 +1083,9 @@ static int attn_bwd_core(const algx_attn_config* cfg, const void* q_scaled, cons
     return s;
   *fast_out = fast;
   if (fast) {
-    if (cfg->mode == ALGX_MODE_CLIPPED) return ALGX_OK;  // see algx_attn_fwd
+    // the tcgen05 kernels cover the clipped link, and under the range guard
+    // both branches (tc_bwd_covers): no CUDA-core stand-by is needed
+    if (cfg->mode == ALGX_MODE_CLIPPED || cfg->mode == ALGX_MODE_GUARDED) return ALGX_OK;
     mask = 1 << BR_SHIFTED | 1 << BR_SOFTMAX;
   }
   const unsigned ggrid = generic_grid(B * H, T, fast);

@@ -100,8 +100,10 @@ __device__ __forceinline__ float weights_chunk(const uint32_t (&sv)[32], uint32_
 }
 
 // p and ds (without the slope n) of C scores of one key row against C query
-// columns (kernels/flash.py:333-361), packed to bf16 pairs.
-template <int N, bool CLIP, bool INV, bool DIAG, int C>
+// columns (kernels/flash.py:333-361), packed to bf16 pairs. EXACT: the stable
+// rho of the shifted branch, 1 / (|x| + sqrt(1 + x^2)) for x < 0
+// (kernels/flash.py:76-80), with the reciprocal on the MUFU pipe.
+template <int N, bool CLIP, bool INV, bool DIAG, int C, bool EXACT = false>
 __device__ __forceinline__ void grads_chunk(const uint32_t (&sv)[C], const uint32_t (&pv)[C],
                                             const float* __restrict__ st, const float* __restrict__ dd,
                                             uint32_t (&pk)[C / 2], uint32_t (&dk)[C / 2], float clamp, int col0,
@@ -122,7 +124,14 @@ __device__ __forceinline__ void grads_chunk(const uint32_t (&sv)[C], const uint3
       }
       const float2 rad = fma2(x, x, one);
       const float2 rr = make_float2(rsqrt_fast(rad.x), rsqrt_fast(rad.y));
-      const float2 rho = fma2(rad, rr, x);
+      float2 rho;
+      if constexpr (EXACT) {
+        const float2 t = fma2(rad, rr, make_float2(fabsf(x.x), fabsf(x.y)));
+        rho.x = x.x >= 0.f ? t.x : rcp_fast(t.x);
+        rho.y = x.y >= 0.f ? t.y : rcp_fast(t.y);
+      } else {
+        rho = fma2(rad, rr, x);
+      }
       const float2 stc = h ? make_float2(s4.z, s4.w) : make_float2(s4.x, s4.y);
       const float2 dic = h ? make_float2(d4.z, d4.w) : make_float2(d4.x, d4.y);
       float2 p = INV ? mul2(ipow2_t<N>(rho), stc) : ipow2_t<N>(mul2(rho, stc));
@@ -407,7 +416,11 @@ __device__ __forceinline__ BwdItem bwd_item(int it, int BH, int nq) {
 // query tiles (each two 128B-swizzled 64-column halves side by side: exactly
 // the MN-major A operand of dQ_tile = dS K), and two 16 KB fp32 staging
 // boxes for the dQ reduce-adds.
-template <int N, bool CLIP, bool INV_STAT>
+// SHIFTED: the instantiation for the range guard's shifted (high) branch:
+// exact rho, root statistic (p = (rho * stat)^N, kernels/flash.py:246-259),
+// no clamp; it runs only when the guard chose that branch, the unshifted
+// instantiation only when it did not.
+template <int N, bool CLIP, bool INV_STAT, bool SHIFTED = false>
 __global__ void __launch_bounds__(kBwdThreads, 1)
     attn_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                        const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
@@ -417,7 +430,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
                        int BH, int T, int* dev_err) {
   pdl_wait();  // launched as a dependent of the di pass, which writes di and zeroes the accumulator
   const Eff e = resolve_variant(cfg, guard);
-  if (e.branch != BR_UNSHIFTED) return;
+  if (e.branch != (SHIFTED ? BR_SHIFTED : BR_UNSHIFTED)) return;
   pdl_trigger();  // the fallback kernels may be scheduled behind this grid
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -713,9 +726,9 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
           const float* st = sStat + hs * 64 + 32 * hc + 16 * jj;
           const float* dd = sDi + hs * 64 + 32 * hc + 16 * jj;
           if (ii == 0)
-            grads_chunk<N, CLIP, INV_STAT, true, 16>(sv, pv, st, dd, pk[jj], dk2[jj], cfg.clamp, col0, r);
+            grads_chunk<N, CLIP, INV_STAT, true, 16, SHIFTED>(sv, pv, st, dd, pk[jj], dk2[jj], cfg.clamp, col0, r);
           else
-            grads_chunk<N, CLIP, INV_STAT, false, 16>(sv, pv, st, dd, pk[jj], dk2[jj], cfg.clamp, col0, r);
+            grads_chunk<N, CLIP, INV_STAT, false, 16, SHIFTED>(sv, pv, st, dd, pk[jj], dk2[jj], cfg.clamp, col0, r);
         }
         // P^T of sub-tile Ug - 2 must have been consumed by its dV product,
         // dS^T of query tile Ig - 2 by its dQ product.
@@ -883,13 +896,14 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
   if (warp == kBwdProducer) tmem_dealloc(tmem_base, 512);
 }
 
-// dq = bf16(acc * n * scale), only when the fast path ran (unshifted branch).
+// dq = bf16(acc * n * scale), for the branch a tcgen05 backward ran: the
+// unshifted one, and with the range guard the shifted one as well.
 __global__ void dq_finish_kernel(algx_attn_config cfg, const float* __restrict__ guard,
                                  const float4* __restrict__ acc, __nv_bfloat16* __restrict__ dq, int64_t n4) {
   pdl_wait();  // launched as a dependent of the fast backward
   pdl_trigger();  // the fallback kernels may be scheduled behind this grid
   const Eff e = resolve_variant(cfg, guard);
-  if (e.branch != BR_UNSHIFTED) return;
+  if (!tc_bwd_covers(cfg, e)) return;
   const float f = (float)cfg.n * cfg.scale;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
     const float4 a = acc[i];
@@ -922,12 +936,12 @@ int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& 
   return ALGX_OK;
 }
 
-template <int N, bool CLIP, bool INV>
+template <int N, bool CLIP, bool INV, bool SHIFTED = false>
 int launch_bwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const CUtensorMap& tdo,
                const CUtensorMap& tdq, const CUtensorMap& tdk, const CUtensorMap& tdv, const algx_attn_config& cfg,
                const float* stat, const float* di, const float* guard, int* item_counter, int64_t B, int64_t H,
                int64_t T, cudaStream_t st) {
-  auto kern = attn_bwd_tc_kernel<N, CLIP, INV>;
+  auto kern = attn_bwd_tc_kernel<N, CLIP, INV, SHIFTED>;
   ALGX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kBwdSmem));
   int dev = 0, sms = 0;
   ALGX_CUDA(cudaGetDevice(&dev));
@@ -1006,17 +1020,27 @@ int tc_attn_bwd(const algx_attn_config& cfg, const void* q_scaled, const void* k
   // The guarded low branch uses the 1/Z statistic; the clipped link follows cfg.inv_stat.
   const bool inv = clip ? cfg.inv_stat != 0 : true;
   int s;
-#define ALGX_BWD(NN, CC, II) \
-  launch_bwd<NN, CC, II>(maps[0], maps[1], maps[2], maps[3], tdq, maps[4], maps[5], cfg, stat, di, guard, item_counter, \
-                         B, H, T, st)
+#define ALGX_BWD(NN, CC, II, SS) \
+  launch_bwd<NN, CC, II, SS>(maps[0], maps[1], maps[2], maps[3], tdq, maps[4], maps[5], cfg, stat, di, guard, \
+                             item_counter, B, H, T, st)
   if (cfg.n == 16)
-    s = clip ? (inv ? ALGX_BWD(16, true, true) : ALGX_BWD(16, true, false)) : ALGX_BWD(16, false, true);
+    s = clip ? (inv ? ALGX_BWD(16, true, true, false) : ALGX_BWD(16, true, false, false))
+             : ALGX_BWD(16, false, true, false);
   else if (cfg.n == 8)
-    s = clip ? (inv ? ALGX_BWD(8, true, true) : ALGX_BWD(8, true, false)) : ALGX_BWD(8, false, true);
+    s = clip ? (inv ? ALGX_BWD(8, true, true, false) : ALGX_BWD(8, true, false, false))
+             : ALGX_BWD(8, false, true, false);
   else
-    s = clip ? (inv ? ALGX_BWD(32, true, true) : ALGX_BWD(32, true, false)) : ALGX_BWD(32, false, true);
-#undef ALGX_BWD
+    s = clip ? (inv ? ALGX_BWD(32, true, true, false) : ALGX_BWD(32, true, false, false))
+             : ALGX_BWD(32, false, true, false);
   if (s) return s;
+  // With the range guard, the shifted branch's backward on the same pipeline
+  // (it returns at once unless the guard chose that branch).
+  if (cfg.mode == ALGX_MODE_GUARDED) {
+    s = cfg.n == 16 ? ALGX_BWD(16, false, false, true)
+                    : (cfg.n == 8 ? ALGX_BWD(8, false, false, true) : ALGX_BWD(32, false, false, true));
+    if (s) return s;
+  }
+#undef ALGX_BWD
   if (finish_dq) {
     const int64_t n4 = (int64_t)(nacc / 4);
     const int grid = (int)std::min<int64_t>((n4 + 255) / 256, 148 * 16);

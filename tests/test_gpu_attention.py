@@ -272,11 +272,12 @@ def test_fused_qknorm_prologue_matches_composed(dtype, with_sink):
 def test_fused_qknorm_backward_matches_composed(dtype, guard, gain, with_sink):
     """algx_qknorm_attn_bwd == algx_attn_bwd then algx_qknorm_bwd on q and k, on the same residuals.
 
-    gain 20 makes the scores exceed the guard bound, so the shifted fallback
-    supplies dq (bf16) instead of the fast path's fp32 accumulator. dk, dv and
+    gain 20 makes the scores exceed the guard bound, so the guarded mode's
+    shifted branch runs (on the tcgen05 backward too, for bf16). dk, dv and
     dsink are computed in a fixed order and must match bit for bit, as must dq
     wherever it does not come from the dQ reduce-adds (whose order varies
-    between any two calls); dgain differs only by the order of its sums.
+    between any two calls: bf16 I/O); dgain differs only by the order of its
+    sums.
     """
     from algx.kernels import flash as F
     from algx.kernels.qk_norm import qknorm_backward
@@ -297,7 +298,7 @@ def test_fused_qknorm_backward_matches_composed(dtype, guard, gain, with_sink):
     g = saved[7].cpu().tolist()  # max||q_s||^2, max||k||^2, max|v|, max|sink| (attn_common.cuh)
     low = g[0] * g[1] <= cfg.guard_qk and g[2] <= cfg.guard_v and (not with_sink or g[3] <= cfg.guard_sink)
     shifted = guard and not low
-    fast_dq = dtype == torch.bfloat16 and not shifted
+    fast_dq = dtype == torch.bfloat16  # both branches reduce-add dq on the tcgen05 path
     assert torch.equal(fused[1], dxk) and torch.equal(fused[2], dv)
     if with_sink:
         assert torch.equal(fused[5], dsink)
