@@ -1014,11 +1014,12 @@ int algx_attn_fwd(const algx_attn_config* cfg, const void* q_scaled, const void*
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   int mask = 7;
   bool fast = false;
-  if (int s = tc_attn_fwd(*cfg, q_scaled, k, v, sink, guard, o, stat, B, H, T, dtype, st, &fast)) return s;
+  if (int s = tc_attn_fwd(*cfg, q_scaled, k, v, sink, guard, o, o_precise, stat, B, H, T, dtype, st, &fast))
+    return s;
   if (fast) {
     // The fast kernel covers the unshifted branch, which the clipped link
-    // always takes; only a guarded call may still need the shifted fallback.
-    if (cfg->mode == ALGX_MODE_CLIPPED) return ALGX_OK;
+    // always takes, and under the range guard the shifted branch as well.
+    if (cfg->mode == ALGX_MODE_CLIPPED || cfg->mode == ALGX_MODE_GUARDED) return ALGX_OK;
     mask = 1 << BR_SHIFTED | 1 << BR_SOFTMAX;
   }
   const unsigned grid = generic_grid(B * H, T, fast);

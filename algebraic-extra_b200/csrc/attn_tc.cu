@@ -1,6 +1,6 @@
-// tcgen05 attention fast path: bf16 I/O, D = 64, T % 128 == 0, asinh
-// unshifted branch (the guarded low branch or the explicit clipped link),
-// fast rho, n in {8, 16, 32}.
+// tcgen05 attention fast path: bf16 I/O, D = 64, T % 128 == 0, asinh with
+// fast rho, n in {8, 16, 32}: the unshifted branch (the guarded low branch or
+// the explicit clipped link) and the range guard's shifted high branch.
 //
 // Forward (kernels/flash.py:189-284, head_resident.py:24-93): one CTA per
 // (128-query tile, head), two CTAs per SM. Warp roles: warps 0-7 compute the
@@ -9,7 +9,8 @@
 // each row into p = rho(x)^n, accumulate the fp32 row sum, and write bf16 P
 // back into TMEM; O += P V reads P from TMEM (A operand) and V from shared
 // memory (MN-major). No running maximum exists on this branch, so O needs no
-// rescaling; O = acc / l and stat = 1/l (or l^(-1/n)) at the end.
+// rescaling; O = acc / l and stat = 1/l (or l^(-1/n)) at the end. The shifted
+// branch takes the row maximum in a first pass over the keys (see below).
 //
 // Backward (kernels/flash.py:333-361, 435-627): one CTA per (128-key tile,
 // head). K, V stay resident; Q, dO, stat and di stream through a 4-stage TMA
@@ -163,16 +164,62 @@ __device__ __forceinline__ void grads_chunk(const uint32_t (&sv)[C], const uint3
 // warp: its 32 query rows, the sub-tile's 64 keys in two 32-column chunks),
 // so one group's TMEM round trips and barrier waits overlap the other's
 // arithmetic; their partial row sums meet in shared memory at the end.
-template <int N, bool CLIP>
-__global__ void __launch_bounds__(kFwdThreads, 2)
-    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                       const __grid_constant__ CUtensorMap tv, algx_attn_config cfg, const float* __restrict__ sink,
-                       const float* __restrict__ guard, __nv_bfloat16* __restrict__ o, float* __restrict__ stat,
-                       int H, int T, int* dev_err) {
-  pdl_wait();  // launched as a dependent of the prologue, which writes q_scaled and the guard maxima
-  const Eff e = resolve_variant(cfg, guard);
-  if (e.branch != BR_UNSHIFTED) return;  // the generic kernel runs the shifted fallback
-  pdl_trigger();  // the fallback kernel may be scheduled behind this grid's last blocks
+//
+// Shifted branch (range guard's high branch, kernels/flash.py:200-214,
+// 246-259): the weights are (rho(x) / rho(m))^n with m the row maximum of the
+// scores (and the sink logit). Rather than rescaling O in TMEM whenever a
+// running maximum grows, the body makes two passes over the keys: pass A
+// computes S = Q K^T only and takes the exact row maximum, pass B computes
+// the weights against that fixed m, so O and l accumulate without any
+// rescale. The result is the reference's up to rounding (a common factor of
+// every weight cancels in O / l). The sub-tile counter runs over both passes
+// (2 x nu sub-tiles), so every barrier keeps one phase sequence; pass A's
+// sub-tiles are released by the P.V thread without a product.
+
+// Weights of 32 scores of one row on the shifted branch: p = (rho(x) * shift)^N
+// with the stable rho (1 / (|x| + sqrt(1 + x^2)) for x < 0, kernels/flash.py:76-80)
+// and shift = 1 / rho(m); returns the fp32 sum.
+template <int N, bool DIAG>
+__device__ __forceinline__ float weights_chunk_shifted(const uint32_t (&sv)[32], uint32_t (&pk)[16], float shift,
+                                                       int col0, int r) {
+  const float2 one = make_float2(1.f, 1.f), sh = make_float2(shift, shift);
+  float2 acc = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float2 x = make_float2(__uint_as_float(sv[2 * i]), __uint_as_float(sv[2 * i + 1]));
+    const float2 rad = fma2(x, x, one);
+    const float2 rr = make_float2(rsqrt_fast(rad.x), rsqrt_fast(rad.y));
+    const float2 t = fma2(rad, rr, make_float2(fabsf(x.x), fabsf(x.y)));
+    float2 rho;
+    rho.x = x.x >= 0.f ? t.x : rcp_fast(t.x);
+    rho.y = x.y >= 0.f ? t.y : rcp_fast(t.y);
+    float2 p = ipow2_t<N>(mul2(rho, sh));
+    if constexpr (DIAG) {
+      if (col0 + 2 * i > r) p.x = 0.f;
+      if (col0 + 2 * i + 1 > r) p.y = 0.f;
+    }
+    acc = add2(acc, p);
+    pk[i] = pack_bf16x2(p.x, p.y);
+  }
+  return acc.x + acc.y;
+}
+
+// Row maximum of 32 scores (keys after the query excluded on the diagonal).
+template <bool DIAG>
+__device__ __forceinline__ float max_chunk(const uint32_t (&sv)[32], float m, int col0, int r) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i)
+    if (!DIAG || col0 + i <= r) m = fmaxf(m, __uint_as_float(sv[i]));
+  return m;
+}
+
+template <int N, bool CLIP, bool SHIFTED>
+__device__ __forceinline__ void attn_fwd_tc_body(const CUtensorMap* tq, const CUtensorMap* tk, const CUtensorMap* tv,
+                                                 const algx_attn_config& cfg, const float* __restrict__ sink,
+                                                 const Eff& e, __nv_bfloat16* __restrict__ o,
+                                                 float* __restrict__ o_prec, float* __restrict__ stat, int H, int T,
+                                                 int* dev_err) {
+  constexpr int kPasses = SHIFTED ? 2 : 1;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   uint8_t* sQ = smem;
@@ -182,6 +229,7 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
   __shared__ uint64_t bar_k_full[kFwdKStages], bar_k_empty[kFwdKStages], bar_v_full[kFwdVStages],
       bar_v_empty[kFwdVStages];
   __shared__ float l_part[kTile];  // row sums of weight group 1
+  __shared__ float m_part[SHIFTED ? 2 * kTile : 1];  // pass A row maxima of the two groups
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
   volatile int* abort_v = &abort_flag;
@@ -195,7 +243,7 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
   const int qt = nq - 1 - (int)blockIdx.y;
   const int bh = blockIdx.x;
   const int nk = qt + 1;   // 128-key tiles
-  const int nu = 2 * nk;   // 64-key sub-tiles
+  const int nu = 2 * nk;   // 64-key sub-tiles of one pass
   const int row_base = bh * T;
 
   if (threadIdx.x == 0) {
@@ -238,23 +286,25 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
 
   if (warp == kFwdProducer) {
     if (lane == 0) {
-      prefetch_tmap(&tq);
-      prefetch_tmap(&tk);
-      prefetch_tmap(&tv);
+      prefetch_tmap(tq);
+      prefetch_tmap(tk);
+      prefetch_tmap(tv);
       mbar_expect_tx(&bar_q, kTileBytes);
-      tma_load_2d(sQ, &tq, &bar_q, 0, row_base + qt * kTile);
-      // K tile j, then V tile j: K waits for the S products of tile j - 3,
-      // V for the P.V products of tile j - 2.
+      tma_load_2d(sQ, tq, &bar_q, 0, row_base + qt * kTile);
+      // K load J (tile J % nk), then V tile j of the weighted pass: K waits
+      // for the S products of load J - 3, V for the P.V products of tile j - 2.
       int issued_k[kFwdKStages] = {-1, -1, -1}, issued_v[kFwdVStages] = {-1, -1};
-      for (int j = 0; j < nk; ++j) {
-        const int sk = j % kFwdKStages, sv = j % kFwdVStages;
-        if (j >= kFwdKStages && !mbar_wait(&bar_k_empty[sk], ((j / kFwdKStages) - 1) & 1, abort_v, dev_err)) break;
+      for (int J = 0; J < kPasses * nk; ++J) {
+        const int sk = J % kFwdKStages;
+        if (J >= kFwdKStages && !mbar_wait(&bar_k_empty[sk], ((J / kFwdKStages) - 1) & 1, abort_v, dev_err)) break;
         mbar_expect_tx(&bar_k_full[sk], kTileBytes);
-        tma_load_2d(sK + sk * kTileBytes, &tk, &bar_k_full[sk], 0, row_base + j * kTile);
-        issued_k[sk] = j;
+        tma_load_2d(sK + sk * kTileBytes, tk, &bar_k_full[sk], 0, row_base + (J % nk) * kTile);
+        issued_k[sk] = J;
+        if (SHIFTED && J < nk) continue;  // pass A reads no V
+        const int j = SHIFTED ? J - nk : J, sv = j % kFwdVStages;
         if (j >= kFwdVStages && !mbar_wait(&bar_v_empty[sv], ((j / kFwdVStages) - 1) & 1, abort_v, dev_err)) break;
         mbar_expect_tx(&bar_v_full[sv], kTileBytes);
-        tma_load_2d(sV + sv * kTileBytes, &tv, &bar_v_full[sv], 0, row_base + j * kTile);
+        tma_load_2d(sV + sv * kTileBytes, tv, &bar_v_full[sv], 0, row_base + j * kTile);
         issued_v[sv] = j;
       }
       if (*abort_v) {  // let copies in flight land before the CTA exits
@@ -266,15 +316,15 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
       }
     }
   } else if (warp == kFwdProducer + 2) {
-    // ----- S_w = Q K_w^T into buffer w % 3 (K rows of half w & 1 of tile w >> 1),
+    // ----- S_w = Q K_J^T into buffer w % 3 (K rows of half w & 1 of load J = w >> 1),
     // up to three sub-tiles ahead of the P.V products
     if (lane == 0) {
       const uint32_t idS = idesc_bf16_f32(128, 64, 0, 0);
       const uint32_t q0 = smem_u32(sQ), k0 = smem_u32(sK);
       bool ok = mbar_wait(&bar_q, 0, abort_v, dev_err);
-      for (int w = 0; ok && w < nu; ++w) {
-        const int b = w % 3, j = w >> 1, s = j % kFwdKStages;
-        if ((w & 1) == 0 && !mbar_wait(&bar_k_full[s], (j / kFwdKStages) & 1, abort_v, dev_err)) break;
+      for (int w = 0; ok && w < kPasses * nu; ++w) {
+        const int b = w % 3, J = w >> 1, s = J % kFwdKStages;
+        if ((w & 1) == 0 && !mbar_wait(&bar_k_full[s], (J / kFwdKStages) & 1, abort_v, dev_err)) break;
         if (w >= 3 && !mbar_wait(&bar_p_free[b], (w / 3 - 1) & 1, abort_v, dev_err)) break;
         tc_fence_after();
         const uint32_t kb = k0 + s * kTileBytes + (w & 1) * (kTileBytes / 2);
@@ -282,19 +332,25 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
         for (int k = 0; k < 4; ++k)
           mma_ss(tS + 64 * b, desc_sw128(q0 + k * 32, 16, 1024), desc_sw128(kb + k * 32, 16, 1024), idS, k > 0);
         mma_commit(&bar_s_full[b]);
-        if (w & 1) mma_commit(&bar_k_empty[s]);  // both halves of K tile j have been read
+        if (w & 1) mma_commit(&bar_k_empty[s]);  // both halves of K load J have been read
       }
       settle_issuer(0);
     }
   } else if (warp == kFwdProducer + 1) {
     // ----- O += P_u V_u, P_u in the first 32 columns of buffer u % 3; the
-    // commit after P.V of a tile's second half releases its V stage.
+    // commit after P.V of a tile's second half releases its V stage. Pass A
+    // sub-tiles only hand their buffer back once the weight warps have read it.
     if (lane == 0) {
       const uint32_t idO = idesc_bf16_f32(128, 64, 0, 1);
       const uint32_t v0 = smem_u32(sV);
-      for (int u = 0; u < nu; ++u) {
-        const int b = u % 3, j = u >> 1, s = j % kFwdVStages;
-        if (!mbar_wait(&bar_p_full[b], (u / 3) & 1, abort_v, dev_err)) break;
+      for (int w = 0; w < kPasses * nu; ++w) {
+        const int b = w % 3;
+        if (!mbar_wait(&bar_p_full[b], (w / 3) & 1, abort_v, dev_err)) break;
+        if (SHIFTED && w < nu) {
+          mbar_arrive(&bar_p_free[b]);
+          continue;
+        }
+        const int u = SHIFTED ? w - nu : w, j = u >> 1, s = j % kFwdVStages;
         if ((u & 1) == 0 && !mbar_wait(&bar_v_full[s], (j / kFwdVStages) & 1, abort_v, dev_err)) break;
         tc_fence_after();
         const uint32_t vb = v0 + s * kTileBytes + (u & 1) * (kTileBytes / 2);
@@ -312,12 +368,46 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
     const int g = warp >> 2;
     const int r = (warp & 3) * 32 + lane;
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    float l = 0.f, rr;
-    if (g == 0 && cfg.has_sink) l = weight<N, CLIP>(sink[bh % H], cfg.clamp, rr);
+    float l = 0.f, rr, shift = 1.f;
     bool ok = true;
-    for (int u = g; u < nu; u += 2) {
-      const int b = u % 3;
-      if (!mbar_wait_warp(&bar_s_full[b], (u / 3) & 1, abort_v, dev_err)) {
+    int w0 = g;  // first sub-tile of the weighted pass owned by this group
+    if constexpr (SHIFTED) {
+      // pass A: the row maximum over the causal keys
+      float m = -INFINITY;
+      for (int u = g; u < nu; u += 2) {
+        const int b = u % 3;
+        if (!mbar_wait_warp(&bar_s_full[b], (u / 3) & 1, abort_v, dev_err)) {
+          ok = false;
+          break;
+        }
+        const bool diag = (u >> 1) == qt;
+        const int col0 = 64 * (u & 1);
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          tc_fence_after();
+          uint32_t sv[32];
+          tmem_ld32(tS + 64 * b + 32 * c + lane_off, sv);
+          m = diag ? max_chunk<true>(sv, m, col0 + 32 * c, r) : max_chunk<false>(sv, m, col0 + 32 * c, r);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar_p_full[b]);
+      }
+      // both groups meet here once, also after an aborted wait (every one of
+      // the 256 threads reaches this barrier exactly once)
+      m_part[g * kTile + r] = m;
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      m = fmaxf(m_part[r], m_part[kTile + r]);
+      if (cfg.has_sink) m = fmaxf(m, sink[bh % H]);
+      shift = rho_exact(-m, rr);  // 1 / rho(m)
+      if (g == 0 && cfg.has_sink) l = ipow_t<N>(rho_exact(sink[bh % H], rr) * shift);
+      w0 = nu + g;
+    } else {
+      if (g == 0 && cfg.has_sink) l = weight<N, CLIP>(sink[bh % H], cfg.clamp, rr);
+    }
+    for (int w = w0; ok && w < kPasses * nu; w += 2) {
+      const int b = w % 3, u = SHIFTED ? w - nu : w;
+      if (!mbar_wait_warp(&bar_s_full[b], (w / 3) & 1, abort_v, dev_err)) {
         ok = false;
         break;
       }
@@ -328,10 +418,17 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
         tc_fence_after();
         uint32_t sv[32], pk[16];
         tmem_ld32(tS + 64 * b + 32 * c + lane_off, sv);
-        if (diag)
-          l += weights_chunk<N, CLIP, true>(sv, pk, cfg.clamp, col0 + 32 * c, r);
-        else
-          l += weights_chunk<N, CLIP, false>(sv, pk, cfg.clamp, col0 + 32 * c, r);
+        if constexpr (SHIFTED) {
+          if (diag)
+            l += weights_chunk_shifted<N, true>(sv, pk, shift, col0 + 32 * c, r);
+          else
+            l += weights_chunk_shifted<N, false>(sv, pk, shift, col0 + 32 * c, r);
+        } else {
+          if (diag)
+            l += weights_chunk<N, CLIP, true>(sv, pk, cfg.clamp, col0 + 32 * c, r);
+          else
+            l += weights_chunk<N, CLIP, false>(sv, pk, cfg.clamp, col0 + 32 * c, r);
+        }
         // P (bf16 pairs) over S columns 16c..16c+15, already consumed by this thread
         tmem_st16(tS + 64 * b + 16 * c + lane_off, pk);
       }
@@ -350,26 +447,57 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
       const float inv = 1.f / l;
       const size_t row = (size_t)row_base + (size_t)qt * kTile + r;
       uint4* dst = reinterpret_cast<uint4*>(o + row * 64);
+      float4* dst_prec = reinterpret_cast<float4*>(o_prec + (SHIFTED ? row * 64 : 0));
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         uint32_t ov[32];
         tmem_ld32(tO + lane_off + 32 * c, ov);
 #pragma unroll
         for (int un = 0; un < 4; ++un) {
+          float f[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(ov[8 * un + i]) * inv;
           uint4 w;
-          w.x = pack_bf16x2(__uint_as_float(ov[8 * un + 0]) * inv, __uint_as_float(ov[8 * un + 1]) * inv);
-          w.y = pack_bf16x2(__uint_as_float(ov[8 * un + 2]) * inv, __uint_as_float(ov[8 * un + 3]) * inv);
-          w.z = pack_bf16x2(__uint_as_float(ov[8 * un + 4]) * inv, __uint_as_float(ov[8 * un + 5]) * inv);
-          w.w = pack_bf16x2(__uint_as_float(ov[8 * un + 6]) * inv, __uint_as_float(ov[8 * un + 7]) * inv);
+          w.x = pack_bf16x2(f[0], f[1]);
+          w.y = pack_bf16x2(f[2], f[3]);
+          w.z = pack_bf16x2(f[4], f[5]);
+          w.w = pack_bf16x2(f[6], f[7]);
           dst[c * 4 + un] = w;
+          if constexpr (SHIFTED) {  // the unrounded output (kernels/flash.py:851-852)
+            dst_prec[c * 8 + 2 * un] = make_float4(f[0], f[1], f[2], f[3]);
+            dst_prec[c * 8 + 2 * un + 1] = make_float4(f[4], f[5], f[6], f[7]);
+          }
         }
       }
-      stat[row] = e.inv_stat ? inv : inv_root(l, N);
+      if constexpr (SHIFTED)
+        stat[row] = shift * inv_root(l, N);  // 1 / (rho(m) l^(1/n))
+      else
+        stat[row] = e.inv_stat ? inv : inv_root(l, N);
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == kFwdProducer) tmem_dealloc(tmem_base, 256);
+}
+
+// The unshifted body always; with the range guard (CLIP false) also the
+// shifted one, chosen on the device from the prologue's maxima, so neither
+// branch needs a second launch.
+template <int N, bool CLIP>
+__global__ void __launch_bounds__(kFwdThreads, 2)
+    attn_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                       const __grid_constant__ CUtensorMap tv, algx_attn_config cfg, const float* __restrict__ sink,
+                       const float* __restrict__ guard, __nv_bfloat16* __restrict__ o, float* __restrict__ o_prec,
+                       float* __restrict__ stat, int H, int T, int* dev_err) {
+  pdl_wait();  // launched as a dependent of the prologue, which writes q_scaled and the guard maxima
+  const Eff e = resolve_variant(cfg, guard);
+  pdl_trigger();
+  if (e.branch == BR_UNSHIFTED) {
+    attn_fwd_tc_body<N, CLIP, false>(&tq, &tk, &tv, cfg, sink, e, o, o_prec, stat, H, T, dev_err);
+  } else if constexpr (!CLIP) {
+    if (e.branch == BR_SHIFTED && cfg.mode == ALGX_MODE_GUARDED)
+      attn_fwd_tc_body<N, false, true>(&tq, &tk, &tv, cfg, sink, e, o, o_prec, stat, H, T, dev_err);
+  }
 }
 
 // ---------------------------------------------------------------- backward
@@ -925,13 +1053,13 @@ bool fast_eligible(const algx_attn_config& cfg, int64_t T, int32_t dtype) {
 
 template <int N, bool CLIP>
 int launch_fwd(const CUtensorMap& tq, const CUtensorMap& tk, const CUtensorMap& tv, const algx_attn_config& cfg,
-               const float* sink, const float* guard, void* o, float* stat, int64_t B, int64_t H, int64_t T,
-               cudaStream_t st) {
+               const float* sink, const float* guard, void* o, float* o_prec, float* stat, int64_t B, int64_t H,
+               int64_t T, cudaStream_t st) {
   auto kern = attn_fwd_tc_kernel<N, CLIP>;
   ALGX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem));
   dim3 grid((unsigned)(B * H), (unsigned)(T / kTile));
   ALGX_CUDA(launch_dependent(kern, grid, kFwdThreads, kFwdSmem, st, tq, tk, tv, cfg, sink, guard,
-                             static_cast<__nv_bfloat16*>(o), stat, (int)H, (int)T, device_error_word()));
+                             static_cast<__nv_bfloat16*>(o), o_prec, stat, (int)H, (int)T, device_error_word()));
   ALGX_LAUNCHED("attn_fwd_tc launch");
   return ALGX_OK;
 }
@@ -963,8 +1091,8 @@ int make_maps(const void* const* ptrs, int count, CUtensorMap* maps, int64_t row
 }  // namespace
 
 int tc_attn_fwd(const algx_attn_config& cfg, const void* q_scaled, const void* k, const void* v, const float* sink,
-                const float* guard, void* o, float* stat, int64_t B, int64_t H, int64_t T, int32_t dtype,
-                cudaStream_t st, bool* launched) {
+                const float* guard, void* o, float* o_prec, float* stat, int64_t B, int64_t H, int64_t T,
+                int32_t dtype, cudaStream_t st, bool* launched) {
   *launched = false;
   if (!fast_eligible(cfg, T, dtype)) return ALGX_OK;
   CUtensorMap maps[3];
@@ -973,14 +1101,14 @@ int tc_attn_fwd(const algx_attn_config& cfg, const void* q_scaled, const void* k
   const bool clip = cfg.mode == ALGX_MODE_CLIPPED;
   int s;
   if (cfg.n == 16)
-    s = clip ? launch_fwd<16, true>(maps[0], maps[1], maps[2], cfg, sink, guard, o, stat, B, H, T, st)
-             : launch_fwd<16, false>(maps[0], maps[1], maps[2], cfg, sink, guard, o, stat, B, H, T, st);
+    s = clip ? launch_fwd<16, true>(maps[0], maps[1], maps[2], cfg, sink, guard, o, o_prec, stat, B, H, T, st)
+             : launch_fwd<16, false>(maps[0], maps[1], maps[2], cfg, sink, guard, o, o_prec, stat, B, H, T, st);
   else if (cfg.n == 8)
-    s = clip ? launch_fwd<8, true>(maps[0], maps[1], maps[2], cfg, sink, guard, o, stat, B, H, T, st)
-             : launch_fwd<8, false>(maps[0], maps[1], maps[2], cfg, sink, guard, o, stat, B, H, T, st);
+    s = clip ? launch_fwd<8, true>(maps[0], maps[1], maps[2], cfg, sink, guard, o, o_prec, stat, B, H, T, st)
+             : launch_fwd<8, false>(maps[0], maps[1], maps[2], cfg, sink, guard, o, o_prec, stat, B, H, T, st);
   else
-    s = clip ? launch_fwd<32, true>(maps[0], maps[1], maps[2], cfg, sink, guard, o, stat, B, H, T, st)
-             : launch_fwd<32, false>(maps[0], maps[1], maps[2], cfg, sink, guard, o, stat, B, H, T, st);
+    s = clip ? launch_fwd<32, true>(maps[0], maps[1], maps[2], cfg, sink, guard, o, o_prec, stat, B, H, T, st)
+             : launch_fwd<32, false>(maps[0], maps[1], maps[2], cfg, sink, guard, o, o_prec, stat, B, H, T, st);
   if (s) return s;
   *launched = true;
   return ALGX_OK;

@@ -1,6 +1,7 @@
-// tcgen05 fast path of the attention (bf16, D = 64, T % 128 == 0, asinh
-// unshifted branch). Each launcher sets *launched when it took the call;
-// the generic kernels then skip the unshifted branch.
+// tcgen05 fast path of the attention (bf16, D = 64, T % 128 == 0, asinh;
+// the unshifted branch, and under the range guard the shifted one too). Each
+// launcher sets *launched when it took the call; the generic kernels then
+// skip the branches it covers.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -11,9 +12,11 @@
 
 namespace algx {
 
+// o_prec: the fp32 output the guarded mode's shifted branch also writes
+// (may be null outside the guarded mode).
 int tc_attn_fwd(const algx_attn_config& cfg, const void* q_scaled, const void* k, const void* v,
-                const float* sink, const float* guard, void* o, float* stat, int64_t B, int64_t H, int64_t T,
-                int32_t dtype, cudaStream_t st, bool* launched);
+                const float* sink, const float* guard, void* o, float* o_prec, float* stat, int64_t B, int64_t H,
+                int64_t T, int32_t dtype, cudaStream_t st, bool* launched);
 
 // With finish_dq false the fp32 dQ accumulator (the first B*H*T*64 floats of
 // the workspace, unscaled) is left for the caller instead of being rounded

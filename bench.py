@@ -283,8 +283,40 @@ def secondary(dev, rank, world, stream, sync_all, max_over_ranks, steps=5, warmu
                 "config": f"B={B4} H={H4} S={T} D={D} bf16 per GPU, QK-norm + guarded asinh n=16 c=8, "
                           "public API (autograd)", "scaling": "weak"}
 
+    def attn_shifted_line():
+        # config 2 with QK-norm gains 4.5: max||q_s||^2 * max||k||^2 (~gain^4) exceeds the
+        # range guard's bound, so the high (shifted) branch runs; timed beside
+        # the same inputs with gains 1 (the low branch) through the public API
+        from algx.kernels.flash import build_config, make_variant, qknorm_attn_prepare
+
+        q, k, v, do = (torch.randn((B, H, T, D), device=dev, generator=gen).to(torch.bfloat16) for _ in range(4))
+        noise = [0.02 * torch.randn(D, device=dev, generator=gen) for _ in range(2)]
+        res = {}
+        for name, gain in (("unshifted", 1.0), ("shifted", 4.5)):
+            gq, gk = gain + noise[0], gain + noise[1]
+            cfg = build_config("asinh", make_variant("asinh", N_POW, C_SCALE, T), T, D, C_SCALE, False, True)
+            guard = qknorm_attn_prepare(q, k, v, gq, gk, None, cfg, EPS)[2].tolist()
+            low = guard[0] * guard[1] <= cfg.guard_qk and guard[2] <= cfg.guard_v
+            leaves = [x.clone().requires_grad_(True) for x in (q, k, v, gq, gk)]
+
+            def attn_step():
+                o = qknorm_flash_attention(*leaves, eps=EPS, kind="asinh", n=N_POW, c=C_SCALE, range_guard=True)
+                o.backward(do)
+                for x in leaves:
+                    x.grad = None
+
+            ms = time_cuda(attn_step, steps, warmup, stream, sync_all, max_over_ranks)
+            res[name] = {"ms_per_step": ms, "branch": "unshifted" if low else "shifted", "gain": gain,
+                         "tflops": world * STEP_FLOP / (ms / 1e3) / 1e12}
+        return {"metric": "asinh-attn fwd+bwd TFLOP/s, range guard's shifted branch", "unit": "TFLOP/s",
+                "value": res["shifted"]["tflops"], "ms_per_step": res["shifted"]["ms_per_step"],
+                "vs_unshifted": res["unshifted"]["ms_per_step"] / res["shifted"]["ms_per_step"], "runs": res,
+                "config": f"B={B} H={H} S={T} D={D} bf16 per GPU, QK-norm gains 4.5 (shifted) vs 1 (unshifted), "
+                          "guarded asinh n=16 c=8, public API (autograd)", "scaling": "weak"}
+
     table = [
         ("qknorm_cfg2", lambda: qknorm_line(dev, gen, world, stream, sync_all, max_over_ranks)),
+        ("attn_cfg2_shifted", attn_shifted_line),
         ("head_cfg3_ce", lambda: head_line(768, "ce", 16, 16.0)),
         ("head_cfg3_alg_ce", lambda: head_line(768, "alg_ce", 8, 2.0)),
         ("head_cfg4_ce", lambda: head_line(1024, "ce", 16, 16.0)),

@@ -8,6 +8,9 @@ both K buffers, every slot of the item queue, mbarrier parities carried from
 one item to the next, a query ring that wraps across items, and dQ reduce-adds
 from many items into one accumulator. The forward runs several waves of CTAs.
 
+A third case raises the QK-norm gains so that the range guard takes the
+shifted branch over the whole batch.
+
 Checks, in the spirit of the reference's whole-head test
 (tests/test_flash_kernel_tpu.py:253-328, head_resident.py:95-132):
 
@@ -37,11 +40,11 @@ T, D, N_POW, C_SCALE, EPS = 2048, 64, 16, 8.0, 1e-5
 TOL = 2e-2  # BASELINE bf16 I/O with fp32 accumulation
 
 
-def _inputs(B, H, with_sink, seed):
+def _inputs(B, H, with_sink, seed, gain):
     g = torch.Generator().manual_seed(seed)
     q, k, v, do = (torch.randn((B, H, T, D), generator=g).to(torch.bfloat16) for _ in range(4))
-    gq = 1 + 0.02 * torch.randn(D, generator=g)
-    gk = 1 + 0.02 * torch.randn(D, generator=g)
+    gq = gain + 0.02 * torch.randn(D, generator=g)
+    gk = gain + 0.02 * torch.randn(D, generator=g)
     sink = 0.5 * torch.randn(H, generator=g) if with_sink else None
     return q, k, v, do, gq, gk, sink
 
@@ -70,23 +73,28 @@ def _oracle_head(qh, kh, vh, doh, gq, gk, sink_h):
             *(t.grad for t in gains), None if s is None else s.grad)
 
 
-@pytest.mark.parametrize("B,H,with_sink,sample", [
-    (8, 12, False, (0, 13, 27, 40, 55, 68, 81, 95)),
-    (8, 16, True, (0, 17, 35, 50, 69, 86, 103, 127)),
-], ids=["config2", "config4_350m_sink"])
-def test_fullsize_qknorm_attention(B, H, with_sink, sample):
+@pytest.mark.parametrize("B,H,with_sink,gain,sample", [
+    (8, 12, False, 1.0, (0, 13, 27, 40, 55, 68, 81, 95)),
+    (8, 16, True, 1.0, (0, 17, 35, 50, 69, 86, 103, 127)),
+    (8, 12, True, 4.5, (1, 14, 30, 47, 58, 70, 83, 94)),
+], ids=["config2", "config4_350m_sink", "config2_sink_shifted"])
+def test_fullsize_qknorm_attention(B, H, with_sink, gain, sample):
     sms = torch.cuda.get_device_properties(0).multi_processor_count
     items = B * H * (T // 128)
     assert items > 2 * sms, "the shape must give every backward CTA several work items"
-    q, k, v, do, gq, gk, sink = _inputs(B, H, with_sink, seed=2048 + H)
+    q, k, v, do, gq, gk, sink = _inputs(B, H, with_sink, seed=2048 + H, gain=gain)
 
-    # the guard must choose the unshifted branch, so the tcgen05 kernels run
+    # gain 1: the guard chooses the unshifted branch; gain 4.5 puts the
+    # product of the squared norms (which grows with gain^4) above the
+    # guard's bound of about 251: the shifted branch, which also runs
+    # on the tcgen05 kernels under the range guard
     var = F.make_variant("asinh", N_POW, C_SCALE, T)
     sk = F.check_inputs(q.cuda(), k.cuda(), v.cuda(), sink, "asinh", C_SCALE)
     cfg = F.build_config("asinh", var, T, D, C_SCALE, with_sink, True)
     _, _, guard = F.qknorm_attn_prepare(q.cuda(), k.cuda(), v.cuda(), gq.cuda(), gk.cuda(), sk, cfg, EPS)
     m = guard.cpu().tolist()
-    assert m[0] * m[1] <= cfg.guard_qk and m[2] <= cfg.guard_v and (not with_sink or m[3] <= cfg.guard_sink)
+    low = m[0] * m[1] <= cfg.guard_qk and m[2] <= cfg.guard_v and (not with_sink or m[3] <= cfg.guard_sink)
+    assert low == (gain == 1.0), (m, gain)
 
     L.device_error()  # clear the device error word
     o1, g1 = _run(q, k, v, do, gq, gk, sink, range_guard=True)
