@@ -213,12 +213,18 @@ class FlatParams:
         self.flat = {k: nn.Parameter(v) for k, v in self.data.items()}
         for k, v in self.flat.items():
             v.grad = self.grad[k]
+        # optional callable(name), run before a parameter is handed out: a
+        # sharded optimizer uses it to wait for the gather of that parameter's
+        # updated values on first use
+        self.fence = None
 
     def zero_grad(self) -> None:
         for g in self.grad.values():
             g.zero_()
 
     def __getitem__(self, name: str) -> nn.Parameter:
+        if self.fence is not None:
+            self.fence(name)
         return self.params[name]
 
 

@@ -15,6 +15,20 @@ Then, on the device and without a host synchronisation:
     AdamW on the two flat master buffers, weight decay on the decayed one only
     (model.py:120-125 mask)
 
+With ``shard_optimizer`` (the default on more than one rank) the decayed
+buckets are reduce-scattered instead of all-reduced: each rank receives the
+summed gradient of its 1/world slice of every bucket, the global norm comes
+from the slices' squared sums (one small all-reduce), AdamW updates only this
+rank's slice of the float32 masters, and the updated slices are all-gathered
+back in place, asynchronously and in the order the forward pass uses them;
+the model's parameter lookup waits for a bucket's gather on first use, so the
+gather overlaps the next forward. Gradient exchange volume is that of the
+all-reduce; the update runs on 1/world of the decayed parameters. The
+element-wise maths is unchanged, so the masters match the replicated update up
+to the summation order of the gradient norm. Gains and sinks (the small
+non-decayed buffer) and any bucket whose length is not a multiple of the world
+size stay all-reduced and replicated.
+
 The step works for any module that exposes ``flat`` (``algx.model.FlatParams``)
 and ``loss(tokens, targets) -> (objective, telemetry)``; ``algx.model.AlgebraicLM``
 is the one this package ships.
@@ -31,6 +45,9 @@ import torch.distributed as dist
 class DataParallelTrainer:
     """Train step over the ranks of ``group`` (all ranks when None).
 
+    ``shard_optimizer``: shard the decayed parameters' update over the ranks
+    (see the module docstring); ignored on one rank.
+
     ``micro_batch``: sequences per forward/backward pass; the rank's share of
     the batch must be a multiple of it. ``bucket_bytes``: target size of one
     all-reduce. ``check_finite``: before each optimizer update, read the loss
@@ -42,22 +59,50 @@ class DataParallelTrainer:
 
     def __init__(self, model, *, lr: float = 2e-3, betas=(0.9, 0.95), eps: float = 1e-8,
                  weight_decay: float = 0.1, clip: float = 1.0, micro_batch: int = 8,
-                 bucket_bytes: int = 32 << 20, group=None, check_finite: bool = False):
+                 bucket_bytes: int = 32 << 20, group=None, check_finite: bool = False,
+                 shard_optimizer: bool = True):
         self.model = model
         self.check_finite = bool(check_finite)
         self.flat = model.flat
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_available() and dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if self.world > 1 else 0
         self.clip = float(clip)
         self.micro_batch = int(micro_batch)
         dev = self.flat.data[True].device
-        groups = [{"params": [self.flat.flat[True]], "weight_decay": weight_decay},
-                  {"params": [self.flat.flat[False]], "weight_decay": 0.0}]
-        self.opt = torch.optim.AdamW(groups, lr=lr, betas=tuple(betas), eps=eps,
-                                     fused=dev.type == "cuda")
         self._works: List = []
         self._last = False
         self._buckets = self._make_buckets(bucket_bytes) if self.world > 1 else []
+        # bucket index -> (this rank's slice of the masters, its gradient buffer)
+        self._shard: Dict[int, Tuple[torch.Tensor, torch.Tensor]] = {}
+        if shard_optimizer and self.world > 1:
+            for bi, (decay, a, b, _) in enumerate(self._buckets):
+                if decay and (b - a) % self.world == 0:
+                    n = (b - a) // self.world
+                    lo = a + self.rank * n
+                    self._shard[bi] = (self.flat.data[True][lo:lo + n],
+                                       torch.zeros(n, dtype=torch.float32, device=dev))
+        if self._shard:
+            decayed = []
+            for bi, (decay, a, b, _) in enumerate(self._buckets):
+                if not decay:
+                    continue
+                m, g = self._shard[bi] if bi in self._shard else (self.flat.data[True][a:b], self.flat.grad[True][a:b])
+                p = torch.nn.Parameter(m)
+                p.grad = g
+                decayed.append(p)
+            groups = [{"params": decayed, "weight_decay": weight_decay},
+                      {"params": [self.flat.flat[False]], "weight_decay": 0.0}]
+        else:
+            groups = [{"params": [self.flat.flat[True]], "weight_decay": weight_decay},
+                      {"params": [self.flat.flat[False]], "weight_decay": 0.0}]
+        self.opt = torch.optim.AdamW(groups, lr=lr, betas=tuple(betas), eps=eps,
+                                     fused=dev.type == "cuda")
+        # in-place gathers of updated slices still in flight: bucket -> work
+        self._gathers: Dict[int, object] = {}
+        self._bucket_of = {n: bi for bi, (_, _, _, names) in enumerate(self._buckets) for n in names}
+        if self._shard:
+            self.flat.fence = self._fence
         self._pending: Dict[int, int] = {}
         self._hooks = []
         if self._buckets:
@@ -99,8 +144,24 @@ class DataParallelTrainer:
             self._pending[bi] = left
             if left == 0:
                 decay, a, b, _ = self._buckets[bi]
-                self._works.append(dist.all_reduce(self.flat.grad[decay][a:b], group=self.group, async_op=True))
+                if bi in self._shard:
+                    self._works.append(dist.reduce_scatter_tensor(self._shard[bi][1], self.flat.grad[decay][a:b],
+                                                                  group=self.group, async_op=True))
+                else:
+                    self._works.append(dist.all_reduce(self.flat.grad[decay][a:b], group=self.group, async_op=True))
         return hook
+
+    def _fence(self, name: str) -> None:
+        """Wait (on the device) for the gather of ``name``'s bucket, once."""
+        if self._gathers:
+            w = self._gathers.pop(self._bucket_of.get(name, -1), None)
+            if w is not None:
+                w.wait()
+
+    def _wait_gathers(self) -> None:
+        for w in self._gathers.values():
+            w.wait()
+        self._gathers = {}
 
     # ------------------------------------------------------------ step
     def step(self, tokens: torch.Tensor, targets: torch.Tensor) -> torch.Tensor:
@@ -131,8 +192,16 @@ class DataParallelTrainer:
             for w in self._works:
                 w.wait()
             self._works = []
-            dist.all_reduce(loss_sum, group=self.group)
-        self._clip_and_scale()
+        if self._shard:
+            # the loss and this rank's share of ||g||^2 in one all-reduce
+            red = torch.stack([loss_sum, self._local_sq()])
+            dist.all_reduce(red, group=self.group)
+            loss_sum = red[0]
+            self._apply_clip(red[1])
+        else:
+            if self.world > 1:
+                dist.all_reduce(loss_sum, group=self.group)
+            self._clip_and_scale()
         loss = loss_sum / (n_micro * self.world)
         if self.check_finite:
             # loss and gnorm are already reduced over the ranks, so every rank
@@ -141,7 +210,15 @@ class DataParallelTrainer:
             if not ok:
                 raise FloatingPointError(f"non-finite loss {float(loss)} or gradient norm "
                                          f"{float(self.last_gnorm)}; the update was not applied")
+        self._wait_gathers()  # a bucket no forward fetched since the last step
         self.opt.step()
+        if self._shard:
+            # every rank's updated slices back into the full masters, in the
+            # order the next forward needs them (the reverse of the buckets')
+            for bi in sorted(self._shard, reverse=True):
+                _, a, b, _ = self._buckets[bi]
+                self._gathers[bi] = dist.all_gather_into_tensor(self.flat.data[True][a:b], self._shard[bi][0],
+                                                                group=self.group, async_op=True)
         if hasattr(self.model, "weights_changed"):
             self.model.weights_changed()
         return loss
@@ -154,7 +231,34 @@ class DataParallelTrainer:
         torch._foreach_mul_(grads, scale)
         self.last_gnorm = gnorm
 
+    def _sharded_grads(self):
+        """(this rank's gradient slices, the replicated gradients)."""
+        shard = [g for _, g in self._shard.values()]
+        repl = [self.flat.grad[True][a:b] for bi, (d, a, b, _) in enumerate(self._buckets)
+                if d and bi not in self._shard]
+        repl.append(self.flat.grad[False])
+        return shard, repl
+
+    def _local_sq(self) -> torch.Tensor:
+        """This rank's share of the squared global norm: its slices, plus the
+        replicated gradients counted on rank 0 only."""
+        shard, repl = self._sharded_grads()
+        parts = [torch.linalg.vector_norm(g) for g in shard]
+        if self.rank == 0:
+            parts += [torch.linalg.vector_norm(g) for g in repl]
+        return torch.sum(torch.stack(parts) ** 2)
+
+    def _apply_clip(self, total_sq: torch.Tensor) -> None:
+        shard, repl = self._sharded_grads()
+        gnorm = torch.sqrt(total_sq) / self.world
+        scale = torch.clamp(self.clip / torch.clamp(gnorm, min=1e-12), max=1.0) / self.world
+        torch._foreach_mul_(shard + repl, scale)
+        self.last_gnorm = gnorm
+
     def close(self) -> None:
+        self._wait_gathers()
+        if self.flat.fence == self._fence:
+            self.flat.fence = None
         for h in self._hooks:
             h.remove()
         self._hooks = []

@@ -104,7 +104,7 @@ def test_clip_scales_to_the_bound():
     assert abs(float(torch.linalg.vector_norm(g)) - 1e-3) < 1e-8
 
 
-def _worker(rank, world, init_file, q):
+def _worker(rank, world, init_file, q, shard=True):
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path[:0] = [root, os.path.join(root, "algebraic-extra_b200")]
@@ -113,35 +113,41 @@ def _worker(rank, world, init_file, q):
         from algx.train import DataParallelTrainer as T
         from tests.test_train_host import ToyLM, _batch
         model = ToyLM()
-        # small buckets: several all-reduces per step, launched from the backward hooks
-        tr = T(model, lr=1e-2, micro_batch=2, clip=0.5, bucket_bytes=256)
+        # small buckets: several exchanges per step, launched from the backward hooks
+        tr = T(model, lr=1e-2, micro_batch=2, clip=0.5, bucket_bytes=256, shard_optimizer=shard)
         tok, tgt = _batch()
         per = tok.shape[0] // world
         sl = slice(rank * per, (rank + 1) * per)
         losses = [float(tr.step(tok[sl], tgt[sl])) for _ in range(2)]
+        nshard = len(tr._shard)
+        tr.close()  # waits for the last step's gathers of the updated slices
         # numpy copies: torch tensors would be shared by file descriptor and vanish with the process
-        q.put((rank, len(tr._buckets), losses, {k: v.numpy().copy() for k, v in model.flat.data.items()}))
-        tr.close()
+        q.put((rank, len(tr._buckets), nshard, losses, {k: v.numpy().copy() for k, v in model.flat.data.items()}))
     finally:
         dist.destroy_process_group()
 
 
-def test_two_ranks_match_one_process():
-    """2 gloo ranks with half the batch each give the single-process step on the whole batch."""
+@pytest.mark.parametrize("shard", [True, False], ids=["sharded_optimizer", "replicated_optimizer"])
+def test_two_ranks_match_one_process(shard):
+    """2 gloo ranks with half the batch each give the single-process step on the
+    whole batch, with the decayed parameters' update sharded over the ranks
+    (reduce-scatter, AdamW on each rank's slice, in-place all-gather fenced on
+    first use by the next forward) and with the replicated update."""
     ref_losses, ref = _run_single(micro=2)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     with tempfile.TemporaryDirectory() as tmp:
         init = os.path.join(tmp, "init")
-        procs = [ctx.Process(target=_worker, args=(r, 2, init, q)) for r in range(2)]
+        procs = [ctx.Process(target=_worker, args=(r, 2, init, q, shard)) for r in range(2)]
         for p in procs:
             p.start()
         out = [q.get(timeout=120) for _ in procs]
         for p in procs:
             p.join(timeout=60)
             assert p.exitcode == 0
-    for rank, nb, losses, params in out:
+    for rank, nb, nshard, losses, params in out:
         assert nb >= 3
+        assert (nshard >= 2) if shard else nshard == 0
         assert all(abs(a - b) < 1e-6 for a, b in zip(losses, ref_losses)), (losses, ref_losses)
         for k in ref:
             torch.testing.assert_close(torch.from_numpy(params[k]), ref[k], rtol=1e-5, atol=1e-6)
