@@ -75,13 +75,22 @@ class DataParallelTrainer:
         self._buckets = self._make_buckets(bucket_bytes) if self.world > 1 else []
         # bucket index -> (this rank's slice of the masters, its gradient buffer)
         self._shard: Dict[int, Tuple[torch.Tensor, torch.Tensor]] = {}
+        # bucket index -> the bucket's masters as a tensor on the same storage
+        # with its own autograd version counter: the gather writes through it,
+        # so finishing a gather (which gloo does at wait time) does not bump the
+        # version of weights the forward has already saved for the backward.
+        # Safe because every bucket is fenced before its first read, and the
+        # model's bf16 weight copies are dropped when the gathers are issued.
+        self._gather_out: Dict[int, torch.Tensor] = {}
         if shard_optimizer and self.world > 1:
+            base = self.flat.data[True]
             for bi, (decay, a, b, _) in enumerate(self._buckets):
                 if decay and (b - a) % self.world == 0:
                     n = (b - a) // self.world
                     lo = a + self.rank * n
-                    self._shard[bi] = (self.flat.data[True][lo:lo + n],
-                                       torch.zeros(n, dtype=torch.float32, device=dev))
+                    self._shard[bi] = (base[lo:lo + n], torch.zeros(n, dtype=torch.float32, device=dev))
+                    self._gather_out[bi] = torch.empty(0, dtype=base.dtype, device=dev).set_(
+                        base.untyped_storage(), base.storage_offset() + a, (b - a,))
         if self._shard:
             decayed = []
             for bi, (decay, a, b, _) in enumerate(self._buckets):
@@ -216,8 +225,7 @@ class DataParallelTrainer:
             # every rank's updated slices back into the full masters, in the
             # order the next forward needs them (the reverse of the buckets')
             for bi in sorted(self._shard, reverse=True):
-                _, a, b, _ = self._buckets[bi]
-                self._gathers[bi] = dist.all_gather_into_tensor(self.flat.data[True][a:b], self._shard[bi][0],
+                self._gathers[bi] = dist.all_gather_into_tensor(self._gather_out[bi], self._shard[bi][0],
                                                                 group=self.group, async_op=True)
         if hasattr(self.model, "weights_changed"):
             self.model.weights_changed()
