@@ -17,9 +17,13 @@
 // to bf16 (the reference's dzb), into a slab-sized workspace; head_gemm_tc_kernel
 // then consumes the slab with both products on tcgen05 tensor cores in one
 // persistent launch: dE_slab = dz^T . h and dh += dz . E_slab (fp32
-// accumulation across slabs by TMA reduce-adds). At config 3 a slab is
-// 16384 x 4096 bf16 (134 MB, about the size of L2), so the products read it
-// mostly from L2.
+// accumulation across slabs by TMA reduce-adds). The slab width sets how
+// evenly the GEMM's tiles (dE tiles with the whole token reduction, four to
+// six times the work of a dh tile) fill 148 SMs: at config 3, 6656 columns
+// (8 slabs of 16384 x 6656 bf16, 218 MB) leave the last wave of each launch
+// ~95% full where 4096 columns (13 slabs) left ~84%; the dz slab then exceeds
+// L2, and the GEMM's second read of it comes partly from HBM, well within
+// the tensor-bound launch's bandwidth.
 #include <algorithm>
 #include <string>
 
@@ -236,7 +240,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
 }
 
 // ------------------------------------------------------------------ backward
-constexpr int kSlabCols = 4096;  // vocabulary columns per backward slab (16 forward tiles)
+constexpr int kSlabCols = 6656;  // vocabulary columns per backward slab (26 forward tiles)
 
 struct DzArgs {
   algx_head_config cfg;

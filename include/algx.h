@@ -214,7 +214,7 @@ ALGX_API int algx_head_finalize(const algx_head_config* cfg, const int32_t* targ
                                 float* stat, float* telemetry, float* objective, float* count,
                                 void* stream);
 
-/* Workspace bytes of algx_head_bwd: one bf16 dz slab of N x min(4096, V
+/* Workspace bytes of algx_head_bwd: one bf16 dz slab of N x min(6656, V
  * rounded up to 256), when dh is bf16 an fp32 dh accumulator, and 256 bytes
  * for the slab GEMM's tile counter. The reference writes dz for the whole
  * vocabulary (fused_head.py:194-216). */
@@ -222,7 +222,7 @@ ALGX_API size_t algx_head_bwd_workspace_size(int64_t N, int64_t d, int64_t V, in
 
 /* dh (N, d) in dh_dtype (partial over this rank's vocabulary rows) and
  * dembed (V, d) fp32, with scale = g * slope / count read from device
- * memory. The logits are recomputed one vocabulary slab of at most 4096
+ * memory. The logits are recomputed one vocabulary slab of at most 6656
  * columns at a time (never in full): a tcgen05 kernel writes the slab's
  * bf16 dz = scale * (softmax - y) or scale * (p - y) r into the workspace,
  * then one persistent tcgen05 GEMM launch computes dE_slab = dz^T . h and
