@@ -128,6 +128,22 @@ class ClockSampler:
                 "source": "NVML, 5 ms sampling inside the timed regions"}
 
 
+def gpu_local_cpus(device_index):
+    """The CPUs NVML reports as local to the GPU (its NUMA node), intersected
+    with this process's allowed CPUs; None when NVML cannot tell."""
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        props = torch.cuda.get_device_properties(device_index)
+        bus = f"{props.pci_domain_id:08X}:{props.pci_bus_id:02X}:{props.pci_device_id:02X}.0"
+        handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        words = pynvml.nvmlDeviceGetCpuAffinity(handle, (os.cpu_count() + 63) // 64)
+        cpus = {64 * w + b for w, m in enumerate(words) for b in range(64) if (int(m) >> b) & 1}
+        return (cpus & os.sched_getaffinity(0)) or None
+    except Exception:  # noqa: BLE001 - NVML missing or no affinity information
+        return None
+
+
 def cpu_baseline(budget_s=10.0):
     """The oracle's dense maths (torch-CPU fp32, all host threads) on whole heads of the workload."""
     from oracle import reference_math as R
@@ -513,7 +529,14 @@ def run_algx(args, rank, world, local_rank):
     bwd_ms = max_over_ranks(bwd_ms)
 
     trace("end to end")
-    # ---- end to end through the public API with pinned host buffers
+    # ---- end to end through the public API with pinned host buffers, placed
+    # (like a data loader's) on the GPU's NUMA node: the process runs on the
+    # GPU-local CPUs while the buffers are allocated and the steps run, so
+    # every copy takes the shortest host-memory path to the GPU's PCIe root
+    all_cpus = os.sched_getaffinity(0)
+    local_cpus = gpu_local_cpus(local_rank)
+    if local_cpus:
+        os.sched_setaffinity(0, local_cpus)
     hq, hk, hv, hdo = (t.cpu().pin_memory() for t in (q, k, v, do))
     hgq, hgk = gq.cpu().pin_memory(), gk.cpu().pin_memory()
     outs = [torch.empty((B, H, T, D), dtype=torch.bfloat16).pin_memory() for _ in range(4)]
@@ -579,6 +602,7 @@ def run_algx(args, rank, world, local_rank):
     if clocks:
         clocks.mark(w2, w3)
     e2e_ms = max_over_ranks(ev2.elapsed_time(ev3))
+    os.sched_setaffinity(0, all_cpus)
     lines = None if not args.lines else set(args.lines.split(","))
     extra = secondary(dev, rank, world, stream, sync_all, max_over_ranks, lines=lines) if not args.no_secondary else None
     trace("done")
@@ -605,7 +629,9 @@ def run_algx(args, rank, world, local_rank):
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms / args.steps,
                 "path": "qknorm_flash_attention (QK norm fused into the attention prologue) -> backward, pinned "
                         "host buffers; uploads of step i+1 and downloads of step i overlap step i on two copy "
-                        "streams"},
+                        "streams",
+                "host_cpus": (f"{len(local_cpus)} CPUs local to the GPU (NVML affinity); buffers allocated there"
+                              if local_cpus else "unbound (NVML gave no CPU affinity)")},
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                      "frac": achieved / peak_tf, "traffic": _traffic(),
                      "kernel": "backward launch group (di, tcgen05 attention bwd, fused QK-norm bwd epilogue)",
