@@ -14,7 +14,7 @@
 // kSlabCols columns at a time, so the logits are never materialised in full:
 // head_dz_tc_kernel recomputes the slab's logits with the forward's pipeline
 // and its epilogue writes dz = (softmax - y) or (p - y) r, scaled and rounded
-// to bf16 (the reference's dzb), into a slab-sized workspace; head_gemm_tc_kernel
+// to bf16 (the reference's dzb), into a slab-sized workspace; head_gemm_pair_kernel
 // then consumes the slab with both products on tcgen05 tensor cores in one
 // persistent launch: dE_slab = dz^T . h and dh += dz . E_slab (fp32
 // accumulation across slabs by TMA reduce-adds). The slab width sets how
@@ -413,25 +413,20 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
   if (warp == kHeadTma) tmem_dealloc(tmem_base, 512);
 }
 
-// ------------------------------------------------------------------ slab GEMMs
+// ------------------------------------------------------------------ slab GEMM
 // The two products of a backward slab on tcgen05 tensor cores, in one
-// persistent launch (one CTA per SM):
+// persistent launch:
 //   problem 0: dE_slab (vc x d) = dz^T . h   (A = dz read MN-major, B = h MN-major, K = N tokens)
 //   problem 1: dh (N x d) (+)= dz . E_slab  (A = dz K-major, B = E_slab MN-major, K = vc columns)
-// Output tiles of 128 x 256 fp32 are handed out by a global counter, the large
+// Output tiles of 256 x 256 fp32 are handed out by a global counter, the large
 // dE tiles (the whole token reduction) first and the dh tiles after them, so
-// the SMs that finish early take the remaining small tiles. A TMA warp streams
-// 64-wide K chunks of A and B through a 4-stage ring; one thread issues the
-// M=128, N=256, K=16 MMAs into two TMEM accumulators; two groups of four
-// epilogue warps take alternate tiles and move each accumulator out in
-// 32-column boxes (fp32, 128B-swizzled shared memory) with TMA stores, or
-// TMA reduce-adds for dh after the first slab (the fp32 sum across slabs).
-constexpr int kGemmBM = 128, kGemmBN = 256, kGemmStages = 4;
-constexpr int kGemmABytes = kGemmBM * 64 * 2;  // 16 KB
-constexpr int kGemmBBytes = kGemmBN * 64 * 2;  // 32 KB
-constexpr int kGemmStageBytes = kGemmABytes + kGemmBBytes;
+// the CTA pairs that finish early take the remaining small tiles. A TMA warp
+// streams 64-wide K chunks of A and B through a 6-stage ring; one thread
+// issues the MMAs into two TMEM accumulators; two groups of four epilogue
+// warps take alternate tiles and move each accumulator out in 32-column
+// boxes (fp32, 128B-swizzled shared memory) with TMA stores, or TMA
+// reduce-adds for dh after the first slab (the fp32 sum across slabs).
 constexpr int kGemmBoxBytes = 128 * 32 * 4;  // epilogue staging box: 128 rows x 32 fp32
-constexpr int kGemmSmem = kGemmStages * kGemmStageBytes + 2 * kGemmBoxBytes + 1024;
 constexpr int kGemmThreads = 320;  // 2 x 4 epilogue warps, TMA warp, MMA warp
 
 struct GemmProblem {
@@ -449,16 +444,35 @@ struct GemmArgs {
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
+// The kernel runs on CTA pairs (cta_group::2): a cluster of two CTAs
+// computes a 256 x 256 output tile with M = 256 products issued by the leader
+// (cluster rank 0). CTA r loads A rows m0 + 128 r .. and B columns n0 + 128 r ..
+// of each 64-wide K chunk into its own shared memory, so each SM reads and
+// receives half of B per product instead of all of it: shared-memory traffic
+// per product drops from ~192 to ~128 bytes per cycle, which is what bounds
+// the one-CTA kernel near 0.65 of the tensor peak. Each CTA's TMEM holds its
+// 128 rows of the two 256-column accumulators, and its epilogue writes them.
+// Hand-offs between the CTAs: the leader's producer takes tiles from the
+// global counter and publishes them in both CTAs' item queues; both CTAs'
+// loads complete on the leader's stage barrier (the leader expects both
+// halves' bytes); the leader's MMA thread frees each stage, and announces each
+// accumulator, with one commit to each CTA's barrier; both epilogues release
+// an accumulator by arriving on the leader's barrier.
+constexpr int kPairBM = 256, kPairBN = 256, kPairStages = 6;
+constexpr int kPairABytes = 128 * 64 * 2;  // this CTA's 128 rows of A x 64 K, 16 KB
+constexpr int kPairBBytes = 128 * 64 * 2;  // this CTA's 128 columns of B x 64 K, 16 KB
+constexpr int kPairStageBytes = kPairABytes + kPairBBytes;
+constexpr int kPairSmem = kPairStages * kPairStageBytes + 2 * kGemmBoxBytes + 1024;
 
-__global__ void __launch_bounds__(kGemmThreads, 1)
-    head_gemm_tc_kernel(const __grid_constant__ CUtensorMap ta0, const __grid_constant__ CUtensorMap tb0,
-                        const __grid_constant__ CUtensorMap tc0, const __grid_constant__ CUtensorMap ta1,
-                        const __grid_constant__ CUtensorMap tb1, const __grid_constant__ CUtensorMap tc1, GemmArgs g,
-                        int* dev_err) {
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+    head_gemm_pair_kernel(const __grid_constant__ CUtensorMap ta0, const __grid_constant__ CUtensorMap tb0,
+                          const __grid_constant__ CUtensorMap tc0, const __grid_constant__ CUtensorMap ta1,
+                          const __grid_constant__ CUtensorMap tb1, const __grid_constant__ CUtensorMap tc1,
+                          GemmArgs g, int* dev_err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1k(smem_raw);
-  uint8_t* sbox = smem + kGemmStages * kGemmStageBytes;  // two staging boxes, one per epilogue group
-  __shared__ uint64_t full[kGemmStages], empty[kGemmStages], acc_full[2], acc_empty[2];
+  uint8_t* sbox = smem + kPairStages * kPairStageBytes;  // two staging boxes, one per epilogue group
+  __shared__ uint64_t full[kPairStages], empty[kPairStages], acc_full[2], acc_empty[2];
   __shared__ uint64_t item_full[4], item_empty[4], issued;
   __shared__ int item_q[4];
   __shared__ uint32_t tmem_base;
@@ -466,17 +480,21 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   volatile int* abort_v = &abort_flag;
   volatile int* item_v = item_q;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
   const int total = g.p[0].tiles + g.p[1].tiles;
-  constexpr int kItemConsumers = 1 + 8;  // the MMA thread and the eight epilogue warps
+  // item-queue consumers, all arriving on the leader's barrier: per CTA the
+  // eight epilogue warps plus the MMA thread (leader) or the TMA thread (peer)
+  constexpr int kItemConsumers = 2 * (1 + 8);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < kGemmStages; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(&full[s], 1);   // the leader's expect-tx arrival (+ both CTAs' bytes)
+      mbar_init(&empty[s], 1);  // the leader's commit
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&acc_empty[b], 8);  // four epilogue warps of each CTA
     }
     for (int i = 0; i < 4; ++i) {
       mbar_init(&item_full[i], 1);
@@ -486,29 +504,29 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     fence_mbar_init();
     abort_flag = 0;
   }
-  if (warp == kHeadTma) {
-    tmem_alloc(&tmem_base, 512);
-    tmem_relinquish();
+  if (warp == kHeadTma) {  // the same warp of both CTAs allocates the pair's TMEM
+    tmem_alloc_pair(&tmem_base, 512);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
   __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers are initialised before any remote arrival
   tc_fence_after();
-  // the item queue: the TMA thread takes tiles from the global counter and
-  // publishes them in a 4-slot ring read by the MMA thread and the epilogues
+  const uint32_t item_empty0 = cluster_addr(&item_empty[0], 0);
   auto next_item = [&](int j, bool whole_warp) -> int {
     const int slot = j & 3;
-    const bool ok = whole_warp ? mbar_wait_warp(&item_full[slot], (j >> 2) & 1, abort_v, dev_err)
-                               : mbar_wait(&item_full[slot], (j >> 2) & 1, abort_v, dev_err);
+    const bool ok = whole_warp ? mbar_wait_cluster_warp(&item_full[slot], (j >> 2) & 1, abort_v, dev_err)
+                               : mbar_wait_cluster(&item_full[slot], (j >> 2) & 1, abort_v, dev_err);
     const int it = ok ? item_v[slot] : -1;
     if (whole_warp) __syncwarp();
-    if (!whole_warp || lane == 0) mbar_arrive(&item_empty[slot]);
+    if (!whole_warp || lane == 0) mbar_arrive_cluster(item_empty0 + slot * 8);
     return it;
   };
   auto decode = [&](int it, int& p, int& m0, int& n0) {
     p = it < g.p[0].tiles ? 0 : 1;
     const int t = it - (p ? g.p[0].tiles : 0);
-    m0 = (t / g.p[p].tiles_n) * kGemmBM;
-    n0 = (t % g.p[p].tiles_n) * kGemmBN;
+    m0 = (t / g.p[p].tiles_n) * kPairBM;
+    n0 = (t % g.p[p].tiles_n) * kPairBN;
   };
 
   if (warp == kHeadTma) {
@@ -517,58 +535,69 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       prefetch_tmap(&tb0);
       prefetch_tmap(&ta1);
       prefetch_tmap(&tb1);
+      const uint32_t full0 = cluster_addr(&full[0], 0);  // the leader's stage barriers
       int it_stage = 0;
-      int last_stage_it[kGemmStages] = {-1, -1, -1, -1};
+      int last_stage_it[kPairStages];
+      for (int s = 0; s < kPairStages; ++s) last_stage_it[s] = -1;
       bool ok = true;
       for (int j = 0; ok; ++j) {
-        const int slot = j & 3;
-        if (j >= 4 && !mbar_wait(&item_empty[slot], ((j >> 2) - 1) & 1, abort_v, dev_err)) break;
-        int it = atomicAdd(g.counter, 1);
-        if (it >= total) it = -1;
-        item_v[slot] = it;
-        mbar_arrive(&item_full[slot]);  // release: the tile index is visible to the waiters
+        int it;
+        if (leader) {
+          // take the next tile and publish it in both CTAs' queues
+          const int slot = j & 3;
+          if (j >= 4 && !mbar_wait_cluster(&item_empty[slot], ((j >> 2) - 1) & 1, abort_v, dev_err)) break;
+          it = atomicAdd(g.counter, 1);
+          if (it >= total) it = -1;
+          item_v[slot] = it;
+          st_cluster_u32(cluster_addr(&item_q[slot], 1), (uint32_t)it);
+          mbar_arrive(&item_full[slot]);
+          mbar_arrive_cluster(cluster_addr(&item_full[slot], 1));  // release: the peer's copy is visible
+        } else {
+          it = next_item(j, false);
+        }
         if (it < 0) break;
         int p, m0, n0;
         decode(it, p, m0, n0);
         const GemmProblem& P = g.p[p];
         const CUtensorMap* tA = p ? &ta1 : &ta0;
         const CUtensorMap* tB = p ? &tb1 : &tb0;
+        const int ma = m0 + 128 * (int)rank, nb = n0 + 128 * (int)rank;  // this CTA's halves
         for (int kc = 0; kc < P.kchunks; ++kc, ++it_stage) {
-          const int s = it_stage % kGemmStages;
-          if (it_stage >= kGemmStages &&
-              !mbar_wait(&empty[s], ((it_stage / kGemmStages) - 1) & 1, abort_v, dev_err)) {
+          const int s = it_stage % kPairStages;
+          if (it_stage >= kPairStages &&
+              !mbar_wait_cluster(&empty[s], ((it_stage / kPairStages) - 1) & 1, abort_v, dev_err)) {
             ok = false;
             break;
           }
-          uint8_t* sa = smem + s * kGemmStageBytes;
-          uint8_t* sb = sa + kGemmABytes;
-          mbar_expect_tx(&full[s], kGemmStageBytes);
+          uint8_t* sa = smem + s * kPairStageBytes;
+          uint8_t* sb = sa + kPairABytes;
+          if (leader) mbar_expect_tx(&full[s], 2 * kPairStageBytes);  // both CTAs' halves
+          const uint32_t fb = full0 + s * 8;
           const int k0 = kc * 64;
           if (P.a_mn) {  // [K][M] in memory: two 64-wide M chunks of 64 K rows
-            tma_load_2d(sa, tA, &full[s], m0, k0);
-            tma_load_2d(sa + kGemmABytes / 2, tA, &full[s], m0 + 64, k0);
+            tma_load_2d_pair(sa, tA, fb, ma, k0);
+            tma_load_2d_pair(sa + kPairABytes / 2, tA, fb, ma + 64, k0);
           } else {  // [M][K]: one box of 128 rows x 64 K
-            tma_load_2d(sa, tA, &full[s], k0, m0);
+            tma_load_2d_pair(sa, tA, fb, k0, ma);
           }
-          if (P.b_mn) {  // [K][N]: four 64-wide N chunks of 64 K rows
-#pragma unroll
-            for (int c = 0; c < 4; ++c) tma_load_2d(sb + c * (kGemmBBytes / 4), tB, &full[s], n0 + 64 * c, k0);
-          } else {
-            tma_load_2d(sb, tB, &full[s], k0, n0);
-          }
+          // B is [K][N] (MN-major) in both problems: two 64-wide N chunks
+          tma_load_2d_pair(sb, tB, fb, nb, k0);
+          tma_load_2d_pair(sb + kPairBBytes / 2, tB, fb, nb + 64, k0);
           last_stage_it[s] = it_stage;
         }
       }
-      if (*abort_v)
-        for (int s = 0; s < kGemmStages; ++s)
+      if (*abort_v && leader)  // let copies in flight land (the leader's barriers count both CTAs')
+        for (int s = 0; s < kPairStages; ++s)
           if (last_stage_it[s] >= 0) {
             volatile int quiet = 0;
-            mbar_wait(&full[s], (last_stage_it[s] / kGemmStages) & 1, &quiet, nullptr);
+            mbar_wait_cluster(&full[s], (last_stage_it[s] / kPairStages) & 1, &quiet, nullptr);
           }
     }
   } else if (warp == kHeadTma + 1) {
-    if (lane == 0) {
+    if (lane == 0 && leader) {
       const uint32_t s0 = smem_u32(smem);
+      const uint32_t empty0 = cluster_addr(&empty[0], 0), empty1 = cluster_addr(&empty[0], 1);
+      const uint32_t accf0 = cluster_addr(&acc_full[0], 0), accf1 = cluster_addr(&acc_full[0], 1);
       int it_stage = 0;
       bool ok = true;
       for (int j = 0; ok; ++j) {
@@ -577,40 +606,47 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         int p, m0, n0;
         decode(it, p, m0, n0);
         const GemmProblem& P = g.p[p];
-        const uint32_t id = idesc_bf16_f32(kGemmBM, kGemmBN, P.a_mn, P.b_mn);
+        const uint32_t id = idesc_bf16_f32(kPairBM, kPairBN, P.a_mn, 1);
         const int buf = j & 1, use = j >> 1;
-        if (use > 0 && !mbar_wait(&acc_empty[buf], (use - 1) & 1, abort_v, dev_err)) break;
+        if (use > 0 && !mbar_wait_cluster(&acc_empty[buf], (use - 1) & 1, abort_v, dev_err)) break;
         tc_fence_after();
-        const uint32_t acc = tmem_base + buf * kGemmBN;
+        const uint32_t acc = tmem_base + buf * kPairBN;
         for (int kc = 0; kc < P.kchunks; ++kc, ++it_stage) {
-          const int s = it_stage % kGemmStages;
-          if (!mbar_wait(&full[s], (it_stage / kGemmStages) & 1, abort_v, dev_err)) {
+          const int s = it_stage % kPairStages;
+          if (!mbar_wait_cluster(&full[s], (it_stage / kPairStages) & 1, abort_v, dev_err)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sa = s0 + s * kGemmStageBytes, sb = sa + kGemmABytes;
+          const uint32_t sa = s0 + s * kPairStageBytes, sb = sa + kPairABytes;
 #pragma unroll
           for (int k = 0; k < 4; ++k) {
-            const uint64_t ad = P.a_mn ? desc_sw128(sa + k * 2048, kGemmABytes / 2, 1024) : desc_sw128(sa + k * 32, 16, 1024);
-            const uint64_t bd = P.b_mn ? desc_sw128(sb + k * 2048, kGemmBBytes / 4, 1024) : desc_sw128(sb + k * 32, 16, 1024);
-            mma_ss(acc, ad, bd, id, (kc > 0 || k > 0));
+            const uint64_t ad = P.a_mn ? desc_sw128(sa + k * 2048, kPairABytes / 2, 1024)
+                                       : desc_sw128(sa + k * 32, 16, 1024);
+            const uint64_t bd = desc_sw128(sb + k * 2048, kPairBBytes / 2, 1024);
+            mma_ss_pair(acc, ad, bd, id, (kc > 0 || k > 0));
           }
-          mma_commit(&empty[s]);
+          mma_commit_pair(empty0 + s * 8);  // the stage is free again in both CTAs
+          mma_commit_pair(empty1 + s * 8);
         }
-        if (ok) mma_commit(&acc_full[buf]);
+        if (ok) {
+          mma_commit_pair(accf0 + buf * 8);
+          mma_commit_pair(accf1 + buf * 8);
+        }
       }
-      mma_commit(&issued);  // settle: every product of this thread completed before TMEM is freed
+      mma_commit_pair(cluster_addr(&issued, 0));  // settle before TMEM is freed
       volatile int quiet = 0;
-      mbar_wait(&issued, 0, &quiet, dev_err);
+      mbar_wait_cluster(&issued, 0, &quiet, dev_err);
     }
   } else {
-    // epilogue group eg = warp / 4 takes the items j with j % 2 == eg; thread r owns row r
+    // epilogue group eg = warp / 4 takes the items j with j % 2 == eg; thread r
+    // owns row r of this CTA's half of the tile
     const int eg = warp >> 2;
     const int r = (warp & 3) * 32 + lane;
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
     uint8_t* box = sbox + eg * kGemmBoxBytes;
     const bool issuer = (warp & 3) == 0 && lane == 0;
+    const uint32_t acce0 = cluster_addr(&acc_empty[0], 0);
     for (int j = 0;; ++j) {
       const int it = next_item(j, true);
       if (it < 0) break;
@@ -620,17 +656,18 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const CUtensorMap* tC = p ? &tc1 : &tc0;
       const bool add = g.p[p].add != 0;
       const int use = j >> 1;
-      if (!mbar_wait_warp(&acc_full[eg], use & 1, abort_v, dev_err)) break;
+      const int mrow = m0 + 128 * (int)rank;
+      if (!mbar_wait_cluster_warp(&acc_full[eg], use & 1, abort_v, dev_err)) break;
       tc_fence_after();
-      const uint32_t acc = tmem_base + eg * kGemmBN + lane_off;
+      const uint32_t acc = tmem_base + eg * kPairBN + lane_off;
 #pragma unroll 1
-      for (int c = 0; c < kGemmBN / 32; ++c) {
+      for (int c = 0; c < kPairBN / 32; ++c) {
         uint32_t v[32];
         tmem_ld32(acc + 32 * c, v);
-        if (c == kGemmBN / 32 - 1) {  // the accumulator is read: the next tile may overwrite it
+        if (c == kPairBN / 32 - 1) {  // the accumulator is read: the next tile may overwrite it
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&acc_empty[eg]);
+          if (lane == 0) mbar_arrive_cluster(acce0 + eg * 8);
         }
         if (issuer) bulk_wait_group_read0();  // the previous box has been read by its TMA
         named_bar_sync(1 + eg, 128);
@@ -642,9 +679,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         named_bar_sync(1 + eg, 128);
         if (issuer) {
           if (add)
-            tma_reduce_add_2d(tC, box, n0 + 32 * c, m0);
+            tma_reduce_add_2d(tC, box, n0 + 32 * c, mrow);
           else
-            tma_store_2d(tC, box, n0 + 32 * c, m0);
+            tma_store_2d(tC, box, n0 + 32 * c, mrow);
           bulk_commit_group();
         }
       }
@@ -653,7 +690,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == kHeadTma) tmem_dealloc(tmem_base, 512);
+  cluster_sync_all();  // the leader's last products (which read this CTA's shared memory) are done
+  tc_fence_after();
+  if (warp == kHeadTma) tmem_dealloc_pair(tmem_base, 512);
 }
 
 __global__ void f32_to_bf16_kernel(const float4* __restrict__ in, uint2* __restrict__ out, int64_t n4) {
@@ -796,16 +835,16 @@ int64_t slab_cols(int64_t V) {
   return std::min<int64_t>(kSlabCols, vt);
 }
 
-int launch_gemm(const CUtensorMap (&maps)[6], const GemmArgs& a, cudaStream_t st) {
+int launch_gemm_pair(const CUtensorMap (&maps)[6], const GemmArgs& a, cudaStream_t st) {
   int dev = 0, sms = 0;
   ALGX_CUDA(cudaGetDevice(&dev));
   ALGX_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const int total = a.p[0].tiles + a.p[1].tiles;
-  const unsigned grid = (unsigned)std::max(1, std::min(total, sms));  // persistent: one CTA per SM
-  ALGX_CUDA(cudaFuncSetAttribute(head_gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGemmSmem));
-  head_gemm_tc_kernel<<<grid, kGemmThreads, kGemmSmem, st>>>(maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], a,
-                                                             device_error_word());
-  ALGX_LAUNCHED("head_gemm_tc launch");
+  const unsigned pairs = (unsigned)std::max(1, std::min(total, sms / 2));  // persistent: one pair per two SMs
+  ALGX_CUDA(cudaFuncSetAttribute(head_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmem));
+  head_gemm_pair_kernel<<<2 * pairs, kGemmThreads, kPairSmem, st>>>(maps[0], maps[1], maps[2], maps[3], maps[4],
+                                                                    maps[5], a, device_error_word());
+  ALGX_LAUNCHED("head_gemm_pair launch");
   return ALGX_OK;
 }
 
@@ -893,7 +932,7 @@ int algx_head_bwd(const algx_head_config* cfg, const void* h, const void* embed,
                                         256);
   const int tb = (int)((N + 127) / 128);
   const int ntiles_total = (int)((V + kFwdNT - 1) / kFwdNT);
-  const int tiles_n = (int)((d + kGemmBN - 1) / kGemmBN);
+  const int tiles_n = (int)((d + kPairBN - 1) / kPairBN);
   for (int64_t c0 = 0; c0 < V; c0 += vs) {
     const int64_t vc = std::min<int64_t>(vs, V - c0);  // valid columns of this slab
     DzArgs a{*cfg, targets, stat, scale, (int)N, (int)d, (int)V, (int)vocab_offset, (int)(c0 / kFwdNT), 0, 0, (int)vs};
@@ -908,20 +947,22 @@ int algx_head_bwd(const algx_head_config* cfg, const void* h, const void* embed,
     if ((s = make_tmap_2d(&maps[0], dz, ALGX_BF16, (uint64_t)vc, (uint64_t)N, (uint64_t)vs * 2, 64, 64, true))) return s;
     if ((s = make_tmap_2d(&maps[1], h, ALGX_BF16, (uint64_t)d, (uint64_t)N, (uint64_t)d * 2, 64, 64, true))) return s;
     if ((s = make_tmap_2d(&maps[2], dembed + (size_t)c0 * d, ALGX_F32, (uint64_t)d, (uint64_t)vc, (uint64_t)d * 4, 32,
-                          kGemmBM, true)))
+                          128, true)))
       return s;
-    if ((s = make_tmap_2d(&maps[3], dz, ALGX_BF16, (uint64_t)vc, (uint64_t)N, (uint64_t)vs * 2, 64, kGemmBM, true)))
+    if ((s = make_tmap_2d(&maps[3], dz, ALGX_BF16, (uint64_t)vc, (uint64_t)N, (uint64_t)vs * 2, 64, 128, true)))
       return s;
     if ((s = make_tmap_2d(&maps[4], eslab, ALGX_BF16, (uint64_t)d, (uint64_t)vc, (uint64_t)d * 2, 64, 64, true)))
       return s;
-    if ((s = make_tmap_2d(&maps[5], dh_acc, ALGX_F32, (uint64_t)d, (uint64_t)N, (uint64_t)d * 4, 32, kGemmBM, true)))
+    if ((s = make_tmap_2d(&maps[5], dh_acc, ALGX_F32, (uint64_t)d, (uint64_t)N, (uint64_t)d * 4, 32, 128, true)))
       return s;
     GemmArgs ga;
-    ga.p[0] = GemmProblem{1, 1, 0, tiles_n, (int)((vc + kGemmBM - 1) / kGemmBM) * tiles_n, (int)((N + 63) / 64)};
-    ga.p[1] = GemmProblem{0, 1, c0 > 0 ? 1 : 0, tiles_n, tb * tiles_n, (int)((vc + 63) / 64)};
+    // 256-row tiles of CTA pairs; B (h for dE, E_slab for dh) is read MN-major in both problems
+    ga.p[0] = GemmProblem{1, 1, 0, tiles_n, (int)((vc + kPairBM - 1) / kPairBM) * tiles_n, (int)((N + 63) / 64)};
+    ga.p[1] = GemmProblem{0, 1, c0 > 0 ? 1 : 0, tiles_n, (int)((N + kPairBM - 1) / kPairBM) * tiles_n,
+                          (int)((vc + 63) / 64)};
     ga.counter = counter;
     ALGX_CUDA(cudaMemsetAsync(counter, 0, sizeof(int), st));
-    if ((s = launch_gemm(maps, ga, st))) return s;
+    if ((s = launch_gemm_pair(maps, ga, st))) return s;
   }
   if (dh_dtype == ALGX_BF16) {
     const int64_t n4 = N * d / 4;
