@@ -40,9 +40,16 @@ constexpr int kRowsT = 128;
 constexpr int kChunkBytes = 128 * 64 * 2;  // 128 rows x 64 bf16, one SW128 box
 
 // ------------------------------------------------------------------ forward
+// The forward and the dz recompute run on CTA pairs (clusters of two,
+// cta_group::2), like the slab GEMM: a pair computes 256 tokens x 256
+// vocabulary columns per tile with M = 256 products issued by the leader
+// (cluster rank 0); CTA r holds token rows 128 r.. (its own TMEM lanes) and
+// loads its 128 tokens of h and 128 of the tile's 256 E rows per 64-wide K
+// chunk, both CTAs' loads completing on the leader's stage barrier. Each
+// CTA's epilogue reads its 128 rows x 256 columns of the accumulator.
 constexpr int kFwdNT = 256;     // vocabulary columns per tile
-constexpr int kFwdStages = 4;
-constexpr int kFwdStageBytes = kChunkBytes + kFwdNT * 64 * 2;  // h chunk + E chunk
+constexpr int kFwdStages = 6;
+constexpr int kFwdStageBytes = kChunkBytes + 128 * 64 * 2;  // this CTA's h chunk + half of the E chunk
 constexpr int kFwdSmem = kFwdStages * kFwdStageBytes + 1024;
 constexpr int kHeadThreads = 320;  // 2 x 4 epilogue warps, TMA warp, MMA warp
 constexpr int kHeadTma = 8;
@@ -62,19 +69,19 @@ struct HeadArgs {
 };
 
 template <int KIND, int NPOW>
-__global__ void __launch_bounds__(kHeadThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kHeadThreads, 1)
     head_fwd_tc_kernel(const __grid_constant__ CUtensorMap th, const __grid_constant__ CUtensorMap te, HeadArgs a,
                        float* __restrict__ part_m, float* __restrict__ part_l, float* __restrict__ part_zt,
                        int* dev_err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1k(smem_raw);
-  __shared__ uint64_t full[kFwdStages], empty[kFwdStages], acc_full[2], acc_empty[2], x_ready;
+  __shared__ uint64_t full[kFwdStages], empty[kFwdStages], acc_full[2], acc_empty[2], x_ready, issued;
   __shared__ float xm[kRowsT], xl[kRowsT], xz[kRowsT];  // statistics of epilogue group 1
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
   volatile int* abort_v = &abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tb = blockIdx.x, split = blockIdx.y;
+  const int tb = blockIdx.x, split = blockIdx.y;  // pairs are consecutive token blocks
   const int ntiles = (a.V + kFwdNT - 1) / kFwdNT;
   const int per = (ntiles + a.splits - 1) / a.splits;
   const int t0 = split * per, t1 = min(ntiles, t0 + per);
@@ -87,19 +94,24 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&acc_empty[b], 8);  // four epilogue warps of each CTA of the pair
     }
     mbar_init(&x_ready, 4);
+    mbar_init(&issued, 1);
     fence_mbar_init();
     abort_flag = 0;
   }
-  if (warp == kHeadTma) {
-    tmem_alloc(&tmem_base, 512);
-    tmem_relinquish();
+  if (warp == kHeadTma) {  // the same warp of both CTAs allocates the pair's TMEM
+    tmem_alloc_pair(&tmem_base, 512);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
   __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers are initialised before any remote arrival
   tc_fence_after();
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const uint32_t full0 = cluster_addr(&full[0], 0);
 
   if (warp == kHeadTma) {
     if (lane == 0 && t0 < t1) {
@@ -110,34 +122,37 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
       for (int t = t0; t < t1 && !*abort_v; ++t)
         for (int kc = 0; kc < nk; ++kc, ++it) {
           const int s = it % kFwdStages;
-          if (it >= kFwdStages && !mbar_wait(&empty[s], ((it / kFwdStages) - 1) & 1, abort_v, dev_err)) break;
+          if (it >= kFwdStages && !mbar_wait_cluster(&empty[s], ((it / kFwdStages) - 1) & 1, abort_v, dev_err))
+            break;
           uint8_t* st = smem + s * kFwdStageBytes;
-          mbar_expect_tx(&full[s], kFwdStageBytes);
-          tma_load_2d(st, &th, &full[s], kc * 64, tb * kRowsT);
-          tma_load_2d(st + kChunkBytes, &te, &full[s], kc * 64, t * kFwdNT);
+          if (leader) mbar_expect_tx(&full[s], 2 * kFwdStageBytes);  // both CTAs' halves
+          tma_load_2d_pair(st, &th, full0 + s * 8, kc * 64, tb * kRowsT);
+          tma_load_2d_pair(st + kChunkBytes, &te, full0 + s * 8, kc * 64, t * kFwdNT + 128 * (int)rank);
           last_stage_it[s] = it;
         }
-      if (*abort_v)
+      if (*abort_v && leader)
         for (int s = 0; s < kFwdStages; ++s)
           if (last_stage_it[s] >= 0) {
             volatile int quiet = 0;
-            mbar_wait(&full[s], (last_stage_it[s] / kFwdStages) & 1, &quiet, nullptr);
+            mbar_wait_cluster(&full[s], (last_stage_it[s] / kFwdStages) & 1, &quiet, nullptr);
           }
     }
   } else if (warp == kHeadTma + 1) {
-    if (lane == 0 && t0 < t1) {
-      const uint32_t id = idesc_bf16_f32(128, kFwdNT, 0, 0);
+    if (lane == 0 && t0 < t1 && leader) {
+      const uint32_t id = idesc_bf16_f32(256, kFwdNT, 0, 0);
+      const uint32_t empty0 = cluster_addr(&empty[0], 0), empty1 = cluster_addr(&empty[0], 1);
+      const uint32_t accf0 = cluster_addr(&acc_full[0], 0), accf1 = cluster_addr(&acc_full[0], 1);
       const uint32_t s0 = smem_u32(smem);
       int it = 0;
       bool ok = true;
       for (int t = t0; ok && t < t1; ++t) {
         const int buf = (t - t0) & 1, use = (t - t0) >> 1;
-        if (use > 0 && !mbar_wait(&acc_empty[buf], (use - 1) & 1, abort_v, dev_err)) break;
+        if (use > 0 && !mbar_wait_cluster(&acc_empty[buf], (use - 1) & 1, abort_v, dev_err)) break;
         tc_fence_after();
         const uint32_t acc = tmem_base + buf * kFwdNT;
         for (int kc = 0; kc < nk; ++kc, ++it) {
           const int s = it % kFwdStages;
-          if (!mbar_wait(&full[s], (it / kFwdStages) & 1, abort_v, dev_err)) {
+          if (!mbar_wait_cluster(&full[s], (it / kFwdStages) & 1, abort_v, dev_err)) {
             ok = false;
             break;
           }
@@ -145,11 +160,19 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
           const uint32_t hb = s0 + s * kFwdStageBytes, eb = hb + kChunkBytes;
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            mma_ss(acc, desc_sw128(hb + k * 32, 16, 1024), desc_sw128(eb + k * 32, 16, 1024), id, (kc > 0 || k > 0));
-          mma_commit(&empty[s]);
+            mma_ss_pair(acc, desc_sw128(hb + k * 32, 16, 1024), desc_sw128(eb + k * 32, 16, 1024), id,
+                        (kc > 0 || k > 0));
+          mma_commit_pair(empty0 + s * 8);  // the stage is free again in both CTAs
+          mma_commit_pair(empty1 + s * 8);
         }
-        if (ok) mma_commit(&acc_full[buf]);
+        if (ok) {
+          mma_commit_pair(accf0 + buf * 8);
+          mma_commit_pair(accf1 + buf * 8);
+        }
       }
+      mma_commit_pair(cluster_addr(&issued, 0));  // settle before TMEM is freed
+      volatile int quiet = 0;
+      mbar_wait_cluster(&issued, 0, &quiet, dev_err);
     }
   } else {
     // epilogue: two groups of four warps take alternate tiles (group g owns
@@ -164,7 +187,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
     const float log2e = 1.4426950408889634f;
     for (int t = t0 + g; t < t1; t += 2) {
       const int buf = g, use = (t - t0) >> 1;
-      if (!mbar_wait_warp(&acc_full[buf], use & 1, abort_v, dev_err)) break;
+      if (!mbar_wait_cluster_warp(&acc_full[buf], use & 1, abort_v, dev_err)) break;
       tc_fence_after();
       const uint32_t acc = tmem_base + buf * kFwdNT + lane_off;
       const int cbase = t * kFwdNT;
@@ -209,7 +232,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      if (lane == 0) mbar_arrive_cluster(cluster_addr(&acc_empty[buf], 0));  // the leader's barrier
     }
     // group 1 hands its statistics to group 0, which merges and writes them
     if (g == 1) {
@@ -236,7 +259,9 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == kHeadTma) tmem_dealloc(tmem_base, 512);
+  cluster_sync_all();  // the leader's last products (which read this CTA's shared memory) are done
+  tc_fence_after();
+  if (warp == kHeadTma) tmem_dealloc_pair(tmem_base, 512);
 }
 
 // ------------------------------------------------------------------ backward
@@ -250,30 +275,30 @@ struct DzArgs {
   int N, d, V, voff;
   int tile0;           // first (local) vocabulary tile of the slab
   int ntiles;          // tiles in the slab
-  int items;           // (128-token block, tile) work items of the slab: blocks x ntiles
+  int items;           // (256-token block, tile) work items of the slab: blocks x ntiles
   int ldz;             // row stride of the dz slab (elements)
 };
 
 // Logits of one slab with the forward's load / MMA pipeline; the epilogue
 // (thread = token) turns each fp32 logit into bf16 dz and stores its row
 // segment of the slab. Columns past the vocabulary and ignored rows give 0.
-// Persistent: one CTA per SM takes the work items blockIdx.x, +gridDim.x, ...
-// (item i = token block i / ntiles, tile i % ntiles), so the load ring and
-// the two TMEM accumulators run on across items and every SM gets an equal
-// share of the slab's items.
+// Persistent: CTA pair p takes the work items p, p + pairs, ... (item i =
+// 256-token block i / ntiles, tile i % ntiles; CTA r of the pair holds token
+// block 2 (i / ntiles) + r), so the load ring and the two TMEM accumulators
+// run on across items and every pair gets an equal share of the slab's items.
 template <int KIND, int NPOW>
-__global__ void __launch_bounds__(kHeadThreads, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kHeadThreads, 1)
     head_dz_tc_kernel(const __grid_constant__ CUtensorMap th, const __grid_constant__ CUtensorMap te, DzArgs a,
                       __nv_bfloat16* __restrict__ dz, int* dev_err) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1k(smem_raw);
-  __shared__ uint64_t full[kFwdStages], empty[kFwdStages], acc_full[2], acc_empty[2];
+  __shared__ uint64_t full[kFwdStages], empty[kFwdStages], acc_full[2], acc_empty[2], issued;
   __shared__ uint32_t tmem_base;
   __shared__ int abort_flag;
   volatile int* abort_v = &abort_flag;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nk = a.d / 64;
-  const int first = blockIdx.x, stride = gridDim.x;
+  const int first = blockIdx.x >> 1, stride = gridDim.x >> 1;  // pair items
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kFwdStages; ++s) {
@@ -282,18 +307,23 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4);
+      mbar_init(&acc_empty[b], 8);  // four epilogue warps of each CTA of the pair
     }
+    mbar_init(&issued, 1);
     fence_mbar_init();
     abort_flag = 0;
   }
-  if (warp == kHeadTma) {
-    tmem_alloc(&tmem_base, 512);
-    tmem_relinquish();
+  if (warp == kHeadTma) {  // the same warp of both CTAs allocates the pair's TMEM
+    tmem_alloc_pair(&tmem_base, 512);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
   __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers are initialised before any remote arrival
   tc_fence_after();
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const uint32_t full0 = cluster_addr(&full[0], 0);
 
   if (warp == kHeadTma) {
     if (lane == 0 && first < a.items) {
@@ -302,38 +332,41 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
       int it = 0;
       int last_stage_it[kFwdStages] = {-1, -1, -1, -1};
       for (int i = first; i < a.items && !*abort_v; i += stride) {
-        const int tb = i / a.ntiles, t = a.tile0 + i % a.ntiles;
+        const int tb = 2 * (i / a.ntiles) + (int)rank, t = a.tile0 + i % a.ntiles;
         for (int kc = 0; kc < nk; ++kc, ++it) {
           const int s = it % kFwdStages;
-          if (it >= kFwdStages && !mbar_wait(&empty[s], ((it / kFwdStages) - 1) & 1, abort_v, dev_err)) break;
+          if (it >= kFwdStages && !mbar_wait_cluster(&empty[s], ((it / kFwdStages) - 1) & 1, abort_v, dev_err))
+            break;
           uint8_t* st = smem + s * kFwdStageBytes;
-          mbar_expect_tx(&full[s], kFwdStageBytes);
-          tma_load_2d(st, &th, &full[s], kc * 64, tb * kRowsT);
-          tma_load_2d(st + kChunkBytes, &te, &full[s], kc * 64, t * kFwdNT);
+          if (leader) mbar_expect_tx(&full[s], 2 * kFwdStageBytes);  // both CTAs' halves
+          tma_load_2d_pair(st, &th, full0 + s * 8, kc * 64, tb * kRowsT);
+          tma_load_2d_pair(st + kChunkBytes, &te, full0 + s * 8, kc * 64, t * kFwdNT + 128 * (int)rank);
           last_stage_it[s] = it;
         }
       }
-      if (*abort_v)
+      if (*abort_v && leader)
         for (int s = 0; s < kFwdStages; ++s)
           if (last_stage_it[s] >= 0) {
             volatile int quiet = 0;
-            mbar_wait(&full[s], (last_stage_it[s] / kFwdStages) & 1, &quiet, nullptr);
+            mbar_wait_cluster(&full[s], (last_stage_it[s] / kFwdStages) & 1, &quiet, nullptr);
           }
     }
   } else if (warp == kHeadTma + 1) {
-    if (lane == 0 && first < a.items) {
-      const uint32_t id = idesc_bf16_f32(128, kFwdNT, 0, 0);
+    if (lane == 0 && first < a.items && leader) {
+      const uint32_t id = idesc_bf16_f32(256, kFwdNT, 0, 0);
+      const uint32_t empty0 = cluster_addr(&empty[0], 0), empty1 = cluster_addr(&empty[0], 1);
+      const uint32_t accf0 = cluster_addr(&acc_full[0], 0), accf1 = cluster_addr(&acc_full[0], 1);
       const uint32_t s0 = smem_u32(smem);
       int it = 0;
       bool ok = true;
       for (int i = first, li = 0; ok && i < a.items; i += stride, ++li) {
         const int buf = li & 1, use = li >> 1;
-        if (use > 0 && !mbar_wait(&acc_empty[buf], (use - 1) & 1, abort_v, dev_err)) break;
+        if (use > 0 && !mbar_wait_cluster(&acc_empty[buf], (use - 1) & 1, abort_v, dev_err)) break;
         tc_fence_after();
         const uint32_t acc = tmem_base + buf * kFwdNT;
         for (int kc = 0; kc < nk; ++kc, ++it) {
           const int s = it % kFwdStages;
-          if (!mbar_wait(&full[s], (it / kFwdStages) & 1, abort_v, dev_err)) {
+          if (!mbar_wait_cluster(&full[s], (it / kFwdStages) & 1, abort_v, dev_err)) {
             ok = false;
             break;
           }
@@ -341,11 +374,19 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
           const uint32_t hb = s0 + s * kFwdStageBytes, eb = hb + kChunkBytes;
 #pragma unroll
           for (int k = 0; k < 4; ++k)
-            mma_ss(acc, desc_sw128(hb + k * 32, 16, 1024), desc_sw128(eb + k * 32, 16, 1024), id, (kc > 0 || k > 0));
-          mma_commit(&empty[s]);
+            mma_ss_pair(acc, desc_sw128(hb + k * 32, 16, 1024), desc_sw128(eb + k * 32, 16, 1024), id,
+                        (kc > 0 || k > 0));
+          mma_commit_pair(empty0 + s * 8);  // the stage is free again in both CTAs
+          mma_commit_pair(empty1 + s * 8);
         }
-        if (ok) mma_commit(&acc_full[buf]);
+        if (ok) {
+          mma_commit_pair(accf0 + buf * 8);
+          mma_commit_pair(accf1 + buf * 8);
+        }
       }
+      mma_commit_pair(cluster_addr(&issued, 0));  // settle before TMEM is freed
+      volatile int quiet = 0;
+      mbar_wait_cluster(&issued, 0, &quiet, dev_err);
     }
   } else {
     // epilogue: two groups of four warps take alternate items (group g owns
@@ -358,7 +399,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
     const float scale = *a.scale;
     const float log2e = 1.4426950408889634f;
     for (int i = first + g * stride, li = g; i < a.items; i += 2 * stride, li += 2) {
-      const int tb = i / a.ntiles, t = a.tile0 + i % a.ntiles;
+      const int tb = 2 * (i / a.ntiles) + (int)rank, t = a.tile0 + i % a.ntiles;
       const int tok = tb * kRowsT + r;
       const int tgt = tok < a.N ? a.targets[tok] : -2147483647 - 1;
       const bool row_ok = tok < a.N && !(c.has_ignore && tgt == c.ignore_index);
@@ -367,7 +408,7 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
       const float stl = st * log2e;
       __nv_bfloat16* drow = dz + (size_t)tok * a.ldz - (size_t)a.tile0 * kFwdNT;
       const int buf = g, use = li >> 1;
-      if (!mbar_wait_warp(&acc_full[buf], use & 1, abort_v, dev_err)) break;
+      if (!mbar_wait_cluster_warp(&acc_full[buf], use & 1, abort_v, dev_err)) break;
       tc_fence_after();
       const uint32_t acc = tmem_base + buf * kFwdNT + lane_off;
 #pragma unroll 1
@@ -405,12 +446,14 @@ __global__ void __launch_bounds__(kHeadThreads, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      if (lane == 0) mbar_arrive_cluster(cluster_addr(&acc_empty[buf], 0));  // the leader's barrier
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == kHeadTma) tmem_dealloc(tmem_base, 512);
+  cluster_sync_all();  // the leader's last products (which read this CTA's shared memory) are done
+  tc_fence_after();
+  if (warp == kHeadTma) tmem_dealloc_pair(tmem_base, 512);
 }
 
 // ------------------------------------------------------------------ slab GEMM
@@ -794,7 +837,7 @@ int launch_fwd_k(const CUtensorMap& th, const CUtensorMap& te, const HeadArgs& a
                  float* pz, cudaStream_t st) {
   auto run = [&](auto kern) -> int {
     ALGX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem));
-    kern<<<dim3(tb, a.splits), kHeadThreads, kFwdSmem, st>>>(th, te, a, pm, pl, pz, device_error_word());
+    kern<<<dim3(tb, a.splits), kHeadThreads, kFwdSmem, st>>>(th, te, a, pm, pl, pz, device_error_word());  // tb even
     ALGX_LAUNCHED("head_fwd_tc launch");
     return ALGX_OK;
   };
@@ -813,7 +856,7 @@ int launch_dz_k(const CUtensorMap& th, const CUtensorMap& te, const DzArgs& a, _
   int dev = 0, sms = 0;
   ALGX_CUDA(cudaGetDevice(&dev));
   ALGX_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  const unsigned grid = (unsigned)std::max(1, std::min(a.items, sms));  // persistent: one CTA per SM
+  const unsigned grid = 2u * (unsigned)std::max(1, std::min(a.items, sms / 2));  // persistent: one pair per 2 SMs
   auto run = [&](auto kern) -> int {
     ALGX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem));
     kern<<<grid, kHeadThreads, kFwdSmem, st>>>(th, te, a, dz, device_error_word());
@@ -855,13 +898,23 @@ using namespace algx;
 
 extern "C" {
 
+// Vocabulary splits of the forward: the grid is (256-token pairs) x splits
+// CTA pairs of equal work, so the split count that minimises waves x (tiles
+// per pair + about one tile of set-up) keeps the last wave of pairs full (3
+// splits at N = 16384, V = 50304 left it 60% full; 8 fill it to ~97%).
 int algx_head_fwd_splits(int64_t N, int64_t V) {
-  const int64_t tb = (N + 127) / 128, nt = (V + kFwdNT - 1) / kFwdNT;
-  int64_t s = (2 * 148 + tb - 1) / tb;
-  if (s < 1) s = 1;
-  if (s > nt) s = nt;
-  if (s > 64) s = 64;
-  return (int)s;
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t pairs = (N + 255) / 256, nt = (V + kFwdNT - 1) / kFwdNT, slots = std::max(1, sms / 2);
+  int64_t best = 1, best_cost = INT64_MAX;
+  for (int64_t s = 1; s <= std::min<int64_t>(nt, 64); ++s) {
+    const int64_t cost = ((pairs * s + slots - 1) / slots) * ((nt + s - 1) / s + 1);  // + ~one tile of set-up per CTA
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = s;
+    }
+  }
+  return (int)best;
 }
 
 int algx_head_fwd(const algx_head_config* cfg, const void* h, const void* embed, const int32_t* targets,
@@ -872,10 +925,10 @@ int algx_head_fwd(const algx_head_config* cfg, const void* h, const void* embed,
   ALGX_REQUIRE(splits >= 1 && splits <= 64, "head_fwd: splits must be in [1, 64]");
   CUtensorMap th, te;
   if (int s = make_tmap_2d(&th, h, ALGX_BF16, (uint64_t)d, (uint64_t)N, (uint64_t)d * 2, 64, 128, true)) return s;
-  if (int s = make_tmap_2d(&te, embed, ALGX_BF16, (uint64_t)d, (uint64_t)V, (uint64_t)d * 2, 64, kFwdNT, true))
+  if (int s = make_tmap_2d(&te, embed, ALGX_BF16, (uint64_t)d, (uint64_t)V, (uint64_t)d * 2, 64, 128, true))
     return s;
   HeadArgs a{*cfg, targets, (int)N, (int)d, (int)V, (int)vocab_offset, splits};
-  const int tb = (int)((N + 127) / 128);
+  const int tb = 2 * (int)((N + 255) / 256);  // whole CTA pairs
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   return cfg->kind == ALGX_HEAD_CE ? launch_fwd_k<ALGX_HEAD_CE>(th, te, a, tb, part_m, part_l, part_zt, st)
                                    : launch_fwd_k<ALGX_HEAD_ALG_CE>(th, te, a, tb, part_m, part_l, part_zt, st);
@@ -922,7 +975,7 @@ int algx_head_bwd(const algx_head_config* cfg, const void* h, const void* embed,
   const int64_t vs = slab_cols(V);
   CUtensorMap th, te;
   if (int s = make_tmap_2d(&th, h, ALGX_BF16, (uint64_t)d, (uint64_t)N, (uint64_t)d * 2, 64, 128, true)) return s;
-  if (int s = make_tmap_2d(&te, embed, ALGX_BF16, (uint64_t)d, (uint64_t)V, (uint64_t)d * 2, 64, kFwdNT, true))
+  if (int s = make_tmap_2d(&te, embed, ALGX_BF16, (uint64_t)d, (uint64_t)V, (uint64_t)d * 2, 64, 128, true))
     return s;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   __nv_bfloat16* dz = static_cast<__nv_bfloat16*>(workspace);
@@ -930,14 +983,14 @@ int algx_head_bwd(const algx_head_config* cfg, const void* h, const void* embed,
                                        : reinterpret_cast<float*>(static_cast<char*>(workspace) + (size_t)N * vs * 2);
   int* counter = reinterpret_cast<int*>(static_cast<char*>(workspace) + algx_head_bwd_workspace_size(N, d, V, dh_dtype) -
                                         256);
-  const int tb = (int)((N + 127) / 128);
+  const int tbp = (int)((N + 255) / 256);  // 256-token blocks of the dz kernel's CTA pairs
   const int ntiles_total = (int)((V + kFwdNT - 1) / kFwdNT);
   const int tiles_n = (int)((d + kPairBN - 1) / kPairBN);
   for (int64_t c0 = 0; c0 < V; c0 += vs) {
     const int64_t vc = std::min<int64_t>(vs, V - c0);  // valid columns of this slab
     DzArgs a{*cfg, targets, stat, scale, (int)N, (int)d, (int)V, (int)vocab_offset, (int)(c0 / kFwdNT), 0, 0, (int)vs};
     a.ntiles = std::min<int>((int)(vs / kFwdNT), ntiles_total - a.tile0);
-    a.items = tb * a.ntiles;
+    a.items = tbp * a.ntiles;
     int s = cfg->kind == ALGX_HEAD_CE ? launch_dz_k<ALGX_HEAD_CE>(th, te, a, dz, st)
                                       : launch_dz_k<ALGX_HEAD_ALG_CE>(th, te, a, dz, st);
     if (s) return s;
