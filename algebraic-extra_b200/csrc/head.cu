@@ -202,7 +202,49 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kHeadThreads, 1)
           for (int i = 0; i < 32; ++i)
             if (col0 + i == tloc) zt += __uint_as_float(zr[i]);
         }
-        if constexpr (KIND == ALGX_HEAD_CE) {
+        if (nvalid == 32) {
+          // full chunk: the same per-element maths on packed f32x2 pairs with
+          // two partial sums (and a max tree for ce), so a thread's 32
+          // elements are not one serial dependency chain
+          if constexpr (KIND == ALGX_HEAD_CE) {
+            float mx[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) mx[i] = fmaxf(__uint_as_float(zr[2 * i]), __uint_as_float(zr[2 * i + 1]));
+#pragma unroll
+            for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+              for (int i = 0; i < w; ++i) mx[i] = fmaxf(mx[i], mx[i + w]);
+            if (mx[0] > m) {
+              l *= exp2f((m - mx[0]) * log2e);
+              m = mx[0];
+            }
+            const float2 lg = make_float2(log2e, log2e), nb = make_float2(-m * log2e, -m * log2e);
+            float2 s0 = make_float2(0.f, 0.f), s1 = s0;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const float2 t = fma2(make_float2(__uint_as_float(zr[2 * i]), __uint_as_float(zr[2 * i + 1])), lg, nb);
+              const float2 e = make_float2(exp2f(t.x), exp2f(t.y));
+              if (i & 1) s1 = add2(s1, e);
+              else s0 = add2(s0, e);
+            }
+            l += (s0.x + s0.y) + (s1.x + s1.y);
+          } else {
+            const float2 ic = make_float2(a.cfg.inv_c, a.cfg.inv_c), one = make_float2(1.f, 1.f);
+            float2 s0 = make_float2(0.f, 0.f), s1 = s0;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              float2 x = mul2(make_float2(__uint_as_float(zr[2 * i]), __uint_as_float(zr[2 * i + 1])), ic);
+              x.x = fminf(x.x, a.cfg.clamp);
+              x.y = fminf(x.y, a.cfg.clamp);
+              const float2 rad = fma2(x, x, one);
+              const float2 rr = make_float2(rsqrt_fast(rad.x), rsqrt_fast(rad.y));
+              const float2 p = ipow2_t<NPOW>(fma2(rad, rr, x));
+              if (i & 1) s1 = add2(s1, p);
+              else s0 = add2(s0, p);
+            }
+            l += (s0.x + s0.y) + (s1.x + s1.y);
+          }
+        } else if constexpr (KIND == ALGX_HEAD_CE) {
           float cm = -1e30f;
 #pragma unroll
           for (int i = 0; i < 32; ++i)
@@ -417,6 +459,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kHeadThreads, 1)
         tmem_ld32(acc + cc * 32, zr);
         const int col0 = t * kFwdNT + cc * 32;
         uint32_t pk[16];
+        if (row_ok && col0 + 32 <= a.V) {
+          // whole chunk valid: the same per-element maths on packed f32x2 pairs
+          const float2 sc = make_float2(scale, scale);
+#pragma unroll
+          for (int i2 = 0; i2 < 16; ++i2) {
+            const float2 z = make_float2(__uint_as_float(zr[2 * i2]), __uint_as_float(zr[2 * i2 + 1]));
+            const float2 y = make_float2(col0 + 2 * i2 == tloc ? 1.f : 0.f, col0 + 2 * i2 + 1 == tloc ? 1.f : 0.f);
+            float2 gr;
+            if constexpr (KIND == ALGX_HEAD_CE) {
+              const float2 u = fma2(z, make_float2(log2e, log2e), make_float2(-stl, -stl));
+              gr = sub2(make_float2(exp2f(u.x), exp2f(u.y)), y);
+            } else {
+              float2 x = mul2(z, make_float2(c.inv_c, c.inv_c));
+              x.x = fminf(x.x, c.clamp);
+              x.y = fminf(x.y, c.clamp);
+              const float2 rad = fma2(x, x, make_float2(1.f, 1.f));
+              const float2 rr = make_float2(rsqrt_fast(rad.x), rsqrt_fast(rad.y));
+              gr = mul2(sub2(ipow2_t<NPOW>(mul2(fma2(rad, rr, x), make_float2(st, st))), y), rr);
+            }
+            const float2 g2 = mul2(gr, sc);
+            pk[i2] = pack_bf16x2(g2.x, g2.y);
+          }
+        } else {
 #pragma unroll
         for (int i2 = 0; i2 < 16; ++i2) {
           float g2[2];
@@ -437,6 +502,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kHeadThreads, 1)
             g2[h] = (row_ok && col < a.V) ? gr * scale : 0.f;
           }
           pk[i2] = pack_bf16x2(g2[0], g2[1]);
+        }
         }
         if (tok < a.N) {
           uint4* d4 = reinterpret_cast<uint4*>(drow + col0);
