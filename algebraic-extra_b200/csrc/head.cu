@@ -68,6 +68,18 @@ struct HeadArgs {
   int splits;    // forward vocabulary splits
 };
 
+// Maximum of 32 fp32 values (raw bits) by a tree of depth 5.
+__device__ __forceinline__ float chunk_max32(const uint32_t (&zr)[32]) {
+  float mx[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) mx[i] = fmaxf(__uint_as_float(zr[2 * i]), __uint_as_float(zr[2 * i + 1]));
+#pragma unroll
+  for (int w = 8; w > 0; w >>= 1)
+#pragma unroll
+    for (int i = 0; i < w; ++i) mx[i] = fmaxf(mx[i], mx[i + w]);
+  return mx[0];
+}
+
 template <int KIND, int NPOW>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kHeadThreads, 1)
     head_fwd_tc_kernel(const __grid_constant__ CUtensorMap th, const __grid_constant__ CUtensorMap te, HeadArgs a,
@@ -207,16 +219,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kHeadThreads, 1)
           // two partial sums (and a max tree for ce), so a thread's 32
           // elements are not one serial dependency chain
           if constexpr (KIND == ALGX_HEAD_CE) {
-            float mx[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) mx[i] = fmaxf(__uint_as_float(zr[2 * i]), __uint_as_float(zr[2 * i + 1]));
-#pragma unroll
-            for (int w = 8; w > 0; w >>= 1)
-#pragma unroll
-              for (int i = 0; i < w; ++i) mx[i] = fmaxf(mx[i], mx[i + w]);
-            if (mx[0] > m) {
-              l *= exp2f((m - mx[0]) * log2e);
-              m = mx[0];
+            const float cm = chunk_max32(zr);
+            if (cm > m) {
+              l *= exp2f((m - cm) * log2e);
+              m = cm;
             }
             const float2 lg = make_float2(log2e, log2e), nb = make_float2(-m * log2e, -m * log2e);
             float2 s0 = make_float2(0.f, 0.f), s1 = s0;
