@@ -47,6 +47,11 @@ class DataParallelTrainer:
 
     ``shard_optimizer``: shard the decayed parameters' update over the ranks
     (see the module docstring); ignored on one rank.
+    ``optimizer``: "adamw" (fused AdamW with the constant ``lr``, the BASELINE
+    configuration) or one of the reference trainer's optimizers,
+    "muon_adamw", "cadamw", "hybrid_muon_cadamw" (``algx.optim``, with its
+    cosine schedule over ``total_steps``; ``opt_kwargs`` go to it), which run
+    replicated on every rank: Muon orthogonalises whole matrices.
 
     ``micro_batch``: sequences per forward/backward pass; the rank's share of
     the batch must be a multiple of it. ``bucket_bytes``: target size of one
@@ -60,7 +65,8 @@ class DataParallelTrainer:
     def __init__(self, model, *, lr: float = 2e-3, betas=(0.9, 0.95), eps: float = 1e-8,
                  weight_decay: float = 0.1, clip: float = 1.0, micro_batch: int = 8,
                  bucket_bytes: int = 32 << 20, group=None, check_finite: bool = False,
-                 shard_optimizer: bool = True):
+                 shard_optimizer: bool = True, optimizer: str = "adamw", total_steps: int = 1000,
+                 opt_kwargs: Optional[dict] = None):
         self.model = model
         self.check_finite = bool(check_finite)
         self.flat = model.flat
@@ -73,6 +79,15 @@ class DataParallelTrainer:
         self._works: List = []
         self._last = False
         self._buckets = self._make_buckets(bucket_bytes) if self.world > 1 else []
+        self._ref_opt = None
+        self._opt_step = 0
+        if optimizer != "adamw":
+            from .optim import ReferenceOptimizer
+            named = [(n, p, self.flat.slices[n][0]) for n, p in self.flat.params.items()]
+            self._ref_opt = ReferenceOptimizer(optimizer, named, lr=lr, weight_decay=weight_decay,
+                                               total_steps=total_steps, b1=betas[0], b2=betas[1], adam_eps=eps,
+                                               **(opt_kwargs or {}))
+            shard_optimizer = False
         # bucket index -> (this rank's slice of the masters, its gradient buffer)
         self._shard: Dict[int, Tuple[torch.Tensor, torch.Tensor]] = {}
         # bucket index -> the bucket's masters as a tensor on the same storage
@@ -220,7 +235,11 @@ class DataParallelTrainer:
                 raise FloatingPointError(f"non-finite loss {float(loss)} or gradient norm "
                                          f"{float(self.last_gnorm)}; the update was not applied")
         self._wait_gathers()  # a bucket no forward fetched since the last step
-        self.opt.step()
+        if self._ref_opt is not None:
+            self._ref_opt.step(self._opt_step)
+        else:
+            self.opt.step()
+        self._opt_step += 1
         if self._shard:
             # every rank's updated slices back into the full masters, in the
             # order the next forward needs them (the reverse of the buckets')
@@ -293,6 +312,10 @@ def main(argv=None) -> None:
     ap.add_argument("--layers", type=int, default=None, help="override n_layers (same as --set n_layers=N)")
     ap.add_argument("--check-finite", action="store_true",
                     help="raise FloatingPointError on a non-finite loss or gradient norm (one host sync per step)")
+    ap.add_argument("--optimizer", default="adamw", choices=("adamw", "muon_adamw", "cadamw", "hybrid_muon_cadamw"),
+                    help="adamw: fused AdamW (BASELINE config 5); the others: the reference trainer's optimizers")
+    ap.add_argument("--lr", type=float, default=2e-3)
+    ap.add_argument("--total-steps", type=int, default=1000, help="cosine schedule length (reference optimizers)")
     args = ap.parse_args(argv)
     over = parse_overrides(args.set)
     if args.layers is not None:
@@ -300,7 +323,8 @@ def main(argv=None) -> None:
     cfg = (config_125m if args.preset == "standard" else config_algebraic_125m)(**over)
     dev = torch.device("cuda", torch.cuda.current_device())
     model = AlgebraicLM(cfg, device=dev, seed=0)
-    tr = DataParallelTrainer(model, micro_batch=args.micro, check_finite=args.check_finite)
+    tr = DataParallelTrainer(model, lr=args.lr, micro_batch=args.micro, check_finite=args.check_finite,
+                             optimizer=args.optimizer, total_steps=args.total_steps)
     g = torch.Generator(device=dev).manual_seed(777)
     seq = torch.randint(0, cfg.vocab_size, (args.batch, cfg.seq_len + 1), device=dev, generator=g)
     tok, tgt = seq[:, :-1].contiguous(), seq[:, 1:].contiguous()
@@ -317,7 +341,8 @@ def main(argv=None) -> None:
     print(json.dumps({"tok_per_s": tokens / (ms / 1e3), "ms_per_step": ms,
                       "tflops_6P": train_flops_per_token(cfg) * tokens / (ms / 1e3) / 1e12,
                       "loss": [float(x) for x in losses], "gnorm": float(tr.last_gnorm), "batch": args.batch,
-                      "micro": args.micro, "layers": cfg.n_layers, "preset": args.preset}))
+                      "micro": args.micro, "layers": cfg.n_layers, "preset": args.preset,
+                      "optimizer": args.optimizer}))
 
 
 if __name__ == "__main__":

@@ -72,3 +72,20 @@ def head_inputs(seed, shape=HEAD_SHAPE, e_scale=0.15):
     e = normal(seed + 1, (V, d), e_scale)
     t = integers(seed + 2, (N,), 0, V)
     return h, e, t
+
+
+# ---- optimizers (optimizers.py): a small parameter tree with every routing
+# class (Muon matrices of three aspect ratios, the embedding, gains, sink) and
+# three steps of gradients
+OPTIM_SHAPES = {"embed": (10, 8), "ln1": (8,), "q_gain": (4,), "sink": (2,), "w_d": (16, 8), "w_o": (8, 8),
+                "w_q": (8, 16)}
+OPTIM_DECAY = {"embed": True, "ln1": False, "q_gain": False, "sink": False, "w_d": True, "w_o": True, "w_q": True}
+OPTIM_ARGS = dict(lr=2e-2, weight_decay=0.1, total_steps=10, warmup_fraction=0.2, min_lr_ratio=0.1)
+OPTIM_NS_SHAPES = [(8, 16), (16, 8), (12, 12), (3, 4, 6)]
+
+
+def optim_inputs(seed):
+    params = {k: normal(seed + i, s, 0.5) for i, (k, s) in enumerate(sorted(OPTIM_SHAPES.items()))}
+    grads = [{k: normal(seed + 100 * (j + 1) + i, s, 0.1) for i, (k, s) in enumerate(sorted(OPTIM_SHAPES.items()))}
+             for j in range(3)]
+    return params, grads

@@ -1,8 +1,8 @@
 """A torch-CPU stand-in for the slice of JAX that the reference's dense maths uses.
 
 Fixture generation only (``tests/golden/make_golden.py``): it lets this
-container execute the reference's own ``algebraic.py``, ``standard.py`` and
-``evaluation.py`` source without JAX, which is not installed here. Arrays are
+container execute the reference's own ``algebraic.py``, ``standard.py``,
+``evaluation.py`` and ``optimizers.py`` source without JAX, which is not installed here. Arrays are
 torch tensors; ``jax.custom_vjp`` becomes a ``torch.autograd.Function`` that
 calls the reference's own forward/backward rules, and plain autodiff becomes
 torch autograd. Nothing outside ``tests/golden/make_golden.py`` imports it.
@@ -10,7 +10,7 @@ torch autograd. Nothing outside ``tests/golden/make_golden.py`` imports it.
 
 import torch
 
-from . import lax, nn, numpy  # noqa: F401
+from . import lax, nn, numpy, tree_util  # noqa: F401
 
 Array = torch.Tensor
 

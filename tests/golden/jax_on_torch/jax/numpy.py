@@ -76,6 +76,8 @@ def max(x, axis=None, keepdims=False):
 
 
 def maximum(a, b):
+    if not isinstance(a, torch.Tensor) and not isinstance(b, torch.Tensor):
+        return builtins.max(a, b)
     if not isinstance(b, torch.Tensor):
         return torch.clamp(a, min=b)
     if not isinstance(a, torch.Tensor):
@@ -84,6 +86,8 @@ def maximum(a, b):
 
 
 def minimum(a, b):
+    if not isinstance(a, torch.Tensor) and not isinstance(b, torch.Tensor):
+        return builtins.min(a, b)
     if not isinstance(b, torch.Tensor):
         return torch.clamp(a, max=b)
     if not isinstance(a, torch.Tensor):
@@ -152,6 +156,8 @@ def exp(x):
 
 
 def sqrt(x):
+    if not isinstance(x, torch.Tensor):  # a Python scalar: float64, the x64 setting of the goldens
+        x = torch.tensor(float(x), dtype=torch.float64)
     return torch.sqrt(x)
 
 
@@ -165,3 +171,26 @@ def sin(x):
 
 def linspace(a, b, n, dtype=None):
     return torch.linspace(a, b, n, dtype=_dt(dtype) or torch.float32)
+
+
+pi = 3.141592653589793
+
+
+def square(x):
+    return x * x
+
+
+def swapaxes(x, a, b):
+    return torch.swapaxes(x, a, b)
+
+
+def eye(n, dtype=None):
+    return torch.eye(n, dtype=_dt(dtype) or torch.float32)
+
+
+def zeros_like(x):
+    return torch.zeros_like(x)
+
+
+def clip(x, lo, hi):
+    return torch.clamp(x, min=lo, max=hi)

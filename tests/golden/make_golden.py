@@ -14,8 +14,9 @@ Two precisions per case:
     reference's rounding points (``p.astype(v.dtype)``, ``out.astype(q.dtype)``).
 
 Usage: python tests/golden/make_golden.py --reference <path-to-reference-checkout>
-Outputs: tests/golden/reference_dense.npz and reference_alu.npz (small; inputs
-are regenerated from seeds; ``--which`` writes one of them).
+Outputs: tests/golden/reference_dense.npz, reference_alu.npz and
+reference_optim.npz (small; inputs are regenerated from seeds; ``--which``
+writes one of them).
 """
 
 import argparse
@@ -155,11 +156,34 @@ def alu_goldens(RA, out):
     out["alu_checksum"] = np.float64(float(np.sum(x, dtype=np.float64)) + float(np.sum(g, dtype=np.float64)))
 
 
+def optim_goldens(RO, out):
+    """newton_schulz_5, the cosine schedule and three steps of each optimizer
+    (optimizers.py:27-62, 96-116, 118-240) through the reference's own code,
+    float64 end to end."""
+    for i, shape in enumerate(cases.OPTIM_NS_SHAPES):
+        g = torch.from_numpy(cases.normal(61 + i, shape)).double()
+        out["ns5_" + "x".join(map(str, shape)) + "_in"] = g.numpy()
+        out["ns5_" + "x".join(map(str, shape))] = RO.newton_schulz_5(g).numpy()
+    sched = RO.make_cosine_schedule(2e-2, 10, 0.2, 0.1)
+    out["schedule"] = np.array([float(sched(torch.tensor(t))) for t in range(13)])
+    params0, grads = cases.optim_inputs(71)
+    mask = {k: torch.tensor(v) for k, v in cases.OPTIM_DECAY.items()}
+    for name in ("muon_adamw", "cadamw", "hybrid_muon_cadamw"):
+        init_fn, step_fn = RO.get_optimizer(name, **cases.OPTIM_ARGS)
+        params = {k: torch.from_numpy(v).double() for k, v in params0.items()}
+        state = init_fn(params)
+        for step, gr in enumerate(grads):
+            params, state = step_fn(step, params, {k: torch.from_numpy(v).double() for k, v in gr.items()}, state,
+                                    mask)
+            for k, v in params.items():
+                out[f"opt_{name}_step{step}_{k}"] = v.numpy()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="root of the reference checkout")
-    ap.add_argument("--which", choices=("all", "dense", "alu"), default="all",
-                    help="dense: reference_dense.npz; alu: reference_alu.npz")
+    ap.add_argument("--which", choices=("all", "dense", "alu", "optim"), default="all",
+                    help="dense: reference_dense.npz; alu: reference_alu.npz; optim: reference_optim.npz")
     args = ap.parse_args()
     src = os.path.join(args.reference, "src")
     sys.path.insert(0, src)
@@ -178,6 +202,14 @@ def main():
         path = os.path.join(HERE, "reference_dense.npz")
         np.savez_compressed(path, **out)
         print(f"wrote {path}: {len(out)} arrays, {os.path.getsize(path) / 1e6:.2f} MB; {prov}")
+    if args.which in ("all", "optim"):
+        RO = importlib.import_module("algebraic.optimizers")
+        oprov = {"optimizers.py": _sha(os.path.join(src, "algebraic", "optimizers.py"))}
+        out = {"provenance": np.array(repr(oprov))}
+        optim_goldens(RO, out)
+        path = os.path.join(HERE, "reference_optim.npz")
+        np.savez_compressed(path, **out)
+        print(f"wrote {path}: {len(out)} arrays, {os.path.getsize(path) / 1e6:.2f} MB; {oprov}")
     if args.which in ("all", "alu"):
         out = {"provenance": np.array(repr(prov))}
         alu_goldens(RA, out)

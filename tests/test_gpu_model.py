@@ -240,3 +240,30 @@ def test_add_rms_norm_matches_composed(dtype, dim):
     tol = 1e-2 if dtype == torch.bfloat16 else 1e-5
     assert _rel_l2(a[0].grad, b[0].grad) < tol and _rel_l2(a[1].grad, b[1].grad) < tol
     assert _rel_l2(a[2].grad, b[2].grad) < 1e-5
+
+
+@pytest.mark.parametrize("name", ["muon_adamw", "hybrid_muon_cadamw"])
+def test_reference_optimizer_step_on_the_model_matches_float64(name):
+    """One trainer step with the reference trainer's optimizer on the GPU
+    (float32 masters, Newton-Schulz in float32) against the same update of the
+    same masters and clipped gradients replayed in float64 on the CPU."""
+    from algx import model as M
+    from algx.optim import ReferenceOptimizer
+    from algx.train import DataParallelTrainer
+    cfg = M.config_125m(vocab_size=1000, d_model=128, n_layers=2, n_heads=2, d_ff=256, seq_len=256)
+    model = M.AlgebraicLM(cfg, device="cuda", seed=1)
+    tr = DataParallelTrainer(model, lr=2e-2, micro_batch=2, optimizer=name, total_steps=10)
+    g = torch.Generator().manual_seed(12)
+    seq = torch.randint(0, 1000, (2, 257), generator=g)
+    before = {k: v.detach().double().cpu() for k, v in model.flat.params.items()}
+    tr.step(seq[:, :-1].cuda(), seq[:, 1:].cuda())
+    torch.cuda.synchronize()
+    after = {k: v.detach().double().cpu() for k, v in model.flat.params.items()}
+    ref = {k: v.clone() for k, v in before.items()}
+    for k, v in ref.items():
+        v.grad = model.flat.params[k].grad.detach().double().cpu()  # the clipped gradient the step used
+    opt = ReferenceOptimizer(name, [(k, ref[k], model.flat.slices[k][0]) for k in ref], lr=2e-2, total_steps=10)
+    opt.step(0)
+    num = sum(float(torch.sum((after[k] - ref[k]) ** 2)) for k in ref)
+    den = sum(float(torch.sum((ref[k] - before[k]) ** 2)) for k in ref)
+    assert den > 0 and (num / den) ** 0.5 < 1e-3, (num, den)

@@ -77,9 +77,9 @@ def _batch():
     return seq[:, :-1], seq[:, 1:] % 6
 
 
-def _run_single(steps=2, micro=2, clip=0.5):
+def _run_single(steps=2, micro=2, clip=0.5, optimizer="adamw"):
     model = ToyLM()
-    tr = DataParallelTrainer(model, lr=1e-2, micro_batch=micro, clip=clip)
+    tr = DataParallelTrainer(model, lr=1e-2, micro_batch=micro, clip=clip, optimizer=optimizer, total_steps=10)
     tok, tgt = _batch()
     losses = [float(tr.step(tok, tgt)) for _ in range(steps)]
     return losses, {k: v.clone() for k, v in model.flat.data.items()}
@@ -104,7 +104,7 @@ def test_clip_scales_to_the_bound():
     assert abs(float(torch.linalg.vector_norm(g)) - 1e-3) < 1e-8
 
 
-def _worker(rank, world, init_file, q, shard=True):
+def _worker(rank, world, init_file, q, shard=True, optimizer="adamw"):
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path[:0] = [root, os.path.join(root, "algebraic-extra_b200")]
@@ -114,7 +114,8 @@ def _worker(rank, world, init_file, q, shard=True):
         from tests.test_train_host import ToyLM, _batch
         model = ToyLM()
         # small buckets: several exchanges per step, launched from the backward hooks
-        tr = T(model, lr=1e-2, micro_batch=2, clip=0.5, bucket_bytes=256, shard_optimizer=shard)
+        tr = T(model, lr=1e-2, micro_batch=2, clip=0.5, bucket_bytes=256, shard_optimizer=shard,
+               optimizer=optimizer, total_steps=10)
         tok, tgt = _batch()
         per = tok.shape[0] // world
         sl = slice(rank * per, (rank + 1) * per)
@@ -127,18 +128,21 @@ def _worker(rank, world, init_file, q, shard=True):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("shard", [True, False], ids=["sharded_optimizer", "replicated_optimizer"])
-def test_two_ranks_match_one_process(shard):
+@pytest.mark.parametrize("shard,optimizer", [(True, "adamw"), (False, "adamw"), (True, "hybrid_muon_cadamw"),
+                                             (True, "muon_adamw")],
+                         ids=["sharded_optimizer", "replicated_optimizer", "hybrid_muon_cadamw", "muon_adamw"])
+def test_two_ranks_match_one_process(shard, optimizer):
     """2 gloo ranks with half the batch each give the single-process step on the
     whole batch, with the decayed parameters' update sharded over the ranks
     (reduce-scatter, AdamW on each rank's slice, in-place all-gather fenced on
-    first use by the next forward) and with the replicated update."""
-    ref_losses, ref = _run_single(micro=2)
+    first use by the next forward), with the replicated update, and with the
+    reference trainer's Muon optimizers (which run replicated)."""
+    ref_losses, ref = _run_single(micro=2, optimizer=optimizer)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     with tempfile.TemporaryDirectory() as tmp:
         init = os.path.join(tmp, "init")
-        procs = [ctx.Process(target=_worker, args=(r, 2, init, q, shard)) for r in range(2)]
+        procs = [ctx.Process(target=_worker, args=(r, 2, init, q, shard, optimizer)) for r in range(2)]
         for p in procs:
             p.start()
         out = [q.get(timeout=120) for _ in procs]
@@ -147,7 +151,7 @@ def test_two_ranks_match_one_process(shard):
             assert p.exitcode == 0
     for rank, nb, nshard, losses, params in out:
         assert nb >= 3
-        assert (nshard >= 2) if shard else nshard == 0
+        assert (nshard >= 2) if (shard and optimizer == "adamw") else nshard == 0
         assert all(abs(a - b) < 1e-6 for a, b in zip(losses, ref_losses)), (losses, ref_losses)
         for k in ref:
             torch.testing.assert_close(torch.from_numpy(params[k]), ref[k], rtol=1e-5, atol=1e-6)
