@@ -6,7 +6,7 @@ cautious AdamW everywhere (``cadamw``), and Muon + cautious AdamW
 The update rules are the reference's, element for element; the schedule and
 the Adam bias corrections are computed in float32 as the reference computes
 them. Parameters are addressed by name: the reference's routing rule
-(``is_muon_param``, optimizers.py:64-85) reads the last path component, and a
+(``is_muon_param``, optimizers.py:68-89) reads the last path component, and a
 weight the model stores fused (``w_qkv`` = [w_q | w_k | w_v], ``w_gu`` =
 [w_g | w_u], column blocks) is updated block by block, so each reference
 matrix gets its own Newton-Schulz orthogonalisation and its own cautious mask
@@ -26,7 +26,7 @@ NAMES = ("muon_adamw", "cadamw", "hybrid_muon_cadamw")
 
 
 def newton_schulz_5(G: torch.Tensor, steps: int = 5, eps: float = 1e-7) -> torch.Tensor:
-    """Orthogonalise the trailing two dimensions of G (optimizers.py:27-61):
+    """Orthogonalise the trailing two dimensions of G (optimizers.py:27-65):
     Frobenius pre-normalisation, ``steps`` quintic iterations, two order-3
     Schulz refinements, then scaling by sqrt(max(1, M / N)). The Gram
     matrices are min(M, N) square (G is transposed first when M > N)."""
@@ -51,7 +51,7 @@ def newton_schulz_5(G: torch.Tensor, steps: int = 5, eps: float = 1e-7) -> torch
 
 
 def is_muon_param(name: str, ndim: int) -> bool:
-    """The reference's routing (optimizers.py:64-85) on the last name component."""
+    """The reference's routing (optimizers.py:68-89) on the last name component."""
     key = name.split(".")[-1]
     if key == "embed":
         return False
@@ -63,7 +63,7 @@ def is_muon_param(name: str, ndim: int) -> bool:
 
 
 def cosine_schedule(peak_lr: float, total_steps: int, warmup_fraction: float, min_lr_ratio: float):
-    """Linear warm-up then cosine decay to peak * min_lr_ratio (optimizers.py:88-115),
+    """Linear warm-up then cosine decay to peak * min_lr_ratio (optimizers.py:92-115),
     in float32 like the reference."""
     f32 = torch.float32
     warm = float(warmup_fraction) if warmup_fraction >= 1 else max(1.0, float(round(warmup_fraction * total_steps)))
@@ -97,7 +97,7 @@ class ReferenceOptimizer:
 
     ``params``: (name, tensor, decayed) triples; the tensors are updated in
     place. ``step(step)`` applies the update for the 0-based step index, with
-    the learning rates of the reference's schedules (optimizers.py:152-153).
+    the learning rates of the reference's schedules (optimizers.py:153-154).
     """
 
     def __init__(self, name: str, params: Iterable[Tuple[str, torch.Tensor, bool]], lr: float,
