@@ -25,26 +25,57 @@ NS_COEFFS = (3.4445, -4.7750, 2.0315)
 NAMES = ("muon_adamw", "cadamw", "hybrid_muon_cadamw")
 
 
-def newton_schulz_5(G: torch.Tensor, steps: int = 5, eps: float = 1e-7) -> torch.Tensor:
+PRECISIONS = ("highest", "default")
+
+
+def _matmul_ops(precision: str, like: torch.Tensor):
+    """(round an operand, multiply rounded operands) for a matmul precision.
+
+    ``highest``: operands and products in the working dtype. ``default``:
+    operands rounded to bf16, products accumulated in float32, which is what
+    XLA's DEFAULT precision computes for a float32 dot on the TPU the
+    reference trains on; on a CUDA float32 tensor it runs on the bf16 tensor
+    cores with a float32 output."""
+    if precision == "highest":
+        return (lambda t: t), torch.matmul
+    if precision != "default":
+        raise ValueError(f"unknown matmul precision {precision!r}; choices: {PRECISIONS}")
+    if like.is_cuda and like.dtype == torch.float32:
+        def mm(a, b):
+            f = torch.bmm if a.ndim == 3 else torch.mm
+            return f(a, b, out_dtype=torch.float32)
+        return (lambda t: t.to(torch.bfloat16)), mm
+    dt = like.dtype
+    return (lambda t: t.to(torch.bfloat16).to(dt)), torch.matmul
+
+
+def newton_schulz_5(G: torch.Tensor, steps: int = 5, eps: float = 1e-7, precision: str = "highest") -> torch.Tensor:
     """Orthogonalise the trailing two dimensions of G (optimizers.py:27-65):
     Frobenius pre-normalisation, ``steps`` quintic iterations, two order-3
     Schulz refinements, then scaling by sqrt(max(1, M / N)). The Gram
-    matrices are min(M, N) square (G is transposed first when M > N)."""
+    matrices are min(M, N) square (G is transposed first when M > N).
+    Leading dimensions are a batch of independent matrices."""
     if G.ndim < 2:
         return G
+    if G.ndim > 3:
+        return newton_schulz_5(G.reshape(-1, *G.shape[-2:]), steps, eps, precision).reshape(G.shape)
+    lo, mm = _matmul_ops(precision, G)
     a, b, c = NS_COEFFS
     M, N = G.shape[-2], G.shape[-1]
     transposed = M > N
     X = G.transpose(-2, -1) if transposed else G
     X = X / torch.sqrt(torch.sum(X * X, dim=(-2, -1), keepdim=True) + eps)
     for _ in range(steps):
-        A = X @ X.transpose(-2, -1)
-        B = b * A + c * (A @ A)
-        X = a * X + B @ X
+        x = lo(X)
+        A = mm(x, x.transpose(-2, -1))
+        a16 = lo(A)
+        B = b * A + c * mm(a16, a16)
+        X = a * X + mm(lo(B), x)
     eye = torch.eye(min(M, N), dtype=X.dtype, device=X.device)
     for _ in range(2):
-        A = X @ X.transpose(-2, -1)
-        X = 0.5 * ((3.0 * eye - A) @ X)
+        x = lo(X)
+        A = mm(x, x.transpose(-2, -1))
+        X = 0.5 * mm(lo(3.0 * eye - A), x)
     if transposed:
         X = X.transpose(-2, -1)
     return X * math.sqrt(max(1.0, float(M) / float(N)))
@@ -92,23 +123,54 @@ def reference_blocks(name: str, param: torch.Tensor) -> List[Tuple[str, torch.Te
     return [(name, param)]
 
 
+class _Group:
+    """Reference parameters of one shape, dtype and routing, updated together:
+    their values and gradients are gathered into one (count, *shape) stack
+    per step, the optimizer state lives stacked, and every per-matrix
+    quantity (the Newton-Schulz normalisation, the cautious mask's mean) is
+    taken per row of the stack."""
+
+    def __init__(self, shape, decayed: bool, muon: bool, like: torch.Tensor):
+        self.shape, self.decayed, self.muon = tuple(shape), decayed, muon
+        self.like = like
+        self.params: List[torch.Tensor] = []
+        self.grads: List[torch.Tensor] = []
+        self.names: List[str] = []
+        self.m = self.v = None
+
+    def add(self, name: str, p: torch.Tensor, g: torch.Tensor) -> None:
+        self.names.append(name)
+        self.params.append(p)
+        self.grads.append(g)
+
+    def init_state(self) -> None:
+        n = len(self.params)
+        self.m = torch.zeros((n,) + self.shape, dtype=self.like.dtype, device=self.like.device)
+        self.v = None if self.muon else torch.zeros_like(self.m)
+
+
 class ReferenceOptimizer:
     """One of the reference's optimizers over named parameters (with .grad).
 
     ``params``: (name, tensor, decayed) triples; the tensors are updated in
     place. ``step(step)`` applies the update for the 0-based step index, with
     the learning rates of the reference's schedules (optimizers.py:153-154).
+    ``precision`` is the Newton-Schulz matmul precision (``highest`` or
+    ``default``, see ``_matmul_ops``).
     """
 
     def __init__(self, name: str, params: Iterable[Tuple[str, torch.Tensor, bool]], lr: float,
                  weight_decay: float = 0.1, total_steps: int = 1000, warmup_fraction: float = 0.02,
                  min_lr_ratio: float = 0.1, b1: float = 0.9, b2: float = 0.95, adam_eps: float = 1e-8,
                  muon_lr: Optional[float] = None, muon_wd: Optional[float] = None, muon_momentum: float = 0.95,
-                 muon_steps: int = 5, cautious_eps: float = 1e-3):
+                 muon_steps: int = 5, cautious_eps: float = 1e-3, precision: str = "highest"):
         name = name.lower().strip()
         if name not in NAMES:
             raise ValueError(f"Unknown optimizer: {name}. Choices: {NAMES}")
+        if precision not in PRECISIONS:
+            raise ValueError(f"unknown matmul precision {precision!r}; choices: {PRECISIONS}")
         self.name = name
+        self.precision = precision
         self.wd = weight_decay
         self.muon_wd = weight_decay if muon_wd is None else muon_wd
         self.b1, self.b2, self.eps = b1, b2, adam_eps
@@ -116,15 +178,19 @@ class ReferenceOptimizer:
         self.adam_lr = cosine_schedule(lr, total_steps, warmup_fraction, min_lr_ratio)
         self.muon_lr = cosine_schedule(lr if muon_lr is None else muon_lr, total_steps, warmup_fraction,
                                        min_lr_ratio)
-        self.slots = []  # (name, param view, grad view, decayed, uses Muon, m, v)
+        groups = {}
         for pname, p, decayed in params:
             if p.grad is None:
                 raise ValueError(f"parameter {pname} has no .grad buffer")
             for (bname, pv), (_, gv) in zip(reference_blocks(pname, p.data), reference_blocks(pname, p.grad)):
                 muon = name != "cadamw" and is_muon_param(bname, pv.ndim)
-                m = torch.zeros_like(pv, memory_format=torch.contiguous_format)
-                v = None if muon else torch.zeros_like(pv, memory_format=torch.contiguous_format)
-                self.slots.append((bname, pv, gv, bool(decayed), muon, m, v))
+                key = (tuple(pv.shape), bool(decayed), muon, pv.dtype, pv.device)
+                if key not in groups:
+                    groups[key] = _Group(pv.shape, bool(decayed), muon, pv)
+                groups[key].add(bname, pv, gv)
+        self.groups: List[_Group] = list(groups.values())
+        for grp in self.groups:
+            grp.init_state()
 
     @torch.no_grad()
     def step(self, step: int) -> None:
@@ -133,22 +199,29 @@ class ReferenceOptimizer:
         c1 = 1.0 - torch.tensor(self.b1, dtype=f32) ** t
         c2 = 1.0 - torch.tensor(self.b2, dtype=f32) ** t
         lr_a, lr_m = self.adam_lr(step), self.muon_lr(step)
-        for _, p, g, decayed, muon, m, v in self.slots:
-            dev = p.device
-            if muon:
+        for grp in self.groups:
+            dev = grp.m.device
+            g = torch.stack(grp.grads)
+            p = torch.stack(grp.params)
+            m, v = grp.m, grp.v
+            if grp.muon:
                 m.mul_(self.mu).add_((1.0 - self.mu) * g)
-                o = newton_schulz_5((1.0 - self.mu) * g + self.mu * m, steps=self.ns_steps)
+                x = (1.0 - self.mu) * g + self.mu * m
+                # a 1-D matrix passes through unchanged (optimizers.py:35-36)
+                o = newton_schulz_5(x, steps=self.ns_steps, precision=self.precision) if len(grp.shape) >= 2 else x
                 lr = lr_m.to(dev)
-                decay = (1.0 - lr * self.muon_wd) if decayed else torch.ones((), dtype=f32, device=dev)
-                p.copy_(p * decay - lr * o)
-                continue
-            m.mul_(self.b1).add_((1.0 - self.b1) * g)
-            v.mul_(self.b2).add_((1.0 - self.b2) * (g * g))
-            u = (m / c1.to(dev)) / (torch.sqrt(v / c2.to(dev)) + self.eps)
-            if self.name != "muon_adamw":  # cautious: keep the components that agree with the gradient
-                # the reference's 0/1 mask is built from Python scalars: float32
-                mask = (u * g > 0.0).to(f32)
-                u = u * (mask / torch.clamp(mask.mean(), min=self.cautious_eps))
-            lr = lr_a.to(dev)
-            decay = (1.0 - lr * self.wd) if decayed else torch.ones((), dtype=f32, device=dev)
-            p.copy_(p * decay - lr * u)
+                decay = (1.0 - lr * self.muon_wd) if grp.decayed else torch.ones((), dtype=f32, device=dev)
+                p = p * decay - lr * o
+            else:
+                m.mul_(self.b1).add_((1.0 - self.b1) * g)
+                v.mul_(self.b2).add_((1.0 - self.b2) * (g * g))
+                u = (m / c1.to(dev)) / (torch.sqrt(v / c2.to(dev)) + self.eps)
+                if self.name != "muon_adamw":  # cautious: keep the components that agree with the gradient
+                    # the reference's 0/1 mask is built from Python scalars: float32
+                    mask = (u * g > 0.0).to(f32)
+                    mean = mask.mean(dim=tuple(range(1, mask.ndim)), keepdim=True) if mask.ndim > 1 else mask
+                    u = u * (mask / torch.clamp(mean, min=self.cautious_eps))
+                lr = lr_a.to(dev)
+                decay = (1.0 - lr * self.wd) if grp.decayed else torch.ones((), dtype=f32, device=dev)
+                p = p * decay - lr * u
+            torch._foreach_copy_(grp.params, list(p.unbind(0)))

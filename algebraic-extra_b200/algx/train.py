@@ -316,6 +316,9 @@ def main(argv=None) -> None:
                     help="adamw: fused AdamW (BASELINE config 5); the others: the reference trainer's optimizers")
     ap.add_argument("--lr", type=float, default=2e-3)
     ap.add_argument("--total-steps", type=int, default=1000, help="cosine schedule length (reference optimizers)")
+    ap.add_argument("--ns-precision", choices=("default", "highest"), default="default",
+                    help="Muon's Newton-Schulz matmuls: default = bf16 operands, float32 accumulation (XLA's "
+                         "DEFAULT float32 dot on TPU); highest = float32 operands")
     args = ap.parse_args(argv)
     over = parse_overrides(args.set)
     if args.layers is not None:
@@ -324,7 +327,8 @@ def main(argv=None) -> None:
     dev = torch.device("cuda", torch.cuda.current_device())
     model = AlgebraicLM(cfg, device=dev, seed=0)
     tr = DataParallelTrainer(model, lr=args.lr, micro_batch=args.micro, check_finite=args.check_finite,
-                             optimizer=args.optimizer, total_steps=args.total_steps)
+                             optimizer=args.optimizer, total_steps=args.total_steps,
+                             opt_kwargs=None if args.optimizer == "adamw" else {"precision": args.ns_precision})
     g = torch.Generator(device=dev).manual_seed(777)
     seq = torch.randint(0, cfg.vocab_size, (args.batch, cfg.seq_len + 1), device=dev, generator=g)
     tok, tgt = seq[:, :-1].contiguous(), seq[:, 1:].contiguous()
@@ -342,7 +346,8 @@ def main(argv=None) -> None:
                       "tflops_6P": train_flops_per_token(cfg) * tokens / (ms / 1e3) / 1e12,
                       "loss": [float(x) for x in losses], "gnorm": float(tr.last_gnorm), "batch": args.batch,
                       "micro": args.micro, "layers": cfg.n_layers, "preset": args.preset,
-                      "optimizer": args.optimizer}))
+                      "optimizer": args.optimizer,
+                      "ns_precision": None if args.optimizer == "adamw" else args.ns_precision}))
 
 
 if __name__ == "__main__":

@@ -77,9 +77,13 @@ def head_inputs(seed, shape=HEAD_SHAPE, e_scale=0.15):
 # ---- optimizers (optimizers.py): a small parameter tree with every routing
 # class (Muon matrices of three aspect ratios, the embedding, gains, sink) and
 # three steps of gradients
-OPTIM_SHAPES = {"embed": (10, 8), "ln1": (8,), "q_gain": (4,), "sink": (2,), "w_d": (16, 8), "w_o": (8, 8),
-                "w_q": (8, 16)}
-OPTIM_DECAY = {"embed": True, "ln1": False, "q_gain": False, "sink": False, "w_d": True, "w_o": True, "w_q": True}
+# every routing class of optimizers.py:68-89: the embedding, gains, a sink, a
+# bias, tall / square / wide matrices (two of one shape) and a 1-D "w_" vector
+# (routed to Muon, which passes it through unorthogonalised)
+OPTIM_SHAPES = {"bias": (8,), "embed": (10, 8), "ln1": (8,), "q_gain": (4,), "sink": (2,), "w_d": (16, 8),
+                "w_k": (8, 8), "w_o": (8, 8), "w_q": (8, 16), "w_scale": (8,)}
+OPTIM_DECAY = {"bias": False, "embed": True, "ln1": False, "q_gain": False, "sink": False, "w_d": True,
+               "w_k": True, "w_o": True, "w_q": True, "w_scale": True}
 OPTIM_ARGS = dict(lr=2e-2, weight_decay=0.1, total_steps=10, warmup_fraction=0.2, min_lr_ratio=0.1)
 OPTIM_NS_SHAPES = [(8, 16), (16, 8), (12, 12), (3, 4, 6)]
 

@@ -242,17 +242,23 @@ def test_add_rms_norm_matches_composed(dtype, dim):
     assert _rel_l2(a[2].grad, b[2].grad) < 1e-5
 
 
-@pytest.mark.parametrize("name", ["muon_adamw", "hybrid_muon_cadamw"])
-def test_reference_optimizer_step_on_the_model_matches_float64(name):
+@pytest.mark.parametrize("name,precision,tol", [("muon_adamw", "highest", 1e-3),
+                                                  ("hybrid_muon_cadamw", "highest", 1e-3),
+                                                  ("hybrid_muon_cadamw", "default", 2e-2)])
+def test_reference_optimizer_step_on_the_model_matches_float64(name, precision, tol):
     """One trainer step with the reference trainer's optimizer on the GPU
-    (float32 masters, Newton-Schulz in float32) against the same update of the
-    same masters and clipped gradients replayed in float64 on the CPU."""
+    (float32 masters; Newton-Schulz batched over same-shape matrices, with
+    float32 or bf16 operands) against the same update of the same masters and
+    clipped gradients replayed in float64 on the CPU with the same operand
+    rounding. ``tol`` bounds the update's relative error: bf16 operands can
+    round differently from float32 and float64 intermediates."""
     from algx import model as M
     from algx.optim import ReferenceOptimizer
     from algx.train import DataParallelTrainer
     cfg = M.config_125m(vocab_size=1000, d_model=128, n_layers=2, n_heads=2, d_ff=256, seq_len=256)
     model = M.AlgebraicLM(cfg, device="cuda", seed=1)
-    tr = DataParallelTrainer(model, lr=2e-2, micro_batch=2, optimizer=name, total_steps=10)
+    tr = DataParallelTrainer(model, lr=2e-2, micro_batch=2, optimizer=name, total_steps=10,
+                             opt_kwargs={"precision": precision})
     g = torch.Generator().manual_seed(12)
     seq = torch.randint(0, 1000, (2, 257), generator=g)
     before = {k: v.detach().double().cpu() for k, v in model.flat.params.items()}
@@ -262,8 +268,24 @@ def test_reference_optimizer_step_on_the_model_matches_float64(name):
     ref = {k: v.clone() for k, v in before.items()}
     for k, v in ref.items():
         v.grad = model.flat.params[k].grad.detach().double().cpu()  # the clipped gradient the step used
-    opt = ReferenceOptimizer(name, [(k, ref[k], model.flat.slices[k][0]) for k in ref], lr=2e-2, total_steps=10)
+    opt = ReferenceOptimizer(name, [(k, ref[k], model.flat.slices[k][0]) for k in ref], lr=2e-2, total_steps=10,
+                             precision=precision)
     opt.step(0)
     num = sum(float(torch.sum((after[k] - ref[k]) ** 2)) for k in ref)
     den = sum(float(torch.sum((ref[k] - before[k]) ** 2)) for k in ref)
-    assert den > 0 and (num / den) ** 0.5 < 1e-3, (num, den)
+    assert den > 0 and (num / den) ** 0.5 < tol, (num, den)
+
+
+def test_newton_schulz_bf16_operands_on_tensor_cores():
+    """precision="default" on a CUDA float32 batch runs bf16 x bf16 -> float32
+    products; against the float64 emulation (operands rounded to bf16) and
+    the exact float64 orthogonalisation."""
+    from algx.optim import newton_schulz_5
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(6, 256, 768, generator=g, dtype=torch.float64)
+    got = newton_schulz_5(x.float().cuda(), precision="default").double().cpu()
+    emul = newton_schulz_5(x, precision="default")
+    exact = newton_schulz_5(x, precision="highest")
+    rel = lambda a, b: float(torch.linalg.norm(a - b) / torch.linalg.norm(b))
+    assert rel(got, emul) < 1e-2 and rel(got, exact) < 3e-2, (rel(got, emul), rel(got, exact))
+    assert rel(newton_schulz_5(x.float().cuda(), precision="highest").double().cpu(), exact) < 1e-4

@@ -92,6 +92,36 @@ def test_fused_weights_update_like_separate_reference_matrices(name):
     assert torch.equal(fused["l.w_gu"], torch.cat([sep[k] for k in ("w_g", "w_u")], 1))
 
 
+def test_batched_newton_schulz_equals_one_matrix_at_a_time():
+    g = torch.from_numpy(cases.normal(9, (5, 12, 20))).double()
+    batched = O.newton_schulz_5(g)
+    for i in range(5):
+        np.testing.assert_allclose(batched[i].numpy(), O.newton_schulz_5(g[i]).numpy(), rtol=1e-12, atol=1e-14)
+    tall = g.transpose(-2, -1)  # the M > N branch, batched: transposed, then scaled by sqrt(M / N)
+    np.testing.assert_allclose(O.newton_schulz_5(tall).numpy(), (batched.transpose(-2, -1) * (20 / 12) ** 0.5).numpy(),
+                               rtol=1e-12, atol=1e-14)
+
+
+def test_default_precision_rounds_the_operands_to_bf16():
+    """precision="default": every matmul operand rounded to bf16 (XLA's DEFAULT
+    f32 dot on TPU). Its result stays within bf16-level error of the exact
+    orthogonalisation and is not the exact one."""
+    g = torch.from_numpy(cases.normal(10, (3, 32, 48))).double()
+    hi = O.newton_schulz_5(g, precision="highest")
+    lo = O.newton_schulz_5(g, precision="default")
+    rel = float(torch.linalg.norm(lo - hi) / torch.linalg.norm(hi))
+    assert 1e-5 < rel < 3e-2, rel
+    sv = torch.linalg.svdvals(lo)
+    assert float(sv.max()) < 1.2 and float(sv.min()) > 0.5
+
+
+def test_unknown_precision_is_rejected():
+    with pytest.raises(ValueError, match="precision"):
+        O.ReferenceOptimizer("muon_adamw", [], lr=1e-3, precision="bf16")
+    with pytest.raises(ValueError, match="precision"):
+        O.newton_schulz_5(torch.zeros(4, 4), precision="high")
+
+
 def test_unknown_optimizer_name_is_rejected():
     with pytest.raises(ValueError, match="Unknown optimizer"):
         O.ReferenceOptimizer("sgd", [], lr=1e-3)
