@@ -162,6 +162,10 @@ __global__ void __launch_bounds__(kThreadsB, 1)
     abort_flag = 0;
   }
   __syncthreads();
+  // launched as a programmatic dependent: the set-up above overlapped the
+  // previous kernel's tail; its results (x, dy, gain, the workspace) are
+  // read only after it has finished
+  pdl_wait();
   if (warp == kConsumerWarpsB) {
     // ----- producer: chunk bytes of x and dy per stage
     if (lane == 0) {
@@ -255,16 +259,25 @@ __global__ void __launch_bounds__(kThreadsB, 1)
 
 // dgain[c] = sum_b partial[c][b]: one warp per column, lane l summing blocks
 // l, l + 32, ... in order, then a fixed butterfly over the lanes
-// (deterministic for a given grid size); 64 warps in two CTAs.
+// (deterministic for a given grid size); 64 warps in two CTAs. A lane's (at
+// most eight) loads are issued together before the in-order sum. It lets the
+// next kernel of the stream launch at once (a row kernel launched as its
+// programmatic dependent waits in pdl_wait() until this grid has finished).
 constexpr int kReduceThreads = 1024;
 __global__ void __launch_bounds__(kReduceThreads) qknorm_dgain_reduce(const float* __restrict__ partial, int nblocks,
                                                                       float* __restrict__ dgain) {
-  pdl_wait();  // launched as a programmatic dependent of the row kernel: its partials are complete
+  pdl_trigger();  // the next kernel may be scheduled now; it waits for this grid to finish
+  pdl_wait();     // launched as a programmatic dependent of the row kernel: its partials are complete
   const int c = blockIdx.x * (kReduceThreads / 32) + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (c >= kDim) return;
   const float* col = partial + (int64_t)c * nblocks;
   float s = 0.f;
-  for (int b = lane; b < nblocks; b += 32) s += col[b];
+  float v[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) v[j] = lane + 32 * j < nblocks ? col[lane + 32 * j] : 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) s += v[j];
+  for (int b = lane + 256; b < nblocks; b += 32) s += col[b];  // grids above 256 CTAs (none launched today)
 #pragma unroll
   for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
   if (lane == 0) dgain[c] = s;
@@ -371,8 +384,9 @@ int algx_qknorm_bwd(const void* x, const float* gain, const void* dy, void* dx, 
   auto run = [&](auto kern, auto tag) -> int {
     using TT = decltype(tag);
     ALGX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemB));
-    kern<<<grid, kThreadsB, kSmemB, st>>>(static_cast<const TT*>(x), gain, static_cast<const TT*>(dy),
-                                          static_cast<TT*>(dx), partial, rows, eps, device_error_word());
+    ALGX_CUDA(launch_dependent(kern, grid, kThreadsB, kSmemB, st, static_cast<const TT*>(x), gain,
+                               static_cast<const TT*>(dy), static_cast<TT*>(dx), partial, rows, eps,
+                               device_error_word()));
     ALGX_LAUNCHED("qknorm_bwd launch");
     return ALGX_OK;
   };
