@@ -19,6 +19,7 @@ import math
 from typing import Iterable, List, Optional, Tuple
 
 import torch
+import torch.distributed as dist
 
 # Quintic Newton-Schulz coefficients of the Muon optimizer (optimizers.py:38)
 NS_COEFFS = (3.4445, -4.7750, 2.0315)
@@ -143,10 +144,28 @@ class _Group:
         self.params.append(p)
         self.grads.append(g)
 
-    def init_state(self) -> None:
+    def init_state(self, rank: int = 0, world: int = 1) -> None:
+        """State for the rows this rank updates: all of them (world 1), or a
+        contiguous share of ceil(n / world) rows, padded with zero rows so that
+        every rank's share has the same size for the all-gather."""
         n = len(self.params)
-        self.m = torch.zeros((n,) + self.shape, dtype=self.like.dtype, device=self.like.device)
+        self.world = world
+        self.chunk = n if world == 1 else -(-n // world)
+        self.lo = min(n, rank * self.chunk) if world > 1 else 0
+        self.hi = min(n, self.lo + self.chunk)
+        self.m = torch.zeros((self.chunk,) + self.shape, dtype=self.like.dtype, device=self.like.device)
         self.v = None if self.muon else torch.zeros_like(self.m)
+
+    def own_stack(self, tensors: List[torch.Tensor]) -> torch.Tensor:
+        """This rank's rows of ``tensors`` stacked, zero rows after them up to
+        the share size (zero rows update to zero: no division by zero)."""
+        own = tensors[self.lo:self.hi]
+        if len(own) == self.chunk:
+            return torch.stack(own)
+        out = torch.zeros((self.chunk,) + self.shape, dtype=self.like.dtype, device=self.like.device)
+        if own:
+            out[:len(own)] = torch.stack(own)
+        return out
 
 
 class ReferenceOptimizer:
@@ -156,14 +175,19 @@ class ReferenceOptimizer:
     place. ``step(step)`` applies the update for the 0-based step index, with
     the learning rates of the reference's schedules (optimizers.py:153-154).
     ``precision`` is the Newton-Schulz matmul precision (``highest`` or
-    ``default``, see ``_matmul_ops``).
+    ``default``, see ``_matmul_ops``). ``shard``: the ranks of ``group`` (a
+    torch.distributed process group whose ranks hold the same parameters and
+    gradients) split every Muon stack of at least as many matrices as ranks,
+    each orthogonalising a contiguous share, and all-gather the updated
+    matrices; the other stacks are updated on every rank.
     """
 
     def __init__(self, name: str, params: Iterable[Tuple[str, torch.Tensor, bool]], lr: float,
                  weight_decay: float = 0.1, total_steps: int = 1000, warmup_fraction: float = 0.02,
                  min_lr_ratio: float = 0.1, b1: float = 0.9, b2: float = 0.95, adam_eps: float = 1e-8,
                  muon_lr: Optional[float] = None, muon_wd: Optional[float] = None, muon_momentum: float = 0.95,
-                 muon_steps: int = 5, cautious_eps: float = 1e-3, precision: str = "highest"):
+                 muon_steps: int = 5, cautious_eps: float = 1e-3, precision: str = "highest",
+                 shard: bool = False, group=None):
         name = name.lower().strip()
         if name not in NAMES:
             raise ValueError(f"Unknown optimizer: {name}. Choices: {NAMES}")
@@ -189,8 +213,14 @@ class ReferenceOptimizer:
                     groups[key] = _Group(pv.shape, bool(decayed), muon, pv)
                 groups[key].add(bname, pv, gv)
         self.groups: List[_Group] = list(groups.values())
+        self.pg = group
+        world = dist.get_world_size(group) if shard and dist.is_available() and dist.is_initialized() else 1
+        rank = dist.get_rank(group) if world > 1 else 0
+        self.sharded_groups = 0
         for grp in self.groups:
-            grp.init_state()
+            split = grp.muon and world > 1 and len(grp.params) >= world
+            grp.init_state(rank, world if split else 1)
+            self.sharded_groups += int(split)
 
     @torch.no_grad()
     def step(self, step: int) -> None:
@@ -201,8 +231,8 @@ class ReferenceOptimizer:
         lr_a, lr_m = self.adam_lr(step), self.muon_lr(step)
         for grp in self.groups:
             dev = grp.m.device
-            g = torch.stack(grp.grads)
-            p = torch.stack(grp.params)
+            g = grp.own_stack(grp.grads)
+            p = grp.own_stack(grp.params)
             m, v = grp.m, grp.v
             if grp.muon:
                 m.mul_(self.mu).add_((1.0 - self.mu) * g)
@@ -224,4 +254,8 @@ class ReferenceOptimizer:
                 lr = lr_a.to(dev)
                 decay = (1.0 - lr * self.wd) if grp.decayed else torch.ones((), dtype=f32, device=dev)
                 p = p * decay - lr * u
+            if grp.world > 1:
+                full = torch.empty((grp.world * grp.chunk,) + grp.shape, dtype=p.dtype, device=dev)
+                dist.all_gather_into_tensor(full, p.contiguous(), group=self.pg)
+                p = full[:len(grp.params)]
             torch._foreach_copy_(grp.params, list(p.unbind(0)))

@@ -50,8 +50,11 @@ class DataParallelTrainer:
     ``optimizer``: "adamw" (fused AdamW with the constant ``lr``, the BASELINE
     configuration) or one of the reference trainer's optimizers,
     "muon_adamw", "cadamw", "hybrid_muon_cadamw" (``algx.optim``, with its
-    cosine schedule over ``total_steps``; ``opt_kwargs`` go to it), which run
-    replicated on every rank: Muon orthogonalises whole matrices.
+    cosine schedule over ``total_steps``; ``opt_kwargs`` go to it). With
+    those the gradients are all-reduced whole; with ``shard_optimizer`` the
+    ranks split the Muon matrices of each shape (Muon orthogonalises whole
+    matrices) and all-gather the updated ones, and the rest of the update
+    runs on every rank.
 
     ``micro_batch``: sequences per forward/backward pass; the rank's share of
     the batch must be a multiple of it. ``bucket_bytes``: target size of one
@@ -84,8 +87,11 @@ class DataParallelTrainer:
         if optimizer != "adamw":
             from .optim import ReferenceOptimizer
             named = [(n, p, self.flat.slices[n][0]) for n, p in self.flat.params.items()]
+            # the gradients are all-reduced; with shard_optimizer the ranks
+            # split the Newton-Schulz work and all-gather the updated matrices
             self._ref_opt = ReferenceOptimizer(optimizer, named, lr=lr, weight_decay=weight_decay,
                                                total_steps=total_steps, b1=betas[0], b2=betas[1], adam_eps=eps,
+                                               shard=shard_optimizer and self.world > 1, group=group,
                                                **(opt_kwargs or {}))
             shard_optimizer = False
         # bucket index -> (this rank's slice of the masters, its gradient buffer)

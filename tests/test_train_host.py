@@ -58,15 +58,22 @@ class ToyLM(torch.nn.Module):
 
     def __init__(self, seed=0):
         super().__init__()
+        # three 12 x 12 matrices: a Muon stack that two ranks split unevenly
         specs = [M.ParamSpec("out_gain", (6,), False, 0.0, 1.0),
                  M.ParamSpec("w_b", (12, 6), True, 0.3),
+                 M.ParamSpec("w_c", (12, 12), True, 0.3),
+                 M.ParamSpec("w_e", (12, 12), True, 0.3),
+                 M.ParamSpec("w_f", (12, 12), True, 0.3),
                  M.ParamSpec("w_a", (8, 12), True, 0.3),
                  M.ParamSpec("embed", (20, 8), True, 0.5)]
         self.flat = M.FlatParams(specs, "cpu", torch.Generator().manual_seed(seed))
 
     def loss(self, tokens, targets):
         x = torch.nn.functional.embedding(tokens, self.flat["embed"])
-        z = torch.tanh(x @ self.flat["w_a"]) @ self.flat["w_b"] * self.flat["out_gain"]
+        h = torch.tanh(x @ self.flat["w_a"])
+        h = h + 0.5 * (torch.tanh(h @ self.flat["w_c"]) + torch.tanh(h @ self.flat["w_e"]) -
+                       torch.tanh(h @ self.flat["w_f"]))
+        z = h @ self.flat["w_b"] * self.flat["out_gain"]
         nll = torch.nn.functional.cross_entropy(z.reshape(-1, 6), targets.reshape(-1), reduction="none")
         return nll.mean(), nll.detach()
 
@@ -121,22 +128,26 @@ def _worker(rank, world, init_file, q, shard=True, optimizer="adamw"):
         sl = slice(rank * per, (rank + 1) * per)
         losses = [float(tr.step(tok[sl], tgt[sl])) for _ in range(2)]
         nshard = len(tr._shard)
+        nsplit = tr._ref_opt.sharded_groups if tr._ref_opt is not None else 0
         tr.close()  # waits for the last step's gathers of the updated slices
         # numpy copies: torch tensors would be shared by file descriptor and vanish with the process
-        q.put((rank, len(tr._buckets), nshard, losses, {k: v.numpy().copy() for k, v in model.flat.data.items()}))
+        q.put((rank, len(tr._buckets), nshard, nsplit, losses,
+               {k: v.numpy().copy() for k, v in model.flat.data.items()}))
     finally:
         dist.destroy_process_group()
 
 
 @pytest.mark.parametrize("shard,optimizer", [(True, "adamw"), (False, "adamw"), (True, "hybrid_muon_cadamw"),
-                                             (True, "muon_adamw")],
-                         ids=["sharded_optimizer", "replicated_optimizer", "hybrid_muon_cadamw", "muon_adamw"])
+                                             (True, "muon_adamw"), (False, "muon_adamw")],
+                         ids=["sharded_optimizer", "replicated_optimizer", "hybrid_muon_cadamw", "muon_adamw",
+                              "muon_adamw_replicated"])
 def test_two_ranks_match_one_process(shard, optimizer):
     """2 gloo ranks with half the batch each give the single-process step on the
     whole batch, with the decayed parameters' update sharded over the ranks
     (reduce-scatter, AdamW on each rank's slice, in-place all-gather fenced on
     first use by the next forward), with the replicated update, and with the
-    reference trainer's Muon optimizers (which run replicated)."""
+    reference trainer's Muon optimizers: the three 12 x 12 matrices split over
+    the ranks (two and one, plus a zero row) and all-gathered, or replicated."""
     ref_losses, ref = _run_single(micro=2, optimizer=optimizer)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -149,9 +160,10 @@ def test_two_ranks_match_one_process(shard, optimizer):
         for p in procs:
             p.join(timeout=60)
             assert p.exitcode == 0
-    for rank, nb, nshard, losses, params in out:
+    for rank, nb, nshard, nsplit, losses, params in out:
         assert nb >= 3
         assert (nshard >= 2) if (shard and optimizer == "adamw") else nshard == 0
+        assert nsplit == (1 if (shard and optimizer != "adamw") else 0)
         assert all(abs(a - b) < 1e-6 for a, b in zip(losses, ref_losses)), (losses, ref_losses)
         for k in ref:
             torch.testing.assert_close(torch.from_numpy(params[k]), ref[k], rtol=1e-5, atol=1e-6)
