@@ -340,6 +340,11 @@ def secondary(dev, rank, world, stream, sync_all, max_over_ranks, steps=5, warmu
         ("train_cfg5", lambda: train_line(dev, rank, world, stream, sync_all, max_over_ranks)),
         ("train_cfg5_algebraic",
          lambda: train_line(dev, rank, world, stream, sync_all, max_over_ranks, preset="algebraic")),
+        # the reference's own published training setup at this size: the
+        # algebraic preset with hybrid Muon + cautious AdamW
+        ("train_cfg5_algebraic_hybrid",
+         lambda: train_line(dev, rank, world, stream, sync_all, max_over_ranks, preset="algebraic",
+                            optimizer="hybrid_muon_cadamw")),
     ]
     for name, fn in table:
         if lines is None or name in lines:
@@ -416,13 +421,16 @@ def qknorm_line(dev, gen, world, stream, sync_all, max_over_ranks, steps=20, war
 TRAIN_GLOBAL_BATCH = 64  # sequences per optimizer step, split over the ranks (config 5)
 
 
-def train_line(dev, rank, world, stream, sync_all, max_over_ranks, steps=3, warmup=3, preset="standard"):
+def train_line(dev, rank, world, stream, sync_all, max_over_ranks, steps=3, warmup=3, preset="standard",
+               optimizer="adamw"):
     """Config 5: the 125M training step (fwd + bwd + clip + AdamW) on synthetic
     uniform token ids, global batch 64 x 2048 split over the ranks, micro-batches
     of up to 32 sequences, gradient all-reduce overlapped with the last backward.
     preset "standard": SwiGLU, RoPE, ce head; "algebraic":
     the reference's algebraic preset at the same size (ALU-GLU, Cayley
-    rotations, learned sink, alg_ce head n=8 c=2)."""
+    rotations, learned sink, alg_ce head n=8 c=2). ``optimizer``: "adamw", or
+    one of the reference trainer's (algx.optim; Newton-Schulz products with
+    bf16 operands, the Muon matrices split over the ranks)."""
     from algx.model import AlgebraicLM, config_125m, config_algebraic_125m, count_params, train_flops_per_token
     from algx.train import DataParallelTrainer
 
@@ -433,7 +441,8 @@ def train_line(dev, rank, world, stream, sync_all, max_over_ranks, steps=3, warm
     # fewer gradient accumulations); the global batch stays 64 sequences
     micro = max(m for m in range(1, 33) if per % m == 0)
     model = AlgebraicLM(cfg, device=dev, seed=0)  # same initial replica on every rank
-    tr = DataParallelTrainer(model, micro_batch=micro)
+    tr = DataParallelTrainer(model, micro_batch=micro, optimizer=optimizer,
+                             opt_kwargs=None if optimizer == "adamw" else {"precision": "default"})
     g = torch.Generator(device=dev).manual_seed(777 + rank)
     seq = torch.randint(0, cfg.vocab_size, (per, cfg.seq_len + 1), device=dev, generator=g)
     tok, tgt = seq[:, :-1].contiguous(), seq[:, 1:].contiguous()
@@ -450,12 +459,15 @@ def train_line(dev, rank, world, stream, sync_all, max_over_ranks, steps=3, warm
             "steps": steps, "warmup": warmup, "tflops_6P": tflops, "mfu": tflops / (peak_tf * world),
             "mfu_peak": f"{peak_tf:.1f} TFLOP/s {peak_src} bf16 dense (sustained) per GPU x {world}",
             "loss_first": float(losses[0]), "loss_last": float(losses[-1]),
-            "params": count_params(cfg), "flop_per_token": train_flops_per_token(cfg),
+            "params": count_params(cfg), "flop_per_token": train_flops_per_token(cfg), "optimizer": optimizer,
             "config": f"L={cfg.n_layers} d={cfg.d_model} H={cfg.n_heads} ff={cfg.d_ff} V={cfg.vocab_size} "
                       f"S={cfg.seq_len}; QK-norm + {cfg.pos} + asinh n={cfg.attn_n} c={cfg.attn_c}, sink "
                       f"{cfg.sink}, {cfg.ffn}, {cfg.head} head; fp32 masters, bf16 compute; "
                       f"global batch {TRAIN_GLOBAL_BATCH} sequences, "
-                      f"{per} per rank in micro-batches of {micro}; clip 1.0; fused AdamW",
+                      f"{per} per rank in micro-batches of {micro}; clip 1.0; "
+                      + ("fused AdamW" if optimizer == "adamw" else
+                         f"{optimizer} (the reference trainer's optimizer, cosine schedule, Newton-Schulz "
+                         "with bf16 operands and float32 accumulation)"),
             "data": "synthetic uniform token ids, seeded per rank",
             "scaling": "strong (global batch fixed, split over the ranks)" if world > 1 else "single GPU"}
     tr.close()
