@@ -50,6 +50,31 @@ def _matmul_ops(precision: str, like: torch.Tensor):
     return (lambda t: t.to(torch.bfloat16).to(dt)), torch.matmul
 
 
+def _ns_iterations_tensor_cores(X: torch.Tensor, steps: int) -> torch.Tensor:
+    """The iterations of newton_schulz_5 at ``default`` precision on a CUDA
+    float32 batch (count, m, n), m <= n: bf16 operands on the tensor cores,
+    float32 products, with each linear combination folded into the product
+    that feeds it (beta * C + alpha * A @ B in the GEMM epilogue):
+    B = b A + c A^2, X <- a X + B X, and the refinement as
+    X <- 1.5 X - 0.5 A X. The operands are rounded to bf16 as in the literal
+    sequence; the result differs from it only at that rounding level, and it
+    saves the separate element-wise passes over the stacks."""
+    a, b, c = NS_COEFFS
+    f32, bf16 = torch.float32, torch.bfloat16
+    fma_mm = torch.ops.aten.baddbmm.dtype
+    for _ in range(steps):
+        x = X.to(bf16)
+        A = torch.bmm(x, x.transpose(-2, -1), out_dtype=f32)
+        a16 = A.to(bf16)
+        B = fma_mm(A, a16, a16, f32, beta=b, alpha=c)
+        X = fma_mm(X, B.to(bf16), x, f32, beta=a, alpha=1.0)
+    for _ in range(2):
+        x = X.to(bf16)
+        A = torch.bmm(x, x.transpose(-2, -1), out_dtype=f32)
+        X = fma_mm(X, A.to(bf16), x, f32, beta=1.5, alpha=-0.5)
+    return X
+
+
 def newton_schulz_5(G: torch.Tensor, steps: int = 5, eps: float = 1e-7, precision: str = "highest") -> torch.Tensor:
     """Orthogonalise the trailing two dimensions of G (optimizers.py:27-65):
     Frobenius pre-normalisation, ``steps`` quintic iterations, two order-3
@@ -66,6 +91,11 @@ def newton_schulz_5(G: torch.Tensor, steps: int = 5, eps: float = 1e-7, precisio
     transposed = M > N
     X = G.transpose(-2, -1) if transposed else G
     X = X / torch.sqrt(torch.sum(X * X, dim=(-2, -1), keepdim=True) + eps)
+    if precision == "default" and X.is_cuda and X.dtype == torch.float32:
+        X = _ns_iterations_tensor_cores(X if X.ndim == 3 else X.unsqueeze(0), steps).reshape(X.shape)
+        if transposed:
+            X = X.transpose(-2, -1)
+        return X * math.sqrt(max(1.0, float(M) / float(N)))
     for _ in range(steps):
         x = lo(X)
         A = mm(x, x.transpose(-2, -1))
@@ -225,10 +255,18 @@ class ReferenceOptimizer:
     @torch.no_grad()
     def step(self, step: int) -> None:
         f32 = torch.float32
+        # The schedule, bias corrections and decay factors are float32
+        # arithmetic, as in the reference, done on the host; their exact
+        # float32 values reach the device ops as Python scalars. (A 0-d host
+        # tensor moved to the device would be a pageable copy, which can hold
+        # the host until the stream drains and then expose every launch of the
+        # update.)
         t = torch.tensor(float(step + 1), dtype=f32)
-        c1 = 1.0 - torch.tensor(self.b1, dtype=f32) ** t
-        c2 = 1.0 - torch.tensor(self.b2, dtype=f32) ** t
-        lr_a, lr_m = self.adam_lr(step), self.muon_lr(step)
+        c1 = float(1.0 - torch.tensor(self.b1, dtype=f32) ** t)
+        c2 = float(1.0 - torch.tensor(self.b2, dtype=f32) ** t)
+        lr_a_t, lr_m_t = self.adam_lr(step), self.muon_lr(step)
+        lr_a, lr_m = float(lr_a_t), float(lr_m_t)
+        decay_a, decay_m = float(1.0 - lr_a_t * self.wd), float(1.0 - lr_m_t * self.muon_wd)
         for grp in self.groups:
             dev = grp.m.device
             g = grp.own_stack(grp.grads)
@@ -239,21 +277,17 @@ class ReferenceOptimizer:
                 x = (1.0 - self.mu) * g + self.mu * m
                 # a 1-D matrix passes through unchanged (optimizers.py:35-36)
                 o = newton_schulz_5(x, steps=self.ns_steps, precision=self.precision) if len(grp.shape) >= 2 else x
-                lr = lr_m.to(dev)
-                decay = (1.0 - lr * self.muon_wd) if grp.decayed else torch.ones((), dtype=f32, device=dev)
-                p = p * decay - lr * o
+                p = p * (decay_m if grp.decayed else 1.0) - lr_m * o
             else:
                 m.mul_(self.b1).add_((1.0 - self.b1) * g)
                 v.mul_(self.b2).add_((1.0 - self.b2) * (g * g))
-                u = (m / c1.to(dev)) / (torch.sqrt(v / c2.to(dev)) + self.eps)
+                u = (m / c1) / (torch.sqrt(v / c2) + self.eps)
                 if self.name != "muon_adamw":  # cautious: keep the components that agree with the gradient
                     # the reference's 0/1 mask is built from Python scalars: float32
                     mask = (u * g > 0.0).to(f32)
                     mean = mask.mean(dim=tuple(range(1, mask.ndim)), keepdim=True) if mask.ndim > 1 else mask
                     u = u * (mask / torch.clamp(mean, min=self.cautious_eps))
-                lr = lr_a.to(dev)
-                decay = (1.0 - lr * self.wd) if grp.decayed else torch.ones((), dtype=f32, device=dev)
-                p = p * decay - lr * u
+                p = p * (decay_a if grp.decayed else 1.0) - lr_a * u
             if grp.world > 1:
                 full = torch.empty((grp.world * grp.chunk,) + grp.shape, dtype=p.dtype, device=dev)
                 dist.all_gather_into_tensor(full, p.contiguous(), group=self.pg)
