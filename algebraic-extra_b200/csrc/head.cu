@@ -465,8 +465,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kHeadThreads, 1)
         tmem_ld32(acc + cc * 32, zr);
         const int col0 = t * kFwdNT + cc * 32;
         uint32_t pk[16];
-        if (row_ok && col0 + 32 <= a.V) {
-          // whole chunk valid: the same per-element maths on packed f32x2 pairs
+        if (col0 + 32 <= a.V) {
+          // whole chunk inside the vocabulary (the same for every thread of the
+          // warp, so ignored rows do not split it between the two paths): the
+          // same per-element maths on packed f32x2 pairs; rows that are ignored
+          // or past the end select zero
           const float2 sc = make_float2(scale, scale);
 #pragma unroll
           for (int i2 = 0; i2 < 16; ++i2) {
@@ -485,7 +488,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kHeadThreads, 1)
               gr = mul2(sub2(ipow2_t<NPOW>(mul2(fma2(rad, rr, x), make_float2(st, st))), y), rr);
             }
             const float2 g2 = mul2(gr, sc);
-            pk[i2] = pack_bf16x2(g2.x, g2.y);
+            pk[i2] = row_ok ? pack_bf16x2(g2.x, g2.y) : 0u;
           }
         } else {
 #pragma unroll

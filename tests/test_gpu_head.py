@@ -93,6 +93,24 @@ def test_ce_head_with_padded_vocab_and_ignore_index(ignore, V):
     assert rel_l2(de, de2) < 1e-2
 
 
+@pytest.mark.parametrize("V", [5000, 50304])
+def test_alg_ce_head_with_ignore_index(V):
+    """alg_ce n=8 c=2 (the algebraic preset's head) with 5% of labels =
+    ignore_index: most warps of the dz epilogue then hold an ignored row next
+    to valid ones; ignored rows leave the objective and get exactly zero dh and
+    telemetry; objective and gradients against the float64 oracle."""
+    h, e, t = _inputs(512, 256, V, 0.02, 5, ignore_frac=0.05)
+    obj, tel, dh, de = _run(h, e, t, kind="alg_ce", n=8, c=2., ignore_index=-100)
+    o2, t2, dh2, de2 = _oracle(h, e, t, "alg_ce", 8, 2., ignore_index=-100)
+    np.testing.assert_allclose(obj.item(), o2.item(), rtol=2e-3, atol=2e-4)
+    np.testing.assert_allclose(tel.double(), t2, rtol=2e-2, atol=2e-4)
+    ign = t == -100
+    assert int(ign.sum()) > 0
+    assert torch.all(tel[ign] == 0) and torch.all(dh[ign] == 0)
+    assert rel_l2(dh, dh2) < 1e-2
+    assert rel_l2(de, de2) < 1e-2
+
+
 @pytest.mark.parametrize("key,kind,n,c", [("head_alg_n8c2", "alg_ce", 8, 2.0),
                                           ("head_alg_n16c16", "alg_ce", 16, 16.0), ("head_ce", "ce", 16, 16.0)])
 def test_head_against_reference_goldens(key, kind, n, c):
