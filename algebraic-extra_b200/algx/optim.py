@@ -11,12 +11,18 @@ weight the model stores fused (``w_qkv`` = [w_q | w_k | w_v], ``w_gu`` =
 [w_g | w_u], column blocks) is updated block by block, so each reference
 matrix gets its own Newton-Schulz orthogonalisation and its own cautious mask
 mean.
+
+Two interfaces share the same update rules: ``get_optimizer`` (init_fn,
+step_fn over trees of tensors, the reference's own functional interface,
+optimizers.py:118-240) and ``ReferenceOptimizer`` (in place over named
+parameters with ``.grad``, stacked by shape, optionally sharded over ranks;
+what the data-parallel trainer uses).
 """
 
 from __future__ import annotations
 
 import math
-from typing import Iterable, List, Optional, Tuple
+from typing import Any, Iterable, List, NamedTuple, Optional, Tuple
 
 import torch
 import torch.distributed as dist
@@ -154,6 +160,48 @@ def reference_blocks(name: str, param: torch.Tensor) -> List[Tuple[str, torch.Te
     return [(name, param)]
 
 
+make_cosine_schedule = cosine_schedule  # the reference's name (optimizers.py:92)
+
+
+def _step_scalars(step: int, adam_lr, muon_lr, b1: float, b2: float, wd: float, muon_wd: float):
+    """The step's float32 host quantities as exact Python floats: bias
+    corrections 1 - b^t (t = step + 1), the two learning rates and the two
+    decay factors 1 - lr * wd (optimizers.py:179-184, 215, 225, 233)."""
+    f32 = torch.float32
+    t = torch.tensor(float(step + 1), dtype=f32)
+    c1 = float(1.0 - torch.tensor(b1, dtype=f32) ** t)
+    c2 = float(1.0 - torch.tensor(b2, dtype=f32) ** t)
+    lr_a_t, lr_m_t = adam_lr(step), muon_lr(step)
+    return (c1, c2, float(lr_a_t), float(lr_m_t), float(1.0 - lr_a_t * wd), float(1.0 - lr_m_t * muon_wd))
+
+
+def _muon_update(p, g, m, mu: float, decay: float, lr: float, ns_steps: int, precision: str, matrix: bool):
+    """Muon on a stack of parameters (optimizers.py:210-219): momentum m
+    updated in place, Newton-Schulz of the Nesterov combination (a vector
+    passes through), returns the new parameters."""
+    m.mul_(mu).add_((1.0 - mu) * g)
+    x = (1.0 - mu) * g + mu * m
+    o = newton_schulz_5(x, steps=ns_steps, precision=precision) if matrix else x
+    return p * decay - lr * o
+
+
+def _adam_update(p, g, m, v, b1: float, b2: float, c1: float, c2: float, eps: float, cautious_eps: Optional[float],
+                 decay: float, lr: float):
+    """AdamW, or cautious AdamW when ``cautious_eps`` is given, on a stack of
+    parameters (optimizers.py:220-238): m and v updated in place, the
+    cautious mask's mean taken per row of the stack; returns the new
+    parameters."""
+    m.mul_(b1).add_((1.0 - b1) * g)
+    v.mul_(b2).add_((1.0 - b2) * (g * g))
+    u = (m / c1) / (torch.sqrt(v / c2) + eps)
+    if cautious_eps is not None:  # keep the components that agree with the gradient
+        # the reference's 0/1 mask is built from Python scalars: float32
+        mask = (u * g > 0.0).to(torch.float32)
+        mean = mask.mean(dim=tuple(range(1, mask.ndim)), keepdim=True) if mask.ndim > 1 else mask
+        u = u * (mask / torch.clamp(mean, min=cautious_eps))
+    return p * decay - lr * u
+
+
 class _Group:
     """Reference parameters of one shape, dtype and routing, updated together:
     their values and gradients are gathered into one (count, *shape) stack
@@ -254,42 +302,118 @@ class ReferenceOptimizer:
 
     @torch.no_grad()
     def step(self, step: int) -> None:
-        f32 = torch.float32
         # The schedule, bias corrections and decay factors are float32
         # arithmetic, as in the reference, done on the host; their exact
         # float32 values reach the device ops as Python scalars. (A 0-d host
         # tensor moved to the device would be a pageable copy, which can hold
         # the host until the stream drains and then expose every launch of the
         # update.)
-        t = torch.tensor(float(step + 1), dtype=f32)
-        c1 = float(1.0 - torch.tensor(self.b1, dtype=f32) ** t)
-        c2 = float(1.0 - torch.tensor(self.b2, dtype=f32) ** t)
-        lr_a_t, lr_m_t = self.adam_lr(step), self.muon_lr(step)
-        lr_a, lr_m = float(lr_a_t), float(lr_m_t)
-        decay_a, decay_m = float(1.0 - lr_a_t * self.wd), float(1.0 - lr_m_t * self.muon_wd)
+        c1, c2, lr_a, lr_m, decay_a, decay_m = _step_scalars(step, self.adam_lr, self.muon_lr, self.b1, self.b2,
+                                                             self.wd, self.muon_wd)
+        cautious = self.cautious_eps if self.name != "muon_adamw" else None
         for grp in self.groups:
             dev = grp.m.device
             g = grp.own_stack(grp.grads)
             p = grp.own_stack(grp.params)
-            m, v = grp.m, grp.v
             if grp.muon:
-                m.mul_(self.mu).add_((1.0 - self.mu) * g)
-                x = (1.0 - self.mu) * g + self.mu * m
-                # a 1-D matrix passes through unchanged (optimizers.py:35-36)
-                o = newton_schulz_5(x, steps=self.ns_steps, precision=self.precision) if len(grp.shape) >= 2 else x
-                p = p * (decay_m if grp.decayed else 1.0) - lr_m * o
+                p = _muon_update(p, g, grp.m, self.mu, decay_m if grp.decayed else 1.0, lr_m, self.ns_steps,
+                                 self.precision, len(grp.shape) >= 2)
             else:
-                m.mul_(self.b1).add_((1.0 - self.b1) * g)
-                v.mul_(self.b2).add_((1.0 - self.b2) * (g * g))
-                u = (m / c1) / (torch.sqrt(v / c2) + self.eps)
-                if self.name != "muon_adamw":  # cautious: keep the components that agree with the gradient
-                    # the reference's 0/1 mask is built from Python scalars: float32
-                    mask = (u * g > 0.0).to(f32)
-                    mean = mask.mean(dim=tuple(range(1, mask.ndim)), keepdim=True) if mask.ndim > 1 else mask
-                    u = u * (mask / torch.clamp(mean, min=self.cautious_eps))
-                p = p * (decay_a if grp.decayed else 1.0) - lr_a * u
+                p = _adam_update(p, g, grp.m, grp.v, self.b1, self.b2, c1, c2, self.eps, cautious,
+                                 decay_a if grp.decayed else 1.0, lr_a)
             if grp.world > 1:
                 full = torch.empty((grp.world * grp.chunk,) + grp.shape, dtype=p.dtype, device=dev)
                 dist.all_gather_into_tensor(full, p.contiguous(), group=self.pg)
                 p = full[:len(grp.params)]
             torch._foreach_copy_(grp.params, list(p.unbind(0)))
+
+
+# ------------------------------------------------- the reference's interface
+class OptState(NamedTuple):
+    """Optimizer state of ``get_optimizer`` (optimizers.py:19-24): the step
+    count, and first / second moments as trees shaped like the parameters
+    (second moment None for the parameters Muon updates)."""
+    count: torch.Tensor
+    m: Any
+    v: Any
+
+
+def _tree_map(fn, n_out: int, path: tuple, *trees):
+    """Apply fn(path, *leaves) -> n_out-tuple over matching nested dicts /
+    lists / tuples; returns n_out trees of the same structure."""
+    t0 = trees[0]
+    if isinstance(t0, dict):
+        sub = {k: _tree_map(fn, n_out, path + (k,), *(t[k] for t in trees)) for k in t0}
+        return tuple({k: sub[k][i] for k in t0} for i in range(n_out))
+    if isinstance(t0, (list, tuple)):
+        sub = [_tree_map(fn, n_out, path + (j,), *(t[j] for t in trees)) for j in range(len(t0))]
+        return tuple(type(t0)(x[i] for x in sub) for i in range(n_out))
+    return fn(path, *trees)
+
+
+def _leaf_name(path: tuple) -> str:
+    return ".".join(str(k) for k in path)
+
+
+def get_optimizer(name: str, lr: float, weight_decay: float = 0.1, total_steps: int = 1000,
+                  warmup_fraction: float = 0.02, min_lr_ratio: float = 0.1, b1: float = 0.9, b2: float = 0.95,
+                  adam_eps: float = 1e-8, muon_lr: Optional[float] = None, muon_wd: Optional[float] = None,
+                  muon_momentum: float = 0.95, muon_steps: int = 5, cautious_eps: float = 1e-3,
+                  precision: str = "highest", **kwargs: Any):
+    """(init_fn, step_fn) with the reference's signatures and names
+    (optimizers.py:118-240), over trees (nested dicts, lists, tuples) of
+    torch tensors: ``init_fn(params) -> OptState``;
+    ``step_fn(step, params, grads, opt_state, decay_mask) -> (params, OptState)``,
+    functional (its inputs are not modified). Routing by the last path
+    component; a leaf named ``w_qkv`` or ``w_gu`` is updated as its reference
+    matrices. ``precision``: the Newton-Schulz matmul precision. Unknown
+    names raise ``ValueError`` with the reference's message."""
+    opt_name = name.lower().strip()
+    if opt_name not in NAMES:
+        raise ValueError(f"Unknown optimizer: {name}. Choices: {NAMES}")
+    if precision not in PRECISIONS:
+        raise ValueError(f"unknown matmul precision {precision!r}; choices: {PRECISIONS}")
+    actual_muon_wd = weight_decay if muon_wd is None else muon_wd
+    adam_schedule = cosine_schedule(lr, total_steps, warmup_fraction, min_lr_ratio)
+    muon_schedule = cosine_schedule(lr if muon_lr is None else muon_lr, total_steps, warmup_fraction, min_lr_ratio)
+    cautious = cautious_eps if opt_name != "muon_adamw" else None
+
+    def uses_muon(bname: str, p: torch.Tensor) -> bool:
+        return opt_name != "cadamw" and is_muon_param(bname, p.ndim)
+
+    def init_fn(params) -> OptState:
+        def leaf(path, p):
+            v = torch.zeros_like(p)
+            blocks = reference_blocks(_leaf_name(path), p)
+            return torch.zeros_like(p), (None if all(uses_muon(b, pv) for b, pv in blocks) else v)
+        m, v = _tree_map(leaf, 2, (), params)
+        return OptState(count=torch.zeros((), dtype=torch.int32), m=m, v=v)
+
+    def step_fn(step, params, grads, opt_state: OptState, decay_mask):
+        step = int(step)
+        c1, c2, lr_a, lr_m, decay_a, decay_m = _step_scalars(step, adam_schedule, muon_schedule, b1, b2,
+                                                             weight_decay, actual_muon_wd)
+
+        def leaf(path, p, g, m, v, d):
+            p_new, m_new = p.clone(), m.clone()
+            v_new = None if v is None else v.clone()
+            d = bool(d)
+            name_ = _leaf_name(path)
+            for (bname, pb), (_, gb), (_, mb) in zip(reference_blocks(name_, p_new), reference_blocks(name_, g),
+                                                     reference_blocks(name_, m_new)):
+                # each reference matrix as a stack of one
+                if uses_muon(bname, pb):
+                    upd = _muon_update(pb.unsqueeze(0), gb.unsqueeze(0), mb.unsqueeze(0), muon_momentum,
+                                       decay_m if d else 1.0, lr_m, muon_steps, precision, pb.ndim >= 2)
+                else:
+                    vb = dict(reference_blocks(name_, v_new))[bname]
+                    upd = _adam_update(pb.unsqueeze(0), gb.unsqueeze(0), mb.unsqueeze(0), vb.unsqueeze(0), b1, b2,
+                                       c1, c2, adam_eps, cautious, decay_a if d else 1.0, lr_a)
+                pb.copy_(upd[0])
+            return p_new, m_new, v_new
+
+        with torch.no_grad():
+            p, m, v = _tree_map(leaf, 3, (), params, grads, opt_state.m, opt_state.v, decay_mask)
+        return p, OptState(count=opt_state.count + 1, m=m, v=v)
+
+    return init_fn, step_fn

@@ -3,7 +3,8 @@
 the reference's unchanged source on the torch stand-in for JAX): the
 Newton-Schulz orthogonalisation, the cosine schedule, and three steps of
 muon_adamw, cadamw and hybrid_muon_cadamw on a parameter tree with every
-routing class, all float64."""
+routing class, all float64, through both interfaces: the reference's own
+get_optimizer / init_fn / step_fn, and the in-place ReferenceOptimizer."""
 
 import os
 
@@ -122,6 +123,59 @@ def test_unknown_precision_is_rejected():
         O.newton_schulz_5(torch.zeros(4, 4), precision="high")
 
 
+@pytest.mark.parametrize("name", O.NAMES)
+def test_get_optimizer_matches_reference(name):
+    """The reference's own call sequence (get_optimizer, init_fn, step_fn per
+    step with a decay mask, as tests/golden/make_golden.py drives the
+    reference) reproduces its parameters step by step; the inputs are not
+    modified and Muon-routed leaves hold no second moment."""
+    params0, grads = cases.optim_inputs(71)
+    mask = {k: torch.tensor(v) for k, v in cases.OPTIM_DECAY.items()}
+    init_fn, step_fn = O.get_optimizer(name, **cases.OPTIM_ARGS)
+    first = {k: torch.from_numpy(v).double() for k, v in params0.items()}
+    params = first
+    state = init_fn(params)
+    for step, gr in enumerate(grads):
+        params, state = step_fn(step, params, {k: torch.from_numpy(v).double() for k, v in gr.items()}, state, mask)
+        for k, p in params.items():
+            np.testing.assert_allclose(p.numpy(), GOLD[f"opt_{name}_step{step}_{k}"], rtol=1e-9, atol=1e-12,
+                                       err_msg=f"{name} step {step} {k}")
+    assert int(state.count) == len(grads)
+    for k, v in params0.items():
+        assert np.array_equal(first[k].numpy(), v)
+    for k in params0:
+        muon = name != "cadamw" and O.is_muon_param(k, params0[k].ndim)
+        assert (state.v[k] is None) == muon
+
+
+def test_get_optimizer_walks_nested_trees_and_fused_leaves():
+    """Nested dicts and lists, the reference model's layout, update as flat
+    leaves; a fused w_qkv leaf updates as its three reference matrices."""
+    g = torch.Generator().manual_seed(8)
+    mk = lambda *s: torch.randn(*s, generator=g, dtype=torch.float64)
+    sep = {"layers": [{"w_q": mk(8, 8), "w_k": mk(8, 8), "w_v": mk(8, 8), "ln1": mk(8)} for _ in range(2)],
+           "embed": mk(10, 8)}
+    fused = {"layers": [{"w_qkv": torch.cat([l["w_q"], l["w_k"], l["w_v"]], 1), "ln1": l["ln1"].clone()}
+                        for l in sep["layers"]], "embed": sep["embed"].clone()}
+    gs = {"layers": [{"w_q": mk(8, 8), "w_k": mk(8, 8), "w_v": mk(8, 8), "ln1": mk(8)} for _ in range(2)],
+          "embed": mk(10, 8)}
+    gf = {"layers": [{"w_qkv": torch.cat([l["w_q"], l["w_k"], l["w_v"]], 1), "ln1": l["ln1"]} for l in gs["layers"]],
+          "embed": gs["embed"]}
+    dm_s = {"layers": [{"w_q": True, "w_k": True, "w_v": True, "ln1": False}] * 2, "embed": True}
+    dm_f = {"layers": [{"w_qkv": True, "ln1": False}] * 2, "embed": True}
+    init_fn, step_fn = O.get_optimizer("hybrid_muon_cadamw", lr=1e-2, total_steps=5)
+    ps, st_s = step_fn(0, sep, gs, init_fn(sep), dm_s)
+    pf, st_f = step_fn(0, fused, gf, init_fn(fused), dm_f)
+    for i in range(2):
+        assert torch.equal(pf["layers"][i]["w_qkv"],
+                           torch.cat([ps["layers"][i][k] for k in ("w_q", "w_k", "w_v")], 1))
+        assert torch.equal(pf["layers"][i]["ln1"], ps["layers"][i]["ln1"])
+        assert st_f.v["layers"][i]["w_qkv"] is None and st_f.v["layers"][i]["ln1"] is not None
+    assert torch.equal(pf["embed"], ps["embed"])
+
+
 def test_unknown_optimizer_name_is_rejected():
     with pytest.raises(ValueError, match="Unknown optimizer"):
         O.ReferenceOptimizer("sgd", [], lr=1e-3)
+    with pytest.raises(ValueError, match="Unknown optimizer: sgd"):
+        O.get_optimizer("sgd", lr=1e-3)
