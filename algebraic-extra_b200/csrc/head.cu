@@ -325,6 +325,7 @@ struct DzArgs {
   int ntiles;          // tiles in the slab
   int items;           // (256-token block, tile) work items of the slab: blocks x ntiles
   int ldz;             // row stride of the dz slab (elements)
+  int* gemm_counter;   // tile counter of this slab's GEMM, zeroed here
 };
 
 // Logits of one slab with the forward's load / MMA pipeline; the epilogue
@@ -338,6 +339,7 @@ template <int KIND, int NPOW>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kHeadThreads, 1)
     head_dz_tc_kernel(const __grid_constant__ CUtensorMap th, const __grid_constant__ CUtensorMap te, DzArgs a,
                       __nv_bfloat16* __restrict__ dz, int* dev_err) {
+  pdl_trigger();  // the slab's GEMM may be scheduled as this grid's CTAs finish
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1k(smem_raw);
   __shared__ uint64_t full[kFwdStages], empty[kFwdStages], acc_full[2], acc_empty[2], issued;
@@ -440,6 +442,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kHeadThreads, 1)
     // epilogue: two groups of four warps take alternate items (group g owns
     // accumulator buffer g); thread r of a group owns row r of the item's
     // 128-token block
+    // Launched as a programmatic dependent of the previous slab's GEMM, which
+    // reads the dz buffer: the loads and products of the first items above
+    // overlap its tail; the epilogue writes dz (and resets this slab's GEMM
+    // counter, last used two slabs ago) only once it has finished. h, E and
+    // the statistics were complete before the first slab's normal launch.
+    pdl_wait();
+    if (blockIdx.x == 0 && warp == 0 && lane == 0) *a.gemm_counter = 0;
     const int g = warp >> 2;
     const int r = (warp & 3) * 32 + lane;
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
@@ -556,7 +565,7 @@ struct GemmProblem {
 };
 struct GemmArgs {
   GemmProblem p[2];
-  int* counter;  // zeroed before the launch
+  int* counter;  // zeroed by the slab's dz kernel
 };
 
 __device__ __forceinline__ void named_bar_sync(int id, int count) {
@@ -587,6 +596,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
                           const __grid_constant__ CUtensorMap tc0, const __grid_constant__ CUtensorMap ta1,
                           const __grid_constant__ CUtensorMap tb1, const __grid_constant__ CUtensorMap tc1,
                           GemmArgs g, int* dev_err) {
+  pdl_trigger();  // the next slab's dz kernel may be scheduled as this grid's CTAs finish
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1k(smem_raw);
   uint8_t* sbox = smem + kPairStages * kPairStageBytes;  // two staging boxes, one per epilogue group
@@ -630,6 +640,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   cluster_sync_all();  // both CTAs' barriers are initialised before any remote arrival
   tc_fence_after();
+  // launched as a programmatic dependent of the slab's dz kernel: the set-up
+  // above overlapped its tail; dz and the tile counter are read only after it
+  pdl_wait();
   const uint32_t item_empty0 = cluster_addr(&item_empty[0], 0);
   auto next_item = [&](int j, bool whole_warp) -> int {
     const int slot = j & 3;
@@ -927,14 +940,20 @@ int launch_fwd_k(const CUtensorMap& th, const CUtensorMap& te, const HeadArgs& a
 }
 
 template <int KIND>
-int launch_dz_k(const CUtensorMap& th, const CUtensorMap& te, const DzArgs& a, __nv_bfloat16* dz, cudaStream_t st) {
+// dependent: launch as a programmatic dependent of the previous kernel of the
+// stream (every slab after the first; see head_dz_tc_kernel's epilogue).
+int launch_dz_k(const CUtensorMap& th, const CUtensorMap& te, const DzArgs& a, __nv_bfloat16* dz, bool dependent,
+                cudaStream_t st) {
   int dev = 0, sms = 0;
   ALGX_CUDA(cudaGetDevice(&dev));
   ALGX_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const unsigned grid = 2u * (unsigned)std::max(1, std::min(a.items, sms / 2));  // persistent: one pair per 2 SMs
   auto run = [&](auto kern) -> int {
     ALGX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem));
-    kern<<<grid, kHeadThreads, kFwdSmem, st>>>(th, te, a, dz, device_error_word());
+    if (dependent)
+      ALGX_CUDA(launch_dependent(kern, grid, kHeadThreads, kFwdSmem, st, th, te, a, dz, device_error_word()));
+    else
+      kern<<<grid, kHeadThreads, kFwdSmem, st>>>(th, te, a, dz, device_error_word());
     ALGX_LAUNCHED("head_dz_tc launch");
     return ALGX_OK;
   };
@@ -960,8 +979,9 @@ int launch_gemm_pair(const CUtensorMap (&maps)[6], const GemmArgs& a, cudaStream
   const int total = a.p[0].tiles + a.p[1].tiles;
   const unsigned pairs = (unsigned)std::max(1, std::min(total, sms / 2));  // persistent: one pair per two SMs
   ALGX_CUDA(cudaFuncSetAttribute(head_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPairSmem));
-  head_gemm_pair_kernel<<<2 * pairs, kGemmThreads, kPairSmem, st>>>(maps[0], maps[1], maps[2], maps[3], maps[4],
-                                                                    maps[5], a, device_error_word());
+  // a programmatic dependent of the slab's dz kernel (it waits for it after its set-up)
+  ALGX_CUDA(launch_dependent(head_gemm_pair_kernel, 2 * pairs, kGemmThreads, kPairSmem, st, maps[0], maps[1],
+                             maps[2], maps[3], maps[4], maps[5], a, device_error_word()));
   ALGX_LAUNCHED("head_gemm_pair launch");
   return ALGX_OK;
 }
@@ -1035,7 +1055,7 @@ size_t algx_head_bwd_workspace_size(int64_t N, int64_t d, int64_t V, int32_t dh_
   if (N < 1 || d < 1 || V < 1) return 0;
   size_t bytes = (size_t)N * (size_t)slab_cols(V) * 2;               // dz slab, bf16
   if (dh_dtype == ALGX_BF16) bytes += (size_t)N * (size_t)d * 4;     // fp32 dh accumulator
-  return bytes + 256;                                                // the GEMM's tile counter
+  return bytes + 256;                                                // the GEMM tile counters (two)
 }
 
 int algx_head_bwd(const algx_head_config* cfg, const void* h, const void* embed, const int32_t* targets,
@@ -1056,18 +1076,24 @@ int algx_head_bwd(const algx_head_config* cfg, const void* h, const void* embed,
   __nv_bfloat16* dz = static_cast<__nv_bfloat16*>(workspace);
   float* dh_acc = dh_dtype == ALGX_F32 ? static_cast<float*>(dh)
                                        : reinterpret_cast<float*>(static_cast<char*>(workspace) + (size_t)N * vs * 2);
+  // two GEMM tile counters, alternating by slab (each reset by its slab's dz kernel)
   int* counter = reinterpret_cast<int*>(static_cast<char*>(workspace) + algx_head_bwd_workspace_size(N, d, V, dh_dtype) -
                                         256);
   const int tbp = (int)((N + 255) / 256);  // 256-token blocks of the dz kernel's CTA pairs
   const int ntiles_total = (int)((V + kFwdNT - 1) / kFwdNT);
   const int tiles_n = (int)((d + kPairBN - 1) / kPairBN);
-  for (int64_t c0 = 0; c0 < V; c0 += vs) {
+  // Slab s: dz kernel, then the GEMM that reads its dz, both programmatic
+  // dependents of the kernel before them except the first dz kernel (a plain
+  // launch: everything the chain reads besides dz is complete when it starts).
+  // The dz buffer and the counters stay ordered by the kernels' own waits.
+  for (int64_t c0 = 0, slab = 0; c0 < V; c0 += vs, ++slab) {
     const int64_t vc = std::min<int64_t>(vs, V - c0);  // valid columns of this slab
     DzArgs a{*cfg, targets, stat, scale, (int)N, (int)d, (int)V, (int)vocab_offset, (int)(c0 / kFwdNT), 0, 0, (int)vs};
     a.ntiles = std::min<int>((int)(vs / kFwdNT), ntiles_total - a.tile0);
     a.items = tbp * a.ntiles;
-    int s = cfg->kind == ALGX_HEAD_CE ? launch_dz_k<ALGX_HEAD_CE>(th, te, a, dz, st)
-                                      : launch_dz_k<ALGX_HEAD_ALG_CE>(th, te, a, dz, st);
+    a.gemm_counter = counter + (slab & 1);
+    int s = cfg->kind == ALGX_HEAD_CE ? launch_dz_k<ALGX_HEAD_CE>(th, te, a, dz, slab > 0, st)
+                                      : launch_dz_k<ALGX_HEAD_ALG_CE>(th, te, a, dz, slab > 0, st);
     if (s) return s;
     // problem 0: dE[c0 : c0 + vc] (vc x d) = dz^T . h; problem 1: dh (N x d) (+)= dz . E[c0 : c0 + vc]
     CUtensorMap maps[6];
@@ -1088,8 +1114,7 @@ int algx_head_bwd(const algx_head_config* cfg, const void* h, const void* embed,
     ga.p[0] = GemmProblem{1, 1, 0, tiles_n, (int)((vc + kPairBM - 1) / kPairBM) * tiles_n, (int)((N + 63) / 64)};
     ga.p[1] = GemmProblem{0, 1, c0 > 0 ? 1 : 0, tiles_n, (int)((N + kPairBM - 1) / kPairBM) * tiles_n,
                           (int)((vc + 63) / 64)};
-    ga.counter = counter;
-    ALGX_CUDA(cudaMemsetAsync(counter, 0, sizeof(int), st));
+    ga.counter = a.gemm_counter;
     if ((s = launch_gemm_pair(maps, ga, st))) return s;
   }
   if (dh_dtype == ALGX_BF16) {
