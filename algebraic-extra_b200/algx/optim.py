@@ -118,9 +118,19 @@ def newton_schulz_5(G: torch.Tensor, steps: int = 5, eps: float = 1e-7, precisio
     return X * math.sqrt(max(1.0, float(M) / float(N)))
 
 
-def is_muon_param(name: str, ndim: int) -> bool:
-    """The reference's routing (optimizers.py:68-89) on the last name component."""
-    key = name.split(".")[-1]
+def is_muon_param(path, param) -> bool:
+    """The reference's routing (optimizers.py:68-89) on the last path
+    component: ``path`` is a dotted name or a sequence of keys (a key object
+    with a ``key`` attribute counts by that attribute, as in the reference),
+    ``param`` a tensor or its number of dimensions."""
+    ndim = param if isinstance(param, int) else getattr(param, "ndim", 0)
+    if isinstance(path, str):
+        key = path.split(".")[-1]
+    elif path:
+        last = path[-1]
+        key = str(getattr(last, "key", last))
+    else:
+        key = ""
     if key == "embed":
         return False
     if key.startswith("w_"):
