@@ -141,7 +141,9 @@ __global__ void __launch_bounds__(kPrepThreads) qknorm_attn_prepare_kernel(
     const float* __restrict__ gain_k, const float* __restrict__ rot_cos, const float* __restrict__ rot_sin,
     const float* __restrict__ sink, int H, int T_, T* __restrict__ qs, T* __restrict__ kn, float* guard,
     int64_t rows, float scale, float eps, int in_stride, T* __restrict__ vh) {
-  pdl_trigger();  // the forward kernel may be scheduled behind this grid (it waits for it)
+  // No early griddepcontrol.launch_dependents: the forward, a programmatic
+  // dependent, is scheduled when this multi-wave grid finishes, so its CTAs do
+  // not take SMs this grid's later waves need.
   using V = Vec<T>;
   constexpr int kUnroll = 4;
   const int which = blockIdx.y;  // 0: q (normalised, scaled, written), 1: k (normalised, written), 2: v
@@ -371,7 +373,7 @@ __global__ void __launch_bounds__(256) attn_di_kernel(algx_attn_config cfg, cons
                                                       float* __restrict__ sink_part, int H, int T_,
                                                       float* __restrict__ zero_acc, int* __restrict__ zero_tail) {
   pdl_wait();  // launched as a dependent: the forward's outputs are complete after this
-  pdl_trigger();
+  // no early launch_dependents (the backward's CTAs would wait on SMs this grid's later waves need)
   const Eff e = resolve_variant(cfg, guard);
   // The fast backward's fp32 dQ accumulator (zero_acc, rows of 64) and its
   // 256-byte counter area (zero_tail) are zeroed here, alongside the o / dO

@@ -491,7 +491,9 @@ __global__ void __launch_bounds__(kFwdThreads, 2)
                        float* __restrict__ stat, int H, int T, int* dev_err) {
   pdl_wait();  // launched as a dependent of the prologue, which writes q_scaled and the guard maxima
   const Eff e = resolve_variant(cfg, guard);
-  pdl_trigger();
+  // No early launch_dependents: this grid runs in several waves (two CTAs per
+  // SM), and a dependent launched now would hold SMs its later waves need while
+  // it waits (measured: 8 us of the config-2 step).
   if (e.branch == BR_UNSHIFTED) {
     attn_fwd_tc_body<N, CLIP, false>(&tq, &tk, &tv, cfg, sink, e, o, o_prec, stat, H, T, dev_err);
   } else if constexpr (!CLIP) {
