@@ -216,7 +216,8 @@ ALGX_API int algx_head_finalize(const algx_head_config* cfg, const int32_t* targ
 
 /* Workspace bytes of algx_head_bwd: one bf16 dz slab of N x min(6656, V
  * rounded up to 256), when dh is bf16 an fp32 dh accumulator, and 256 bytes
- * for the slab GEMM's tile counter. The reference writes dz for the whole
+ * for the slab GEMMs' two tile counters (reset by the kernels themselves; the
+ * workspace needs no initialisation). The reference writes dz for the whole
  * vocabulary (fused_head.py:194-216). */
 ALGX_API size_t algx_head_bwd_workspace_size(int64_t N, int64_t d, int64_t V, int32_t dh_dtype);
 
