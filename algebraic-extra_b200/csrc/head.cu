@@ -51,6 +51,11 @@ constexpr int kFwdNT = 256;     // vocabulary columns per tile
 constexpr int kFwdStages = 6;
 constexpr int kFwdStageBytes = kChunkBytes + 128 * 64 * 2;  // this CTA's h chunk + half of the E chunk
 constexpr int kFwdSmem = kFwdStages * kFwdStageBytes + 1024;
+// dz kernel: the load ring plus one 16 KB staging box per epilogue group
+// (128 token rows x 64 bf16 columns, 128-byte swizzle) for its TMA stores
+constexpr int kDzBoxBytes = 128 * 64 * 2;
+constexpr int kDzSmem = kFwdSmem + 2 * kDzBoxBytes;
+static_assert(kDzSmem <= 227 * 1024, "dz kernel shared memory");
 constexpr int kHeadThreads = 320;  // 2 x 4 epilogue warps, TMA warp, MMA warp
 constexpr int kHeadTma = 8;
 
@@ -328,6 +333,10 @@ struct DzArgs {
   int* gemm_counter;   // tile counter of this slab's GEMM, zeroed here
 };
 
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 // Logits of one slab with the forward's load / MMA pipeline; the epilogue
 // (thread = token) turns each fp32 logit into bf16 dz and stores its row
 // segment of the slab. Columns past the vocabulary and ignored rows give 0.
@@ -337,8 +346,8 @@ struct DzArgs {
 // run on across items and every pair gets an equal share of the slab's items.
 template <int KIND, int NPOW>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kHeadThreads, 1)
-    head_dz_tc_kernel(const __grid_constant__ CUtensorMap th, const __grid_constant__ CUtensorMap te, DzArgs a,
-                      __nv_bfloat16* __restrict__ dz, int* dev_err) {
+    head_dz_tc_kernel(const __grid_constant__ CUtensorMap th, const __grid_constant__ CUtensorMap te,
+                      const __grid_constant__ CUtensorMap tdz, DzArgs a, int* dev_err) {
   pdl_trigger();  // the slab's GEMM may be scheduled as this grid's CTAs finish
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1k(smem_raw);
@@ -455,6 +464,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kHeadThreads, 1)
     const algx_head_config& c = a.cfg;
     const float scale = *a.scale;
     const float log2e = 1.4426950408889634f;
+    // dz leaves through the group's staging box: two 32-column chunks fill its
+    // 128-byte rows (swizzled), then one thread stores the box with TMA
+    // (whole 128-byte lines instead of 16-byte pieces of 32 different rows
+    // per warp store; rows past N are clipped by the tensor map)
+    uint8_t* box = smem + kFwdStages * kFwdStageBytes + g * kDzBoxBytes;
+    const bool issuer = (warp & 3) == 0 && lane == 0;
     for (int i = first + g * stride, li = g; i < a.items; i += 2 * stride, li += 2) {
       const int tb = 2 * (i / a.ntiles) + (int)rank, t = a.tile0 + i % a.ntiles;
       const int tok = tb * kRowsT + r;
@@ -463,7 +478,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kHeadThreads, 1)
       const int tloc = tgt - a.voff;  // local column of the target, may be out of range
       const float st = tok < a.N ? a.stat[tok] : 0.f;
       const float stl = st * log2e;
-      __nv_bfloat16* drow = dz + (size_t)tok * a.ldz - (size_t)a.tile0 * kFwdNT;
+      const int xcol = (t - a.tile0) * kFwdNT;  // the tile's first column in the slab buffer
       const int buf = g, use = li >> 1;
       if (!mbar_wait_cluster_warp(&acc_full[buf], use & 1, abort_v, dev_err)) break;
       tc_fence_after();
@@ -522,16 +537,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kHeadThreads, 1)
           pk[i2] = pack_bf16x2(g2[0], g2[1]);
         }
         }
-        if (tok < a.N) {
-          uint4* d4 = reinterpret_cast<uint4*>(drow + col0);
+        const int half = cc & 1;
+        if (!half) {  // the box's previous store has been read out of shared memory
+          if (issuer) bulk_wait_group_read0();
+          named_bar_sync(1 + g, 128);
+        }
 #pragma unroll
-          for (int u = 0; u < 4; ++u) d4[u] = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+        for (int u = 0; u < 4; ++u)
+          *reinterpret_cast<uint4*>(box + r * 128 + (((4 * half + u) ^ (r & 7)) << 4)) =
+              make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
+        if (half) {
+          fence_proxy_async_smem();
+          named_bar_sync(1 + g, 128);
+          if (issuer) {
+            tma_store_2d(&tdz, box, xcol + (cc - 1) * 32, tb * kRowsT);
+            bulk_commit_group();
+          }
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(cluster_addr(&acc_empty[buf], 0));  // the leader's barrier
     }
+    if (issuer) bulk_wait_group0();  // every store of this group has completed
   }
   tc_fence_before();
   __syncthreads();
@@ -568,9 +596,6 @@ struct GemmArgs {
   int* counter;  // zeroed by the slab's dz kernel
 };
 
-__device__ __forceinline__ void named_bar_sync(int id, int count) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
-}
 // The kernel runs on CTA pairs (cta_group::2): a cluster of two CTAs
 // computes a 256 x 256 output tile with M = 256 products issued by the leader
 // (cluster rank 0). CTA r loads A rows m0 + 128 r .. and B columns n0 + 128 r ..
@@ -942,18 +967,18 @@ int launch_fwd_k(const CUtensorMap& th, const CUtensorMap& te, const HeadArgs& a
 template <int KIND>
 // dependent: launch as a programmatic dependent of the previous kernel of the
 // stream (every slab after the first; see head_dz_tc_kernel's epilogue).
-int launch_dz_k(const CUtensorMap& th, const CUtensorMap& te, const DzArgs& a, __nv_bfloat16* dz, bool dependent,
+int launch_dz_k(const CUtensorMap& th, const CUtensorMap& te, const CUtensorMap& tdz, const DzArgs& a, bool dependent,
                 cudaStream_t st) {
   int dev = 0, sms = 0;
   ALGX_CUDA(cudaGetDevice(&dev));
   ALGX_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const unsigned grid = 2u * (unsigned)std::max(1, std::min(a.items, sms / 2));  // persistent: one pair per 2 SMs
   auto run = [&](auto kern) -> int {
-    ALGX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kFwdSmem));
+    ALGX_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kDzSmem));
     if (dependent)
-      ALGX_CUDA(launch_dependent(kern, grid, kHeadThreads, kFwdSmem, st, th, te, a, dz, device_error_word()));
+      ALGX_CUDA(launch_dependent(kern, grid, kHeadThreads, kDzSmem, st, th, te, tdz, a, device_error_word()));
     else
-      kern<<<grid, kHeadThreads, kFwdSmem, st>>>(th, te, a, dz, device_error_word());
+      kern<<<grid, kHeadThreads, kDzSmem, st>>>(th, te, tdz, a, device_error_word());
     ALGX_LAUNCHED("head_dz_tc launch");
     return ALGX_OK;
   };
@@ -1092,8 +1117,12 @@ int algx_head_bwd(const algx_head_config* cfg, const void* h, const void* embed,
     a.ntiles = std::min<int>((int)(vs / kFwdNT), ntiles_total - a.tile0);
     a.items = tbp * a.ntiles;
     a.gemm_counter = counter + (slab & 1);
-    int s = cfg->kind == ALGX_HEAD_CE ? launch_dz_k<ALGX_HEAD_CE>(th, te, a, dz, slab > 0, st)
-                                      : launch_dz_k<ALGX_HEAD_ALG_CE>(th, te, a, dz, slab > 0, st);
+    // the dz kernel's store map: the slab buffer, 128-row x 64-column boxes
+    CUtensorMap tdz;
+    int s = make_tmap_2d(&tdz, dz, ALGX_BF16, (uint64_t)vs, (uint64_t)N, (uint64_t)vs * 2, 64, 128, true);
+    if (s) return s;
+    s = cfg->kind == ALGX_HEAD_CE ? launch_dz_k<ALGX_HEAD_CE>(th, te, tdz, a, slab > 0, st)
+                                  : launch_dz_k<ALGX_HEAD_ALG_CE>(th, te, tdz, a, slab > 0, st);
     if (s) return s;
     // problem 0: dE[c0 : c0 + vc] (vc x d) = dz^T . h; problem 1: dh (N x d) (+)= dz . E[c0 : c0 + vc]
     CUtensorMap maps[6];
