@@ -329,7 +329,6 @@ struct DzArgs {
   int tile0;           // first (local) vocabulary tile of the slab
   int ntiles;          // tiles in the slab
   int items;           // (256-token block, tile) work items of the slab: blocks x ntiles
-  int ldz;             // row stride of the dz slab (elements)
   int* gemm_counter;   // tile counter of this slab's GEMM, zeroed here
 };
 
@@ -1113,7 +1112,7 @@ int algx_head_bwd(const algx_head_config* cfg, const void* h, const void* embed,
   // The dz buffer and the counters stay ordered by the kernels' own waits.
   for (int64_t c0 = 0, slab = 0; c0 < V; c0 += vs, ++slab) {
     const int64_t vc = std::min<int64_t>(vs, V - c0);  // valid columns of this slab
-    DzArgs a{*cfg, targets, stat, scale, (int)N, (int)d, (int)V, (int)vocab_offset, (int)(c0 / kFwdNT), 0, 0, (int)vs};
+    DzArgs a{*cfg, targets, stat, scale, (int)N, (int)d, (int)V, (int)vocab_offset, (int)(c0 / kFwdNT), 0, 0};
     a.ntiles = std::min<int>((int)(vs / kFwdNT), ntiles_total - a.tile0);
     a.items = tbp * a.ntiles;
     a.gemm_counter = counter + (slab & 1);
